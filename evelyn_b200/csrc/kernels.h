@@ -1,0 +1,107 @@
+// kernels.h -- host-side launchers of the decode kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace evl {
+
+// ---------------------------------------------------------------- dequant.cu
+cudaError_t launch_dequant_raw(uint32_t type, const void* raw, uint64_t n, float* out, cudaStream_t s);
+cudaError_t launch_dequant_repacked(const QMatDev& m, uint32_t row0, uint32_t nrows, float* out, cudaStream_t s);
+
+// ---------------------------------------------------------------- qmatvec.cu
+enum MatvecEpilogue : int {
+    EPI_STORE = 0,   // y[r] = W x
+    EPI_ADD = 1,     // y[r] += W x          (residual add after o-proj / down-proj)
+    EPI_SWIGLU = 2,  // y[r] = silu(Wg x) * (Wu x)   (m = gate, m2 = up)
+};
+
+struct MatvecSeg {
+    QMatDev m;
+    QMatDev m2;          // up matrix for EPI_SWIGLU
+    float* y = nullptr;
+    int epi = EPI_STORE;
+};
+
+constexpr int kMaxSegs = 3;
+
+struct MatvecArgs {
+    MatvecSeg seg[kMaxSegs];
+    int nseg = 0;
+    const float* x = nullptr;      // input vector, cols floats
+    uint32_t cols = 0;
+    const float* norm_w = nullptr; // fused RMSNorm weight (null: x used as is)
+    float eps = 1e-6f;
+    float* x_out = nullptr;        // if set, the (normalised) input is also written here
+};
+
+// One fused launch over up to three matrices that share the input vector.
+cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------- attention.cu
+// Paged KV cache. The K tile of (page, layer, head) starts at
+//   pool + page*page_stride + layer*layer_stride + head*head_stride
+// and its V tile v_offset bytes further on. The engine's own pool is
+// [pages][layers][k|v][kv_heads][page_size][head_dim] (v_offset = kv_heads*head_stride).
+struct KvCacheDev {
+    void* pool = nullptr;
+    uint64_t page_stride = 0;      // bytes per page (all layers)
+    uint64_t layer_stride = 0;     // bytes per layer inside a page
+    uint64_t head_stride = 0;      // bytes per (k|v, head) tile
+    int64_t v_offset = 0;          // bytes from a K tile to its V tile
+    uint32_t page_size = 16;
+    uint32_t elem_bytes = 2;       // 2 = f16, 4 = f32
+};
+
+struct RopeArgs {
+    float* q = nullptr;            // [batch][heads*hd]   in/out
+    const float* k = nullptr;      // [batch][kv_heads*hd]
+    const float* v = nullptr;
+    const float* q_norm = nullptr; // per-head RMSNorm weights (null: none)
+    const float* k_norm = nullptr;
+    KvCacheDev kv;
+    uint32_t layer = 0;
+    const int32_t* page_table = nullptr;  // [batch][max_pages]
+    uint32_t max_pages = 0;
+    const int32_t* pos = nullptr;  // [batch] position of the new token
+    uint32_t batch = 1, heads = 0, kv_heads = 0, head_dim = 0, rope_dim = 0;
+    float rope_base = 1e6f, eps = 1e-6f;
+    int interleaved = 0;
+    const float* rope_inv_freq = nullptr;  // [rope_dim/2] base^(-2i/rope_dim), host-computed
+    int* err = nullptr;            // device error flag (DeviceError)
+};
+cudaError_t launch_qk_norm_rope_append(const RopeArgs& a, cudaStream_t s, bool pdl);
+
+struct AttnArgs {
+    const float* q = nullptr;      // [batch][heads*hd] (normed + rotated)
+    float* out = nullptr;          // [batch][heads*hd]
+    KvCacheDev kv;
+    uint32_t layer = 0;
+    const int32_t* page_table = nullptr;
+    uint32_t max_pages = 0;
+    const int32_t* pos = nullptr;  // attend to positions [0, pos]
+    uint32_t batch = 1, heads = 0, kv_heads = 0, head_dim = 0;
+    uint32_t nsplit = 1;           // fixed grid split count; each split covers
+                                   // ceil(t / nsplit) positions rounded up to whole pages
+    float* part = nullptr;         // scratch [batch][heads][nsplit][head_dim + 2]
+    float scale = 0.f;
+    int* err = nullptr;            // device error flag (DeviceError)
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------- misc.cu
+cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t batch, float* x, int32_t* err,
+                         cudaStream_t s, bool pdl);
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t batch, float eps,
+                           cudaStream_t s, bool pdl);
+cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, bool pdl);
+// Greedy pick over [batch][n] logits: first maximum wins (strict '>' like src/runtime.rs:897-905).
+// Optionally writes the pick to next_tokens, logs it at hist[b*hist_stride + pos[b]] and
+// advances pos[b] (null pointers skip each part).
+cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t batch, float* part_v, int32_t* part_i,
+                          uint32_t parts, int32_t* out, int32_t* next_tokens, int32_t* pos, int32_t* hist,
+                          uint32_t hist_stride, cudaStream_t s, bool pdl);
+
+}  // namespace evl
