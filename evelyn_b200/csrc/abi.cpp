@@ -1,0 +1,452 @@
+// abi.cpp -- the extern "C" surface declared in include/evelyn.h.
+//
+// Each entry point catches every C++ exception at the boundary and turns it into an
+// evl_status plus a thread-local message, the way the reference surfaces
+// io::Error values (src/runtime.rs, src/gguf.rs).
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <cfloat>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <thread>
+
+#include "engine.hpp"
+
+using namespace evl;
+
+namespace {
+
+template <class F> evl_status guarded(F&& f) {
+    try {
+        f();
+        return EVL_OK;
+    } catch (const Error& e) {
+        set_last_error(e.msg);
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("out of host memory");
+        return EVL_ERR_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return EVL_ERR_IO;
+    }
+}
+
+void require(bool ok, const char* msg) {
+    if (!ok) raise(EVL_ERR_INVALID_INPUT, msg);
+}
+
+evl_model_options defaults() {
+    evl_model_options o;
+    std::memset(&o, 0, sizeof(o));
+    o.struct_size = sizeof(o);
+    o.device = -1;
+    o.tp_rank = 0;
+    o.tp_size = 1;
+    return o;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* evl_last_error(void) { return last_error(); }
+uint32_t evl_abi_version(void) { return EVL_ABI_VERSION; }
+void evl_model_options_init(evl_model_options* o) {
+    if (o) *o = defaults();
+}
+
+evl_status evl_validate_token_ids(const uint32_t* ids, size_t n, size_t vocab) {
+    return guarded([&] {
+        require(ids || n == 0, "null ids");
+        for (size_t i = 0; i < n; ++i)
+            if (ids[i] >= vocab)
+                raise(EVL_ERR_INVALID_INPUT, "token ID " + std::to_string(ids[i]) + " is outside model vocabulary (" +
+                                                 std::to_string(vocab) + "); check that tokenizer and GGUF match");
+    });
+}
+
+uint32_t evl_argmax(const float* v, size_t n) {
+    size_t bi = 0;
+    float bv = -FLT_MAX;
+    for (size_t i = 0; i < n; ++i)
+        if (v[i] > bv) {
+            bv = v[i];
+            bi = i;
+        }
+    return (uint32_t)bi;
+}
+
+float evl_log_prob(const float* logits, size_t n, uint32_t target) {
+    float mx = -FLT_MAX;
+    for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, logits[i]);
+    float sum = 0.f;
+    for (size_t i = 0; i < n; ++i) sum += std::exp(logits[i] - mx);
+    return logits[target] - (mx + std::log(sum));
+}
+
+evl_status evl_tp_unique_id(uint8_t out[128]) {
+    return guarded([&] {
+        require(out, "null output");
+        ncclUniqueId id;
+        ncclResult_t r = ncclGetUniqueId(&id);
+        if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        std::memcpy(out, id.internal, 128);
+    });
+}
+
+// ------------------------------------------------------------------ model
+evl_status evl_model_load_memory(const void* data, size_t len, const evl_model_options* opts, evl_model** out) {
+    return guarded([&] {
+        require(data && out, "null argument");
+        evl_model_options o = opts ? *opts : defaults();
+        auto* m = new evl_model();
+        try {
+            m->m = load_model(static_cast<const uint8_t*>(data), len, o);
+        } catch (...) {
+            delete m;
+            throw;
+        }
+        *out = m;
+    });
+}
+
+evl_status evl_model_load(const char* path, const evl_model_options* opts, evl_model** out) {
+    return guarded([&] {
+        require(path && out, "null argument");
+        const int fd = ::open(path, O_RDONLY);
+        if (fd < 0) raise(errno == ENOENT ? EVL_ERR_NOT_FOUND : EVL_ERR_IO, std::string(path) + ": " + strerror(errno));
+        struct stat st;
+        if (fstat(fd, &st) != 0) {
+            ::close(fd);
+            raise(EVL_ERR_IO, strerror(errno));
+        }
+        const size_t len = (size_t)st.st_size;
+        void* p = len ? mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0) : nullptr;
+        ::close(fd);
+        if (!len) raise(EVL_ERR_IO, "failed to fill whole buffer");
+        if (p == MAP_FAILED) raise(EVL_ERR_IO, strerror(errno));
+        evl_model_options o = opts ? *opts : defaults();
+        auto* m = new evl_model();
+        try {
+            m->m = load_model(static_cast<const uint8_t*>(p), len, o);
+        } catch (...) {
+            munmap(p, len);
+            delete m;
+            throw;
+        }
+        munmap(p, len);
+        *out = m;
+    });
+}
+
+void evl_model_free(evl_model* m) {
+    if (!m) return;
+    DeviceGuard g(m->m->device);
+    delete m;
+}
+
+evl_status evl_model_config(const evl_model* model, evl_config* o) {
+    return guarded([&] {
+        require(model && o, "null argument");
+        const Config& c = model->m->cfg;
+        std::memset(o, 0, sizeof(*o));
+        std::snprintf(o->arch, sizeof(o->arch), "%s", c.arch.c_str());
+        o->layers = c.layers;
+        o->dim = c.dim;
+        o->ffn = c.ffn;
+        o->heads = c.heads;
+        o->kv_heads = c.kv_heads;
+        o->head_dim = c.head_dim;
+        o->rope_dim = c.rope_dim;
+        o->vocab = c.vocab;
+        o->rope_base = c.rope_base;
+        o->eps = c.eps;
+        o->rope_interleaved = c.rope_interleaved;
+        o->eos_token_id = c.eos;
+    });
+}
+
+uint64_t evl_model_weight_bytes(const evl_model* model) { return model ? model->m->weight_bytes_per_step : 0; }
+
+evl_status evl_model_dense_ffn(evl_model* model, size_t layer, const float* x, float* y) {
+    return guarded([&] {
+        require(model && x && y, "null argument");
+        Model& m = *model->m;
+        require(layer < m.cfg.layers, "layer out of range");
+        std::lock_guard<std::mutex> lk(m.mu);
+        DeviceGuard g(m.device);
+        const size_t dim = m.cfg.dim;
+        float* s = m.scratch.as<float>();
+        float* dx = s;
+        float* dy = s + dim;
+        float* ybuf = s + 2 * dim;
+        float* h = s + 3 * dim;
+        cuda_check(cudaMemcpyAsync(dx, x, dim * 4, cudaMemcpyHostToDevice, m.stream), "H2D");
+        run_dense_ffn(m, layer, dx, nullptr, dy, false, 1, h, ybuf, m.stream, false);
+        cuda_check(cudaMemcpyAsync(y, dy, dim * 4, cudaMemcpyDeviceToHost, m.stream), "D2H");
+        cuda_check(cudaStreamSynchronize(m.stream), "dense_ffn");
+    });
+}
+
+evl_status evl_model_ffn_input(evl_model* model, size_t layer, const float* x, float* y) {
+    return guarded([&] {
+        require(model && x && y, "null argument");
+        Model& m = *model->m;
+        require(layer < m.cfg.layers, "layer out of range");
+        std::lock_guard<std::mutex> lk(m.mu);
+        DeviceGuard g(m.device);
+        const size_t dim = m.cfg.dim;
+        float* s = m.scratch.as<float>();
+        cuda_check(cudaMemcpyAsync(s, x, dim * 4, cudaMemcpyHostToDevice, m.stream), "H2D");
+        cuda_check(launch_rmsnorm(s, m.layers[layer].ffn_norm, s + dim, (uint32_t)dim, 1, m.cfg.eps, m.stream, false),
+                   "rmsnorm");
+        cuda_check(cudaMemcpyAsync(y, s + dim, dim * 4, cudaMemcpyDeviceToHost, m.stream), "D2H");
+        cuda_check(cudaStreamSynchronize(m.stream), "ffn_input");
+    });
+}
+
+evl_status evl_model_dequantize(evl_model* model, const char* tensor, float* out, size_t n) {
+    return guarded([&] {
+        require(model && tensor && out, "null argument");
+        Model& m = *model->m;
+        std::lock_guard<std::mutex> lk(m.mu);
+        DeviceGuard g(m.device);
+        auto vit = m.vecs.find(tensor);
+        if (vit != m.vecs.end()) {
+            require(n == vit->second.second, "element count mismatch");
+            cuda_check(cudaMemcpy(out, vit->second.first, n * 4, cudaMemcpyDeviceToHost), "D2H");
+            return;
+        }
+        auto it = m.matrices.find(tensor);
+        if (it == m.matrices.end()) raise(EVL_ERR_NOT_FOUND, std::string("tensor ") + tensor + " not found");
+        const QMatrix& q = *it->second;
+        require(n == (size_t)q.rows * q.cols, "element count mismatch");
+        DeviceBuffer buf;
+        const uint32_t chunk_rows = std::max<uint32_t>(1, (uint32_t)((256ull << 20) / (4ull * q.cols)));
+        buf.alloc((size_t)std::min<uint32_t>(chunk_rows, q.rows) * q.cols * 4);
+        for (uint32_t r0 = 0; r0 < q.rows; r0 += chunk_rows) {
+            const uint32_t nr = std::min(chunk_rows, q.rows - r0);
+            cuda_check(launch_dequant_repacked(q.dev, r0, nr, buf.as<float>(), m.stream), "dequantize");
+            cuda_check(cudaMemcpyAsync(out + (size_t)r0 * q.cols, buf.p, (size_t)nr * q.cols * 4,
+                                       cudaMemcpyDeviceToHost, m.stream),
+                       "D2H");
+            cuda_check(cudaStreamSynchronize(m.stream), "dequantize");
+        }
+    });
+}
+
+evl_status evl_model_matvec(evl_model* model, const char* tensor, const float* x, size_t xn, float* y, size_t yn) {
+    return guarded([&] {
+        require(model && tensor && x && y, "null argument");
+        Model& m = *model->m;
+        auto it = m.matrices.find(tensor);
+        if (it == m.matrices.end()) raise(EVL_ERR_NOT_FOUND, std::string("tensor ") + tensor + " not found");
+        const QMatrix& q = *it->second;
+        require(xn == q.cols && yn == q.rows, "matvec shape mismatch");
+        std::lock_guard<std::mutex> lk(m.mu);
+        DeviceGuard g(m.device);
+        DeviceBuffer bx, by;
+        bx.alloc(xn * 4);
+        by.alloc(yn * 4);
+        cuda_check(cudaMemcpyAsync(bx.p, x, xn * 4, cudaMemcpyHostToDevice, m.stream), "H2D");
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = q.dev;
+        a.seg[0].y = by.as<float>();
+        a.x = bx.as<float>();
+        a.cols = q.cols;
+        cuda_check(launch_qmatvec(a, m.stream, false), "matvec");
+        cuda_check(cudaMemcpyAsync(y, by.p, yn * 4, cudaMemcpyDeviceToHost, m.stream), "D2H");
+        cuda_check(cudaStreamSynchronize(m.stream), "matvec");
+    });
+}
+
+// ------------------------------------------------------------------ sessions
+evl_status evl_session_new(evl_model* model, uint32_t max_ctx, evl_session** out) {
+    return guarded([&] {
+        require(model && out, "null argument");
+        DeviceGuard g(model->m->device);
+        auto* s = new evl_session();
+        try {
+            s->d.init(model->m.get(), 1, max_ctx);
+        } catch (...) {
+            delete s;
+            throw;
+        }
+        *out = s;
+    });
+}
+
+void evl_session_free(evl_session* s) { delete s; }
+uint64_t evl_session_pos(const evl_session* s) { return s ? s->d.host_pos[0] : 0; }
+
+evl_status evl_session_step(evl_session* s, uint32_t token, const evl_ffn_backend* ffn, float* logits_out,
+                            uint32_t* argmax_out) {
+    return guarded([&] {
+        require(s, "null session");
+        s->d.step(&token, ffn, logits_out, argmax_out);
+    });
+}
+
+evl_status evl_session_generate(evl_session* s, uint32_t token, uint32_t n, uint32_t* tokens_out) {
+    return guarded([&] {
+        require(s && (tokens_out || n == 0), "null argument");
+        s->d.generate(token, n, tokens_out);
+    });
+}
+
+void* evl_session_stream(evl_session* s) { return s ? (void*)s->d.stream : nullptr; }
+uint32_t evl_session_kernels_per_step(const evl_session* s) { return s ? s->d.kernels_per_step : 0; }
+
+evl_status evl_batch_new(evl_model* model, uint32_t n_seqs, uint32_t max_ctx, evl_batch** out) {
+    return guarded([&] {
+        require(model && out, "null argument");
+        DeviceGuard g(model->m->device);
+        auto* b = new evl_batch();
+        try {
+            b->d.init(model->m.get(), n_seqs, max_ctx);
+        } catch (...) {
+            delete b;
+            throw;
+        }
+        *out = b;
+    });
+}
+
+void evl_batch_free(evl_batch* b) { delete b; }
+uint64_t evl_batch_pos(const evl_batch* b, uint32_t seq) {
+    return (b && seq < b->d.host_pos.size()) ? b->d.host_pos[seq] : 0;
+}
+evl_status evl_batch_step(evl_batch* b, const uint32_t* tokens, float* logits_out, uint32_t* argmax_out) {
+    return guarded([&] {
+        require(b && tokens, "null argument");
+        b->d.step(tokens, nullptr, logits_out, argmax_out);
+    });
+}
+void* evl_batch_stream(evl_batch* b) { return b ? (void*)b->d.stream : nullptr; }
+
+// ------------------------------------------------------------------ kernels on caller buffers
+evl_status evl_dequantize_raw(uint32_t type, const void* d_raw, size_t n, float* d_out, void* stream) {
+    return guarded([&] {
+        require(d_raw && d_out, "null argument");
+        type_bytes(type, n);  // Unsupported for unknown types
+        cuda_check(launch_dequant_raw(type, d_raw, n, d_out, as_stream(stream)), "dequantize");
+    });
+}
+
+evl_status evl_qmatrix_create(uint32_t type, uint32_t rows, uint32_t cols, const void* host_raw, int device,
+                              evl_qmatrix** out) {
+    return guarded([&] {
+        require(host_raw && out && rows && cols, "null argument or empty matrix");
+        auto* q = new evl_qmatrix();
+        try {
+            q->device = device;
+            DeviceGuard g(device);
+            q->m.name = "matrix";
+            q->m.type = type;
+            q->m.rows = rows;
+            q->m.cols = cols;
+            repack_sizes(q->m);
+            q->buf.alloc(q->m.bytes());
+            place(q->m, q->buf.as<uint8_t>());
+            std::vector<uint8_t> staging(q->m.bytes());
+            repack_host(q->m, static_cast<const uint8_t*>(host_raw), type_bytes(type, cols), staging.data(),
+                        (int)std::max(1u, std::thread::hardware_concurrency()));
+            cuda_check(cudaMemcpy(q->buf.p, staging.data(), staging.size(), cudaMemcpyHostToDevice), "upload");
+        } catch (...) {
+            delete q;
+            throw;
+        }
+        *out = q;
+    });
+}
+
+void evl_qmatrix_free(evl_qmatrix* q) {
+    if (!q) return;
+    DeviceGuard g(q->device);
+    delete q;
+}
+uint64_t evl_qmatrix_bytes(const evl_qmatrix* q) { return q ? q->m.bytes() : 0; }
+
+evl_status evl_qmatrix_matvec(const evl_qmatrix* q, const float* d_x, float* d_y, void* stream) {
+    return guarded([&] {
+        require(q && d_x && d_y, "null argument");
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = q->m.dev;
+        a.seg[0].y = d_y;
+        a.x = d_x;
+        a.cols = q->m.cols;
+        cuda_check(launch_qmatvec(a, as_stream(stream), false), "matvec");
+    });
+}
+
+evl_status evl_qmatrix_dequantize(const evl_qmatrix* q, float* d_out, void* stream) {
+    return guarded([&] {
+        require(q && d_out, "null argument");
+        cuda_check(launch_dequant_repacked(q->m.dev, 0, q->m.rows, d_out, as_stream(stream)), "dequantize");
+    });
+}
+
+evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
+                                const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
+                                uint32_t head_dim, uint32_t page_size, float* d_out, void* stream) {
+    return guarded([&] {
+        require(d_q && d_k_pages && d_v_pages && d_page_table && d_out, "null argument");
+        require(t > 0, "no positions to attend");
+        require(head_dim == 128 || head_dim == 64, "head_dim must be 64 or 128");
+        require(page_size == 16, "page_size must be 16");
+        require(kv_heads && heads % kv_heads == 0, "heads must be a multiple of kv_heads");
+        cudaStream_t s = as_stream(stream);
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const uint32_t pages = (t + page_size - 1) / page_size;
+        const uint32_t nsplit = std::max<uint32_t>(1, std::min<uint32_t>((2u * sms) / kv_heads, pages));
+        // scratch: split partials, then position and error flag
+        const size_t part_floats = (size_t)heads * nsplit * (head_dim + 2);
+        DeviceBuffer scratch;
+        scratch.alloc(part_floats * 4 + 16);
+        int32_t* d_pos = reinterpret_cast<int32_t*>(scratch.as<uint8_t>() + part_floats * 4);
+        int32_t* d_err = d_pos + 1;
+        const int32_t host[2] = {(int32_t)(t - 1), 0};
+        cuda_check(cudaMemcpyAsync(d_pos, host, 8, cudaMemcpyHostToDevice, s), "H2D");
+        AttnArgs a;
+        a.q = d_q;
+        a.out = d_out;
+        a.kv.pool = const_cast<void*>(d_k_pages);
+        a.kv.head_stride = (uint64_t)page_size * head_dim * 2;
+        a.kv.page_stride = a.kv.head_stride * kv_heads;
+        a.kv.layer_stride = 0;
+        a.kv.v_offset = static_cast<const uint8_t*>(d_v_pages) - static_cast<const uint8_t*>(d_k_pages);
+        a.kv.page_size = page_size;
+        a.kv.elem_bytes = 2;
+        a.page_table = d_page_table;
+        a.max_pages = pages;
+        a.pos = d_pos;
+        a.heads = heads;
+        a.kv_heads = kv_heads;
+        a.head_dim = head_dim;
+        a.nsplit = nsplit;
+        a.part = scratch.as<float>();
+        a.scale = 1.0f / sqrtf((float)head_dim);
+        a.err = d_err;
+        cuda_check(launch_attention(a, s, false), "attention");
+        int32_t err = 0;
+        cuda_check(cudaMemcpyAsync(&err, d_err, 4, cudaMemcpyDeviceToHost, s), "D2H");
+        cuda_check(cudaStreamSynchronize(s), "attention");
+        if (err == DEV_ERR_WAIT_TIMEOUT) raise(EVL_ERR_TIMEOUT, "a device wait for KV pages timed out");
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,230 @@
+// engine.hpp -- internal host-side types of the decode engine (not part of the ABI).
+//
+// Model   ~ runtime.rs Model (:184-425): config, device-resident repacked weights.
+// Decoder ~ runtime.rs Session (:634-808): per-sequence paged KV cache, work buffers,
+//           the captured CUDA graph of one dense step. evl_session wraps one with a
+//           single sequence, evl_batch one with n sequences.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/evelyn.h"
+#include "kernels.h"
+
+namespace evl {
+
+// ------------------------------------------------------------------ errors
+struct Error {
+    evl_status code;
+    std::string msg;
+};
+[[noreturn]] void raise(evl_status code, const std::string& msg);
+void cuda_check(cudaError_t e, const char* what);
+void set_last_error(const std::string& msg);
+const char* last_error();
+
+// Makes `device` current for the lifetime of the guard.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int device);
+    ~DeviceGuard();
+};
+
+struct DeviceBuffer {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    ~DeviceBuffer();
+    void alloc(size_t n);
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinnedBuffer {
+    void* p = nullptr;
+    size_t bytes = 0;
+    PinnedBuffer() = default;
+    PinnedBuffer(const PinnedBuffer&) = delete;
+    PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+    ~PinnedBuffer();
+    void alloc(size_t n);
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+// ------------------------------------------------------------------ GGUF (src/gguf.rs)
+size_t type_bytes(uint32_t t, size_t n);  // gguf.rs:288-298; raises Unsupported
+const char* type_name(uint32_t t);
+
+struct GgufValue {
+    enum Kind { U64, I64, F64, BOOL, STR, ARRAY } kind = U64;
+    uint64_t u = 0;
+    int64_t i = 0;
+    double f = 0;
+    bool b = false;
+    std::string s;
+    std::vector<GgufValue> arr;
+    bool as_u64(uint64_t* o) const;
+    bool as_f64(double* o) const;
+};
+
+struct GgufTensor {
+    std::string name;
+    std::vector<uint64_t> dims;
+    uint32_t type = 0;
+    uint64_t offset = 0;
+    uint64_t elements() const;
+};
+
+class Gguf {
+public:
+    // Parses an image that stays alive for the parser's lifetime.
+    void open(const uint8_t* data, size_t len);
+    const GgufValue* meta(const std::string& key) const;
+    std::string architecture() const;
+    bool has(const std::string& tensor) const { return tensors_.count(tensor) != 0; }
+    const GgufTensor& tensor(const std::string& name) const;  // NotFound
+    const uint8_t* raw(const GgufTensor& t, size_t* nbytes) const;
+    const std::map<std::string, GgufTensor>& tensors() const { return tensors_; }
+
+private:
+    const uint8_t* base_ = nullptr;
+    size_t len_ = 0;
+    std::map<std::string, GgufValue> meta_;
+    std::map<std::string, GgufTensor> tensors_;
+    uint64_t data_start_ = 0;
+};
+
+// ------------------------------------------------------------------ repacked matrices
+// Host-side description of one repacked matrix (or one tensor-parallel shard of it).
+struct QMatrix {
+    std::string name;
+    uint32_t type = 0, rows = 0, cols = 0;
+    size_t payload_bytes = 0, aux_bytes = 0, d_bytes = 0;
+    size_t offset = 0;  // inside the model's weight buffer
+    QMatDev dev;        // device pointers once placed
+    size_t bytes() const { return payload_bytes + aux_bytes + d_bytes; }
+};
+
+// Sizes of the repacked form of a [rows][cols] tensor of `type`; raises Unsupported.
+void repack_sizes(QMatrix& m);
+// Repacks raw GGUF rows [rows][type_bytes(type, cols)] (already sliced to the shard)
+// into host memory at dst (payload, then aux, then d), using `threads` threads.
+void repack_host(const QMatrix& m, const uint8_t* raw, size_t raw_row_stride, uint8_t* dst, int threads);
+// Points m.dev at base + m.offset.
+void place(QMatrix& m, uint8_t* base);
+
+// ------------------------------------------------------------------ model
+struct Config {
+    std::string arch;
+    uint64_t layers = 0, dim = 0, ffn = 0, heads = 0, kv_heads = 0, head_dim = 0, rope_dim = 0, vocab = 0;
+    float rope_base = 10000.f, eps = 1e-6f;
+    bool rope_interleaved = false;
+    int64_t eos = -1;
+};
+
+struct LayerWeights {
+    QMatrix q, k, v, o, gate, up, down;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    float* q_norm = nullptr;  // null when the GGUF has no attn_q_norm
+    float* k_norm = nullptr;
+};
+
+struct Model {
+    Config cfg;
+    int device = 0;
+    int tp_rank = 0, tp_size = 1;
+    ncclComm_t comm = nullptr;
+    bool kv_f32 = false;
+    // this rank's shard sizes
+    uint32_t lheads = 0, lkv_heads = 0, lffn = 0, lvocab = 0, vocab0 = 0;
+
+    DeviceBuffer weights;  // every repacked matrix
+    DeviceBuffer vectors;  // norms + rope table (f32)
+    QMatrix embed, lm_head;
+    std::vector<LayerWeights> layers;
+    float* out_norm = nullptr;
+    float* rope_inv_freq = nullptr;
+    std::map<std::string, QMatrix*> matrices;
+    std::map<std::string, std::pair<float*, size_t>> vecs;
+    uint64_t weight_bytes_per_step = 0;
+
+    // model-level calls (dense_ffn, matvec, dequantize) run on this stream
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    DeviceBuffer scratch;  // x[dim] | y[dim] | ybuf[dim] | h[lffn] | spare
+    int32_t* d_err = nullptr;
+
+    ~Model();
+};
+
+std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_model_options& opts);
+
+void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s);
+
+// Device launch sequence of one dense FFN on `x` (already normalised when norm_w is
+// null) writing y; add=true accumulates into y (residual). TP: partial + all-reduce.
+void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
+                   float* h_buf, float* y_buf, cudaStream_t s, bool pdl);
+
+// ------------------------------------------------------------------ sessions
+struct StepBuffers {
+    uint32_t batch = 1;
+    uint32_t max_ctx = 0, pages_per_seq = 0;
+    DeviceBuffer kv, page_table, pos, tokens, argmax, hist, err;
+    DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
+    uint32_t nsplit = 1, amax_parts = 1;
+    PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;
+};
+
+struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
+    Model* model = nullptr;
+    StepBuffers b;
+    KvCacheDev kv;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    bool graph_pdl = true;
+    std::vector<uint64_t> host_pos;
+    uint32_t kernels = 0, kernels_per_step = 0;
+
+    ~Decoder();
+    void init(Model* m, uint32_t batch, uint32_t max_ctx);
+    // Enqueue one dense step (every kernel) on `stream`.
+    void enqueue_dense(bool pdl);
+    void enqueue_layer_attention(uint32_t layer, bool pdl);
+    void enqueue_head(bool pdl);
+    // A step with a routed-FFN hook (eager, synchronising at routed layers).
+    void run_routed(const evl_ffn_backend& ffn);
+    void launch_graph();
+    void check_device_error();
+    // Session::step for every sequence: host tokens in, optional host logits/argmax out.
+    void step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* logits_out, uint32_t* argmax_out);
+    // On-device greedy loop of n steps (single sequence).
+    void generate(uint32_t token, uint32_t n, uint32_t* tokens_out);
+};
+
+}  // namespace evl
+
+struct evl_model {
+    std::unique_ptr<evl::Model> m;
+};
+struct evl_session {
+    evl::Decoder d;
+};
+struct evl_batch {
+    evl::Decoder d;
+};
+struct evl_qmatrix {
+    evl::QMatrix m;
+    evl::DeviceBuffer buf;
+    int device = 0;
+};

@@ -1,0 +1,374 @@
+// model.cpp -- Model::load for the device (src/runtime.rs:199-406).
+//
+// Reads the same metadata keys with the same defaults (rope.freq_base 1e4,
+// rope.dimension_count = head_dim, layer_norm_rms_epsilon 1e-6, head_count_kv from
+// a number or the first positive array entry, key_length or dim/heads), the same
+// tensor names (post_attention_norm preferred over ffn_norm, optional q/k norms,
+// output.weight falling back to the tied token_embd.weight), and the same errors
+// (InvalidData "missing {arch}.{key}", NotFound for absent tensors). It then
+// uploads every matrix once, repacked for the GPU, keeping it quantised.
+//
+// Tensor parallelism (tp_size > 1): column split of attn_q/k/v by heads and of
+// ffn_gate/up by output rows, row split of attn_output and ffn_down along their
+// inputs on 256-value super-block boundaries (uneven shards when the block count
+// does not divide), LM head split by vocabulary rows, norms replicated.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "engine.hpp"
+
+namespace evl {
+
+namespace {
+
+struct Planned {
+    QMatrix* m;
+    const uint8_t* raw;      // first byte of the first row of the shard
+    size_t stride;           // bytes between rows in `raw`
+    uint32_t col_byte0 = 0;  // byte offset of the shard's first column within a row
+    uint32_t col_bytes = 0;  // bytes per row in the shard (0: whole row)
+};
+
+uint32_t block_elems(uint32_t t) {
+    switch (t) {
+        case GGML_Q4_K:
+        case GGML_Q5_K:
+        case GGML_Q6_K: return 256;
+        case GGML_Q8_0: return 32;
+        default: return 1;
+    }
+}
+
+// Even split of n items over p parts: part i gets [lo, hi).
+void split_range(uint64_t n, int p, int i, uint64_t* lo, uint64_t* hi) {
+    const uint64_t base = n / p, rem = n % p;
+    *lo = i * base + std::min<uint64_t>(i, rem);
+    *hi = *lo + base + (i < (int)rem ? 1 : 0);
+}
+
+}  // namespace
+
+Model::~Model() {
+    if (comm) ncclCommDestroy(comm);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_model_options& o) {
+    auto M = std::make_unique<Model>();
+    Model& m = *M;
+    if (o.device >= 0) {
+        m.device = o.device;
+    } else {
+        cuda_check(cudaGetDevice(&m.device), "cudaGetDevice");
+    }
+    DeviceGuard guard(m.device);
+    m.tp_size = o.tp_size > 0 ? o.tp_size : 1;
+    m.tp_rank = o.tp_rank;
+    if (m.tp_rank < 0 || m.tp_rank >= m.tp_size) raise(EVL_ERR_INVALID_INPUT, "tp_rank outside [0, tp_size)");
+    m.kv_f32 = o.kv_f32 != 0;
+
+    Gguf g;
+    g.open(data, len);
+    Config& c = m.cfg;
+    std::string arch = g.architecture();
+    if (arch.empty()) arch = "llama";
+    auto need = [&](const std::string& k) -> uint64_t {
+        uint64_t v;
+        const GgufValue* val = g.meta(arch + "." + k);
+        if (!val || !val->as_u64(&v)) raise(EVL_ERR_INVALID_DATA, "missing " + arch + "." + k);
+        return v;
+    };
+    c.arch = arch;
+    c.dim = need("embedding_length");
+    c.heads = need("attention.head_count");
+    if (const GgufValue* kv = g.meta(arch + ".attention.head_count_kv")) {
+        uint64_t u;
+        if (kv->as_u64(&u)) {
+            c.kv_heads = u;
+        } else {
+            c.kv_heads = c.heads;
+            if (kv->kind == GgufValue::ARRAY)
+                for (const auto& e : kv->arr)
+                    if (e.as_u64(&u) && u > 0) {
+                        c.kv_heads = u;
+                        break;
+                    }
+        }
+    } else {
+        c.kv_heads = c.heads;
+    }
+    uint64_t u64;
+    const GgufValue* kl = g.meta(arch + ".attention.key_length");
+    if (c.heads == 0) raise(EVL_ERR_INVALID_DATA, arch + ".attention.head_count is zero");
+    c.head_dim = (kl && kl->as_u64(&u64)) ? u64 : c.dim / c.heads;
+    if (arch == "qwen35")
+        raise(EVL_ERR_UNSUPPORTED, "qwen35 gated-delta layers are not part of the device decode path");
+    c.layers = need("block_count");
+    c.ffn = need("feed_forward_length");
+    double f64;
+    const GgufValue* rb = g.meta(arch + ".rope.freq_base");
+    c.rope_base = (rb && rb->as_f64(&f64)) ? (float)f64 : 10000.0f;
+    const GgufValue* rd = g.meta(arch + ".rope.dimension_count");
+    c.rope_dim = (rd && rd->as_u64(&u64)) ? u64 : c.head_dim;
+    const GgufValue* ri = g.meta(arch + ".rope.mrope_interleaved");
+    c.rope_interleaved = ri && ri->kind == GgufValue::BOOL && ri->b;
+    const GgufValue* ep = g.meta(arch + ".attention.layer_norm_rms_epsilon");
+    c.eps = (ep && ep->as_f64(&f64)) ? (float)f64 : 1e-6f;
+    c.vocab = g.has("token_embd.weight") && g.tensor("token_embd.weight").dims.size() > 1
+                  ? g.tensor("token_embd.weight").dims[1]
+                  : 0;
+    const GgufValue* eos = g.meta("tokenizer.ggml.eos_token_id");
+    c.eos = (eos && eos->as_u64(&u64) && u64 <= 0xffffffffu) ? (int64_t)u64 : -1;
+
+    // ---- device-path constraints
+    if (c.head_dim != 64 && c.head_dim != 128)
+        raise(EVL_ERR_UNSUPPORTED,
+              "head_dim " + std::to_string(c.head_dim) + " (device attention handles 64 and 128)");
+    if (c.kv_heads == 0 || c.heads % c.kv_heads)
+        raise(EVL_ERR_INVALID_DATA, "head_count is not a multiple of head_count_kv");
+    const uint64_t group = c.heads / c.kv_heads;
+    if (group != 1 && group != 2 && group != 4 && group != 8)
+        raise(EVL_ERR_UNSUPPORTED,
+              "GQA group size " + std::to_string(group) + " (device attention handles 1, 2, 4, 8)");
+    const int T = m.tp_size, R = m.tp_rank;
+    if (c.kv_heads % T) raise(EVL_ERR_INVALID_INPUT, "tp_size must divide head_count_kv");
+    m.lkv_heads = (uint32_t)(c.kv_heads / T);
+    m.lheads = (uint32_t)(c.heads / T);
+    const uint64_t hd = c.head_dim, qw = c.heads * hd, kw = c.kv_heads * hd;
+
+    // ---- plan every matrix
+    std::vector<Planned> plan;
+    auto add_matrix = [&](QMatrix& q, const std::string& name, uint64_t want_rows, uint64_t want_cols, uint64_t r0,
+                          uint64_t r1, uint64_t c0, uint64_t c1) {
+        const GgufTensor& t = g.tensor(name);
+        uint64_t cols, rows;
+        if (t.dims.size() == 2) {
+            cols = t.dims[0];
+            rows = t.dims[1];
+        } else if (t.dims.size() == 1) {
+            cols = t.dims[0];
+            rows = 1;
+        } else {
+            raise(EVL_ERR_INVALID_DATA, name + ": unsupported rank");
+        }
+        if ((want_rows && rows != want_rows) || (want_cols && cols != want_cols))
+            raise(EVL_ERR_INVALID_DATA, name + ": shape [" + std::to_string(cols) + ", " + std::to_string(rows) +
+                                            "] does not match the model metadata");
+        if (r1 == 0) r1 = rows;
+        if (c1 == 0) c1 = cols;
+        const size_t nbytes_row = type_bytes(t.type, cols);
+        size_t nb;
+        const uint8_t* raw = g.raw(t, &nb);
+        q.name = name;
+        q.type = t.type;
+        q.rows = (uint32_t)(r1 - r0);
+        q.cols = (uint32_t)(c1 - c0);
+        repack_sizes(q);
+        Planned p;
+        p.m = &q;
+        p.raw = raw + r0 * nbytes_row;
+        p.stride = nbytes_row;
+        if (c0 != 0 || c1 != cols) {
+            const uint32_t be = block_elems(t.type);
+            if (c0 % be || c1 % be) raise(EVL_ERR_UNSUPPORTED, name + ": shard is not block aligned");
+            p.col_byte0 = (uint32_t)type_bytes(t.type, c0);
+            p.col_bytes = (uint32_t)type_bytes(t.type, c1 - c0);
+        }
+        plan.push_back(p);
+        m.matrices[name] = &q;
+    };
+
+    // the FFN is split on 256-value boundaries so ffn_down shards stay block aligned
+    uint64_t f0 = 0, f1 = c.ffn;
+    if (T > 1) {
+        if (c.ffn % 256) raise(EVL_ERR_UNSUPPORTED, "tensor parallelism needs feed_forward_length % 256 == 0");
+        uint64_t b0, b1;
+        split_range(c.ffn / 256, T, R, &b0, &b1);
+        f0 = b0 * 256;
+        f1 = b1 * 256;
+    }
+    m.lffn = (uint32_t)(f1 - f0);
+    uint64_t v0 = 0, v1 = c.vocab;
+    if (T > 1) split_range(c.vocab, T, R, &v0, &v1);
+    m.vocab0 = (uint32_t)v0;
+    m.lvocab = (uint32_t)(v1 - v0);
+
+    add_matrix(m.embed, "token_embd.weight", 0, c.dim, 0, 0, 0, 0);
+    m.layers.resize(c.layers);
+    const uint64_t hq0 = (uint64_t)R * m.lheads * hd, hq1 = hq0 + (uint64_t)m.lheads * hd;
+    const uint64_t hk0 = (uint64_t)R * m.lkv_heads * hd, hk1 = hk0 + (uint64_t)m.lkv_heads * hd;
+    for (uint64_t i = 0; i < c.layers; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        if (g.has(p + "attn_qkv.weight"))
+            raise(EVL_ERR_UNSUPPORTED, p + "gated-delta layers are not part of the device decode path");
+        LayerWeights& L = m.layers[i];
+        add_matrix(L.q, p + "attn_q.weight", qw, c.dim, hq0, hq1, 0, 0);
+        add_matrix(L.k, p + "attn_k.weight", kw, c.dim, hk0, hk1, 0, 0);
+        add_matrix(L.v, p + "attn_v.weight", kw, c.dim, hk0, hk1, 0, 0);
+        add_matrix(L.o, p + "attn_output.weight", c.dim, qw, 0, 0, T > 1 ? hq0 : 0, T > 1 ? hq1 : 0);
+        add_matrix(L.gate, p + "ffn_gate.weight", c.ffn, c.dim, f0, f1, 0, 0);
+        add_matrix(L.up, p + "ffn_up.weight", c.ffn, c.dim, f0, f1, 0, 0);
+        add_matrix(L.down, p + "ffn_down.weight", c.dim, c.ffn, 0, 0, T > 1 ? f0 : 0, T > 1 ? f1 : 0);
+        if (L.gate.type != L.up.type) raise(EVL_ERR_UNSUPPORTED, p + "ffn_gate and ffn_up differ in type");
+    }
+    // LM head: output.weight, else the tied embedding (runtime.rs:392-396). Tied, it is
+    // planned as its own (vocabulary-sharded) copy and the embedding keeps the name.
+    const std::string head_name = g.has("output.weight") ? "output.weight" : "token_embd.weight";
+    add_matrix(m.lm_head, head_name, c.vocab, c.dim, v0, v1, 0, 0);
+    if (head_name == "token_embd.weight") m.matrices["token_embd.weight"] = &m.embed;
+
+    // ---- vectors (f32 on the device)
+    struct VecPlan {
+        std::string name;
+        float** dst;
+        uint64_t n;
+    };
+    std::vector<VecPlan> vplan;
+    for (uint64_t i = 0; i < c.layers; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        LayerWeights& L = m.layers[i];
+        vplan.push_back({p + "attn_norm.weight", &L.attn_norm, c.dim});
+        const std::string fn = g.has(p + "post_attention_norm.weight") ? p + "post_attention_norm.weight"
+                                                                         : p + "ffn_norm.weight";
+        vplan.push_back({fn, &L.ffn_norm, c.dim});
+        if (g.has(p + "attn_q_norm.weight")) vplan.push_back({p + "attn_q_norm.weight", &L.q_norm, hd});
+        if (g.has(p + "attn_k_norm.weight")) vplan.push_back({p + "attn_k_norm.weight", &L.k_norm, hd});
+    }
+    vplan.push_back({"output_norm.weight", &m.out_norm, c.dim});
+    const uint32_t rdim = (uint32_t)(std::min<uint64_t>(c.rope_dim, hd) & ~1ull);
+    const size_t rope_floats = std::max<uint32_t>((rdim / 2 + 63) / 64 * 64, 64);
+    size_t vfloats = rope_floats;
+    for (auto& v : vplan) {
+        const GgufTensor& t = g.tensor(v.name);
+        if (t.elements() != v.n) raise(EVL_ERR_INVALID_DATA, v.name + ": unexpected length");
+        vfloats += (v.n + 63) / 64 * 64;
+    }
+
+    // ---- allocate and fill
+    size_t total = 0;
+    for (auto& p : plan) {
+        p.m->offset = total;
+        total += p.m->bytes();
+    }
+    m.weights.alloc(total);
+    m.vectors.alloc(vfloats * 4);
+    size_t max_bytes = 0, max_raw = 0;
+    for (auto& p : plan) {
+        place(*p.m, m.weights.as<uint8_t>());
+        max_bytes = std::max(max_bytes, p.m->bytes());
+        if (p.col_bytes) max_raw = std::max(max_raw, (size_t)p.col_bytes * p.m->rows);
+    }
+    std::vector<uint8_t> staging(max_bytes), rawbuf(max_raw);
+    const int threads = (int)std::max(1u, std::thread::hardware_concurrency());
+    for (auto& p : plan) {
+        const uint8_t* src = p.raw;
+        size_t stride = p.stride;
+        if (p.col_bytes) {  // gather the column shard into a contiguous buffer
+            for (uint32_t r = 0; r < p.m->rows; ++r)
+                std::memcpy(rawbuf.data() + (size_t)r * p.col_bytes, p.raw + (size_t)r * p.stride + p.col_byte0,
+                            p.col_bytes);
+            src = rawbuf.data();
+            stride = p.col_bytes;
+        }
+        repack_host(*p.m, src, stride, staging.data(), threads);
+        cuda_check(cudaMemcpy(m.weights.as<uint8_t>() + p.m->offset, staging.data(), p.m->bytes(),
+                              cudaMemcpyHostToDevice),
+                   "upload weights");
+    }
+    float* vbase = m.vectors.as<float>();
+    m.rope_inv_freq = vbase;
+    {
+        std::vector<float> inv(rope_floats, 0.f);
+        // src/runtime.rs:443 and :467: base.powf(-2i / rotary_dim), f32 powf
+        for (uint32_t i = 0; i < rdim / 2; ++i) inv[i] = powf(c.rope_base, (-2.0f * (float)i) / (float)rdim);
+        cuda_check(cudaMemcpy(vbase, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice), "upload rope table");
+    }
+    size_t voff = rope_floats;
+    DeviceBuffer tmp;
+    for (auto& v : vplan) {
+        const GgufTensor& t = g.tensor(v.name);
+        size_t nb;
+        const uint8_t* raw = g.raw(t, &nb);
+        float* dst = vbase + voff;
+        if (t.type == GGML_F32) {
+            cuda_check(cudaMemcpy(dst, raw, nb, cudaMemcpyHostToDevice), "upload norm");
+        } else {
+            if (tmp.bytes < nb) tmp.alloc(nb);
+            cuda_check(cudaMemcpy(tmp.p, raw, nb, cudaMemcpyHostToDevice), "upload norm");
+            cuda_check(launch_dequant_raw(t.type, tmp.p, v.n, dst, 0), "dequantize norm");
+        }
+        *v.dst = dst;
+        m.vecs[v.name] = {dst, (size_t)v.n};
+        voff += (v.n + 63) / 64 * 64;
+    }
+    cuda_check(cudaDeviceSynchronize(), "load");
+
+    // weight bytes one decode step streams on this rank
+    uint64_t wb = 0;
+    for (auto& L : m.layers)
+        wb += L.q.bytes() + L.k.bytes() + L.v.bytes() + L.o.bytes() + L.gate.bytes() + L.up.bytes() + L.down.bytes();
+    wb += m.lm_head.bytes();
+    m.weight_bytes_per_step = wb;
+
+    // ---- tensor-parallel communicator
+    if (T > 1) {
+        ncclUniqueId id;
+        static_assert(sizeof(id.internal) == 128, "ncclUniqueId size");
+        std::memcpy(id.internal, o.nccl_id, 128);
+        ncclResult_t r = ncclCommInitRank(&m.comm, T, id, R);
+        if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    }
+    cuda_check(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    const size_t sc = (size_t)c.dim * 3 + m.lffn + std::max<size_t>(c.dim, c.vocab) + 64;
+    m.scratch.alloc(sc * 4 + 256);
+    m.d_err = reinterpret_cast<int32_t*>(m.scratch.as<uint8_t>() + sc * 4);
+    cuda_check(cudaMemset(m.d_err, 0, 4), "memset");
+    return M;
+}
+
+void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s) {
+    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, m.comm, s);
+    if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+}
+
+void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
+                   float* h_buf, float* y_buf, cudaStream_t s, bool pdl) {
+    const LayerWeights& L = m.layers[layer];
+    const uint32_t dim = (uint32_t)m.cfg.dim;
+    for (uint32_t b = 0; b < batch; ++b) {
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = L.gate.dev;
+        a.seg[0].m2 = L.up.dev;
+        a.seg[0].y = h_buf + (size_t)b * m.lffn;
+        a.seg[0].epi = EPI_SWIGLU;
+        a.x = x + (size_t)b * dim;
+        a.cols = dim;
+        a.norm_w = norm_w;
+        a.eps = m.cfg.eps;
+        cuda_check(launch_qmatvec(a, s, pdl), "ffn gate/up");
+    }
+    const bool tp = m.tp_size > 1;
+    for (uint32_t b = 0; b < batch; ++b) {
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = L.down.dev;
+        a.seg[0].y = (tp ? y_buf : y) + (size_t)b * dim;
+        a.seg[0].epi = (add && !tp) ? EPI_ADD : EPI_STORE;
+        a.x = h_buf + (size_t)b * m.lffn;
+        a.cols = m.lffn;
+        cuda_check(launch_qmatvec(a, s, pdl), "ffn down");
+    }
+    if (tp) {
+        allreduce_sum(m, y_buf, (size_t)batch * dim, s);
+        if (add) {
+            cuda_check(launch_add(y, y_buf, (size_t)batch * dim, s, false), "residual add");
+        } else {
+            cuda_check(cudaMemcpyAsync(y, y_buf, (size_t)batch * dim * 4, cudaMemcpyDeviceToDevice, s), "copy");
+        }
+    }
+}
+
+}  // namespace evl

@@ -1,0 +1,146 @@
+// repack.cpp -- GGUF blocks -> the unit-interleaved device layout of common.cuh.
+//
+// The reference keeps each QMatrix as the raw GGUF bytes (src/runtime.rs:23-51) and
+// re-reads whole 144/210/34-byte blocks per row. On the GPU the matvec wants every
+// 128-bit load of a warp to be one contiguous 512-byte span, so each row's blocks
+// are split into 16-byte chunks grouped by 64-value unit (see common.cuh), with the
+// block headers moved to side arrays. Every byte of the original survives: the
+// exact dequantiser reads this layout back bit-for-bit (dequant.cuh).
+#include <algorithm>
+#include <cstring>
+#include <thread>
+
+#include "engine.hpp"
+
+namespace evl {
+
+void repack_sizes(QMatrix& m) {
+    const uint64_t rows = m.rows, cols = m.cols;
+    switch (m.type) {
+        case GGML_Q4_K:
+        case GGML_Q6_K:
+            if (cols % 256) raise(EVL_ERR_INVALID_DATA, m.name + ": row length is not a multiple of 256");
+            break;
+        case GGML_Q8_0:
+        case GGML_F16:
+        case GGML_BF16:
+        case GGML_F32:
+            if (cols % 64) raise(EVL_ERR_UNSUPPORTED, m.name + ": row length is not a multiple of 64");
+            break;
+        default:
+            raise(EVL_ERR_UNSUPPORTED, m.name + ": ggml type " + std::to_string(m.type) + " (" + type_name(m.type) +
+                                           ") is not supported for device matrices");
+    }
+    const uint64_t nunits = cols / 64, ch = chunks_per_unit(m.type);
+    m.payload_bytes = rows * nunits * ch * 16;
+    m.aux_bytes = 0;
+    m.d_bytes = 0;
+    switch (m.type) {
+        case GGML_Q4_K: m.aux_bytes = rows * (cols / 256) * 16; break;
+        case GGML_Q6_K:
+            m.aux_bytes = rows * nunits * 4;
+            m.d_bytes = rows * (cols / 256) * 2;
+            break;
+        case GGML_Q8_0: m.aux_bytes = rows * nunits * 4; break;
+        default: break;
+    }
+    // keep each section 256-byte aligned inside the model buffer
+    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+    m.payload_bytes = up(m.payload_bytes);
+    m.aux_bytes = up(m.aux_bytes);
+    m.d_bytes = up(m.d_bytes);
+    m.dev.type = m.type;
+    m.dev.rows = m.rows;
+    m.dev.cols = m.cols;
+    m.dev.nunits = (uint32_t)nunits;
+}
+
+void place(QMatrix& m, uint8_t* base) {
+    uint8_t* p = base + m.offset;
+    m.dev.q = p;
+    m.dev.aux = m.aux_bytes ? p + m.payload_bytes : nullptr;
+    m.dev.d = m.d_bytes ? reinterpret_cast<const uint16_t*>(p + m.payload_bytes + m.aux_bytes) : nullptr;
+}
+
+namespace {
+
+void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* dst, uint32_t r0, uint32_t r1) {
+    const uint32_t nunits = m.cols / 64, ch = chunks_per_unit(m.type), nb = m.cols / 256;
+    const size_t row_payload = (size_t)nunits * ch * 16;
+    uint8_t* payload = dst;
+    uint8_t* aux = dst + m.payload_bytes;
+    uint8_t* dd = aux + m.aux_bytes;
+    for (uint32_t r = r0; r < r1; ++r) {
+        const uint8_t* src = raw + (size_t)r * stride;
+        uint8_t* prow = payload + (size_t)r * row_payload;
+        switch (m.type) {
+            case GGML_Q4_K:
+                for (uint32_t sb = 0; sb < nb; ++sb) {
+                    const uint8_t* blk = src + (size_t)sb * 144;
+                    std::memcpy(aux + ((size_t)r * nb + sb) * 16, blk, 16);
+                    for (uint32_t j = 0; j < 4; ++j)
+                        for (uint32_t c = 0; c < 2; ++c)
+                            std::memcpy(prow + chunk_offset(nunits, 2, sb * 4 + j, c), blk + 16 + 32 * j + 16 * c, 16);
+                }
+                break;
+            case GGML_Q6_K:
+                for (uint32_t sb = 0; sb < nb; ++sb) {
+                    const uint8_t* blk = src + (size_t)sb * 210;
+                    const uint8_t* ql = blk;
+                    const uint8_t* qh = blk + 128;
+                    const uint8_t* sc = blk + 192;
+                    std::memcpy(dd + ((size_t)r * nb + sb) * 2, blk + 208, 2);
+                    for (uint32_t h = 0; h < 2; ++h)
+                        for (uint32_t b = 0; b < 2; ++b) {
+                            const uint32_t u = sb * 4 + h * 2 + b, l0 = 16 * b;
+                            std::memcpy(prow + chunk_offset(nunits, 3, u, 0), ql + 64 * h + l0, 16);
+                            std::memcpy(prow + chunk_offset(nunits, 3, u, 1), ql + 64 * h + 32 + l0, 16);
+                            std::memcpy(prow + chunk_offset(nunits, 3, u, 2), qh + 32 * h + l0, 16);
+                            uint8_t w[4];
+                            for (uint32_t k = 0; k < 4; ++k) w[k] = sc[8 * h + b + 2 * k];
+                            std::memcpy(aux + ((size_t)r * nunits + u) * 4, w, 4);
+                        }
+                }
+                break;
+            case GGML_Q8_0:
+                for (uint32_t u = 0; u < nunits; ++u) {
+                    const uint8_t* b0 = src + (size_t)(2 * u) * 34;
+                    const uint8_t* b1 = b0 + 34;
+                    std::memcpy(prow + chunk_offset(nunits, 4, u, 0), b0 + 2, 16);
+                    std::memcpy(prow + chunk_offset(nunits, 4, u, 1), b0 + 18, 16);
+                    std::memcpy(prow + chunk_offset(nunits, 4, u, 2), b1 + 2, 16);
+                    std::memcpy(prow + chunk_offset(nunits, 4, u, 3), b1 + 18, 16);
+                    uint8_t w[4] = {b0[0], b0[1], b1[0], b1[1]};
+                    std::memcpy(aux + ((size_t)r * nunits + u) * 4, w, 4);
+                }
+                break;
+            default: {  // F16 / BF16 / F32: plain values, chunked
+                const uint32_t eb = m.type == GGML_F32 ? 4 : 2;
+                for (uint32_t u = 0; u < nunits; ++u)
+                    for (uint32_t c = 0; c < ch; ++c)
+                        std::memcpy(prow + chunk_offset(nunits, ch, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
+            }
+        }
+    }
+}
+
+}  // namespace
+
+void repack_host(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* dst, int threads) {
+    std::memset(dst, 0, m.bytes());
+    threads = std::max(1, std::min<int>(threads, (int)(m.rows / 64) + 1));
+    if (threads == 1) {
+        repack_rows(m, raw, stride, dst, 0, m.rows);
+        return;
+    }
+    std::vector<std::thread> ts;
+    const uint32_t per = (m.rows + threads - 1) / threads;
+    for (int t = 0; t < threads; ++t) {
+        const uint32_t a = t * per, b = std::min<uint32_t>(m.rows, a + per);
+        if (a >= b) break;
+        ts.emplace_back([&, a, b] { repack_rows(m, raw, stride, dst, a, b); });
+    }
+    for (auto& t : ts) t.join();
+}
+
+}  // namespace evl

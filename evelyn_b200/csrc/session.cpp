@@ -1,0 +1,379 @@
+// session.cpp -- Session::step on the device (src/runtime.rs:634-808).
+//
+// One dense step is a fixed launch sequence over device-resident state:
+//   embed row -> per layer { RMSNorm+QKV matvec (one launch over Wq, Wk, Wv),
+//   QK-norm + RoPE + paged-KV append, split-K GQA attention + merge,
+//   o-proj matvec with the residual add fused, RMSNorm + gate/up matvec with the
+//   SwiGLU fused, down matvec with the residual add fused } -> final RMSNorm +
+//   LM-head matvec -> argmax (which also feeds the next token and advances pos).
+// Token, position and page table live in device memory, so the sequence is
+// captured once as a CUDA graph (with programmatic dependent launches between
+// kernels) and replayed every step. Layers routed through an FfnBackend hook
+// (runtime.rs:801-804) break the graph: the step then runs eagerly and crosses to
+// the host only at those layers.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "engine.hpp"
+
+namespace evl {
+
+namespace {
+constexpr uint32_t kPageSize = 16;
+
+// One launch of a fused matvec per sequence.
+void matvec_each(const MatvecArgs& base, uint32_t batch, uint64_t x_stride, const uint64_t* y_strides, cudaStream_t s,
+                 bool pdl, const char* what) {
+    for (uint32_t bi = 0; bi < batch; ++bi) {
+        MatvecArgs a = base;
+        a.x = base.x + bi * x_stride;
+        for (int k = 0; k < a.nseg; ++k) a.seg[k].y = base.seg[k].y + bi * y_strides[k];
+        cuda_check(launch_qmatvec(a, s, pdl), what);
+    }
+}
+}  // namespace
+
+Decoder::~Decoder() {
+    if (model) {
+        DeviceGuard g(model->device);
+        if (graph) cudaGraphExecDestroy(graph);
+        if (stream) cudaStreamDestroy(stream);
+    }
+}
+
+void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
+    model = m;
+    const Config& c = m->cfg;
+    if (batch == 0) raise(EVL_ERR_INVALID_INPUT, "batch must be at least 1");
+    if (max_ctx == 0) raise(EVL_ERR_INVALID_INPUT, "max_ctx must be at least 1");
+    b.batch = batch;
+    b.max_ctx = max_ctx;
+    b.pages_per_seq = (max_ctx + kPageSize - 1) / kPageSize;
+    const uint64_t hd = c.head_dim, L = c.layers;
+    const uint64_t elem = m->kv_f32 ? 4 : 2;
+    const uint64_t head_stride = (uint64_t)kPageSize * hd * elem;
+    const uint64_t layer_stride = 2ull * m->lkv_heads * head_stride;
+    const uint64_t page_stride = L * layer_stride;
+    const uint64_t pages = (uint64_t)batch * b.pages_per_seq;
+    b.kv.alloc(pages * page_stride);
+    kv.pool = b.kv.p;
+    kv.page_stride = page_stride;
+    kv.layer_stride = layer_stride;
+    kv.head_stride = head_stride;
+    kv.v_offset = (int64_t)(m->lkv_heads * head_stride);
+    kv.page_size = kPageSize;
+    kv.elem_bytes = (uint32_t)elem;
+    {  // every sequence owns a contiguous run of pages
+        std::vector<int32_t> pt(pages);
+        for (uint64_t i = 0; i < pages; ++i) pt[i] = (int32_t)i;
+        b.page_table.alloc(pages * 4);
+        cuda_check(cudaMemcpy(b.page_table.p, pt.data(), pages * 4, cudaMemcpyHostToDevice), "page table");
+    }
+    const uint64_t qw = (uint64_t)m->lheads * hd, kw = (uint64_t)m->lkv_heads * hd;
+    b.pos.alloc(batch * 4);
+    b.tokens.alloc(batch * 4);
+    b.argmax.alloc(batch * 4);
+    b.hist.alloc((uint64_t)batch * max_ctx * 4);
+    b.err.alloc(4);
+    cuda_check(cudaMemset(b.pos.p, 0, batch * 4), "memset");
+    cuda_check(cudaMemset(b.tokens.p, 0, batch * 4), "memset");
+    cuda_check(cudaMemset(b.err.p, 0, 4), "memset");
+    b.x.alloc(batch * c.dim * 4);
+    b.q.alloc(batch * qw * 4);
+    b.k.alloc(batch * kw * 4);
+    b.v.alloc(batch * kw * 4);
+    b.att.alloc(batch * qw * 4);
+    b.h.alloc((uint64_t)batch * m->lffn * 4);
+    b.y.alloc(batch * std::max<uint64_t>(c.dim, m->lvocab) * 4);
+    b.logits.alloc(batch * c.vocab * 4);
+    b.xn.alloc(batch * c.dim * 4);
+    // enough (kv_head, split) CTAs to cover the SMs twice
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+    const uint32_t want = (uint32_t)(2 * sms) / std::max<uint32_t>(1, m->lkv_heads * batch);
+    b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>(want, 1), b.pages_per_seq));
+    b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
+    b.amax_parts = (uint32_t)sms;
+    b.amax_v.alloc((uint64_t)batch * b.amax_parts * 4);
+    b.amax_i.alloc((uint64_t)batch * b.amax_parts * 4);
+    b.h_tokens.alloc(batch * 4);
+    b.h_argmax.alloc(batch * 4);
+    b.h_logits.alloc(batch * c.vocab * 4);
+    b.h_xn.alloc(c.dim * 4);
+    b.h_y.alloc(c.dim * 4);
+    b.h_err.alloc(4);
+    *b.h_err.as<int>() = 0;
+    cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    host_pos.assign(batch, 0);
+}
+
+void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const LayerWeights& L = m.layers[li];
+    const uint32_t B = b.batch;
+    const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd, kw = (uint64_t)m.lkv_heads * hd;
+    float* x = b.x.as<float>();
+    {  // attn RMSNorm + Q/K/V in one launch
+        MatvecArgs a;
+        a.nseg = 3;
+        a.seg[0].m = L.q.dev;
+        a.seg[0].y = b.q.as<float>();
+        a.seg[1].m = L.k.dev;
+        a.seg[1].y = b.k.as<float>();
+        a.seg[2].m = L.v.dev;
+        a.seg[2].y = b.v.as<float>();
+        a.x = x;
+        a.cols = (uint32_t)c.dim;
+        a.norm_w = L.attn_norm;
+        a.eps = c.eps;
+        const uint64_t ys[3] = {qw, kw, kw};
+        matvec_each(a, B, c.dim, ys, stream, pdl, "qkv matvec");
+        kernels += B;
+    }
+    RopeArgs r;
+    r.q = b.q.as<float>();
+    r.k = b.k.as<float>();
+    r.v = b.v.as<float>();
+    r.q_norm = L.q_norm;
+    r.k_norm = L.k_norm;
+    r.kv = kv;
+    r.layer = li;
+    r.page_table = b.page_table.as<int32_t>();
+    r.max_pages = b.pages_per_seq;
+    r.pos = b.pos.as<int32_t>();
+    r.batch = B;
+    r.heads = m.lheads;
+    r.kv_heads = m.lkv_heads;
+    r.head_dim = (uint32_t)hd;
+    r.rope_dim = (uint32_t)c.rope_dim;
+    r.rope_base = c.rope_base;
+    r.eps = c.eps;
+    r.interleaved = c.rope_interleaved;
+    r.rope_inv_freq = m.rope_inv_freq;
+    r.err = b.err.as<int>();
+    cuda_check(launch_qk_norm_rope_append(r, stream, pdl), "qk-norm/rope/append");
+    kernels += 1;
+    AttnArgs at;
+    at.q = b.q.as<float>();
+    at.out = b.att.as<float>();
+    at.kv = kv;
+    at.layer = li;
+    at.page_table = b.page_table.as<int32_t>();
+    at.max_pages = b.pages_per_seq;
+    at.pos = b.pos.as<int32_t>();
+    at.batch = B;
+    at.heads = m.lheads;
+    at.kv_heads = m.lkv_heads;
+    at.head_dim = (uint32_t)hd;
+    at.nsplit = b.nsplit;
+    at.part = b.part.as<float>();
+    at.scale = 1.0f / sqrtf((float)hd);
+    at.err = b.err.as<int>();
+    cuda_check(launch_attention(at, stream, pdl), "attention");
+    kernels += 2;
+    {  // o-proj, residual add fused (TP: partial sums, all-reduce, then add)
+        const bool tp = m.tp_size > 1;
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = L.o.dev;
+        a.seg[0].y = tp ? b.y.as<float>() : x;
+        a.seg[0].epi = tp ? EPI_STORE : EPI_ADD;
+        a.x = b.att.as<float>();
+        a.cols = (uint32_t)qw;
+        const uint64_t ys[1] = {c.dim};
+        matvec_each(a, B, qw, ys, stream, pdl, "o-proj matvec");
+        kernels += B;
+        if (tp) {
+            allreduce_sum(m, b.y.as<float>(), (size_t)B * c.dim, stream);
+            cuda_check(launch_add(x, b.y.as<float>(), (size_t)B * c.dim, stream, false), "residual add");
+            kernels += 1;
+        }
+    }
+}
+
+void Decoder::enqueue_head(bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const uint32_t B = b.batch;
+    const bool tp = m.tp_size > 1;
+    MatvecArgs a;
+    a.nseg = 1;
+    a.seg[0].m = m.lm_head.dev;
+    a.seg[0].y = tp ? b.y.as<float>() : b.logits.as<float>();
+    a.x = b.x.as<float>();
+    a.cols = (uint32_t)c.dim;
+    a.norm_w = m.out_norm;
+    a.eps = c.eps;
+    const uint64_t ys[1] = {tp ? (uint64_t)m.lvocab : c.vocab};
+    matvec_each(a, B, c.dim, ys, stream, pdl, "lm-head matvec");
+    kernels += B;
+    if (tp) {  // vocabulary shards -> full logits on every rank
+        const uint64_t V = c.vocab;
+        ncclGroupStart();
+        for (int r = 0; r < m.tp_size; ++r) {
+            const uint64_t base = V / m.tp_size, rem = V % m.tp_size;
+            const uint64_t lo = r * base + std::min<uint64_t>(r, rem), n = base + (r < (int)rem ? 1 : 0);
+            for (uint32_t bi = 0; bi < B; ++bi)
+                ncclBroadcast(b.y.as<float>() + (uint64_t)bi * m.lvocab, b.logits.as<float>() + bi * V + lo, n,
+                              ncclFloat32, r, m.comm, stream);
+        }
+        ncclResult_t rr = ncclGroupEnd();
+        if (rr != ncclSuccess) raise(EVL_ERR_NCCL, std::string("logits gather: ") + ncclGetErrorString(rr));
+    }
+    cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, B, b.amax_v.as<float>(), b.amax_i.as<int32_t>(),
+                             b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),
+                             b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
+               "argmax");
+    kernels += 2;
+}
+
+void Decoder::enqueue_dense(bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    kernels = 0;
+    cuda_check(launch_embed(m.embed.dev, b.tokens.as<int32_t>(), b.batch, b.x.as<float>(), b.err.as<int32_t>(), stream,
+                            pdl),
+               "embed");
+    kernels += 1;
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        enqueue_layer_attention(li, pdl);
+        run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch, b.h.as<float>(),
+                      b.y.as<float>(), stream, pdl);
+        kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);
+    }
+    enqueue_head(pdl);
+    kernels_per_step = kernels;
+}
+
+void Decoder::run_routed(const evl_ffn_backend& ffn) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    if (b.batch != 1) raise(EVL_ERR_UNSUPPORTED, "FFN routing is available for single sessions");
+    if (m.tp_size > 1) raise(EVL_ERR_UNSUPPORTED, "FFN routing with tensor parallelism is not supported");
+    const bool pdl = false;
+    float* x = b.x.as<float>();
+    cuda_check(launch_embed(m.embed.dev, b.tokens.as<int32_t>(), 1, x, b.err.as<int32_t>(), stream, pdl), "embed");
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        enqueue_layer_attention(li, pdl);
+        const bool routed = ffn.ffn && (!ffn.routed || (li < ffn.routed_len && ffn.routed[li]));
+        if (!routed) {
+            run_dense_ffn(m, li, x, m.layers[li].ffn_norm, x, true, 1, b.h.as<float>(), b.y.as<float>(), stream, pdl);
+            continue;
+        }
+        // Model::ffn_input (runtime.rs:801), then the backend on the host
+        float* xn = b.xn.as<float>();
+        cuda_check(launch_rmsnorm(x, m.layers[li].ffn_norm, xn, (uint32_t)c.dim, 1, c.eps, stream, pdl), "ffn norm");
+        cuda_check(cudaMemcpyAsync(b.h_xn.p, xn, c.dim * 4, cudaMemcpyDeviceToHost, stream), "D2H ffn input");
+        cuda_check(cudaStreamSynchronize(stream), "sync");
+        const int rc = ffn.ffn(ffn.ctx, li, b.h_xn.as<float>(), c.dim, b.h_y.as<float>());
+        if (rc == 0) {
+            cuda_check(cudaMemcpyAsync(b.y.p, b.h_y.p, c.dim * 4, cudaMemcpyHostToDevice, stream), "H2D ffn output");
+            cuda_check(launch_add(x, b.y.as<float>(), c.dim, stream, pdl), "residual add");
+        } else {
+            if (rc != EVL_FFN_DENSE && ffn.fallbacks) *ffn.fallbacks += 1;
+            run_dense_ffn(m, li, xn, nullptr, x, true, 1, b.h.as<float>(), b.y.as<float>(), stream, pdl);
+        }
+    }
+    enqueue_head(pdl);
+}
+
+void Decoder::launch_graph() {
+    if (!graph) {
+        for (int attempt = 0; attempt < 2 && !graph; ++attempt) {
+            const bool pdl = attempt == 0;
+            cudaGraph_t g = nullptr;
+            cuda_check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+            try {
+                enqueue_dense(pdl);
+            } catch (...) {
+                cudaStreamEndCapture(stream, &g);
+                if (g) cudaGraphDestroy(g);
+                throw;
+            }
+            cuda_check(cudaStreamEndCapture(stream, &g), "end capture");
+            cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                graph = nullptr;
+                if (attempt == 1) cuda_check(e, "graph instantiate");
+            }
+            graph_pdl = pdl;
+        }
+    }
+    cuda_check(cudaGraphLaunch(graph, stream), "graph launch");
+}
+
+void Decoder::check_device_error() {
+    const int e = *b.h_err.as<int>();
+    if (e == DEV_OK) return;
+    *b.h_err.as<int>() = 0;
+    cudaMemsetAsync(b.err.p, 0, 4, stream);
+    cudaStreamSynchronize(stream);
+    switch (e) {
+        case DEV_ERR_TOKEN: raise(EVL_ERR_INVALID_INPUT, "token ID outside the model vocabulary");
+        case DEV_ERR_POSITION: raise(EVL_ERR_INVALID_INPUT, "position outside the session's KV cache");
+        case DEV_ERR_WAIT_TIMEOUT: raise(EVL_ERR_TIMEOUT, "a device wait for KV pages timed out");
+        default: raise(EVL_ERR_CUDA, "device error " + std::to_string(e));
+    }
+}
+
+void Decoder::step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* logits_out, uint32_t* argmax_out) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    DeviceGuard g(m.device);
+    for (uint32_t i = 0; i < b.batch; ++i) {
+        if (tokens[i] >= c.vocab)
+            raise(EVL_ERR_INVALID_INPUT, "token ID " + std::to_string(tokens[i]) + " is outside model vocabulary (" +
+                                             std::to_string(c.vocab) + "); check that tokenizer and GGUF match");
+        if (host_pos[i] >= b.max_ctx)
+            raise(EVL_ERR_INVALID_INPUT, "session context is full (" + std::to_string(b.max_ctx) + " positions)");
+    }
+    std::memcpy(b.h_tokens.p, tokens, b.batch * 4);
+    cuda_check(cudaMemcpyAsync(b.tokens.p, b.h_tokens.p, b.batch * 4, cudaMemcpyHostToDevice, stream), "H2D tokens");
+    if (ffn && ffn->ffn) {
+        run_routed(*ffn);
+    } else {
+        launch_graph();
+    }
+    if (logits_out)
+        cuda_check(cudaMemcpyAsync(b.h_logits.p, b.logits.p, (size_t)b.batch * c.vocab * 4, cudaMemcpyDeviceToHost,
+                                   stream),
+                   "D2H logits");
+    if (argmax_out)
+        cuda_check(cudaMemcpyAsync(b.h_argmax.p, b.argmax.p, b.batch * 4, cudaMemcpyDeviceToHost, stream), "D2H argmax");
+    cuda_check(cudaMemcpyAsync(b.h_err.p, b.err.p, 4, cudaMemcpyDeviceToHost, stream), "D2H error flag");
+    cuda_check(cudaStreamSynchronize(stream), "step");
+    check_device_error();
+    for (auto& p : host_pos) ++p;
+    if (logits_out) std::memcpy(logits_out, b.h_logits.p, (size_t)b.batch * c.vocab * 4);
+    if (argmax_out) std::memcpy(argmax_out, b.h_argmax.p, b.batch * 4);
+}
+
+void Decoder::generate(uint32_t token, uint32_t n, uint32_t* tokens_out) {
+    Model& m = *model;
+    DeviceGuard g(m.device);
+    if (b.batch != 1) raise(EVL_ERR_INVALID_INPUT, "generate drives a single sequence");
+    if (token >= m.cfg.vocab)
+        raise(EVL_ERR_INVALID_INPUT, "token ID " + std::to_string(token) + " is outside model vocabulary (" +
+                                         std::to_string(m.cfg.vocab) + "); check that tokenizer and GGUF match");
+    if (host_pos[0] + n > b.max_ctx)
+        raise(EVL_ERR_INVALID_INPUT, "session context is full (" + std::to_string(b.max_ctx) + " positions)");
+    if (n == 0) return;
+    const uint64_t p0 = host_pos[0];
+    *b.h_tokens.as<uint32_t>() = token;
+    cuda_check(cudaMemcpyAsync(b.tokens.p, b.h_tokens.p, 4, cudaMemcpyHostToDevice, stream), "H2D token");
+    for (uint32_t i = 0; i < n; ++i) launch_graph();
+    std::vector<int32_t> hist(n);
+    cuda_check(cudaMemcpyAsync(hist.data(), b.hist.as<int32_t>() + p0, n * 4, cudaMemcpyDeviceToHost, stream),
+               "D2H tokens");
+    cuda_check(cudaMemcpyAsync(b.h_err.p, b.err.p, 4, cudaMemcpyDeviceToHost, stream), "D2H error flag");
+    cuda_check(cudaStreamSynchronize(stream), "generate");
+    check_device_error();
+    host_pos[0] += n;
+    for (uint32_t i = 0; i < n; ++i) tokens_out[i] = (uint32_t)hist[i];
+}
+
+}  // namespace evl

@@ -1,0 +1,198 @@
+/*
+ * evelyn.h -- C ABI of the B200 decode engine for Evelyn's token loop.
+ *
+ * Every entry point is a drop-in for one item of the reference's Rust runtime
+ * API (paths below are inside the neuralmimicry/evelyn tree). A Rust FFI crate
+ * binds these one-to-one; INTEGRATION.md shows the binding.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. "host" buffers are ordinary CPU memory;
+ *     "device" buffers are CUDA device pointers on the model's device.
+ *   - Every call returns an evl_status. On failure evl_last_error() holds a
+ *     message (thread-local). Status codes map one-to-one to the io::ErrorKind
+ *     values the reference returns (src/gguf.rs, src/runtime.rs).
+ *   - No CPU fallback exists: without a usable CUDA device every call that
+ *     needs one fails with EVL_ERR_CUDA.
+ */
+#ifndef EVELYN_H
+#define EVELYN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EVL_ABI_VERSION 1
+
+typedef enum evl_status {
+    EVL_OK = 0,
+    EVL_ERR_INVALID_INPUT = 1, /* io::ErrorKind::InvalidInput (runtime.rs:125-135, :55-63) */
+    EVL_ERR_INVALID_DATA = 2,  /* io::ErrorKind::InvalidData  (bad GGUF, shapes, metadata) */
+    EVL_ERR_NOT_FOUND = 3,     /* io::ErrorKind::NotFound     (gguf.rs:203-205) */
+    EVL_ERR_UNSUPPORTED = 4,   /* io::ErrorKind::Unsupported  (gguf.rs:280-285) */
+    EVL_ERR_IO = 5,            /* any other io::Error (file access, short reads) */
+    EVL_ERR_CUDA = 6,          /* CUDA runtime / device error (no CPU counterpart) */
+    EVL_ERR_OUT_OF_MEMORY = 7, /* device or pinned-host allocation failed */
+    EVL_ERR_NCCL = 8,          /* tensor-parallel collective failed */
+    EVL_ERR_TIMEOUT = 9        /* a bounded device wait gave up */
+} evl_status;
+
+typedef struct evl_model evl_model;
+typedef struct evl_session evl_session;
+typedef struct evl_batch evl_batch;
+typedef struct evl_qmatrix evl_qmatrix;
+typedef struct evl_remote_ffn evl_remote_ffn;
+
+/* Mirrors `pub struct Config` (src/runtime.rs:93-110) for the dense-attention path. */
+typedef struct evl_config {
+    char arch[64];
+    uint64_t layers, dim, ffn, heads, kv_heads, head_dim, rope_dim, vocab;
+    float rope_base, eps;
+    int32_t rope_interleaved;
+    int64_t eos_token_id; /* -1 when the GGUF has none */
+} evl_config;
+
+typedef struct evl_model_options {
+    uint32_t struct_size; /* sizeof(evl_model_options) */
+    int32_t device;       /* CUDA device ordinal; -1 = the calling thread's current device */
+    int32_t tp_rank;      /* tensor-parallel rank in [0, tp_size) */
+    int32_t tp_size;      /* 1 = one GPU; 2/4/8 = Megatron split over that many ranks */
+    uint8_t nccl_id[128]; /* evl_tp_unique_id() of rank 0, shared with every rank (tp_size > 1) */
+    uint32_t kv_f32;      /* 1: keep the KV cache in f32 like the reference; 0: f16 pages */
+    uint32_t reserved[7];
+} evl_model_options;
+
+/* FfnBackend (src/runtime.rs:138-140). `ffn` receives the normalised FFN input x of
+ * width n (what Model::ffn_input returns, runtime.rs:422) in host memory and writes
+ * the FFN output y (width n). Return values:
+ *   0             y holds the answer (RemoteAarnnFfn success, remote.rs:253);
+ *   EVL_FFN_DENSE run the model's dense FFN for this layer on the device (DenseFfn,
+ *                 CaptureFfn: runtime.rs:428-434, remote.rs:35-45);
+ *   anything else failure: the engine runs the dense FFN and increments
+ *                 *fallbacks (the fallback of remote.rs:254-268).
+ * `routed[layer] != 0` selects the layers that call `ffn`; the others stay dense on
+ * the device with no host round trip. routed == NULL routes every layer. */
+#define EVL_FFN_DENSE 1
+typedef int (*evl_ffn_fn)(void* ctx, size_t layer, const float* x, size_t n, float* y);
+typedef struct evl_ffn_backend {
+    evl_ffn_fn ffn;
+    void* ctx;
+    const uint8_t* routed;
+    size_t routed_len;
+    uint64_t* fallbacks; /* optional */
+} evl_ffn_backend;
+
+/* ------------------------------------------------------------------ library */
+const char* evl_last_error(void);
+uint32_t evl_abi_version(void);
+void evl_model_options_init(evl_model_options* opts);
+/* validate_token_ids (src/runtime.rs:125-135) */
+evl_status evl_validate_token_ids(const uint32_t* ids, size_t n, size_t vocab);
+/* argmax (src/runtime.rs:897-905): first maximum, strict '>' from f32::MIN. host */
+uint32_t evl_argmax(const float* logits, size_t n);
+/* log_prob (src/runtime.rs:908-912). host */
+float evl_log_prob(const float* logits, size_t n, uint32_t target);
+/* ncclGetUniqueId for tensor parallelism: rank 0 calls it and shares the bytes. */
+evl_status evl_tp_unique_id(uint8_t out[128]);
+
+/* ------------------------------------------------------------------ model */
+/* Model::load (src/runtime.rs:199-406). Weights stay quantised, repacked in HBM. */
+evl_status evl_model_load(const char* path, const evl_model_options* opts, evl_model** out);
+/* Same, from a GGUF image already in host memory (not retained after return). */
+evl_status evl_model_load_memory(const void* data, size_t len, const evl_model_options* opts, evl_model** out);
+void evl_model_free(evl_model* model);
+/* Model.cfg (src/runtime.rs:185) */
+evl_status evl_model_config(const evl_model* model, evl_config* out);
+/* Model::dense_ffn (src/runtime.rs:409-418): host x[dim] -> host y[dim], on the device.
+ * With tp_size > 1 every rank must make the same call (it runs a collective). */
+evl_status evl_model_dense_ffn(evl_model* model, size_t layer, const float* x, float* y);
+/* Model::ffn_input (src/runtime.rs:422-424): rms_norm(x, ffn_norm). host -> host */
+evl_status evl_model_ffn_input(evl_model* model, size_t layer, const float* x, float* y);
+/* Gguf::tensor_f32 (src/gguf.rs:199-215) of a model tensor, dequantised exactly on the
+ * device from the repacked weights. n must equal the element count (this rank's shard
+ * under tensor parallelism). host out */
+evl_status evl_model_dequantize(evl_model* model, const char* tensor, float* out, size_t n);
+/* QMatrix::matvec (src/runtime.rs:72-88) of one model matrix. host x[cols] -> host y[rows] */
+evl_status evl_model_matvec(evl_model* model, const char* tensor, const float* x, size_t xn, float* y, size_t yn);
+/* Bytes of quantised weights one decode step streams from HBM on this rank. */
+uint64_t evl_model_weight_bytes(const evl_model* model);
+
+/* ------------------------------------------------------------------ session (one sequence) */
+/* Session::new (src/runtime.rs:643-660); max_ctx bounds the paged KV cache. */
+evl_status evl_session_new(evl_model* model, uint32_t max_ctx, evl_session** out);
+void evl_session_free(evl_session* s);
+/* Session.pos (src/runtime.rs:639) */
+uint64_t evl_session_pos(const evl_session* s);
+/* Session::step (src/runtime.rs:773-808). ffn == NULL is DenseFfn on every layer.
+ * logits_out (host, vocab floats) and argmax_out (host) are each optional. */
+evl_status evl_session_step(evl_session* s, uint32_t token, const evl_ffn_backend* ffn, float* logits_out,
+                            uint32_t* argmax_out);
+/* The greedy loop of src/bin/evelyn-generate.rs:81-86 without host round trips:
+ * feeds `token`, then n-1 times the argmax of the previous step; tokens_out[i] is the
+ * argmax after step i (n entries, host). Dense FFN on every layer. */
+evl_status evl_session_generate(evl_session* s, uint32_t token, uint32_t n, uint32_t* tokens_out);
+/* Device CUDA stream the session launches on (cudaStream_t), for event timing. */
+void* evl_session_stream(evl_session* s);
+/* Number of engine kernels one dense step launches (known after the first step). */
+uint32_t evl_session_kernels_per_step(const evl_session* s);
+
+/* ------------------------------------------------------------------ batched decode */
+/* n_seqs independent Sessions stepped together (one token each per step), sharing
+ * every weight read. Dense FFN on every layer. */
+evl_status evl_batch_new(evl_model* model, uint32_t n_seqs, uint32_t max_ctx, evl_batch** out);
+void evl_batch_free(evl_batch* b);
+uint64_t evl_batch_pos(const evl_batch* b, uint32_t seq);
+/* tokens[n_seqs] (host) in; logits_out [n_seqs][vocab] and argmax_out [n_seqs], both optional (host). */
+evl_status evl_batch_step(evl_batch* b, const uint32_t* tokens, float* logits_out, uint32_t* argmax_out);
+void* evl_batch_stream(evl_batch* b);
+
+/* ------------------------------------------------------------------ kernels on caller buffers */
+/* dequantize (src/gguf.rs:338-430) of raw GGUF blocks: d_raw holds type_bytes(type, n)
+ * bytes; d_out receives n floats. Bit-exact. device pointers; stream may be NULL. */
+evl_status evl_dequantize_raw(uint32_t ggml_type, const void* d_raw, size_t n, float* d_out, void* stream);
+/* A standalone quantised matrix (QMatrix, src/runtime.rs:23-51) built from host GGUF
+ * bytes [rows][type_bytes(type, cols)] on `device`. */
+evl_status evl_qmatrix_create(uint32_t ggml_type, uint32_t rows, uint32_t cols, const void* host_raw, int device,
+                              evl_qmatrix** out);
+void evl_qmatrix_free(evl_qmatrix* m);
+uint64_t evl_qmatrix_bytes(const evl_qmatrix* m);
+/* y = W x (QMatrix::matvec, runtime.rs:72-88). device pointers; stream may be NULL */
+evl_status evl_qmatrix_matvec(const evl_qmatrix* m, const float* d_x, float* d_y, void* stream);
+/* exact dequantisation of all rows to d_out [rows][cols]. device pointers */
+evl_status evl_qmatrix_dequantize(const evl_qmatrix* m, float* d_out, void* stream);
+/* GQA decode attention for one new position (the attention core of full_attention,
+ * runtime.rs:723-766) over a paged KV cache of f16 rows:
+ *   d_q        [heads][head_dim] f32, already normed and rotated
+ *   d_k_pages  [n_pages][kv_heads][page_size][head_dim] f16, likewise d_v_pages
+ *   d_page_table [ceil(t / page_size)] int32 page ids, t = positions to attend
+ *   d_out      [heads][head_dim] f32
+ * head_dim must be 64 or 128 and page_size 16. Allocates its split scratch per call
+ * and synchronises `stream` before returning. */
+evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
+                                const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
+                                uint32_t head_dim, uint32_t page_size, float* d_out, void* stream);
+
+/* ------------------------------------------------------------------ AARNN routing (src/remote.rs) */
+typedef struct evl_endpoint_stats { /* EndpointStats, remote.rs:13-24 */
+    uint64_t calls, failures, retries;
+    uint64_t total_ns, max_ns;
+} evl_endpoint_stats;
+/* RemoteAarnnFfn::new (remote.rs:185-205): layers[i] is served by the AARNN region at
+ * addrs[i] ("host:port") over the wire protocol of remote.rs:69-111, with one
+ * reconnect and a dense fallback; timeout_ms is the read timeout. */
+evl_status evl_remote_ffn_new(evl_model* model, size_t n, const size_t* layers, const char* const* addrs,
+                              uint32_t timeout_ms, evl_remote_ffn** out);
+void evl_remote_ffn_free(evl_remote_ffn* r);
+/* The evl_ffn_backend that routes the configured layers through `r`. */
+evl_status evl_remote_ffn_backend(evl_remote_ffn* r, evl_ffn_backend* out);
+/* RemoteAarnnFfn.fallbacks (remote.rs:166) */
+uint64_t evl_remote_ffn_fallbacks(const evl_remote_ffn* r);
+/* endpoint_stats (remote.rs:236-244) for one routed layer */
+evl_status evl_remote_ffn_stats(const evl_remote_ffn* r, size_t layer, evl_endpoint_stats* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EVELYN_H */
