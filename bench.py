@@ -1,0 +1,353 @@
+#!/usr/bin/env python3
+"""Decode benchmark: Qwen3-8B-shape Q4_K_M-mix synthetic GGUF, batch 1, 512-token
+random prompt then greedy decode (ctx up to 512 + warmup + steps).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode token through every layer (embedding, 36 x {RMSNorm+QKV,
+QK-norm+RoPE+KV append, paged GQA attention, o-proj+residual, RMSNorm+gate/up+SwiGLU,
+down+residual}, final norm, LM head, argmax). With N > 1 (torchrun) the model is
+tensor-parallel over N GPUs (Megatron split, NCCL all-reduce after o-proj and down).
+
+Printed JSON (rank 0): value = tok/s timed on the device with CUDA events on the
+session stream, weights and KV resident in HBM, inputs larger than L2 (5 GB of
+weights per step); e2e = the same through evl_session_step with host buffers
+(token H2D, logits + argmax D2H every step); roofline = the dominant kernel
+(Q4_K dequant-matvec of the ffn_gate shape 12288x4096) timed live; cpu_baseline =
+the CPU oracle (a restatement of the reference's runtime) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Qwen3-8B-shape Q4_K decode tok/s (bs1, bs32) and % of HBM roofline"
+PROMPT = 512
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n):
+    if n <= 1:
+        return 0, 1, 0
+    import torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600))
+    return rank, world, local
+
+
+def dist_max(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(img, seconds: float = 20.0, max_steps: int = 8):
+    """The CPU oracle on this host: one 8B decode step at context PROMPT (synthetic KV
+    prefix), repeated until `seconds` of CPU work or `max_steps` steps."""
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    m = orc.Model(img)
+    s = orc.Session(m)
+    s.fill_kv(PROMPT, seed=7)
+    s.step(1)  # warm the page cache / thread pool
+    n, t0 = 0, time.perf_counter()
+    tok = 2
+    while n < max_steps:
+        lg = s.step(tok)
+        tok = orc.argmax(lg)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of the 8B-shape model at context {PROMPT + 1}..{PROMPT + n} "
+                      f"(synthetic KV prefix), CPU oracle restating src/runtime.rs, {threads} threads"}
+
+
+def kernel_roofline(evl_rt, stream, hbm_peak, peak_kind, reps=8):
+    """Time the dominant kernel (Q4_K dequant-matvec, ffn_gate shape 12288x4096) with CUDA
+    events on its stream, cycling 8 distinct matrices (226 MB > L2)."""
+    import torch
+    from evelyn_b200 import synth
+    rows, cols = 12288, 4096
+    rng = np.random.default_rng(1)
+    mats = []
+    lib = evl_rt.lib()
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    raw = np.frombuffer(synth.encode(synth.GGML_Q4_K, w), dtype=np.uint8)
+    for i in range(8):
+        h = C.c_void_p()
+        raw_i = raw.copy()
+        raw_i[16::144] ^= np.uint8(i)  # distinct payloads, same statistics
+        evl_rt.check(lib.evl_qmatrix_create(synth.GGML_Q4_K, rows, cols, C.c_void_p(raw_i.ctypes.data), 0,
+                                            C.byref(h)))
+        mats.append(h)
+    x = torch.randn(cols, device="cuda:0")
+    y = torch.empty(rows, device="cuda:0")
+    ext = torch.cuda.ExternalStream(stream)
+    for h in mats:  # warm up
+        evl_rt.check(lib.evl_qmatrix_matvec(h, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), C.c_void_p(stream)))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(reps):
+        for h in mats:
+            evl_rt.check(lib.evl_qmatrix_matvec(h, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()),
+                                                C.c_void_p(stream)))
+    e1.record(ext)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(mats))
+    alg = rows * cols // 256 * 144 + cols * 4 + rows * 4
+    for h in mats:
+        lib.evl_qmatrix_free(h)
+    gbs = alg / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(gbs / hbm_peak, 4), "traffic": None, "peak_source": peak_kind,
+            "kernel": "qmatvec_kernel (Q4_K, 12288x4096, ffn_gate shape)", "launch_us": round(ms * 1e3, 2),
+            "bytes_per_launch": alg}
+
+
+def run_ours(args):
+    rank, world, local = dist_setup(args.gpus)
+    import torch
+    torch.cuda.set_device(local)
+    import evelyn_b200 as evl
+    from evelyn_b200 import runtime, synth
+
+    spec = synth.qwen3_8b(seed=0)
+    t0 = time.perf_counter()
+    img = synth.build(spec)
+    log(f"[rank {rank}] synthetic GGUF {img.nbytes / 1e9:.2f} GB in {time.perf_counter() - t0:.1f}s")
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [evl.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    t0 = time.perf_counter()
+    model = evl.Model.load_memory(img, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    log(f"[rank {rank}] loaded in {time.perf_counter() - t0:.1f}s; {model.weight_bytes / 1e9:.3f} GB/step on this rank")
+    K, W = args.steps, args.warmup
+    max_ctx = PROMPT + 2 * (W + K) + 16
+    sess = evl.Session(model, max_ctx=max_ctx)
+    prompt = np.random.default_rng(0).integers(0, spec.vocab, PROMPT)
+    for t in prompt[:-1]:
+        sess.step(int(t), logits=False)
+    last = int(prompt[-1])
+    # warm-up, then K timed device-resident steps (greedy loop stays on the GPU)
+    toks = sess.generate(last, W)
+    stream = sess.stream
+    ext = torch.cuda.ExternalStream(stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    ctx0 = sess.pos
+    with ClockSampler(local) as clk:
+        e0.record(ext)
+        toks = sess.generate(toks[-1], K)
+        e1.record(ext)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    ms_max = dist_max(ms, world)
+    # end to end through evl_session_step: token H2D, logits + argmax D2H, every step
+    tok = toks[-1]
+    barrier(world)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(ext)
+    for _ in range(K):
+        lg = sess.step(tok)
+        tok = evl.argmax(lg)
+    f1.record(ext)
+    f1.synchronize()
+    e2e_ms = dist_max(f0.elapsed_time(f1), world)
+    hbm, peak_kind = peaks()
+    roof = kernel_roofline(runtime, stream, hbm, peak_kind) if rank == 0 else None
+    kv_pos = spec.kv_bytes_per_position(2)
+    mean_ctx = ctx0 + (K + 1) / 2
+    step_bytes = spec.weight_bytes_per_token() + kv_pos * mean_ctx + kv_pos / 1
+    tok_s = K / (ms_max / 1e3)
+    base = cpu_baseline(img) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(ms_max / K, 4), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q4_k/q6_k/q8_0 weights, f32 math",
+            "data": "synthetic: seeded N(0,0.02) weights quantised to a Q4_K_M-style mix, uniform-random prompt ids",
+            "config": {"workload": f"Qwen3-8B-shape decode bs1, {PROMPT}-token prompt then greedy decode "
+                                   f"(ctx {ctx0}..{ctx0 + K})", "model": "qwen3-8b-shape (36L, d4096, 32Q/8KV x128,"
+                       " ffn 12288, vocab 151936)", "global_batch": 1, "seq_len": ctx0 + K,
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "kv_cache": "paged f16, 16-token pages", "l2": "inputs larger than L2 (5.08 GB weights/step)"},
+            "step_hbm": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes * K / (ms_max / 1e3) / 1e9, 1),
+                         "frac": round(step_bytes * K / (ms_max / 1e3) / 1e9 / hbm, 4), "peak": hbm,
+                         "peak_source": peak_kind},
+            "e2e": {"value": round(K / (e2e_ms / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": spec.vocab * 4 + 4 + 4},
+            "roofline": roof,
+            "gpu_launches": sess.kernels_per_step * K,
+            "clocks": clocks,
+        }
+        if base:
+            line["cpu_baseline"] = base
+        print(json.dumps(line), flush=True)
+    del sess, model
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's CPU runtime (the oracle port: cargo/rustc are not in this image) on the
+    host cores, same metric and workload; each step one 8B decode token at ctx >= 512."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from evelyn_b200 import synth
+    from oracle import oracle as orc
+    spec = synth.qwen3_8b(seed=0)
+    img = synth.build(spec)
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    m = orc.Model(img)
+    s = orc.Session(m)
+    s.fill_kv(PROMPT, seed=7)
+    tok = 1
+    budget = 90.0
+    for _ in range(min(args.warmup, 1)):
+        tok = orc.argmax(s.step(tok))
+    n, t0 = 0, time.perf_counter()
+    while n < args.steps:
+        tok = orc.argmax(s.step(tok))
+        n += 1
+        if time.perf_counter() - t0 > budget:
+            break
+    dt = time.perf_counter() - t0
+    v = n / dt
+    sample = (f"{n} of {args.steps} requested decode steps (capped at {budget:.0f}s) at ctx {PROMPT + 1}.., "
+              f"synthetic KV prefix, {threads} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": round(dt / n * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"Qwen3-8B-shape decode bs1, ctx {PROMPT}+ (CPU, sampled)"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=512, help="prompt tokens fed before decoding")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    global PROMPT
+    PROMPT = max(1, args.prompt)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

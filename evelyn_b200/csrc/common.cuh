@@ -107,19 +107,26 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n selp.u32 %0, 1, 0, p;\n}"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(phase)
         : "memory");
     return ok != 0;
 }
-// Bounded wait: after `limit` failed polls the wait gives up and reports false;
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: after kWaitNs of wall time the wait gives up and reports false;
 // callers record the error and return instead of spinning forever.
-constexpr uint32_t kWaitLimit = 1u << 16;
+constexpr uint64_t kWaitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
-        if (mbar_try_wait(bar, phase)) return true;
-    return false;
+    if (mbar_try_wait(bar, phase)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, phase))
+        if (global_ns() - t0 > kWaitNs) return false;
+    return true;
 }
 
 // Device error flags, read by the host after a step (0 = ok).

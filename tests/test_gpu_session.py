@@ -1,0 +1,203 @@
+"""Model-level parity of the device decode loop against the CPU oracle (a restatement
+of src/runtime.rs:773-808): logits within max-abs 2e-3, greedy tokens identical,
+perplexity within 0.5 %, plus the FfnBackend routing hook, batching and errors."""
+import math
+
+import numpy as np
+import pytest
+
+import evelyn_b200 as evl
+from evelyn_b200 import synth
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-3
+
+
+def _models(spec, kv_f32=False):
+    img = synth.build(spec)
+    return img, evl.Model.load_memory(img, device=0, kv_f32=kv_f32), orc.Model(img)
+
+
+def _tokens(n, vocab, seed=0):
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+@pytest.mark.parametrize("mix", ["q4k_mix", "q8_0", "q6k"])
+def test_step_logits_match_oracle(mix, kv_f32):
+    spec = synth.tiny(seed=11)
+    if mix == "q8_0":
+        spec = spec.with_types(synth.GGML_Q8_0)
+    elif mix == "q6k":
+        spec = spec.with_types(synth.GGML_Q6_K)
+        spec.embed = spec.output = synth.GGML_Q8_0
+    img, m, r = _models(spec, kv_f32)
+    s, rs = evl.Session(m, max_ctx=256), orc.Session(r)
+    worst = 0.0
+    for tok in _tokens(48, spec.vocab, seed=1):
+        got, want = s.step(tok), rs.step(tok)
+        worst = max(worst, float(np.abs(got - want).max()))
+    assert s.pos == rs.pos == 48
+    assert worst <= LOGIT_TOL, worst
+
+
+def test_greedy_64_tokens_identical_and_ppl():
+    spec = synth.tiny(seed=3, layers=3)
+    img, m, r = _models(spec)
+    s, rs = evl.Session(m, max_ctx=256), orc.Session(r)
+    prompt = _tokens(32, spec.vocab, seed=2)
+    nll_g = nll_o = 0.0
+    for i, tok in enumerate(prompt):
+        lg, lo = s.step(tok), rs.step(tok)
+        if i + 1 < len(prompt):
+            nll_g -= evl.log_prob(lg, prompt[i + 1])
+            nll_o -= orc.log_prob(lo, prompt[i + 1])
+    ppl_g, ppl_o = math.exp(nll_g / (len(prompt) - 1)), math.exp(nll_o / (len(prompt) - 1))
+    assert abs(ppl_g / ppl_o - 1) < 0.005, (ppl_g, ppl_o)
+    tg, to = evl.argmax(lg), orc.argmax(lo)
+    out_g, out_o = [], []
+    for _ in range(64):
+        out_g.append(tg)
+        out_o.append(to)
+        tg, to = evl.argmax(s.step(tg)), orc.argmax(rs.step(to))
+    assert out_g == out_o
+
+
+def test_generate_matches_stepwise_argmax():
+    spec = synth.tiny(seed=5)
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=0)
+    a, b = evl.Session(m, max_ctx=128), evl.Session(m, max_ctx=128)
+    toks = a.generate(17, 40)
+    ref, t = [], 17
+    for _ in range(40):
+        t = b.step(t, logits=False)
+        ref.append(t)
+    assert toks == ref
+    assert a.pos == b.pos == 40
+
+
+class _OracleFfn(evl.FfnBackend):
+    """Serves chosen layers from the oracle's dense FFN on the host (a stand-in AARNN region)."""
+
+    def __init__(self, oracle_model, layers):
+        self.o = oracle_model
+        self.routed_layers = layers
+        self.calls = []
+
+    def ffn(self, layer, x):
+        self.calls.append(layer)
+        return self.o.dense_ffn(layer, x)
+
+
+def test_ffn_routing_hook_matches_dense():
+    spec = synth.tiny(seed=9, layers=3)
+    img, m, r = _models(spec)
+    hook = _OracleFfn(r, [1])
+    s_hook, s_dense = evl.Session(m, max_ctx=64), evl.Session(m, max_ctx=64)
+    for tok in _tokens(12, spec.vocab, seed=4):
+        a, b = s_hook.step(tok, hook), s_dense.step(tok, evl.DenseFfn(m))
+        assert np.abs(a - b).max() <= LOGIT_TOL
+    assert hook.calls == [1] * 12
+
+
+def test_capture_ffn_records_ffn_input():
+    spec = synth.tiny(seed=9)
+    img, m, r = _models(spec)
+    cap = evl.CaptureFfn(m, 1)
+    s, rs = evl.Session(m, max_ctx=64), orc.Session(r)
+    captured = []
+    for tok in _tokens(5, spec.vocab, seed=6):
+        s.step(tok, cap)
+        rs.step(tok, lambda layer, x: (captured.append(x) if layer == 1 else None) or None)
+    assert len(cap.captured) == 5
+    for g, w in zip(cap.captured, captured):
+        assert np.abs(g - w).max() <= 1e-3
+
+
+def test_failing_hook_falls_back_to_dense():
+    spec = synth.tiny(seed=9)
+    img, m, r = _models(spec)
+
+    class Broken(evl.FfnBackend):
+        routed_layers = [0]
+
+        def ffn(self, layer, x):
+            raise ConnectionError("region down")
+
+    s, d = evl.Session(m, max_ctx=32), evl.Session(m, max_ctx=32)
+    for tok in _tokens(4, spec.vocab, seed=8):
+        assert np.abs(s.step(tok, Broken()) - d.step(tok)).max() <= LOGIT_TOL
+    assert s.fallbacks == 4
+
+
+def test_batch_matches_independent_sessions():
+    spec = synth.tiny(seed=13)
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=0)
+    B = 3
+    batch = evl.Batch(m, B, max_ctx=64)
+    sessions = [evl.Session(m, max_ctx=64) for _ in range(B)]
+    rng = np.random.default_rng(0)
+    for _ in range(10):
+        toks = rng.integers(0, spec.vocab, B)
+        got = batch.step(toks)
+        for i in range(B):
+            assert np.abs(got[i] - sessions[i].step(int(toks[i]))).max() <= 1e-4
+
+
+def test_model_level_apis_match_oracle():
+    spec = synth.tiny(seed=21)
+    img, m, r = _models(spec)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal(spec.dim).astype(np.float32)
+    assert np.abs(m.ffn_input(0, x) - r.ffn_input(0, x)).max() <= 1e-5
+    xn = r.ffn_input(1, x)
+    y, yo = m.dense_ffn(1, xn), r.dense_ffn(1, xn)
+    assert np.abs(y - yo).max() <= 1e-4 * max(1.0, float(np.abs(yo).max()))
+    for name in ("token_embd.weight", "blk.0.attn_q.weight", "blk.1.attn_v.weight", "blk.1.ffn_down.weight",
+                 "output.weight", "blk.0.attn_norm.weight"):
+        want = r.tensor_f32(name)
+        got = m.dequantize(name, want.size)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), name
+    w = r.tensor_f32("blk.0.ffn_gate.weight").reshape(spec.ffn, spec.dim).astype(np.float64)
+    assert np.abs(m.matvec("blk.0.ffn_gate.weight", x, spec.ffn) - w @ x).max() <= 1e-4
+
+
+def test_tied_lm_head():
+    spec = synth.tiny(seed=2, tied_output=True)
+    img, m, r = _models(spec)
+    s, rs = evl.Session(m, max_ctx=32), orc.Session(r)
+    for tok in _tokens(6, spec.vocab, seed=3):
+        assert np.abs(s.step(tok) - rs.step(tok)).max() <= LOGIT_TOL
+
+
+def test_token_and_context_errors():
+    spec = synth.tiny(seed=1)
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=0)
+    s = evl.Session(m, max_ctx=4)
+    with pytest.raises(evl.EvelynError) as e:
+        s.step(spec.vocab)
+    assert e.value.kind == "InvalidInput" and "tokenizer and GGUF match" in str(e.value)
+    assert s.pos == 0
+    for t in range(4):
+        s.step(t)
+    with pytest.raises(evl.EvelynError) as e:
+        s.step(0)
+    assert e.value.kind == "InvalidInput"
+    # the session survives an error
+    s2 = evl.Session(m, max_ctx=8)
+    s2.step(1)
+    assert s2.pos == 1
+
+
+def test_load_errors():
+    with pytest.raises(evl.EvelynError) as e:
+        evl.Model.load("/nonexistent/model.gguf", device=0)
+    assert e.value.kind == "NotFound"
+    with pytest.raises(evl.EvelynError) as e:
+        evl.Model.load_memory(b"GGUX" + b"\0" * 64, device=0)
+    assert e.value.kind == "InvalidData"
