@@ -291,6 +291,117 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def _random_raw(ggml_type: int, rows: int, cols: int, rng) -> np.ndarray:
+    """Random GGUF rows with moderate f16 scales (bandwidth does not depend on values)."""
+    from evelyn_b200 import synth
+    be = 32 if ggml_type == synth.GGML_Q8_0 else 256
+    bb = synth.type_bytes(ggml_type, be)
+    nb = rows * cols // be
+    raw = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
+    scale = np.full(nb, 0.004, dtype=np.float16).view(np.uint8).reshape(nb, 2)
+    if ggml_type == synth.GGML_Q6_K:
+        raw[:, 208:210] = scale
+    else:
+        raw[:, 0:2] = scale
+        if ggml_type == synth.GGML_Q4_K:
+            raw[:, 2:4] = scale
+    return raw.reshape(-1)
+
+
+def run_sweep(args):
+    """Isolated kernel sweep: dequant-matvec for 4096x4096, 4096x12288, 12288x4096, 151936x4096
+    in Q4_K/Q6_K/Q8_0, and GQA decode attention 32Q/8KV hd128 at KV length 512..32768.
+    Each case cycles enough distinct copies to exceed L2 twice; CUDA events on one stream."""
+    import torch
+    from evelyn_b200 import runtime, synth
+    lib = runtime.lib()
+    hbm, peak_kind = peaks()
+    only = set(args.sweep_only.split(",")) if args.sweep_only else None
+    stream = torch.cuda.Stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    rng = np.random.default_rng(0)
+    names = {synth.GGML_Q4_K: "q4k", synth.GGML_Q6_K: "q6k", synth.GGML_Q8_0: "q8_0"}
+    for rows, cols in [(4096, 4096), (4096, 12288), (12288, 4096), (151936, 4096)]:
+        for t in (synth.GGML_Q4_K, synth.GGML_Q6_K, synth.GGML_Q8_0):
+            name = f"{names[t]}_{rows}x{cols}"
+            if only and name not in only:
+                continue
+            raw = _random_raw(t, rows, cols, rng)
+            nbytes = raw.size
+            copies = max(1, -(-2 * 126 * 2**20 // nbytes))
+            mats = []
+            for i in range(copies):
+                h = C.c_void_p()
+                r = raw.copy()
+                r[7::97] ^= np.uint8(i)
+                runtime.check(lib.evl_qmatrix_create(t, rows, cols, C.c_void_p(r.ctypes.data), 0, C.byref(h)))
+                mats.append(h)
+            x = torch.randn(cols, device="cuda:0")
+            y = torch.empty(rows, device="cuda:0")
+            px, py = C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
+            for h in mats:
+                runtime.check(lib.evl_qmatrix_matvec(h, px, py, sp))
+            reps = max(1, args.reps)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                for h in mats:
+                    runtime.check(lib.evl_qmatrix_matvec(h, px, py, sp))
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(mats))
+            alg = nbytes + 4 * (rows + cols)
+            gbs = alg / (us * 1e-6) / 1e9
+            print(json.dumps({"kernel": "qmatvec", "case": name, "bytes": alg, "us": round(us, 2),
+                              "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
+                              "peak_source": peak_kind}), flush=True)
+            for h in mats:
+                lib.evl_qmatrix_free(h)
+            del mats
+    heads, kvh, hd, ps = 32, 8, 128, 16
+    L = 512
+    while L <= 32768:
+        name = f"attn_{L}"
+        if not only or name in only:
+            pages = L // ps
+            kv_bytes = 2 * pages * kvh * ps * hd * 2
+            copies = max(1, -(-2 * 126 * 2**20 // kv_bytes))
+            kvs = [(torch.randn(pages, kvh, ps, hd, device="cuda:0").half(),
+                    torch.randn(pages, kvh, ps, hd, device="cuda:0").half()) for _ in range(copies)]
+            pt = torch.arange(pages, dtype=torch.int32, device="cuda:0")
+            q = torch.randn(heads * hd, device="cuda:0")
+            out = torch.empty(heads * hd, device="cuda:0")
+            wsb = lib.evl_attention_workspace_bytes(L, heads, kvh, hd)
+            ws = torch.empty(wsb // 4 + 64, dtype=torch.float32, device="cuda:0")
+            wp = (ws.data_ptr() + 255) // 256 * 256
+
+            def call(k, v):
+                runtime.check(lib.evl_attention_decode_ws(
+                    C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                    C.c_void_p(pt.data_ptr()), L, heads, kvh, hd, ps, C.c_void_p(out.data_ptr()), C.c_void_p(wp),
+                    wsb, sp))
+            for k, v in kvs:
+                call(k, v)
+            reps = max(1, args.reps)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                for k, v in kvs:
+                    call(k, v)
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(kvs))
+            alg = kv_bytes + 2 * heads * hd * 4
+            gbs = alg / (us * 1e-6) / 1e9
+            print(json.dumps({"kernel": "attention", "case": name, "bytes": alg, "us": round(us, 2),
+                              "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
+                              "peak_source": peak_kind}), flush=True)
+            del kvs
+        L *= 2
+
+
 def run_reference(args):
     """The reference's CPU runtime (the oracle port: cargo/rustc are not in this image) on the
     host cores, same metric and workload; each step one 8B decode token at ctx >= 512."""
@@ -338,12 +449,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens fed before decoding")
+    ap.add_argument("--sweep", action="store_true", help="isolated kernel sweep (one JSON line per case)")
+    ap.add_argument("--sweep-only", default="", help="comma-separated sweep case names")
+    ap.add_argument("--reps", type=int, default=10, help="timed passes per sweep case")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     global PROMPT
     PROMPT = max(1, args.prompt)
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

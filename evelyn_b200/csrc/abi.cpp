@@ -98,8 +98,7 @@ evl_status evl_tp_unique_id(uint8_t out[128]) {
     return guarded([&] {
         require(out, "null output");
         ncclUniqueId id;
-        ncclResult_t r = ncclGetUniqueId(&id);
-        if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        nccl_check(nccl().GetUniqueId(&id), "ncclGetUniqueId");
         std::memcpy(out, id.internal, 128);
     });
 }
@@ -398,54 +397,104 @@ evl_status evl_qmatrix_dequantize(const evl_qmatrix* q, float* d_out, void* stre
     });
 }
 
+namespace {
+
+void check_attention_args(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table,
+                          uint32_t t, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size,
+                          const float* d_out) {
+    require(d_q && d_k_pages && d_v_pages && d_page_table && d_out, "null argument");
+    require(t > 0, "no positions to attend");
+    require(head_dim == 128 || head_dim == 64, "head_dim must be 64 or 128");
+    require(page_size == 16, "page_size must be 16");
+    require(kv_heads && heads % kv_heads == 0, "heads must be a multiple of kv_heads");
+    const uint32_t g = heads / kv_heads;
+    require(g == 1 || g == 2 || g == 4 || g == 8, "heads / kv_heads must be 1, 2, 4 or 8");
+}
+
+// Splits over the sequence: enough (kv_head, split) CTAs to cover the SMs twice.
+uint32_t attention_splits(uint32_t t, uint32_t kv_heads, uint32_t page_size) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t pages = (t + page_size - 1) / page_size;
+    return std::max<uint32_t>(1, std::min<uint32_t>((2u * sms) / kv_heads, pages));
+}
+
+size_t attention_part_bytes(uint32_t heads, uint32_t nsplit, uint32_t head_dim) {
+    return (size_t)heads * nsplit * (head_dim + 2) * 4;
+}
+
+// One standalone decode attention with caller-provided partials (`part`) and error flag.
+void attention_standalone(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table,
+                          uint32_t t, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size,
+                          float* d_out, float* part, uint32_t nsplit, int32_t* d_err, cudaStream_t s) {
+    AttnArgs a;
+    a.q = d_q;
+    a.out = d_out;
+    a.kv.pool = const_cast<void*>(d_k_pages);
+    a.kv.head_stride = (uint64_t)page_size * head_dim * 2;
+    a.kv.page_stride = a.kv.head_stride * kv_heads;
+    a.kv.layer_stride = 0;
+    a.kv.v_offset = static_cast<const uint8_t*>(d_v_pages) - static_cast<const uint8_t*>(d_k_pages);
+    a.kv.page_size = page_size;
+    a.kv.elem_bytes = 2;
+    a.page_table = d_page_table;
+    a.max_pages = (t + page_size - 1) / page_size;
+    a.pos = nullptr;
+    a.pos_value = (int32_t)(t - 1);
+    a.heads = heads;
+    a.kv_heads = kv_heads;
+    a.head_dim = head_dim;
+    a.nsplit = nsplit;
+    a.part = part;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    a.err = d_err;
+    cuda_check(launch_attention(a, s, false), "attention");
+}
+
+constexpr size_t kWsHeader = 256;  // error flag, padded so the partials stay aligned
+
+}  // namespace
+
 evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
                                 const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
                                 uint32_t head_dim, uint32_t page_size, float* d_out, void* stream) {
     return guarded([&] {
-        require(d_q && d_k_pages && d_v_pages && d_page_table && d_out, "null argument");
-        require(t > 0, "no positions to attend");
-        require(head_dim == 128 || head_dim == 64, "head_dim must be 64 or 128");
-        require(page_size == 16, "page_size must be 16");
-        require(kv_heads && heads % kv_heads == 0, "heads must be a multiple of kv_heads");
+        check_attention_args(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out);
         cudaStream_t s = as_stream(stream);
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const uint32_t pages = (t + page_size - 1) / page_size;
-        const uint32_t nsplit = std::max<uint32_t>(1, std::min<uint32_t>((2u * sms) / kv_heads, pages));
-        // scratch: split partials, then position and error flag
-        const size_t part_floats = (size_t)heads * nsplit * (head_dim + 2);
+        const uint32_t nsplit = attention_splits(t, kv_heads, page_size);
         DeviceBuffer scratch;
-        scratch.alloc(part_floats * 4 + 16);
-        int32_t* d_pos = reinterpret_cast<int32_t*>(scratch.as<uint8_t>() + part_floats * 4);
-        int32_t* d_err = d_pos + 1;
-        const int32_t host[2] = {(int32_t)(t - 1), 0};
-        cuda_check(cudaMemcpyAsync(d_pos, host, 8, cudaMemcpyHostToDevice, s), "H2D");
-        AttnArgs a;
-        a.q = d_q;
-        a.out = d_out;
-        a.kv.pool = const_cast<void*>(d_k_pages);
-        a.kv.head_stride = (uint64_t)page_size * head_dim * 2;
-        a.kv.page_stride = a.kv.head_stride * kv_heads;
-        a.kv.layer_stride = 0;
-        a.kv.v_offset = static_cast<const uint8_t*>(d_v_pages) - static_cast<const uint8_t*>(d_k_pages);
-        a.kv.page_size = page_size;
-        a.kv.elem_bytes = 2;
-        a.page_table = d_page_table;
-        a.max_pages = pages;
-        a.pos = d_pos;
-        a.heads = heads;
-        a.kv_heads = kv_heads;
-        a.head_dim = head_dim;
-        a.nsplit = nsplit;
-        a.part = scratch.as<float>();
-        a.scale = 1.0f / sqrtf((float)head_dim);
-        a.err = d_err;
-        cuda_check(launch_attention(a, s, false), "attention");
+        scratch.alloc(kWsHeader + attention_part_bytes(heads, nsplit, head_dim));
+        int32_t* d_err = scratch.as<int32_t>();
+        cuda_check(cudaMemsetAsync(d_err, 0, 4, s), "memset");
+        attention_standalone(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out,
+                             reinterpret_cast<float*>(scratch.as<uint8_t>() + kWsHeader), nsplit, d_err, s);
         int32_t err = 0;
         cuda_check(cudaMemcpyAsync(&err, d_err, 4, cudaMemcpyDeviceToHost, s), "D2H");
         cuda_check(cudaStreamSynchronize(s), "attention");
         if (err == DEV_ERR_WAIT_TIMEOUT) raise(EVL_ERR_TIMEOUT, "a device wait for KV pages timed out");
+    });
+}
+
+size_t evl_attention_workspace_bytes(uint32_t t_max, uint32_t heads, uint32_t kv_heads, uint32_t head_dim) {
+    if (!t_max || !kv_heads) return 0;
+    return kWsHeader + attention_part_bytes(heads, attention_splits(t_max, kv_heads, 16), head_dim);
+}
+
+evl_status evl_attention_decode_ws(const float* d_q, const void* d_k_pages, const void* d_v_pages,
+                                   const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
+                                   uint32_t head_dim, uint32_t page_size, float* d_out, void* d_workspace,
+                                   size_t workspace_bytes, void* stream) {
+    return guarded([&] {
+        check_attention_args(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out);
+        require(d_workspace, "null workspace");
+        require((reinterpret_cast<uintptr_t>(d_workspace) & 255) == 0, "workspace must be 256-byte aligned");
+        const uint32_t nsplit = attention_splits(t, kv_heads, page_size);
+        if (workspace_bytes < kWsHeader + attention_part_bytes(heads, nsplit, head_dim))
+            raise(EVL_ERR_INVALID_INPUT, "workspace too small; size it with evl_attention_workspace_bytes");
+        attention_standalone(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out,
+                             reinterpret_cast<float*>(static_cast<uint8_t*>(d_workspace) + kWsHeader), nsplit,
+                             static_cast<int32_t*>(d_workspace), as_stream(stream));
     });
 }
 

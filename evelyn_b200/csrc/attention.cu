@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_split_kernel(const __g
     }
     __syncthreads();
     pdl_wait();
-    const uint32_t t_all = (uint32_t)a.pos[b] + 1;
+    const uint32_t t_all = (uint32_t)(a.pos ? a.pos[b] : a.pos_value) + 1;
     const uint32_t S = split_len(t_all, a.nsplit, ps);
     const uint32_t t0 = split * S;
     if (t0 >= t_all) return;  // empty split
@@ -275,7 +275,7 @@ template <int HD>
 __global__ void attention_combine_kernel(const __grid_constant__ AttnArgs a) {
     const uint32_t head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     pdl_wait();
-    const uint32_t t = (uint32_t)a.pos[b] + 1;
+    const uint32_t t = (uint32_t)(a.pos ? a.pos[b] : a.pos_value) + 1;
     const uint32_t S = split_len(t, a.nsplit, a.kv.page_size);
     const uint32_t ns = (t + S - 1) / S;
     const float* part = a.part + ((uint64_t)b * a.heads + head) * a.nsplit * (HD + 2);

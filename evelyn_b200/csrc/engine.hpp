@@ -60,6 +60,23 @@ struct PinnedBuffer {
     template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
+// ------------------------------------------------------------------ NCCL (resolved at run time)
+struct Nccl {
+    bool loaded = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+const Nccl& nccl();  // raises EVL_ERR_NCCL when no libnccl can be loaded
+void nccl_check(ncclResult_t r, const char* what);
+
 // ------------------------------------------------------------------ GGUF (src/gguf.rs)
 size_t type_bytes(uint32_t t, size_t n);  // gguf.rs:288-298; raises Unsupported
 const char* type_name(uint32_t t);

@@ -81,7 +81,8 @@ struct AttnArgs {
     uint32_t layer = 0;
     const int32_t* page_table = nullptr;
     uint32_t max_pages = 0;
-    const int32_t* pos = nullptr;  // attend to positions [0, pos]
+    const int32_t* pos = nullptr;  // attend to positions [0, pos]; null: use pos_value
+    int32_t pos_value = 0;         // (single sequence)
     uint32_t batch = 1, heads = 0, kv_heads = 0, head_dim = 0;
     uint32_t nsplit = 1;           // fixed grid split count; each split covers
                                    // ceil(t / nsplit) positions rounded up to whole pages

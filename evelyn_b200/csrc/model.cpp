@@ -51,7 +51,7 @@ void split_range(uint64_t n, int p, int i, uint64_t* lo, uint64_t* hi) {
 }  // namespace
 
 Model::~Model() {
-    if (comm) ncclCommDestroy(comm);
+    if (comm) nccl().CommDestroy(comm);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -317,8 +317,7 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         ncclUniqueId id;
         static_assert(sizeof(id.internal) == 128, "ncclUniqueId size");
         std::memcpy(id.internal, o.nccl_id, 128);
-        ncclResult_t r = ncclCommInitRank(&m.comm, T, id, R);
-        if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+        nccl_check(nccl().CommInitRank(&m.comm, T, id, R), "ncclCommInitRank");
     }
     cuda_check(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking), "cudaStreamCreate");
     const size_t sc = (size_t)c.dim * 3 + m.lffn + std::max<size_t>(c.dim, c.vocab) + 64;
@@ -329,8 +328,7 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
 }
 
 void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s) {
-    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, m.comm, s);
-    if (r != ncclSuccess) raise(EVL_ERR_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+    nccl_check(nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, m.comm, s), "ncclAllReduce");
 }
 
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,

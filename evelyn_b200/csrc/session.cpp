@@ -211,16 +211,16 @@ void Decoder::enqueue_head(bool pdl) {
     kernels += B;
     if (tp) {  // vocabulary shards -> full logits on every rank
         const uint64_t V = c.vocab;
-        ncclGroupStart();
+        const Nccl& nc = nccl();
+        nccl_check(nc.GroupStart(), "ncclGroupStart");
         for (int r = 0; r < m.tp_size; ++r) {
             const uint64_t base = V / m.tp_size, rem = V % m.tp_size;
             const uint64_t lo = r * base + std::min<uint64_t>(r, rem), n = base + (r < (int)rem ? 1 : 0);
             for (uint32_t bi = 0; bi < B; ++bi)
-                ncclBroadcast(b.y.as<float>() + (uint64_t)bi * m.lvocab, b.logits.as<float>() + bi * V + lo, n,
-                              ncclFloat32, r, m.comm, stream);
+                nc.Broadcast(b.y.as<float>() + (uint64_t)bi * m.lvocab, b.logits.as<float>() + bi * V + lo, n,
+                             ncclFloat32, r, m.comm, stream);
         }
-        ncclResult_t rr = ncclGroupEnd();
-        if (rr != ncclSuccess) raise(EVL_ERR_NCCL, std::string("logits gather: ") + ncclGetErrorString(rr));
+        nccl_check(nc.GroupEnd(), "logits gather");
     }
     cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, B, b.amax_v.as<float>(), b.amax_i.as<int32_t>(),
                              b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),

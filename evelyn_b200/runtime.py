@@ -132,6 +132,9 @@ SIGNATURES = {
     "evl_qmatrix_dequantize": (C.c_int, [_P, _P, _P]),
     "evl_attention_decode": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                        _P, _P]),
+    "evl_attention_workspace_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "evl_attention_decode_ws": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                          C.c_uint32, _P, _P, C.c_size_t, _P]),
     "evl_remote_ffn_new": (C.c_int, [_P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_char_p), C.c_uint32,
                                      C.POINTER(_P)]),
     "evl_remote_ffn_free": (None, [_P]),
@@ -141,10 +144,27 @@ SIGNATURES = {
 }
 
 
+def _prefer_wheel_nccl():
+    """Point the engine's run-time NCCL lookup at the NCCL wheel PyTorch uses, when it is
+    installed, so the engine and torch never load two NCCL builds under one soname."""
+    if os.environ.get("EVELYN_NCCL_LIBRARY"):
+        return
+    try:
+        import nvidia
+        for base in list(getattr(nvidia, "__path__", [])):
+            cand = os.path.join(base, "nccl", "lib", "libnccl.so.2")
+            if os.path.exists(cand):
+                os.environ["EVELYN_NCCL_LIBRARY"] = cand
+                return
+    except ImportError:
+        pass
+
+
 def lib():
     """The loaded engine library (raises NativeLibraryMissing when it is not built)."""
     global _L
     if _L is None:
+        _prefer_wheel_nccl()
         L = _native.load(LIB_NAME)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(L, name)

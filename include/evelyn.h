@@ -173,6 +173,16 @@ evl_status evl_qmatrix_dequantize(const evl_qmatrix* m, float* d_out, void* stre
 evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
                                 const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
                                 uint32_t head_dim, uint32_t page_size, float* d_out, void* stream);
+/* Bytes of device workspace evl_attention_decode_ws needs for up to t_max positions. */
+size_t evl_attention_workspace_bytes(uint32_t t_max, uint32_t heads, uint32_t kv_heads, uint32_t head_dim);
+/* evl_attention_decode with the split scratch in a caller-allocated device workspace
+ * (256-byte aligned, evl_attention_workspace_bytes(t_max, ...) bytes, t <= t_max);
+ * asynchronous on `stream`. The workspace's first int32 is a device error flag the
+ * kernel sets (2) if a wait for KV pages timed out; the caller clears it. */
+evl_status evl_attention_decode_ws(const float* d_q, const void* d_k_pages, const void* d_v_pages,
+                                   const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
+                                   uint32_t head_dim, uint32_t page_size, float* d_out, void* d_workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ AARNN routing (src/remote.rs) */
 typedef struct evl_endpoint_stats { /* EndpointStats, remote.rs:13-24 */

@@ -132,3 +132,13 @@ def test_attention_decode_paged(t, hd):
                                                      kv_heads, hd, ps, gu.ptr(dout), None))
     got = dout.cpu().numpy().reshape(heads, hd)
     assert np.abs(got - want).max() < 2e-5
+    # the caller-workspace variant gives the same bits
+    lib = runtime.lib()
+    wsb = lib.evl_attention_workspace_bytes(t + 40, heads, kv_heads, hd)
+    ws = gu.torch().empty(wsb // 4 + 64, dtype=gu.torch().float32, device="cuda:0")
+    wp = C.c_void_p((ws.data_ptr() + 255) // 256 * 256)
+    dout2 = gu.empty_f32(heads * hd)
+    runtime.check(lib.evl_attention_decode_ws(gu.ptr(dq), gu.ptr(dk), gu.ptr(dv), gu.ptr(dpt), t, heads, kv_heads, hd,
+                                              ps, gu.ptr(dout2), wp, wsb, None))
+    gu.sync()
+    assert np.array_equal(dout2.cpu().numpy(), dout.cpu().numpy())
