@@ -220,12 +220,17 @@ extern "C" {
 
 evl_status evl_remote_ffn_new(evl_model* model, size_t n, const size_t* layers, const char* const* addrs,
                               uint32_t timeout_ms, evl_remote_ffn** out) {
-    if (!model || !out || (n && (!layers || !addrs))) {
+    if (!out || (n && (!layers || !addrs))) {
         evl::set_last_error("null argument");
         return EVL_ERR_INVALID_INPUT;
     }
     auto* r = new evl_remote_ffn();
-    const size_t L = model->m->cfg.layers;
+    size_t L = 0;
+    if (model) {
+        L = model->m->cfg.layers;
+    } else {  // no model: size the routing table by the routed layers themselves
+        for (size_t i = 0; i < n; ++i) L = std::max(L, layers[i] + 1);
+    }
     r->routed.assign(L, 0);
     for (size_t i = 0; i < n; ++i) {
         if (layers[i] >= L || !addrs[i]) {

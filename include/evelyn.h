@@ -191,7 +191,8 @@ typedef struct evl_endpoint_stats { /* EndpointStats, remote.rs:13-24 */
 } evl_endpoint_stats;
 /* RemoteAarnnFfn::new (remote.rs:185-205): layers[i] is served by the AARNN region at
  * addrs[i] ("host:port") over the wire protocol of remote.rs:69-111, with one
- * reconnect and a dense fallback; timeout_ms is the read timeout. */
+ * reconnect and a dense fallback; timeout_ms is the read timeout. model may be NULL,
+ * in which case the routed layers are not checked against a model's layer count. */
 evl_status evl_remote_ffn_new(evl_model* model, size_t n, const size_t* layers, const char* const* addrs,
                               uint32_t timeout_ms, evl_remote_ffn** out);
 void evl_remote_ffn_free(evl_remote_ffn* r);
