@@ -191,7 +191,7 @@ evl_status evl_model_dense_ffn(evl_model* model, size_t layer, const float* x, f
         float* ybuf = s + 2 * dim;
         float* h = s + 3 * dim;
         cuda_check(cudaMemcpyAsync(dx, x, dim * 4, cudaMemcpyHostToDevice, m.stream), "H2D");
-        run_dense_ffn(m, layer, dx, nullptr, dy, false, 1, h, ybuf, m.stream, false);
+        run_dense_ffn(m, layer, dx, nullptr, dy, false, 1, h, ybuf, m.d_err, nullptr, m.stream, false);
         cuda_check(cudaMemcpyAsync(y, dy, dim * 4, cudaMemcpyDeviceToHost, m.stream), "D2H");
         cuda_check(cudaStreamSynchronize(m.stream), "dense_ffn");
     });
@@ -264,6 +264,7 @@ evl_status evl_model_matvec(evl_model* model, const char* tensor, const float* x
         a.seg[0].y = by.as<float>();
         a.x = bx.as<float>();
         a.cols = q.cols;
+        a.err = m.d_err;
         cuda_check(launch_qmatvec(a, m.stream, false), "matvec");
         cuda_check(cudaMemcpyAsync(y, by.p, yn * 4, cudaMemcpyDeviceToHost, m.stream), "D2H");
         cuda_check(cudaStreamSynchronize(m.stream), "matvec");
@@ -357,6 +358,8 @@ evl_status evl_qmatrix_create(uint32_t type, uint32_t rows, uint32_t cols, const
             q->m.cols = cols;
             repack_sizes(q->m);
             q->buf.alloc(q->m.bytes());
+            q->err.alloc(4);
+            cuda_check(cudaMemset(q->err.p, 0, 4), "memset");
             place(q->m, q->buf.as<uint8_t>());
             std::vector<uint8_t> staging(q->m.bytes());
             repack_host(q->m, static_cast<const uint8_t*>(host_raw), type_bytes(type, cols), staging.data(),
@@ -386,6 +389,7 @@ evl_status evl_qmatrix_matvec(const evl_qmatrix* q, const float* d_x, float* d_y
         a.seg[0].y = d_y;
         a.x = d_x;
         a.cols = q->m.cols;
+        a.err = q->err.as<int>();
         cuda_check(launch_qmatvec(a, as_stream(stream), false), "matvec");
     });
 }

@@ -1,21 +1,24 @@
 // common.cuh -- device-side types shared by the decode kernels.
 //
-// Quantised weights live in HBM in a "unit-interleaved" repack of the GGUF
-// blocks (the reference keeps the raw GGUF bytes, src/runtime.rs:23-51). A unit is
-// 64 consecutive values of one row; units are grouped 32 at a time, and inside a
-// group the k-th 16-byte chunk of every unit is stored contiguously, so the 32
-// lanes of a warp that each own one unit read 512 contiguous bytes per 128-bit load.
+// Quantised weights live in HBM in a tiled repack of the GGUF blocks (the
+// reference keeps the raw GGUF bytes, src/runtime.rs:23-51). A unit is 64 values of
+// one row; a row is a sequence of tiles, each covering a group of up to 32 units
+// (the last group of a row may be shorter, U units). A tile is self-contained and
+// 16-byte aligned, so one TMA bulk copy moves it:
+//
+//   [payload: chunk-major, chunk c of unit u at c*U*16 + u*16 (16 B per chunk)]
+//   [aux: block scales, padded to 16 B] [d: Q6_K super-block scales, padded to 16 B]
 //
 //   Q4_K  unit = 32-byte qs group j of super-block i (values 256i+64j+[0,64)),
-//         2 chunks/unit;  aux = the 16-byte block header (d, dmin, scales[12]) per
-//         super-block, [rows][nb][16].
-//   Q6_K  unit = (super-block i, half h, l0 in {0,16}): 3 chunks/unit
-//         (ql[64h+l0..+16], ql[64h+32+l0..+16], qh[32h+l0..+16]);
-//         aux = u32 per unit holding the 4 int8 scales sc[8h+l0/16+2k], k=0..3;
-//         d = f16 bits per super-block.
-//   Q8_0  unit = two 32-value blocks: 4 chunks/unit; aux = u32 per unit with
-//         the two f16 block scales.
-//   F16, BF16, F32: plain values, 8 (16) chunks per unit.
+//         2 chunks; aux = the 16-byte header (d, dmin, scales[12]) of each of the
+//         U/4 super-blocks.
+//   Q6_K  unit = (super-block i, half h, l0 in {0,16}) (values 256i+128h+32k+l0+[0,16),
+//         k=0..3): 3 chunks (ql[64h+l0..+16], ql[64h+32+l0..+16], qh[32h+l0..+16]);
+//         aux = u32 per unit with the 4 int8 scales sc[8h+l0/16+2k]; d = f16 per
+//         super-block.
+//   Q8_0  unit = two 32-value blocks: 4 chunks; aux = u32 per unit with the two
+//         f16 block scales.
+//   F16, BF16, F32: plain values, 8 (16) chunks per unit, no aux.
 // Q5_K has no device-matrix layout (it is read only through the raw dequantiser).
 #pragma once
 #include <cstdint>
@@ -31,10 +34,9 @@ constexpr uint32_t GGML_F32 = 0, GGML_F16 = 1, GGML_Q8_0 = 8, GGML_Q4_K = 12, GG
 struct QMatDev {
     uint32_t type = 0;
     uint32_t rows = 0, cols = 0;
-    uint32_t nunits = 0;          // 64-value units per row
-    const uint8_t* q = nullptr;   // chunk payload, row stride = nunits * chunks * 16
-    const uint8_t* aux = nullptr; // see above
-    const uint16_t* d = nullptr;  // Q6_K super-block scales
+    uint32_t nunits = 0;         // 64-value units per row
+    uint32_t row_bytes = 0;      // bytes per row (sum of its tiles)
+    const uint8_t* q = nullptr;  // rows * row_bytes
 };
 
 __host__ __device__ inline uint32_t chunks_per_unit(uint32_t type) {
@@ -49,12 +51,51 @@ __host__ __device__ inline uint32_t chunks_per_unit(uint32_t type) {
     }
 }
 
-// Byte offset of chunk c of unit u inside one row's payload.
-__host__ __device__ inline uint64_t chunk_offset(uint32_t nunits, uint32_t chunks, uint32_t u, uint32_t c) {
-    uint32_t g = u >> 5, lane = u & 31;
-    uint32_t rest = nunits - (g << 5);
-    uint32_t gsize = rest < 32u ? rest : 32u;
-    return (uint64_t)g * 32u * chunks * 16u + (uint64_t)c * gsize * 16u + (uint64_t)lane * 16u;
+__host__ __device__ inline uint32_t pad16(uint32_t v) { return (v + 15u) & ~15u; }
+
+// Sections of one tile of U units.
+__host__ __device__ inline uint32_t tile_payload_bytes(uint32_t type, uint32_t U) {
+    return U * chunks_per_unit(type) * 16u;
+}
+__host__ __device__ inline uint32_t tile_aux_bytes(uint32_t type, uint32_t U) {
+    switch (type) {
+        case GGML_Q4_K: return (U / 4u) * 16u;
+        case GGML_Q6_K:
+        case GGML_Q8_0: return pad16(U * 4u);
+        default: return 0;
+    }
+}
+__host__ __device__ inline uint32_t tile_d_bytes(uint32_t type, uint32_t U) {
+    return type == GGML_Q6_K ? pad16((U / 4u) * 2u) : 0u;
+}
+__host__ __device__ inline uint32_t tile_bytes(uint32_t type, uint32_t U) {
+    return tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + tile_d_bytes(type, U);
+}
+// Units in group g of a row of `nunits` units.
+__host__ __device__ inline uint32_t group_units(uint32_t nunits, uint32_t g) {
+    const uint32_t rest = nunits - g * 32u;
+    return rest < 32u ? rest : 32u;
+}
+__host__ __device__ inline uint32_t row_tile_bytes(uint32_t type, uint32_t nunits) {
+    return (nunits / 32u) * tile_bytes(type, 32u) + ((nunits % 32u) ? tile_bytes(type, nunits % 32u) : 0u);
+}
+// Byte offset of tile g inside a row (all full tiles precede it).
+__host__ __device__ inline uint32_t tile_offset(uint32_t type, uint32_t g) { return g * tile_bytes(type, 32u); }
+// Byte offset of chunk c of unit u inside a row.
+__host__ __device__ inline uint32_t chunk_offset(uint32_t type, uint32_t nunits, uint32_t u, uint32_t c) {
+    const uint32_t g = u >> 5;
+    return tile_offset(type, g) + c * group_units(nunits, g) * 16u + (u & 31u) * 16u;
+}
+// Byte offset of the aux entry of unit u (Q6_K, Q8_0: u32 per unit; Q4_K: 16-byte
+// header of u's super-block) inside a row.
+__host__ __device__ inline uint32_t aux_offset(uint32_t type, uint32_t nunits, uint32_t u) {
+    const uint32_t g = u >> 5, U = group_units(nunits, g), base = tile_offset(type, g) + tile_payload_bytes(type, U);
+    return type == GGML_Q4_K ? base + ((u & 31u) / 4u) * 16u : base + (u & 31u) * 4u;
+}
+// Byte offset of the Q6_K f16 super-block scale of unit u inside a row.
+__host__ __device__ inline uint32_t d_offset(uint32_t type, uint32_t nunits, uint32_t u) {
+    const uint32_t g = u >> 5, U = group_units(nunits, g);
+    return tile_offset(type, g) + tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + ((u & 31u) / 4u) * 2u;
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

@@ -125,16 +125,16 @@ private:
 struct QMatrix {
     std::string name;
     uint32_t type = 0, rows = 0, cols = 0;
-    size_t payload_bytes = 0, aux_bytes = 0, d_bytes = 0;
-    size_t offset = 0;  // inside the model's weight buffer
-    QMatDev dev;        // device pointers once placed
-    size_t bytes() const { return payload_bytes + aux_bytes + d_bytes; }
+    size_t total_bytes = 0;  // rows * row_bytes, rounded up to 256
+    size_t offset = 0;       // inside the model's weight buffer
+    QMatDev dev;             // device view once placed
+    size_t bytes() const { return total_bytes; }
 };
 
 // Sizes of the repacked form of a [rows][cols] tensor of `type`; raises Unsupported.
 void repack_sizes(QMatrix& m);
 // Repacks raw GGUF rows [rows][type_bytes(type, cols)] (already sliced to the shard)
-// into host memory at dst (payload, then aux, then d), using `threads` threads.
+// into host memory at dst (the tile layout of common.cuh), using `threads` threads.
 void repack_host(const QMatrix& m, const uint8_t* raw, size_t raw_row_stride, uint8_t* dst, int threads);
 // Points m.dev at base + m.offset.
 void place(QMatrix& m, uint8_t* base);
@@ -190,8 +190,9 @@ void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s);
 
 // Device launch sequence of one dense FFN on `x` (already normalised when norm_w is
 // null) writing y; add=true accumulates into y (residual). TP: partial + all-reduce.
+// `next` (may be null) is the matrix the launch after the FFN reads (warmed into L2).
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
-                   float* h_buf, float* y_buf, cudaStream_t s, bool pdl);
+                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl);
 
 // ------------------------------------------------------------------ sessions
 struct StepBuffers {
@@ -243,5 +244,6 @@ struct evl_batch {
 struct evl_qmatrix {
     evl::QMatrix m;
     evl::DeviceBuffer buf;
+    evl::DeviceBuffer err;  // device error flag of this matrix's launches
     int device = 0;
 };

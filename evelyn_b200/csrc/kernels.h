@@ -35,9 +35,13 @@ struct MatvecArgs {
     const float* norm_w = nullptr; // fused RMSNorm weight (null: x used as is)
     float eps = 1e-6f;
     float* x_out = nullptr;        // if set, the (normalised) input is also written here
+    QMatDev prefetch;              // matrix the next launch reads (q == null: none); its
+                                   // first rows are warmed into L2 at the end
+    int* err = nullptr;            // device error flag (DeviceError), required
 };
 
-// One fused launch over up to three matrices that share the input vector.
+// One fused launch over up to three matrices that share the input vector (all of
+// the same width). Types Q4_K, Q6_K, Q8_0.
 cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------- attention.cu

@@ -332,7 +332,7 @@ void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s) {
 }
 
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
-                   float* h_buf, float* y_buf, cudaStream_t s, bool pdl) {
+                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl) {
     const LayerWeights& L = m.layers[layer];
     const uint32_t dim = (uint32_t)m.cfg.dim;
     for (uint32_t b = 0; b < batch; ++b) {
@@ -346,6 +346,8 @@ void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, 
         a.cols = dim;
         a.norm_w = norm_w;
         a.eps = m.cfg.eps;
+        a.err = err;
+        if (b + 1 == batch) a.prefetch = L.down.dev;
         cuda_check(launch_qmatvec(a, s, pdl), "ffn gate/up");
     }
     const bool tp = m.tp_size > 1;
@@ -357,6 +359,8 @@ void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, 
         a.seg[0].epi = (add && !tp) ? EPI_ADD : EPI_STORE;
         a.x = h_buf + (size_t)b * m.lffn;
         a.cols = m.lffn;
+        a.err = err;
+        if (next && b + 1 == batch) a.prefetch = *next;
         cuda_check(launch_qmatvec(a, s, pdl), "ffn down");
     }
     if (tp) {

@@ -1,20 +1,30 @@
 // qmatvec.cu -- dequant-fused matrix-vector products for Q4_K, Q6_K and Q8_0.
 //
 // Replaces QMatrix::matvec (src/runtime.rs:72-88), which dequantises every row into
-// a fresh Vec<f32> and sums sequentially. Here the quantised blocks stream from HBM
-// with 128-bit non-allocating loads (the unit-interleaved layout of common.cuh), are
-// unpacked in registers with integer byte permutes (2^23 magic-number conversion:
-// exact for 0..255), and meet the input vector, which every CTA stages once in
-// shared memory in the unit order of the matrix type (64 values + 4 pad floats per
-// unit, so the 32 lanes of a warp hit distinct banks). Each warp owns NR rows at a
-// time and reuses each x register NR times; f32 pairs go through the sm_100 packed
-// FFMA2/FADD2 pipes. The block scales are applied once per 32 (Q4_K, Q8_0) or 16
-// (Q6_K) values per row, the Q4_K minimum term through per-32 sums of x.
+// a fresh Vec<f32> and sums sequentially in f32.
 //
-// Optional fused prologue: RMSNorm of the input (src/runtime.rs:193-196) with the
-// reference's evaluation order v*inv*g.  Epilogues: store, residual add
-// (src/runtime.rs:798-804), and SwiGLU silu(g)*u over paired gate/up rows
-// (src/runtime.rs:409-418, src/activation.rs:50).
+// Shape of the kernel (one persistent CTA per SM, warp-specialised):
+//   * a producer warp streams the CTA's contiguous range of 32-row blocks, one
+//     32-unit column tile at a time, from HBM into a ring of shared-memory stages
+//     with TMA bulk copies (cp.async.bulk + mbarrier complete_tx). It needs nothing
+//     from the previous kernel, so it starts before griddepcontrol.wait and keeps the
+//     ring full across the kernel boundary; after its last copy it prefetches the
+//     next matrix's first tiles into L2;
+//   * eight consumer warps stage the input vector once per CTA as 24-bit block
+//     fixed point -- per 32-value block x = 2^-s * m, |m| < 2^22, m split into three
+//     signed 8-bit limbs -- then run the dot products on the raw quant bytes with
+//     integer dp4a (4 products per instruction), four rows per warp per stage, one
+//     64-value unit per lane. Block scales (d*s_j, dmin*m_j, Q6_K int8 scales, the
+//     2^-s of x) are applied in f32 once per 32 (Q4_K, Q8_0) or 16 (Q6_K) values.
+// The integer products are exact, so the only rounding against the reference's
+// f32 loop is the 2^-22-relative quantisation of x and the order of the f32 sums.
+//
+// Optional fused prologue: RMSNorm of the input (src/runtime.rs:193-196) in the
+// reference's v*inv*g order. Epilogues: store, residual add (src/runtime.rs:798-804),
+// and SwiGLU silu(g)*u over paired gate/up rows (src/runtime.rs:409-418,
+// src/activation.rs:50).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -22,285 +32,438 @@ namespace evl {
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kUnitStride = 68;  // floats per unit in shared memory
-constexpr float kMagic = 8388608.0f;
+constexpr int kCW = 8;                // consumer warps
+constexpr int kThreads = 32 * (kCW + 1);
+constexpr int kNR = 4;                 // row slots per consumer warp
+constexpr int kRB = kCW * kNR;         // 32 row slots per stage
+constexpr int kLimbStride = 208;       // bytes of limbs per unit: 3 x 64 + 16 pad (bank spread)
+constexpr int kMaxStages = 8;
+constexpr uint32_t kSmemBudget = 225 * 1024;
+constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the 256 consumer threads
 
-__device__ __forceinline__ uint32_t word(const uint4& v, int t) {
-    return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
-}
+// need bits
+constexpr uint32_t NEED_NAT = 1, NEED_Q6 = 2, NEED_XSUM = 4, NEED_MSUM = 8;
 
-__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-
-// 4 bytes of w (each 0..255) as exact floats minus `bias`, multiplied into acc.
-__device__ __forceinline__ void fma_bytes(uint32_t w, float bias, float4 x, float2& acc) {
-    const float2 nb = f2(-bias, -bias);
-    float2 a = __fadd2_rn(f2(byte_magic(w, 0x7650), byte_magic(w, 0x7651)), nb);
-    float2 b = __fadd2_rn(f2(byte_magic(w, 0x7652), byte_magic(w, 0x7653)), nb);
-    acc = __ffma2_rn(a, f2(x.x, x.y), acc);
-    acc = __ffma2_rn(b, f2(x.z, x.w), acc);
-}
-
-struct RowPtrs {
-    const uint8_t* q;
-    const uint8_t* aux;
-    const uint16_t* d;
+struct Plan {
+    MatvecArgs a;
+    uint32_t rb_begin[kMaxSegs + 1];  // first row-block of each segment (+ total)
+    uint32_t nunits, ngroups;
+    uint32_t slot_bytes, stages, need;
+    uint32_t off_nat, off_q6, off_fscale, off_xsum, off_msum;  // smem offsets after the ring
+    uint32_t smem_bytes;
+    const uint8_t* pf_base;  // next matrix to prefetch into L2 (optional)
+    uint32_t pf_row_bytes, pf_rows;
+    int* err;
 };
 
-// ---------------------------------------------------------------- Q4_K
-template <int NR>
-__device__ __forceinline__ void dot_q4k(const RowPtrs (&rp)[NR], uint32_t nunits, const float* __restrict__ xs,
-                                        const float* __restrict__ xsum, int lane, float (&acc)[NR]) {
-    for (uint32_t u = lane; u < nunits; u += 32) {
-        const uint64_t o0 = chunk_offset(nunits, 2, u, 0), o1 = chunk_offset(nunits, 2, u, 1);
-        uint4 w0[NR], w1[NR], hd[NR];
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-            w0[i] = ldg_nc(rp[i].q + o0);
-            w1[i] = ldg_nc(rp[i].q + o1);
-            hd[i] = ldg_nc_keep(rp[i].aux + (u >> 2) * 16);
-        }
-        const float* xu = xs + u * kUnitStride;
-        float2 p1[NR], p2[NR];
-#pragma unroll
-        for (int i = 0; i < NR; ++i) p1[i] = p2[i] = f2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float4 xl = *reinterpret_cast<const float4*>(xu + 16 * c + 4 * t);
-                const float4 xh = *reinterpret_cast<const float4*>(xu + 32 + 16 * c + 4 * t);
-#pragma unroll
-                for (int i = 0; i < NR; ++i) {
-                    const uint32_t wd = word(c == 0 ? w0[i] : w1[i], t);
-                    fma_bytes(wd & 0x0F0F0F0Fu, kMagic, xl, p1[i]);
-                    fma_bytes((wd >> 4) & 0x0F0F0F0Fu, kMagic, xh, p2[i]);
-                }
-            }
-        }
-        const float X1 = xsum[2 * u], X2 = xsum[2 * u + 1];
-        const uint32_t j = u & 3, k = (2 * j) & 3, sh = 8 * k;
-        const bool high = j >= 2;
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-            const float d = h2f(hd[i].x & 0xffff), dmin = h2f(hd[i].x >> 16);
-            const uint32_t w0s = hd[i].y >> sh, w1s = hd[i].z >> sh, w2s = hd[i].w >> sh;
-            // get_scale_min_k4 (src/gguf.rs:327-336) for sub-blocks 2j and 2j+1:
-            // bytes k and k+1 of each scale word
-            uint32_t s1, m1, s2, m2;
-            if (!high) {
-                s1 = w0s & 63; m1 = w1s & 63;
-                s2 = (w0s >> 8) & 63; m2 = (w1s >> 8) & 63;
-            } else {
-                s1 = (w2s & 15) | (((w0s >> 6) & 3) << 4);
-                m1 = ((w2s >> 4) & 15) | (((w1s >> 6) & 3) << 4);
-                s2 = ((w2s >> 8) & 15) | (((w0s >> 14) & 3) << 4);
-                m2 = ((w2s >> 12) & 15) | (((w1s >> 14) & 3) << 4);
-            }
-            const float dot = (float)s1 * (p1[i].x + p1[i].y) + (float)s2 * (p2[i].x + p2[i].y);
-            const float mn = (float)m1 * X1 + (float)m2 * X2;
-            acc[i] += d * dot - dmin * mn;
-        }
-    }
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// ---------------------------------------------------------------- Q6_K
-template <int NR>
-__device__ __forceinline__ void dot_q6k(const RowPtrs (&rp)[NR], uint32_t nunits, const float* __restrict__ xs,
-                                        int lane, float (&acc)[NR]) {
-    for (uint32_t u = lane; u < nunits; u += 32) {
-        const uint64_t o0 = chunk_offset(nunits, 3, u, 0), o1 = chunk_offset(nunits, 3, u, 1),
-                       o2 = chunk_offset(nunits, 3, u, 2);
-        uint4 lo[NR], hi[NR], qh[NR];
-        uint32_t scw[NR];
-        uint16_t dd[NR];
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-            lo[i] = ldg_nc(rp[i].q + o0);
-            hi[i] = ldg_nc(rp[i].q + o1);
-            qh[i] = ldg_nc(rp[i].q + o2);
-            scw[i] = __ldg(reinterpret_cast<const uint32_t*>(rp[i].aux) + u);
-            dd[i] = __ldg(rp[i].d + (u >> 2));
-        }
-        const float* xu = xs + u * kUnitStride;
-        float2 p[NR][4];
-#pragma unroll
-        for (int i = 0; i < NR; ++i)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) p[i][k] = f2(0.f, 0.f);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const float4 x0 = *reinterpret_cast<const float4*>(xu + 0 + 4 * t);
-            const float4 x1 = *reinterpret_cast<const float4*>(xu + 16 + 4 * t);
-            const float4 x2 = *reinterpret_cast<const float4*>(xu + 32 + 4 * t);
-            const float4 x3 = *reinterpret_cast<const float4*>(xu + 48 + 4 * t);
-#pragma unroll
-            for (int i = 0; i < NR; ++i) {
-                const uint32_t L = word(lo[i], t), H = word(hi[i], t), Q = word(qh[i], t);
-                const uint32_t q0 = (L & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u);
-                const uint32_t q1 = (H & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u);
-                const uint32_t q2 = ((L >> 4) & 0x0F0F0F0Fu) | (Q & 0x30303030u);
-                const uint32_t q3 = ((H >> 4) & 0x0F0F0F0Fu) | ((Q >> 2) & 0x30303030u);
-                fma_bytes(q0, kMagic + 32.f, x0, p[i][0]);
-                fma_bytes(q1, kMagic + 32.f, x1, p[i][1]);
-                fma_bytes(q2, kMagic + 32.f, x2, p[i][2]);
-                fma_bytes(q3, kMagic + 32.f, x3, p[i][3]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-            const float d = h2f(dd[i]);
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) s += (float)(int8_t)((scw[i] >> (8 * k)) & 0xff) * (p[i][k].x + p[i][k].y);
-            acc[i] += d * s;
-        }
-    }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// ---------------------------------------------------------------- Q8_0
-template <int NR>
-__device__ __forceinline__ void dot_q8_0(const RowPtrs (&rp)[NR], uint32_t nunits, const float* __restrict__ xs,
-                                         int lane, float (&acc)[NR]) {
-    for (uint32_t u = lane; u < nunits; u += 32) {
-        uint4 w[NR][4];
-        uint32_t dw[NR];
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) w[i][c] = ldg_nc(rp[i].q + chunk_offset(nunits, 4, u, c));
-            dw[i] = __ldg(reinterpret_cast<const uint32_t*>(rp[i].aux) + u);
+// Bounded wait that also gives up as soon as another thread of the CTA has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            *abort_flag = 1;
+            return false;
         }
-        const float* xu = xs + u * kUnitStride;
-        float2 p0[NR], p1[NR];
-#pragma unroll
-        for (int i = 0; i < NR; ++i) p0[i] = p1[i] = f2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float4 xv = *reinterpret_cast<const float4*>(xu + 16 * c + 4 * t);
-#pragma unroll
-                for (int i = 0; i < NR; ++i) {
-                    const uint32_t wd = word(w[i][c], t) ^ 0x80808080u;  // int8 -> q + 128
-                    fma_bytes(wd, kMagic + 128.f, xv, c < 2 ? p0[i] : p1[i]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < NR; ++i)
-            acc[i] += h2f(dw[i] & 0xffff) * (p0[i].x + p0[i].y) + h2f(dw[i] >> 16) * (p1[i].x + p1[i].y);
     }
-}
-
-__device__ __forceinline__ RowPtrs row_ptrs(const QMatDev& m, uint32_t r) {
-    const uint32_t ch = chunks_per_unit(m.type);
-    RowPtrs p;
-    p.q = m.q + (uint64_t)r * m.nunits * ch * 16;
-    p.d = nullptr;
-    switch (m.type) {
-        case GGML_Q4_K: p.aux = m.aux + (uint64_t)r * (m.cols / 256) * 16; break;
-        case GGML_Q6_K:
-            p.aux = m.aux + (uint64_t)r * m.nunits * 4;
-            p.d = m.d + (uint64_t)r * (m.cols / 256);
-            break;
-        default: p.aux = m.aux + (uint64_t)r * m.nunits * 4; break;
-    }
-    return p;
+    return true;
 }
 
 __device__ __forceinline__ float silu(float z) { return __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))); }
 
-template <int NR>
-__global__ void __launch_bounds__(kThreads) qmatvec_kernel(const __grid_constant__ MatvecArgs a, uint32_t need_layouts,
-                                                           uint32_t total_rg, uint32_t rg_begin1, uint32_t rg_begin2) {
-    extern __shared__ __align__(16) float smem[];
-    const uint32_t nunits = a.cols / 64;
-    float* xs_nat = smem;
-    float* xs_q6 = smem + ((need_layouts & 1) ? nunits * kUnitStride : 0);
-    float* xsum = xs_q6 + ((need_layouts & 2) ? nunits * kUnitStride : 0);
-    __shared__ float red[kWarps];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__device__ __forceinline__ int seg_of(const Plan& p, uint32_t rb) {
+    return rb >= p.rb_begin[2] ? 2 : rb >= p.rb_begin[1] ? 1 : 0;
+}
 
-    pdl_wait();
+// Row slot i of a row-block: which matrix and row it holds.
+__device__ __forceinline__ const QMatDev& slot_matrix(const MatvecSeg& sg, uint32_t local, uint32_t i, uint32_t* row) {
+    if (sg.epi == EPI_SWIGLU) {
+        *row = local * (kRB / 2) + (i & (kRB / 2 - 1));
+        return i < (uint32_t)kRB / 2 ? sg.m : sg.m2;
+    }
+    *row = local * kRB + i;
+    return sg.m;
+}
+
+// ---------------------------------------------------------------- per-unit dot products
+// Each returns, per row slot, the f32 contribution of one 64-value unit.
+
+// Q4_K: low nibbles of the 32 qs bytes are values 0..31 of the unit (sub-block A),
+// high nibbles values 32..63 (sub-block B).
+__device__ __forceinline__ void unit_q4k(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
+                                         const uint8_t* limbs, const float* fscale, const float* xsum,
+                                         float (&acc)[kNR]) {
+    int SA[kNR][3], SB[kNR][3];
+#pragma unroll
+    for (int i = 0; i < kNR; ++i)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) SA[i][k] = SB[i][k] = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // qs chunk `half`: words t = 4*half .. 4*half+3
+        int4 la[3], lb[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            la[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 16 * half);
+            lb[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 32 + 16 * half);
+        }
+#pragma unroll
+        for (int i = 0; i < kNR; ++i) {
+            const int4 w = *reinterpret_cast<const int4*>(tiles[i] + half * U * 16 + lane * 16);
+            const int wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int lo = wv[t] & 0x0F0F0F0F, hi = (wv[t] >> 4) & 0x0F0F0F0F;
+                const int a0 = t == 0 ? la[0].x : t == 1 ? la[0].y : t == 2 ? la[0].z : la[0].w;
+                const int a1 = t == 0 ? la[1].x : t == 1 ? la[1].y : t == 2 ? la[1].z : la[1].w;
+                const int a2 = t == 0 ? la[2].x : t == 1 ? la[2].y : t == 2 ? la[2].z : la[2].w;
+                const int b0 = t == 0 ? lb[0].x : t == 1 ? lb[0].y : t == 2 ? lb[0].z : lb[0].w;
+                const int b1 = t == 0 ? lb[1].x : t == 1 ? lb[1].y : t == 2 ? lb[1].z : lb[1].w;
+                const int b2 = t == 0 ? lb[2].x : t == 1 ? lb[2].y : t == 2 ? lb[2].z : lb[2].w;
+                SA[i][0] = dp4a(lo, a0, SA[i][0]);
+                SA[i][1] = dp4a(lo, a1, SA[i][1]);
+                SA[i][2] = dp4a(lo, a2, SA[i][2]);
+                SB[i][0] = dp4a(hi, b0, SB[i][0]);
+                SB[i][1] = dp4a(hi, b1, SB[i][1]);
+                SB[i][2] = dp4a(hi, b2, SB[i][2]);
+            }
+        }
+    }
+    const float fa = fscale[2 * u], fb = fscale[2 * u + 1];
+    const float XA = xsum[2 * u], XB = xsum[2 * u + 1];
+    const uint32_t j = u & 3, sh = 8 * ((2 * j) & 3);
+    const bool high = j >= 2;
+#pragma unroll
+    for (int i = 0; i < kNR; ++i) {
+        const uint4 hd = *reinterpret_cast<const uint4*>(tiles[i] + U * 32 + (lane / 4) * 16);
+        const float d = h2f(hd.x & 0xffff), dmin = h2f(hd.x >> 16);
+        const uint32_t w0s = hd.y >> sh, w1s = hd.z >> sh, w2s = hd.w >> sh;
+        // get_scale_min_k4 (src/gguf.rs:327-336) for sub-blocks 2j, 2j+1
+        uint32_t s1, m1, s2, m2;
+        if (!high) {
+            s1 = w0s & 63; m1 = w1s & 63;
+            s2 = (w0s >> 8) & 63; m2 = (w1s >> 8) & 63;
+        } else {
+            s1 = (w2s & 15) | (((w0s >> 6) & 3) << 4);
+            m1 = ((w2s >> 4) & 15) | (((w1s >> 6) & 3) << 4);
+            s2 = ((w2s >> 8) & 15) | (((w0s >> 14) & 3) << 4);
+            m2 = ((w2s >> 12) & 15) | (((w1s >> 14) & 3) << 4);
+        }
+        const float va = fmaf((float)SA[i][2], 65536.f, (float)(SA[i][0] + 256 * SA[i][1])) * fa;
+        const float vb = fmaf((float)SB[i][2], 65536.f, (float)(SB[i][0] + 256 * SB[i][1])) * fb;
+        acc[i] += d * ((float)s1 * va + (float)s2 * vb) - dmin * ((float)m1 * XA + (float)m2 * XB);
+    }
+}
+
+// Q6_K: unit (super-block, half h, l0) holds values 128h + 32k + l0 + l for k = 0..3,
+// l < 16; its limbs are stored [limb][l/4][k][l%4].
+__device__ __forceinline__ void unit_q6k(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
+                                         const uint8_t* limbs, const float* fscale, const int* msum,
+                                         float (&acc)[kNR]) {
+    int S[kNR][4][3];
+#pragma unroll
+    for (int i = 0; i < kNR; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) S[i][k][0] = S[i][k][1] = S[i][k][2] = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        int4 lv[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) lv[c] = *reinterpret_cast<const int4*>(limbs + c * 64 + 16 * t);
+#pragma unroll
+        for (int i = 0; i < kNR; ++i) {
+            const uint8_t* base = tiles[i] + lane * 16 + 4 * t;
+            const uint32_t L = *reinterpret_cast<const uint32_t*>(base);
+            const uint32_t H = *reinterpret_cast<const uint32_t*>(base + U * 16);
+            const uint32_t Q = *reinterpret_cast<const uint32_t*>(base + 2 * U * 16);
+            const int q0 = (int)((L & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u));
+            const int q1 = (int)((H & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u));
+            const int q2 = (int)(((L >> 4) & 0x0F0F0F0Fu) | (Q & 0x30303030u));
+            const int q3 = (int)(((H >> 4) & 0x0F0F0F0Fu) | ((Q >> 2) & 0x30303030u));
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                S[i][0][c] = dp4a(q0, lv[c].x, S[i][0][c]);
+                S[i][1][c] = dp4a(q1, lv[c].y, S[i][1][c]);
+                S[i][2][c] = dp4a(q2, lv[c].z, S[i][2][c]);
+                S[i][3][c] = dp4a(q3, lv[c].w, S[i][3][c]);
+            }
+        }
+    }
+    // x-block of run k: 8*(u/4) + 4*h + k with h = (u/2) & 1
+    const uint32_t jb = 8 * (u >> 2) + 4 * ((u >> 1) & 1);
+    const int* ms = msum + u * 12;  // [k][limb] sums of the limbs (the -32 bias)
+#pragma unroll
+    for (int i = 0; i < kNR; ++i) {
+        const uint32_t scw = *reinterpret_cast<const uint32_t*>(tiles[i] + U * 48 + lane * 4);
+        const uint32_t dh = *reinterpret_cast<const uint16_t*>(tiles[i] + U * 48 + pad16(U * 4) + (lane / 4) * 2);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int a = S[i][k][0] - 32 * ms[3 * k], b = S[i][k][1] - 32 * ms[3 * k + 1],
+                      c = S[i][k][2] - 32 * ms[3 * k + 2];
+            const float v = fmaf((float)c, 65536.f, (float)(a + 256 * b)) * fscale[jb + k];
+            s = fmaf((float)(int8_t)((scw >> (8 * k)) & 0xff), v, s);
+        }
+        acc[i] = fmaf(h2f(dh), s, acc[i]);
+    }
+}
+
+// Q8_0: two 32-value blocks per unit.
+__device__ __forceinline__ void unit_q8_0(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
+                                          const uint8_t* limbs, const float* fscale, float (&acc)[kNR]) {
+    int S[kNR][2][3];
+#pragma unroll
+    for (int i = 0; i < kNR; ++i)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) S[i][b][0] = S[i][b][1] = S[i][b][2] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        int4 lv[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) lv[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 16 * c);
+#pragma unroll
+        for (int i = 0; i < kNR; ++i) {
+            const int4 w = *reinterpret_cast<const int4*>(tiles[i] + c * U * 16 + lane * 16);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                int s = S[i][c >> 1][k];
+                s = dp4a(w.x, lv[k].x, s);
+                s = dp4a(w.y, lv[k].y, s);
+                s = dp4a(w.z, lv[k].z, s);
+                s = dp4a(w.w, lv[k].w, s);
+                S[i][c >> 1][k] = s;
+            }
+        }
+    }
+    const float f0 = fscale[2 * u], f1 = fscale[2 * u + 1];
+#pragma unroll
+    for (int i = 0; i < kNR; ++i) {
+        const uint32_t dw = *reinterpret_cast<const uint32_t*>(tiles[i] + U * 64 + lane * 4);
+        const float v0 = fmaf((float)S[i][0][2], 65536.f, (float)(S[i][0][0] + 256 * S[i][0][1])) * f0;
+        const float v1 = fmaf((float)S[i][1][2], 65536.f, (float)(S[i][1][0] + 256 * S[i][1][1])) * f1;
+        acc[i] += h2f(dw & 0xffff) * v0 + h2f(dw >> 16) * v1;
+    }
+}
+
+// ---------------------------------------------------------------- input staging
+// x (optionally RMS-normalised) -> per-32-block scale 2^-s and 3 int8 limbs per value.
+__device__ void stage_input(const Plan& p, uint8_t* smem, int warp, int lane, float* red) {
+    const MatvecArgs& a = p.a;
+    const uint32_t K = a.cols;
     float inv = 1.f;
     if (a.norm_w) {
         float ss = 0.f;
-        for (uint32_t i = tid; i < a.cols; i += kThreads) {
-            float v = a.x[i];
+        for (uint32_t i = warp * 32 + lane; i < K; i += kCW * 32) {
+            const float v = a.x[i];
             ss += v * v;
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
-        __syncthreads();
+        named_sync(kConsumerBarrier, kCW * 32);
         ss = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) ss += red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
+        for (int w = 0; w < kCW; ++w) ss += red[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
     }
-    for (uint32_t i = tid; i < a.cols; i += kThreads) {
+    uint8_t* nat = smem + p.off_nat;
+    uint8_t* q6 = smem + p.off_q6;
+    float* fscale = reinterpret_cast<float*>(smem + p.off_fscale);
+    float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
+    int* msum = reinterpret_cast<int*>(smem + p.off_msum);
+    for (uint32_t j = warp; j < K / 32; j += kCW) {
+        const uint32_t i = 32 * j + lane;
         float v = a.x[i];
         if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
         if (a.x_out && blockIdx.x == 0) a.x_out[i] = v;
-        if (need_layouts & 1) xs_nat[(i >> 6) * kUnitStride + (i & 63)] = v;
-        if (need_layouts & 2) {
-            const uint32_t r = i & 255, h = r >> 7, k = (r >> 5) & 3, b = (r >> 4) & 1, l = r & 15;
-            const uint32_t u = (i >> 8) * 4 + h * 2 + b;
-            xs_q6[u * kUnitStride + k * 16 + l] = v;
+        const float amax = warp_max(fabsf(v));
+        int s = 0;
+        if (amax > 0.f) {
+            int e;
+            frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+            s = min(max(22 - e, -100), 120);
         }
+        const int m = __float2int_rn(ldexpf(v, s));
+        const int l0 = (m << 24) >> 24;
+        const int r1 = (m - l0) >> 8;
+        const int l1 = (r1 << 24) >> 24;
+        const int l2 = (r1 - l1) >> 8;
+        if (lane == 0) fscale[j] = ldexpf(1.0f, -s);
+        if (p.need & NEED_XSUM) {
+            const float sum = warp_sum(v);
+            if (lane == 0) xsum[j] = sum;
+        }
+        if (p.need & NEED_NAT) {
+            uint8_t* b = nat + (j >> 1) * kLimbStride + (j & 1) * 32 + lane;
+            b[0] = (uint8_t)l0;
+            b[64] = (uint8_t)l1;
+            b[128] = (uint8_t)l2;
+        }
+        if (p.need & NEED_Q6) {
+            const uint32_t r8 = i & 255, h = r8 >> 7, k = (r8 >> 5) & 3, bb = lane >> 4, l = lane & 15;
+            const uint32_t u = (i >> 8) * 4 + h * 2 + bb;
+            uint8_t* b = q6 + u * kLimbStride + (l >> 2) * 16 + k * 4 + (l & 3);
+            b[0] = (uint8_t)l0;
+            b[64] = (uint8_t)l1;
+            b[128] = (uint8_t)l2;
+            if (p.need & NEED_MSUM) {  // per 16-value run: sums of each limb
+                int s0 = l0, s1 = l1, s2 = l2;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) {
+                    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+                }
+                if (l == 0) {
+                    int* ms = msum + u * 12 + 3 * k;
+                    ms[0] = s0;
+                    ms[1] = s1;
+                    ms[2] = s2;
+                }
+            }
+        }
+    }
+    named_sync(kConsumerBarrier, kCW * 32);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_constant__ Plan p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ float red[kCW];
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t total = p.rb_begin[3];
+    const uint32_t rb0 = (uint32_t)(((uint64_t)total * blockIdx.x) / gridDim.x);
+    const uint32_t rb1 = (uint32_t)(((uint64_t)total * (blockIdx.x + 1)) / gridDim.x);
+    const uint32_t S = p.stages, G = p.ngroups;
+
+    if (tid == 0) {
+        abort_flag = 0;
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        fence_barrier_init();
     }
     __syncthreads();
-    if (need_layouts & 4) {  // per-32 sums for the Q4_K minimum term
-        for (uint32_t s = tid; s < a.cols / 32; s += kThreads) {
-            const float* p = xs_nat + (s >> 1) * kUnitStride + (s & 1) * 32;
-            float acc = 0.f;
-#pragma unroll 8
-            for (int e = 0; e < 32; ++e) acc += p[e];
-            xsum[s] = acc;
-        }
-        __syncthreads();
-    }
-    pdl_launch_dependents();
 
-    const uint32_t stride = gridDim.x * kWarps;
-    for (uint32_t rg = blockIdx.x * kWarps + warp; rg < total_rg; rg += stride) {
-        const int si = rg >= rg_begin2 ? 2 : rg >= rg_begin1 ? 1 : 0;
-        const MatvecSeg& sg = a.seg[si];
-        const uint32_t local = rg - (si == 2 ? rg_begin2 : si == 1 ? rg_begin1 : 0);
+    if (warp == kCW) {
+        // ------------------------------------------------------------ producer
+        if (lane != 0) return;
+        uint32_t item = 0;
+        for (uint32_t rb = rb0; rb < rb1 && !abort_flag; ++rb) {
+            const int si = seg_of(p, rb);
+            const MatvecSeg& sg = p.a.seg[si];
+            const uint32_t local = rb - p.rb_begin[si];
+            const uint32_t T = sg.m.type;
+            for (uint32_t g = 0; g < G; ++g, ++item) {
+                const uint32_t s = item % S, n = item / S;
+                if (n > 0 && !wait_or_abort(&empty[s], (n - 1) & 1, &abort_flag)) break;
+                const uint32_t U = group_units(p.nunits, g), tb = tile_bytes(T, U);
+                uint8_t* slot = smem + s * p.slot_bytes;
+                uint32_t valid = 0;
+                for (uint32_t i = 0; i < (uint32_t)kRB; ++i) {
+                    uint32_t row;
+                    const QMatDev& m = slot_matrix(sg, local, i, &row);
+                    valid += row < m.rows;
+                }
+                mbar_arrive_expect_tx(&full[s], valid * tb);
+                for (uint32_t i = 0; i < (uint32_t)kRB; ++i) {
+                    uint32_t row;
+                    const QMatDev& m = slot_matrix(sg, local, i, &row);
+                    if (row < m.rows)
+                        tma_load_1d(slot + i * tb, m.q + (uint64_t)row * m.row_bytes + tile_offset(T, g), tb, &full[s]);
+                }
+            }
+        }
+        if (p.pf_base && p.pf_rows) {  // warm L2 with the next matrix's first rows for this CTA
+            const uint32_t pr0 = (uint32_t)(((uint64_t)p.pf_rows * blockIdx.x) / gridDim.x);
+            const uint32_t pr1 = (uint32_t)(((uint64_t)p.pf_rows * (blockIdx.x + 1)) / gridDim.x);
+            uint64_t bytes = (uint64_t)(pr1 - pr0) * p.pf_row_bytes;
+            if (bytes > (96u << 10)) bytes = 96u << 10;
+            const uint8_t* base = p.pf_base + (uint64_t)pr0 * p.pf_row_bytes;
+            for (uint64_t o = 0; o < bytes; o += 16384)
+                prefetch_l2_bulk(base + o, (uint32_t)((bytes - o) < 16384 ? (bytes - o) & ~15ull : 16384));
+        }
+        if (abort_flag) {  // give copies in flight a bounded chance to land before exiting
+            for (uint32_t s = 0; s < S && s < item; ++s) mbar_wait(&full[s], ((item - 1 - s) / S) & 1);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    pdl_wait();
+    stage_input(p, smem, warp, lane, red);
+    pdl_launch_dependents();
+    const uint8_t* nat = smem + p.off_nat;
+    const uint8_t* q6 = smem + p.off_q6;
+    const float* fscale = reinterpret_cast<const float*>(smem + p.off_fscale);
+    const float* xsum = reinterpret_cast<const float*>(smem + p.off_xsum);
+    const int* msum = reinterpret_cast<const int*>(smem + p.off_msum);
+    uint32_t item = 0;
+    bool ok = true;
+    for (uint32_t rb = rb0; rb < rb1 && ok; ++rb) {
+        const int si = seg_of(p, rb);
+        const MatvecSeg& sg = p.a.seg[si];
+        const uint32_t local = rb - p.rb_begin[si];
+        const uint32_t T = sg.m.type;
         const bool dual = sg.epi == EPI_SWIGLU;
-        const int rpg = dual ? NR / 2 : NR;  // output rows per group
-        const uint32_t r0 = local * rpg;
-        RowPtrs rp[NR];
+        uint32_t slots[kNR];
 #pragma unroll
-        for (int i = 0; i < NR; ++i) {
-            const bool second = dual && i >= NR / 2;
-            const QMatDev& m = second ? sg.m2 : sg.m;
-            const uint32_t r = min(r0 + (second ? i - NR / 2 : i), m.rows - 1);
-            rp[i] = row_ptrs(m, r);
+        for (int i = 0; i < kNR; ++i)
+            slots[i] = dual ? (uint32_t)((i < 2 ? 0 : kRB / 2) + 2 * warp + (i & 1)) : (uint32_t)(kNR * warp + i);
+        float acc[kNR];
+#pragma unroll
+        for (int i = 0; i < kNR; ++i) acc[i] = 0.f;
+        for (uint32_t g = 0; g < p.ngroups; ++g, ++item) {
+            const uint32_t s = item % S, n = item / S;
+            if (!wait_or_abort(&full[s], n & 1, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            const uint32_t U = group_units(p.nunits, g), tb = tile_bytes(T, U);
+            const uint8_t* slot = smem + s * p.slot_bytes;
+            if ((uint32_t)lane < U) {
+                const uint32_t u = g * 32 + lane;
+                const uint8_t* tiles[kNR];
+#pragma unroll
+                for (int i = 0; i < kNR; ++i) tiles[i] = slot + slots[i] * tb;
+                // rows past the end were not copied: their slots hold stale bytes whose
+                // (finite) results are discarded below
+                if (T == GGML_Q4_K) {
+                    unit_q4k(tiles, U, lane, u, nat + u * kLimbStride, fscale, xsum, acc);
+                } else if (T == GGML_Q6_K) {
+                    unit_q6k(tiles, U, lane, u, q6 + u * kLimbStride, fscale, msum, acc);
+                } else {
+                    unit_q8_0(tiles, U, lane, u, nat + u * kLimbStride, fscale, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        float acc[NR];
+        if (!ok) break;
 #pragma unroll
-        for (int i = 0; i < NR; ++i) acc[i] = 0.f;
-        switch (sg.m.type) {
-            case GGML_Q4_K: dot_q4k<NR>(rp, nunits, xs_nat, xsum, lane, acc); break;
-            case GGML_Q6_K: dot_q6k<NR>(rp, nunits, xs_q6, lane, acc); break;
-            case GGML_Q8_0: dot_q8_0<NR>(rp, nunits, xs_nat, lane, acc); break;
-            default: break;
-        }
-#pragma unroll
-        for (int i = 0; i < NR; ++i) acc[i] = warp_sum(acc[i]);
+        for (int i = 0; i < kNR; ++i) acc[i] = warp_sum(acc[i]);
         if (lane == 0) {
             if (dual) {
 #pragma unroll
-                for (int i = 0; i < NR / 2; ++i) {
-                    const uint32_t r = r0 + i;
-                    if (r < sg.m.rows) sg.y[r] = __fmul_rn(silu(acc[i]), acc[i + NR / 2]);
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t r = local * (kRB / 2) + 2 * warp + i;
+                    if (r < sg.m.rows) sg.y[r] = __fmul_rn(silu(acc[i]), acc[i + 2]);
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < NR; ++i) {
-                    const uint32_t r = r0 + i;
+                for (int i = 0; i < kNR; ++i) {
+                    const uint32_t r = local * kRB + kNR * warp + i;
                     if (r < sg.m.rows) {
                         if (sg.epi == EPI_ADD) sg.y[r] += acc[i];
                         else sg.y[r] = acc[i];
@@ -309,59 +472,84 @@ __global__ void __launch_bounds__(kThreads) qmatvec_kernel(const __grid_constant
             }
         }
     }
+    if (!ok && lane == 0) atomicExch(p.err, DEV_ERR_WAIT_TIMEOUT);
 }
 
-template <int NR>
-cudaError_t launch_nr(const MatvecArgs& a, cudaStream_t s, bool pdl) {
-    uint32_t need = 0, rg[kMaxSegs] = {0, 0, 0};
-    for (int i = 0; i < a.nseg; ++i) {
-        const uint32_t t = a.seg[i].m.type;
-        need |= (t == GGML_Q6_K) ? 2u : 1u;
-        if (t == GGML_Q4_K) need |= 4u;
-        const int rpg = a.seg[i].epi == EPI_SWIGLU ? NR / 2 : NR;
-        rg[i] = (a.seg[i].m.rows + rpg - 1) / rpg;
+int g_sms = 0;
+
+}  // namespace
+
+cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
+    if (a.nseg < 1 || a.nseg > kMaxSegs || a.cols % 64 != 0 || a.cols == 0 || !a.err) return cudaErrorInvalidValue;
+    Plan p = {};
+    p.a = a;
+    p.err = a.err;
+    p.nunits = a.cols / 64;
+    p.ngroups = (p.nunits + 31) / 32;
+    uint32_t slot = 0;
+    p.rb_begin[0] = 0;
+    for (int i = 0; i < kMaxSegs; ++i) {
+        uint32_t rbs = 0;
+        if (i < a.nseg) {
+            const MatvecSeg& sg = a.seg[i];
+            const uint32_t t = sg.m.type;
+            if (t != GGML_Q4_K && t != GGML_Q6_K && t != GGML_Q8_0) return cudaErrorInvalidValue;
+            if (sg.m.cols != a.cols || sg.m.rows == 0 || !sg.y) return cudaErrorInvalidValue;
+            if (sg.epi == EPI_SWIGLU && (sg.m2.type != t || sg.m2.rows != sg.m.rows || sg.m2.cols != a.cols))
+                return cudaErrorInvalidValue;
+            p.need |= t == GGML_Q6_K ? NEED_Q6 | NEED_MSUM : NEED_NAT;
+            if (t == GGML_Q4_K) p.need |= NEED_XSUM;
+            slot = std::max(slot, kRB * tile_bytes(t, 32));
+            const uint32_t per = sg.epi == EPI_SWIGLU ? kRB / 2 : kRB;
+            rbs = (sg.m.rows + per - 1) / per;
+        }
+        p.rb_begin[i + 1] = p.rb_begin[i] + rbs;
     }
-    const uint32_t b1 = rg[0], b2 = rg[0] + rg[1], total = rg[0] + rg[1] + rg[2];
-    const uint32_t nunits = a.cols / 64;
-    size_t smem = 0;
-    if (need & 1) smem += (size_t)nunits * kUnitStride * 4;
-    if (need & 2) smem += (size_t)nunits * kUnitStride * 4;
-    if (need & 4) smem += (size_t)(a.cols / 32) * 4;
-    cudaError_t e = cudaFuncSetAttribute(qmatvec_kernel<NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    const uint32_t K = a.cols, nb = K / 32;
+    uint32_t off = 0;
+    p.off_nat = off;
+    if (p.need & NEED_NAT) off += p.nunits * kLimbStride;
+    p.off_q6 = off;
+    if (p.need & NEED_Q6) off += p.nunits * kLimbStride;
+    p.off_fscale = off;
+    off += nb * 4;
+    p.off_xsum = off;
+    if (p.need & NEED_XSUM) off += nb * 4;
+    p.off_msum = off;
+    if (p.need & NEED_MSUM) off += p.nunits * 48;
+    off = (off + 127) & ~127u;
+    const uint32_t xbytes = off;
+    if (xbytes + 2 * slot > kSmemBudget) return cudaErrorInvalidValue;
+    p.slot_bytes = slot;
+    p.stages = std::min<uint32_t>(kMaxStages, (kSmemBudget - xbytes) / slot);
+    const uint32_t ring = p.stages * slot;
+    p.off_nat += ring;
+    p.off_q6 += ring;
+    p.off_fscale += ring;
+    p.off_xsum += ring;
+    p.off_msum += ring;
+    p.smem_bytes = ring + xbytes;
+    p.pf_base = a.prefetch.q;
+    p.pf_row_bytes = a.prefetch.row_bytes;
+    p.pf_rows = a.prefetch.q ? a.prefetch.rows : 0;
+    if (!g_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    cudaError_t e = cudaFuncSetAttribute(qmatvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
     if (e != cudaSuccess) return e;
-    const uint32_t grid = (total + kWarps - 1) / kWarps;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(std::min<uint32_t>(p.rb_begin[3], (uint32_t)g_sms));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, qmatvec_kernel<NR>, a, need, total, b1, b2);
-}
-
-}  // namespace
-
-cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
-    if (a.nseg < 1 || a.nseg > kMaxSegs || a.cols % 64 != 0 || a.cols == 0) return cudaErrorInvalidValue;
-    uint32_t rows = 0;
-    bool dual = false;
-    for (int i = 0; i < a.nseg; ++i) {
-        rows += a.seg[i].m.rows;
-        dual |= a.seg[i].epi == EPI_SWIGLU;
-        const uint32_t t = a.seg[i].m.type;
-        if (t != GGML_Q4_K && t != GGML_Q6_K && t != GGML_Q8_0) return cudaErrorInvalidValue;
-        if (a.seg[i].m.cols != a.cols || a.seg[i].m.rows == 0) return cudaErrorInvalidValue;
-    }
-    // Rows per warp: enough warps to cover the SMs several times over, and
-    // as many rows per warp as that allows (each x register is reused NR times).
-    if (dual) return rows >= 148 * 16 * 2 ? launch_nr<4>(a, s, pdl) : launch_nr<2>(a, s, pdl);
-    if (rows >= 148 * 16 * 4) return launch_nr<4>(a, s, pdl);
-    if (rows >= 148 * 16 * 2) return launch_nr<2>(a, s, pdl);
-    return launch_nr<1>(a, s, pdl);
+    return cudaLaunchKernelEx(&cfg, qmatvec_kernel, p);
 }
 
 }  // namespace evl

@@ -1,11 +1,12 @@
-// repack.cpp -- GGUF blocks -> the unit-interleaved device layout of common.cuh.
+// repack.cpp -- GGUF blocks -> the tiled device layout of common.cuh.
 //
 // The reference keeps each QMatrix as the raw GGUF bytes (src/runtime.rs:23-51) and
-// re-reads whole 144/210/34-byte blocks per row. On the GPU the matvec wants every
-// 128-bit load of a warp to be one contiguous 512-byte span, so each row's blocks
-// are split into 16-byte chunks grouped by 64-value unit (see common.cuh), with the
-// block headers moved to side arrays. Every byte of the original survives: the
-// exact dequantiser reads this layout back bit-for-bit (dequant.cuh).
+// re-reads whole 144/210/34-byte blocks per row. On the GPU a row is cut into tiles of
+// up to 32 units (64 values each); inside a tile the 16-byte chunks are stored
+// chunk-major so the 32 lanes of a warp read consecutive 16-byte pieces, and the
+// block scales of the tile follow its payload, so one bulk copy moves a whole tile.
+// Every byte of the original survives: the exact dequantiser reads this layout back
+// bit-for-bit (dequant.cuh).
 #include <algorithm>
 #include <cstring>
 #include <thread>
@@ -15,7 +16,7 @@
 namespace evl {
 
 void repack_sizes(QMatrix& m) {
-    const uint64_t rows = m.rows, cols = m.cols;
+    const uint64_t cols = m.cols;
     switch (m.type) {
         case GGML_Q4_K:
         case GGML_Q6_K:
@@ -31,56 +32,32 @@ void repack_sizes(QMatrix& m) {
             raise(EVL_ERR_UNSUPPORTED, m.name + ": ggml type " + std::to_string(m.type) + " (" + type_name(m.type) +
                                            ") is not supported for device matrices");
     }
-    const uint64_t nunits = cols / 64, ch = chunks_per_unit(m.type);
-    m.payload_bytes = rows * nunits * ch * 16;
-    m.aux_bytes = 0;
-    m.d_bytes = 0;
-    switch (m.type) {
-        case GGML_Q4_K: m.aux_bytes = rows * (cols / 256) * 16; break;
-        case GGML_Q6_K:
-            m.aux_bytes = rows * nunits * 4;
-            m.d_bytes = rows * (cols / 256) * 2;
-            break;
-        case GGML_Q8_0: m.aux_bytes = rows * nunits * 4; break;
-        default: break;
-    }
-    // keep each section 256-byte aligned inside the model buffer
-    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
-    m.payload_bytes = up(m.payload_bytes);
-    m.aux_bytes = up(m.aux_bytes);
-    m.d_bytes = up(m.d_bytes);
+    const uint32_t nunits = (uint32_t)(cols / 64);
     m.dev.type = m.type;
     m.dev.rows = m.rows;
     m.dev.cols = m.cols;
-    m.dev.nunits = (uint32_t)nunits;
+    m.dev.nunits = nunits;
+    m.dev.row_bytes = row_tile_bytes(m.type, nunits);
+    m.total_bytes = ((uint64_t)m.rows * m.dev.row_bytes + 255) / 256 * 256;
 }
 
-void place(QMatrix& m, uint8_t* base) {
-    uint8_t* p = base + m.offset;
-    m.dev.q = p;
-    m.dev.aux = m.aux_bytes ? p + m.payload_bytes : nullptr;
-    m.dev.d = m.d_bytes ? reinterpret_cast<const uint16_t*>(p + m.payload_bytes + m.aux_bytes) : nullptr;
-}
+void place(QMatrix& m, uint8_t* base) { m.dev.q = base + m.offset; }
 
 namespace {
 
 void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* dst, uint32_t r0, uint32_t r1) {
-    const uint32_t nunits = m.cols / 64, ch = chunks_per_unit(m.type), nb = m.cols / 256;
-    const size_t row_payload = (size_t)nunits * ch * 16;
-    uint8_t* payload = dst;
-    uint8_t* aux = dst + m.payload_bytes;
-    uint8_t* dd = aux + m.aux_bytes;
+    const uint32_t T = m.type, N = m.dev.nunits, nb = m.cols / 256, ch = chunks_per_unit(T);
     for (uint32_t r = r0; r < r1; ++r) {
         const uint8_t* src = raw + (size_t)r * stride;
-        uint8_t* prow = payload + (size_t)r * row_payload;
-        switch (m.type) {
+        uint8_t* row = dst + (size_t)r * m.dev.row_bytes;
+        switch (T) {
             case GGML_Q4_K:
                 for (uint32_t sb = 0; sb < nb; ++sb) {
                     const uint8_t* blk = src + (size_t)sb * 144;
-                    std::memcpy(aux + ((size_t)r * nb + sb) * 16, blk, 16);
+                    std::memcpy(row + aux_offset(T, N, sb * 4), blk, 16);
                     for (uint32_t j = 0; j < 4; ++j)
                         for (uint32_t c = 0; c < 2; ++c)
-                            std::memcpy(prow + chunk_offset(nunits, 2, sb * 4 + j, c), blk + 16 + 32 * j + 16 * c, 16);
+                            std::memcpy(row + chunk_offset(T, N, sb * 4 + j, c), blk + 16 + 32 * j + 16 * c, 16);
                 }
                 break;
             case GGML_Q6_K:
@@ -89,36 +66,36 @@ void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* d
                     const uint8_t* ql = blk;
                     const uint8_t* qh = blk + 128;
                     const uint8_t* sc = blk + 192;
-                    std::memcpy(dd + ((size_t)r * nb + sb) * 2, blk + 208, 2);
+                    std::memcpy(row + d_offset(T, N, sb * 4), blk + 208, 2);
                     for (uint32_t h = 0; h < 2; ++h)
                         for (uint32_t b = 0; b < 2; ++b) {
                             const uint32_t u = sb * 4 + h * 2 + b, l0 = 16 * b;
-                            std::memcpy(prow + chunk_offset(nunits, 3, u, 0), ql + 64 * h + l0, 16);
-                            std::memcpy(prow + chunk_offset(nunits, 3, u, 1), ql + 64 * h + 32 + l0, 16);
-                            std::memcpy(prow + chunk_offset(nunits, 3, u, 2), qh + 32 * h + l0, 16);
+                            std::memcpy(row + chunk_offset(T, N, u, 0), ql + 64 * h + l0, 16);
+                            std::memcpy(row + chunk_offset(T, N, u, 1), ql + 64 * h + 32 + l0, 16);
+                            std::memcpy(row + chunk_offset(T, N, u, 2), qh + 32 * h + l0, 16);
                             uint8_t w[4];
                             for (uint32_t k = 0; k < 4; ++k) w[k] = sc[8 * h + b + 2 * k];
-                            std::memcpy(aux + ((size_t)r * nunits + u) * 4, w, 4);
+                            std::memcpy(row + aux_offset(T, N, u), w, 4);
                         }
                 }
                 break;
             case GGML_Q8_0:
-                for (uint32_t u = 0; u < nunits; ++u) {
+                for (uint32_t u = 0; u < N; ++u) {
                     const uint8_t* b0 = src + (size_t)(2 * u) * 34;
                     const uint8_t* b1 = b0 + 34;
-                    std::memcpy(prow + chunk_offset(nunits, 4, u, 0), b0 + 2, 16);
-                    std::memcpy(prow + chunk_offset(nunits, 4, u, 1), b0 + 18, 16);
-                    std::memcpy(prow + chunk_offset(nunits, 4, u, 2), b1 + 2, 16);
-                    std::memcpy(prow + chunk_offset(nunits, 4, u, 3), b1 + 18, 16);
-                    uint8_t w[4] = {b0[0], b0[1], b1[0], b1[1]};
-                    std::memcpy(aux + ((size_t)r * nunits + u) * 4, w, 4);
+                    std::memcpy(row + chunk_offset(T, N, u, 0), b0 + 2, 16);
+                    std::memcpy(row + chunk_offset(T, N, u, 1), b0 + 18, 16);
+                    std::memcpy(row + chunk_offset(T, N, u, 2), b1 + 2, 16);
+                    std::memcpy(row + chunk_offset(T, N, u, 3), b1 + 18, 16);
+                    const uint8_t w[4] = {b0[0], b0[1], b1[0], b1[1]};
+                    std::memcpy(row + aux_offset(T, N, u), w, 4);
                 }
                 break;
             default: {  // F16 / BF16 / F32: plain values, chunked
-                const uint32_t eb = m.type == GGML_F32 ? 4 : 2;
-                for (uint32_t u = 0; u < nunits; ++u)
+                const uint32_t eb = T == GGML_F32 ? 4 : 2;
+                for (uint32_t u = 0; u < N; ++u)
                     for (uint32_t c = 0; c < ch; ++c)
-                        std::memcpy(prow + chunk_offset(nunits, ch, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
+                        std::memcpy(row + chunk_offset(T, N, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
             }
         }
     }

@@ -128,6 +128,8 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         a.cols = (uint32_t)c.dim;
         a.norm_w = L.attn_norm;
         a.eps = c.eps;
+        a.err = b.err.as<int>();
+        a.prefetch = L.o.dev;  // read after the attention kernels
         const uint64_t ys[3] = {qw, kw, kw};
         matvec_each(a, B, c.dim, ys, stream, pdl, "qkv matvec");
         kernels += B;
@@ -182,6 +184,8 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         a.seg[0].epi = tp ? EPI_STORE : EPI_ADD;
         a.x = b.att.as<float>();
         a.cols = (uint32_t)qw;
+        a.err = b.err.as<int>();
+        a.prefetch = L.gate.dev;
         const uint64_t ys[1] = {c.dim};
         matvec_each(a, B, qw, ys, stream, pdl, "o-proj matvec");
         kernels += B;
@@ -206,6 +210,7 @@ void Decoder::enqueue_head(bool pdl) {
     a.cols = (uint32_t)c.dim;
     a.norm_w = m.out_norm;
     a.eps = c.eps;
+    a.err = b.err.as<int>();
     const uint64_t ys[1] = {tp ? (uint64_t)m.lvocab : c.vocab};
     matvec_each(a, B, c.dim, ys, stream, pdl, "lm-head matvec");
     kernels += B;
@@ -239,8 +244,9 @@ void Decoder::enqueue_dense(bool pdl) {
     kernels += 1;
     for (uint32_t li = 0; li < c.layers; ++li) {
         enqueue_layer_attention(li, pdl);
+        const QMatDev* next = li + 1 < c.layers ? &m.layers[li + 1].q.dev : &m.lm_head.dev;
         run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch, b.h.as<float>(),
-                      b.y.as<float>(), stream, pdl);
+                      b.y.as<float>(), b.err.as<int>(), next, stream, pdl);
         kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);
     }
     enqueue_head(pdl);
@@ -259,7 +265,8 @@ void Decoder::run_routed(const evl_ffn_backend& ffn) {
         enqueue_layer_attention(li, pdl);
         const bool routed = ffn.ffn && (!ffn.routed || (li < ffn.routed_len && ffn.routed[li]));
         if (!routed) {
-            run_dense_ffn(m, li, x, m.layers[li].ffn_norm, x, true, 1, b.h.as<float>(), b.y.as<float>(), stream, pdl);
+            run_dense_ffn(m, li, x, m.layers[li].ffn_norm, x, true, 1, b.h.as<float>(), b.y.as<float>(), b.err.as<int>(),
+                          nullptr, stream, pdl);
             continue;
         }
         // Model::ffn_input (runtime.rs:801), then the backend on the host
@@ -273,7 +280,8 @@ void Decoder::run_routed(const evl_ffn_backend& ffn) {
             cuda_check(launch_add(x, b.y.as<float>(), c.dim, stream, pdl), "residual add");
         } else {
             if (rc != EVL_FFN_DENSE && ffn.fallbacks) *ffn.fallbacks += 1;
-            run_dense_ffn(m, li, xn, nullptr, x, true, 1, b.h.as<float>(), b.y.as<float>(), stream, pdl);
+            run_dense_ffn(m, li, xn, nullptr, x, true, 1, b.h.as<float>(), b.y.as<float>(), b.err.as<int>(), nullptr,
+                          stream, pdl);
         }
     }
     enqueue_head(pdl);
