@@ -2,9 +2,11 @@
 //
 // Quantised weights live in HBM in a tiled repack of the GGUF blocks (the
 // reference keeps the raw GGUF bytes, src/runtime.rs:23-51). A unit is 64 values of
-// one row; a row is a sequence of tiles, each covering a group of up to 32 units
-// (the last group of a row may be shorter, U units). A tile is self-contained and
-// 16-byte aligned, so one TMA bulk copy moves it:
+// one row; a row is cut into tiles, each covering a group of up to 32 units (the last
+// group of a row may be shorter, U units). Rows are padded to a multiple of 16 and
+// stored as 16-row slabs: slab b holds, for each group g in turn, the 16 tiles
+// (b*16 + i, g), i = 0..15, back to back -- so one TMA bulk copy moves 16 rows of one
+// column group. A tile is self-contained and 16-byte aligned:
 //
 //   [payload: chunk-major, chunk c of unit u at c*U*16 + u*16 (16 B per chunk)]
 //   [aux: block scales, padded to 16 B] [d: Q6_K super-block scales, padded to 16 B]
@@ -35,9 +37,11 @@ struct QMatDev {
     uint32_t type = 0;
     uint32_t rows = 0, cols = 0;
     uint32_t nunits = 0;         // 64-value units per row
-    uint32_t row_bytes = 0;      // bytes per row (sum of its tiles)
-    const uint8_t* q = nullptr;  // rows * row_bytes
+    uint32_t row_bytes = 0;      // bytes of one row's tiles; a 16-row slab is 16 * row_bytes
+    const uint8_t* q = nullptr;  // ceil(rows / 16) slabs
 };
+
+constexpr uint32_t kSlabRows = 16;
 
 __host__ __device__ inline uint32_t chunks_per_unit(uint32_t type) {
     switch (type) {
@@ -79,23 +83,29 @@ __host__ __device__ inline uint32_t group_units(uint32_t nunits, uint32_t g) {
 __host__ __device__ inline uint32_t row_tile_bytes(uint32_t type, uint32_t nunits) {
     return (nunits / 32u) * tile_bytes(type, 32u) + ((nunits % 32u) ? tile_bytes(type, nunits % 32u) : 0u);
 }
-// Byte offset of tile g inside a row (all full tiles precede it).
-__host__ __device__ inline uint32_t tile_offset(uint32_t type, uint32_t g) { return g * tile_bytes(type, 32u); }
-// Byte offset of chunk c of unit u inside a row.
-__host__ __device__ inline uint32_t chunk_offset(uint32_t type, uint32_t nunits, uint32_t u, uint32_t c) {
-    const uint32_t g = u >> 5;
-    return tile_offset(type, g) + c * group_units(nunits, g) * 16u + (u & 31u) * 16u;
+// Byte offset, inside a 16-row slab, of the 16 tiles of group g.
+__host__ __device__ inline uint32_t slab_group_offset(uint32_t type, uint32_t g) {
+    return g * kSlabRows * tile_bytes(type, 32u);
 }
-// Byte offset of the aux entry of unit u (Q6_K, Q8_0: u32 per unit; Q4_K: 16-byte
-// header of u's super-block) inside a row.
-__host__ __device__ inline uint32_t aux_offset(uint32_t type, uint32_t nunits, uint32_t u) {
-    const uint32_t g = u >> 5, U = group_units(nunits, g), base = tile_offset(type, g) + tile_payload_bytes(type, U);
+// Byte offset of tile (r, g) from the start of the matrix.
+__host__ __device__ inline uint64_t tile_address(uint32_t type, uint32_t nunits, uint32_t row_bytes, uint32_t r,
+                                                 uint32_t g) {
+    return (uint64_t)(r / kSlabRows) * kSlabRows * row_bytes + slab_group_offset(type, g) +
+           (r % kSlabRows) * tile_bytes(type, group_units(nunits, g));
+}
+// Offsets inside one tile of unit u (u's group is u >> 5; lane = u & 31).
+__host__ __device__ inline uint32_t chunk_in_tile(uint32_t nunits, uint32_t u, uint32_t c) {
+    return c * group_units(nunits, u >> 5) * 16u + (u & 31u) * 16u;
+}
+// aux entry of unit u (Q6_K, Q8_0: u32 per unit; Q4_K: 16-byte header of u's super-block)
+__host__ __device__ inline uint32_t aux_in_tile(uint32_t type, uint32_t nunits, uint32_t u) {
+    const uint32_t base = tile_payload_bytes(type, group_units(nunits, u >> 5));
     return type == GGML_Q4_K ? base + ((u & 31u) / 4u) * 16u : base + (u & 31u) * 4u;
 }
-// Byte offset of the Q6_K f16 super-block scale of unit u inside a row.
-__host__ __device__ inline uint32_t d_offset(uint32_t type, uint32_t nunits, uint32_t u) {
-    const uint32_t g = u >> 5, U = group_units(nunits, g);
-    return tile_offset(type, g) + tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + ((u & 31u) / 4u) * 2u;
+// Q6_K f16 super-block scale of unit u
+__host__ __device__ inline uint32_t d_in_tile(uint32_t type, uint32_t nunits, uint32_t u) {
+    const uint32_t U = group_units(nunits, u >> 5);
+    return tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + ((u & 31u) / 4u) * 2u;
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

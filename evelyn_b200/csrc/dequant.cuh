@@ -85,14 +85,15 @@ __device__ __forceinline__ float dq_raw_value(uint32_t type, const uint8_t* b, u
 
 // Value `c` of row `r` from the repacked layout (common.cuh).
 __device__ __forceinline__ float dq_repacked_value(const QMatDev& m, uint32_t r, uint32_t c) {
-    const uint8_t* row = m.q + (uint64_t)r * m.row_bytes;
     const uint32_t T = m.type, N = m.nunits;
+    const uint32_t u_of_c = (T == GGML_Q6_K) ? (c >> 8) * 4 + ((c & 255) >> 7) * 2 + ((c >> 4) & 1) : c >> 6;
+    const uint8_t* tile = m.q + tile_address(T, N, m.row_bytes, r, u_of_c >> 5);
     switch (T) {
         case GGML_Q4_K: {
             uint32_t sb = c >> 8, e = c & 255, j = e >> 6, hi = (e >> 5) & 1, l = e & 31;
             uint32_t u = sb * 4 + j;
-            uint8_t v = row[chunk_offset(T, N, u, l >> 4) + (l & 15)];
-            const uint8_t* h = row + aux_offset(T, N, u);
+            uint8_t v = tile[chunk_in_tile(N, u, l >> 4) + (l & 15)];
+            const uint8_t* h = tile + aux_in_tile(T, N, u);
             float d = f16_exact(ld_u16(h)), dmin = f16_exact(ld_u16(h + 2));
             float s, mm;
             scale_min_bytes(2 * j + hi, h + 4, &s, &mm);
@@ -103,31 +104,31 @@ __device__ __forceinline__ float dq_repacked_value(const QMatDev& m, uint32_t r,
             uint32_t sb = c >> 8, e = c & 255, half = e >> 7, rr = e & 127, k = rr >> 5, l = rr & 31;
             uint32_t u = sb * 4 + half * 2 + (l >> 4);
             uint32_t li = l & 15;
-            uint8_t lo = row[chunk_offset(T, N, u, k & 1) + li];
-            uint8_t qh = row[chunk_offset(T, N, u, 2) + li];
+            uint8_t lo = tile[chunk_in_tile(N, u, k & 1) + li];
+            uint8_t qh = tile[chunk_in_tile(N, u, 2) + li];
             uint32_t nib = (k >> 1) ? (lo >> 4) : (lo & 0xf);
             int q = (int)(nib | (((qh >> (2 * k)) & 3) << 4)) - 32;
-            uint32_t scw = *reinterpret_cast<const uint32_t*>(row + aux_offset(T, N, u));
+            uint32_t scw = *reinterpret_cast<const uint32_t*>(tile + aux_in_tile(T, N, u));
             float sc = (float)(int8_t)((scw >> (8 * k)) & 0xff);
-            float d = f16_exact(ld_u16(row + d_offset(T, N, u)));
+            float d = f16_exact(ld_u16(tile + d_in_tile(T, N, u)));
             return __fmul_rn(__fmul_rn(d, sc), (float)q);
         }
         case GGML_Q8_0: {
             uint32_t u = c >> 6, e = c & 63;
-            int8_t q = (int8_t)row[chunk_offset(T, N, u, e >> 4) + (e & 15)];
-            uint32_t dw = *reinterpret_cast<const uint32_t*>(row + aux_offset(T, N, u));
+            int8_t q = (int8_t)tile[chunk_in_tile(N, u, e >> 4) + (e & 15)];
+            uint32_t dw = *reinterpret_cast<const uint32_t*>(tile + aux_in_tile(T, N, u));
             float d = f16_exact((e < 32) ? (dw & 0xffff) : (dw >> 16));
             return __fmul_rn(d, (float)q);
         }
         case GGML_F16:
         case GGML_BF16: {
             uint32_t u = c >> 6, e = c & 63;
-            uint32_t h = ld_u16(row + chunk_offset(T, N, u, e >> 3) + (e & 7) * 2);
+            uint32_t h = ld_u16(tile + chunk_in_tile(N, u, e >> 3) + (e & 7) * 2);
             return T == GGML_F16 ? f16_exact(h) : __uint_as_float(h << 16);
         }
         case GGML_F32: {
             uint32_t u = c >> 6, e = c & 63;
-            return __uint_as_float(*(const uint32_t*)(row + chunk_offset(T, N, u, e >> 2) + (e & 3) * 4));
+            return __uint_as_float(*(const uint32_t*)(tile + chunk_in_tile(N, u, e >> 2) + (e & 3) * 4));
         }
         default: return 0.f;
     }

@@ -86,15 +86,6 @@ __device__ __forceinline__ int seg_of(const Plan& p, uint32_t rb) {
     return rb >= p.rb_begin[2] ? 2 : rb >= p.rb_begin[1] ? 1 : 0;
 }
 
-// Row slot i of a row-block: which matrix and row it holds.
-__device__ __forceinline__ const QMatDev& slot_matrix(const MatvecSeg& sg, uint32_t local, uint32_t i, uint32_t* row) {
-    if (sg.epi == EPI_SWIGLU) {
-        *row = local * (kRB / 2) + (i & (kRB / 2 - 1));
-        return i < (uint32_t)kRB / 2 ? sg.m : sg.m2;
-    }
-    *row = local * kRB + i;
-    return sg.m;
-}
 
 // ---------------------------------------------------------------- per-unit dot products
 // Each returns, per row slot, the f32 contribution of one 64-value unit.
@@ -369,28 +360,31 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
                 const uint32_t s = item % S, n = item / S;
                 if (n > 0 && !wait_or_abort(&empty[s], (n - 1) & 1, &abort_flag)) break;
                 const uint32_t U = group_units(p.nunits, g), tb = tile_bytes(T, U);
+                const uint32_t slab_bytes = kSlabRows * tb;
                 uint8_t* slot = smem + s * p.slot_bytes;
-                uint32_t valid = 0;
-                for (uint32_t i = 0; i < (uint32_t)kRB; ++i) {
-                    uint32_t row;
-                    const QMatDev& m = slot_matrix(sg, local, i, &row);
-                    valid += row < m.rows;
-                }
-                mbar_arrive_expect_tx(&full[s], valid * tb);
-                for (uint32_t i = 0; i < (uint32_t)kRB; ++i) {
-                    uint32_t row;
-                    const QMatDev& m = slot_matrix(sg, local, i, &row);
-                    if (row < m.rows)
-                        tma_load_1d(slot + i * tb, m.q + (uint64_t)row * m.row_bytes + tile_offset(T, g), tb, &full[s]);
-                }
+                // two 16-row slabs of group g: rows [32*local, +32), or gate and up
+                // rows [16*local, +16) for the SwiGLU pair
+                const bool dual = sg.epi == EPI_SWIGLU;
+                const QMatDev& ma = sg.m;
+                const QMatDev& mb = dual ? sg.m2 : sg.m;
+                const uint32_t sa = dual ? local : 2 * local, sbk = dual ? local : 2 * local + 1;
+                const bool has_b = sbk * kSlabRows < mb.rows;
+                mbar_arrive_expect_tx(&full[s], (has_b ? 2 : 1) * slab_bytes);
+                tma_load_1d(slot, ma.q + (uint64_t)sa * kSlabRows * ma.row_bytes + slab_group_offset(T, g), slab_bytes,
+                            &full[s]);
+                if (has_b)
+                    tma_load_1d(slot + slab_bytes,
+                                mb.q + (uint64_t)sbk * kSlabRows * mb.row_bytes + slab_group_offset(T, g), slab_bytes,
+                                &full[s]);
             }
         }
-        if (p.pf_base && p.pf_rows) {  // warm L2 with the next matrix's first rows for this CTA
-            const uint32_t pr0 = (uint32_t)(((uint64_t)p.pf_rows * blockIdx.x) / gridDim.x);
-            const uint32_t pr1 = (uint32_t)(((uint64_t)p.pf_rows * (blockIdx.x + 1)) / gridDim.x);
-            uint64_t bytes = (uint64_t)(pr1 - pr0) * p.pf_row_bytes;
+        if (p.pf_base && p.pf_rows) {  // warm L2 with the next matrix's first slabs for this CTA
+            const uint32_t slabs = (p.pf_rows + kSlabRows - 1) / kSlabRows;
+            const uint32_t pr0 = (uint32_t)(((uint64_t)slabs * blockIdx.x) / gridDim.x);
+            const uint32_t pr1 = (uint32_t)(((uint64_t)slabs * (blockIdx.x + 1)) / gridDim.x);
+            uint64_t bytes = (uint64_t)(pr1 - pr0) * kSlabRows * p.pf_row_bytes;
             if (bytes > (96u << 10)) bytes = 96u << 10;
-            const uint8_t* base = p.pf_base + (uint64_t)pr0 * p.pf_row_bytes;
+            const uint8_t* base = p.pf_base + (uint64_t)pr0 * kSlabRows * p.pf_row_bytes;
             for (uint64_t o = 0; o < bytes; o += 16384)
                 prefetch_l2_bulk(base + o, (uint32_t)((bytes - o) < 16384 ? (bytes - o) & ~15ull : 16384));
         }

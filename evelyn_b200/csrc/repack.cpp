@@ -38,7 +38,8 @@ void repack_sizes(QMatrix& m) {
     m.dev.cols = m.cols;
     m.dev.nunits = nunits;
     m.dev.row_bytes = row_tile_bytes(m.type, nunits);
-    m.total_bytes = ((uint64_t)m.rows * m.dev.row_bytes + 255) / 256 * 256;
+    const uint64_t slabs = (m.rows + kSlabRows - 1) / kSlabRows;
+    m.total_bytes = (slabs * kSlabRows * m.dev.row_bytes + 255) / 256 * 256;
 }
 
 void place(QMatrix& m, uint8_t* base) { m.dev.q = base + m.offset; }
@@ -46,18 +47,21 @@ void place(QMatrix& m, uint8_t* base) { m.dev.q = base + m.offset; }
 namespace {
 
 void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* dst, uint32_t r0, uint32_t r1) {
-    const uint32_t T = m.type, N = m.dev.nunits, nb = m.cols / 256, ch = chunks_per_unit(T);
+    const uint32_t T = m.type, N = m.dev.nunits, nb = m.cols / 256, ch = chunks_per_unit(T), RB = m.dev.row_bytes;
     for (uint32_t r = r0; r < r1; ++r) {
         const uint8_t* src = raw + (size_t)r * stride;
-        uint8_t* row = dst + (size_t)r * m.dev.row_bytes;
+        // tile of unit u in this row
+        auto tile = [&](uint32_t u) { return dst + tile_address(T, N, RB, r, u >> 5); };
         switch (T) {
             case GGML_Q4_K:
                 for (uint32_t sb = 0; sb < nb; ++sb) {
                     const uint8_t* blk = src + (size_t)sb * 144;
-                    std::memcpy(row + aux_offset(T, N, sb * 4), blk, 16);
-                    for (uint32_t j = 0; j < 4; ++j)
+                    std::memcpy(tile(sb * 4) + aux_in_tile(T, N, sb * 4), blk, 16);
+                    for (uint32_t j = 0; j < 4; ++j) {
+                        const uint32_t u = sb * 4 + j;
                         for (uint32_t c = 0; c < 2; ++c)
-                            std::memcpy(row + chunk_offset(T, N, sb * 4 + j, c), blk + 16 + 32 * j + 16 * c, 16);
+                            std::memcpy(tile(u) + chunk_in_tile(N, u, c), blk + 16 + 32 * j + 16 * c, 16);
+                    }
                 }
                 break;
             case GGML_Q6_K:
@@ -66,16 +70,17 @@ void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* d
                     const uint8_t* ql = blk;
                     const uint8_t* qh = blk + 128;
                     const uint8_t* sc = blk + 192;
-                    std::memcpy(row + d_offset(T, N, sb * 4), blk + 208, 2);
+                    std::memcpy(tile(sb * 4) + d_in_tile(T, N, sb * 4), blk + 208, 2);
                     for (uint32_t h = 0; h < 2; ++h)
                         for (uint32_t b = 0; b < 2; ++b) {
                             const uint32_t u = sb * 4 + h * 2 + b, l0 = 16 * b;
-                            std::memcpy(row + chunk_offset(T, N, u, 0), ql + 64 * h + l0, 16);
-                            std::memcpy(row + chunk_offset(T, N, u, 1), ql + 64 * h + 32 + l0, 16);
-                            std::memcpy(row + chunk_offset(T, N, u, 2), qh + 32 * h + l0, 16);
+                            uint8_t* t = tile(u);
+                            std::memcpy(t + chunk_in_tile(N, u, 0), ql + 64 * h + l0, 16);
+                            std::memcpy(t + chunk_in_tile(N, u, 1), ql + 64 * h + 32 + l0, 16);
+                            std::memcpy(t + chunk_in_tile(N, u, 2), qh + 32 * h + l0, 16);
                             uint8_t w[4];
                             for (uint32_t k = 0; k < 4; ++k) w[k] = sc[8 * h + b + 2 * k];
-                            std::memcpy(row + aux_offset(T, N, u), w, 4);
+                            std::memcpy(t + aux_in_tile(T, N, u), w, 4);
                         }
                 }
                 break;
@@ -83,19 +88,20 @@ void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* d
                 for (uint32_t u = 0; u < N; ++u) {
                     const uint8_t* b0 = src + (size_t)(2 * u) * 34;
                     const uint8_t* b1 = b0 + 34;
-                    std::memcpy(row + chunk_offset(T, N, u, 0), b0 + 2, 16);
-                    std::memcpy(row + chunk_offset(T, N, u, 1), b0 + 18, 16);
-                    std::memcpy(row + chunk_offset(T, N, u, 2), b1 + 2, 16);
-                    std::memcpy(row + chunk_offset(T, N, u, 3), b1 + 18, 16);
+                    uint8_t* t = tile(u);
+                    std::memcpy(t + chunk_in_tile(N, u, 0), b0 + 2, 16);
+                    std::memcpy(t + chunk_in_tile(N, u, 1), b0 + 18, 16);
+                    std::memcpy(t + chunk_in_tile(N, u, 2), b1 + 2, 16);
+                    std::memcpy(t + chunk_in_tile(N, u, 3), b1 + 18, 16);
                     const uint8_t w[4] = {b0[0], b0[1], b1[0], b1[1]};
-                    std::memcpy(row + aux_offset(T, N, u), w, 4);
+                    std::memcpy(t + aux_in_tile(T, N, u), w, 4);
                 }
                 break;
             default: {  // F16 / BF16 / F32: plain values, chunked
                 const uint32_t eb = T == GGML_F32 ? 4 : 2;
                 for (uint32_t u = 0; u < N; ++u)
                     for (uint32_t c = 0; c < ch; ++c)
-                        std::memcpy(row + chunk_offset(T, N, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
+                        std::memcpy(tile(u) + chunk_in_tile(N, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
             }
         }
     }
