@@ -135,6 +135,8 @@ SIGNATURES = {
     "evl_attention_workspace_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
     "evl_attention_decode_ws": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                           C.c_uint32, _P, _P, C.c_size_t, _P]),
+    "evl_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                               C.c_uint32, _P, _P]),
     "evl_remote_ffn_new": (C.c_int, [_P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_char_p), C.c_uint32,
                                      C.POINTER(_P)]),
     "evl_remote_ffn_free": (None, [_P]),

@@ -183,6 +183,20 @@ evl_status evl_attention_decode_ws(const float* d_q, const void* d_k_pages, cons
                                    const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
                                    uint32_t head_dim, uint32_t page_size, float* d_out, void* d_workspace,
                                    size_t workspace_bytes, void* stream);
+/* evl_attention_decode without any device allocation (no counterpart in the reference,
+ * whose attention runs on the host). For callers that may not allocate device memory
+ * during a decode call: a process whose HBM belongs to its own pool, or one that must
+ * not let a cudaFree synchronise the device mid-step. The split scratch is a fixed
+ * 1.5 MiB array per device inside this library; a shape needing more is rejected
+ * with EVL_ERR_INVALID_INPUT (on a 148-SM B200 every accepted shape fits). The call
+ * clears the scratch's error flag itself and synchronises `stream` before returning.
+ * The first call on a device resolves the array's address (set-up): make it before
+ * any stream capture. Calls on one device that overlap in time race on the shared
+ * scratch; the caller serialises them. Same arguments and results as
+ * evl_attention_decode. */
+evl_status evl_attention_decode_noalloc(const float* d_q, const void* d_k_pages, const void* d_v_pages,
+                                        const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
+                                        uint32_t head_dim, uint32_t page_size, float* d_out, void* stream);
 
 /* ------------------------------------------------------------------ AARNN routing (src/remote.rs) */
 typedef struct evl_endpoint_stats { /* EndpointStats, remote.rs:13-24 */
