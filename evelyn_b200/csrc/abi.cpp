@@ -383,6 +383,7 @@ uint64_t evl_qmatrix_bytes(const evl_qmatrix* q) { return q ? q->m.bytes() : 0; 
 evl_status evl_qmatrix_matvec(const evl_qmatrix* q, const float* d_x, float* d_y, void* stream) {
     return guarded([&] {
         require(q && d_x && d_y, "null argument");
+        require((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, "x must be 16-byte aligned");
         MatvecArgs a;
         a.nseg = 1;
         a.seg[0].m = q->m.dev;

@@ -10,10 +10,10 @@
 //     from the previous kernel, so it starts before griddepcontrol.wait and keeps the
 //     ring full across the kernel boundary; after its last copy it prefetches the
 //     next matrix's first tiles into L2;
-//   * eight consumer warps stage the input vector once per CTA as 24-bit block
-//     fixed point -- per 32-value block x = 2^-s * m, |m| < 2^22, m split into three
+//   * sixteen consumer warps stage the input vector once per CTA as 24-bit block
+//     fixed point -- per 32-value block x = 2^-s * m, |m| <= 2^22, m split into three
 //     signed 8-bit limbs -- then run the dot products on the raw quant bytes with
-//     integer dp4a (4 products per instruction), four rows per warp per stage, one
+//     integer dp4a (4 products per instruction), two rows per warp per stage, one
 //     64-value unit per lane. Block scales (d*s_j, dmin*m_j, Q6_K int8 scales, the
 //     2^-s of x) are applied in f32 once per 32 (Q4_K, Q8_0) or 16 (Q6_K) values.
 // The integer products are exact, so the only rounding against the reference's
@@ -32,14 +32,15 @@ namespace evl {
 
 namespace {
 
-constexpr int kCW = 8;                // consumer warps
+constexpr int kCW = 16;               // consumer warps
 constexpr int kThreads = 32 * (kCW + 1);
-constexpr int kNR = 4;                 // row slots per consumer warp
+constexpr int kNR = 2;                 // row slots per consumer warp
 constexpr int kRB = kCW * kNR;         // 32 row slots per stage
 constexpr int kLimbStride = 208;       // bytes of limbs per unit: 3 x 64 + 16 pad (bank spread)
 constexpr int kMaxStages = 8;
 constexpr uint32_t kSmemBudget = 225 * 1024;
-constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the 256 consumer threads
+constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the consumer threads
+static_assert(kRB == 2 * kSlabRows && kNR % 2 == 0, "a stage is two 16-row slabs; SwiGLU pairs split kNR");
 
 // need bits
 constexpr uint32_t NEED_NAT = 1, NEED_Q6 = 2, NEED_XSUM = 4, NEED_MSUM = 8;
@@ -166,6 +167,15 @@ __device__ __forceinline__ void unit_q6k(const uint8_t* const (&tiles)[kNR], uin
     for (int i = 0; i < kNR; ++i)
 #pragma unroll
         for (int k = 0; k < 4; ++k) S[i][k][0] = S[i][k][1] = S[i][k][2] = 0;
+    // the three 16-byte chunks of each row, as whole vector loads (a lane's chunk is
+    // 16 contiguous bytes; word-sized loads at a 16-byte lane stride would conflict)
+    uint4 Lc[kNR], Hc[kNR], Qc[kNR];
+#pragma unroll
+    for (int i = 0; i < kNR; ++i) {
+        Lc[i] = *reinterpret_cast<const uint4*>(tiles[i] + lane * 16);
+        Hc[i] = *reinterpret_cast<const uint4*>(tiles[i] + U * 16 + lane * 16);
+        Qc[i] = *reinterpret_cast<const uint4*>(tiles[i] + 2 * U * 16 + lane * 16);
+    }
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         int4 lv[3];
@@ -173,10 +183,9 @@ __device__ __forceinline__ void unit_q6k(const uint8_t* const (&tiles)[kNR], uin
         for (int c = 0; c < 3; ++c) lv[c] = *reinterpret_cast<const int4*>(limbs + c * 64 + 16 * t);
 #pragma unroll
         for (int i = 0; i < kNR; ++i) {
-            const uint8_t* base = tiles[i] + lane * 16 + 4 * t;
-            const uint32_t L = *reinterpret_cast<const uint32_t*>(base);
-            const uint32_t H = *reinterpret_cast<const uint32_t*>(base + U * 16);
-            const uint32_t Q = *reinterpret_cast<const uint32_t*>(base + 2 * U * 16);
+            const uint32_t L = t == 0 ? Lc[i].x : t == 1 ? Lc[i].y : t == 2 ? Lc[i].z : Lc[i].w;
+            const uint32_t H = t == 0 ? Hc[i].x : t == 1 ? Hc[i].y : t == 2 ? Hc[i].z : Hc[i].w;
+            const uint32_t Q = t == 0 ? Qc[i].x : t == 1 ? Qc[i].y : t == 2 ? Qc[i].z : Qc[i].w;
             const int q0 = (int)((L & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u));
             const int q1 = (int)((H & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u));
             const int q2 = (int)(((L >> 4) & 0x0F0F0F0Fu) | (Q & 0x30303030u));
@@ -247,16 +256,37 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t* const (&tiles)[kNR], ui
 }
 
 // ---------------------------------------------------------------- input staging
-// x (optionally RMS-normalised) -> per-32-block scale 2^-s and 3 int8 limbs per value.
+// x (optionally RMS-normalised, src/runtime.rs:193-196) -> per 32-value block j a scale
+// 2^-s and |m| <= 2^22 with x = 2^-s * m, m = l0 + 2^8 l1 + 2^16 l2 in three int8 limbs,
+// written in the layouts the unit functions read. Each consumer thread stages one
+// 16-value half of a block from registers: the two halves of a block sit in adjacent
+// lanes and meet with one shuffle for the block maximum and sum.
+
+// limb bytes of four staged values: t = m + 0x8080 makes bytes 0 and 1 of t the
+// limbs l0, l1 biased by 128, and t >> 16 = l2
+__device__ __forceinline__ void pack_limbs(int m0, int m1, int m2, int m3, uint32_t& w0, uint32_t& w1, uint32_t& w2) {
+    const uint32_t t0 = (uint32_t)(m0 + 0x8080), t1 = (uint32_t)(m1 + 0x8080), t2 = (uint32_t)(m2 + 0x8080),
+                   t3 = (uint32_t)(m3 + 0x8080);
+    const uint32_t a01 = __byte_perm(t0, t1, 0x5140), a23 = __byte_perm(t2, t3, 0x5140);  // b0 b0' b1 b1'
+    w0 = __byte_perm(a01, a23, 0x5410) ^ 0x80808080u;  // byte 0 of each
+    w1 = __byte_perm(a01, a23, 0x7632) ^ 0x80808080u;  // byte 1 of each
+    w2 = __byte_perm(__byte_perm(t0, t1, 0x0062), __byte_perm(t2, t3, 0x0062), 0x5410);  // byte 2 of each
+}
+
 __device__ void stage_input(const Plan& p, uint8_t* smem, int warp, int lane, float* red) {
     const MatvecArgs& a = p.a;
-    const uint32_t K = a.cols;
+    const uint32_t K = a.cols, nhalf = K / 16;
+    const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
     float inv = 1.f;
     if (a.norm_w) {
         float ss = 0.f;
-        for (uint32_t i = warp * 32 + lane; i < K; i += kCW * 32) {
-            const float v = a.x[i];
-            ss += v * v;
+        for (uint32_t hb = c; hb < nhalf; hb += kCW * 32) {
+            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = xp[q];
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
@@ -271,60 +301,99 @@ __device__ void stage_input(const Plan& p, uint8_t* smem, int warp, int lane, fl
     float* fscale = reinterpret_cast<float*>(smem + p.off_fscale);
     float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
     int* msum = reinterpret_cast<int*>(smem + p.off_msum);
-    for (uint32_t j = warp; j < K / 32; j += kCW) {
-        const uint32_t i = 32 * j + lane;
-        float v = a.x[i];
-        if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
-        if (a.x_out && blockIdx.x == 0) a.x_out[i] = v;
-        const float amax = warp_max(fabsf(v));
-        int s = 0;
-        if (amax > 0.f) {
-            int e;
-            frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
-            s = min(max(22 - e, -100), 120);
-        }
-        const int m = __float2int_rn(ldexpf(v, s));
-        const int l0 = (m << 24) >> 24;
-        const int r1 = (m - l0) >> 8;
-        const int l1 = (r1 << 24) >> 24;
-        const int l2 = (r1 - l1) >> 8;
-        if (lane == 0) fscale[j] = ldexpf(1.0f, -s);
-        if (p.need & NEED_XSUM) {
-            const float sum = warp_sum(v);
-            if (lane == 0) xsum[j] = sum;
-        }
-        if (p.need & NEED_NAT) {
-            uint8_t* b = nat + (j >> 1) * kLimbStride + (j & 1) * 32 + lane;
-            b[0] = (uint8_t)l0;
-            b[64] = (uint8_t)l1;
-            b[128] = (uint8_t)l2;
-        }
-        if (p.need & NEED_Q6) {
-            const uint32_t r8 = i & 255, h = r8 >> 7, k = (r8 >> 5) & 3, bb = lane >> 4, l = lane & 15;
-            const uint32_t u = (i >> 8) * 4 + h * 2 + bb;
-            uint8_t* b = q6 + u * kLimbStride + (l >> 2) * 16 + k * 4 + (l & 3);
-            b[0] = (uint8_t)l0;
-            b[64] = (uint8_t)l1;
-            b[128] = (uint8_t)l2;
-            if (p.need & NEED_MSUM) {  // per 16-value run: sums of each limb
-                int s0 = l0, s1 = l1, s2 = l2;
+    // nhalf is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
+    for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nhalf; hb0 += kCW * 32) {
+        const uint32_t hb = hb0 + lane;
+        const bool on = hb < nhalf;  // uniform per lane pair
+        float v[16];
+        if (on) {
+            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
 #pragma unroll
-                for (int o = 8; o > 0; o >>= 1) {
-                    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-                    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-                    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+            for (int q = 0; q < 4; ++q) {
+                const float4 t = xp[q];
+                v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+            }
+            if (a.norm_w) {
+                const float4* gp = reinterpret_cast<const float4*>(a.norm_w + 16 * hb);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 g = gp[q];
+                    v[4 * q] = __fmul_rn(__fmul_rn(v[4 * q], inv), g.x);
+                    v[4 * q + 1] = __fmul_rn(__fmul_rn(v[4 * q + 1], inv), g.y);
+                    v[4 * q + 2] = __fmul_rn(__fmul_rn(v[4 * q + 2], inv), g.z);
+                    v[4 * q + 3] = __fmul_rn(__fmul_rn(v[4 * q + 3], inv), g.w);
                 }
-                if (l == 0) {
-                    int* ms = msum + u * 12 + 3 * k;
-                    ms[0] = s0;
-                    ms[1] = s1;
-                    ms[2] = s2;
+            }
+            if (a.x_out && blockIdx.x == 0) {
+                float4* op = reinterpret_cast<float4*>(a.x_out + 16 * hb);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) op[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        }
+        // |x| bit patterns order like the values; the biased exponent E of the block
+        // maximum puts it in [2^(E-127), 2^(E-126)), i.e. frexp's e = E - 126, and
+        // s = 22 - e keeps |m| <= 2^22
+        uint32_t abits = 0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) abits = max(abits, __float_as_uint(v[e]) & 0x7fffffffu);
+        abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
+        const int s = abits ? min(max(148 - (int)(abits >> 23), -100), 120) : 0;
+        // 2^s and 2^-s are normal floats for s in [-100, 120]: the scaling is exact
+        const float up = __uint_as_float((uint32_t)(s + 127) << 23);
+        int m[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) m[e] = __float2int_rn(__fmul_rn(v[e], up));
+        uint32_t L0[4], L1[4], L2[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
+        const uint32_t j = hb >> 1, h = hb & 1;
+        const float fs = __uint_as_float((uint32_t)(127 - s) << 23);
+        if (p.need & NEED_XSUM) {  // sum of the staged (quantised) block: exact in int32
+            int sm = 0;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sm += m[e];
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            if (on && h == 0) xsum[j] = __fmul_rn((float)sm, fs);
+        }
+        if (!on) continue;
+        if (h == 0) fscale[j] = fs;
+        if (p.need & NEED_NAT) {  // unit j/2: [limb][64 values], block j&1 at +32, half at +16
+            uint8_t* b = nat + (j >> 1) * kLimbStride + (j & 1) * 32 + h * 16;
+            *reinterpret_cast<uint4*>(b) = make_uint4(L0[0], L0[1], L0[2], L0[3]);
+            *reinterpret_cast<uint4*>(b + 64) = make_uint4(L1[0], L1[1], L1[2], L1[3]);
+            *reinterpret_cast<uint4*>(b + 128) = make_uint4(L2[0], L2[1], L2[2], L2[3]);
+        }
+        if (p.need & NEED_Q6) {  // the half is run k of unit u: value l at (l/4)*16 + k*4 + l%4
+            const uint32_t i = 16 * hb, r8 = i & 255, hh = r8 >> 7, k = (r8 >> 5) & 3;
+            const uint32_t u = (i >> 8) * 4 + hh * 2 + h;
+            uint8_t* b = q6 + u * kLimbStride + k * 4;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                *reinterpret_cast<uint32_t*>(b + q * 16) = L0[q];
+                *reinterpret_cast<uint32_t*>(b + 64 + q * 16) = L1[q];
+                *reinterpret_cast<uint32_t*>(b + 128 + q * 16) = L2[q];
+            }
+            if (p.need & NEED_MSUM) {  // per run: sums of each limb (the -32 bias)
+                int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    s0 = dp4a((int)L0[q], 0x01010101, s0);
+                    s1 = dp4a((int)L1[q], 0x01010101, s1);
+                    s2 = dp4a((int)L2[q], 0x01010101, s2);
                 }
+                int* ms = msum + u * 12 + 3 * k;
+                ms[0] = s0;
+                ms[1] = s1;
+                ms[2] = s2;
             }
         }
     }
     named_sync(kConsumerBarrier, kCW * 32);
 }
+
 
 __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_constant__ Plan p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -414,7 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
         uint32_t slots[kNR];
 #pragma unroll
         for (int i = 0; i < kNR; ++i)
-            slots[i] = dual ? (uint32_t)((i < 2 ? 0 : kRB / 2) + 2 * warp + (i & 1)) : (uint32_t)(kNR * warp + i);
+            slots[i] = dual ? (uint32_t)((i < kNR / 2 ? 0 : kRB / 2) + (kNR / 2) * warp + i % (kNR / 2))
+                            : (uint32_t)(kNR * warp + i);
         float acc[kNR];
 #pragma unroll
         for (int i = 0; i < kNR; ++i) acc[i] = 0.f;
@@ -450,9 +520,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
         if (lane == 0) {
             if (dual) {
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t r = local * (kRB / 2) + 2 * warp + i;
-                    if (r < sg.m.rows) sg.y[r] = __fmul_rn(silu(acc[i]), acc[i + 2]);
+                for (int i = 0; i < kNR / 2; ++i) {
+                    const uint32_t r = local * (kRB / 2) + (kNR / 2) * warp + i;
+                    if (r < sg.m.rows) sg.y[r] = __fmul_rn(silu(acc[i]), acc[i + kNR / 2]);
                 }
             } else {
 #pragma unroll
@@ -475,6 +545,9 @@ int g_sms = 0;
 
 cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
     if (a.nseg < 1 || a.nseg > kMaxSegs || a.cols % 64 != 0 || a.cols == 0 || !a.err) return cudaErrorInvalidValue;
+    // the staging reads x, norm_w and writes x_out as float4
+    auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+    if (!a.x || misaligned(a.x) || misaligned(a.norm_w) || misaligned(a.x_out)) return cudaErrorMisalignedAddress;
     Plan p = {};
     p.a = a;
     p.err = a.err;

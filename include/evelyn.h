@@ -158,7 +158,8 @@ evl_status evl_qmatrix_create(uint32_t ggml_type, uint32_t rows, uint32_t cols, 
                               evl_qmatrix** out);
 void evl_qmatrix_free(evl_qmatrix* m);
 uint64_t evl_qmatrix_bytes(const evl_qmatrix* m);
-/* y = W x (QMatrix::matvec, runtime.rs:72-88). device pointers; stream may be NULL */
+/* y = W x (QMatrix::matvec, runtime.rs:72-88). device pointers, x 16-byte aligned;
+ * stream may be NULL */
 evl_status evl_qmatrix_matvec(const evl_qmatrix* m, const float* d_x, float* d_y, void* stream);
 /* exact dequantisation of all rows to d_out [rows][cols]. device pointers */
 evl_status evl_qmatrix_dequantize(const evl_qmatrix* m, float* d_out, void* stream);
