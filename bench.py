@@ -156,6 +156,20 @@ def cpu_baseline(img, seconds: float = 20.0, max_steps: int = 8):
                       f"(synthetic KV prefix), CPU oracle restating src/runtime.rs, {threads} threads"}
 
 
+def profiled_traffic(name):
+    """DRAM bytes (read + write) per launch from the committed ncu summary
+    profiles/<name>.md (its `traffic_bytes_per_launch:` line), or None."""
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", name + ".md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def kernel_roofline(evl_rt, stream, hbm_peak, peak_kind, reps=8):
     """Time the dominant kernel (Q4_K dequant-matvec, ffn_gate shape 12288x4096) with CUDA
     events on its stream, cycling 8 distinct matrices (226 MB > L2)."""
@@ -180,21 +194,27 @@ def kernel_roofline(evl_rt, stream, hbm_peak, peak_kind, reps=8):
     for h in mats:  # warm up
         evl_rt.check(lib.evl_qmatrix_matvec(h, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), C.c_void_p(stream)))
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ext)
+    # one event pair around every launch, so host-side launch gaps between kernels are
+    # not counted as kernel time
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps * len(mats))]
+    i = 0
     for _ in range(reps):
         for h in mats:
+            evs[i][0].record(ext)
             evl_rt.check(lib.evl_qmatrix_matvec(h, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()),
                                                 C.c_void_p(stream)))
-    e1.record(ext)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / (reps * len(mats))
+            evs[i][1].record(ext)
+            i += 1
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
     alg = rows * cols // 256 * 144 + cols * 4 + rows * 4
     for h in mats:
         lib.evl_qmatrix_free(h)
     gbs = alg / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(gbs / hbm_peak, 4), "traffic": None, "peak_source": peak_kind,
+            "frac": round(gbs / hbm_peak, 4), "traffic": profiled_traffic("qmatvec_q4k_12288x4096"),
+            "peak_source": peak_kind,
             "kernel": "qmatvec_kernel (Q4_K, 12288x4096, ffn_gate shape)", "launch_us": round(ms * 1e3, 2),
             "bytes_per_launch": alg}
 

@@ -24,6 +24,7 @@
 // and SwiGLU silu(g)*u over paired gate/up rows (src/runtime.rs:409-418,
 // src/activation.rs:50).
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -539,7 +540,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
     if (!ok && lane == 0) atomicExch(p.err, DEV_ERR_WAIT_TIMEOUT);
 }
 
-int g_sms = 0;
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sms[kMaxDevices];  // SM count per device, 0 until set up (zero-initialised static)
 
 }  // namespace
 
@@ -599,15 +601,21 @@ cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
     p.pf_base = a.prefetch.q;
     p.pf_row_bytes = a.prefetch.row_bytes;
     p.pf_rows = a.prefetch.q ? a.prefetch.rows : 0;
-    if (!g_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
-    cudaError_t e = cudaFuncSetAttribute(qmatvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
+    // per-device set-up once: SM count and the kernel's shared-memory opt-in
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!g_sms[dev]) {
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(qmatvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
+        if (e != cudaSuccess) return e;
+        g_sms[dev] = sms;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min<uint32_t>(p.rb_begin[3], (uint32_t)g_sms));
+    cfg.gridDim = dim3(std::min<uint32_t>(p.rb_begin[3], (uint32_t)g_sms[dev]));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
