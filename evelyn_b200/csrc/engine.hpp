@@ -213,9 +213,16 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     bool graph_pdl = true;
     std::vector<uint64_t> host_pos;
     uint32_t kernels = 0, kernels_per_step = 0;
+    StepKernel* step_k = nullptr;  // persistent layer-stack kernel (single sequence, one GPU)
+    bool step_tried = false;
+    std::string step_note;        // why the step kernel is not used, if it is not
 
     ~Decoder();
     void init(Model* m, uint32_t batch, uint32_t max_ctx);
+    MatvecArgs qkv_args(uint32_t layer) const;
+    RopeArgs rope_args(uint32_t layer) const;
+    AttnArgs attn_args(uint32_t layer, uint32_t nsplit) const;
+    void build_step_kernel();
     // Enqueue one dense step (every kernel) on `stream`.
     void enqueue_dense(bool pdl);
     void enqueue_layer_attention(uint32_t layer, bool pdl);

@@ -96,6 +96,25 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 
+// ---------------------------------------------------------------- step_kernel.cu
+// One decoder layer of a single-sequence step, as the separate launches would run it:
+// fused QKV matvec (attn norm), QK-norm/RoPE/append, attention (its nsplit and part
+// sized for this kernel), o matvec + residual, SwiGLU gate/up (ffn norm), down + residual.
+struct StepLayer {
+    MatvecArgs qkv;
+    RopeArgs rope;
+    AttnArgs attn;
+    MatvecArgs o, gateup, down;
+};
+struct StepKernel;
+// Builds the persistent layer-stack kernel (one cooperative CTA per SM) for these
+// layers; cudaErrorNotSupported / cudaErrorInvalidValue when it does not apply.
+cudaError_t step_kernel_create(const StepLayer* layers, uint32_t nlayers, int* err, StepKernel** out);
+cudaError_t step_kernel_launch(const StepKernel* k, cudaStream_t s);
+// Clears the grid-barrier and abort state (after a step that reported an error).
+cudaError_t step_kernel_reset(const StepKernel* k, cudaStream_t s);
+void step_kernel_destroy(StepKernel* k);
+
 // ---------------------------------------------------------------- misc.cu
 cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t batch, float* x, int32_t* err,
                          cudaStream_t s, bool pdl);

@@ -13,7 +13,10 @@
 // the host only at those layers.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <string>
+#include <vector>
 
 #include "engine.hpp"
 
@@ -38,6 +41,7 @@ Decoder::~Decoder() {
     if (model) {
         DeviceGuard g(model->device);
         if (graph) cudaGraphExecDestroy(graph);
+        if (step_k) step_kernel_destroy(step_k);
         if (stream) cudaStreamDestroy(stream);
     }
 }
@@ -108,32 +112,31 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     host_pos.assign(batch, 0);
 }
 
-void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
-    Model& m = *model;
+MatvecArgs Decoder::qkv_args(uint32_t li) const {
+    const Model& m = *model;
     const Config& c = m.cfg;
     const LayerWeights& L = m.layers[li];
-    const uint32_t B = b.batch;
-    const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd, kw = (uint64_t)m.lkv_heads * hd;
-    float* x = b.x.as<float>();
-    {  // attn RMSNorm + Q/K/V in one launch
-        MatvecArgs a;
-        a.nseg = 3;
-        a.seg[0].m = L.q.dev;
-        a.seg[0].y = b.q.as<float>();
-        a.seg[1].m = L.k.dev;
-        a.seg[1].y = b.k.as<float>();
-        a.seg[2].m = L.v.dev;
-        a.seg[2].y = b.v.as<float>();
-        a.x = x;
-        a.cols = (uint32_t)c.dim;
-        a.norm_w = L.attn_norm;
-        a.eps = c.eps;
-        a.err = b.err.as<int>();
-        a.prefetch = L.o.dev;  // read after the attention kernels
-        const uint64_t ys[3] = {qw, kw, kw};
-        matvec_each(a, B, c.dim, ys, stream, pdl, "qkv matvec");
-        kernels += B;
-    }
+    MatvecArgs a;  // attn RMSNorm + Q/K/V in one launch
+    a.nseg = 3;
+    a.seg[0].m = L.q.dev;
+    a.seg[0].y = b.q.as<float>();
+    a.seg[1].m = L.k.dev;
+    a.seg[1].y = b.k.as<float>();
+    a.seg[2].m = L.v.dev;
+    a.seg[2].y = b.v.as<float>();
+    a.x = b.x.as<float>();
+    a.cols = (uint32_t)c.dim;
+    a.norm_w = L.attn_norm;
+    a.eps = c.eps;
+    a.err = b.err.as<int>();
+    a.prefetch = L.o.dev;  // read after the attention kernels
+    return a;
+}
+
+RopeArgs Decoder::rope_args(uint32_t li) const {
+    const Model& m = *model;
+    const Config& c = m.cfg;
+    const LayerWeights& L = m.layers[li];
     RopeArgs r;
     r.q = b.q.as<float>();
     r.k = b.k.as<float>();
@@ -145,18 +148,22 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
     r.page_table = b.page_table.as<int32_t>();
     r.max_pages = b.pages_per_seq;
     r.pos = b.pos.as<int32_t>();
-    r.batch = B;
+    r.batch = b.batch;
     r.heads = m.lheads;
     r.kv_heads = m.lkv_heads;
-    r.head_dim = (uint32_t)hd;
+    r.head_dim = (uint32_t)c.head_dim;
     r.rope_dim = (uint32_t)c.rope_dim;
     r.rope_base = c.rope_base;
     r.eps = c.eps;
     r.interleaved = c.rope_interleaved;
     r.rope_inv_freq = m.rope_inv_freq;
     r.err = b.err.as<int>();
-    cuda_check(launch_qk_norm_rope_append(r, stream, pdl), "qk-norm/rope/append");
-    kernels += 1;
+    return r;
+}
+
+AttnArgs Decoder::attn_args(uint32_t li, uint32_t nsplit) const {
+    const Model& m = *model;
+    const uint64_t hd = m.cfg.head_dim;
     AttnArgs at;
     at.q = b.q.as<float>();
     at.out = b.att.as<float>();
@@ -165,15 +172,32 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
     at.page_table = b.page_table.as<int32_t>();
     at.max_pages = b.pages_per_seq;
     at.pos = b.pos.as<int32_t>();
-    at.batch = B;
+    at.batch = b.batch;
     at.heads = m.lheads;
     at.kv_heads = m.lkv_heads;
     at.head_dim = (uint32_t)hd;
-    at.nsplit = b.nsplit;
+    at.nsplit = nsplit;
     at.part = b.part.as<float>();
     at.scale = 1.0f / sqrtf((float)hd);
     at.err = b.err.as<int>();
-    cuda_check(launch_attention(at, stream, pdl), "attention");
+    return at;
+}
+
+void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const LayerWeights& L = m.layers[li];
+    const uint32_t B = b.batch;
+    const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd, kw = (uint64_t)m.lkv_heads * hd;
+    float* x = b.x.as<float>();
+    {
+        const uint64_t ys[3] = {qw, kw, kw};
+        matvec_each(qkv_args(li), B, c.dim, ys, stream, pdl, "qkv matvec");
+        kernels += B;
+    }
+    cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
+    kernels += 1;
+    cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
     kernels += 2;
     {  // o-proj, residual add fused (TP: partial sums, all-reduce, then add)
         const bool tp = m.tp_size > 1;
@@ -195,6 +219,66 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
             kernels += 1;
         }
     }
+}
+
+// The persistent layer-stack kernel for a single sequence on one GPU (step_kernel.cu),
+// used when EVELYN_STEP_KERNEL=1. It is correct (same matvec code, tested against the
+// launch sequence and the oracle) but not yet faster than the launch sequence with
+// programmatic dependent launches, which stays the default.
+void Decoder::build_step_kernel() {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    step_tried = true;
+    const char* env = std::getenv("EVELYN_STEP_KERNEL");
+    if (!env || env[0] != '1') return;
+    if (b.batch != 1 || m.tp_size != 1) return;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m.device);
+    const uint32_t nsplit =
+        std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sms / std::max<uint32_t>(1, m.lkv_heads), b.pages_per_seq));
+    if (nsplit > b.nsplit) return;  // the partials buffer is sized for b.nsplit
+    const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd;
+    std::vector<StepLayer> layers(c.layers);
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        const LayerWeights& L = m.layers[li];
+        StepLayer& s = layers[li];
+        s.qkv = qkv_args(li);
+        s.qkv.prefetch = QMatDev{};
+        s.rope = rope_args(li);
+        s.attn = attn_args(li, nsplit);
+        s.o.nseg = 1;
+        s.o.seg[0].m = L.o.dev;
+        s.o.seg[0].y = b.x.as<float>();
+        s.o.seg[0].epi = EPI_ADD;
+        s.o.x = b.att.as<float>();
+        s.o.cols = (uint32_t)qw;
+        s.o.err = b.err.as<int>();
+        s.gateup.nseg = 1;
+        s.gateup.seg[0].m = L.gate.dev;
+        s.gateup.seg[0].m2 = L.up.dev;
+        s.gateup.seg[0].y = b.h.as<float>();
+        s.gateup.seg[0].epi = EPI_SWIGLU;
+        s.gateup.x = b.x.as<float>();
+        s.gateup.cols = (uint32_t)c.dim;
+        s.gateup.norm_w = L.ffn_norm;
+        s.gateup.eps = c.eps;
+        s.gateup.err = b.err.as<int>();
+        s.down.nseg = 1;
+        s.down.seg[0].m = L.down.dev;
+        s.down.seg[0].y = b.x.as<float>();
+        s.down.seg[0].epi = EPI_ADD;
+        s.down.x = b.h.as<float>();
+        s.down.cols = m.lffn;
+        s.down.err = b.err.as<int>();
+    }
+    StepKernel* k = nullptr;
+    const cudaError_t e = step_kernel_create(layers.data(), (uint32_t)layers.size(), b.err.as<int>(), &k);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        step_note = std::string("step kernel not used: ") + cudaGetErrorString(e);
+        return;
+    }
+    step_k = k;
 }
 
 void Decoder::enqueue_head(bool pdl) {
@@ -242,12 +326,17 @@ void Decoder::enqueue_dense(bool pdl) {
                             pdl),
                "embed");
     kernels += 1;
-    for (uint32_t li = 0; li < c.layers; ++li) {
-        enqueue_layer_attention(li, pdl);
-        const QMatDev* next = li + 1 < c.layers ? &m.layers[li + 1].q.dev : &m.lm_head.dev;
-        run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch, b.h.as<float>(),
-                      b.y.as<float>(), b.err.as<int>(), next, stream, pdl);
-        kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);
+    if (step_k) {
+        cuda_check(step_kernel_launch(step_k, stream), "step kernel");
+        kernels += 1;
+    } else {
+        for (uint32_t li = 0; li < c.layers; ++li) {
+            enqueue_layer_attention(li, pdl);
+            const QMatDev* next = li + 1 < c.layers ? &m.layers[li + 1].q.dev : &m.lm_head.dev;
+            run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch,
+                          b.h.as<float>(), b.y.as<float>(), b.err.as<int>(), next, stream, pdl);
+            kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);
+        }
     }
     enqueue_head(pdl);
     kernels_per_step = kernels;
@@ -289,12 +378,23 @@ void Decoder::run_routed(const evl_ffn_backend& ffn) {
 
 void Decoder::launch_graph() {
     if (!graph) {
+        if (!step_tried) build_step_kernel();  // allocates: before any capture
         for (int attempt = 0; attempt < 2 && !graph; ++attempt) {
             const bool pdl = attempt == 0;
             cudaGraph_t g = nullptr;
             cuda_check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             try {
                 enqueue_dense(pdl);
+            } catch (const Error& err) {
+                cudaStreamEndCapture(stream, &g);
+                if (g) cudaGraphDestroy(g);
+                cudaGetLastError();
+                if (!step_k) throw;
+                step_note = "step kernel not captured: " + err.msg;  // retry with the launch sequence
+                step_kernel_destroy(step_k);
+                step_k = nullptr;
+                --attempt;
+                continue;
             } catch (...) {
                 cudaStreamEndCapture(stream, &g);
                 if (g) cudaGraphDestroy(g);
@@ -306,6 +406,13 @@ void Decoder::launch_graph() {
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 graph = nullptr;
+                if (step_k) {  // retry with the per-kernel launch sequence
+                    step_note = std::string("step kernel not captured: ") + cudaGetErrorString(e);
+                    step_kernel_destroy(step_k);
+                    step_k = nullptr;
+                    --attempt;
+                    continue;
+                }
                 if (attempt == 1) cuda_check(e, "graph instantiate");
             }
             graph_pdl = pdl;
@@ -319,6 +426,7 @@ void Decoder::check_device_error() {
     if (e == DEV_OK) return;
     *b.h_err.as<int>() = 0;
     cudaMemsetAsync(b.err.p, 0, 4, stream);
+    if (step_k) step_kernel_reset(step_k, stream);
     cudaStreamSynchronize(stream);
     switch (e) {
         case DEV_ERR_TOKEN: raise(EVL_ERR_INVALID_INPUT, "token ID outside the model vocabulary");

@@ -201,3 +201,26 @@ def test_load_errors():
     with pytest.raises(evl.EvelynError) as e:
         evl.Model.load_memory(b"GGUX" + b"\0" * 64, device=0)
     assert e.value.kind == "InvalidData"
+
+
+def test_step_kernel_matches_launch_sequence(monkeypatch):
+    """The persistent layer-stack kernel (one launch per step) against the per-kernel
+    launch sequence on the same model and tokens: same logits within the attention's
+    summation-order tolerance, same greedy tokens, and far fewer launches."""
+    spec = synth.tiny(seed=21, layers=3)
+    img, m, r = _models(spec)
+    toks = _tokens(40, spec.vocab, seed=4)
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "1")
+    s1 = evl.Session(m, max_ctx=256)
+    out1 = [s1.step(t) for t in toks]
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "0")
+    s2 = evl.Session(m, max_ctx=256)
+    out2 = [s2.step(t) for t in toks]
+    assert s1.kernels_per_step < 8 < s2.kernels_per_step
+    assert max(float(np.abs(a - b).max()) for a, b in zip(out1, out2)) <= 1e-4
+    g1 = s1.generate(evl.argmax(out1[-1]), 24)
+    g2 = s2.generate(evl.argmax(out2[-1]), 24)
+    assert list(g1) == list(g2)
+    rs = orc.Session(r)  # and the oracle
+    worst = max(float(np.abs(a - rs.step(t)).max()) for a, t in zip(out1, toks))
+    assert worst <= LOGIT_TOL, worst
