@@ -395,6 +395,64 @@ evl_status evl_qmatrix_matvec(const evl_qmatrix* q, const float* d_x, float* d_y
     });
 }
 
+evl_status evl_qmatrix_matmul(evl_qmatrix* q, const float* d_x, uint32_t nvec, float* d_y, void* stream) {
+    return guarded([&] {
+        require(q && d_x && d_y, "null argument");
+        require(nvec >= 1 && nvec <= 32, "nvec must be 1..32");
+        const QMatrix& m = q->m;
+        const uint64_t gb = gemm_layout_bytes(m.type, m.rows, m.cols);
+        if (!gb) raise(EVL_ERR_UNSUPPORTED, "batched product needs Q4_K, Q6_K or Q8_0 with cols a multiple of 256");
+        DeviceGuard g(q->device);
+        cudaStream_t s = as_stream(stream);
+        if (!q->gemm_buf.p) {
+            q->gemm_buf.alloc(gb);
+            q->gemm = gemm_view(m.type, m.rows, m.cols, q->gemm_buf.as<uint8_t>());
+            cuda_check(launch_gemm_repack(m.dev, q->gemm, s), "gemm repack");
+        }
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q->device);
+        const uint32_t ksplit = gemm_ksplit(q->gemm, sms), rows_pad = q->gemm.mtiles * 128;
+        const uint64_t xb = gemm_x_bytes(32, m.cols), pb = (uint64_t)ksplit * 32 * rows_pad * 4;
+        if (q->bx.bytes < xb) q->bx.alloc(xb);
+        if (q->xinv.bytes < 128) q->xinv.alloc(128);
+        if (q->part.bytes < pb) q->part.alloc(pb);
+        GemmX gx;
+        gx.x = d_x;
+        gx.nseq = nvec;
+        gx.cols = m.cols;
+        gx.x_stride = m.cols;
+        gx.bx = q->bx.as<uint8_t>();
+        gx.xinv = q->xinv.as<float>();
+        cuda_check(launch_gemm_stage_x(gx, s, false), "stage x");
+        GemmArgs ga;
+        ga.w = q->gemm;
+        ga.bx = gx.bx;
+        ga.xinv = gx.xinv;
+        ga.nseq = nvec;
+        ga.ksplit = ksplit;
+        ga.rows_pad = rows_pad;
+        ga.part = q->part.as<float>();
+        ga.err = q->err.as<int>();
+        cuda_check(launch_qgemm(ga, s, false), "gemm");
+        GemmReduce r;
+        r.part = ga.part;
+        r.ksplit = ksplit;
+        r.rows_pad = rows_pad;
+        r.nseq = nvec;
+        r.rows = m.rows;
+        r.y = d_y;
+        r.y_stride = m.rows;
+        cuda_check(launch_gemm_reduce(r, s, false), "gemm reduce");
+        int32_t err = 0;
+        cuda_check(cudaMemcpyAsync(&err, q->err.p, 4, cudaMemcpyDeviceToHost, s), "D2H");
+        cuda_check(cudaStreamSynchronize(s), "matmul");
+        if (err) {
+            cudaMemset(q->err.p, 0, 4);
+            raise(EVL_ERR_TIMEOUT, "a device wait in the batched product timed out");
+        }
+    });
+}
+
 evl_status evl_qmatrix_dequantize(const evl_qmatrix* q, float* d_out, void* stream) {
     return guarded([&] {
         require(q && d_out, "null argument");

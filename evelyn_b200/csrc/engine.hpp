@@ -253,4 +253,7 @@ struct evl_qmatrix {
     evl::DeviceBuffer buf;
     evl::DeviceBuffer err;  // device error flag of this matrix's launches
     int device = 0;
+    // batched products (made on first use): GEMM-layout copy, staged x, partial sums
+    evl::DeviceBuffer gemm_buf, bx, xinv, part;
+    evl::QGemmDev gemm;
 };

@@ -115,6 +115,54 @@ cudaError_t step_kernel_launch(const StepKernel* k, cudaStream_t s);
 cudaError_t step_kernel_reset(const StepKernel* k, cudaStream_t s);
 void step_kernel_destroy(StepKernel* k);
 
+// ---------------------------------------------------------------- qgemm.cu
+// A matrix in the GEMM layout (per 128-row M tile and 256-value K chunk, one block of
+// the original quant bytes split by field), made on the device from the matvec layout.
+struct QGemmDev {
+    uint32_t type = 0, rows = 0, cols = 0;
+    uint32_t mtiles = 0, nchunks = 0, block_bytes = 0;
+    const uint8_t* q = nullptr;
+};
+uint64_t gemm_layout_bytes(uint32_t type, uint32_t rows, uint32_t cols);  // 0: unsupported
+QGemmDev gemm_view(uint32_t type, uint32_t rows, uint32_t cols, const uint8_t* q);
+cudaError_t launch_gemm_repack(const QMatDev& src, const QGemmDev& dst, cudaStream_t s);
+
+// x of nseq <= 32 sequences -> the MMA B operand (gemm_x_bytes) and per-sequence 2^-e
+struct GemmX {
+    const float* x = nullptr;  // [nseq][x_stride]
+    uint32_t nseq = 0, cols = 0, x_stride = 0, nsp = 0;
+    const float* norm_w = nullptr;  // fused RMSNorm (null: none)
+    float eps = 1e-6f;
+    uint8_t* bx = nullptr;
+    float* xinv = nullptr;          // [nseq]
+};
+uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols);
+cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl);
+
+// part[kr][seq][rows_pad] = sum over K range kr of W x (ksplit ranges per M tile)
+struct GemmArgs {
+    QGemmDev w;
+    const uint8_t* bx = nullptr;
+    const float* xinv = nullptr;
+    uint32_t nseq = 0, ksplit = 1, rows_pad = 0;
+    float* part = nullptr;
+    int* err = nullptr;
+};
+uint32_t gemm_ksplit(const QGemmDev& w, int sms);
+cudaError_t launch_qgemm(const GemmArgs& a, cudaStream_t s, bool pdl);
+
+// y[seq][r] (op)= sum_kr part[kr][seq][r]; EPI_SWIGLU: silu(sum part) * sum part2
+struct GemmReduce {
+    const float* part = nullptr;
+    const float* part2 = nullptr;
+    uint32_t ksplit = 1, ksplit2 = 1, rows_pad = 0, rows_pad2 = 0;
+    uint32_t nseq = 0, rows = 0;
+    float* y = nullptr;
+    uint32_t y_stride = 0;
+    int epi = EPI_STORE;
+};
+cudaError_t launch_gemm_reduce(const GemmReduce& a, cudaStream_t s, bool pdl);
+
 // ---------------------------------------------------------------- misc.cu
 cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t batch, float* x, int32_t* err,
                          cudaStream_t s, bool pdl);

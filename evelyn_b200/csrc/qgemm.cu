@@ -1,0 +1,779 @@
+// qgemm.cu -- batched decode products Y[s][r] = sum_k W[r][k] X[s][k] for up to 32
+// sequences on the 5th-generation tensor cores (tcgen05), for Batch steps (the
+// reference runs one Session::step per sequence, src/runtime.rs:773-808, each doing
+// QMatrix::matvec, :72-88).
+//
+// Weights: a second, GEMM-shaped copy of every matrix, made on the device from the
+// matvec layout (gemm_repack_kernel): per 128-row M tile and 256-value K chunk one
+// contiguous block holding the original quant bytes of those rows, split by field
+// (Q4_K: d|dmin, scales, qs; Q6_K: ql, qh, scales, d; Q8_0: d x 8, qs) with 16-byte
+// chunks XOR-swizzled by row so a warp reading 32 rows at once hits 32 banks.
+//
+// Inputs: x of every sequence (optionally RMS-normalised, src/runtime.rs:193-196)
+// becomes f16 hi + lo parts, x * 2^e = hi + lo exactly to ~22 bits, laid out as the
+// MMA's B operand (K-major canonical core matrices, N = 2 x sequences padded to 8),
+// one 34 KB block per K chunk (gemm_stage_x_kernel).
+//
+// Kernel (one CTA per SM, items = (M tile, K range)):
+//   warp 0    TMA producer: weight block + x block of each chunk into a 3-stage ring;
+//   warp 1    TMEM owner and MMA issuer (one thread): tcgen05.mma kind::f16 with A in
+//             tensor memory, B from shared memory, f32 accumulators in tensor memory;
+//   warps 2-9 dequantisation and epilogue, one row (TMEM lane) per thread: the quant
+//             values times their integer sub-block scale are exact in f16 (Q4_K
+//             q*s <= 945; Q6_K q*sc as two planes q*(sc & 15) and q*16*(sc >> 4);
+//             Q8_0 q), written to tensor memory with tcgen05.st; the f16/f32 scales
+//             (Q4_K d, dmin; Q6_K d; Q8_0 d per 32) are applied when the accumulators of
+//             one scale span are read back (tcgen05.ld). The Q4_K -dmin*m term is one
+//             more MMA per chunk against per-sub-block sums of x.
+// The tensor cores multiply exact integers by the 22-bit x parts and accumulate in
+// f32, so the result differs from the reference's sequential f32 sum only by
+// rounding order and the 2^-22-relative split of x.
+// Split K ranges write partial sums; gemm_reduce_kernel adds them in a fixed order
+// and applies the epilogue (store, residual add, SwiGLU).
+// Every wait is bounded; on a timeout the CTA raises the error flag, lets its copies
+// and MMAs land, frees its tensor memory and leaves.
+#include <algorithm>
+#include <atomic>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "kernels.h"
+
+namespace evl {
+
+namespace {
+
+constexpr uint32_t kMT = 128;          // rows per M tile (TMEM lanes)
+constexpr uint32_t kChunk = 256;       // values per K chunk
+constexpr uint32_t kGemmThreads = 320; // producer, MMA, 8 math warps
+constexpr uint32_t kMathWarps = 8;
+constexpr uint32_t kStages = 3;
+constexpr uint32_t kASlots = 4;        // A operand slots in TMEM, 32 columns each
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColA = 0, kColMin = 128, kColD = 256;  // TMEM column map; D slots 2 x 128
+
+__host__ __device__ inline uint32_t gemm_block_bytes(uint32_t type) {
+    switch (type) {
+        case GGML_Q4_K: return kMT * 144;  // 512 d|dmin + 1536 scales + 16384 qs
+        case GGML_Q6_K: return kMT * 210;  // 16384 ql + 8192 qh + 2048 scales + 256 d
+        case GGML_Q8_0: return kMT * 272;  // 2048 d + 32768 qs
+        default: return 0;
+    }
+}
+// staged x per K chunk: 16 B tiles of N x 16 plus the min-term tile, f16
+__host__ __device__ inline uint32_t gemm_xchunk_bytes(uint32_t nsp) { return 17u * (2 * nsp) * 32u; }
+
+// position of value kk (0..15) of a 16-value K step inside the MMA's K order: the
+// dequantisers pack values (4a, 4a+2) and (4a+1, 4a+3) into one 32-bit column each
+__device__ __forceinline__ uint32_t kslot(uint32_t kk) {
+    const uint32_t r = kk & 3;
+    return (kk & ~3u) | (r == 1 ? 2u : r == 2 ? 1u : r);
+}
+// byte offset of element (n, slot) in a K-major canonical tile (8x16 B core matrices,
+// K-adjacent cores 128 B apart, 8-row groups 256 B apart)
+__device__ __forceinline__ uint32_t bt_off(uint32_t n, uint32_t slot) {
+    return (n >> 3) * 256u + (slot >> 3) * 128u + (n & 7u) * 16u + (slot & 7u) * 2u;
+}
+
+// ------------------------------------------------------------------ PTX wrappers (tcgen05)
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[128 x N] (+)= A[128 x 16] (TMEM) x B[N x 16]^T (shared memory descriptor)
+__device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d),
+        "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// arrive on `bar` once every tcgen05 operation this thread issued so far has completed
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st8(uint32_t t, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(t), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t t, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            t),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t t, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(t)
+        : "memory");
+}
+
+// shared-memory matrix descriptor: K-major, no swizzle, LBO 128 B, SBO 256 B
+__device__ __forceinline__ uint64_t bdesc(const void* p) {
+    const uint64_t a = (smem_addr(p) & 0x3FFFFu) >> 4;
+    return a | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
+}
+// instruction descriptor: kind::f16, f16 A and B (K-major), f32 D, M = 128, N
+__host__ __device__ inline uint32_t mma_idesc(uint32_t n) {
+    return (1u << 4) | ((n >> 3) << 17) | ((kMT >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t h2bits(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// two 10-bit unsigned integers in the low 10 bits of each half -> exact f16 pair,
+// times (s, s) minus (bias, bias): (1024 + v) * s - 1024 * s = v * s, one rounding of
+// an exact value (all terms < 65504)
+__device__ __forceinline__ uint32_t magic_fma(uint32_t v2, uint32_t s2, uint32_t b2) {
+    const uint32_t h = v2 | 0x64006400u;
+    __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), *reinterpret_cast<const __half2*>(&s2),
+                        *reinterpret_cast<const __half2*>(&b2));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// ------------------------------------------------------------------ device repack
+// One thread per (row, K chunk): copies the chunk's original block bytes out of the
+// matvec layout (dequant.cuh's addressing) into the GEMM block.
+__global__ void gemm_repack_kernel(const QMatDev src, QGemmDev dst) {
+    const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t rows_pad = (uint64_t)dst.mtiles * kMT;
+    if (idx >= rows_pad * dst.nchunks) return;
+    const uint32_t r = (uint32_t)(idx % rows_pad), c = (uint32_t)(idx / rows_pad);
+    const uint32_t mt = r / kMT, t = r % kMT, T = src.type, N = src.nunits;
+    uint8_t* blk = const_cast<uint8_t*>(dst.q) + ((uint64_t)mt * dst.nchunks + c) * dst.block_bytes;
+    const bool live = r < src.rows;
+    auto tile = [&](uint32_t u) { return src.q + tile_address(T, N, src.row_bytes, r, u >> 5); };
+    if (T == GGML_Q4_K) {
+        uint8_t head[16];
+        uint4 qs[8];
+        if (live) {
+            const uint8_t* h = tile(4 * c) + aux_in_tile(T, N, 4 * c);
+            for (int i = 0; i < 16; ++i) head[i] = h[i];
+            for (uint32_t q = 0; q < 8; ++q) {
+                const uint32_t u = 4 * c + q / 2;
+                qs[q] = *reinterpret_cast<const uint4*>(tile(u) + chunk_in_tile(N, u, q & 1));
+            }
+        } else {
+            for (int i = 0; i < 16; ++i) head[i] = 0;
+            for (int q = 0; q < 8; ++q) qs[q] = make_uint4(0, 0, 0, 0);
+        }
+        for (int i = 0; i < 4; ++i) blk[t * 4 + i] = head[i];
+        for (int i = 0; i < 12; ++i) blk[512 + t * 12 + i] = head[4 + i];
+        for (uint32_t q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(blk + 2048 + t * 128 + ((q ^ (t & 7)) * 16)) = qs[q];
+    } else if (T == GGML_Q6_K) {
+        // units (c, h, b): chunk 0 ql[64h+16b..], chunk 1 ql[64h+32+16b..], chunk 2 qh[32h+16b..]
+        for (uint32_t h = 0; h < 2; ++h)
+            for (uint32_t b = 0; b < 2; ++b) {
+                const uint32_t u = 4 * c + 2 * h + b;
+                uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0;
+                uint32_t scw = 0;
+                if (live) {
+                    const uint8_t* tl = tile(u);
+                    q0 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 0));
+                    q1 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 1));
+                    q2 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 2));
+                    scw = *reinterpret_cast<const uint32_t*>(tl + aux_in_tile(T, N, u));
+                }
+                // ql chunk index (16-byte pieces of ql[128]): 4h + b and 4h + 2 + b
+                const uint32_t l0 = 4 * h + b, l1 = 4 * h + 2 + b, hq = 2 * h + b;
+                *reinterpret_cast<uint4*>(blk + t * 128 + ((l0 ^ (t & 7)) * 16)) = q0;
+                *reinterpret_cast<uint4*>(blk + t * 128 + ((l1 ^ (t & 7)) * 16)) = q1;
+                *reinterpret_cast<uint4*>(blk + 16384 + t * 64 + ((hq ^ ((t >> 1) & 3)) * 16)) = q2;
+                for (uint32_t k = 0; k < 4; ++k) blk[24576 + t * 16 + 8 * h + b + 2 * k] = (uint8_t)(scw >> (8 * k));
+            }
+        const uint16_t d = live ? (uint16_t)ld_u16(tile(4 * c) + d_in_tile(T, N, 4 * c)) : (uint16_t)0;
+        *reinterpret_cast<uint16_t*>(blk + 26624 + t * 2) = d;
+    } else {  // Q8_0: units 4c..4c+3, two 32-value blocks each
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t u = 4 * c + j;
+            uint32_t dw = 0;
+            uint4 q[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+            if (live) {
+                const uint8_t* tl = tile(u);
+                for (uint32_t k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, k));
+                dw = *reinterpret_cast<const uint32_t*>(tl + aux_in_tile(T, N, u));
+            }
+            *reinterpret_cast<uint32_t*>(blk + t * 16 + j * 4) = dw;  // d of blocks 2j, 2j+1
+            for (uint32_t k = 0; k < 4; ++k) {
+                const uint32_t ci = 4 * j + k;  // 16-byte piece of the chunk's 256 qs bytes
+                *reinterpret_cast<uint4*>(blk + 2048 + t * 256 + (((ci & 8) | ((ci & 7) ^ (t & 7))) * 16)) = q[k];
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ x staging
+// CTA s (< nsp): sequence s's x (normalised when norm_w) -> hi/lo f16 B rows s and
+// nsp + s of every chunk, the Q4_K min-term sums, and xinv[s] = 2^-e. Sequences
+// >= nseq are zero rows.
+__global__ void gemm_stage_x_kernel(const GemmX a) {
+    const uint32_t s = blockIdx.x, K = a.cols, nsp = a.nsp, N = 2 * nsp;
+    const uint32_t tid = threadIdx.x, nt = blockDim.x;
+    __shared__ float red[32];
+    __shared__ float sh_inv, sh_up;
+    const bool live = s < a.nseq;
+    const float* x = a.x + (uint64_t)s * a.x_stride;
+    pdl_wait();
+    float inv = 1.f;
+    if (live && a.norm_w) {
+        float ss = 0.f;
+        for (uint32_t i = tid; i < K; i += nt) ss += x[i] * x[i];
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (uint32_t w = 0; w < nt / 32; ++w) t += red[w];
+            sh_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+        }
+        __syncthreads();
+        inv = sh_inv;
+    }
+    auto val = [&](uint32_t i) {
+        float v = x[i];
+        if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
+        return v;
+    };
+    float mx = 0.f;
+    if (live)
+        for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(val(i)));
+    mx = warp_max(mx);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < nt / 32; ++w) t = fmaxf(t, red[w]);
+        int e = 0;
+        if (t > 0.f) frexpf(t, &e);  // t in [2^(e-1), 2^e)
+        const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
+        sh_up = ldexpf(1.0f, sc);
+        if (live) a.xinv[s] = ldexpf(1.0f, -sc);
+    }
+    __syncthreads();
+    const float up = sh_up;
+    const uint32_t nchunks = K / kChunk, cb = gemm_xchunk_bytes(nsp);
+    for (uint32_t i = tid; i < K; i += nt) {
+        const float v = live ? __fmul_rn(val(i), up) : 0.f;
+        const __half hi = __float2half_rn(v);
+        const __half lo = __float2half_rn(v - __half2float(hi));
+        const uint32_t c = i / kChunk, k = i % kChunk;
+        uint8_t* base = a.bx + (uint64_t)c * cb + (k / 16) * (N * 32u);
+        const uint32_t sl = kslot(k % 16);
+        *reinterpret_cast<__half*>(base + bt_off(s, sl)) = hi;
+        *reinterpret_cast<__half*>(base + bt_off(nsp + s, sl)) = lo;
+    }
+    // per 32-value sub-block sums, scaled by 2^-5 to stay inside f16, into the min tile
+    for (uint32_t j = tid; j < K / 32; j += nt) {
+        float sm = 0.f;
+        if (live)
+            for (uint32_t e = 0; e < 32; ++e) sm += __fmul_rn(val(32 * j + e), up);
+        sm *= 0.03125f;
+        const __half hi = __float2half_rn(sm);
+        const __half lo = __float2half_rn(sm - __half2float(hi));
+        const uint32_t c = j / 8, sb = j % 8;
+        uint8_t* base = a.bx + (uint64_t)c * cb + 16 * (N * 32u);
+        *reinterpret_cast<__half*>(base + bt_off(s, kslot(sb))) = hi;
+        *reinterpret_cast<__half*>(base + bt_off(nsp + s, kslot(sb))) = lo;
+        *reinterpret_cast<__half*>(base + bt_off(s, kslot(8 + sb))) = __float2half_rn(0.f);
+        *reinterpret_cast<__half*>(base + bt_off(nsp + s, kslot(8 + sb))) = __float2half_rn(0.f);
+    }
+    (void)nchunks;
+    pdl_launch_dependents();
+}
+
+// ------------------------------------------------------------------ the GEMM
+struct GemmPlan {
+    GemmArgs a;
+    uint32_t nsp, N, ksplit, items, xchunk;
+    uint32_t sub_per_chunk;  // A slots per chunk: Q4_K 4 (64 values), Q6_K 8 (32 x 2 planes), Q8_0 8
+    uint32_t eu_per_chunk;   // accumulator spans per chunk: Q4_K, Q6_K 1; Q8_0 8
+};
+
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void item_range(const GemmPlan& P, uint32_t item, uint32_t& mt, uint32_t& c0, uint32_t& c1,
+                                           uint32_t& kr) {
+    const uint32_t nch = P.a.w.nchunks;
+    mt = item / P.ksplit;
+    kr = item % P.ksplit;
+    c0 = (uint32_t)(((uint64_t)nch * kr) / P.ksplit);
+    c1 = (uint32_t)(((uint64_t)nch * (kr + 1)) / P.ksplit);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_constant__ GemmPlan P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t st_full[kStages], st_empty[kStages];
+    __shared__ __align__(8) uint64_t a_full[kASlots], a_empty[kASlots];
+    __shared__ __align__(8) uint64_t m_full[2], m_empty[2];
+    __shared__ __align__(8) uint64_t d_full[2], d_empty[2];
+    __shared__ __align__(8) uint64_t fin_bar;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const GemmArgs& A = P.a;
+    const uint32_t T = A.w.type, wbytes = A.w.block_bytes, stage_bytes = wbytes + P.xchunk;
+    const uint32_t SP = P.sub_per_chunk;
+    const uint32_t item0 = (uint32_t)(((uint64_t)P.items * blockIdx.x) / gridDim.x);
+    const uint32_t item1 = (uint32_t)(((uint64_t)P.items * (blockIdx.x + 1)) / gridDim.x);
+
+    if (tid == 0) {
+        abort_flag = 0;
+        for (uint32_t i = 0; i < kStages; ++i) {
+            mbar_init(&st_full[i], 1);
+            mbar_init(&st_empty[i], kMathWarps + 1);
+        }
+        for (uint32_t i = 0; i < kASlots; ++i) {
+            mbar_init(&a_full[i], 4);  // the four quadrant warps of one math group
+            mbar_init(&a_empty[i], 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            mbar_init(&m_full[i], 4);
+            mbar_init(&m_empty[i], 1);
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], kMathWarps);
+        }
+        mbar_init(&fin_bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t tm = tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            uint32_t n = 0;
+            for (uint32_t it = item0; it < item1 && !abort_flag; ++it) {
+                uint32_t mt, c0, c1, kr;
+                item_range(P, it, mt, c0, c1, kr);
+                for (uint32_t c = c0; c < c1; ++c, ++n) {
+                    const uint32_t s = n % kStages, ph = n / kStages;
+                    if (ph > 0 && !bwait(&st_empty[s], (ph - 1) & 1, &abort_flag)) break;
+                    uint8_t* dst = smem + s * stage_bytes;
+                    mbar_arrive_expect_tx(&st_full[s], stage_bytes);
+                    tma_load_1d(dst, A.w.q + ((uint64_t)mt * A.w.nchunks + c) * wbytes, wbytes, &st_full[s]);
+                    tma_load_1d(dst + wbytes, A.bx + (uint64_t)c * P.xchunk, P.xchunk, &st_full[s]);
+                }
+                if (abort_flag) break;
+            }
+            if (abort_flag)  // copies in flight land before the CTA leaves
+                for (uint32_t s = 0; s < kStages && s < n; ++s) mbar_wait(&st_full[s], ((n - 1 - s) / kStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = mma_idesc(P.N);
+            uint32_t n = 0, g = 0, e = 0, mc = 0;
+            bool ok = true;
+            for (uint32_t it = item0; it < item1 && ok; ++it) {
+                uint32_t mt, c0, c1, kr;
+                item_range(P, it, mt, c0, c1, kr);
+                for (uint32_t c = c0; c < c1 && ok; ++c, ++n) {
+                    const uint32_t s = n % kStages;
+                    if (!bwait(&st_full[s], (n / kStages) & 1, &abort_flag)) { ok = false; break; }
+                    const uint8_t* bx = smem + s * stage_bytes + wbytes;
+                    const uint32_t tile_b = P.N * 32;
+                    for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
+                        const uint32_t as = g % kASlots;
+                        const uint32_t eu_first = (T == GGML_Q8_0) || q == 0;
+                        const uint32_t ds = e % 2;
+                        if (eu_first && e >= 2 && !bwait(&d_empty[ds], ((e / 2) - 1) & 1, &abort_flag)) { ok = false; break; }
+                        if (!bwait(&a_full[as], (g / kASlots) & 1, &abort_flag)) { ok = false; break; }
+                        tc_after();
+                        const uint32_t acol = tm + kColA + as * 32, dcol = tm + kColD + ds * 128;
+                        if (T == GGML_Q4_K) {  // 64 values: B tiles 4q..4q+3
+                            for (uint32_t i = 0; i < 4; ++i)
+                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (4 * q + i) * tile_b), idesc, (q | i) != 0);
+                        } else if (T == GGML_Q6_K) {  // 32 values x two planes: B tiles 2q, 2q+1
+                            for (uint32_t i = 0; i < 4; ++i)
+                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (2 * q + (i & 1)) * tile_b), idesc,
+                                           (q | i) != 0);
+                        } else {  // Q8_0 block q: B tiles 2q, 2q+1
+                            for (uint32_t i = 0; i < 2; ++i)
+                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (2 * q + i) * tile_b), idesc, i != 0);
+                        }
+                        mma_commit(&a_empty[as]);
+                        const bool eu_last = (T == GGML_Q8_0) || q + 1 == SP;
+                        if (eu_last) {
+                            if (T == GGML_Q4_K) {  // -dmin * sum_j m_j * sum(x of sub-block j)
+                                const uint32_t ms = mc % 2;
+                                if (!bwait(&m_full[ms], (mc / 2) & 1, &abort_flag)) { ok = false; break; }
+                                tc_after();
+                                mma_tmem_a(dcol + 64, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b), idesc, 0);
+                                mma_commit(&m_empty[ms]);
+                                ++mc;
+                            }
+                            mma_commit(&d_full[ds]);
+                            ++e;
+                        }
+                    }
+                    if (ok) mma_commit(&st_empty[s]);
+                }
+            }
+            if (!ok) {
+                abort_flag = 1;
+                if (A.err) atomicExch(A.err, DEV_ERR_WAIT_TIMEOUT);
+            }
+            // every MMA issued has completed before the tensor memory is freed
+            mma_commit(&fin_bar);
+            mbar_wait(&fin_bar, 0);
+        }
+    } else {
+        // ---------------------------------------------------------------- math warps
+        const uint32_t mw = warp - 2, grp = mw / 4, qd = warp & 3;  // group 0/1, TMEM lane quadrant
+        const uint32_t t = qd * 32 + lane;                            // row within the M tile
+        const uint32_t lane_addr = (qd * 32u) << 16;
+        const uint32_t half = P.nsp / 2;                               // sequences per group in the epilogue
+        float acc[16];
+        uint32_t n = 0, g = 0, e = 0, mc = 0;
+        bool ok = true;
+        // scales of the accumulator spans not yet read back (two in flight)
+        float eu_d[2] = {0.f, 0.f}, eu_dmin[2] = {0.f, 0.f};
+        auto epilogue = [&](uint32_t eu) -> bool {  // read span eu back and scale it into acc
+            const uint32_t ds = eu % 2;
+            if (!bwait(&d_full[ds], (eu / 2) & 1, &abort_flag)) return false;
+            tc_after();
+            uint32_t hi[16], lo[16], mh[16], ml[16];
+            const uint32_t dcol = tm + lane_addr + kColD + ds * 128 + grp * half;
+            tmem_ld16(dcol, hi);
+            tmem_ld16(dcol + P.nsp, lo);
+            if (T == GGML_Q4_K) {
+                tmem_ld16(dcol + 64, mh);
+                tmem_ld16(dcol + 64 + P.nsp, ml);
+            }
+            tmem_ld_wait();
+            tc_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_empty[ds]);
+            const float d = eu_d[ds], dm = eu_dmin[ds];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float v = __uint_as_float(hi[i]) + __uint_as_float(lo[i]);
+                acc[i] = fmaf(d, v, acc[i]);
+                if (T == GGML_Q4_K) acc[i] = fmaf(-dm * 32.f, __uint_as_float(mh[i]) + __uint_as_float(ml[i]), acc[i]);
+            }
+            return true;
+        };
+        for (uint32_t it = item0; it < item1 && ok; ++it) {
+            uint32_t mt, c0, c1, kr;
+            item_range(P, it, mt, c0, c1, kr);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            uint32_t first_eu = e;
+            for (uint32_t c = c0; c < c1 && ok; ++c, ++n) {
+                const uint32_t s = n % kStages;
+                if (!bwait(&st_full[s], (n / kStages) & 1, &abort_flag)) { ok = false; break; }
+                const uint8_t* wb = smem + s * stage_bytes;
+                // this row's scales for the chunk
+                float q4_s[8], q4_m[8], d = 0.f, dmin = 0.f;
+                float q8_d[8];
+                uint32_t q6_sc[4];
+                if (T == GGML_Q4_K) {
+                    const uint32_t dm = *reinterpret_cast<const uint32_t*>(wb + t * 4);
+                    d = f16_exact(dm & 0xffff);
+                    dmin = f16_exact(dm >> 16);
+                    const uint8_t* sc = wb + 512 + t * 12;
+                    for (int j = 0; j < 8; ++j) scale_min_bytes(j, sc, &q4_s[j], &q4_m[j]);
+                } else if (T == GGML_Q6_K) {
+                    const uint4 sc4 = *reinterpret_cast<const uint4*>(wb + 24576 + t * 16);
+                    q6_sc[0] = sc4.x; q6_sc[1] = sc4.y; q6_sc[2] = sc4.z; q6_sc[3] = sc4.w;
+                    d = f16_exact(*reinterpret_cast<const uint16_t*>(wb + 26624 + t * 2));
+                } else {
+                    const uint4 dd = *reinterpret_cast<const uint4*>(wb + t * 16);
+                    const uint32_t w4[4] = {dd.x, dd.y, dd.z, dd.w};
+                    for (int j = 0; j < 4; ++j) {
+                        q8_d[2 * j] = f16_exact(w4[j] & 0xffff);
+                        q8_d[2 * j + 1] = f16_exact(w4[j] >> 16);
+                    }
+                }
+                for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
+                    if ((g & 1) == grp) {  // this group dequantises sub-chunk g
+                        const uint32_t as = g % kASlots;
+                        if (g >= kASlots && !bwait(&a_empty[as], ((g / kASlots) - 1) & 1, &abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_after();
+                        uint32_t v[32];
+                        if (T == GGML_Q4_K) {  // unit q: qs bytes 32q..32q+31, sub-blocks 2q (low), 2q+1 (high)
+                            const uint32_t sl = (uint32_t)q4_s[2 * q], sh = (uint32_t)q4_s[2 * q + 1];
+                            const uint32_t s2l = h2bits((float)sl, (float)sl), b2l = h2bits(-1024.f * sl, -1024.f * sl);
+                            const uint32_t s2h = h2bits((float)sh, (float)sh), b2h = h2bits(-1024.f * sh, -1024.f * sh);
+                            for (uint32_t hc = 0; hc < 2; ++hc) {
+                                const uint32_t ci = 2 * q + hc;
+                                const uint4 w = *reinterpret_cast<const uint4*>(wb + 2048 + t * 128 + ((ci ^ (t & 7)) * 16));
+                                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int a = 0; a < 4; ++a) {
+                                    const uint32_t col = 2 * (4 * hc + a);  // value group 16hc + 4a
+                                    v[col] = magic_fma(ws[a] & 0x000F000Fu, s2l, b2l);
+                                    v[col + 1] = magic_fma((ws[a] >> 8) & 0x000F000Fu, s2l, b2l);
+                                    v[16 + col] = magic_fma((ws[a] >> 4) & 0x000F000Fu, s2h, b2h);
+                                    v[16 + col + 1] = magic_fma((ws[a] >> 12) & 0x000F000Fu, s2h, b2h);
+                                }
+                            }
+                            tmem_st16(tm + lane_addr + kColA + as * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                            tmem_st16(tm + lane_addr + kColA + as * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                        } else if (T == GGML_Q6_K) {  // values 32q..32q+31: half hh = q/4, run kq = q%4
+                            const uint32_t hh = q >> 2, kq = q & 3;
+                            const uint32_t lci0 = 4 * hh + 2 * (kq & 1), hci0 = 2 * hh;  // 16-byte pieces
+                            const uint32_t sw = (t & 7), swq = ((t >> 1) & 3);
+                            const uint4 L0 = *reinterpret_cast<const uint4*>(wb + t * 128 + (((lci0) ^ sw) * 16));
+                            const uint4 L1 = *reinterpret_cast<const uint4*>(wb + t * 128 + (((lci0 + 1) ^ sw) * 16));
+                            const uint4 H0 = *reinterpret_cast<const uint4*>(wb + 16384 + t * 64 + (((hci0) ^ swq) * 16));
+                            const uint4 H1 = *reinterpret_cast<const uint4*>(wb + 16384 + t * 64 + (((hci0 + 1) ^ swq) * 16));
+                            const uint32_t lw[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+                            const uint32_t hw[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+                            // run scales sc[8hh + l/16 + 2kq] for l < 16 and l >= 16
+                            const uint32_t sidx0 = 8 * hh + 2 * kq, sidx1 = sidx0 + 1;
+                            const int sc0 = (int8_t)(q6_sc[sidx0 >> 2] >> (8 * (sidx0 & 3)));
+                            const int sc1 = (int8_t)(q6_sc[sidx1 >> 2] >> (8 * (sidx1 & 3)));
+                            const __half2 bias = __floats2half2_rn(1056.f, 1056.f);
+#pragma unroll
+                            for (int a = 0; a < 8; ++a) {  // bytes 4a..4a+3 of the 32-value run pair
+                                const int sc = a < 4 ? sc0 : sc1;
+                                const int shi = sc >> 4, slo = sc - 16 * shi;
+                                const __half2 p1 = __floats2half2_rn((float)slo, (float)slo);
+                                const __half2 p2 = __floats2half2_rn((float)(16 * shi), (float)(16 * shi));
+                                const uint32_t nib = (kq < 2) ? (lw[a] & 0x0F0F0F0Fu) : ((lw[a] >> 4) & 0x0F0F0F0Fu);
+                                const uint32_t qv = nib | (((hw[a] >> (2 * kq)) & 0x03030303u) << 4);  // 0..63 per byte
+                                const uint32_t e0 = (qv & 0x00FF00FFu) | 0x64006400u, e1 = ((qv >> 8) & 0x00FF00FFu) | 0x64006400u;
+                                const __half2 q0 = __hsub2(*reinterpret_cast<const __half2*>(&e0), bias);  // q - 32
+                                const __half2 q1 = __hsub2(*reinterpret_cast<const __half2*>(&e1), bias);
+                                __half2 r;
+                                r = __hmul2(q0, p1); v[2 * a] = *reinterpret_cast<uint32_t*>(&r);
+                                r = __hmul2(q1, p1); v[2 * a + 1] = *reinterpret_cast<uint32_t*>(&r);
+                                r = __hmul2(q0, p2); v[16 + 2 * a] = *reinterpret_cast<uint32_t*>(&r);
+                                r = __hmul2(q1, p2); v[16 + 2 * a + 1] = *reinterpret_cast<uint32_t*>(&r);
+                            }
+                            tmem_st16(tm + lane_addr + kColA + as * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                            tmem_st16(tm + lane_addr + kColA + as * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                        } else {  // Q8_0 block q: qs bytes 32q..32q+31
+                            const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+                            for (uint32_t hc = 0; hc < 2; ++hc) {
+                                const uint32_t ci = 2 * q + hc;
+                                const uint4 w = *reinterpret_cast<const uint4*>(
+                                    wb + 2048 + t * 256 + (((ci & 8) | ((ci & 7) ^ (t & 7))) * 16));
+                                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int a = 0; a < 4; ++a) {
+                                    const uint32_t u = ws[a] ^ 0x80808080u;  // q + 128, per byte
+                                    const uint32_t e0 = (u & 0x00FF00FFu) | 0x64006400u, e1 = ((u >> 8) & 0x00FF00FFu) | 0x64006400u;
+                                    __half2 r;
+                                    r = __hsub2(*reinterpret_cast<const __half2*>(&e0), bias);
+                                    v[2 * (4 * hc + a)] = *reinterpret_cast<uint32_t*>(&r);
+                                    r = __hsub2(*reinterpret_cast<const __half2*>(&e1), bias);
+                                    v[2 * (4 * hc + a) + 1] = *reinterpret_cast<uint32_t*>(&r);
+                                }
+                            }
+                            tmem_st16(tm + lane_addr + kColA + as * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                        }
+                        tmem_st_wait();
+                        tc_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[as]);
+                    }
+                    const bool eu_last = (T == GGML_Q8_0) || q + 1 == SP;
+                    if (eu_last) {
+                        const uint32_t ds = e % 2;
+                        eu_d[ds] = (T == GGML_Q8_0) ? q8_d[q] : d;
+                        eu_dmin[ds] = dmin;
+                        if (T == GGML_Q4_K && grp == 0) {  // the chunk's mins: A of the min-term MMA
+                            const uint32_t ms = mc % 2;
+                            if (mc >= 2 && !bwait(&m_empty[ms], ((mc / 2) - 1) & 1, &abort_flag)) { ok = false; break; }
+                            tc_after();
+                            uint32_t mv[8];
+                            mv[0] = h2bits(q4_m[0], q4_m[2]);
+                            mv[1] = h2bits(q4_m[1], q4_m[3]);
+                            mv[2] = h2bits(q4_m[4], q4_m[6]);
+                            mv[3] = h2bits(q4_m[5], q4_m[7]);
+                            mv[4] = mv[5] = mv[6] = mv[7] = 0u;
+                            tmem_st8(tm + lane_addr + kColMin + ms * 8, mv);
+                            tmem_st_wait();
+                            tc_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&m_full[ms]);
+                        }
+                        if (T == GGML_Q4_K) ++mc;
+                        // read back the previous span (one span of lag keeps the MMAs busy)
+                        if (e > first_eu && !epilogue(e - 1)) { ok = false; break; }
+                        ++e;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&st_empty[s]);  // done with this stage's weights
+            }
+            if (!ok) break;
+            if (e > first_eu && !epilogue(e - 1)) { ok = false; break; }
+            // partial sums of this item: part[kr][seq][row]
+            const uint32_t row = mt * kMT + t;
+            for (uint32_t i = 0; i < half; ++i) {
+                const uint32_t sq = grp * half + i;
+                if (sq < A.nseq)
+                    A.part[((uint64_t)kr * A.nseq + sq) * A.rows_pad + row] = acc[i] * A.xinv[sq];
+            }
+        }
+        if (!ok) {
+            abort_flag = 1;
+            if (lane == 0 && A.err) atomicExch(A.err, DEV_ERR_WAIT_TIMEOUT);
+        }
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 1) tmem_dealloc(tm, kTmemCols);
+}
+
+// ------------------------------------------------------------------ reduce + epilogue
+__global__ void gemm_reduce_kernel(const GemmReduce a) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)a.nseq * a.rows) return;
+    const uint32_t s = (uint32_t)(i / a.rows), r = (uint32_t)(i % a.rows);
+    pdl_wait();
+    float sum = 0.f, sum2 = 0.f;
+    for (uint32_t k = 0; k < a.ksplit; ++k) sum += a.part[((uint64_t)k * a.nseq + s) * a.rows_pad + r];
+    if (a.part2)
+        for (uint32_t k = 0; k < a.ksplit2; ++k) sum2 += a.part2[((uint64_t)k * a.nseq + s) * a.rows_pad2 + r];
+    float* y = a.y + (uint64_t)s * a.y_stride + r;
+    if (a.epi == EPI_SWIGLU) *y = __fmul_rn(__fdiv_rn(sum, __fadd_rn(1.0f, expf(-sum))), sum2);
+    else if (a.epi == EPI_ADD) *y += sum;
+    else *y = sum;
+    pdl_launch_dependents();
+}
+
+std::atomic<int> g_gemm_attr[64];
+
+cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, cudaLaunchAttribute* at) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+}  // namespace
+
+uint64_t gemm_layout_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
+    const uint32_t bb = gemm_block_bytes(type);
+    if (!bb || !rows || cols % kChunk) return 0;
+    return (uint64_t)((rows + kMT - 1) / kMT) * (cols / kChunk) * bb;
+}
+
+QGemmDev gemm_view(uint32_t type, uint32_t rows, uint32_t cols, const uint8_t* q) {
+    QGemmDev g;
+    g.type = type;
+    g.rows = rows;
+    g.cols = cols;
+    g.mtiles = (rows + kMT - 1) / kMT;
+    g.nchunks = cols / kChunk;
+    g.block_bytes = gemm_block_bytes(type);
+    g.q = q;
+    return g;
+}
+
+cudaError_t launch_gemm_repack(const QMatDev& src, const QGemmDev& dst, cudaStream_t s) {
+    if (src.type != dst.type || !gemm_block_bytes(src.type) || src.cols != dst.cols || src.cols % kChunk)
+        return cudaErrorInvalidValue;
+    const uint64_t n = (uint64_t)dst.mtiles * kMT * dst.nchunks;
+    gemm_repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, dst);
+    return cudaGetLastError();
+}
+
+uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols) {
+    const uint32_t nsp = (nseq + 7) / 8 * 8;
+    return (uint64_t)(cols / kChunk) * gemm_xchunk_bytes(nsp);
+}
+
+cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl) {
+    if (!a.nseq || a.nseq > 32 || a.cols % kChunk || !a.x || !a.bx || !a.xinv) return cudaErrorInvalidValue;
+    a.nsp = (a.nseq + 7) / 8 * 8;
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3(a.nsp), dim3(256), 0, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, gemm_stage_x_kernel, a);
+}
+
+uint32_t gemm_ksplit(const QGemmDev& w, int sms) {
+    const uint32_t want = (uint32_t)std::max(1, (2 * sms + (int)w.mtiles / 2) / (int)w.mtiles);
+    return std::max<uint32_t>(1, std::min<uint32_t>(want, w.nchunks));
+}
+
+cudaError_t launch_qgemm(const GemmArgs& a, cudaStream_t s, bool pdl) {
+    if (!a.w.q || !a.bx || !a.part || !a.xinv || !a.nseq || a.nseq > 32 || !a.ksplit) return cudaErrorInvalidValue;
+    if (a.w.type != GGML_Q4_K && a.w.type != GGML_Q6_K && a.w.type != GGML_Q8_0) return cudaErrorInvalidValue;
+    GemmPlan P{};
+    P.a = a;
+    P.nsp = (a.nseq + 7) / 8 * 8;
+    P.N = 2 * P.nsp;
+    P.ksplit = a.ksplit;
+    P.items = a.w.mtiles * a.ksplit;
+    P.xchunk = gemm_xchunk_bytes(P.nsp);
+    P.sub_per_chunk = a.w.type == GGML_Q4_K ? 4 : 8;
+    P.eu_per_chunk = a.w.type == GGML_Q8_0 ? 8 : 1;
+    int dev = 0, sms = 148;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // at least 116 KB so that no two CTAs share an SM: each allocates all 512 TMEM columns
+    const size_t smem = std::max<size_t>(kStages * (size_t)(a.w.block_bytes + P.xchunk), 116 * 1024);
+    if (dev >= 0 && dev < 64 && !g_gemm_attr[dev]) {
+        e = cudaFuncSetAttribute(qgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+        if (e != cudaSuccess) return e;
+        g_gemm_attr[dev] = 1;
+    }
+    if (smem > 225 * 1024) return cudaErrorInvalidValue;
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3(std::min<uint32_t>(P.items, (uint32_t)sms)), dim3(kGemmThreads), smem, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, qgemm_kernel, P);
+}
+
+cudaError_t launch_gemm_reduce(const GemmReduce& a, cudaStream_t s, bool pdl) {
+    if (!a.part || !a.y || !a.nseq || !a.rows || !a.ksplit) return cudaErrorInvalidValue;
+    const uint64_t n = (uint64_t)a.nseq * a.rows;
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, gemm_reduce_kernel, a);
+}
+
+}  // namespace evl

@@ -130,6 +130,7 @@ SIGNATURES = {
     "evl_qmatrix_bytes": (C.c_uint64, [_P]),
     "evl_qmatrix_matvec": (C.c_int, [_P, _P, _P, _P]),
     "evl_qmatrix_dequantize": (C.c_int, [_P, _P, _P]),
+    "evl_qmatrix_matmul": (C.c_int, [_P, _P, C.c_uint32, _P, _P]),
     "evl_attention_decode": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                        _P, _P]),
     "evl_attention_workspace_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),

@@ -161,6 +161,11 @@ uint64_t evl_qmatrix_bytes(const evl_qmatrix* m);
 /* y = W x (QMatrix::matvec, runtime.rs:72-88). device pointers, x 16-byte aligned;
  * stream may be NULL */
 evl_status evl_qmatrix_matvec(const evl_qmatrix* m, const float* d_x, float* d_y, void* stream);
+/* QMatrix::matvec (runtime.rs:72-88) of nvec (1..32) vectors at once, as a Batch step
+ * needs: d_x [nvec][cols] -> d_y [nvec][rows], on the tensor cores (the first call
+ * also builds the matrix's GEMM-layout copy). cols must be a multiple of 256; types
+ * Q4_K, Q6_K, Q8_0. Synchronises `stream`. */
+evl_status evl_qmatrix_matmul(evl_qmatrix* m, const float* d_x, uint32_t nvec, float* d_y, void* stream);
 /* exact dequantisation of all rows to d_out [rows][cols]. device pointers */
 evl_status evl_qmatrix_dequantize(const evl_qmatrix* m, float* d_out, void* stream);
 /* GQA decode attention for one new position (the attention core of full_attention,
