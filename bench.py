@@ -281,6 +281,9 @@ def run_ours(args):
     step_bytes = spec.weight_bytes_per_token() + kv_pos * mean_ctx + kv_pos / 1
     tok_s = K / (ms_max / 1e3)
     base = cpu_baseline(img) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    launches = sess.kernels_per_step * K
+    del sess
+    bs32 = run_batch(model, spec, args, hbm, peak_kind) if (world == 1 and args.batch > 1) else None
     if rank == 0:
         clocks = clk.summary()
         line = {
@@ -299,16 +302,54 @@ def run_ours(args):
             "e2e": {"value": round(K / (e2e_ms / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": spec.vocab * 4 + 4 + 4},
             "roofline": roof,
-            "gpu_launches": sess.kernels_per_step * K,
+            "gpu_launches": launches,
             "clocks": clocks,
         }
         if base:
             line["cpu_baseline"] = base
+        if bs32:
+            line["bs32"] = bs32
         print(json.dumps(line), flush=True)
-    del sess, model
+    del model
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_batch(model, spec, args, hbm, peak_kind):
+    """The batched half of the metric: `args.batch` sequences decoded together after a
+    `args.batch_prefix`-token prefix each (prefilled by batch steps); K timed steps through
+    evl_batch_step (tokens H2D, argmax D2H, synchronised each step)."""
+    import torch
+    from evelyn_b200 import runtime as evl_rt
+    B, P, K = args.batch, args.batch_prefix, args.batch_steps
+    batch = evl_rt.Batch(model, B, max_ctx=P + K + 8)
+    rng = np.random.default_rng(1)
+    for _ in range(P):
+        batch.step(rng.integers(0, spec.vocab, B), logits=False)
+    toks = rng.integers(0, spec.vocab, B)
+    for _ in range(3):  # warm-up
+        toks = batch.step(toks, logits=False)
+    ext = torch.cuda.ExternalStream(batch.stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(K):
+        toks = batch.step(toks, logits=False)
+    e1.record(ext)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    ctx0 = P + 3
+    kv_pos = spec.kv_bytes_per_position(2)
+    step_bytes = spec.weight_bytes_per_token() + B * kv_pos * (ctx0 + (K + 1) / 2)
+    gbs = step_bytes * K / (ms / 1e3) / 1e9
+    del batch
+    return {"value": round(B * K / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / K, 4),
+            "global_batch": B, "workload": f"{B} sequences, {P}-token prefix each, then {K} greedy steps "
+                                           f"(ctx {ctx0}..{ctx0 + K}); products on tcgen05 tensor cores",
+            "e2e_note": "each step through evl_batch_step: token ids H2D, argmax D2H, synchronised",
+            "step_hbm": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
+                         "frac": round(gbs / hbm, 4), "peak": hbm, "peak_source": peak_kind}}
 
 
 def _random_raw(ggml_type: int, rows: int, cols: int, rng) -> np.ndarray:
@@ -471,6 +512,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens fed before decoding")
     ap.add_argument("--sweep", action="store_true", help="isolated kernel sweep (one JSON line per case)")
     ap.add_argument("--sweep-only", default="", help="comma-separated sweep case names")
+    ap.add_argument("--batch", type=int, default=32, help="sequences of the batched measurement (0: skip)")
+    ap.add_argument("--batch-prefix", type=int, default=2048, help="prefix tokens per sequence before timing")
+    ap.add_argument("--batch-steps", type=int, default=64, help="timed batched steps")
     ap.add_argument("--reps", type=int, default=10, help="timed passes per sweep case")
     args = ap.parse_args()
     if args.warmup < 3:

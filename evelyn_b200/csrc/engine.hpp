@@ -128,6 +128,7 @@ struct QMatrix {
     size_t total_bytes = 0;  // rows * row_bytes, rounded up to 256
     size_t offset = 0;       // inside the model's weight buffer
     QMatDev dev;             // device view once placed
+    QGemmDev gemm;           // GEMM-layout copy for batched steps (q == null until built)
     size_t bytes() const { return total_bytes; }
 };
 
@@ -175,6 +176,11 @@ struct Model {
     std::map<std::string, std::pair<float*, size_t>> vecs;
     uint64_t weight_bytes_per_step = 0;
 
+    // GEMM-layout copies of every layer matrix and the LM head, built on the device the
+    // first time a batch of more than one sequence is created (build_gemm_weights)
+    DeviceBuffer gemm_weights;
+    bool gemm_ready = false;
+
     // model-level calls (dense_ffn, matvec, dequantize) run on this stream
     std::mutex mu;
     cudaStream_t stream = nullptr;
@@ -188,6 +194,10 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
 
 void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s);
 
+// Makes the GEMM-layout copies (QMatrix::gemm) of the layer matrices and the LM head;
+// returns false (nothing built) when some matrix has no GEMM layout.
+bool build_gemm_weights(Model& m);
+
 // Device launch sequence of one dense FFN on `x` (already normalised when norm_w is
 // null) writing y; add=true accumulates into y (residual). TP: partial + all-reduce.
 // `next` (may be null) is the matrix the launch after the FFN reads (warmed into L2).
@@ -200,6 +210,7 @@ struct StepBuffers {
     uint32_t max_ctx = 0, pages_per_seq = 0;
     DeviceBuffer kv, page_table, pos, tokens, argmax, hist, err;
     DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
+    DeviceBuffer gbx, gxinv, gpart, gpart2;  // batched products: staged x, 2^-e, partial sums
     uint32_t nsplit = 1, amax_parts = 1;
     PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;
 };
@@ -223,6 +234,12 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     RopeArgs rope_args(uint32_t layer) const;
     AttnArgs attn_args(uint32_t layer, uint32_t nsplit) const;
     void build_step_kernel();
+    bool use_gemm = false;  // batch > 1 on one GPU: tensor-core products
+    void enqueue_batched(bool pdl);
+    void gemm_stage(const float* x, uint32_t cols, uint32_t stride, const float* norm_w, bool pdl);
+    void gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool pdl);
+    void gemm_reduce(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride, int epi,
+                     const float* part2, uint32_t ksplit2, bool pdl);
     // Enqueue one dense step (every kernel) on `stream`.
     void enqueue_dense(bool pdl);
     void enqueue_layer_attention(uint32_t layer, bool pdl);

@@ -331,6 +331,32 @@ void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s) {
     nccl_check(nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, m.comm, s), "ncclAllReduce");
 }
 
+bool build_gemm_weights(Model& m) {
+    if (m.gemm_ready) return true;
+    std::vector<QMatrix*> mats;
+    for (auto& L : m.layers)
+        for (QMatrix* q : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(q);
+    mats.push_back(&m.lm_head);
+    uint64_t total = 0;
+    std::vector<uint64_t> off;
+    for (QMatrix* q : mats) {
+        const uint64_t b = gemm_layout_bytes(q->type, q->rows, q->cols);
+        if (!b) return false;
+        off.push_back(total);
+        total += (b + 255) / 256 * 256;
+    }
+    DeviceGuard g(m.device);
+    m.gemm_weights.alloc(total);
+    for (size_t i = 0; i < mats.size(); ++i) {
+        QMatrix& q = *mats[i];
+        q.gemm = gemm_view(q.type, q.rows, q.cols, m.gemm_weights.as<uint8_t>() + off[i]);
+        cuda_check(launch_gemm_repack(q.dev, q.gemm, m.stream), "gemm repack");
+    }
+    cuda_check(cudaStreamSynchronize(m.stream), "gemm repack");
+    m.gemm_ready = true;
+    return true;
+}
+
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
                    float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl) {
     const LayerWeights& L = m.layers[layer];

@@ -110,6 +110,115 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     *b.h_err.as<int>() = 0;
     cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
     host_pos.assign(batch, 0);
+    // a batch of sequences on one GPU runs its products on the tensor cores
+    const char* env = std::getenv("EVELYN_BATCH_GEMM");
+    if (batch > 1 && batch <= 32 && m->tp_size == 1 && !(env && env[0] == '0') && build_gemm_weights(*m)) {
+        use_gemm = true;
+        const uint64_t kmax = std::max<uint64_t>({c.dim, (uint64_t)m->lffn, qw});
+        b.gbx.alloc(gemm_x_bytes(32, (uint32_t)kmax));
+        b.gxinv.alloc(32 * 4);
+        uint64_t pmax = 0;
+        std::vector<const QMatrix*> mats = {&m->lm_head};
+        for (const auto& L : m->layers)
+            for (const QMatrix* q : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(q);
+        for (const QMatrix* q : mats)
+            pmax = std::max<uint64_t>(pmax, (uint64_t)gemm_ksplit(q->gemm, sms) * batch * q->gemm.mtiles * 128 * 4);
+        b.gpart.alloc(pmax);
+        b.gpart2.alloc(pmax);
+    }
+}
+
+void Decoder::gemm_stage(const float* x, uint32_t cols, uint32_t stride, const float* norm_w, bool pdl) {
+    GemmX g;
+    g.x = x;
+    g.nseq = b.batch;
+    g.cols = cols;
+    g.x_stride = stride;
+    g.norm_w = norm_w;
+    g.eps = model->cfg.eps;
+    g.bx = b.gbx.as<uint8_t>();
+    g.xinv = b.gxinv.as<float>();
+    cuda_check(launch_gemm_stage_x(g, stream, pdl), "stage x");
+    kernels += 1;
+}
+
+void Decoder::gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool pdl) {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, model->device);
+    GemmArgs a;
+    a.w = w.gemm;
+    a.bx = b.gbx.as<uint8_t>();
+    a.xinv = b.gxinv.as<float>();
+    a.nseq = b.batch;
+    a.ksplit = ksplit = gemm_ksplit(w.gemm, sms);
+    a.rows_pad = w.gemm.mtiles * 128;
+    a.part = part;
+    a.err = b.err.as<int>();
+    cuda_check(launch_qgemm(a, stream, pdl), "gemm");
+    kernels += 1;
+}
+
+void Decoder::gemm_reduce(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride, int epi,
+                          const float* part2, uint32_t ksplit2, bool pdl) {
+    GemmReduce r;
+    r.part = part;
+    r.ksplit = ksplit;
+    r.rows_pad = w.gemm.mtiles * 128;
+    r.part2 = part2;
+    r.ksplit2 = ksplit2;
+    r.rows_pad2 = r.rows_pad;
+    r.nseq = b.batch;
+    r.rows = w.rows;
+    r.y = y;
+    r.y_stride = y_stride;
+    r.epi = epi;
+    cuda_check(launch_gemm_reduce(r, stream, pdl), "gemm reduce");
+    kernels += 1;
+}
+
+// A step for 2..32 sequences on one GPU: every matrix is read once per step by the
+// tensor-core products (qgemm.cu); attention and the small kernels are the batched
+// ones of the single-sequence path.
+void Decoder::enqueue_batched(bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const uint32_t dim = (uint32_t)c.dim, hd = (uint32_t)c.head_dim;
+    const uint32_t qw = m.lheads * hd, kw = m.lkv_heads * hd, F = m.lffn;
+    float* x = b.x.as<float>();
+    float* p1 = b.gpart.as<float>();
+    float* p2 = b.gpart2.as<float>();
+    uint32_t k1 = 1, k2 = 1;
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        const LayerWeights& L = m.layers[li];
+        gemm_stage(x, dim, dim, L.attn_norm, pdl);
+        gemm_product(L.q, p1, k1, pdl);
+        gemm_reduce(L.q, p1, k1, b.q.as<float>(), qw, EPI_STORE, nullptr, 0, pdl);
+        gemm_product(L.k, p1, k1, pdl);
+        gemm_reduce(L.k, p1, k1, b.k.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
+        gemm_product(L.v, p1, k1, pdl);
+        gemm_reduce(L.v, p1, k1, b.v.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
+        cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
+        cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
+        kernels += 3;
+        gemm_stage(b.att.as<float>(), qw, qw, nullptr, pdl);
+        gemm_product(L.o, p1, k1, pdl);
+        gemm_reduce(L.o, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+        gemm_stage(x, dim, dim, L.ffn_norm, pdl);
+        gemm_product(L.gate, p1, k1, pdl);
+        gemm_product(L.up, p2, k2, pdl);
+        gemm_reduce(L.gate, p1, k1, b.h.as<float>(), F, EPI_SWIGLU, p2, k2, pdl);
+        gemm_stage(b.h.as<float>(), F, F, nullptr, pdl);
+        gemm_product(L.down, p1, k1, pdl);
+        gemm_reduce(L.down, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+    }
+    gemm_stage(x, dim, dim, m.out_norm, pdl);
+    gemm_product(m.lm_head, p1, k1, pdl);
+    gemm_reduce(m.lm_head, p1, k1, b.logits.as<float>(), (uint32_t)c.vocab, EPI_STORE, nullptr, 0, pdl);
+    cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, b.batch, b.amax_v.as<float>(),
+                             b.amax_i.as<int32_t>(), b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(),
+                             b.pos.as<int32_t>(), b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
+               "argmax");
+    kernels += 2;
 }
 
 MatvecArgs Decoder::qkv_args(uint32_t li) const {
@@ -326,6 +435,11 @@ void Decoder::enqueue_dense(bool pdl) {
                             pdl),
                "embed");
     kernels += 1;
+    if (use_gemm) {
+        enqueue_batched(pdl);
+        kernels_per_step = kernels;
+        return;
+    }
     if (step_k) {
         cuda_check(step_kernel_launch(step_k, stream), "step kernel");
         kernels += 1;

@@ -133,19 +133,28 @@ def test_failing_hook_falls_back_to_dense():
     assert s.fallbacks == 4
 
 
-def test_batch_matches_independent_sessions():
+@pytest.mark.parametrize("B,gemm", [(3, "1"), (32, "1"), (3, "0")])
+def test_batch_matches_independent_sessions(B, gemm, monkeypatch):
+    """A Batch step (tensor-core products for 2..32 sequences, or one matvec per
+    sequence with EVELYN_BATCH_GEMM=0) against independent sessions and the oracle."""
+    monkeypatch.setenv("EVELYN_BATCH_GEMM", gemm)
     spec = synth.tiny(seed=13)
     img = synth.build(spec)
     m = evl.Model.load_memory(img, device=0)
-    B = 3
+    r = orc.Model(img)
     batch = evl.Batch(m, B, max_ctx=64)
-    sessions = [evl.Session(m, max_ctx=64) for _ in range(B)]
+    sessions = [evl.Session(m, max_ctx=64) for _ in range(min(B, 4))]
+    oracles = [orc.Session(r) for _ in range(min(B, 2))]
     rng = np.random.default_rng(0)
+    worst = 0.0
     for _ in range(10):
         toks = rng.integers(0, spec.vocab, B)
         got = batch.step(toks)
-        for i in range(B):
-            assert np.abs(got[i] - sessions[i].step(int(toks[i]))).max() <= 1e-4
+        for i, s in enumerate(sessions):
+            assert np.abs(got[i] - s.step(int(toks[i]))).max() <= LOGIT_TOL
+        for i, o in enumerate(oracles):
+            worst = max(worst, float(np.abs(got[i] - o.step(int(toks[i]))).max()))
+    assert worst <= LOGIT_TOL, worst
 
 
 def test_model_level_apis_match_oracle():
