@@ -414,7 +414,7 @@ evl_status evl_qmatrix_matmul(evl_qmatrix* q, const float* d_x, uint32_t nvec, f
         const uint32_t ksplit = gemm_ksplit(q->gemm, sms), rows_pad = q->gemm.mtiles * 128;
         const uint64_t xb = gemm_x_bytes(32, m.cols), pb = (uint64_t)ksplit * 32 * rows_pad * 4;
         if (q->bx.bytes < xb) q->bx.alloc(xb);
-        if (q->xinv.bytes < 128) q->xinv.alloc(128);
+        if (q->xinv.bytes < 3 * 128) q->xinv.alloc(3 * 128);  // xinv[32] | stats[32][2]
         if (q->part.bytes < pb) q->part.alloc(pb);
         GemmX gx;
         gx.x = d_x;
@@ -423,6 +423,7 @@ evl_status evl_qmatrix_matmul(evl_qmatrix* q, const float* d_x, uint32_t nvec, f
         gx.x_stride = m.cols;
         gx.bx = q->bx.as<uint8_t>();
         gx.xinv = q->xinv.as<float>();
+        gx.stats = q->xinv.as<float>() + 32;
         cuda_check(launch_gemm_stage_x(gx, s, false), "stage x");
         GemmArgs ga;
         ga.w = q->gemm;

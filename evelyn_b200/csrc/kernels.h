@@ -135,6 +135,7 @@ struct GemmX {
     float eps = 1e-6f;
     uint8_t* bx = nullptr;
     float* xinv = nullptr;          // [nseq]
+    float* stats = nullptr;         // [nseq][2] scratch: RMS scale, 2^e
 };
 uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols);
 cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl);

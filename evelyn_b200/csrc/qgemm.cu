@@ -47,10 +47,14 @@ constexpr uint32_t kMT = 128;          // rows per M tile (TMEM lanes)
 constexpr uint32_t kChunk = 256;       // values per K chunk
 constexpr uint32_t kGemmThreads = 320; // producer, MMA, 8 math warps
 constexpr uint32_t kMathWarps = 8;
-constexpr uint32_t kStages = 3;
-constexpr uint32_t kASlots = 4;        // A operand slots in TMEM, 32 columns each
+constexpr uint32_t kMaxStages = 4;     // weight + x stages in shared memory (as many as fit)
+constexpr uint32_t kASlots = 7;        // A operand slots in TMEM, 32 columns each
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColA = 0, kColMin = 128, kColD = 256;  // TMEM column map; D slots 2 x 128
+// TMEM column map: A slots [0, 224), min-term A 2 x 8 [224, 240), accumulator slots
+// 4 x 64 [256, 512) (per slot: the product at +0, the Q4_K min term at +32)
+constexpr uint32_t kColA = 0, kColMin = 224, kColD = 256;
+constexpr uint32_t kDSlots = 4, kDCols = 64;
+constexpr uint32_t kLag = 2;  // accumulator spans between an MMA and its read-back
 
 __host__ __device__ inline uint32_t gemm_block_bytes(uint32_t type) {
     switch (type) {
@@ -223,19 +227,25 @@ __global__ void gemm_repack_kernel(const QMatDev src, QGemmDev dst) {
 }
 
 // ------------------------------------------------------------------ x staging
-// CTA s (< nsp): sequence s's x (normalised when norm_w) -> hi/lo f16 B rows s and
-// nsp + s of every chunk, the Q4_K min-term sums, and xinv[s] = 2^-e. Sequences
-// >= nseq are zero rows.
-__global__ void gemm_stage_x_kernel(const GemmX a) {
-    const uint32_t s = blockIdx.x, K = a.cols, nsp = a.nsp, N = 2 * nsp;
-    const uint32_t tid = threadIdx.x, nt = blockDim.x;
+// Two launches: per sequence (CTA s < nsp) the RMS scale and the power of two that
+// brings max|x| just under 2^14 (stats[2s] = inv, stats[2s+1] = 2^e, xinv[s] = 2^-e);
+// then one CTA per (sequence, K chunk) writes that chunk's hi/lo f16 B rows s and
+// nsp + s and the Q4_K min-term sums. Sequences >= nseq are zero rows.
+__device__ __forceinline__ float staged_val(const GemmX& a, const float* x, uint32_t i, float inv) {
+    float v = x[i];
+    if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
+    return v;
+}
+
+__global__ void gemm_stage_stats_kernel(const GemmX a) {
+    const uint32_t s = blockIdx.x, K = a.cols, tid = threadIdx.x, nt = blockDim.x;
     __shared__ float red[32];
-    __shared__ float sh_inv, sh_up;
-    const bool live = s < a.nseq;
-    const float* x = a.x + (uint64_t)s * a.x_stride;
+    __shared__ float sh_inv;
     pdl_wait();
+    if (s >= a.nseq) return;
+    const float* x = a.x + (uint64_t)s * a.x_stride;
     float inv = 1.f;
-    if (live && a.norm_w) {
+    if (a.norm_w) {
         float ss = 0.f;
         for (uint32_t i = tid; i < K; i += nt) ss += x[i] * x[i];
         ss = warp_sum(ss);
@@ -249,14 +259,8 @@ __global__ void gemm_stage_x_kernel(const GemmX a) {
         __syncthreads();
         inv = sh_inv;
     }
-    auto val = [&](uint32_t i) {
-        float v = x[i];
-        if (a.norm_w) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
-        return v;
-    };
     float mx = 0.f;
-    if (live)
-        for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(val(i)));
+    for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(staged_val(a, x, i, inv)));
     mx = warp_max(mx);
     __syncthreads();
     if ((tid & 31) == 0) red[tid >> 5] = mx;
@@ -267,45 +271,48 @@ __global__ void gemm_stage_x_kernel(const GemmX a) {
         int e = 0;
         if (t > 0.f) frexpf(t, &e);  // t in [2^(e-1), 2^e)
         const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
-        sh_up = ldexpf(1.0f, sc);
-        if (live) a.xinv[s] = ldexpf(1.0f, -sc);
+        a.stats[2 * s] = inv;
+        a.stats[2 * s + 1] = ldexpf(1.0f, sc);
+        a.xinv[s] = ldexpf(1.0f, -sc);
     }
-    __syncthreads();
-    const float up = sh_up;
-    const uint32_t nchunks = K / kChunk, cb = gemm_xchunk_bytes(nsp);
-    for (uint32_t i = tid; i < K; i += nt) {
-        const float v = live ? __fmul_rn(val(i), up) : 0.f;
-        const __half hi = __float2half_rn(v);
-        const __half lo = __float2half_rn(v - __half2float(hi));
-        const uint32_t c = i / kChunk, k = i % kChunk;
-        uint8_t* base = a.bx + (uint64_t)c * cb + (k / 16) * (N * 32u);
-        const uint32_t sl = kslot(k % 16);
-        *reinterpret_cast<__half*>(base + bt_off(s, sl)) = hi;
-        *reinterpret_cast<__half*>(base + bt_off(nsp + s, sl)) = lo;
+}
+
+// grid (nsp, K / 256), 256 threads: thread k stages value k of the chunk
+__global__ void gemm_stage_x_kernel(const GemmX a) {
+    const uint32_t s = blockIdx.x, c = blockIdx.y, k = threadIdx.x, nsp = a.nsp, N = 2 * nsp;
+    pdl_wait();
+    const bool live = s < a.nseq;
+    float v = 0.f;
+    if (live) {
+        const float* x = a.x + (uint64_t)s * a.x_stride;
+        v = __fmul_rn(staged_val(a, x, c * kChunk + k, a.stats[2 * s]), a.stats[2 * s + 1]);
     }
-    // per 32-value sub-block sums, scaled by 2^-5 to stay inside f16, into the min tile
-    for (uint32_t j = tid; j < K / 32; j += nt) {
-        float sm = 0.f;
-        if (live)
-            for (uint32_t e = 0; e < 32; ++e) sm += __fmul_rn(val(32 * j + e), up);
-        sm *= 0.03125f;
-        const __half hi = __float2half_rn(sm);
-        const __half lo = __float2half_rn(sm - __half2float(hi));
-        const uint32_t c = j / 8, sb = j % 8;
-        uint8_t* base = a.bx + (uint64_t)c * cb + 16 * (N * 32u);
-        *reinterpret_cast<__half*>(base + bt_off(s, kslot(sb))) = hi;
-        *reinterpret_cast<__half*>(base + bt_off(nsp + s, kslot(sb))) = lo;
-        *reinterpret_cast<__half*>(base + bt_off(s, kslot(8 + sb))) = __float2half_rn(0.f);
-        *reinterpret_cast<__half*>(base + bt_off(nsp + s, kslot(8 + sb))) = __float2half_rn(0.f);
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    uint8_t* chunk = a.bx + (uint64_t)c * gemm_xchunk_bytes(nsp);
+    uint8_t* tile = chunk + (k / 16) * (N * 32u);
+    const uint32_t sl = kslot(k % 16);
+    *reinterpret_cast<__half*>(tile + bt_off(s, sl)) = hi;
+    *reinterpret_cast<__half*>(tile + bt_off(nsp + s, sl)) = lo;
+    // per 32-value sub-block sums (warp w = sub-block w), scaled by 2^-5 to stay inside f16
+    const float sm = warp_sum(v) * 0.03125f;
+    if ((k & 31) == 0) {
+        const uint32_t sb = k / 32;
+        uint8_t* mt = chunk + 16 * (N * 32u);
+        const __half mhi = __float2half_rn(sm);
+        const __half mlo = __float2half_rn(sm - __half2float(mhi));
+        *reinterpret_cast<__half*>(mt + bt_off(s, kslot(sb))) = mhi;
+        *reinterpret_cast<__half*>(mt + bt_off(nsp + s, kslot(sb))) = mlo;
+        *reinterpret_cast<__half*>(mt + bt_off(s, kslot(8 + sb))) = __float2half_rn(0.f);
+        *reinterpret_cast<__half*>(mt + bt_off(nsp + s, kslot(8 + sb))) = __float2half_rn(0.f);
     }
-    (void)nchunks;
     pdl_launch_dependents();
 }
 
 // ------------------------------------------------------------------ the GEMM
 struct GemmPlan {
     GemmArgs a;
-    uint32_t nsp, N, ksplit, items, xchunk;
+    uint32_t nsp, N, ksplit, items, xchunk, stages;
     uint32_t sub_per_chunk;  // A slots per chunk: Q4_K 4 (64 values), Q6_K 8 (32 x 2 planes), Q8_0 8
     uint32_t eu_per_chunk;   // accumulator spans per chunk: Q4_K, Q6_K 1; Q8_0 8
 };
@@ -332,19 +339,21 @@ __device__ __forceinline__ void item_range(const GemmPlan& P, uint32_t item, uin
     c1 = (uint32_t)(((uint64_t)nch * (kr + 1)) / P.ksplit);
 }
 
+// T is the weight type: the sub-chunk loops unroll and the per-chunk scales stay in registers.
+template <uint32_t T>
 __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_constant__ GemmPlan P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t st_full[kStages], st_empty[kStages];
+    __shared__ __align__(8) uint64_t st_full[kMaxStages], st_empty[kMaxStages];
     __shared__ __align__(8) uint64_t a_full[kASlots], a_empty[kASlots];
     __shared__ __align__(8) uint64_t m_full[2], m_empty[2];
-    __shared__ __align__(8) uint64_t d_full[2], d_empty[2];
+    __shared__ __align__(8) uint64_t d_full[kDSlots], d_empty[kDSlots];
     __shared__ __align__(8) uint64_t fin_bar;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const GemmArgs& A = P.a;
-    const uint32_t T = A.w.type, wbytes = A.w.block_bytes, stage_bytes = wbytes + P.xchunk;
-    const uint32_t SP = P.sub_per_chunk;
+    const uint32_t wbytes = A.w.block_bytes, stage_bytes = wbytes + P.xchunk, kStages = P.stages;
+    constexpr uint32_t SP = T == GGML_Q4_K ? 4 : 8;  // A slots per chunk
     const uint32_t item0 = (uint32_t)(((uint64_t)P.items * blockIdx.x) / gridDim.x);
     const uint32_t item1 = (uint32_t)(((uint64_t)P.items * (blockIdx.x + 1)) / gridDim.x);
 
@@ -361,6 +370,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         for (uint32_t i = 0; i < 2; ++i) {
             mbar_init(&m_full[i], 4);
             mbar_init(&m_empty[i], 1);
+        }
+        for (uint32_t i = 0; i < kDSlots; ++i) {
             mbar_init(&d_full[i], 1);
             mbar_init(&d_empty[i], kMathWarps);
         }
@@ -375,6 +386,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
     __syncthreads();
     tc_after();
     const uint32_t tm = tmem_base;
+    pdl_wait();  // the staged x (and xinv) come from the previous launch
 
     if (warp == 0) {
         // ---------------------------------------------------------------- producer
@@ -399,7 +411,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = mma_idesc(P.N);
+            const uint32_t idesc = mma_idesc(P.nsp);  // hi and lo parts are two MMAs of N = nsp
             uint32_t n = 0, g = 0, e = 0, mc = 0;
             bool ok = true;
             for (uint32_t it = item0; it < item1 && ok; ++it) {
@@ -409,25 +421,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     const uint32_t s = n % kStages;
                     if (!bwait(&st_full[s], (n / kStages) & 1, &abort_flag)) { ok = false; break; }
                     const uint8_t* bx = smem + s * stage_bytes + wbytes;
-                    const uint32_t tile_b = P.N * 32;
+                    const uint32_t tile_b = P.N * 32, lo_b = (P.nsp / 8) * 256;  // lo rows start at nsp
+#pragma unroll
                     for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
                         const uint32_t as = g % kASlots;
                         const uint32_t eu_first = (T == GGML_Q8_0) || q == 0;
-                        const uint32_t ds = e % 2;
-                        if (eu_first && e >= 2 && !bwait(&d_empty[ds], ((e / 2) - 1) & 1, &abort_flag)) { ok = false; break; }
+                        const uint32_t ds = e % kDSlots;
+                        if (eu_first && e >= kDSlots &&
+                            !bwait(&d_empty[ds], ((e / kDSlots) - 1) & 1, &abort_flag)) { ok = false; break; }
                         if (!bwait(&a_full[as], (g / kASlots) & 1, &abort_flag)) { ok = false; break; }
                         tc_after();
-                        const uint32_t acol = tm + kColA + as * 32, dcol = tm + kColD + ds * 128;
+                        const uint32_t acol = tm + kColA + as * 32, dcol = tm + kColD + ds * kDCols;
+                        // A columns 8i..8i+7 against B tile `bt`, its hi rows then its lo rows
+                        auto mma2 = [&](uint32_t i, uint32_t bt, bool first) {
+                            mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + bt * tile_b), idesc, !first);
+                            mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + bt * tile_b + lo_b), idesc, 1);
+                        };
                         if (T == GGML_Q4_K) {  // 64 values: B tiles 4q..4q+3
-                            for (uint32_t i = 0; i < 4; ++i)
-                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (4 * q + i) * tile_b), idesc, (q | i) != 0);
+                            for (uint32_t i = 0; i < 4; ++i) mma2(i, 4 * q + i, (q | i) == 0);
                         } else if (T == GGML_Q6_K) {  // 32 values x two planes: B tiles 2q, 2q+1
-                            for (uint32_t i = 0; i < 4; ++i)
-                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (2 * q + (i & 1)) * tile_b), idesc,
-                                           (q | i) != 0);
+                            for (uint32_t i = 0; i < 4; ++i) mma2(i, 2 * q + (i & 1), (q | i) == 0);
                         } else {  // Q8_0 block q: B tiles 2q, 2q+1
-                            for (uint32_t i = 0; i < 2; ++i)
-                                mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + (2 * q + i) * tile_b), idesc, i != 0);
+                            for (uint32_t i = 0; i < 2; ++i) mma2(i, 2 * q + i, i == 0);
                         }
                         mma_commit(&a_empty[as]);
                         const bool eu_last = (T == GGML_Q8_0) || q + 1 == SP;
@@ -436,7 +451,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                                 const uint32_t ms = mc % 2;
                                 if (!bwait(&m_full[ms], (mc / 2) & 1, &abort_flag)) { ok = false; break; }
                                 tc_after();
-                                mma_tmem_a(dcol + 64, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b), idesc, 0);
+                                mma_tmem_a(dcol + 32, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b), idesc, 0);
+                                mma_tmem_a(dcol + 32, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b + lo_b), idesc, 1);
                                 mma_commit(&m_empty[ms]);
                                 ++mc;
                             }
@@ -465,19 +481,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         uint32_t n = 0, g = 0, e = 0, mc = 0;
         bool ok = true;
         // scales of the accumulator spans not yet read back (two in flight)
-        float eu_d[2] = {0.f, 0.f}, eu_dmin[2] = {0.f, 0.f};
+        float eu_d[kDSlots] = {0.f, 0.f, 0.f, 0.f}, eu_dmin[kDSlots] = {0.f, 0.f, 0.f, 0.f};
         auto epilogue = [&](uint32_t eu) -> bool {  // read span eu back and scale it into acc
-            const uint32_t ds = eu % 2;
-            if (!bwait(&d_full[ds], (eu / 2) & 1, &abort_flag)) return false;
+            const uint32_t ds = eu % kDSlots;
+            if (!bwait(&d_full[ds], (eu / kDSlots) & 1, &abort_flag)) return false;
             tc_after();
-            uint32_t hi[16], lo[16], mh[16], ml[16];
-            const uint32_t dcol = tm + lane_addr + kColD + ds * 128 + grp * half;
-            tmem_ld16(dcol, hi);
-            tmem_ld16(dcol + P.nsp, lo);
-            if (T == GGML_Q4_K) {
-                tmem_ld16(dcol + 64, mh);
-                tmem_ld16(dcol + 64 + P.nsp, ml);
-            }
+            uint32_t dv[16], mv[16];
+            const uint32_t dcol = tm + lane_addr + kColD + ds * kDCols + grp * half;
+            tmem_ld16(dcol, dv);
+            if (T == GGML_Q4_K) tmem_ld16(dcol + 32, mv);
             tmem_ld_wait();
             tc_before();
             __syncwarp();
@@ -485,9 +497,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
             const float d = eu_d[ds], dm = eu_dmin[ds];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const float v = __uint_as_float(hi[i]) + __uint_as_float(lo[i]);
-                acc[i] = fmaf(d, v, acc[i]);
-                if (T == GGML_Q4_K) acc[i] = fmaf(-dm * 32.f, __uint_as_float(mh[i]) + __uint_as_float(ml[i]), acc[i]);
+                acc[i] = fmaf(d, __uint_as_float(dv[i]), acc[i]);
+                if (T == GGML_Q4_K) acc[i] = fmaf(-dm * 32.f, __uint_as_float(mv[i]), acc[i]);
             }
             return true;
         };
@@ -523,6 +534,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                         q8_d[2 * j + 1] = f16_exact(w4[j] >> 16);
                     }
                 }
+#pragma unroll
                 for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
                     if ((g & 1) == grp) {  // this group dequantises sub-chunk g
                         const uint32_t as = g % kASlots;
@@ -612,7 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     }
                     const bool eu_last = (T == GGML_Q8_0) || q + 1 == SP;
                     if (eu_last) {
-                        const uint32_t ds = e % 2;
+                        const uint32_t ds = e % kDSlots;
                         eu_d[ds] = (T == GGML_Q8_0) ? q8_d[q] : d;
                         eu_dmin[ds] = dmin;
                         if (T == GGML_Q4_K && grp == 0) {  // the chunk's mins: A of the min-term MMA
@@ -633,7 +645,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                         }
                         if (T == GGML_Q4_K) ++mc;
                         // read back the previous span (one span of lag keeps the MMAs busy)
-                        if (e > first_eu && !epilogue(e - 1)) { ok = false; break; }
+                        if (e >= first_eu + kLag && !epilogue(e - kLag)) { ok = false; break; }
                         ++e;
                     }
                 }
@@ -641,7 +653,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                 if (lane == 0) mbar_arrive(&st_empty[s]);  // done with this stage's weights
             }
             if (!ok) break;
-            if (e > first_eu && !epilogue(e - 1)) { ok = false; break; }
+            for (uint32_t k = kLag; k >= 1 && ok; --k)  // drain the spans still in flight
+                if (e >= first_eu + k && !epilogue(e - k)) ok = false;
+            if (!ok) break;
             // partial sums of this item: part[kr][seq][row]
             const uint32_t row = mt * kMT + t;
             for (uint32_t i = 0; i < half; ++i) {
@@ -722,16 +736,19 @@ cudaError_t launch_gemm_repack(const QMatDev& src, const QGemmDev& dst, cudaStre
 }
 
 uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols) {
-    const uint32_t nsp = (nseq + 7) / 8 * 8;
+    const uint32_t nsp = (nseq + 15) / 16 * 16;
     return (uint64_t)(cols / kChunk) * gemm_xchunk_bytes(nsp);
 }
 
 cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl) {
-    if (!a.nseq || a.nseq > 32 || a.cols % kChunk || !a.x || !a.bx || !a.xinv) return cudaErrorInvalidValue;
-    a.nsp = (a.nseq + 7) / 8 * 8;
+    if (!a.nseq || a.nseq > 32 || a.cols % kChunk || !a.x || !a.bx || !a.xinv || !a.stats) return cudaErrorInvalidValue;
+    a.nsp = (a.nseq + 15) / 16 * 16;  // the MMA's N (M = 128 needs a multiple of 16)
     cudaLaunchAttribute at[1];
-    auto cfg = cfg_of(dim3(a.nsp), dim3(256), 0, s, pdl, at);
-    return cudaLaunchKernelEx(&cfg, gemm_stage_x_kernel, a);
+    auto cfg = cfg_of(dim3(a.nseq), dim3(256), 0, s, pdl, at);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_stage_stats_kernel, a);
+    if (e != cudaSuccess) return e;
+    auto cfg2 = cfg_of(dim3(a.nsp, a.cols / kChunk), dim3(kChunk), 0, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg2, gemm_stage_x_kernel, a);
 }
 
 uint32_t gemm_ksplit(const QGemmDev& w, int sms) {
@@ -742,9 +759,11 @@ uint32_t gemm_ksplit(const QGemmDev& w, int sms) {
 cudaError_t launch_qgemm(const GemmArgs& a, cudaStream_t s, bool pdl) {
     if (!a.w.q || !a.bx || !a.part || !a.xinv || !a.nseq || a.nseq > 32 || !a.ksplit) return cudaErrorInvalidValue;
     if (a.w.type != GGML_Q4_K && a.w.type != GGML_Q6_K && a.w.type != GGML_Q8_0) return cudaErrorInvalidValue;
+    auto kernel = a.w.type == GGML_Q4_K ? qgemm_kernel<GGML_Q4_K>
+                  : a.w.type == GGML_Q6_K ? qgemm_kernel<GGML_Q6_K> : qgemm_kernel<GGML_Q8_0>;
     GemmPlan P{};
     P.a = a;
-    P.nsp = (a.nseq + 7) / 8 * 8;
+    P.nsp = (a.nseq + 15) / 16 * 16;
     P.N = 2 * P.nsp;
     P.ksplit = a.ksplit;
     P.items = a.w.mtiles * a.ksplit;
@@ -756,16 +775,21 @@ cudaError_t launch_qgemm(const GemmArgs& a, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     // at least 116 KB so that no two CTAs share an SM: each allocates all 512 TMEM columns
-    const size_t smem = std::max<size_t>(kStages * (size_t)(a.w.block_bytes + P.xchunk), 116 * 1024);
+    const uint32_t stage_bytes = a.w.block_bytes + P.xchunk;
+    P.stages = std::min<uint32_t>(kMaxStages, (225u * 1024) / stage_bytes);
+    if (P.stages < 2) return cudaErrorInvalidValue;
+    // at least 116 KB so that no two CTAs share an SM: each allocates all 512 TMEM columns
+    const size_t smem = std::max<size_t>((size_t)P.stages * stage_bytes, 116 * 1024);
     if (dev >= 0 && dev < 64 && !g_gemm_attr[dev]) {
-        e = cudaFuncSetAttribute(qgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
-        if (e != cudaSuccess) return e;
+        for (auto k : {qgemm_kernel<GGML_Q4_K>, qgemm_kernel<GGML_Q6_K>, qgemm_kernel<GGML_Q8_0>}) {
+            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+            if (e != cudaSuccess) return e;
+        }
         g_gemm_attr[dev] = 1;
     }
-    if (smem > 225 * 1024) return cudaErrorInvalidValue;
     cudaLaunchAttribute at[1];
     auto cfg = cfg_of(dim3(std::min<uint32_t>(P.items, (uint32_t)sms)), dim3(kGemmThreads), smem, s, pdl, at);
-    return cudaLaunchKernelEx(&cfg, qgemm_kernel, P);
+    return cudaLaunchKernelEx(&cfg, kernel, P);
 }
 
 cudaError_t launch_gemm_reduce(const GemmReduce& a, cudaStream_t s, bool pdl) {

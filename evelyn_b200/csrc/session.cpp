@@ -95,8 +95,12 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     // enough (kv_head, split) CTAs to cover the SMs twice
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+    // splits per (kv head, sequence): enough CTAs to cover the SMs twice; a batch keeps
+    // at least 32 pages (512 positions) of each sequence per split so long contexts
+    // still spread over many CTAs
     const uint32_t want = (uint32_t)(2 * sms) / std::max<uint32_t>(1, m->lkv_heads * batch);
-    b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>(want, 1), b.pages_per_seq));
+    const uint32_t by_len = batch > 1 ? (b.pages_per_seq + 31) / 32 : 1;
+    b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
     b.amax_parts = (uint32_t)sms;
     b.amax_v.alloc((uint64_t)batch * b.amax_parts * 4);
@@ -116,7 +120,7 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
         use_gemm = true;
         const uint64_t kmax = std::max<uint64_t>({c.dim, (uint64_t)m->lffn, qw});
         b.gbx.alloc(gemm_x_bytes(32, (uint32_t)kmax));
-        b.gxinv.alloc(32 * 4);
+        b.gxinv.alloc(3 * 32 * 4);  // xinv[32] | stats[32][2]
         uint64_t pmax = 0;
         std::vector<const QMatrix*> mats = {&m->lm_head};
         for (const auto& L : m->layers)
@@ -138,8 +142,9 @@ void Decoder::gemm_stage(const float* x, uint32_t cols, uint32_t stride, const f
     g.eps = model->cfg.eps;
     g.bx = b.gbx.as<uint8_t>();
     g.xinv = b.gxinv.as<float>();
+    g.stats = b.gxinv.as<float>() + 32;
     cuda_check(launch_gemm_stage_x(g, stream, pdl), "stage x");
-    kernels += 1;
+    kernels += 2;
 }
 
 void Decoder::gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool pdl) {
