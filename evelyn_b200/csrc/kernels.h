@@ -95,6 +95,10 @@ struct AttnArgs {
     int* err = nullptr;            // device error flag (DeviceError)
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+// Single sequence: QK-norm + RoPE + append, split-K attention and the split merge in one
+// launch (step_kernel.cu); kv_done is [kv_heads] zeroed counters, left zeroed.
+cudaError_t launch_attention_fused(const RopeArgs& r, const AttnArgs& a, unsigned int* kv_done, cudaStream_t s,
+                                   bool pdl);
 
 // ---------------------------------------------------------------- step_kernel.cu
 // One decoder layer of a single-sequence step, as the separate launches would run it:

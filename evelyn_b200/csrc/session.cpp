@@ -102,6 +102,16 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     const uint32_t by_len = batch > 1 ? (b.pages_per_seq + 31) / 32 : 1;
     b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
+    {  // one sequence: attention with QK-norm/RoPE/append and the merge in one launch
+        const char* fe = std::getenv("EVELYN_FUSED_ATTN");
+        if (batch == 1 && !(fe && fe[0] == '0')) {
+            b.nsplit_fused = std::max<uint32_t>(
+                1, std::min<uint32_t>((uint32_t)sms / std::max<uint32_t>(1, m->lkv_heads), b.pages_per_seq));
+            b.nsplit_fused = std::min(b.nsplit_fused, b.nsplit);
+            b.kvdone.alloc(std::max<uint64_t>(4, (uint64_t)m->lkv_heads * 4));
+            cuda_check(cudaMemset(b.kvdone.p, 0, b.kvdone.bytes), "memset");
+        }
+    }
     b.amax_parts = (uint32_t)sms;
     b.amax_v.alloc((uint64_t)batch * b.amax_parts * 4);
     b.amax_i.alloc((uint64_t)batch * b.amax_parts * 4);
@@ -309,10 +319,17 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         matvec_each(qkv_args(li), B, c.dim, ys, stream, pdl, "qkv matvec");
         kernels += B;
     }
-    cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
-    kernels += 1;
-    cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
-    kernels += 2;
+    if (b.nsplit_fused) {
+        cuda_check(launch_attention_fused(rope_args(li), attn_args(li, b.nsplit_fused), b.kvdone.as<unsigned int>(),
+                                          stream, pdl),
+                   "attention");
+        kernels += 1;
+    } else {
+        cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
+        kernels += 1;
+        cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
+        kernels += 2;
+    }
     {  // o-proj, residual add fused (TP: partial sums, all-reduce, then add)
         const bool tp = m.tp_size > 1;
         MatvecArgs a;
@@ -546,6 +563,7 @@ void Decoder::check_device_error() {
     *b.h_err.as<int>() = 0;
     cudaMemsetAsync(b.err.p, 0, 4, stream);
     if (step_k) step_kernel_reset(step_k, stream);
+    if (b.kvdone.p) cudaMemsetAsync(b.kvdone.p, 0, b.kvdone.bytes, stream);
     cudaStreamSynchronize(stream);
     switch (e) {
         case DEV_ERR_TOKEN: raise(EVL_ERR_INVALID_INPUT, "token ID outside the model vocabulary");
