@@ -1,27 +1,33 @@
 // common.cuh -- device-side types shared by the decode kernels.
 //
-// Quantised weights live in HBM in a tiled repack of the GGUF blocks (the
-// reference keeps the raw GGUF bytes, src/runtime.rs:23-51). A unit is 64 values of
-// one row; a row is cut into tiles, each covering a group of up to 32 units (the last
-// group of a row may be shorter, U units). Rows are padded to a multiple of 16 and
-// stored as 16-row slabs: slab b holds, for each group g in turn, the 16 tiles
-// (b*16 + i, g), i = 0..15, back to back -- so one TMA bulk copy moves 16 rows of one
-// column group. A tile is self-contained and 16-byte aligned:
+// Quantised weights live in HBM in a repack of the GGUF blocks (the reference keeps
+// the raw GGUF bytes, src/runtime.rs:23-51) ordered for the matvec's warp-level
+// integer MMA (mma.sync m16n8k32, one 16-row x 32-value A tile per instruction). A
+// unit is 64 values of one row. Rows are padded to a multiple of 16 and stored as
+// 16-row slabs; a slab is cut into panels of up to 32 units (2048 values), panel g
+// holding units [32g, 32g + U) of the slab's 16 rows, so one TMA bulk copy moves one
+// panel. Inside a panel the bytes of the 16 rows are interleaved so that lane
+// L = 4*g8 + t of a warp (g8 = L/4, t = L%4; MMA rows g8 and g8 + 8) finds its A
+// fragments in one 16-byte word per load:
 //
-//   [payload: chunk-major, chunk c of unit u at c*U*16 + u*16 (16 B per chunk)]
-//   [aux: block scales, padded to 16 B] [d: Q6_K super-block scales, padded to 16 B]
-//
-//   Q4_K  unit = 32-byte qs group j of super-block i (values 256i+64j+[0,64)),
-//         2 chunks; aux = the 16-byte header (d, dmin, scales[12]) of each of the
-//         U/4 super-blocks.
-//   Q6_K  unit = (super-block i, half h, l0 in {0,16}) (values 256i+128h+32k+l0+[0,16),
-//         k=0..3): 3 chunks (ql[64h+l0..+16], ql[64h+32+l0..+16], qh[32h+l0..+16]);
-//         aux = u32 per unit with the 4 int8 scales sc[8h+l0/16+2k]; d = f16 per
-//         super-block.
-//   Q8_0  unit = two 32-value blocks: 4 chunks; aux = u32 per unit with the two
-//         f16 block scales.
-//   F16, BF16, F32: plain values, 8 (16) chunks per unit, no aux.
-// Q5_K has no device-matrix layout (it is read only through the raw dequantiser).
+//   Q4_K  per super-block (4 units, 2304 B): 4 qs groups j x 512 B, lane L at
+//         j*512 + 16L holding the qs words (bytes 4w..4w+3 of group j) w = t and
+//         w = 4 + t of rows g8 and g8 + 8 as [w=t row g8, w=t row g8+8, w=4+t row g8,
+//         w=4+t row g8+8]; then the 16-byte header (d, dmin, scales[12]) of each row.
+//   Q6_K  per super-block (3360 B): halves H = 0, 1 of 1536 B, lane L at H*1536 + 48L
+//         holding ql words at 64H + 16a + 4t (a = 0..3) and qh words at 32H + 16a + 4t
+//         (a = 0, 1) of rows g8 and g8 + 8 as
+//         [ql a0 g8, ql a1 g8, ql a0 g8+8, ql a1 g8+8 | ql a2 .., ql a3 .. | qh a0 g8,
+//          qh a1 g8, qh a0 g8+8, qh a1 g8+8]; then the 16 int8 scales of each row, then
+//         the f16 d of each row.
+//   Q8_0  per unit (two 32-value blocks A, B; 1088 B): halves h = 0, 1 of 512 B, lane L
+//         at h*512 + 16L holding the q words at bytes 16h + 4t of A row g8, A row g8+8,
+//         B row g8, B row g8+8; then the f16 scales (A, B) of each row.
+//   F16, BF16, F32: plain values, each row of the panel contiguous.
+// No byte is added or dropped: a slab of Q4_K / Q6_K / Q8_0 is exactly 16 rows of GGUF
+// blocks, and block_byte_address maps every GGUF byte to its place (4-byte payload
+// words stay contiguous). Q5_K has no device-matrix layout (it is read only through
+// the raw dequantiser).
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -37,75 +43,79 @@ struct QMatDev {
     uint32_t type = 0;
     uint32_t rows = 0, cols = 0;
     uint32_t nunits = 0;         // 64-value units per row
-    uint32_t row_bytes = 0;      // bytes of one row's tiles; a 16-row slab is 16 * row_bytes
+    uint32_t row_bytes = 0;      // bytes per row; a 16-row slab is 16 * row_bytes
     const uint8_t* q = nullptr;  // ceil(rows / 16) slabs
 };
 
 constexpr uint32_t kSlabRows = 16;
+constexpr uint32_t kPanelUnits = 32;
 
-__host__ __device__ inline uint32_t chunks_per_unit(uint32_t type) {
+// Bytes of one unit over the 16 rows of a slab.
+__host__ __device__ inline uint32_t unit16_bytes(uint32_t type) {
     switch (type) {
-        case GGML_Q4_K: return 2;
-        case GGML_Q6_K: return 3;
-        case GGML_Q8_0: return 4;
+        case GGML_Q4_K: return 576;   // 16 x 144 / 4
+        case GGML_Q6_K: return 840;   // 16 x 210 / 4
+        case GGML_Q8_0: return 1088;  // 16 x 2 x 34
         case GGML_F16:
-        case GGML_BF16: return 8;
-        case GGML_F32: return 16;
+        case GGML_BF16: return 2048;
+        case GGML_F32: return 4096;
         default: return 0;
     }
 }
-
-__host__ __device__ inline uint32_t pad16(uint32_t v) { return (v + 15u) & ~15u; }
-
-// Sections of one tile of U units.
-__host__ __device__ inline uint32_t tile_payload_bytes(uint32_t type, uint32_t U) {
-    return U * chunks_per_unit(type) * 16u;
-}
-__host__ __device__ inline uint32_t tile_aux_bytes(uint32_t type, uint32_t U) {
-    switch (type) {
-        case GGML_Q4_K: return (U / 4u) * 16u;
-        case GGML_Q6_K:
-        case GGML_Q8_0: return pad16(U * 4u);
-        default: return 0;
-    }
-}
-__host__ __device__ inline uint32_t tile_d_bytes(uint32_t type, uint32_t U) {
-    return type == GGML_Q6_K ? pad16((U / 4u) * 2u) : 0u;
-}
-__host__ __device__ inline uint32_t tile_bytes(uint32_t type, uint32_t U) {
-    return tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + tile_d_bytes(type, U);
-}
-// Units in group g of a row of `nunits` units.
+// Units in panel g of a row of `nunits` units.
 __host__ __device__ inline uint32_t group_units(uint32_t nunits, uint32_t g) {
-    const uint32_t rest = nunits - g * 32u;
-    return rest < 32u ? rest : 32u;
+    const uint32_t rest = nunits - g * kPanelUnits;
+    return rest < kPanelUnits ? rest : kPanelUnits;
 }
-__host__ __device__ inline uint32_t row_tile_bytes(uint32_t type, uint32_t nunits) {
-    return (nunits / 32u) * tile_bytes(type, 32u) + ((nunits % 32u) ? tile_bytes(type, nunits % 32u) : 0u);
+__host__ __device__ inline uint32_t slab_row_bytes(uint32_t type, uint32_t nunits) {
+    return nunits * unit16_bytes(type) / kSlabRows;
 }
-// Byte offset, inside a 16-row slab, of the 16 tiles of group g.
-__host__ __device__ inline uint32_t slab_group_offset(uint32_t type, uint32_t g) {
-    return g * kSlabRows * tile_bytes(type, 32u);
+// Byte offset, inside a slab, of panel g; and the panel's size.
+__host__ __device__ inline uint32_t panel_offset(uint32_t type, uint32_t g) {
+    return g * kPanelUnits * unit16_bytes(type);
 }
-// Byte offset of tile (r, g) from the start of the matrix.
-__host__ __device__ inline uint64_t tile_address(uint32_t type, uint32_t nunits, uint32_t row_bytes, uint32_t r,
-                                                 uint32_t g) {
-    return (uint64_t)(r / kSlabRows) * kSlabRows * row_bytes + slab_group_offset(type, g) +
-           (r % kSlabRows) * tile_bytes(type, group_units(nunits, g));
+__host__ __device__ inline uint32_t panel_bytes(uint32_t type, uint32_t U) { return U * unit16_bytes(type); }
+
+// Byte offset from the start of the matrix of byte `o` of GGUF block `b` of row r
+// (Q4_K / Q6_K: 256-value super-block, o < 144 / 210; Q8_0: 32-value block, o < 34).
+// Bytes o..o+3 of a payload word (o % 4 == 0 for Q4_K qs, Q6_K ql/qh; o % 4 == 2 for
+// Q8_0 q) are contiguous, as are the 16 header bytes of a Q4_K block and the 16
+// scales of a Q6_K block.
+__host__ __device__ inline uint64_t block_byte_address(const QMatDev& m, uint32_t r, uint32_t b, uint32_t o) {
+    const uint32_t T = m.type, r16 = r % kSlabRows, g8 = r16 & 7, hi = r16 >> 3;
+    const uint64_t slab = (uint64_t)(r / kSlabRows) * kSlabRows * m.row_bytes;
+    if (T == GGML_Q8_0) {
+        const uint32_t u = b >> 1, blk = b & 1;
+        const uint64_t base = slab + panel_offset(T, u / kPanelUnits) + (u % kPanelUnits) * 1088u;
+        if (o < 2) return base + 1024u + r16 * 4u + blk * 2u + o;
+        const uint32_t q = o - 2, h = q >> 4, t = (q >> 2) & 3;
+        return base + h * 512u + (g8 * 4u + t) * 16u + (blk * 2u + hi) * 4u + (q & 3u);
+    }
+    const uint32_t u = 4 * b;
+    const uint64_t base = slab + panel_offset(T, u / kPanelUnits) + ((u % kPanelUnits) / 4u) * 4u * unit16_bytes(T);
+    if (T == GGML_Q4_K) {
+        if (o < 16) return base + 2048u + r16 * 16u + o;
+        const uint32_t q = o - 16, j = q >> 5, w = (q >> 2) & 7, t = w & 3;
+        return base + j * 512u + (g8 * 4u + t) * 16u + ((w >> 2) * 2u + hi) * 4u + (q & 3u);
+    }
+    // Q6_K
+    if (o < 128) {
+        const uint32_t H = o >> 6, oo = o & 63, a = oo >> 4, t = (oo >> 2) & 3;
+        return base + H * 1536u + (g8 * 4u + t) * 48u + (a >> 1) * 16u + (hi * 2u + (a & 1)) * 4u + (oo & 3u);
+    }
+    if (o < 192) {
+        const uint32_t q = o - 128, H = q >> 5, oo = q & 31, a = oo >> 4, t = (oo >> 2) & 3;
+        return base + H * 1536u + (g8 * 4u + t) * 48u + 32u + (hi * 2u + a) * 4u + (oo & 3u);
+    }
+    if (o < 208) return base + 3072u + r16 * 16u + (o - 192);
+    return base + 3328u + r16 * 2u + (o - 208);
 }
-// Offsets inside one tile of unit u (u's group is u >> 5; lane = u & 31).
-__host__ __device__ inline uint32_t chunk_in_tile(uint32_t nunits, uint32_t u, uint32_t c) {
-    return c * group_units(nunits, u >> 5) * 16u + (u & 31u) * 16u;
-}
-// aux entry of unit u (Q6_K, Q8_0: u32 per unit; Q4_K: 16-byte header of u's super-block)
-__host__ __device__ inline uint32_t aux_in_tile(uint32_t type, uint32_t nunits, uint32_t u) {
-    const uint32_t base = tile_payload_bytes(type, group_units(nunits, u >> 5));
-    return type == GGML_Q4_K ? base + ((u & 31u) / 4u) * 16u : base + (u & 31u) * 4u;
-}
-// Q6_K f16 super-block scale of unit u
-__host__ __device__ inline uint32_t d_in_tile(uint32_t type, uint32_t nunits, uint32_t u) {
-    const uint32_t U = group_units(nunits, u >> 5);
-    return tile_payload_bytes(type, U) + tile_aux_bytes(type, U) + ((u & 31u) / 4u) * 2u;
+
+// Plain types: byte offset of value c of row r (element size eb).
+__host__ __device__ inline uint64_t plain_value_address(const QMatDev& m, uint32_t r, uint32_t c, uint32_t eb) {
+    const uint32_t u = c / 64, g = u / kPanelUnits, U = group_units(m.nunits, g);
+    return (uint64_t)(r / kSlabRows) * kSlabRows * m.row_bytes + panel_offset(m.type, g) +
+           (uint64_t)(r % kSlabRows) * U * 64u * eb + (uint64_t)(c - g * kPanelUnits * 64u) * eb;
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

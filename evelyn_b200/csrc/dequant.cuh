@@ -83,53 +83,46 @@ __device__ __forceinline__ float dq_raw_value(uint32_t type, const uint8_t* b, u
     }
 }
 
-// Value `c` of row `r` from the repacked layout (common.cuh).
+// Value `c` of row `r` from the repacked layout (common.cuh): the bytes of the
+// value's GGUF block are fetched through block_byte_address and fed to the same
+// arithmetic as the raw path.
 __device__ __forceinline__ float dq_repacked_value(const QMatDev& m, uint32_t r, uint32_t c) {
-    const uint32_t T = m.type, N = m.nunits;
-    const uint32_t u_of_c = (T == GGML_Q6_K) ? (c >> 8) * 4 + ((c & 255) >> 7) * 2 + ((c >> 4) & 1) : c >> 6;
-    const uint8_t* tile = m.q + tile_address(T, N, m.row_bytes, r, u_of_c >> 5);
+    const uint32_t T = m.type;
+    auto byte = [&](uint32_t b, uint32_t o) { return m.q[block_byte_address(m, r, b, o)]; };
     switch (T) {
         case GGML_Q4_K: {
-            uint32_t sb = c >> 8, e = c & 255, j = e >> 6, hi = (e >> 5) & 1, l = e & 31;
-            uint32_t u = sb * 4 + j;
-            uint8_t v = tile[chunk_in_tile(N, u, l >> 4) + (l & 15)];
-            const uint8_t* h = tile + aux_in_tile(T, N, u);
-            float d = f16_exact(ld_u16(h)), dmin = f16_exact(ld_u16(h + 2));
+            const uint32_t b = c >> 8, e = c & 255;
+            uint8_t blk[16];
+            for (uint32_t i = 0; i < 16; ++i) blk[i] = byte(b, i);
+            float d = f16_exact(ld_u16(blk)), dmin = f16_exact(ld_u16(blk + 2));
+            const uint32_t j = e >> 6, hi = (e >> 5) & 1, l = e & 31;
             float s, mm;
-            scale_min_bytes(2 * j + hi, h + 4, &s, &mm);
+            scale_min_bytes(2 * j + hi, blk + 4, &s, &mm);
+            const uint8_t v = byte(b, 16 + j * 32 + l);
             float q = (float)(hi ? (v >> 4) : (v & 0xf));
             return __fsub_rn(__fmul_rn(__fmul_rn(d, s), q), __fmul_rn(dmin, mm));
         }
         case GGML_Q6_K: {
-            uint32_t sb = c >> 8, e = c & 255, half = e >> 7, rr = e & 127, k = rr >> 5, l = rr & 31;
-            uint32_t u = sb * 4 + half * 2 + (l >> 4);
-            uint32_t li = l & 15;
-            uint8_t lo = tile[chunk_in_tile(N, u, k & 1) + li];
-            uint8_t qh = tile[chunk_in_tile(N, u, 2) + li];
-            uint32_t nib = (k >> 1) ? (lo >> 4) : (lo & 0xf);
-            int q = (int)(nib | (((qh >> (2 * k)) & 3) << 4)) - 32;
-            uint32_t scw = *reinterpret_cast<const uint32_t*>(tile + aux_in_tile(T, N, u));
-            float sc = (float)(int8_t)((scw >> (8 * k)) & 0xff);
-            float d = f16_exact(ld_u16(tile + d_in_tile(T, N, u)));
+            const uint32_t b = c >> 8, e = c & 255, half = e >> 7, rr = e & 127, k = rr >> 5, l = rr & 31;
+            const uint8_t lo = byte(b, 64 * half + ((k & 1) ? 32 : 0) + l);
+            const uint8_t qh = byte(b, 128 + 32 * half + l);
+            const uint32_t nib = (k >> 1) ? (lo >> 4) : (lo & 0xf);
+            const int q = (int)(nib | (((qh >> (2 * k)) & 3) << 4)) - 32;
+            const float sc = (float)(int8_t)byte(b, 192 + 8 * half + l / 16 + 2 * k);
+            const float d = f16_exact((uint32_t)byte(b, 208) | ((uint32_t)byte(b, 209) << 8));
             return __fmul_rn(__fmul_rn(d, sc), (float)q);
         }
         case GGML_Q8_0: {
-            uint32_t u = c >> 6, e = c & 63;
-            int8_t q = (int8_t)tile[chunk_in_tile(N, u, e >> 4) + (e & 15)];
-            uint32_t dw = *reinterpret_cast<const uint32_t*>(tile + aux_in_tile(T, N, u));
-            float d = f16_exact((e < 32) ? (dw & 0xffff) : (dw >> 16));
-            return __fmul_rn(d, (float)q);
+            const uint32_t b = c >> 5, e = c & 31;
+            const float d = f16_exact((uint32_t)byte(b, 0) | ((uint32_t)byte(b, 1) << 8));
+            return __fmul_rn(d, (float)(int8_t)byte(b, 2 + e));
         }
         case GGML_F16:
         case GGML_BF16: {
-            uint32_t u = c >> 6, e = c & 63;
-            uint32_t h = ld_u16(tile + chunk_in_tile(N, u, e >> 3) + (e & 7) * 2);
+            const uint32_t h = ld_u16(m.q + plain_value_address(m, r, c, 2));
             return T == GGML_F16 ? f16_exact(h) : __uint_as_float(h << 16);
         }
-        case GGML_F32: {
-            uint32_t u = c >> 6, e = c & 63;
-            return __uint_as_float(*(const uint32_t*)(tile + chunk_in_tile(N, u, e >> 2) + (e & 3) * 4));
-        }
+        case GGML_F32: return __uint_as_float(*(const uint32_t*)(m.q + plain_value_address(m, r, c, 4)));
         default: return 0.f;
     }
 }

@@ -8,24 +8,22 @@
 //
 // Shape of the kernel (one persistent CTA per SM, warp-specialised):
 //   * a producer warp streams the CTA's contiguous range of 32-row blocks, one
-//     32-unit column tile at a time, from HBM into a ring of shared-memory stages
-//     with TMA bulk copies (cp.async.bulk + mbarrier complete_tx). It needs nothing
-//     from the previous kernel, so it starts before griddepcontrol.wait and keeps the
-//     ring full across the kernel boundary; after its last copy it prefetches the
-//     next matrix's first tiles into L2;
+//     32-unit panel of both 16-row slabs at a time, from HBM into a ring of shared-
+//     memory stages with TMA bulk copies (cp.async.bulk + mbarrier complete_tx). It
+//     needs nothing from the previous kernel, so it starts before griddepcontrol.wait
+//     and keeps the ring full across the kernel boundary; after its last copy it
+//     prefetches the next matrix's first slabs into L2;
 //   * sixteen consumer warps stage the input vector once per CTA as 24-bit block
 //     fixed point -- per 32-value block x = 2^-s * m, |m| <= 2^22, m split into three
-//     signed 8-bit limbs -- then run the dot products on the raw quant bytes with
-//     integer dp4a (4 products per instruction), two rows per warp per stage, one
-//     64-value unit per lane. Block scales (d*s_j, dmin*m_j, Q6_K int8 scales, the
-//     2^-s of x) are applied in f32 once per 32 (Q4_K, Q8_0) or 16 (Q6_K) values.
-// The integer products are exact, so the only rounding against the reference's
-// f32 loop is the 2^-22-relative quantisation of x and the order of the f32 sums.
-//
-// Optional fused prologue: RMSNorm of the input (src/runtime.rs:193-196) in the
-// reference's v*inv*g order. Epilogues: store, residual add (src/runtime.rs:798-804),
-// and SwiGLU silu(g)*u over paired gate/up rows (src/runtime.rs:409-418,
-// src/activation.rs:50).
+//     signed 8-bit limbs -- laid out as the B fragments of mma.sync m16n8k32. Consumer
+//     warp (slab, k) of a stage takes the 16 rows of one slab over one super-block (4
+//     units) and runs the dot products on the tensor cores: A = the raw quant bytes of
+//     16 rows (Q4_K nibbles masked in place, Q6_K 6-bit values, Q8_0 int8), B = the
+//     limbs of x; each k32 step holds 16 values of two sub-blocks, B columns 0-2 the
+//     limbs of the first and 4-6 those of the second, so every lane of a quad ends with
+//     one sub-block's limb sums of rows g and g+8. Block scales (d*s_j, dmin*m_j, Q6_K
+//     int8 scales, the 2^-s of x) are applied to those exact integer sums in f32; the
+//     eight warps of a slab meet in shared memory at the end of each row block.
 #pragma once
 #include <algorithm>
 
@@ -39,26 +37,27 @@ namespace {
 
 constexpr int kCW = 16;               // consumer warps
 constexpr int kThreads = 32 * (kCW + 1);
-constexpr int kNR = 2;                 // row slots per consumer warp
-constexpr int kRB = kCW * kNR;         // 32 row slots per stage
-constexpr int kLimbStride = 208;       // bytes of limbs per unit: 3 x 64 + 16 pad (bank spread)
+constexpr int kRB = 2 * kSlabRows;     // rows per row block (two slabs)
+constexpr int kSbWarps = kCW / 2;      // consumer warps per slab of a stage
+constexpr int kXUnit = 192;            // staged B-fragment bytes of one unit
 constexpr int kMaxStages = 8;
 constexpr uint32_t kSmemBudget = 225 * 1024;
 constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the consumer threads
-static_assert(kRB == 2 * kSlabRows && kNR % 2 == 0, "a stage is two 16-row slabs; SwiGLU pairs split kNR");
+constexpr uint32_t kRedBytes = 2 * kSbWarps * kRB * 4;  // double-buffered row-block partials
+static_assert(kSbWarps * 4 == kPanelUnits, "each consumer warp of a slab takes one super-block of a panel");
 
 // need bits
-constexpr uint32_t NEED_NAT = 1, NEED_Q6 = 2, NEED_XSUM = 4, NEED_MSUM = 8;
+constexpr uint32_t NEED_XSUM = 1, NEED_MSUM = 2;
 
 // One matvec launch (or one phase of the step kernel), prepared on the host.
 struct Plan {
     MatvecArgs a;
     uint32_t rb_begin[kMaxSegs + 1];  // first row-block of each segment (+ total)
     uint32_t nunits, ngroups;
-    uint32_t item_bytes;  // largest stage (32 rows x one 32-unit group) of any segment
+    uint32_t item_bytes;  // largest stage (two slabs x one 32-unit panel) of any segment
     uint32_t need;
-    uint32_t off_nat, off_q6, off_fscale, off_xsum, off_msum;  // offsets in the staged-input area
-    uint32_t xbytes;                                           // size of the staged-input area
+    uint32_t off_fscale, off_xsum, off_msum, off_red;  // offsets in the staged-input area (B fragments at 0)
+    uint32_t xbytes;                                   // size of the staged-input area
     const uint8_t* pf_base;  // next matrix to prefetch into L2 (optional)
     uint32_t pf_row_bytes, pf_rows;
     int* err;
@@ -99,179 +98,179 @@ __device__ __forceinline__ int seg_of(const Plan& p, uint32_t rb) {
 }
 
 
-// ---------------------------------------------------------------- per-unit dot products
-// Each returns, per row slot, the f32 contribution of one 64-value unit.
+// ---------------------------------------------------------------- MMA dot products
+// D (16 x 8, s32) += A (16 x 32, u8 / s8, row) * B (32 x 8, s8, col): rows g8, g8+8 of
+// A in a0/a2 (k < 16) and a1/a3 (k >= 16); B k 4t..4t+3 in b0, 16+4t.. in b1, column g8.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
-// Q4_K: low nibbles of the 32 qs bytes are values 0..31 of the unit (sub-block A),
-// high nibbles values 32..63 (sub-block B).
-__device__ __forceinline__ void unit_q4k(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
-                                         const uint8_t* limbs, const float* fscale, const float* xsum,
-                                         float (&acc)[kNR]) {
-    int SA[kNR][3], SB[kNR][3];
+// Per-lane constants of the fragment layout. A k32 step of unit u, half h covers the
+// 16-value quarters 2h' = h (k < 16, "part 0") and 2 + h (k >= 16, "part 1") of the
+// unit; B column c < 3 holds limb c of part 0, 4 <= c < 7 limb c - 4 of part 1, the
+// rest zero. So the D columns 2t, 2t+1 of lane t are (limb 0, limb 1) of part t/2 for
+// even t and (limb 2, zero) for odd t, and v = d[2t] + 256 d[2t+1] is exact.
+struct Lane {
+    uint32_t g8, t, part;  // part: which of the two sub-blocks of a step this lane's D holds
+    uint32_t boff;         // this lane's B words inside a unit's staged fragments
+    bool bload;            // B column g8 is a limb column
+    uint32_t mlo, mhi;     // b0 / b1 select: part-0 columns feed b0, part-1 columns b1
+};
+__device__ __forceinline__ Lane make_lane(int lane) {
+    Lane L;
+    L.g8 = (uint32_t)lane >> 2;
+    L.t = (uint32_t)lane & 3;
+    L.part = L.t >> 1;
+    L.bload = (L.g8 & 3) < 3;
+    L.boff = ((L.g8 >> 2) * 3 + (L.g8 & 3)) * 32 + L.t * 8;
+    L.mlo = L.g8 < 4 ? 0xffffffffu : 0u;
+    L.mhi = ~L.mlo;
+    return L;
+}
+// the staged B words (halves 0 and 1) of unit u for this lane
+__device__ __forceinline__ uint2 load_b(const uint8_t* xb, uint32_t u, const Lane& L) {
+    return L.bload ? *reinterpret_cast<const uint2*>(xb + u * kXUnit + L.boff) : make_uint2(0u, 0u);
+}
+// byte k of w as an exact float (unsigned), or of w ^ 0x80808080 minus 128 (signed)
+__device__ __forceinline__ float ubyte_f(uint32_t w, uint32_t k) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u | k)) - 8388608.f;
+}
+__device__ __forceinline__ float sbyte_f(uint32_t wx, uint32_t k) {
+    return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7650u | k)) - 8388736.f;
+}
+
+// Q4_K: one super-block (4 units from u0) of 16 rows. The qs byte holds value l of
+// sub-block 2j in its low nibble and of 2j+1 in its high nibble: the low nibbles are
+// masked in place (part 0), the high ones kept at 16x (part 1, wt carries the 1/16).
+// acc += d*s_j*(q . x) per sub-block, minus dmin*m_j*sum(x) of sub-blocks 2t, 2t+1.
+__device__ __forceinline__ void q4k_row_scales(uint4 h, const Lane& L, float wt, const float* X, float (&c)[4],
+                                               float& acc) {
+    const float d = h2f(h.x & 0xffff), dmin = h2f(h.x >> 16);
+    const uint32_t scl = h.y & 0x3F3F3F3Fu;                                  // s_0..3
+    const uint32_t sch = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);   // s_4..7
+    const uint32_t mnl = h.z & 0x3F3F3F3Fu;                                  // m_0..3
+    const uint32_t mnh = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);  // m_4..7
+    const float dw = d * wt;
+    c[0] = dw * ubyte_f(scl, L.part);
+    c[1] = dw * ubyte_f(scl, 2 + L.part);
+    c[2] = dw * ubyte_f(sch, L.part);
+    c[3] = dw * ubyte_f(sch, 2 + L.part);
+    const uint32_t mw = L.t < 2 ? mnl : mnh, k0 = (2 * L.t) & 3;
+    acc -= dmin * fmaf(ubyte_f(mw, k0), X[2 * L.t], ubyte_f(mw, k0 + 1) * X[2 * L.t + 1]);
+}
+
+__device__ __forceinline__ void sb_q4k(const uint8_t* sb, uint32_t u0, const uint8_t* xb, const float* fs,
+                                       const float* xsum, const Lane& L, int lane, float wt, float& acc0,
+                                       float& acc1) {
+    float c0[4], c1[4];
+    q4k_row_scales(*reinterpret_cast<const uint4*>(sb + 2048 + L.g8 * 16), L, wt, xsum + 2 * u0, c0, acc0);
+    q4k_row_scales(*reinterpret_cast<const uint4*>(sb + 2048 + (L.g8 + 8) * 16), L, wt, xsum + 2 * u0, c1, acc1);
 #pragma unroll
-    for (int i = 0; i < kNR; ++i)
-#pragma unroll
-        for (int k = 0; k < 3; ++k) SA[i][k] = SB[i][k] = 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {  // qs chunk `half`: words t = 4*half .. 4*half+3
-        int4 la[3], lb[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            la[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 16 * half);
-            lb[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 32 + 16 * half);
-        }
-#pragma unroll
-        for (int i = 0; i < kNR; ++i) {
-            const int4 w = *reinterpret_cast<const int4*>(tiles[i] + half * U * 16 + lane * 16);
-            const int wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int lo = wv[t] & 0x0F0F0F0F, hi = (wv[t] >> 4) & 0x0F0F0F0F;
-                const int a0 = t == 0 ? la[0].x : t == 1 ? la[0].y : t == 2 ? la[0].z : la[0].w;
-                const int a1 = t == 0 ? la[1].x : t == 1 ? la[1].y : t == 2 ? la[1].z : la[1].w;
-                const int a2 = t == 0 ? la[2].x : t == 1 ? la[2].y : t == 2 ? la[2].z : la[2].w;
-                const int b0 = t == 0 ? lb[0].x : t == 1 ? lb[0].y : t == 2 ? lb[0].z : lb[0].w;
-                const int b1 = t == 0 ? lb[1].x : t == 1 ? lb[1].y : t == 2 ? lb[1].z : lb[1].w;
-                const int b2 = t == 0 ? lb[2].x : t == 1 ? lb[2].y : t == 2 ? lb[2].z : lb[2].w;
-                SA[i][0] = dp4a(lo, a0, SA[i][0]);
-                SA[i][1] = dp4a(lo, a1, SA[i][1]);
-                SA[i][2] = dp4a(lo, a2, SA[i][2]);
-                SB[i][0] = dp4a(hi, b0, SB[i][0]);
-                SB[i][1] = dp4a(hi, b1, SB[i][1]);
-                SB[i][2] = dp4a(hi, b2, SB[i][2]);
-            }
-        }
-    }
-    const float fa = fscale[2 * u], fb = fscale[2 * u + 1];
-    const float XA = xsum[2 * u], XB = xsum[2 * u + 1];
-    const uint32_t j = u & 3, sh = 8 * ((2 * j) & 3);
-    const bool high = j >= 2;
-#pragma unroll
-    for (int i = 0; i < kNR; ++i) {
-        const uint4 hd = *reinterpret_cast<const uint4*>(tiles[i] + U * 32 + (lane / 4) * 16);
-        const float d = h2f(hd.x & 0xffff), dmin = h2f(hd.x >> 16);
-        const uint32_t w0s = hd.y >> sh, w1s = hd.z >> sh, w2s = hd.w >> sh;
-        // get_scale_min_k4 (src/gguf.rs:327-336) for sub-blocks 2j, 2j+1
-        uint32_t s1, m1, s2, m2;
-        if (!high) {
-            s1 = w0s & 63; m1 = w1s & 63;
-            s2 = (w0s >> 8) & 63; m2 = (w1s >> 8) & 63;
-        } else {
-            s1 = (w2s & 15) | (((w0s >> 6) & 3) << 4);
-            m1 = ((w2s >> 4) & 15) | (((w1s >> 6) & 3) << 4);
-            s2 = ((w2s >> 8) & 15) | (((w0s >> 14) & 3) << 4);
-            m2 = ((w2s >> 12) & 15) | (((w1s >> 14) & 3) << 4);
-        }
-        const float va = fmaf((float)SA[i][2], 65536.f, (float)(SA[i][0] + 256 * SA[i][1])) * fa;
-        const float vb = fmaf((float)SB[i][2], 65536.f, (float)(SB[i][0] + 256 * SB[i][1])) * fb;
-        acc[i] += d * ((float)s1 * va + (float)s2 * vb) - dmin * ((float)m1 * XA + (float)m2 * XB);
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t u = u0 + j;
+        const uint4 A = *reinterpret_cast<const uint4*>(sb + j * 512 + lane * 16);
+        const uint2 B = load_b(xb, u, L);
+        int d[4] = {0, 0, 0, 0};
+        mma_u8s8(d, A.x & 0x0F0F0F0Fu, A.y & 0x0F0F0F0Fu, A.x & 0xF0F0F0F0u, A.y & 0xF0F0F0F0u, B.x & L.mlo,
+                 B.x & L.mhi);
+        mma_u8s8(d, A.z & 0x0F0F0F0Fu, A.w & 0x0F0F0F0Fu, A.z & 0xF0F0F0F0u, A.w & 0xF0F0F0F0u, B.y & L.mlo,
+                 B.y & L.mhi);
+        const float f = fs[2 * u + L.part];
+        acc0 = fmaf(c0[j] * f, (float)(d[0] + 256 * d[1]), acc0);
+        acc1 = fmaf(c1[j] * f, (float)(d[2] + 256 * d[3]), acc1);
     }
 }
 
-// Q6_K: unit (super-block, half h, l0) holds values 128h + 32k + l0 + l for k = 0..3,
-// l < 16; its limbs are stored [limb][l/4][k][l%4].
-__device__ __forceinline__ void unit_q6k(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
-                                         const uint8_t* limbs, const float* fscale, const int* msum,
-                                         float (&acc)[kNR]) {
-    int S[kNR][4][3];
+// Q6_K: one super-block of 16 rows. Step (unit j = 2H + jj, half h) holds the values
+// 128H + 32kq + 16h + l', kq = 2jj (part 0) and 2jj + 1 (part 1), i.e. sub-blocks
+// 4j + h and 4j + 2 + h; q = 6-bit value (u8), the -32 offset is taken off the integer
+// sums with the staged limb sums of each part.
+__device__ __forceinline__ void sb_q6k(const uint8_t* sb, uint32_t u0, const uint8_t* xb, const float* fs,
+                                       const int* ms, const Lane& L, int lane, float wt, float& acc0, float& acc1) {
+    const uint4 S0 = *reinterpret_cast<const uint4*>(sb + 3072 + L.g8 * 16);
+    const uint4 S1 = *reinterpret_cast<const uint4*>(sb + 3072 + (L.g8 + 8) * 16);
+    const float dA = h2f(*reinterpret_cast<const uint16_t*>(sb + 3328 + L.g8 * 2)) * wt;
+    const float dB = h2f(*reinterpret_cast<const uint16_t*>(sb + 3328 + (L.g8 + 8) * 2)) * wt;
+    const uint32_t sA[4] = {S0.x ^ 0x80808080u, S0.y ^ 0x80808080u, S0.z ^ 0x80808080u, S0.w ^ 0x80808080u};
+    const uint32_t sB[4] = {S1.x ^ 0x80808080u, S1.y ^ 0x80808080u, S1.z ^ 0x80808080u, S1.w ^ 0x80808080u};
 #pragma unroll
-    for (int i = 0; i < kNR; ++i)
+    for (int H = 0; H < 2; ++H) {
+        const uint8_t* lp = sb + H * 1536 + lane * 48;
+        const uint4 P0 = *reinterpret_cast<const uint4*>(lp);
+        const uint4 P1 = *reinterpret_cast<const uint4*>(lp + 16);
+        const uint4 P2 = *reinterpret_cast<const uint4*>(lp + 32);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) S[i][k][0] = S[i][k][1] = S[i][k][2] = 0;
-    // the three 16-byte chunks of each row, as whole vector loads (a lane's chunk is
-    // 16 contiguous bytes; word-sized loads at a 16-byte lane stride would conflict)
-    uint4 Lc[kNR], Hc[kNR], Qc[kNR];
+        for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * H + jj;
+            const uint32_t u = u0 + j;
+            const uint2 B = load_b(xb, u, L);
+            const int2 M = *reinterpret_cast<const int2*>(ms + u * 8 + L.t * 2);
+            const float f = fs[2 * u + L.part];
+            const float fA = dA * f, fB = dB * f;
 #pragma unroll
-    for (int i = 0; i < kNR; ++i) {
-        Lc[i] = *reinterpret_cast<const uint4*>(tiles[i] + lane * 16);
-        Hc[i] = *reinterpret_cast<const uint4*>(tiles[i] + U * 16 + lane * 16);
-        Qc[i] = *reinterpret_cast<const uint4*>(tiles[i] + 2 * U * 16 + lane * 16);
-    }
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        int4 lv[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) lv[c] = *reinterpret_cast<const int4*>(limbs + c * 64 + 16 * t);
-#pragma unroll
-        for (int i = 0; i < kNR; ++i) {
-            const uint32_t L = t == 0 ? Lc[i].x : t == 1 ? Lc[i].y : t == 2 ? Lc[i].z : Lc[i].w;
-            const uint32_t H = t == 0 ? Hc[i].x : t == 1 ? Hc[i].y : t == 2 ? Hc[i].z : Hc[i].w;
-            const uint32_t Q = t == 0 ? Qc[i].x : t == 1 ? Qc[i].y : t == 2 ? Qc[i].z : Qc[i].w;
-            const int q0 = (int)((L & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u));
-            const int q1 = (int)((H & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u));
-            const int q2 = (int)(((L >> 4) & 0x0F0F0F0Fu) | (Q & 0x30303030u));
-            const int q3 = (int)(((H >> 4) & 0x0F0F0F0Fu) | ((Q >> 2) & 0x30303030u));
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                S[i][0][c] = dp4a(q0, lv[c].x, S[i][0][c]);
-                S[i][1][c] = dp4a(q1, lv[c].y, S[i][1][c]);
-                S[i][2][c] = dp4a(q2, lv[c].z, S[i][2][c]);
-                S[i][3][c] = dp4a(q3, lv[c].w, S[i][3][c]);
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t l0a = h ? P0.y : P0.x, l0b = h ? P0.w : P0.z;  // rows g8, g8 + 8
+                const uint32_t l1a = h ? P1.y : P1.x, l1b = h ? P1.w : P1.z;
+                const uint32_t qa = h ? P2.y : P2.x, qb = h ? P2.w : P2.z;
+                uint32_t a0, a1, a2, a3;
+                if (jj == 0) {
+                    a0 = (l0a & 0x0F0F0F0Fu) | ((qa << 4) & 0x30303030u);
+                    a1 = (l0b & 0x0F0F0F0Fu) | ((qb << 4) & 0x30303030u);
+                    a2 = (l1a & 0x0F0F0F0Fu) | ((qa << 2) & 0x30303030u);
+                    a3 = (l1b & 0x0F0F0F0Fu) | ((qb << 2) & 0x30303030u);
+                } else {
+                    a0 = ((l0a >> 4) & 0x0F0F0F0Fu) | (qa & 0x30303030u);
+                    a1 = ((l0b >> 4) & 0x0F0F0F0Fu) | (qb & 0x30303030u);
+                    a2 = ((l1a >> 4) & 0x0F0F0F0Fu) | ((qa >> 2) & 0x30303030u);
+                    a3 = ((l1b >> 4) & 0x0F0F0F0Fu) | ((qb >> 2) & 0x30303030u);
+                }
+                const uint32_t bw = h ? B.y : B.x;
+                int d[4] = {0, 0, 0, 0};
+                mma_u8s8(d, a0, a1, a2, a3, bw & L.mlo, bw & L.mhi);
+                const int bias = 32 * (h ? M.y : M.x);
+                const uint32_t k = h + 2 * L.part;  // scale byte of sub-block 4j + k in word j
+                acc0 = fmaf(fA * sbyte_f(sA[j], k), (float)(d[0] + 256 * d[1] - bias), acc0);
+                acc1 = fmaf(fB * sbyte_f(sB[j], k), (float)(d[2] + 256 * d[3] - bias), acc1);
             }
         }
-    }
-    // x-block of run k: 8*(u/4) + 4*h + k with h = (u/2) & 1
-    const uint32_t jb = 8 * (u >> 2) + 4 * ((u >> 1) & 1);
-    const int* ms = msum + u * 12;  // [k][limb] sums of the limbs (the -32 bias)
-#pragma unroll
-    for (int i = 0; i < kNR; ++i) {
-        const uint32_t scw = *reinterpret_cast<const uint32_t*>(tiles[i] + U * 48 + lane * 4);
-        const uint32_t dh = *reinterpret_cast<const uint16_t*>(tiles[i] + U * 48 + pad16(U * 4) + (lane / 4) * 2);
-        float s = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int a = S[i][k][0] - 32 * ms[3 * k], b = S[i][k][1] - 32 * ms[3 * k + 1],
-                      c = S[i][k][2] - 32 * ms[3 * k + 2];
-            const float v = fmaf((float)c, 65536.f, (float)(a + 256 * b)) * fscale[jb + k];
-            s = fmaf((float)(int8_t)((scw >> (8 * k)) & 0xff), v, s);
-        }
-        acc[i] = fmaf(h2f(dh), s, acc[i]);
     }
 }
 
-// Q8_0: two 32-value blocks per unit.
-__device__ __forceinline__ void unit_q8_0(const uint8_t* const (&tiles)[kNR], uint32_t U, uint32_t lane, uint32_t u,
-                                          const uint8_t* limbs, const float* fscale, float (&acc)[kNR]) {
-    int S[kNR][2][3];
-#pragma unroll
-    for (int i = 0; i < kNR; ++i)
-#pragma unroll
-        for (int b = 0; b < 2; ++b) S[i][b][0] = S[i][b][1] = S[i][b][2] = 0;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        int4 lv[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) lv[k] = *reinterpret_cast<const int4*>(limbs + k * 64 + 16 * c);
-#pragma unroll
-        for (int i = 0; i < kNR; ++i) {
-            const int4 w = *reinterpret_cast<const int4*>(tiles[i] + c * U * 16 + lane * 16);
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                int s = S[i][c >> 1][k];
-                s = dp4a(w.x, lv[k].x, s);
-                s = dp4a(w.y, lv[k].y, s);
-                s = dp4a(w.z, lv[k].z, s);
-                s = dp4a(w.w, lv[k].w, s);
-                S[i][c >> 1][k] = s;
-            }
-        }
-    }
-    const float f0 = fscale[2 * u], f1 = fscale[2 * u + 1];
-#pragma unroll
-    for (int i = 0; i < kNR; ++i) {
-        const uint32_t dw = *reinterpret_cast<const uint32_t*>(tiles[i] + U * 64 + lane * 4);
-        const float v0 = fmaf((float)S[i][0][2], 65536.f, (float)(S[i][0][0] + 256 * S[i][0][1])) * f0;
-        const float v1 = fmaf((float)S[i][1][2], 65536.f, (float)(S[i][1][0] + 256 * S[i][1][1])) * f1;
-        acc[i] += h2f(dw & 0xffff) * v0 + h2f(dw >> 16) * v1;
-    }
+// Q8_0: one unit (blocks 2u = part 0, 2u + 1 = part 1) of 16 rows.
+__device__ __forceinline__ void unit_q8_0(const uint8_t* ub, uint32_t u, const uint8_t* xb, const float* fs,
+                                          const Lane& L, int lane, float wt, float& acc0, float& acc1) {
+    const uint4 A0 = *reinterpret_cast<const uint4*>(ub + lane * 16);
+    const uint4 A1 = *reinterpret_cast<const uint4*>(ub + 512 + lane * 16);
+    const uint32_t dw0 = *reinterpret_cast<const uint32_t*>(ub + 1024 + L.g8 * 4);
+    const uint32_t dw1 = *reinterpret_cast<const uint32_t*>(ub + 1024 + (L.g8 + 8) * 4);
+    const uint2 B = load_b(xb, u, L);
+    int d[4] = {0, 0, 0, 0};
+    mma_s8s8(d, A0.x, A0.y, A0.z, A0.w, B.x & L.mlo, B.x & L.mhi);
+    mma_s8s8(d, A1.x, A1.y, A1.z, A1.w, B.y & L.mlo, B.y & L.mhi);
+    const float f = fs[2 * u + L.part] * wt;
+    const float d0 = h2f(L.part ? dw0 >> 16 : dw0 & 0xffff), d1 = h2f(L.part ? dw1 >> 16 : dw1 & 0xffff);
+    acc0 = fmaf(d0 * f, (float)(d[0] + 256 * d[1]), acc0);
+    acc1 = fmaf(d1 * f, (float)(d[2] + 256 * d[3]), acc1);
 }
 
 // ---------------------------------------------------------------- input staging
 // x (optionally RMS-normalised, src/runtime.rs:193-196) -> per 32-value block j a scale
 // 2^-s and |m| <= 2^22 with x = 2^-s * m, m = l0 + 2^8 l1 + 2^16 l2 in three int8 limbs,
-// written in the layouts the unit functions read. Each consumer thread stages one
-// 16-value half of a block from registers: the two halves of a block sit in adjacent
-// lanes and meet with one shuffle for the block maximum and sum.
+// written as the B fragments of the MMA steps: unit u's 192 bytes hold, for part p
+// (values 64u + 32p + 16h + [0, 16) in half h) and limb l, the words of lanes
+// t = 0..3 (values 4t..4t+3 of the quarter) for halves h = 0, 1 at
+// ((3p + l) * 4 + t) * 8 + 4h. Each consumer thread stages one 16-value quarter from
+// registers: the two quarters of a block sit in adjacent lanes and meet with one
+// shuffle for the block maximum and sum.
 
 // x is read through L2 (ld.global.cg): inside the persistent step kernel it was written
 // by other CTAs in the previous phase, and L1 is not coherent across SMs.
@@ -289,12 +288,12 @@ __device__ __forceinline__ void pack_limbs(int m0, int m1, int m2, int m3, uint3
 
 __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, float* red) {
     const MatvecArgs& a = p.a;
-    const uint32_t K = a.cols, nhalf = K / 16;
+    const uint32_t K = a.cols, nq = K / 16;
     const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
     float inv = 1.f;
     if (a.norm_w) {
         float ss = 0.f;
-        for (uint32_t hb = c; hb < nhalf; hb += kCW * 32) {
+        for (uint32_t hb = c; hb < nq; hb += kCW * 32) {
             const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -310,15 +309,14 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
         for (int w = 0; w < kCW; ++w) ss += red[w];
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
     }
-    uint8_t* nat = xs + p.off_nat;
-    uint8_t* q6 = xs + p.off_q6;
+    uint8_t* xb = xs;
     float* fscale = reinterpret_cast<float*>(xs + p.off_fscale);
     float* xsum = reinterpret_cast<float*>(xs + p.off_xsum);
     int* msum = reinterpret_cast<int*>(xs + p.off_msum);
-    // nhalf is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
-    for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nhalf; hb0 += kCW * 32) {
+    // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
+    for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nq; hb0 += kCW * 32) {
         const uint32_t hb = hb0 + lane;
-        const bool on = hb < nhalf;  // uniform per lane pair
+        const bool on = hb < nq;  // uniform per lane pair
         float v[16];
         if (on) {
             const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
@@ -363,7 +361,7 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
         uint32_t L0[4], L1[4], L2[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
-        const uint32_t j = hb >> 1, h = hb & 1;
+        const uint32_t j = hb >> 1, h = hb & 1, u = hb >> 2, part = (hb >> 1) & 1;
         const float fs = __uint_as_float((uint32_t)(127 - s) << 23);
         if (p.need & NEED_XSUM) {  // sum of the staged (quantised) block: exact in int32
             int sm = 0;
@@ -374,35 +372,24 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
         }
         if (!on) continue;
         if (h == 0) fscale[j] = fs;
-        if (p.need & NEED_NAT) {  // unit j/2: [limb][64 values], block j&1 at +32, half at +16
-            uint8_t* b = nat + (j >> 1) * kLimbStride + (j & 1) * 32 + h * 16;
-            *reinterpret_cast<uint4*>(b) = make_uint4(L0[0], L0[1], L0[2], L0[3]);
-            *reinterpret_cast<uint4*>(b + 64) = make_uint4(L1[0], L1[1], L1[2], L1[3]);
-            *reinterpret_cast<uint4*>(b + 128) = make_uint4(L2[0], L2[1], L2[2], L2[3]);
+        uint8_t* b = xb + u * kXUnit + part * 96 + h * 4;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            *reinterpret_cast<uint32_t*>(b + e * 8) = L0[e];
+            *reinterpret_cast<uint32_t*>(b + 32 + e * 8) = L1[e];
+            *reinterpret_cast<uint32_t*>(b + 64 + e * 8) = L2[e];
         }
-        if (p.need & NEED_Q6) {  // the half is run k of unit u: value l at (l/4)*16 + k*4 + l%4
-            const uint32_t i = 16 * hb, r8 = i & 255, hh = r8 >> 7, k = (r8 >> 5) & 3;
-            const uint32_t u = (i >> 8) * 4 + hh * 2 + h;
-            uint8_t* b = q6 + u * kLimbStride + k * 4;
+        if (p.need & NEED_MSUM) {  // per quarter: limb sums for the Q6_K -32 offset, as the lanes combine them
+            int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                *reinterpret_cast<uint32_t*>(b + q * 16) = L0[q];
-                *reinterpret_cast<uint32_t*>(b + 64 + q * 16) = L1[q];
-                *reinterpret_cast<uint32_t*>(b + 128 + q * 16) = L2[q];
+                s0 = dp4a((int)L0[q], 0x01010101, s0);
+                s1 = dp4a((int)L1[q], 0x01010101, s1);
+                s2 = dp4a((int)L2[q], 0x01010101, s2);
             }
-            if (p.need & NEED_MSUM) {  // per run: sums of each limb (the -32 bias)
-                int s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    s0 = dp4a((int)L0[q], 0x01010101, s0);
-                    s1 = dp4a((int)L1[q], 0x01010101, s1);
-                    s2 = dp4a((int)L2[q], 0x01010101, s2);
-                }
-                int* ms = msum + u * 12 + 3 * k;
-                ms[0] = s0;
-                ms[1] = s1;
-                ms[2] = s2;
-            }
+            int* ms = msum + u * 8 + part * 4 + h;  // [u][t = 2 part + (limb 2)][h]
+            ms[0] = s0 + 256 * s1;
+            ms[2] = s2;
         }
     }
     named_sync(kConsumerBarrier, kCW * 32);
@@ -416,21 +403,21 @@ __device__ __forceinline__ void cta_rows(const Plan& p, uint32_t cta, uint32_t n
     rb1 = (uint32_t)(((uint64_t)total * (cta + 1)) / ncta);
 }
 
-// Global addresses of item (rb, g): the one or two 16-row slabs of column group g that
-// one stage holds -- rows [32*local, +32), or gate and up rows [16*local, +16) for the
-// SwiGLU pair. Returns the number of slabs (1 when the second is past the end).
+// Global addresses of item (rb, g): panel g of the one or two 16-row slabs one stage
+// holds -- rows [32*local, +32), or gate and up rows [16*local, +16) for the SwiGLU
+// pair. Returns the number of slabs (1 when the second is past the end).
 __device__ __forceinline__ uint32_t item_slabs(const Plan& p, uint32_t rb, uint32_t g, const uint8_t*& a,
                                                const uint8_t*& b, uint32_t& slab_bytes) {
     const int si = seg_of(p, rb);
     const MatvecSeg& sg = p.a.seg[si];
     const uint32_t local = rb - p.rb_begin[si];
     const uint32_t T = sg.m.type;
-    slab_bytes = kSlabRows * tile_bytes(T, group_units(p.nunits, g));
+    slab_bytes = panel_bytes(T, group_units(p.nunits, g));
     const bool dual = sg.epi == EPI_SWIGLU;
     const QMatDev& mb = dual ? sg.m2 : sg.m;
     const uint32_t sa = dual ? local : 2 * local, sbk = dual ? local : 2 * local + 1;
-    a = sg.m.q + (uint64_t)sa * kSlabRows * sg.m.row_bytes + slab_group_offset(T, g);
-    b = mb.q + (uint64_t)sbk * kSlabRows * mb.row_bytes + slab_group_offset(T, g);
+    a = sg.m.q + (uint64_t)sa * kSlabRows * sg.m.row_bytes + panel_offset(T, g);
+    b = mb.q + (uint64_t)sbk * kSlabRows * mb.row_bytes + panel_offset(T, g);
     return sbk * kSlabRows < mb.rows ? 2 : 1;
 }
 
@@ -480,71 +467,78 @@ __device__ void drain_ring(const Ring& r, uint32_t item) {
 }
 
 // Consumers (all kCW warps): dot products of row blocks [rb0, rb1) against the staged
-// input `xs`, epilogue per row block. Returns false after an abort.
-__device__ bool consume_items(const Plan& p, const Ring& r, const uint8_t* xs, uint32_t rb0, uint32_t rb1,
+// input `xs`; warp (slab w / 8, super-block w % 8) of every stage. At the end of a row
+// block the eight partial sums of each row meet in shared memory (fixed order) and
+// warp 0 runs the epilogue. Returns false after an abort (every consumer warp returns
+// at the same stage, before the row block's barrier).
+__device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_t rb0, uint32_t rb1,
                               uint32_t& item, int warp, int lane, volatile int* abort_flag) {
-    const uint8_t* nat = xs + p.off_nat;
-    const uint8_t* q6 = xs + p.off_q6;
+    const uint8_t* xb = xs;
     const float* fscale = reinterpret_cast<const float*>(xs + p.off_fscale);
     const float* xsum = reinterpret_cast<const float*>(xs + p.off_xsum);
     const int* msum = reinterpret_cast<const int*>(xs + p.off_msum);
+    float* red = reinterpret_cast<float*>(xs + p.off_red);
+    const Lane L = make_lane(lane);
+    const uint32_t slab = (uint32_t)warp / kSbWarps, sbw = (uint32_t)warp % kSbWarps;
+    uint32_t buf = 0;
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
         const int si = seg_of(p, rb);
         const MatvecSeg& sg = p.a.seg[si];
         const uint32_t local = rb - p.rb_begin[si];
         const uint32_t T = sg.m.type;
         const bool dual = sg.epi == EPI_SWIGLU;
-        uint32_t slots[kNR];
-#pragma unroll
-        for (int i = 0; i < kNR; ++i)
-            slots[i] = dual ? (uint32_t)((i < kNR / 2 ? 0 : kRB / 2) + (kNR / 2) * warp + i % (kNR / 2))
-                            : (uint32_t)(kNR * warp + i);
-        float acc[kNR];
-#pragma unroll
-        for (int i = 0; i < kNR; ++i) acc[i] = 0.f;
+        // limb weight of this lane's D columns (and the 16x of Q4_K high nibbles)
+        const float wt = ((L.t & 1) ? 65536.f : 1.f) * ((T == GGML_Q4_K && L.part) ? 0.0625f : 1.f);
+        float acc0 = 0.f, acc1 = 0.f;  // rows g8 and g8 + 8 of this warp's slab
         for (uint32_t g = 0; g < p.ngroups; ++g, ++item) {
             const uint32_t s = item % r.stages, n = item / r.stages;
             if (!wait_or_abort(&r.full[s], n & 1, abort_flag)) return false;
-            const uint32_t U = group_units(p.nunits, g), tb = tile_bytes(T, U);
-            const uint8_t* slot = r.base + s * r.slot_bytes;
-            if ((uint32_t)lane < U) {
-                const uint32_t u = g * 32 + lane;
-                const uint8_t* tiles[kNR];
-#pragma unroll
-                for (int i = 0; i < kNR; ++i) tiles[i] = slot + slots[i] * tb;
-                // rows past the end were not copied: their slots hold stale bytes whose
-                // (finite) results are discarded below
+            const uint32_t U = group_units(p.nunits, g), ub = 4 * sbw;
+            // rows past the end were not copied: their slots hold stale bytes whose
+            // (finite) results are discarded below
+            const uint8_t* pan = r.base + s * r.slot_bytes + slab * panel_bytes(T, U);
+            if (ub < U) {
+                const uint32_t u0 = g * kPanelUnits + ub;
                 if (T == GGML_Q4_K) {
-                    unit_q4k(tiles, U, lane, u, nat + u * kLimbStride, fscale, xsum, acc);
+                    sb_q4k(pan + sbw * 2304, u0, xb, fscale, xsum, L, lane, wt, acc0, acc1);
                 } else if (T == GGML_Q6_K) {
-                    unit_q6k(tiles, U, lane, u, q6 + u * kLimbStride, fscale, msum, acc);
+                    sb_q6k(pan + sbw * 3360, u0, xb, fscale, msum, L, lane, wt, acc0, acc1);
                 } else {
-                    unit_q8_0(tiles, U, lane, u, nat + u * kLimbStride, fscale, acc);
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i)
+                        if (ub + i < U) unit_q8_0(pan + (ub + i) * 1088, u0 + i, xb, fscale, L, lane, wt, acc0, acc1);
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&r.empty[s]);
         }
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        float* rd = red + buf * (kSbWarps * kRB);
+        if (L.t == 0) {
+            rd[sbw * kRB + slab * kSlabRows + L.g8] = acc0;
+            rd[sbw * kRB + slab * kSlabRows + L.g8 + 8] = acc1;
+        }
+        named_sync(kConsumerBarrier, kCW * 32);
+        if (warp == 0) {  // lane = row slot of the block
+            float v = 0.f;
 #pragma unroll
-        for (int i = 0; i < kNR; ++i) acc[i] = warp_sum(acc[i]);
-        if (lane == 0) {
+            for (int w = 0; w < kSbWarps; ++w) v += rd[w * kRB + lane];
             if (dual) {
-#pragma unroll
-                for (int i = 0; i < kNR / 2; ++i) {
-                    const uint32_t row = local * (kRB / 2) + (kNR / 2) * warp + i;
-                    if (row < sg.m.rows) sg.y[row] = __fmul_rn(silu(acc[i]), acc[i + kNR / 2]);
-                }
+                const float up = __shfl_down_sync(0xffffffffu, v, kSlabRows);
+                const uint32_t row = local * kSlabRows + lane;
+                if (lane < (int)kSlabRows && row < sg.m.rows) sg.y[row] = __fmul_rn(silu(v), up);
             } else {
-#pragma unroll
-                for (int i = 0; i < kNR; ++i) {
-                    const uint32_t row = local * kRB + kNR * warp + i;
-                    if (row < sg.m.rows) {
-                        if (sg.epi == EPI_ADD) sg.y[row] = __ldcg(sg.y + row) + acc[i];
-                        else sg.y[row] = acc[i];
-                    }
+                const uint32_t row = local * kRB + lane;
+                if (row < sg.m.rows) {
+                    if (sg.epi == EPI_ADD) sg.y[row] = __ldcg(sg.y + row) + v;
+                    else sg.y[row] = v;
                 }
             }
         }
+        buf ^= 1;
     }
     return true;
 }
@@ -573,26 +567,24 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
             if (sg.m.cols != a.cols || sg.m.rows == 0 || !sg.y) return cudaErrorInvalidValue;
             if (sg.epi == EPI_SWIGLU && (sg.m2.type != t || sg.m2.rows != sg.m.rows || sg.m2.cols != a.cols))
                 return cudaErrorInvalidValue;
-            p.need |= t == GGML_Q6_K ? NEED_Q6 | NEED_MSUM : NEED_NAT;
+            if (t == GGML_Q6_K) p.need |= NEED_MSUM;
             if (t == GGML_Q4_K) p.need |= NEED_XSUM;
-            slot = std::max(slot, kRB * tile_bytes(t, 32));
+            slot = std::max(slot, 2 * panel_bytes(t, kPanelUnits));
             const uint32_t per = sg.epi == EPI_SWIGLU ? kRB / 2 : kRB;
             rbs = (sg.m.rows + per - 1) / per;
         }
         p.rb_begin[i + 1] = p.rb_begin[i] + rbs;
     }
     const uint32_t K = a.cols, nb = K / 32;
-    uint32_t off = 0;
-    p.off_nat = off;
-    if (p.need & NEED_NAT) off += p.nunits * kLimbStride;
-    p.off_q6 = off;
-    if (p.need & NEED_Q6) off += p.nunits * kLimbStride;
+    uint32_t off = p.nunits * kXUnit;  // B fragments
     p.off_fscale = off;
     off += nb * 4;
     p.off_xsum = off;
     if (p.need & NEED_XSUM) off += nb * 4;
     p.off_msum = off;
-    if (p.need & NEED_MSUM) off += p.nunits * 48;
+    if (p.need & NEED_MSUM) off += p.nunits * 32;
+    p.off_red = (off + 15) & ~15u;
+    off = p.off_red + kRedBytes;
     p.xbytes = (off + 127) & ~127u;
     p.item_bytes = slot;
     if (p.xbytes + 2 * slot > kSmemBudget) return cudaErrorInvalidValue;

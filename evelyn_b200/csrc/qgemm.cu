@@ -157,65 +157,60 @@ __device__ __forceinline__ uint32_t magic_fma(uint32_t v2, uint32_t s2, uint32_t
 
 // ------------------------------------------------------------------ device repack
 // One thread per (row, K chunk): copies the chunk's original block bytes out of the
-// matvec layout (dequant.cuh's addressing) into the GEMM block.
+// matvec layout (block_byte_address) into the GEMM block.
+__device__ __forceinline__ uint32_t ld_word(const QMatDev& m, uint32_t r, uint32_t b, uint32_t o) {
+    const uint8_t* p = m.q + block_byte_address(m, r, b, o);
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+// 16 GGUF bytes o..o+15 of block b (four payload words)
+__device__ __forceinline__ uint4 ld_piece(const QMatDev& m, uint32_t r, uint32_t b, uint32_t o) {
+    return make_uint4(ld_word(m, r, b, o), ld_word(m, r, b, o + 4), ld_word(m, r, b, o + 8), ld_word(m, r, b, o + 12));
+}
+
 __global__ void gemm_repack_kernel(const QMatDev src, QGemmDev dst) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t rows_pad = (uint64_t)dst.mtiles * kMT;
     if (idx >= rows_pad * dst.nchunks) return;
     const uint32_t r = (uint32_t)(idx % rows_pad), c = (uint32_t)(idx / rows_pad);
-    const uint32_t mt = r / kMT, t = r % kMT, T = src.type, N = src.nunits;
+    const uint32_t t = r % kMT, mt = r / kMT, T = src.type;
     uint8_t* blk = const_cast<uint8_t*>(dst.q) + ((uint64_t)mt * dst.nchunks + c) * dst.block_bytes;
     const bool live = r < src.rows;
-    auto tile = [&](uint32_t u) { return src.q + tile_address(T, N, src.row_bytes, r, u >> 5); };
+    const uint4 zero = make_uint4(0, 0, 0, 0);
     if (T == GGML_Q4_K) {
         uint8_t head[16];
         uint4 qs[8];
         if (live) {
-            const uint8_t* h = tile(4 * c) + aux_in_tile(T, N, 4 * c);
+            const uint8_t* h = src.q + block_byte_address(src, r, c, 0);
             for (int i = 0; i < 16; ++i) head[i] = h[i];
-            for (uint32_t q = 0; q < 8; ++q) {
-                const uint32_t u = 4 * c + q / 2;
-                qs[q] = *reinterpret_cast<const uint4*>(tile(u) + chunk_in_tile(N, u, q & 1));
-            }
+            for (uint32_t q = 0; q < 8; ++q) qs[q] = ld_piece(src, r, c, 16 + 16 * q);
         } else {
             for (int i = 0; i < 16; ++i) head[i] = 0;
-            for (int q = 0; q < 8; ++q) qs[q] = make_uint4(0, 0, 0, 0);
+            for (int q = 0; q < 8; ++q) qs[q] = zero;
         }
         for (int i = 0; i < 4; ++i) blk[t * 4 + i] = head[i];
         for (int i = 0; i < 12; ++i) blk[512 + t * 12 + i] = head[4 + i];
         for (uint32_t q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(blk + 2048 + t * 128 + ((q ^ (t & 7)) * 16)) = qs[q];
     } else if (T == GGML_Q6_K) {
-        // units (c, h, b): chunk 0 ql[64h+16b..], chunk 1 ql[64h+32+16b..], chunk 2 qh[32h+16b..]
-        for (uint32_t h = 0; h < 2; ++h)
-            for (uint32_t b = 0; b < 2; ++b) {
-                const uint32_t u = 4 * c + 2 * h + b;
-                uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0;
-                uint32_t scw = 0;
-                if (live) {
-                    const uint8_t* tl = tile(u);
-                    q0 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 0));
-                    q1 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 1));
-                    q2 = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, 2));
-                    scw = *reinterpret_cast<const uint32_t*>(tl + aux_in_tile(T, N, u));
-                }
-                // ql chunk index (16-byte pieces of ql[128]): 4h + b and 4h + 2 + b
-                const uint32_t l0 = 4 * h + b, l1 = 4 * h + 2 + b, hq = 2 * h + b;
-                *reinterpret_cast<uint4*>(blk + t * 128 + ((l0 ^ (t & 7)) * 16)) = q0;
-                *reinterpret_cast<uint4*>(blk + t * 128 + ((l1 ^ (t & 7)) * 16)) = q1;
-                *reinterpret_cast<uint4*>(blk + 16384 + t * 64 + ((hq ^ ((t >> 1) & 3)) * 16)) = q2;
-                for (uint32_t k = 0; k < 4; ++k) blk[24576 + t * 16 + 8 * h + b + 2 * k] = (uint8_t)(scw >> (8 * k));
-            }
-        const uint16_t d = live ? (uint16_t)ld_u16(tile(4 * c) + d_in_tile(T, N, 4 * c)) : (uint16_t)0;
-        *reinterpret_cast<uint16_t*>(blk + 26624 + t * 2) = d;
+        // ql pieces i (bytes 16i..16i+15 of ql[128]), qh pieces k (of qh[64])
+        for (uint32_t i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4*>(blk + t * 128 + ((i ^ (t & 7)) * 16)) = live ? ld_piece(src, r, c, 16 * i) : zero;
+        for (uint32_t k = 0; k < 4; ++k)
+            *reinterpret_cast<uint4*>(blk + 16384 + t * 64 + ((k ^ ((t >> 1) & 3)) * 16)) =
+                live ? ld_piece(src, r, c, 128 + 16 * k) : zero;
+        const uint8_t* sc = src.q + block_byte_address(src, r, c, 192);
+        for (uint32_t i = 0; i < 16; ++i) blk[24576 + t * 16 + i] = live ? sc[i] : (uint8_t)0;
+        const uint8_t* dp = src.q + block_byte_address(src, r, c, 208);
+        *reinterpret_cast<uint16_t*>(blk + 26624 + t * 2) = live ? (uint16_t)(dp[0] | (dp[1] << 8)) : (uint16_t)0;
     } else {  // Q8_0: units 4c..4c+3, two 32-value blocks each
         for (uint32_t j = 0; j < 4; ++j) {
-            const uint32_t u = 4 * c + j;
+            const uint32_t b0 = 2 * (4 * c + j);
             uint32_t dw = 0;
-            uint4 q[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+            uint4 q[4] = {zero, zero, zero, zero};
             if (live) {
-                const uint8_t* tl = tile(u);
-                for (uint32_t k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4*>(tl + chunk_in_tile(N, u, k));
-                dw = *reinterpret_cast<const uint32_t*>(tl + aux_in_tile(T, N, u));
+                const uint8_t* d0 = src.q + block_byte_address(src, r, b0, 0);
+                const uint8_t* d1 = src.q + block_byte_address(src, r, b0 + 1, 0);
+                dw = (uint32_t)d0[0] | ((uint32_t)d0[1] << 8) | ((uint32_t)d1[0] << 16) | ((uint32_t)d1[1] << 24);
+                for (uint32_t k = 0; k < 4; ++k) q[k] = ld_piece(src, r, b0 + (k >> 1), 2 + 16 * (k & 1));
             }
             *reinterpret_cast<uint32_t*>(blk + t * 16 + j * 4) = dw;  // d of blocks 2j, 2j+1
             for (uint32_t k = 0; k < 4; ++k) {

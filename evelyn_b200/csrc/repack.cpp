@@ -1,12 +1,11 @@
-// repack.cpp -- GGUF blocks -> the tiled device layout of common.cuh.
+// repack.cpp -- GGUF blocks -> the MMA-fragment device layout of common.cuh.
 //
 // The reference keeps each QMatrix as the raw GGUF bytes (src/runtime.rs:23-51) and
-// re-reads whole 144/210/34-byte blocks per row. On the GPU a row is cut into tiles of
-// up to 32 units (64 values each); inside a tile the 16-byte chunks are stored
-// chunk-major so the 32 lanes of a warp read consecutive 16-byte pieces, and the
-// block scales of the tile follow its payload, so one bulk copy moves a whole tile.
-// Every byte of the original survives: the exact dequantiser reads this layout back
-// bit-for-bit (dequant.cuh).
+// re-reads whole 144/210/34-byte blocks per row. On the GPU the 16 rows of a slab are
+// interleaved word by word so that each lane of the matvec's MMA warps loads its
+// fragments with 16-byte shared-memory reads, and a panel of 32 units is one bulk
+// copy. Every byte of the original survives at block_byte_address: the exact
+// dequantiser reads this layout back bit-for-bit (dequant.cuh).
 #include <algorithm>
 #include <cstring>
 #include <thread>
@@ -37,7 +36,7 @@ void repack_sizes(QMatrix& m) {
     m.dev.rows = m.rows;
     m.dev.cols = m.cols;
     m.dev.nunits = nunits;
-    m.dev.row_bytes = row_tile_bytes(m.type, nunits);
+    m.dev.row_bytes = slab_row_bytes(m.type, nunits);
     const uint64_t slabs = (m.rows + kSlabRows - 1) / kSlabRows;
     m.total_bytes = (slabs * kSlabRows * m.dev.row_bytes + 255) / 256 * 256;
 }
@@ -47,61 +46,42 @@ void place(QMatrix& m, uint8_t* base) { m.dev.q = base + m.offset; }
 namespace {
 
 void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* dst, uint32_t r0, uint32_t r1) {
-    const uint32_t T = m.type, N = m.dev.nunits, nb = m.cols / 256, ch = chunks_per_unit(T), RB = m.dev.row_bytes;
+    const uint32_t T = m.type;
+    const QMatDev& d = m.dev;
     for (uint32_t r = r0; r < r1; ++r) {
         const uint8_t* src = raw + (size_t)r * stride;
-        // tile of unit u in this row
-        auto tile = [&](uint32_t u) { return dst + tile_address(T, N, RB, r, u >> 5); };
+        auto put = [&](uint32_t b, uint32_t o, const uint8_t* from, uint32_t n) {
+            std::memcpy(dst + block_byte_address(d, r, b, o), from, n);
+        };
         switch (T) {
             case GGML_Q4_K:
-                for (uint32_t sb = 0; sb < nb; ++sb) {
-                    const uint8_t* blk = src + (size_t)sb * 144;
-                    std::memcpy(tile(sb * 4) + aux_in_tile(T, N, sb * 4), blk, 16);
-                    for (uint32_t j = 0; j < 4; ++j) {
-                        const uint32_t u = sb * 4 + j;
-                        for (uint32_t c = 0; c < 2; ++c)
-                            std::memcpy(tile(u) + chunk_in_tile(N, u, c), blk + 16 + 32 * j + 16 * c, 16);
-                    }
+                for (uint32_t b = 0; b < m.cols / 256; ++b) {
+                    const uint8_t* blk = src + (size_t)b * 144;
+                    put(b, 0, blk, 16);
+                    for (uint32_t o = 16; o < 144; o += 4) put(b, o, blk + o, 4);
                 }
                 break;
             case GGML_Q6_K:
-                for (uint32_t sb = 0; sb < nb; ++sb) {
-                    const uint8_t* blk = src + (size_t)sb * 210;
-                    const uint8_t* ql = blk;
-                    const uint8_t* qh = blk + 128;
-                    const uint8_t* sc = blk + 192;
-                    std::memcpy(tile(sb * 4) + d_in_tile(T, N, sb * 4), blk + 208, 2);
-                    for (uint32_t h = 0; h < 2; ++h)
-                        for (uint32_t b = 0; b < 2; ++b) {
-                            const uint32_t u = sb * 4 + h * 2 + b, l0 = 16 * b;
-                            uint8_t* t = tile(u);
-                            std::memcpy(t + chunk_in_tile(N, u, 0), ql + 64 * h + l0, 16);
-                            std::memcpy(t + chunk_in_tile(N, u, 1), ql + 64 * h + 32 + l0, 16);
-                            std::memcpy(t + chunk_in_tile(N, u, 2), qh + 32 * h + l0, 16);
-                            uint8_t w[4];
-                            for (uint32_t k = 0; k < 4; ++k) w[k] = sc[8 * h + b + 2 * k];
-                            std::memcpy(t + aux_in_tile(T, N, u), w, 4);
-                        }
+                for (uint32_t b = 0; b < m.cols / 256; ++b) {
+                    const uint8_t* blk = src + (size_t)b * 210;
+                    for (uint32_t o = 0; o < 192; o += 4) put(b, o, blk + o, 4);
+                    put(b, 192, blk + 192, 16);
+                    put(b, 208, blk + 208, 2);
                 }
                 break;
             case GGML_Q8_0:
-                for (uint32_t u = 0; u < N; ++u) {
-                    const uint8_t* b0 = src + (size_t)(2 * u) * 34;
-                    const uint8_t* b1 = b0 + 34;
-                    uint8_t* t = tile(u);
-                    std::memcpy(t + chunk_in_tile(N, u, 0), b0 + 2, 16);
-                    std::memcpy(t + chunk_in_tile(N, u, 1), b0 + 18, 16);
-                    std::memcpy(t + chunk_in_tile(N, u, 2), b1 + 2, 16);
-                    std::memcpy(t + chunk_in_tile(N, u, 3), b1 + 18, 16);
-                    const uint8_t w[4] = {b0[0], b0[1], b1[0], b1[1]};
-                    std::memcpy(t + aux_in_tile(T, N, u), w, 4);
+                for (uint32_t b = 0; b < m.cols / 32; ++b) {
+                    const uint8_t* blk = src + (size_t)b * 34;
+                    put(b, 0, blk, 2);
+                    for (uint32_t o = 2; o < 34; o += 4) put(b, o, blk + o, 4);
                 }
                 break;
-            default: {  // F16 / BF16 / F32: plain values, chunked
+            default: {  // F16 / BF16 / F32: each panel row contiguous
                 const uint32_t eb = T == GGML_F32 ? 4 : 2;
-                for (uint32_t u = 0; u < N; ++u)
-                    for (uint32_t c = 0; c < ch; ++c)
-                        std::memcpy(tile(u) + chunk_in_tile(N, u, c), src + (size_t)u * 64 * eb + 16 * c, 16);
+                for (uint32_t g = 0; g * kPanelUnits < d.nunits; ++g) {
+                    const uint32_t c0 = g * kPanelUnits * 64, n = group_units(d.nunits, g) * 64;
+                    std::memcpy(dst + plain_value_address(d, r, c0, eb), src + (size_t)c0 * eb, (size_t)n * eb);
+                }
             }
         }
     }
