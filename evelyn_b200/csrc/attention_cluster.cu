@@ -1,0 +1,385 @@
+// attention_cluster.cu -- single-sequence decode attention in one launch: QK-norm,
+// RoPE, KV append, split-K GQA attention and the split merge.
+//
+// Same arithmetic as attention.cu (full_attention, src/runtime.rs:663-768): per-head
+// RMSNorm of q and k (:700-713), NeoX or adjacent-pair RoPE (:437-474) with accurate
+// sincosf of pos * base^(-2i/rot_dim), K/V append (:721-722) in f16 (or f32) pages,
+// max-subtracted softmax of q.k / sqrt(hd) and the weighted sum of v (:723-766).
+//
+// Layout of the launch: one thread-block cluster of C CTAs per kv head; CTA `rank`
+// of the cluster owns positions [rank*S, (rank+1)*S) (S whole pages). Everything
+// that does not come from the QKV matvec is done before griddepcontrol.wait: the
+// position and page table are read, the split's K and V page tiles are copied into
+// shared memory with TMA bulk copies, and the norm weights and RoPE sin/cos for the
+// position are loaded. (The position, the page table and the cached K/V rows were
+// written by earlier steps or by the host before this step's first kernel; the
+// launch before this one has passed its own griddepcontrol.wait, so every kernel
+// before it has completed.) After the wait, one warp per q head, k and v loads its
+// vector, normalises and rotates it in registers, the split that holds the new
+// position appends k and v (to HBM and to its shared copy), and the 16 warps run an
+// online softmax over the split's positions, one position per warp at a time,
+// entirely out of shared memory. The C partials (m, l, o) of a kv head meet through
+// distributed shared memory: cluster rank 0 merges them in rank order.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace evl {
+
+namespace {
+
+namespace cg = cooperative_groups;
+
+constexpr int kAW = 16;  // warps per CTA
+constexpr uint32_t kMaxRingPages = 16;
+constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
+
+struct ClusterAttn {
+    RopeArgs r;
+    AttnArgs a;
+    uint32_t ring_pages;  // page tiles (K and V) the shared ring holds
+};
+
+__device__ __forceinline__ const uint8_t* kv_tile(const KvCacheDev& kv, int32_t page, uint32_t layer, uint32_t which,
+                                                  uint32_t head) {
+    return (const uint8_t*)kv.pool + (uint64_t)page * kv.page_stride + (uint64_t)layer * kv.layer_stride +
+           (uint64_t)head * kv.head_stride + (which ? kv.v_offset : 0);
+}
+
+// Positions per split (attention.cu's split_len): whole pages, nsplit splits at most.
+__host__ __device__ __forceinline__ uint32_t split_len(uint32_t t, uint32_t nsplit, uint32_t ps) {
+    const uint32_t per = (t + nsplit - 1) / nsplit;
+    return (per + ps - 1) / ps * ps;
+}
+
+template <int N>
+__device__ __forceinline__ void load_kv(const __half* p, float (&o)[N]) {
+    if constexpr (N == 4) {
+        const uint2 r = *reinterpret_cast<const uint2*>(p);
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+        const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+        o[0] = x.x; o[1] = x.y; o[2] = y.x; o[3] = y.y;
+    } else {
+        const unsigned r = *reinterpret_cast<const unsigned*>(p);
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&r));
+        o[0] = x.x; o[1] = x.y;
+    }
+}
+template <int N>
+__device__ __forceinline__ void load_kv(const float* p, float (&o)[N]) {
+#pragma unroll
+    for (int e = 0; e < N; ++e) o[e] = p[e];
+}
+template <typename KV>
+__device__ __forceinline__ KV to_kv(float v) {
+    if constexpr (sizeof(KV) == 2) return __float2half_rn(v);
+    else return v;
+}
+
+// Shared-memory bytes of one CTA (ring, q, per-warp vectors, warp partials, CTA partial).
+__host__ __device__ __forceinline__ size_t cluster_smem(uint32_t ring_pages, uint32_t ps, uint32_t hd, uint32_t eb,
+                                                       uint32_t G) {
+    return (size_t)ring_pages * 2 * ps * hd * eb + 4ull * G * hd + 4ull * (G + 2) * hd +
+           4ull * kAW * G * (hd + 2) + 4ull * G * (hd + 2);
+}
+
+template <typename KV, int G, int HD>
+__global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_constant__ ClusterAttn F) {
+    constexpr int DPL = HD / 32;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full;
+    __shared__ int bad_sh;
+    cg::cluster_group cl = cg::this_cluster();
+    const RopeArgs& r = F.r;
+    const AttnArgs& a = F.a;
+    const uint32_t C = cl.num_blocks(), rank = cl.block_rank(), kvh = blockIdx.x / C;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t ps = a.kv.page_size, tile = ps * HD;  // elements of one K (or V) page tile
+    KV* ring = reinterpret_cast<KV*>(smem);                                   // [ring][K|V][ps][HD]
+    float* qs = reinterpret_cast<float*>(smem + (size_t)F.ring_pages * 2 * tile * sizeof(KV));  // [G][HD]
+    float* vec = qs + G * HD;                                                 // [G+2][HD] per-warp vectors
+    float* wpart = vec + (G + 2) * HD;                                        // [warps][G][HD+2]
+    float* cpart = wpart + kAW * G * (HD + 2);                                // [G][HD+2]: o, m, l
+
+    if (tid == 0) {
+        mbar_init(&full, 1);
+        fence_barrier_init();
+        bad_sh = 0;
+    }
+    __syncthreads();
+    pdl_launch_dependents();  // the next kernel's weight streaming may start on idle SMs
+
+    // ---- before the wait: position, pages, static vectors
+    const int32_t pos = __ldcg(a.pos);
+    const bool pos_ok = pos >= 0 && (uint32_t)pos / ps < a.max_pages;
+    const uint32_t t_all = pos_ok ? (uint32_t)pos + 1 : 0;
+    const uint32_t S = pos_ok ? split_len(t_all, C, ps) : 0;
+    const uint32_t t0 = rank * S, t1 = pos_ok ? min(t_all, t0 + S) : 0;
+    const uint32_t npg = t0 < t1 ? (t1 - t0 + ps - 1) / ps : 0;
+    const bool valid = pos_ok && npg <= F.ring_pages;  // the same in every thread
+    const bool last = valid && npg > 0 && t1 == t_all;  // this split holds the new position
+    if (tid == 0) {
+        if (!valid) {
+            atomicExch(a.err, DEV_ERR_POSITION);
+        } else if (npg) {
+            mbar_arrive_expect_tx(&full, npg * 2 * tile * (uint32_t)sizeof(KV));
+            for (uint32_t i = 0; i < npg; ++i) {
+                const int32_t page = __ldcg(a.page_table + t0 / ps + i);
+                tma_load_1d(ring + (2 * i) * tile, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full);
+                tma_load_1d(ring + (2 * i + 1) * tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full);
+            }
+        }
+    }
+    // warp w < G: q head kvh*G + w; w == G: k; w == G+1: v. Lane dims d = DPL*lane + e.
+    const bool vw = warp < G + 2, normed = warp <= G;
+    float nw[DPL], sn[DPL], cs[DPL];
+    uint32_t i0[DPL], i1[DPL];
+    bool rot[DPL], second[DPL];
+    const uint32_t rd = min(r.rope_dim, (uint32_t)HD) & ~1u;
+    if (vw && normed) {
+        const float* w = warp < G ? r.q_norm : r.k_norm;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            const uint32_t d = DPL * lane + e;
+            nw[e] = w ? w[d] : 1.f;
+            rot[e] = d < rd && pos_ok;
+            uint32_t k = 0;
+            if (r.interleaved) {
+                k = d / 2;
+                i0[e] = d & ~1u;
+                i1[e] = i0[e] + 1;
+                second[e] = d & 1;
+            } else {
+                const uint32_t half = rd / 2;
+                second[e] = d >= half;
+                k = second[e] ? d - half : d;
+                i0[e] = k;
+                i1[e] = k + half;
+            }
+            sn[e] = 0.f;
+            cs[e] = 1.f;
+            if (rot[e]) sincosf(__fmul_rn((float)pos, r.rope_inv_freq[k]), &sn[e], &cs[e]);
+        }
+    }
+
+    pdl_wait();
+
+    // ---- q, k, v of this kv head: norm + rope in registers
+    float val[DPL];
+    if (vw) {
+        const float* src = warp < G ? r.q + (uint64_t)(kvh * G + warp) * HD : (warp == G ? r.k : r.v) + (uint64_t)kvh * HD;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) val[e] = __ldcg(src + DPL * lane + e);
+        if (normed) {
+            const float* w = warp < G ? r.q_norm : r.k_norm;
+            if (w) {  // rms_norm over the head (src/runtime.rs:193-196)
+                float ss = 0.f;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) ss += val[e] * val[e];
+                ss = warp_sum(ss);
+                const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), r.eps)));
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) val[e] = __fmul_rn(__fmul_rn(val[e], inv), nw[e]);
+            }
+            float* vv = vec + warp * HD;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) vv[DPL * lane + e] = val[e];
+            __syncwarp();
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) {
+                if (!rot[e]) continue;
+                const float x0 = vv[i0[e]], x1 = vv[i1[e]];
+                val[e] = second[e] ? __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, cs[e]))
+                                   : __fsub_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]));
+            }
+        }
+        if (warp < G) {
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) qs[warp * HD + DPL * lane + e] = val[e];
+        } else if (last) {  // KV append at pos (src/runtime.rs:721-722)
+            const int32_t page = __ldcg(a.page_table + (uint32_t)pos / ps);
+            KV* dst = (KV*)kv_tile(a.kv, page, r.layer, warp == G ? 0 : 1, kvh) + ((uint32_t)pos % ps) * HD;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) dst[DPL * lane + e] = to_kv<KV>(val[e]);
+        }
+    }
+    // ---- the staged pages (and the new row in the split's own copy)
+    if (valid && npg && !mbar_wait(&full, 0)) {
+        atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
+        bad_sh = 1;
+    }
+    __syncthreads();
+    const bool run = valid && npg > 0 && !bad_sh;
+    if (run && last && (warp == G || warp == G + 1)) {
+        const uint32_t li = (uint32_t)pos - t0;
+        KV* row = ring + ((li / ps) * 2 + (warp == G ? 0 : 1)) * tile + (li % ps) * HD;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) row[DPL * lane + e] = to_kv<KV>(val[e]);
+    }
+    __syncthreads();
+
+    // ---- online softmax over this split's positions, one per warp at a time
+    float qr[G][DPL], m[G], l[G], o[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            qr[g][e] = qs[g * HD + DPL * lane + e];
+            o[g][e] = 0.f;
+        }
+    }
+    if (run) {
+        for (uint32_t t = t0 + warp; t < t1; t += kAW) {
+            const uint32_t li = t - t0;
+            const KV* kp = ring + (li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
+            float kf[DPL], vf[DPL];
+            load_kv<DPL>(kp, kf);
+            load_kv<DPL>(kp + tile, vf);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float sc = qr[g][0] * kf[0];
+#pragma unroll
+                for (int e = 1; e < DPL; ++e) sc = fmaf(qr[g][e], kf[e], sc);
+                sc = warp_sum(sc) * a.scale;
+                const float mn = fmaxf(m[g], sc);
+                const float alpha = expf(m[g] - mn);  // exp(-inf) = 0 on the first position
+                const float w = expf(sc - mn);
+                l[g] = l[g] * alpha + w;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(w, vf[e], o[g][e] * alpha);
+                m[g] = mn;
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float* wp = wpart + (warp * G + g) * (HD + 2);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) wp[DPL * lane + e] = o[g][e];
+        if (lane == 0) {
+            wp[HD] = m[g];
+            wp[HD + 1] = l[g];
+        }
+    }
+    __syncthreads();
+    // ---- this CTA's partial: the warps merged in order (attention_combine_kernel's arithmetic)
+    for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
+        const uint32_t g = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < kAW; ++w) M = fmaxf(M, wpart[(w * G + g) * (HD + 2) + HD]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < kAW; ++w) {
+            const float* wp = wpart + (w * G + g) * (HD + 2);
+            if (wp[HD] == -INFINITY) continue;
+            const float f = expf(wp[HD] - M);
+            L += wp[HD + 1] * f;
+            O += wp[d] * f;
+        }
+        cpart[g * (HD + 2) + d] = O;
+        if (d == 0) {
+            cpart[g * (HD + 2) + HD] = M;
+            cpart[g * (HD + 2) + HD + 1] = L;
+        }
+    }
+    cl.sync();  // every CTA's partial is in its shared memory
+    if (rank == 0) {
+        for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
+            const uint32_t g = i / HD, d = i % HD;
+            float M = -INFINITY;
+            for (uint32_t c = 0; c < C; ++c) {
+                const float* cp = cl.map_shared_rank(cpart, c);
+                M = fmaxf(M, cp[g * (HD + 2) + HD]);
+            }
+            float L = 0.f, O = 0.f;
+            for (uint32_t c = 0; c < C; ++c) {
+                const float* cp = cl.map_shared_rank(cpart, c) + g * (HD + 2);
+                if (cp[HD] == -INFINITY) continue;
+                const float f = expf(cp[HD] - M);
+                L += cp[HD + 1] * f;
+                O += cp[d] * f;
+            }
+            if (valid && !bad_sh) a.out[(uint64_t)(kvh * G + g) * HD + d] = O / L;
+        }
+    }
+    cl.sync();  // the partials stay in place until rank 0 has read them
+}
+
+template <typename KV, int G, int HD>
+cudaError_t launch_t(const ClusterAttn& F, cudaStream_t s, bool pdl) {
+    const size_t smem = cluster_smem(F.ring_pages, F.a.kv.page_size, HD, sizeof(KV), G);
+    static std::atomic<int> attr_done[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_cluster_kernel<KV, G, HD>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
+        if (e != cudaSuccess) return e;
+        attr_done[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(F.a.kv_heads * F.a.nsplit);
+    cfg.blockDim = dim3(kAW * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = F.a.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<KV, G, HD>, F);
+}
+
+template <typename KV, int HD>
+cudaError_t launch_hd(const ClusterAttn& F, uint32_t G, cudaStream_t s, bool pdl) {
+    switch (G) {
+        case 1: return launch_t<KV, 1, HD>(F, s, pdl);
+        case 2: return launch_t<KV, 2, HD>(F, s, pdl);
+        case 4: return launch_t<KV, 4, HD>(F, s, pdl);
+        default: return launch_t<KV, 8, HD>(F, s, pdl);
+    }
+}
+
+}  // namespace
+
+uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t page_size, uint32_t head_dim,
+                                 uint32_t elem_bytes, uint32_t group) {
+    if (!nsplit || nsplit > 8 || (nsplit & (nsplit - 1)) || !page_size) return 0;
+    if (head_dim != 64 && head_dim != 128) return 0;
+    if (group != 1 && group != 2 && group != 4 && group != 8) return 0;
+    if (elem_bytes != 2 && elem_bytes != 4) return 0;
+    // a split holds at most ceil(ceil(t / nsplit) / page) pages
+    const uint32_t need = (max_pages + nsplit - 1) / nsplit + 1;
+    if (need > kMaxRingPages || cluster_smem(need, page_size, head_dim, elem_bytes, group) > kSmemCap) return 0;
+    return need;
+}
+
+cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
+                                     bool pdl) {
+    if (a.batch != 1 || r.batch != 1 || !a.out || !a.pos || r.pos != a.pos || !ring_pages) return cudaErrorInvalidValue;
+    const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
+    if (!a.kv_heads || a.heads % a.kv_heads ||
+        attention_cluster_pages(1, a.nsplit, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G) == 0)
+        return cudaErrorInvalidValue;
+    if (cluster_smem(ring_pages, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G) > kSmemCap)
+        return cudaErrorInvalidValue;
+    ClusterAttn F;
+    F.r = r;
+    F.a = a;
+    F.ring_pages = ring_pages;
+    const bool f16 = a.kv.elem_bytes == 2;
+    if (a.head_dim == 128) return f16 ? launch_hd<__half, 128>(F, G, s, pdl) : launch_hd<float, 128>(F, G, s, pdl);
+    return f16 ? launch_hd<__half, 64>(F, G, s, pdl) : launch_hd<float, 64>(F, G, s, pdl);
+}
+
+}  // namespace evl

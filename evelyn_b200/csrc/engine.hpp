@@ -211,8 +211,7 @@ struct StepBuffers {
     DeviceBuffer kv, page_table, pos, tokens, argmax, hist, err;
     DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
     DeviceBuffer gbx, gxinv, gpart, gpart2;  // batched products: staged x, 2^-e, partial sums
-    DeviceBuffer kvdone;                      // fused attention: per kv head split counters
-    uint32_t nsplit_fused = 0;                // splits of the fused single-sequence attention (0: off)
+    uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
     uint32_t nsplit = 1, amax_parts = 1;
     PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;
 };

@@ -96,9 +96,14 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // Single sequence: QK-norm + RoPE + append, split-K attention and the split merge in one
-// launch (step_kernel.cu); kv_done is [kv_heads] zeroed counters, left zeroed.
-cudaError_t launch_attention_fused(const RopeArgs& r, const AttnArgs& a, unsigned int* kv_done, cudaStream_t s,
-                                   bool pdl);
+// launch of one thread-block cluster of a.nsplit (1, 2, 4 or 8) CTAs per kv head
+// (attention_cluster.cu); each CTA stages its split's pages in a shared ring of
+// `ring_pages` pages. attention_cluster_pages: the ring a cache of max_pages pages
+// per sequence needs, 0 when this path does not apply.
+uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t page_size, uint32_t head_dim,
+                                 uint32_t elem_bytes, uint32_t group);
+cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
+                                     bool pdl);
 
 // ---------------------------------------------------------------- step_kernel.cu
 // One decoder layer of a single-sequence step, as the separate launches would run it:

@@ -286,110 +286,150 @@ __device__ __forceinline__ void pack_limbs(int m0, int m1, int m2, int m3, uint3
     w2 = __byte_perm(__byte_perm(t0, t1, 0x0062), __byte_perm(t2, t3, 0x0062), 0x5410);  // byte 2 of each
 }
 
+// One 16-value quarter hb of the (normalised) input, held in v: block scale, limbs,
+// sums, and the writes of the staged layouts. All lanes of the warp call it (the
+// block maximum and sum meet by shuffle); `on` is uniform per lane pair.
+__device__ __forceinline__ void stage_quarter(const Plan& p, uint8_t* xs, uint32_t hb, bool on, const float (&v)[16]) {
+    if (on && p.a.x_out && blockIdx.x == 0) {
+        float4* op = reinterpret_cast<float4*>(p.a.x_out + 16 * hb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) op[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    // |x| bit patterns order like the values; the biased exponent E of the block
+    // maximum puts it in [2^(E-127), 2^(E-126)), i.e. frexp's e = E - 126, and
+    // s = 22 - e keeps |m| <= 2^22
+    uint32_t abits = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) abits = max(abits, __float_as_uint(v[e]) & 0x7fffffffu);
+    abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
+    const int s = abits ? min(max(148 - (int)(abits >> 23), -100), 120) : 0;
+    // 2^s and 2^-s are normal floats for s in [-100, 120]: the scaling is exact
+    const float up = __uint_as_float((uint32_t)(s + 127) << 23);
+    int m[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) m[e] = __float2int_rn(__fmul_rn(v[e], up));
+    uint32_t L0[4], L1[4], L2[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
+    const uint32_t j = hb >> 1, h = hb & 1, u = hb >> 2, part = (hb >> 1) & 1;
+    const float fs = __uint_as_float((uint32_t)(127 - s) << 23);
+    if (p.need & NEED_XSUM) {  // sum of the staged (quantised) block: exact in int32
+        int sm = 0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) sm += m[e];
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        if (on && h == 0) reinterpret_cast<float*>(xs + p.off_xsum)[j] = __fmul_rn((float)sm, fs);
+    }
+    if (!on) return;
+    if (h == 0) reinterpret_cast<float*>(xs + p.off_fscale)[j] = fs;
+    uint8_t* b = xs + u * kXUnit + part * 96 + h * 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        *reinterpret_cast<uint32_t*>(b + e * 8) = L0[e];
+        *reinterpret_cast<uint32_t*>(b + 32 + e * 8) = L1[e];
+        *reinterpret_cast<uint32_t*>(b + 64 + e * 8) = L2[e];
+    }
+    if (p.need & NEED_MSUM) {  // per quarter: limb sums for the Q6_K -32 offset, as the lanes combine them
+        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            s0 = dp4a((int)L0[q], 0x01010101, s0);
+            s1 = dp4a((int)L1[q], 0x01010101, s1);
+            s2 = dp4a((int)L2[q], 0x01010101, s2);
+        }
+        int* ms = reinterpret_cast<int*>(xs + p.off_msum) + u * 8 + part * 4 + h;  // [u][t = 2 part + (limb 2)][h]
+        ms[0] = s0 + 256 * s1;
+        ms[2] = s2;
+    }
+}
+
+__device__ __forceinline__ void load_quarter(const float* x, uint32_t hb, bool on, float (&v)[16]) {
+    if (on) {
+        const float4* xp = reinterpret_cast<const float4*>(x + 16 * hb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 t = __ldcg(xp + q);
+            v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = 0.f;
+    }
+}
+__device__ __forceinline__ void load_weights(const float* w, uint32_t hb, bool on, float (&g)[16]) {
+    if (on) {
+        const float4* gp = reinterpret_cast<const float4*>(w + 16 * hb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 t = gp[q];
+            g[4 * q] = t.x; g[4 * q + 1] = t.y; g[4 * q + 2] = t.z; g[4 * q + 3] = t.w;
+        }
+    }
+}
+__device__ __forceinline__ float sum_sq(const float (&v)[16]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss += v[e] * v[e];
+    return ss;
+}
+__device__ __forceinline__ void apply_norm(float (&v)[16], const float (&g)[16], float inv) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], inv), g[e]);
+}
+
+// Called by the consumer threads after griddepcontrol.wait. Rows of up to 1024
+// quarters (16384 values) are read once into registers, the norm weights in the same
+// round trip; longer rows take a second pass for the normalisation.
 __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, float* red) {
     const MatvecArgs& a = p.a;
-    const uint32_t K = a.cols, nq = K / 16;
+    const uint32_t K = a.cols, nq = K / 16, per = kCW * 32;
     const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
-    float inv = 1.f;
-    if (a.norm_w) {
-        float ss = 0.f;
-        for (uint32_t hb = c; hb < nq; hb += kCW * 32) {
-            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 v = __ldcg(xp + q);
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            }
-        }
+    auto block_inv = [&](float ss) {
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         named_sync(kConsumerBarrier, kCW * 32);
         ss = 0.f;
 #pragma unroll
         for (int w = 0; w < kCW; ++w) ss += red[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-    }
-    uint8_t* xb = xs;
-    float* fscale = reinterpret_cast<float*>(xs + p.off_fscale);
-    float* xsum = reinterpret_cast<float*>(xs + p.off_xsum);
-    int* msum = reinterpret_cast<int*>(xs + p.off_msum);
-    // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
-    for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nq; hb0 += kCW * 32) {
-        const uint32_t hb = hb0 + lane;
-        const bool on = hb < nq;  // uniform per lane pair
-        float v[16];
-        if (on) {
-            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * hb);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 t = __ldcg(xp + q);
-                v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+        return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+    };
+    if (nq <= 2 * per) {
+        // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
+        const uint32_t q0 = c, q1 = c + per;
+        const bool on0 = q0 < nq, on1 = q1 < nq, two = nq > per;
+        float v0[16], v1[16], g0[16], g1[16];
+        load_quarter(a.x, q0, on0, v0);
+        if (two) load_quarter(a.x, q1, on1, v1);
+        if (a.norm_w) {
+            load_weights(a.norm_w, q0, on0, g0);
+            if (two) load_weights(a.norm_w, q1, on1, g1);
+            const float inv = block_inv(sum_sq(v0) + (two ? sum_sq(v1) : 0.f));
+            if (on0) apply_norm(v0, g0, inv);
+            if (two && on1) apply_norm(v1, g1, inv);
+        }
+        stage_quarter(p, xs, q0, on0, v0);
+        if (two) stage_quarter(p, xs, q1, on1, v1);
+    } else {
+        float inv = 1.f;
+        if (a.norm_w) {
+            float ss = 0.f;
+            for (uint32_t hb = c; hb < nq; hb += per) {
+                float v[16];
+                load_quarter(a.x, hb, true, v);
+                ss += sum_sq(v);
             }
+            inv = block_inv(ss);
+        }
+        for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nq; hb0 += per) {
+            const uint32_t hb = hb0 + lane;
+            const bool on = hb < nq;  // uniform per lane pair
+            float v[16], g[16];
+            load_quarter(a.x, hb, on, v);
             if (a.norm_w) {
-                const float4* gp = reinterpret_cast<const float4*>(a.norm_w + 16 * hb);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 g = gp[q];
-                    v[4 * q] = __fmul_rn(__fmul_rn(v[4 * q], inv), g.x);
-                    v[4 * q + 1] = __fmul_rn(__fmul_rn(v[4 * q + 1], inv), g.y);
-                    v[4 * q + 2] = __fmul_rn(__fmul_rn(v[4 * q + 2], inv), g.z);
-                    v[4 * q + 3] = __fmul_rn(__fmul_rn(v[4 * q + 3], inv), g.w);
-                }
+                load_weights(a.norm_w, hb, on, g);
+                if (on) apply_norm(v, g, inv);
             }
-            if (a.x_out && blockIdx.x == 0) {
-                float4* op = reinterpret_cast<float4*>(a.x_out + 16 * hb);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) op[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = 0.f;
-        }
-        // |x| bit patterns order like the values; the biased exponent E of the block
-        // maximum puts it in [2^(E-127), 2^(E-126)), i.e. frexp's e = E - 126, and
-        // s = 22 - e keeps |m| <= 2^22
-        uint32_t abits = 0;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) abits = max(abits, __float_as_uint(v[e]) & 0x7fffffffu);
-        abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
-        const int s = abits ? min(max(148 - (int)(abits >> 23), -100), 120) : 0;
-        // 2^s and 2^-s are normal floats for s in [-100, 120]: the scaling is exact
-        const float up = __uint_as_float((uint32_t)(s + 127) << 23);
-        int m[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) m[e] = __float2int_rn(__fmul_rn(v[e], up));
-        uint32_t L0[4], L1[4], L2[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
-        const uint32_t j = hb >> 1, h = hb & 1, u = hb >> 2, part = (hb >> 1) & 1;
-        const float fs = __uint_as_float((uint32_t)(127 - s) << 23);
-        if (p.need & NEED_XSUM) {  // sum of the staged (quantised) block: exact in int32
-            int sm = 0;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) sm += m[e];
-            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-            if (on && h == 0) xsum[j] = __fmul_rn((float)sm, fs);
-        }
-        if (!on) continue;
-        if (h == 0) fscale[j] = fs;
-        uint8_t* b = xb + u * kXUnit + part * 96 + h * 4;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            *reinterpret_cast<uint32_t*>(b + e * 8) = L0[e];
-            *reinterpret_cast<uint32_t*>(b + 32 + e * 8) = L1[e];
-            *reinterpret_cast<uint32_t*>(b + 64 + e * 8) = L2[e];
-        }
-        if (p.need & NEED_MSUM) {  // per quarter: limb sums for the Q6_K -32 offset, as the lanes combine them
-            int s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                s0 = dp4a((int)L0[q], 0x01010101, s0);
-                s1 = dp4a((int)L1[q], 0x01010101, s1);
-                s2 = dp4a((int)L2[q], 0x01010101, s2);
-            }
-            int* ms = msum + u * 8 + part * 4 + h;  // [u][t = 2 part + (limb 2)][h]
-            ms[0] = s0 + 256 * s1;
-            ms[2] = s2;
+            stage_quarter(p, xs, hb, on, v);
         }
     }
     named_sync(kConsumerBarrier, kCW * 32);

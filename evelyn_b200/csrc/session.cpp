@@ -102,14 +102,16 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     const uint32_t by_len = batch > 1 ? (b.pages_per_seq + 31) / 32 : 1;
     b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
-    {  // one sequence: attention with QK-norm/RoPE/append and the merge in one launch
+    {  // one sequence: attention with QK-norm/RoPE/append and the merge in one cluster launch
         const char* fe = std::getenv("EVELYN_FUSED_ATTN");
         if (batch == 1 && !(fe && fe[0] == '0')) {
-            b.nsplit_fused = std::max<uint32_t>(
-                1, std::min<uint32_t>((uint32_t)sms / std::max<uint32_t>(1, m->lkv_heads), b.pages_per_seq));
-            b.nsplit_fused = std::min(b.nsplit_fused, b.nsplit);
-            b.kvdone.alloc(std::max<uint64_t>(4, (uint64_t)m->lkv_heads * 4));
-            cuda_check(cudaMemset(b.kvdone.p, 0, b.kvdone.bytes), "memset");
+            const uint32_t C = 8;
+            const uint32_t ring = attention_cluster_pages(b.pages_per_seq, C, kPageSize, (uint32_t)hd, (uint32_t)elem,
+                                                          m->lheads / std::max<uint32_t>(1, m->lkv_heads));
+            if (ring) {
+                b.cluster_splits = C;
+                b.cluster_ring = ring;
+            }
         }
     }
     b.amax_parts = (uint32_t)sms;
@@ -319,9 +321,8 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         matvec_each(qkv_args(li), B, c.dim, ys, stream, pdl, "qkv matvec");
         kernels += B;
     }
-    if (b.nsplit_fused) {
-        cuda_check(launch_attention_fused(rope_args(li), attn_args(li, b.nsplit_fused), b.kvdone.as<unsigned int>(),
-                                          stream, pdl),
+    if (b.cluster_ring) {
+        cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream, pdl),
                    "attention");
         kernels += 1;
     } else {
@@ -563,7 +564,6 @@ void Decoder::check_device_error() {
     *b.h_err.as<int>() = 0;
     cudaMemsetAsync(b.err.p, 0, 4, stream);
     if (step_k) step_kernel_reset(step_k, stream);
-    if (b.kvdone.p) cudaMemsetAsync(b.kvdone.p, 0, b.kvdone.bytes, stream);
     cudaStreamSynchronize(stream);
     switch (e) {
         case DEV_ERR_TOKEN: raise(EVL_ERR_INVALID_INPUT, "token ID outside the model vocabulary");

@@ -491,26 +491,6 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     }
 }
 
-// Standalone single-sequence attention for the launch sequence: QK-norm + RoPE + KV
-// append + split-K GQA attention + split merge in one launch (replaces
-// qk_norm_rope_append, attention_split and attention_combine for batch 1). One CTA of
-// 16 warps per (kv head, split).
-__global__ void __launch_bounds__(kCW * 32) attention_fused_kernel(const __grid_constant__ AttnPhase P,
-                                                                    unsigned int* kv_done) {
-    extern __shared__ __align__(16) float scr_f[];
-    __shared__ int flag_sh;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    pdl_wait();
-    const int32_t pos = __ldcg(P.rope.pos);
-    if (pos < 0 || (uint32_t)pos / P.at.kv.page_size >= P.at.max_pages) {
-        if (blockIdx.x == 0 && tid == 0) atomicExch(P.at.err, DEV_ERR_POSITION);
-        return;
-    }
-    if (P.at.head_dim == 128) attn_phase_hd<128>(P, kv_done, pos, scr_f, &flag_sh, warp, lane, tid);
-    else attn_phase_hd<64>(P, kv_done, pos, scr_f, &flag_sh, warp, lane, tid);
-    pdl_launch_dependents();
-}
-
 // Shared scratch one attention item needs (see attn_item).
 size_t attn_scratch_bytes(uint32_t G, uint32_t hd) {
     return 4ull * (2 * (G + 1) * hd + (G + 1) * (hd / 32) + 2 * kAttnWarps * G + (size_t)kAttnWarps * G * hd);
@@ -519,39 +499,6 @@ size_t attn_scratch_bytes(uint32_t G, uint32_t hd) {
 std::atomic<int> g_attr_done[64];
 
 }  // namespace
-
-cudaError_t launch_attention_fused(const RopeArgs& r, const AttnArgs& a, unsigned int* kv_done, cudaStream_t s,
-                                   bool pdl) {
-    if (a.batch != 1 || r.batch != 1 || !kv_done || !a.part || !a.out || !a.nsplit || r.pos != a.pos || !a.pos)
-        return cudaErrorInvalidValue;
-    if (a.head_dim != 64 && a.head_dim != 128) return cudaErrorInvalidValue;
-    const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
-    if (!a.kv_heads || a.heads % a.kv_heads || (G != 1 && G != 2 && G != 4 && G != 8)) return cudaErrorInvalidValue;
-    AttnPhase P;
-    P.rope = r;
-    P.at = a;
-    const size_t smem = attn_scratch_bytes(G, a.head_dim);
-    static std::atomic<int> attr_done[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attention_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)std::max<size_t>(smem, 48 * 1024));
-        if (e != cudaSuccess) return e;
-        attr_done[dev] = 1;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads * a.nsplit);
-    cfg.blockDim = dim3(kCW * 32);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attention_fused_kernel, P, kv_done);
-}
 
 struct StepKernel {
     StepArgs args{};
