@@ -43,7 +43,9 @@ constexpr int kXUnit = 192;            // staged B-fragment bytes of one unit
 constexpr int kMaxStages = 8;
 constexpr uint32_t kSmemBudget = 225 * 1024;
 constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the consumer threads
-constexpr uint32_t kRedBytes = 2 * kSbWarps * kRB * 4;  // double-buffered row-block partials
+constexpr uint32_t kRedBufs = kMaxStages + 1;            // row-block partial buffers (> stages)
+constexpr uint32_t kRedBufBytes = kSbWarps * kRB * 4;
+constexpr uint32_t kRedBytes = kRedBufs * kRedBufBytes + 16 * kRedBufs;  // + arrival counters
 static_assert(kSbWarps * 4 == kPanelUnits, "each consumer warp of a slab takes one super-block of a panel");
 
 // need bits
@@ -53,7 +55,7 @@ constexpr uint32_t NEED_XSUM = 1, NEED_MSUM = 2;
 struct Plan {
     MatvecArgs a;
     uint32_t rb_begin[kMaxSegs + 1];  // first row-block of each segment (+ total)
-    uint32_t nunits, ngroups;
+    uint32_t nunits, ngroups, last_units;  // units per row, panels per row, units of the last panel
     uint32_t item_bytes;  // largest stage (two slabs x one 32-unit panel) of any segment
     uint32_t need;
     uint32_t off_fscale, off_xsum, off_msum, off_red;  // offsets in the staged-input area (B fragments at 0)
@@ -432,6 +434,7 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
             stage_quarter(p, xs, hb, on, v);
         }
     }
+    if (c < kRedBufs) reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes)[c] = 0u;
     named_sync(kConsumerBarrier, kCW * 32);
 }
 
@@ -472,16 +475,30 @@ __device__ __forceinline__ void issue_item(const Plan& p, const Ring& r, uint32_
     if (n == 2) tma_load_1d(slot + sb, b, sb, &r.full[s]);
 }
 
-// Producer (one thread): stream row blocks [rb0, rb1) of `p`, one 32-unit column group
-// per stage, continuing the ring sequence at `item`. Returns false after an abort.
-__device__ bool produce_items(const Plan& p, const Ring& r, uint32_t rb0, uint32_t rb1, uint32_t& item,
+// Position in the ring sequence: items issued (or consumed) so far, the slot, and the
+// parity of the slot's current lap.
+struct RingPos {
+    uint32_t n = 0, s = 0, par = 0;
+    __device__ __forceinline__ void advance(uint32_t stages) {
+        ++n;
+        if (++s == stages) {
+            s = 0;
+            par ^= 1;
+        }
+    }
+};
+
+// Producer (one thread): stream row blocks [rb0, rb1) of `p`, one 32-unit panel of the
+// row block's slabs per stage, continuing the ring sequence at `rp`. Returns false
+// after an abort.
+__device__ bool produce_items(const Plan& p, const Ring& r, uint32_t rb0, uint32_t rb1, RingPos& rp,
                               volatile int* abort_flag) {
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
-        for (uint32_t g = 0; g < p.ngroups; ++g, ++item) {
-            const uint32_t s = item % r.stages, n = item / r.stages;
-            if (n > 0 && !wait_or_abort(&r.empty[s], (n - 1) & 1, abort_flag)) return false;
+        for (uint32_t g = 0; g < p.ngroups; ++g, rp.advance(r.stages)) {
+            // a slot's lap L >= 1 waits for the consumers' release of lap L - 1
+            if (rp.n >= r.stages && !wait_or_abort(&r.empty[rp.s], rp.par ^ 1, abort_flag)) return false;
             if (*abort_flag) return false;
-            issue_item(p, r, rb, g, s);
+            issue_item(p, r, rb, g, rp.s);
         }
     }
     return true;
@@ -506,79 +523,99 @@ __device__ void drain_ring(const Ring& r, uint32_t item) {
     for (uint32_t s = 0; s < r.stages && s < item; ++s) mbar_wait(&r.full[s], ((item - 1 - s) / r.stages) & 1);
 }
 
-// Consumers (all kCW warps): dot products of row blocks [rb0, rb1) against the staged
-// input `xs`; warp (slab w / 8, super-block w % 8) of every stage. At the end of a row
-// block the eight partial sums of each row meet in shared memory (fixed order) and
-// warp 0 runs the epilogue. Returns false after an abort (every consumer warp returns
-// at the same stage, before the row block's barrier).
-__device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_t rb0, uint32_t rb1,
-                              uint32_t& item, int warp, int lane, volatile int* abort_flag) {
+// One consumer warp's part of a row block of type T: for every panel, super-block
+// `sbw` of slab `slab` (or the Q8_0 units of it). Returns false after an abort.
+template <uint32_t T>
+__device__ __forceinline__ bool consume_rows(const Plan& p, const Ring& r, const uint8_t* xs, RingPos& rp,
+                                             uint32_t slab, uint32_t sbw, const Lane& L, int lane,
+                                             volatile int* abort_flag, float& acc0, float& acc1) {
+    constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q6_K ? 840u : 1088u;
     const uint8_t* xb = xs;
     const float* fscale = reinterpret_cast<const float*>(xs + p.off_fscale);
-    const float* xsum = reinterpret_cast<const float*>(xs + p.off_xsum);
-    const int* msum = reinterpret_cast<const int*>(xs + p.off_msum);
+    // limb weight of this lane's D columns (and the 16x of Q4_K high nibbles)
+    const float wt = ((L.t & 1) ? 65536.f : 1.f) * ((T == GGML_Q4_K && L.part) ? 0.0625f : 1.f);
+    for (uint32_t g = 0; g < p.ngroups; ++g, rp.advance(r.stages)) {
+        if (!wait_or_abort(&r.full[rp.s], rp.par, abort_flag)) return false;
+        const uint32_t U = g + 1 == p.ngroups ? p.last_units : kPanelUnits, ub = 4 * sbw;
+        // rows past the end were not copied: their slots hold stale bytes whose
+        // (finite) results are discarded by the epilogue
+        const uint8_t* q = r.base + rp.s * r.slot_bytes + slab * U * u16 + ub * u16;
+        const uint32_t u0 = g * kPanelUnits + ub;
+        if (ub < U) {
+            if constexpr (T == GGML_Q4_K) {
+                sb_q4k(q, u0, xb, fscale, reinterpret_cast<const float*>(xs + p.off_xsum), L, lane, wt, acc0, acc1);
+            } else if constexpr (T == GGML_Q6_K) {
+                sb_q6k(q, u0, xb, fscale, reinterpret_cast<const int*>(xs + p.off_msum), L, lane, wt, acc0, acc1);
+            } else {
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i)
+                    if (ub + i < U) unit_q8_0(q + i * 1088, u0 + i, xb, fscale, L, lane, wt, acc0, acc1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[rp.s]);
+    }
+    return true;
+}
+
+// Consumers (all kCW warps): dot products of row blocks [rb0, rb1) against the staged
+// input `xs`; warp (slab w / 8, super-block w % 8) of every stage. At the end of a row
+// block each warp parks its partial sums of the block's rows in one of kRedBufs
+// shared buffers and the last warp to arrive adds the eight partials of each row in
+// warp order and runs the epilogue -- no CTA-wide barrier. (A warp is at most
+// `stages` items, so at most `stages` row blocks, ahead of the slowest one, and
+// stages < kRedBufs, so a buffer is reused only after its last reader is done.)
+// Returns false after an abort (every consumer warp returns at the same stage).
+__device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_t rb0, uint32_t rb1, RingPos& rp,
+                              int warp, int lane, volatile int* abort_flag) {
     float* red = reinterpret_cast<float*>(xs + p.off_red);
+    unsigned* cnt = reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes);
     const Lane L = make_lane(lane);
     const uint32_t slab = (uint32_t)warp / kSbWarps, sbw = (uint32_t)warp % kSbWarps;
-    uint32_t buf = 0;
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
         const int si = seg_of(p, rb);
         const MatvecSeg& sg = p.a.seg[si];
         const uint32_t local = rb - p.rb_begin[si];
-        const uint32_t T = sg.m.type;
-        const bool dual = sg.epi == EPI_SWIGLU;
-        // limb weight of this lane's D columns (and the 16x of Q4_K high nibbles)
-        const float wt = ((L.t & 1) ? 65536.f : 1.f) * ((T == GGML_Q4_K && L.part) ? 0.0625f : 1.f);
         float acc0 = 0.f, acc1 = 0.f;  // rows g8 and g8 + 8 of this warp's slab
-        for (uint32_t g = 0; g < p.ngroups; ++g, ++item) {
-            const uint32_t s = item % r.stages, n = item / r.stages;
-            if (!wait_or_abort(&r.full[s], n & 1, abort_flag)) return false;
-            const uint32_t U = group_units(p.nunits, g), ub = 4 * sbw;
-            // rows past the end were not copied: their slots hold stale bytes whose
-            // (finite) results are discarded below
-            const uint8_t* pan = r.base + s * r.slot_bytes + slab * panel_bytes(T, U);
-            if (ub < U) {
-                const uint32_t u0 = g * kPanelUnits + ub;
-                if (T == GGML_Q4_K) {
-                    sb_q4k(pan + sbw * 2304, u0, xb, fscale, xsum, L, lane, wt, acc0, acc1);
-                } else if (T == GGML_Q6_K) {
-                    sb_q6k(pan + sbw * 3360, u0, xb, fscale, msum, L, lane, wt, acc0, acc1);
-                } else {
-#pragma unroll
-                    for (uint32_t i = 0; i < 4; ++i)
-                        if (ub + i < U) unit_q8_0(pan + (ub + i) * 1088, u0 + i, xb, fscale, L, lane, wt, acc0, acc1);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&r.empty[s]);
+        bool ok;
+        switch (sg.m.type) {
+            case GGML_Q4_K: ok = consume_rows<GGML_Q4_K>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1); break;
+            case GGML_Q6_K: ok = consume_rows<GGML_Q6_K>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1); break;
+            default: ok = consume_rows<GGML_Q8_0>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1);
         }
+        if (!ok) return false;
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        const uint32_t buf = (rb - rb0) % kRedBufs;
         float* rd = red + buf * (kSbWarps * kRB);
         if (L.t == 0) {
             rd[sbw * kRB + slab * kSlabRows + L.g8] = acc0;
             rd[sbw * kRB + slab * kSlabRows + L.g8 + 8] = acc1;
         }
-        named_sync(kConsumerBarrier, kCW * 32);
-        if (warp == 0) {  // lane = row slot of the block
-            float v = 0.f;
+        __threadfence_block();
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) last = atomicAdd(cnt + buf, 1u) == (unsigned)(kCW - 1);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence_block();
+        float v = 0.f;  // lane = row slot of the block
 #pragma unroll
-            for (int w = 0; w < kSbWarps; ++w) v += rd[w * kRB + lane];
-            if (dual) {
-                const float up = __shfl_down_sync(0xffffffffu, v, kSlabRows);
-                const uint32_t row = local * kSlabRows + lane;
-                if (lane < (int)kSlabRows && row < sg.m.rows) sg.y[row] = __fmul_rn(silu(v), up);
-            } else {
-                const uint32_t row = local * kRB + lane;
-                if (row < sg.m.rows) {
-                    if (sg.epi == EPI_ADD) sg.y[row] = __ldcg(sg.y + row) + v;
-                    else sg.y[row] = v;
-                }
+        for (int w = 0; w < kSbWarps; ++w) v += rd[w * kRB + lane];
+        if (lane == 0) cnt[buf] = 0u;
+        if (sg.epi == EPI_SWIGLU) {
+            const float up = __shfl_down_sync(0xffffffffu, v, kSlabRows);
+            const uint32_t row = local * kSlabRows + lane;
+            if (lane < (int)kSlabRows && row < sg.m.rows) sg.y[row] = __fmul_rn(silu(v), up);
+        } else {
+            const uint32_t row = local * kRB + lane;
+            if (row < sg.m.rows) {
+                if (sg.epi == EPI_ADD) sg.y[row] = __ldcg(sg.y + row) + v;
+                else sg.y[row] = v;
             }
         }
-        buf ^= 1;
     }
     return true;
 }
@@ -596,6 +633,7 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
     p.err = a.err;
     p.nunits = a.cols / 64;
     p.ngroups = (p.nunits + 31) / 32;
+    p.last_units = group_units(p.nunits, p.ngroups - 1);
     uint32_t slot = 0;
     p.rb_begin[0] = 0;
     for (int i = 0; i < kMaxSegs; ++i) {

@@ -35,17 +35,17 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
 
     if (warp == kCW) {  // producer: needs nothing from the previous kernel
         if (lane != 0) return;
-        uint32_t item = 0;
-        if (produce_items(p, r, rb0, rb1, item, &abort_flag)) prefetch_next(p, blockIdx.x, gridDim.x);
-        if (abort_flag) drain_ring(r, item);
+        RingPos rp;
+        if (produce_items(p, r, rb0, rb1, rp, &abort_flag)) prefetch_next(p, blockIdx.x, gridDim.x);
+        if (abort_flag) drain_ring(r, rp.n);
         return;
     }
 
     pdl_wait();
     stage_input(p, xs, warp, lane, red);
     pdl_launch_dependents();
-    uint32_t item = 0;
-    if (!consume_items(p, r, xs, rb0, rb1, item, warp, lane, &abort_flag) && lane == 0)
+    RingPos rp;
+    if (!consume_items(p, r, xs, rb0, rb1, rp, warp, lane, &abort_flag) && lane == 0)
         atomicExch(p.err, DEV_ERR_WAIT_TIMEOUT);
 }
 

@@ -436,26 +436,25 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             prefetch_item(A, f);
             fv = cursor_next(A, f);
         }
-        uint32_t item = 0;
+        RingPos rp;
         while (cv) {
-            const uint32_t s = item % A.stages, n = item / A.stages;
-            if (n > 0 && !wait_or_abort(&empty[s], (n - 1) & 1, &abort_flag)) break;
+            if (rp.n >= A.stages && !wait_or_abort(&empty[rp.s], rp.par ^ 1, &abort_flag)) break;
             if (abort_flag) break;
-            issue_item(A.phases[c.ph].mv, ring, c.rb, c.g, s);
-            ++item;
+            issue_item(A.phases[c.ph].mv, ring, c.rb, c.g, rp.s);
+            rp.advance(A.stages);
             cv = cursor_next(A, c);
             if (fv) {
                 prefetch_item(A, f);
                 fv = cursor_next(A, f);
             }
         }
-        if (abort_flag) drain_ring(ring, item);
+        if (abort_flag) drain_ring(ring, rp.n);
         return;
     }
 
     // consumers
     const int tc = tid;
-    uint32_t item = 0;
+    RingPos rp;
     bool ok = true;
     for (uint32_t ph = 0; ph < A.nphases && ok; ++ph) {
         if (ph > 0 && !grid_sync(A, bar_base + (unsigned long long)ph * gridDim.x, tc, &abort_flag, &ok_sh)) {
@@ -467,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             stage_input(P.mv, xs, warp, lane, red);
             uint32_t rb0, rb1;
             cta_rows(P.mv, blockIdx.x, gridDim.x, rb0, rb1);
-            if (!consume_items(P.mv, ring, xs, rb0, rb1, item, warp, lane, &abort_flag)) ok = false;
+            if (!consume_items(P.mv, ring, xs, rb0, rb1, rp, warp, lane, &abort_flag)) ok = false;
         } else {
             const int32_t pos = __ldcg(P.att.rope.pos);
             if (pos < 0 || (uint32_t)pos / P.att.at.kv.page_size >= P.att.at.max_pages) {
