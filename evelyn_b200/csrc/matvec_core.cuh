@@ -46,6 +46,7 @@ constexpr uint32_t kConsumerBarrier = 1;  // named barrier of the consumer threa
 constexpr uint32_t kRedBufs = kMaxStages + 1;            // row-block partial buffers (> stages)
 constexpr uint32_t kRedBufBytes = kSbWarps * kRB * 4;
 constexpr uint32_t kRedBytes = kRedBufs * kRedBufBytes + 16 * kRedBufs;  // + arrival counters
+constexpr uint32_t kRowBuf = 256;  // residual rows a CTA keeps in shared memory
 static_assert(kSbWarps * 4 == kPanelUnits, "each consumer warp of a slab takes one super-block of a panel");
 
 // need bits
@@ -59,6 +60,7 @@ struct Plan {
     uint32_t item_bytes;  // largest stage (two slabs x one 32-unit panel) of any segment
     uint32_t need;
     uint32_t off_fscale, off_xsum, off_msum, off_red;  // offsets in the staged-input area (B fragments at 0)
+    uint32_t off_rows;                                 // residual rows of this CTA (kRowBuf floats)
     uint32_t xbytes;                                   // size of the staged-input area
     const uint8_t* pf_base;  // next matrix to prefetch into L2 (optional)
     uint32_t pf_row_bytes, pf_rows;
@@ -305,11 +307,13 @@ __device__ __forceinline__ void stage_quarter(const Plan& p, uint8_t* xs, uint32
     for (int e = 0; e < 16; ++e) abits = max(abits, __float_as_uint(v[e]) & 0x7fffffffu);
     abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
     const int s = abits ? min(max(148 - (int)(abits >> 23), -100), 120) : 0;
-    // 2^s and 2^-s are normal floats for s in [-100, 120]: the scaling is exact
+    // 2^s and 2^-s are normal floats for s in [-100, 120]: the scaling is exact, and
+    // |v * 2^s| <= 2^22, so adding 1.5 * 2^23 in the same FMA leaves the integer
+    // rounded to nearest even in the low mantissa bits (= __float2int_rn(v * 2^s))
     const float up = __uint_as_float((uint32_t)(s + 127) << 23);
     int m[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) m[e] = __float2int_rn(__fmul_rn(v[e], up));
+    for (int e = 0; e < 16; ++e) m[e] = __float_as_int(__fmaf_rn(v[e], up, 12582912.0f)) - 0x4B400000;
     uint32_t L0[4], L1[4], L2[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
@@ -438,6 +442,20 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
     named_sync(kConsumerBarrier, kCW * 32);
 }
 
+
+// The residual y of a single-segment EPI_ADD plan whose CTA rows fit kRowBuf, read
+// into shared memory after griddepcontrol.wait (it was written by an earlier kernel)
+// alongside the input staging, so the row epilogue does no dependent global load.
+// Consumer thread c; visible after the staging's closing barrier.
+__device__ __forceinline__ bool rows_cached(const Plan& p, uint32_t rb0, uint32_t rb1) {
+    return p.a.nseg == 1 && p.a.seg[0].epi == EPI_ADD && (rb1 - rb0) * kRB <= kRowBuf;
+}
+__device__ __forceinline__ void prefetch_rows(const Plan& p, uint8_t* xs, uint32_t rb0, uint32_t rb1, uint32_t c) {
+    if (!rows_cached(p, rb0, rb1) || c >= (rb1 - rb0) * kRB) return;
+    const MatvecSeg& sg = p.a.seg[0];
+    const uint32_t row = rb0 * kRB + c;
+    reinterpret_cast<float*>(xs + p.off_rows)[c] = row < sg.m.rows ? __ldcg(sg.y + row) : 0.f;
+}
 
 // This CTA's row blocks [rb0, rb1) of a plan. Every CTA takes a contiguous range.
 __device__ __forceinline__ void cta_rows(const Plan& p, uint32_t cta, uint32_t ncta, uint32_t& rb0, uint32_t& rb1) {
@@ -572,6 +590,7 @@ __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_
     unsigned* cnt = reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes);
     const Lane L = make_lane(lane);
     const uint32_t slab = (uint32_t)warp / kSbWarps, sbw = (uint32_t)warp % kSbWarps;
+    const bool cached = rows_cached(p, rb0, rb1);
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
         const int si = seg_of(p, rb);
         const MatvecSeg& sg = p.a.seg[si];
@@ -612,7 +631,9 @@ __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_
         } else {
             const uint32_t row = local * kRB + lane;
             if (row < sg.m.rows) {
-                if (sg.epi == EPI_ADD) sg.y[row] = __ldcg(sg.y + row) + v;
+                if (sg.epi == EPI_ADD)
+                    sg.y[row] = (cached ? reinterpret_cast<const float*>(xs + p.off_rows)[(rb - rb0) * kRB + lane]
+                                        : __ldcg(sg.y + row)) + v;
                 else sg.y[row] = v;
             }
         }
@@ -663,6 +684,8 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
     if (p.need & NEED_MSUM) off += p.nunits * 32;
     p.off_red = (off + 15) & ~15u;
     off = p.off_red + kRedBytes;
+    p.off_rows = off;
+    off += kRowBuf * 4;
     p.xbytes = (off + 127) & ~127u;
     p.item_bytes = slot;
     if (p.xbytes + 2 * slot > kSmemBudget) return cudaErrorInvalidValue;

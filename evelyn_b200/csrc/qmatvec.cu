@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
     }
 
     pdl_wait();
+    prefetch_rows(p, xs, rb0, rb1, (uint32_t)tid);
     stage_input(p, xs, warp, lane, red);
     pdl_launch_dependents();
     RingPos rp;

@@ -463,9 +463,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         }
         const StepPhase& P = A.phases[ph];
         if (P.kind == PH_MATVEC) {
-            stage_input(P.mv, xs, warp, lane, red);
             uint32_t rb0, rb1;
             cta_rows(P.mv, blockIdx.x, gridDim.x, rb0, rb1);
+            prefetch_rows(P.mv, xs, rb0, rb1, (uint32_t)tc);
+            stage_input(P.mv, xs, warp, lane, red);
             if (!consume_items(P.mv, ring, xs, rb0, rb1, rp, warp, lane, &abort_flag)) ok = false;
         } else {
             const int32_t pos = __ldcg(P.att.rope.pos);
