@@ -391,7 +391,10 @@ evl_status evl_qmatrix_matvec(const evl_qmatrix* q, const float* d_x, float* d_y
         a.x = d_x;
         a.cols = q->m.cols;
         a.err = q->err.as<int>();
-        cuda_check(launch_qmatvec(a, as_stream(stream), false), "matvec");
+        // programmatic dependent launch on a caller's stream: the kernel streams weights
+        // while the previous kernel finishes and reads x, writes y only after
+        // griddepcontrol.wait
+        cuda_check(launch_qmatvec(a, as_stream(stream), stream != nullptr), "matvec");
     });
 }
 

@@ -159,7 +159,9 @@ evl_status evl_qmatrix_create(uint32_t ggml_type, uint32_t rows, uint32_t cols, 
 void evl_qmatrix_free(evl_qmatrix* m);
 uint64_t evl_qmatrix_bytes(const evl_qmatrix* m);
 /* y = W x (QMatrix::matvec, runtime.rs:72-88). device pointers, x 16-byte aligned;
- * stream may be NULL */
+ * stream may be NULL. On a non-NULL stream the launch may begin (streaming weights)
+ * while the stream's previous kernel finishes; it reads x and writes y only after that
+ * kernel has completed. */
 evl_status evl_qmatrix_matvec(const evl_qmatrix* m, const float* d_x, float* d_y, void* stream);
 /* QMatrix::matvec (runtime.rs:72-88) of nvec (1..32) vectors at once, as a Batch step
  * needs: d_x [nvec][cols] -> d_y [nvec][rows], on the tensor cores (the first call
