@@ -91,7 +91,7 @@ template <typename KV, int G, int HD>
 __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_constant__ ClusterAttn F) {
     constexpr int DPL = HD / 32;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full;
+    __shared__ __align__(8) uint64_t full[2];  // the two halves of the page ring
     __shared__ int bad_sh;
     cg::cluster_group cl = cg::this_cluster();
     const RopeArgs& r = F.r;
@@ -106,7 +106,8 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     float* cpart = wpart + kAW * G * (HD + 2);                                // [G][HD+2]: o, m, l
 
     if (tid == 0) {
-        mbar_init(&full, 1);
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
         fence_barrier_init();
         bad_sh = 0;
     }
@@ -120,18 +121,28 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     const uint32_t S = pos_ok ? split_len(t_all, C, ps) : 0;
     const uint32_t t0 = rank * S, t1 = pos_ok ? min(t_all, t0 + S) : 0;
     const uint32_t npg = t0 < t1 ? (t1 - t0 + ps - 1) / ps : 0;
-    const bool valid = pos_ok && npg <= F.ring_pages;  // the same in every thread
+    const bool valid = pos_ok;  // the same in every thread
     const bool last = valid && npg > 0 && t1 == t_all;  // this split holds the new position
+    // The split's pages stream through the ring in chunks of H pages, chunk c into half
+    // c & 1 (double buffering): chunks 0 and 1 are issued now, chunk c + 2 once every
+    // warp is done with chunk c.
+    const uint32_t H = F.ring_pages / 2, nch = (npg + H - 1) / H;
+    auto issue = [&](uint32_t c) {  // consumer thread 0
+        const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c & 1;
+        mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
+        for (uint32_t i = p0; i < p1; ++i) {
+            const int32_t page = __ldcg(a.page_table + t0 / ps + i);
+            KV* slot = ring + (half * H + (i - p0)) * 2 * tile;
+            tma_load_1d(slot, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full[half]);
+            tma_load_1d(slot + tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full[half]);
+        }
+    };
     if (tid == 0) {
         if (!valid) {
             atomicExch(a.err, DEV_ERR_POSITION);
-        } else if (npg) {
-            mbar_arrive_expect_tx(&full, npg * 2 * tile * (uint32_t)sizeof(KV));
-            for (uint32_t i = 0; i < npg; ++i) {
-                const int32_t page = __ldcg(a.page_table + t0 / ps + i);
-                tma_load_1d(ring + (2 * i) * tile, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full);
-                tma_load_1d(ring + (2 * i + 1) * tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full);
-            }
+        } else {
+            if (nch > 0) issue(0);
+            if (nch > 1) issue(1);
         }
     }
     // warp w < G: q head kvh*G + w; w == G: k; w == G+1: v. Lane dims d = DPL*lane + e.
@@ -207,22 +218,10 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             for (int e = 0; e < DPL; ++e) dst[DPL * lane + e] = to_kv<KV>(val[e]);
         }
     }
-    // ---- the staged pages (and the new row in the split's own copy)
-    if (valid && npg && !mbar_wait(&full, 0)) {
-        atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
-        bad_sh = 1;
-    }
-    __syncthreads();
-    const bool run = valid && npg > 0 && !bad_sh;
-    if (run && last && (warp == G || warp == G + 1)) {
-        const uint32_t li = (uint32_t)pos - t0;
-        KV* row = ring + ((li / ps) * 2 + (warp == G ? 0 : 1)) * tile + (li % ps) * HD;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) row[DPL * lane + e] = to_kv<KV>(val[e]);
-    }
-    __syncthreads();
+    __syncthreads();  // q in shared memory
 
-    // ---- online softmax over this split's positions, one per warp at a time
+    // ---- online softmax over this split's positions, chunk by chunk, one position per
+    // warp at a time, entirely out of shared memory
     float qr[G][DPL], m[G], l[G], o[G][DPL];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -234,10 +233,25 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             o[g][e] = 0.f;
         }
     }
-    if (run) {
-        for (uint32_t t = t0 + warp; t < t1; t += kAW) {
-            const uint32_t li = t - t0;
-            const KV* kp = ring + (li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
+    const uint32_t pnew = last ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
+    for (uint32_t c = 0; valid && c < nch; ++c) {
+        const uint32_t half = c & 1, p0 = c * H, p1 = min(npg, p0 + H);
+        if (!mbar_wait(&full[half], (c >> 1) & 1)) {
+            atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
+            bad_sh = 1;
+        }
+        // the new position's k and v (registers of warps G, G+1) into the split's copy
+        if (pnew >= p0 && pnew < p1 && (warp == G || warp == G + 1)) {
+            KV* row = ring + ((half * H + pnew - p0) * 2 + (warp == G ? 0 : 1)) * tile + ((uint32_t)pos % ps) * HD;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) row[DPL * lane + e] = to_kv<KV>(val[e]);
+        }
+        __syncthreads();
+        if (bad_sh) break;  // uniform after the barrier
+        const uint32_t tc0 = t0 + p0 * ps, tc1 = min(t1, t0 + p1 * ps);
+        for (uint32_t t = tc0 + warp; t < tc1; t += kAW) {
+            const uint32_t li = t - tc0;
+            const KV* kp = ring + (half * H + li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
             float kf[DPL], vf[DPL];
             load_kv<DPL>(kp, kf);
             load_kv<DPL>(kp + tile, vf);
@@ -256,6 +270,8 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 m[g] = mn;
             }
         }
+        __syncthreads();  // every warp is done with this half of the ring
+        if (tid == 0 && c + 2 < nch) issue(c + 2);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -358,15 +374,17 @@ uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t p
     if (head_dim != 64 && head_dim != 128) return 0;
     if (group != 1 && group != 2 && group != 4 && group != 8) return 0;
     if (elem_bytes != 2 && elem_bytes != 4) return 0;
-    // a split holds at most ceil(ceil(t / nsplit) / page) pages
-    const uint32_t need = (max_pages + nsplit - 1) / nsplit + 1;
-    if (need > kMaxRingPages || cluster_smem(need, page_size, head_dim, elem_bytes, group) > kSmemCap) return 0;
-    return need;
+    // a split holds at most ceil(ceil(t / nsplit) / page) pages; longer splits stream
+    // through the ring, which holds an even number of pages (two halves)
+    uint32_t ring = std::min<uint32_t>(kMaxRingPages, ((max_pages + nsplit - 1) / nsplit + 2) & ~1u);
+    while (ring > 2 && cluster_smem(ring, page_size, head_dim, elem_bytes, group) > kSmemCap) ring -= 2;
+    return cluster_smem(ring, page_size, head_dim, elem_bytes, group) <= kSmemCap ? ring : 0;
 }
 
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
                                      bool pdl) {
-    if (a.batch != 1 || r.batch != 1 || !a.out || !a.pos || r.pos != a.pos || !ring_pages) return cudaErrorInvalidValue;
+    if (a.batch != 1 || r.batch != 1 || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1))
+        return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
     if (!a.kv_heads || a.heads % a.kv_heads ||
         attention_cluster_pages(1, a.nsplit, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G) == 0)

@@ -108,9 +108,13 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             const uint32_t C = 8;
             const uint32_t ring = attention_cluster_pages(b.pages_per_seq, C, kPageSize, (uint32_t)hd, (uint32_t)elem,
                                                           m->lheads / std::max<uint32_t>(1, m->lkv_heads));
+            // EVELYN_ATTN_RING caps the ring (even, >= 2), so tests reach the streamed
+            // multi-chunk case at small contexts
+            const char* re = std::getenv("EVELYN_ATTN_RING");
+            const uint32_t cap = re ? (uint32_t)std::strtoul(re, nullptr, 10) & ~1u : 0;
             if (ring) {
                 b.cluster_splits = C;
-                b.cluster_ring = ring;
+                b.cluster_ring = cap >= 2 ? std::min(ring, cap) : ring;
             }
         }
     }

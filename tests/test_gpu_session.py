@@ -212,6 +212,27 @@ def test_load_errors():
     assert e.value.kind == "InvalidData"
 
 
+@pytest.mark.parametrize("ring", [2, 4])
+def test_cluster_attention_streamed_pages(monkeypatch, ring):
+    """Single-sequence attention with its KV pages streamed through a small shared ring
+    (many chunks per split) against the unfused three-kernel path and the oracle."""
+    spec = synth.tiny(seed=23, layers=2)
+    img, m, r = _models(spec)
+    toks = _tokens(150, spec.vocab, seed=9)
+    monkeypatch.setenv("EVELYN_ATTN_RING", str(ring))
+    s1 = evl.Session(m, max_ctx=256)
+    out1 = [s1.step(t) for t in toks]
+    monkeypatch.delenv("EVELYN_ATTN_RING")
+    monkeypatch.setenv("EVELYN_FUSED_ATTN", "0")
+    s2 = evl.Session(m, max_ctx=256)
+    out2 = [s2.step(t) for t in toks]
+    assert s1.kernels_per_step < s2.kernels_per_step  # one attention launch per layer vs three
+    assert max(float(np.abs(a - b).max()) for a, b in zip(out1, out2)) <= 1e-4
+    rs = orc.Session(r)
+    worst = max(float(np.abs(a - rs.step(t)).max()) for a, t in zip(out1, toks))
+    assert worst <= LOGIT_TOL, worst
+
+
 def test_step_kernel_matches_launch_sequence(monkeypatch):
     """The persistent layer-stack kernel (one launch per step) against the per-kernel
     launch sequence on the same model and tokens: same logits within the attention's
