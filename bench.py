@@ -405,6 +405,8 @@ def run_sweep(args):
             reps = max(1, args.reps)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            with torch.cuda.stream(stream):  # launches queue behind a device sleep: back to back
+                torch.cuda._sleep(int(20e-3 * 1.9e9))
             e0.record(stream)
             for _ in range(reps):
                 for h in mats:
@@ -417,6 +419,46 @@ def run_sweep(args):
             print(json.dumps({"kernel": "qmatvec", "case": name, "bytes": alg, "us": round(us, 2),
                               "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
                               "peak_source": peak_kind}), flush=True)
+            for h in mats:
+                lib.evl_qmatrix_free(h)
+            del mats
+    # batched products on the tensor cores: 32 vectors per call (evl_qmatrix_matmul: input
+    # staging, tcgen05 GEMM, split-K reduce; the call synchronises its stream)
+    nvec = 32
+    for rows, cols in [(4096, 4096), (4096, 12288), (12288, 4096), (151936, 4096)]:
+        for t in (synth.GGML_Q4_K, synth.GGML_Q6_K, synth.GGML_Q8_0):
+            name = f"gemm_{names[t]}_{rows}x{cols}_n{nvec}"
+            if not only or name not in only:
+                continue
+            raw = _random_raw(t, rows, cols, rng)
+            copies = max(1, -(-2 * 126 * 2**20 // raw.size))
+            mats = []
+            for i in range(copies):
+                h = C.c_void_p()
+                r = raw.copy()
+                r[7::97] ^= np.uint8(i)
+                runtime.check(lib.evl_qmatrix_create(t, rows, cols, C.c_void_p(r.ctypes.data), 0, C.byref(h)))
+                mats.append(h)
+            x = torch.randn(nvec, cols, device="cuda:0")
+            y = torch.empty(nvec, rows, device="cuda:0")
+            px, py = C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
+            for h in mats:  # builds each matrix's GEMM-layout copy
+                runtime.check(lib.evl_qmatrix_matmul(h, px, nvec, py, sp))
+            reps = max(1, args.reps)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                for h in mats:
+                    runtime.check(lib.evl_qmatrix_matmul(h, px, nvec, py, sp))
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(mats))
+            flops = 2.0 * rows * cols * nvec
+            print(json.dumps({"kernel": "qgemm (stage + gemm + reduce, synchronised call)", "case": name,
+                              "bytes": raw.size + 4 * nvec * (rows + cols), "us": round(us, 2),
+                              "tflops": round(flops / (us * 1e-6) / 1e12, 2),
+                              "gbs": round(raw.size / (us * 1e-6) / 1e9, 1)}), flush=True)
             for h in mats:
                 lib.evl_qmatrix_free(h)
             del mats
@@ -447,6 +489,8 @@ def run_sweep(args):
             reps = max(1, args.reps)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(int(20e-3 * 1.9e9))
             e0.record(stream)
             for _ in range(reps):
                 for k, v in kvs:
