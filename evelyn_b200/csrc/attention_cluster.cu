@@ -6,8 +6,9 @@
 // sincosf of pos * base^(-2i/rot_dim), K/V append (:721-722) in f16 (or f32) pages,
 // max-subtracted softmax of q.k / sqrt(hd) and the weighted sum of v (:723-766).
 //
-// Layout of the launch: one thread-block cluster of C CTAs per kv head; CTA `rank`
-// of the cluster owns positions [rank*S, (rank+1)*S) (S whole pages). Everything
+// Layout of the launch: one thread-block cluster of C CTAs per (sequence, kv head);
+// CTA `rank` of the cluster owns positions [rank*S, (rank+1)*S) (S whole pages). A
+// batch of many sequences uses C = 1 (one CTA per sequence and kv head, no merge). Everything
 // that does not come from the QKV matvec is done before griddepcontrol.wait: the
 // position and page table are read, the split's K and V page tiles are copied into
 // shared memory with TMA bulk copies, and the norm weights and RoPE sin/cos for the
@@ -96,7 +97,10 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     cg::cluster_group cl = cg::this_cluster();
     const RopeArgs& r = F.r;
     const AttnArgs& a = F.a;
-    const uint32_t C = cl.num_blocks(), rank = cl.block_rank(), kvh = blockIdx.x / C;
+    // CTA (sequence sq, kv head kvh, split rank): clusters of C consecutive CTAs
+    const uint32_t C = cl.num_blocks(), rank = cl.block_rank();
+    const uint32_t sq = blockIdx.x / (a.kv_heads * C), kvh = (blockIdx.x / C) % a.kv_heads;
+    const int32_t* ptab = a.page_table + (uint64_t)sq * a.max_pages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t ps = a.kv.page_size, tile = ps * HD;  // elements of one K (or V) page tile
     KV* ring = reinterpret_cast<KV*>(smem);                                   // [ring][K|V][ps][HD]
@@ -115,7 +119,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     pdl_launch_dependents();  // the next kernel's weight streaming may start on idle SMs
 
     // ---- before the wait: position, pages, static vectors
-    const int32_t pos = __ldcg(a.pos);
+    const int32_t pos = __ldcg(a.pos + sq);
     const bool pos_ok = pos >= 0 && (uint32_t)pos / ps < a.max_pages;
     const uint32_t t_all = pos_ok ? (uint32_t)pos + 1 : 0;
     const uint32_t S = pos_ok ? split_len(t_all, C, ps) : 0;
@@ -131,7 +135,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c & 1;
         mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
         for (uint32_t i = p0; i < p1; ++i) {
-            const int32_t page = __ldcg(a.page_table + t0 / ps + i);
+            const int32_t page = __ldcg(ptab + t0 / ps + i);
             KV* slot = ring + (half * H + (i - p0)) * 2 * tile;
             tma_load_1d(slot, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full[half]);
             tma_load_1d(slot + tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full[half]);
@@ -182,7 +186,8 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // ---- q, k, v of this kv head: norm + rope in registers
     float val[DPL];
     if (vw) {
-        const float* src = warp < G ? r.q + (uint64_t)(kvh * G + warp) * HD : (warp == G ? r.k : r.v) + (uint64_t)kvh * HD;
+        const float* src = warp < G ? r.q + ((uint64_t)sq * a.heads + kvh * G + warp) * HD
+                                    : (warp == G ? r.k : r.v) + ((uint64_t)sq * a.kv_heads + kvh) * HD;
 #pragma unroll
         for (int e = 0; e < DPL; ++e) val[e] = __ldcg(src + DPL * lane + e);
         if (normed) {
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
 #pragma unroll
             for (int e = 0; e < DPL; ++e) qs[warp * HD + DPL * lane + e] = val[e];
         } else if (last) {  // KV append at pos (src/runtime.rs:721-722)
-            const int32_t page = __ldcg(a.page_table + (uint32_t)pos / ps);
+            const int32_t page = __ldcg(ptab + (uint32_t)pos / ps);
             KV* dst = (KV*)kv_tile(a.kv, page, r.layer, warp == G ? 0 : 1, kvh) + ((uint32_t)pos % ps) * HD;
 #pragma unroll
             for (int e = 0; e < DPL; ++e) dst[DPL * lane + e] = to_kv<KV>(val[e]);
@@ -320,7 +325,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 L += cp[HD + 1] * f;
                 O += cp[d] * f;
             }
-            if (valid && !bad_sh) a.out[(uint64_t)(kvh * G + g) * HD + d] = O / L;
+            if (valid && !bad_sh) a.out[((uint64_t)sq * a.heads + kvh * G + g) * HD + d] = O / L;
         }
     }
     cl.sync();  // the partials stay in place until rank 0 has read them
@@ -340,7 +345,7 @@ cudaError_t launch_t(const ClusterAttn& F, cudaStream_t s, bool pdl) {
         attr_done[dev] = 1;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(F.a.kv_heads * F.a.nsplit);
+    cfg.gridDim = dim3(F.a.kv_heads * F.a.nsplit * F.a.batch);
     cfg.blockDim = dim3(kAW * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -369,25 +374,26 @@ cudaError_t launch_hd(const ClusterAttn& F, uint32_t G, cudaStream_t s, bool pdl
 }  // namespace
 
 uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t page_size, uint32_t head_dim,
-                                 uint32_t elem_bytes, uint32_t group) {
+                                 uint32_t elem_bytes, uint32_t group, uint32_t cap) {
     if (!nsplit || nsplit > 8 || (nsplit & (nsplit - 1)) || !page_size) return 0;
     if (head_dim != 64 && head_dim != 128) return 0;
     if (group != 1 && group != 2 && group != 4 && group != 8) return 0;
     if (elem_bytes != 2 && elem_bytes != 4) return 0;
     // a split holds at most ceil(ceil(t / nsplit) / page) pages; longer splits stream
     // through the ring, which holds an even number of pages (two halves)
-    uint32_t ring = std::min<uint32_t>(kMaxRingPages, ((max_pages + nsplit - 1) / nsplit + 2) & ~1u);
+    uint32_t ring = std::min<uint32_t>(std::min<uint32_t>(kMaxRingPages, std::max<uint32_t>(cap, 2) & ~1u),
+                                       ((max_pages + nsplit - 1) / nsplit + 2) & ~1u);
     while (ring > 2 && cluster_smem(ring, page_size, head_dim, elem_bytes, group) > kSmemCap) ring -= 2;
     return cluster_smem(ring, page_size, head_dim, elem_bytes, group) <= kSmemCap ? ring : 0;
 }
 
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
                                      bool pdl) {
-    if (a.batch != 1 || r.batch != 1 || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1))
+    if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1))
         return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
     if (!a.kv_heads || a.heads % a.kv_heads ||
-        attention_cluster_pages(1, a.nsplit, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G) == 0)
+        attention_cluster_pages(1, a.nsplit, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G, 2) == 0)
         return cudaErrorInvalidValue;
     if (cluster_smem(ring_pages, a.kv.page_size, a.head_dim, a.kv.elem_bytes, G) > kSmemCap)
         return cudaErrorInvalidValue;

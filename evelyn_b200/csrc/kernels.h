@@ -95,13 +95,13 @@ struct AttnArgs {
     int* err = nullptr;            // device error flag (DeviceError)
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
-// Single sequence: QK-norm + RoPE + append, split-K attention and the split merge in one
-// launch of one thread-block cluster of a.nsplit (1, 2, 4 or 8) CTAs per kv head
-// (attention_cluster.cu); each CTA stages its split's pages in a shared ring of
-// `ring_pages` pages. attention_cluster_pages: the ring a cache of max_pages pages
-// per sequence needs, 0 when this path does not apply.
+// QK-norm + RoPE + append, split-K attention and the split merge in one launch of one
+// thread-block cluster of a.nsplit (1, 2, 4 or 8) CTAs per (sequence, kv head)
+// (attention_cluster.cu); each CTA streams its split's pages through a shared ring of
+// `ring_pages` pages. attention_cluster_pages: the ring for a cache of max_pages pages
+// per sequence (at most cap pages), 0 when this path does not apply.
 uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t page_size, uint32_t head_dim,
-                                 uint32_t elem_bytes, uint32_t group);
+                                 uint32_t elem_bytes, uint32_t group, uint32_t cap = 16);
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
                                      bool pdl);
 

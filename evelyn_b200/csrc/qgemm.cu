@@ -45,14 +45,15 @@ namespace {
 
 constexpr uint32_t kMT = 128;          // rows per M tile (TMEM lanes)
 constexpr uint32_t kChunk = 256;       // values per K chunk
-constexpr uint32_t kGemmThreads = 320; // producer, MMA, 8 math warps
-constexpr uint32_t kMathWarps = 8;
+constexpr uint32_t kMathWarps = 16;   // four groups of four (one warp per TMEM lane quadrant)
+constexpr uint32_t kGroups = kMathWarps / 4;
+constexpr uint32_t kGemmThreads = 64 + 32 * kMathWarps;  // producer, MMA, math warps
 constexpr uint32_t kMaxStages = 4;     // weight + x stages in shared memory (as many as fit)
 constexpr uint32_t kASlots = 7;        // A operand slots in TMEM, 32 columns each
 constexpr uint32_t kTmemCols = 512;
 // TMEM column map: A slots [0, 224), min-term A 2 x 8 [224, 240), accumulator slots
 // 4 x 64 [256, 512) (per slot: the product at +0, the Q4_K min term at +32)
-constexpr uint32_t kColA = 0, kColMin = 224, kColD = 256;
+constexpr uint32_t kColA = 0, kColD = 256;
 constexpr uint32_t kDSlots = 4, kDCols = 64;
 constexpr uint32_t kLag = 2;  // accumulator spans between an MMA and its read-back
 
@@ -64,8 +65,9 @@ __host__ __device__ inline uint32_t gemm_block_bytes(uint32_t type) {
         default: return 0;
     }
 }
-// staged x per K chunk: 16 B tiles of N x 16 plus the min-term tile, f16
-__host__ __device__ inline uint32_t gemm_xchunk_bytes(uint32_t nsp) { return 17u * (2 * nsp) * 32u; }
+// staged x per K chunk: 16 B tiles of N x 16 f16 (hi rows, then lo rows), then the f32
+// sums of x over each 32-value sub-block, [8][nsp] (the Q4_K min term)
+__host__ __device__ inline uint32_t gemm_xchunk_bytes(uint32_t nsp) { return 16u * (2 * nsp) * 32u + 8u * nsp * 4u; }
 
 // position of value kk (0..15) of a 16-value K step inside the MMA's K order: the
 // dequantisers pack values (4a, 4a+2) and (4a+1, 4a+3) into one 32-bit column each
@@ -109,11 +111,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_st8(uint32_t t, const uint32_t (&v)[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(t), "r"(v[0]),
-                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
-}
 __device__ __forceinline__ void tmem_st16(uint32_t t, const uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -122,15 +119,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t t, const uint32_t (&v)[16]) {
         "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t t, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(t)
-        : "memory");
+__device__ __forceinline__ void tmem_ld8(uint32_t t, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(t)
+                 : "memory");
 }
-
+__device__ __forceinline__ void tmem_ld4(uint32_t t, uint32_t (&v)[8]) {  // columns 0..3 of v
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(t)
+                 : "memory");
+}
 // shared-memory matrix descriptor: K-major, no swizzle, LBO 128 B, SBO 256 B
 __device__ __forceinline__ uint64_t bdesc(const void* p) {
     const uint64_t a = (smem_addr(p) & 0x3FFFFu) >> 4;
@@ -232,37 +232,67 @@ __device__ __forceinline__ float staged_val(const GemmX& a, const float* x, uint
     return v;
 }
 
-__global__ void gemm_stage_stats_kernel(const GemmX a) {
+constexpr uint32_t kStatsThreads = 1024, kStatsPer = 16;  // rows of up to 16384 values in registers
+
+// One CTA per sequence: x (and the norm weights, loaded before the dependency wait)
+// read once into registers, then two block reductions (sum of squares, maximum).
+// Longer rows take the loop below.
+__global__ void __launch_bounds__(kStatsThreads) gemm_stage_stats_kernel(const GemmX a) {
     const uint32_t s = blockIdx.x, K = a.cols, tid = threadIdx.x, nt = blockDim.x;
     __shared__ float red[32];
-    __shared__ float sh_inv;
-    pdl_wait();
-    if (s >= a.nseq) return;
-    const float* x = a.x + (uint64_t)s * a.x_stride;
-    float inv = 1.f;
-    if (a.norm_w) {
-        float ss = 0.f;
-        for (uint32_t i = tid; i < K; i += nt) ss += x[i] * x[i];
-        ss = warp_sum(ss);
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-        __syncthreads();
-        if (tid == 0) {
-            float t = 0.f;
-            for (uint32_t w = 0; w < nt / 32; ++w) t += red[w];
-            sh_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
-        }
-        __syncthreads();
-        inv = sh_inv;
+    const bool inreg = K <= nt * kStatsPer;
+    float v[kStatsPer], g[kStatsPer];
+    if (inreg && a.norm_w) {
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) g[i] = tid + i * nt < K ? a.norm_w[tid + i * nt] : 0.f;
     }
-    float mx = 0.f;
-    for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(staged_val(a, x, i, inv)));
-    mx = warp_max(mx);
-    __syncthreads();
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
+    pdl_wait();
+    if (s >= a.nseq) return;  // the whole CTA
+    const float* x = a.x + (uint64_t)s * a.x_stride;
+    auto block_sum = [&](float t) {
+        t = warp_sum(t);
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = t;
+        __syncthreads();
+        float r = 0.f;
+        for (uint32_t w = 0; w < nt / 32; ++w) r += red[w];
+        return r;
+    };
+    auto block_max = [&](float t) {
+        t = warp_max(t);
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = t;
+        __syncthreads();
+        float r = 0.f;
+        for (uint32_t w = 0; w < nt / 32; ++w) r = fmaxf(r, red[w]);
+        return r;
+    };
+    float inv = 1.f, mx = 0.f;
+    if (inreg) {
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = tid + i * nt < K ? x[tid + i * nt] : 0.f;
+        if (a.norm_w) {
+            float ss = 0.f;
+#pragma unroll
+            for (uint32_t i = 0; i < kStatsPer; ++i) ss += v[i] * v[i];
+            const float t = block_sum(ss);
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+#pragma unroll
+            for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), g[i]);  // staged_val
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    } else {
+        if (a.norm_w) {
+            float ss = 0.f;
+            for (uint32_t i = tid; i < K; i += nt) ss += x[i] * x[i];
+            const float t = block_sum(ss);
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+        }
+        for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(staged_val(a, x, i, inv)));
+    }
+    const float t = block_max(mx);
     if (tid == 0) {
-        float t = 0.f;
-        for (uint32_t w = 0; w < nt / 32; ++w) t = fmaxf(t, red[w]);
         int e = 0;
         if (t > 0.f) frexpf(t, &e);  // t in [2^(e-1), 2^e)
         const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
@@ -289,18 +319,9 @@ __global__ void gemm_stage_x_kernel(const GemmX a) {
     const uint32_t sl = kslot(k % 16);
     *reinterpret_cast<__half*>(tile + bt_off(s, sl)) = hi;
     *reinterpret_cast<__half*>(tile + bt_off(nsp + s, sl)) = lo;
-    // per 32-value sub-block sums (warp w = sub-block w), scaled by 2^-5 to stay inside f16
-    const float sm = warp_sum(v) * 0.03125f;
-    if ((k & 31) == 0) {
-        const uint32_t sb = k / 32;
-        uint8_t* mt = chunk + 16 * (N * 32u);
-        const __half mhi = __float2half_rn(sm);
-        const __half mlo = __float2half_rn(sm - __half2float(mhi));
-        *reinterpret_cast<__half*>(mt + bt_off(s, kslot(sb))) = mhi;
-        *reinterpret_cast<__half*>(mt + bt_off(nsp + s, kslot(sb))) = mlo;
-        *reinterpret_cast<__half*>(mt + bt_off(s, kslot(8 + sb))) = __float2half_rn(0.f);
-        *reinterpret_cast<__half*>(mt + bt_off(nsp + s, kslot(8 + sb))) = __float2half_rn(0.f);
-    }
+    // per 32-value sub-block sums (warp w = sub-block w)
+    const float sm = warp_sum(v);
+    if ((k & 31) == 0) reinterpret_cast<float*>(chunk + 16 * (N * 32u))[(k / 32) * nsp + s] = sm;
     pdl_launch_dependents();
 }
 
@@ -340,7 +361,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t st_full[kMaxStages], st_empty[kMaxStages];
     __shared__ __align__(8) uint64_t a_full[kASlots], a_empty[kASlots];
-    __shared__ __align__(8) uint64_t m_full[2], m_empty[2];
     __shared__ __align__(8) uint64_t d_full[kDSlots], d_empty[kDSlots];
     __shared__ __align__(8) uint64_t fin_bar;
     __shared__ uint32_t tmem_base;
@@ -361,10 +381,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         for (uint32_t i = 0; i < kASlots; ++i) {
             mbar_init(&a_full[i], 4);  // the four quadrant warps of one math group
             mbar_init(&a_empty[i], 1);
-        }
-        for (uint32_t i = 0; i < 2; ++i) {
-            mbar_init(&m_full[i], 4);
-            mbar_init(&m_empty[i], 1);
         }
         for (uint32_t i = 0; i < kDSlots; ++i) {
             mbar_init(&d_full[i], 1);
@@ -406,8 +422,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = mma_idesc(P.nsp);  // hi and lo parts are two MMAs of N = nsp
-            uint32_t n = 0, g = 0, e = 0, mc = 0;
+            const uint32_t idesc = mma_idesc(2 * P.nsp);  // N = x hi rows then lo rows, one MMA per K step
+            uint32_t n = 0, g = 0, e = 0;
             bool ok = true;
             for (uint32_t it = item0; it < item1 && ok; ++it) {
                 uint32_t mt, c0, c1, kr;
@@ -416,7 +432,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     const uint32_t s = n % kStages;
                     if (!bwait(&st_full[s], (n / kStages) & 1, &abort_flag)) { ok = false; break; }
                     const uint8_t* bx = smem + s * stage_bytes + wbytes;
-                    const uint32_t tile_b = P.N * 32, lo_b = (P.nsp / 8) * 256;  // lo rows start at nsp
+                    const uint32_t tile_b = P.N * 32;
 #pragma unroll
                     for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
                         const uint32_t as = g % kASlots;
@@ -427,30 +443,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                         if (!bwait(&a_full[as], (g / kASlots) & 1, &abort_flag)) { ok = false; break; }
                         tc_after();
                         const uint32_t acol = tm + kColA + as * 32, dcol = tm + kColD + ds * kDCols;
-                        // A columns 8i..8i+7 against B tile `bt`, its hi rows then its lo rows
-                        auto mma2 = [&](uint32_t i, uint32_t bt, bool first) {
+                        // A columns 8i..8i+7 against B tile `bt` (x hi rows, then x lo rows)
+                        auto mma1 = [&](uint32_t i, uint32_t bt, bool first) {
                             mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + bt * tile_b), idesc, !first);
-                            mma_tmem_a(dcol, acol + 8 * i, bdesc(bx + bt * tile_b + lo_b), idesc, 1);
                         };
                         if (T == GGML_Q4_K) {  // 64 values: B tiles 4q..4q+3
-                            for (uint32_t i = 0; i < 4; ++i) mma2(i, 4 * q + i, (q | i) == 0);
+                            for (uint32_t i = 0; i < 4; ++i) mma1(i, 4 * q + i, (q | i) == 0);
                         } else if (T == GGML_Q6_K) {  // 32 values x two planes: B tiles 2q, 2q+1
-                            for (uint32_t i = 0; i < 4; ++i) mma2(i, 2 * q + (i & 1), (q | i) == 0);
+                            for (uint32_t i = 0; i < 4; ++i) mma1(i, 2 * q + (i & 1), (q | i) == 0);
                         } else {  // Q8_0 block q: B tiles 2q, 2q+1
-                            for (uint32_t i = 0; i < 2; ++i) mma2(i, 2 * q + i, i == 0);
+                            for (uint32_t i = 0; i < 2; ++i) mma1(i, 2 * q + i, i == 0);
                         }
                         mma_commit(&a_empty[as]);
                         const bool eu_last = (T == GGML_Q8_0) || q + 1 == SP;
                         if (eu_last) {
-                            if (T == GGML_Q4_K) {  // -dmin * sum_j m_j * sum(x of sub-block j)
-                                const uint32_t ms = mc % 2;
-                                if (!bwait(&m_full[ms], (mc / 2) & 1, &abort_flag)) { ok = false; break; }
-                                tc_after();
-                                mma_tmem_a(dcol + 32, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b), idesc, 0);
-                                mma_tmem_a(dcol + 32, tm + kColMin + ms * 8, bdesc(bx + 16 * tile_b + lo_b), idesc, 1);
-                                mma_commit(&m_empty[ms]);
-                                ++mc;
-                            }
                             mma_commit(&d_full[ds]);
                             ++e;
                         }
@@ -468,40 +474,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         }
     } else {
         // ---------------------------------------------------------------- math warps
-        const uint32_t mw = warp - 2, grp = mw / 4, qd = warp & 3;  // group 0/1, TMEM lane quadrant
+        const uint32_t mw = warp - 2, grp = mw / 4, qd = warp & 3;  // group 0..kGroups-1, TMEM lane quadrant
         const uint32_t t = qd * 32 + lane;                            // row within the M tile
         const uint32_t lane_addr = (qd * 32u) << 16;
-        const uint32_t half = P.nsp / 2;                               // sequences per group in the epilogue
-        float acc[16];
-        uint32_t n = 0, g = 0, e = 0, mc = 0;
+        const uint32_t half = P.nsp / kGroups;                         // sequences per group in the epilogue (4 or 8)
+        float acc[8];
+        uint32_t n = 0, g = 0, e = 0;
         bool ok = true;
         // scales of the accumulator spans not yet read back (two in flight)
-        float eu_d[kDSlots] = {0.f, 0.f, 0.f, 0.f}, eu_dmin[kDSlots] = {0.f, 0.f, 0.f, 0.f};
+        float eu_d[kDSlots] = {0.f, 0.f, 0.f, 0.f};
         auto epilogue = [&](uint32_t eu) -> bool {  // read span eu back and scale it into acc
             const uint32_t ds = eu % kDSlots;
             if (!bwait(&d_full[ds], (eu / kDSlots) & 1, &abort_flag)) return false;
             tc_after();
-            uint32_t dv[16], mv[16];
+            uint32_t dv[8], lv[8];  // this group's sequences: x hi columns, x lo columns
             const uint32_t dcol = tm + lane_addr + kColD + ds * kDCols + grp * half;
-            tmem_ld16(dcol, dv);
-            if (T == GGML_Q4_K) tmem_ld16(dcol + 32, mv);
+            if (half == 8) {
+                tmem_ld8(dcol, dv);
+                tmem_ld8(dcol + P.nsp, lv);
+            } else {
+                tmem_ld4(dcol, dv);
+                tmem_ld4(dcol + P.nsp, lv);
+#pragma unroll
+                for (int i = 4; i < 8; ++i) dv[i] = lv[i] = 0u;
+            }
             tmem_ld_wait();
             tc_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&d_empty[ds]);
-            const float d = eu_d[ds], dm = eu_dmin[ds];
+            const float d = eu_d[ds];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                acc[i] = fmaf(d, __uint_as_float(dv[i]), acc[i]);
-                if (T == GGML_Q4_K) acc[i] = fmaf(-dm * 32.f, __uint_as_float(mv[i]), acc[i]);
-            }
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(d, __uint_as_float(dv[i]) + __uint_as_float(lv[i]), acc[i]);
             return true;
         };
         for (uint32_t it = item0; it < item1 && ok; ++it) {
             uint32_t mt, c0, c1, kr;
             item_range(P, it, mt, c0, c1, kr);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
             uint32_t first_eu = e;
             for (uint32_t c = c0; c < c1 && ok; ++c, ++n) {
                 const uint32_t s = n % kStages;
@@ -517,6 +527,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     dmin = f16_exact(dm >> 16);
                     const uint8_t* sc = wb + 512 + t * 12;
                     for (int j = 0; j < 8; ++j) scale_min_bytes(j, sc, &q4_s[j], &q4_m[j]);
+                    // -dmin * sum_j m_j * sum(x of sub-block j), this group's sequences
+                    const float* xs = reinterpret_cast<const float*>(wb + wbytes + 16u * (P.N * 32u)) + grp * half;
+#pragma unroll
+                    for (uint32_t i = 0; i < 8; ++i) {
+                        if (i >= half) break;
+                        float mt = 0.f;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) mt = fmaf(q4_m[j], xs[j * P.nsp + i], mt);
+                        acc[i] = fmaf(-dmin, mt, acc[i]);
+                    }
                 } else if (T == GGML_Q6_K) {
                     const uint4 sc4 = *reinterpret_cast<const uint4*>(wb + 24576 + t * 16);
                     q6_sc[0] = sc4.x; q6_sc[1] = sc4.y; q6_sc[2] = sc4.z; q6_sc[3] = sc4.w;
@@ -531,7 +551,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                 }
 #pragma unroll
                 for (uint32_t q = 0; q < SP && ok; ++q, ++g) {
-                    if ((g & 1) == grp) {  // this group dequantises sub-chunk g
+                    if (g % kGroups == grp) {  // this group dequantises sub-chunk g
                         const uint32_t as = g % kASlots;
                         if (g >= kASlots && !bwait(&a_empty[as], ((g / kASlots) - 1) & 1, &abort_flag)) {
                             ok = false;
@@ -621,24 +641,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     if (eu_last) {
                         const uint32_t ds = e % kDSlots;
                         eu_d[ds] = (T == GGML_Q8_0) ? q8_d[q] : d;
-                        eu_dmin[ds] = dmin;
-                        if (T == GGML_Q4_K && grp == 0) {  // the chunk's mins: A of the min-term MMA
-                            const uint32_t ms = mc % 2;
-                            if (mc >= 2 && !bwait(&m_empty[ms], ((mc / 2) - 1) & 1, &abort_flag)) { ok = false; break; }
-                            tc_after();
-                            uint32_t mv[8];
-                            mv[0] = h2bits(q4_m[0], q4_m[2]);
-                            mv[1] = h2bits(q4_m[1], q4_m[3]);
-                            mv[2] = h2bits(q4_m[4], q4_m[6]);
-                            mv[3] = h2bits(q4_m[5], q4_m[7]);
-                            mv[4] = mv[5] = mv[6] = mv[7] = 0u;
-                            tmem_st8(tm + lane_addr + kColMin + ms * 8, mv);
-                            tmem_st_wait();
-                            tc_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&m_full[ms]);
-                        }
-                        if (T == GGML_Q4_K) ++mc;
                         // read back the previous span (one span of lag keeps the MMAs busy)
                         if (e >= first_eu + kLag && !epilogue(e - kLag)) { ok = false; break; }
                         ++e;
@@ -653,9 +655,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
             if (!ok) break;
             // partial sums of this item: part[kr][seq][row]
             const uint32_t row = mt * kMT + t;
-            for (uint32_t i = 0; i < half; ++i) {
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
                 const uint32_t sq = grp * half + i;
-                if (sq < A.nseq)
+                if (i < half && sq < A.nseq)
                     A.part[((uint64_t)kr * A.nseq + sq) * A.rows_pad + row] = acc[i] * A.xinv[sq];
             }
         }
@@ -739,7 +742,7 @@ cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl) {
     if (!a.nseq || a.nseq > 32 || a.cols % kChunk || !a.x || !a.bx || !a.xinv || !a.stats) return cudaErrorInvalidValue;
     a.nsp = (a.nseq + 15) / 16 * 16;  // the MMA's N (M = 128 needs a multiple of 16)
     cudaLaunchAttribute at[1];
-    auto cfg = cfg_of(dim3(a.nseq), dim3(256), 0, s, pdl, at);
+    auto cfg = cfg_of(dim3(a.nseq), dim3(kStatsThreads), 0, s, pdl, at);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_stage_stats_kernel, a);
     if (e != cudaSuccess) return e;
     auto cfg2 = cfg_of(dim3(a.nsp, a.cols / kChunk), dim3(kChunk), 0, s, pdl, at);

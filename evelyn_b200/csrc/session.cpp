@@ -102,19 +102,22 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     const uint32_t by_len = batch > 1 ? (b.pages_per_seq + 31) / 32 : 1;
     b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
-    {  // one sequence: attention with QK-norm/RoPE/append and the merge in one cluster launch
+    {  // attention with QK-norm/RoPE/append and the split merge in one cluster launch
+        // (one sequence only: a batch's many (sequence, kv head) pairs run faster on the
+        // split kernels, which keep more CTAs per SM)
         const char* fe = std::getenv("EVELYN_FUSED_ATTN");
         if (batch == 1 && !(fe && fe[0] == '0')) {
-            const uint32_t C = 8;
-            const uint32_t ring = attention_cluster_pages(b.pages_per_seq, C, kPageSize, (uint32_t)hd, (uint32_t)elem,
-                                                          m->lheads / std::max<uint32_t>(1, m->lkv_heads));
+            const uint32_t C = 8;  // splits per kv head
             // EVELYN_ATTN_RING caps the ring (even, >= 2), so tests reach the streamed
             // multi-chunk case at small contexts
             const char* re = std::getenv("EVELYN_ATTN_RING");
-            const uint32_t cap = re ? (uint32_t)std::strtoul(re, nullptr, 10) & ~1u : 0;
+            const uint32_t cap = re ? (uint32_t)std::strtoul(re, nullptr, 10) & ~1u : 16;
+            const uint32_t ring = attention_cluster_pages(b.pages_per_seq, C, kPageSize, (uint32_t)hd, (uint32_t)elem,
+                                                          m->lheads / std::max<uint32_t>(1, m->lkv_heads),
+                                                          std::max<uint32_t>(cap, 2));
             if (ring) {
                 b.cluster_splits = C;
-                b.cluster_ring = cap >= 2 ? std::min(ring, cap) : ring;
+                b.cluster_ring = ring;
             }
         }
     }
@@ -218,9 +221,16 @@ void Decoder::enqueue_batched(bool pdl) {
         gemm_reduce(L.k, p1, k1, b.k.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
         gemm_product(L.v, p1, k1, pdl);
         gemm_reduce(L.v, p1, k1, b.v.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
-        cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
-        cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
-        kernels += 3;
+        if (b.cluster_ring) {
+            cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream,
+                                                pdl),
+                       "attention");
+            kernels += 1;
+        } else {
+            cuda_check(launch_qk_norm_rope_append(rope_args(li), stream, pdl), "qk-norm/rope/append");
+            cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
+            kernels += 3;
+        }
         gemm_stage(b.att.as<float>(), qw, qw, nullptr, pdl);
         gemm_product(L.o, p1, k1, pdl);
         gemm_reduce(L.o, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
