@@ -22,6 +22,8 @@
 // entirely out of shared memory. The C partials (m, l, o) of a kv head meet through
 // distributed shared memory: cluster rank 0 merges them in rank order.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <atomic>
@@ -40,6 +42,7 @@ constexpr uint32_t kMaxRingPages = 16;
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
 
 struct ClusterAttn {
+    KvTmap tmap;          // the KV pool as [rows][head_dim] f16 (tensor-core path)
     RopeArgs r;
     AttnArgs a;
     uint32_t ring_pages;  // page tiles (K and V) the shared ring holds
@@ -81,17 +84,60 @@ __device__ __forceinline__ KV to_kv(float v) {
     else return v;
 }
 
+// ---- tensor-core path (f16 KV, 16-token pages): page tiles arrive by TMA tensor copies
+// in boxes of 16 rows x 64 values (128 B) with the 128-byte swizzle, so that ldmatrix
+// reads 8 rows of one 16-byte column without bank conflicts.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t x, int32_t y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+// byte offset of 16-byte column c (values 8c..8c+7) of row r in a swizzled page tile
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
+    return (c >> 3) * 2048u + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// D (rows g, g+8; cols 2t, 2t+1) = A (16 x 16 f16, rows 8-15 zero) * B (16 x 8 f16) + C;
+// only rows g (the heads) are kept: c0, c1 accumulate, the rows-g+8 outputs are dropped
+__device__ __forceinline__ void mma_rows(float& c0, float& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm("{\n .reg .f32 z2, z3;\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,z2,z3}, {%2,%3,%4,%5}, {%6,%7}, {%8,%9,%10,%11};\n}"
+        : "=f"(c0), "=f"(c1)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f), "f"(0.f));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// f32 pair -> f16 hi pair and f16 residual pair (v = hi + lo to ~22 bits)
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    hi = pack_h2(__half2float(ha), __half2float(hb));
+    lo = pack_h2(a - __half2float(ha), b - __half2float(hb));
+}
+
 // Shared-memory bytes of one CTA (ring, q, per-warp vectors, warp partials, CTA partial).
 __host__ __device__ __forceinline__ size_t cluster_smem(uint32_t ring_pages, uint32_t ps, uint32_t hd, uint32_t eb,
                                                        uint32_t G) {
-    return (size_t)ring_pages * 2 * ps * hd * eb + 4ull * G * hd + 4ull * (G + 2) * hd +
-           4ull * kAW * G * (hd + 2) + 4ull * G * (hd + 2);
+    return 1024 + (size_t)ring_pages * 2 * ps * hd * eb + 4ull * G * hd + 4ull * (G + 2) * hd +
+           4ull * kAW * G * (hd + 2) + 4ull * G * (hd + 2) + 2ull * 32 * hd;  // + q fragments (hd/16 x 32 x 16 B)
 }
 
-template <typename KV, int G, int HD>
+template <typename KV, int G, int HD, bool MM>
 __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_constant__ ClusterAttn F) {
     constexpr int DPL = HD / 32;
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // the ring starts on a 1024-byte boundary (the swizzle atom of the tensor copies)
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[2];  // the two halves of the page ring
     __shared__ int bad_sh;
     cg::cluster_group cl = cg::this_cluster();
@@ -108,6 +154,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     float* vec = qs + G * HD;                                                 // [G+2][HD] per-warp vectors
     float* wpart = vec + (G + 2) * HD;                                        // [warps][G][HD+2]
     float* cpart = wpart + kAW * G * (HD + 2);                                // [G][HD+2]: o, m, l
+    uint4* qfrag = reinterpret_cast<uint4*>(cpart + G * (HD + 2));            // [HD/16][lanes]: q hi/lo fragments
 
     if (tid == 0) {
         mbar_init(&full[0], 1);
@@ -137,8 +184,19 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         for (uint32_t i = p0; i < p1; ++i) {
             const int32_t page = __ldcg(ptab + t0 / ps + i);
             KV* slot = ring + (half * H + (i - p0)) * 2 * tile;
-            tma_load_1d(slot, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full[half]);
-            tma_load_1d(slot + tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full[half]);
+            if constexpr (MM) {  // row coordinates of the K and V tiles in the pool's [rows][HD] view
+                const uint8_t* pool = (const uint8_t*)a.kv.pool;
+                const int32_t yk = (int32_t)((kv_tile(a.kv, page, r.layer, 0, kvh) - pool) / (HD * 2));
+                const int32_t yv = (int32_t)((kv_tile(a.kv, page, r.layer, 1, kvh) - pool) / (HD * 2));
+#pragma unroll
+                for (int bx = 0; bx < HD / 64; ++bx) {
+                    tma_load_2d(reinterpret_cast<uint8_t*>(slot) + bx * 2048, &F.tmap, 64 * bx, yk, &full[half]);
+                    tma_load_2d(reinterpret_cast<uint8_t*>(slot + tile) + bx * 2048, &F.tmap, 64 * bx, yv, &full[half]);
+                }
+            } else {
+                tma_load_1d(slot, kv_tile(a.kv, page, r.layer, 0, kvh), tile * sizeof(KV), &full[half]);
+                tma_load_1d(slot + tile, kv_tile(a.kv, page, r.layer, 1, kvh), tile * sizeof(KV), &full[half]);
+            }
         }
     };
     if (tid == 0) {
@@ -220,22 +278,49 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             const int32_t page = __ldcg(ptab + (uint32_t)pos / ps);
             KV* dst = (KV*)kv_tile(a.kv, page, r.layer, warp == G ? 0 : 1, kvh) + ((uint32_t)pos % ps) * HD;
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) dst[DPL * lane + e] = to_kv<KV>(val[e]);
+            for (int e = 0; e < DPL; ++e) {
+                dst[DPL * lane + e] = to_kv<KV>(val[e]);
+                vec[warp * HD + DPL * lane + e] = val[e];  // for the split's own copy (same lane reads it)
+            }
         }
     }
     __syncthreads();  // q in shared memory
 
-    // ---- online softmax over this split's positions, chunk by chunk, one position per
-    // warp at a time, entirely out of shared memory
+    // ---- online softmax over this split's positions, chunk by chunk, entirely out of
+    // shared memory. Scalar path: one position per warp at a time, lanes over the head
+    // dimensions. Tensor-core path: one 8-position half page per warp at a time, the G
+    // heads as the rows of mma.sync m16n8k16 (q and the softmax weights split into f16
+    // hi + lo, so the products carry ~22 bits like the f32 reference), the scores of a
+    // head meet in its lane quad.
     float qr[G][DPL], m[G], l[G], o[G][DPL];
+    const uint32_t g8 = (uint32_t)lane >> 2, t4 = (uint32_t)lane & 3;  // MMA row (head) and column pair
+    float mrow = -INFINITY, lrow = 0.f, oacc[MM ? HD / 8 : 1][2];
+    if constexpr (MM) {
+        // the q fragments of every k step, the same for all warps: built once (lane =
+        // (head g, column pair t) of the MMA; heads >= G are zero rows)
+        if (tid < (HD / 16) * 32) {
+            const uint32_t ks = tid >> 5, fg = (tid & 31) >> 2, ft = tid & 3;
+            uint4 f = make_uint4(0u, 0u, 0u, 0u);
+            if (fg < (uint32_t)G) {
+                const float* qg = qs + fg * HD + 16 * ks + 2 * ft;
+                split_h2(qg[0], qg[1], f.x, f.z);
+                split_h2(qg[8], qg[9], f.y, f.w);
+            }
+            qfrag[tid] = f;  // x, y: hi (a0, a2); z, w: lo
+        }
+        __syncthreads();
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
+        for (int nd = 0; nd < HD / 8; ++nd) oacc[nd][0] = oacc[nd][1] = 0.f;
+    } else {
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) {
-            qr[g][e] = qs[g * HD + DPL * lane + e];
-            o[g][e] = 0.f;
+        for (int g = 0; g < G; ++g) {
+            m[g] = -INFINITY;
+            l[g] = 0.f;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) {
+                qr[g][e] = qs[g * HD + DPL * lane + e];
+                o[g][e] = 0.f;
+            }
         }
     }
     const uint32_t pnew = last ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
@@ -247,45 +332,119 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
         // the new position's k and v (registers of warps G, G+1) into the split's copy
         if (pnew >= p0 && pnew < p1 && (warp == G || warp == G + 1)) {
-            KV* row = ring + ((half * H + pnew - p0) * 2 + (warp == G ? 0 : 1)) * tile + ((uint32_t)pos % ps) * HD;
+            KV* tl = ring + ((half * H + pnew - p0) * 2 + (warp == G ? 0 : 1)) * tile;
+            const uint32_t rr = (uint32_t)pos % ps;
+            if constexpr (MM) {  // swizzled tile: this lane's DPL values are contiguous in one 16-byte column
+                const uint32_t d0 = DPL * lane;
+                __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(tl) + swz(rr, d0 / 8) + (d0 % 8) * 2);
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) row[DPL * lane + e] = to_kv<KV>(val[e]);
+                for (int e = 0; e < DPL; ++e) dst[e] = __float2half_rn(vec[warp * HD + DPL * lane + e]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) tl[rr * HD + DPL * lane + e] = to_kv<KV>(vec[warp * HD + DPL * lane + e]);
+            }
         }
         __syncthreads();
         if (bad_sh) break;  // uniform after the barrier
         const uint32_t tc0 = t0 + p0 * ps, tc1 = min(t1, t0 + p1 * ps);
-        for (uint32_t t = tc0 + warp; t < tc1; t += kAW) {
-            const uint32_t li = t - tc0;
-            const KV* kp = ring + (half * H + li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
-            float kf[DPL], vf[DPL];
-            load_kv<DPL>(kp, kf);
-            load_kv<DPL>(kp + tile, vf);
+        if constexpr (MM) {
+            const uint32_t nunits = 2 * (p1 - p0);
+            for (uint32_t u = warp; u < nunits; u += kAW) {
+                const uint32_t pg = u >> 1, hf = u & 1, tu = tc0 + pg * 16 + hf * 8;
+                if (tu >= tc1) continue;  // uniform over the warp
+                const uint32_t kb = smem_addr(ring + (half * H + pg) * 2 * tile), vb = kb + tile * 2;
+                // scores of head g8 at positions tu + 2 t4, + 1: four independent accumulator
+                // pairs (q hi / q lo x even / odd k step) keep the MMA chains short
+                float sa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll 2
+                for (int ks = 0; ks < HD / 16; ++ks) {
+                    uint32_t b0, b1;
+                    ldsm_x2(kb + swz(8 * hf + (lane & 7), 2 * ks + ((lane >> 3) & 1)), b0, b1);
+                    const uint4 f = qfrag[ks * 32 + lane];
+                    mma_rows(sa[2 * (ks & 1)][0], sa[2 * (ks & 1)][1], f.x, f.y, b0, b1);
+                    mma_rows(sa[2 * (ks & 1) + 1][0], sa[2 * (ks & 1) + 1][1], f.z, f.w, b0, b1);
+                }
+                float s0 = (sa[0][0] + sa[2][0]) + (sa[1][0] + sa[3][0]);
+                float s1 = (sa[0][1] + sa[2][1]) + (sa[1][1] + sa[3][1]);
+                const uint32_t pa = tu + 2 * t4;
+                s0 = pa < tc1 ? s0 * a.scale : -INFINITY;
+                s1 = pa + 1 < tc1 ? s1 * a.scale : -INFINITY;
+                float mx = fmaxf(s0, s1);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(mrow, mx);     // finite: position tu is live
+                const float alpha = expf(mrow - mn);  // exp(-inf) = 0 on the first unit
+                const float e0 = expf(s0 - mn), e1 = expf(s1 - mn);
+                lrow = lrow * alpha + e0 + e1;        // this lane's columns; the quad adds them at the end
+                mrow = mn;
+                uint32_t ph, pl;
+                split_h2(e0, e1, ph, pl);
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float sc = qr[g][0] * kf[0];
+                for (int j = 0; j < HD / 32; ++j) {  // four 8-value dimension tiles per ldmatrix
+                    uint32_t vv[4];
+                    ldsm_x4_t(vb + swz(8 * hf + (lane & 7), 4 * j + (lane >> 3)), vv[0], vv[1], vv[2], vv[3]);
 #pragma unroll
-                for (int e = 1; e < DPL; ++e) sc = fmaf(qr[g][e], kf[e], sc);
-                sc = warp_sum(sc) * a.scale;
-                const float mn = fmaxf(m[g], sc);
-                const float alpha = expf(m[g] - mn);  // exp(-inf) = 0 on the first position
-                const float w = expf(sc - mn);
-                l[g] = l[g] * alpha + w;
+                    for (int q = 0; q < 4; ++q) {
+                        float& o0 = oacc[4 * j + q][0];
+                        float& o1 = oacc[4 * j + q][1];
+                        o0 *= alpha;
+                        o1 *= alpha;
+                        mma_rows(o0, o1, ph, 0u, vv[q], 0u);  // k = the unit's 8 positions (rest zero)
+                        mma_rows(o0, o1, pl, 0u, vv[q], 0u);
+                    }
+                }
+            }
+        } else {
+            for (uint32_t t = tc0 + warp; t < tc1; t += kAW) {
+                const uint32_t li = t - tc0;
+                const KV* kp = ring + (half * H + li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
+                float kf[DPL], vf[DPL];
+                load_kv<DPL>(kp, kf);
+                load_kv<DPL>(kp + tile, vf);
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(w, vf[e], o[g][e] * alpha);
-                m[g] = mn;
+                for (int g = 0; g < G; ++g) {
+                    float sc = qr[g][0] * kf[0];
+#pragma unroll
+                    for (int e = 1; e < DPL; ++e) sc = fmaf(qr[g][e], kf[e], sc);
+                    sc = warp_sum(sc) * a.scale;
+                    const float mn = fmaxf(m[g], sc);
+                    const float alpha = expf(m[g] - mn);  // exp(-inf) = 0 on the first position
+                    const float w = expf(sc - mn);
+                    l[g] = l[g] * alpha + w;
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(w, vf[e], o[g][e] * alpha);
+                    m[g] = mn;
+                }
             }
         }
         __syncthreads();  // every warp is done with this half of the ring
         if (tid == 0 && c + 2 < nch) issue(c + 2);
     }
+    if constexpr (MM) {
+        lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
+        lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
+        if (g8 < (uint32_t)G) {
+            float* wp = wpart + (warp * G + g8) * (HD + 2);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        float* wp = wpart + (warp * G + g) * (HD + 2);
+            for (int nd = 0; nd < HD / 8; ++nd) {
+                wp[8 * nd + 2 * t4] = oacc[nd][0];
+                wp[8 * nd + 2 * t4 + 1] = oacc[nd][1];
+            }
+            if (t4 == 0) {
+                wp[HD] = mrow;
+                wp[HD + 1] = lrow;
+            }
+        }
+    } else {
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) wp[DPL * lane + e] = o[g][e];
-        if (lane == 0) {
-            wp[HD] = m[g];
-            wp[HD + 1] = l[g];
+        for (int g = 0; g < G; ++g) {
+            float* wp = wpart + (warp * G + g) * (HD + 2);
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) wp[DPL * lane + e] = o[g][e];
+            if (lane == 0) {
+                wp[HD] = m[g];
+                wp[HD + 1] = l[g];
+            }
         }
     }
     __syncthreads();
@@ -331,7 +490,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     cl.sync();  // the partials stay in place until rank 0 has read them
 }
 
-template <typename KV, int G, int HD>
+template <typename KV, int G, int HD, bool MM>
 cudaError_t launch_t(const ClusterAttn& F, cudaStream_t s, bool pdl) {
     const size_t smem = cluster_smem(F.ring_pages, F.a.kv.page_size, HD, sizeof(KV), G);
     static std::atomic<int> attr_done[64];
@@ -339,7 +498,7 @@ cudaError_t launch_t(const ClusterAttn& F, cudaStream_t s, bool pdl) {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_cluster_kernel<KV, G, HD>,
+        cudaError_t e = cudaFuncSetAttribute(attn_cluster_kernel<KV, G, HD, MM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
         if (e != cudaSuccess) return e;
         attr_done[dev] = 1;
@@ -358,16 +517,16 @@ cudaError_t launch_t(const ClusterAttn& F, cudaStream_t s, bool pdl) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<KV, G, HD>, F);
+    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<KV, G, HD, MM>, F);
 }
 
-template <typename KV, int HD>
+template <typename KV, int HD, bool MM>
 cudaError_t launch_hd(const ClusterAttn& F, uint32_t G, cudaStream_t s, bool pdl) {
     switch (G) {
-        case 1: return launch_t<KV, 1, HD>(F, s, pdl);
-        case 2: return launch_t<KV, 2, HD>(F, s, pdl);
-        case 4: return launch_t<KV, 4, HD>(F, s, pdl);
-        default: return launch_t<KV, 8, HD>(F, s, pdl);
+        case 1: return launch_t<KV, 1, HD, MM>(F, s, pdl);
+        case 2: return launch_t<KV, 2, HD, MM>(F, s, pdl);
+        case 4: return launch_t<KV, 4, HD, MM>(F, s, pdl);
+        default: return launch_t<KV, 8, HD, MM>(F, s, pdl);
     }
 }
 
@@ -387,8 +546,31 @@ uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t p
     return cluster_smem(ring, page_size, head_dim, elem_bytes, group) <= kSmemCap ? ring : 0;
 }
 
+bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* out) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::atomic<int> tried{0};
+    if (!tried.exchange(1)) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if (!encode || !pool || (head_dim != 64 && head_dim != 128) || (reinterpret_cast<uintptr_t>(pool) & 127))
+        return false;
+    // the pool as [rows][head_dim] f16 rows; a box is 16 rows x 64 values (128 B), swizzled
+    const cuuint64_t dims[2] = {head_dim, bytes / (2ull * head_dim)};
+    const cuuint64_t strides[1] = {2ull * head_dim};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t estr[2] = {1, 1};
+    static_assert(sizeof(KvTmap) == sizeof(CUtensorMap), "tensor map size");
+    return encode(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(pool), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
-                                     bool pdl) {
+                                     bool pdl, const KvTmap* tmap) {
     if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1))
         return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
@@ -402,8 +584,18 @@ cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint3
     F.a = a;
     F.ring_pages = ring_pages;
     const bool f16 = a.kv.elem_bytes == 2;
-    if (a.head_dim == 128) return f16 ? launch_hd<__half, 128>(F, G, s, pdl) : launch_hd<float, 128>(F, G, s, pdl);
-    return f16 ? launch_hd<__half, 64>(F, G, s, pdl) : launch_hd<float, 64>(F, G, s, pdl);
+    // tensor cores for f16 pages of 16 rows whose tiles the tensor map addresses (row
+    // strides and offsets multiples of one head_dim row)
+    const uint64_t row = 2ull * a.head_dim;
+    const bool mm = tmap && f16 && a.kv.page_size == 16 && a.kv.page_stride % row == 0 && a.kv.layer_stride % row == 0 &&
+                    a.kv.head_stride % row == 0 && a.kv.v_offset % (int64_t)row == 0;
+    if (mm) {
+        F.tmap = *tmap;
+        return a.head_dim == 128 ? launch_hd<__half, 128, true>(F, G, s, pdl) : launch_hd<__half, 64, true>(F, G, s, pdl);
+    }
+    if (a.head_dim == 128)
+        return f16 ? launch_hd<__half, 128, false>(F, G, s, pdl) : launch_hd<float, 128, false>(F, G, s, pdl);
+    return f16 ? launch_hd<__half, 64, false>(F, G, s, pdl) : launch_hd<float, 64, false>(F, G, s, pdl);
 }
 
 }  // namespace evl

@@ -165,6 +165,23 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// An L2 policy under which the lines a copy brings in are the first to be evicted: the
+// weight stream (each byte read once per step, gigabytes against a 126 MB L2) then does
+// not push out the code, kernel parameters, norm weights, activations and KV pages
+// that the following kernels read again.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void tma_load_1d_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
 __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }

@@ -34,7 +34,6 @@ struct MatvecArgs {
     uint32_t cols = 0;
     const float* norm_w = nullptr; // fused RMSNorm weight (null: x used as is)
     float eps = 1e-6f;
-    float* x_out = nullptr;        // if set, the (normalised) input is also written here
     QMatDev prefetch;              // matrix the next launch reads (q == null: none); its
                                    // first rows are warmed into L2 at the end
     int* err = nullptr;            // device error flag (DeviceError), required
@@ -102,8 +101,17 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // per sequence (at most cap pages), 0 when this path does not apply.
 uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t page_size, uint32_t head_dim,
                                  uint32_t elem_bytes, uint32_t group, uint32_t cap = 16);
+// The KV pool viewed as [rows][head_dim] f16 rows (16-row x 64-value boxes, 128-byte
+// swizzle), for the tensor-core path of launch_attention_cluster. Opaque copy of a
+// CUtensorMap; false when the driver call or the shape is not available.
+struct alignas(64) KvTmap {
+    unsigned long long w[16];
+};
+bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* out);
+// tmap (optional): f16 pages of 16 rows run on the tensor cores (mma.sync), else the
+// scalar loop
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
-                                     bool pdl);
+                                     bool pdl, const KvTmap* tmap = nullptr);
 
 // ---------------------------------------------------------------- step_kernel.cu
 // One decoder layer of a single-sequence step, as the separate launches would run it:

@@ -290,15 +290,10 @@ __device__ __forceinline__ void pack_limbs(int m0, int m1, int m2, int m3, uint3
     w2 = __byte_perm(__byte_perm(t0, t1, 0x0062), __byte_perm(t2, t3, 0x0062), 0x5410);  // byte 2 of each
 }
 
-// One 16-value quarter hb of the (normalised) input, held in v: block scale, limbs,
-// sums, and the writes of the staged layouts. All lanes of the warp call it (the
-// block maximum and sum meet by shuffle); `on` is uniform per lane pair.
+// One 16-value quarter hb of the input (times the norm weight), held in v: block
+// scale, limbs, sums, and the writes of the staged layouts. All lanes of the warp call
+// it (the block maximum and sum meet by shuffle); `on` is uniform per lane pair.
 __device__ __forceinline__ void stage_quarter(const Plan& p, uint8_t* xs, uint32_t hb, bool on, const float (&v)[16]) {
-    if (on && p.a.x_out && blockIdx.x == 0) {
-        float4* op = reinterpret_cast<float4*>(p.a.x_out + 16 * hb);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) op[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    }
     // |x| bit patterns order like the values; the biased exponent E of the block
     // maximum puts it in [2^(E-127), 2^(E-126)), i.e. frexp's e = E - 126, and
     // s = 22 - e keeps |m| <= 2^22
@@ -378,54 +373,49 @@ __device__ __forceinline__ float sum_sq(const float (&v)[16]) {
     for (int e = 0; e < 16; ++e) ss += v[e] * v[e];
     return ss;
 }
-__device__ __forceinline__ void apply_norm(float (&v)[16], const float (&g)[16], float inv) {
+__device__ __forceinline__ void mul_weights(float (&v)[16], const float (&g)[16]) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], inv), g[e]);
+    for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], g[e]);
 }
 
-// Called by the consumer threads after griddepcontrol.wait. Rows of up to 1024
-// quarters (16384 values) are read once into registers, the norm weights in the same
-// round trip; longer rows take a second pass for the normalisation.
-__device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, float* red) {
+// The norm weights of this consumer thread's quarters, read before
+// griddepcontrol.wait (they do not depend on the previous kernel); rows of up to 1024
+// quarters (16384 values) only, longer rows read them while staging.
+struct NormRegs {
+    float g0[16], g1[16];
+};
+__device__ __forceinline__ void load_norm_regs(const Plan& p, int warp, int lane, NormRegs& n) {
+    const MatvecArgs& a = p.a;
+    const uint32_t nq = a.cols / 16, per = kCW * 32, c = (uint32_t)(warp * 32 + lane);
+    if (!a.norm_w || nq > 2 * per) return;
+    load_weights(a.norm_w, c, c < nq, n.g0);
+    if (nq > per) load_weights(a.norm_w, c + per, c + per < nq, n.g1);
+}
+
+// Called by the consumer threads after griddepcontrol.wait, in one pass over the row.
+// With a fused RMSNorm (src/runtime.rs:193-196) the staged values are x * w and the
+// returned 1/rms(x) scales each dot product in the row epilogue, so staging needs no
+// barrier between the sum of squares and the writes; without a norm it returns 1.
+__device__ float stage_input(const Plan& p, uint8_t* xs, int warp, int lane, float* red, const NormRegs& nr) {
     const MatvecArgs& a = p.a;
     const uint32_t K = a.cols, nq = K / 16, per = kCW * 32;
     const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
-    auto block_inv = [&](float ss) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        named_sync(kConsumerBarrier, kCW * 32);
-        ss = 0.f;
-#pragma unroll
-        for (int w = 0; w < kCW; ++w) ss += red[w];
-        return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-    };
+    float ss = 0.f;
     if (nq <= 2 * per) {
         // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
         const uint32_t q0 = c, q1 = c + per;
         const bool on0 = q0 < nq, on1 = q1 < nq, two = nq > per;
-        float v0[16], v1[16], g0[16], g1[16];
+        float v0[16], v1[16];
         load_quarter(a.x, q0, on0, v0);
         if (two) load_quarter(a.x, q1, on1, v1);
         if (a.norm_w) {
-            load_weights(a.norm_w, q0, on0, g0);
-            if (two) load_weights(a.norm_w, q1, on1, g1);
-            const float inv = block_inv(sum_sq(v0) + (two ? sum_sq(v1) : 0.f));
-            if (on0) apply_norm(v0, g0, inv);
-            if (two && on1) apply_norm(v1, g1, inv);
+            ss = sum_sq(v0) + (two ? sum_sq(v1) : 0.f);
+            if (on0) mul_weights(v0, nr.g0);
+            if (two && on1) mul_weights(v1, nr.g1);
         }
         stage_quarter(p, xs, q0, on0, v0);
         if (two) stage_quarter(p, xs, q1, on1, v1);
     } else {
-        float inv = 1.f;
-        if (a.norm_w) {
-            float ss = 0.f;
-            for (uint32_t hb = c; hb < nq; hb += per) {
-                float v[16];
-                load_quarter(a.x, hb, true, v);
-                ss += sum_sq(v);
-            }
-            inv = block_inv(ss);
-        }
         for (uint32_t hb0 = (uint32_t)warp * 32; hb0 < nq; hb0 += per) {
             const uint32_t hb = hb0 + lane;
             const bool on = hb < nq;  // uniform per lane pair
@@ -433,13 +423,23 @@ __device__ void stage_input(const Plan& p, uint8_t* xs, int warp, int lane, floa
             load_quarter(a.x, hb, on, v);
             if (a.norm_w) {
                 load_weights(a.norm_w, hb, on, g);
-                if (on) apply_norm(v, g, inv);
+                ss += sum_sq(v);
+                if (on) mul_weights(v, g);
             }
             stage_quarter(p, xs, hb, on, v);
         }
     }
+    if (a.norm_w) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+    }
     if (c < kRedBufs) reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes)[c] = 0u;
     named_sync(kConsumerBarrier, kCW * 32);
+    if (!a.norm_w) return 1.f;
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) ss += red[w];
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
 }
 
 
@@ -488,9 +488,10 @@ __device__ __forceinline__ void issue_item(const Plan& p, const Ring& r, uint32_
     uint32_t sb;
     const uint32_t n = item_slabs(p, rb, g, a, b, sb);
     uint8_t* slot = r.base + s * r.slot_bytes;
+    const uint64_t pol = l2_evict_first();
     mbar_arrive_expect_tx(&r.full[s], n * sb);
-    tma_load_1d(slot, a, sb, &r.full[s]);
-    if (n == 2) tma_load_1d(slot + sb, b, sb, &r.full[s]);
+    tma_load_1d_hint(slot, a, sb, &r.full[s], pol);
+    if (n == 2) tma_load_1d_hint(slot + sb, b, sb, &r.full[s], pol);
 }
 
 // Position in the ring sequence: items issued (or consumed) so far, the slot, and the
@@ -576,25 +577,55 @@ __device__ __forceinline__ bool consume_rows(const Plan& p, const Ring& r, const
     return true;
 }
 
+// Row slot i (0 .. kRB-1) of row block rb (CTA range from rb0): the eight super-block
+// warps' partials in `rd` added in warp order, scaled by the norm's 1/rms `inv`, and
+// the segment's epilogue (store, residual add, or SiLU(gate) * up for slots < 16).
+__device__ __forceinline__ void finish_row(const Plan& p, const uint8_t* xs, const float* rd, uint32_t rb, uint32_t rb0,
+                                           uint32_t i, float inv, bool cached) {
+    const int si = seg_of(p, rb);
+    const MatvecSeg& sg = p.a.seg[si];
+    const uint32_t local = rb - p.rb_begin[si];
+    auto sum = [&](uint32_t k) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSbWarps; ++w) v += rd[w * kRB + k];
+        return __fmul_rn(v, inv);
+    };
+    if (sg.epi == EPI_SWIGLU) {
+        const uint32_t row = local * kSlabRows + i;
+        if (i < kSlabRows && row < sg.m.rows) sg.y[row] = __fmul_rn(silu(sum(i)), sum(i + kSlabRows));
+    } else {
+        const uint32_t row = local * kRB + i;
+        if (row < sg.m.rows) {
+            const float v = sum(i);
+            if (sg.epi == EPI_ADD)
+                sg.y[row] = (cached ? reinterpret_cast<const float*>(xs + p.off_rows)[(rb - rb0) * kRB + i]
+                                    : __ldcg(sg.y + row)) + v;
+            else sg.y[row] = v;
+        }
+    }
+}
+
 // Consumers (all kCW warps): dot products of row blocks [rb0, rb1) against the staged
 // input `xs`; warp (slab w / 8, super-block w % 8) of every stage. At the end of a row
-// block each warp parks its partial sums of the block's rows in one of kRedBufs
-// shared buffers and the last warp to arrive adds the eight partials of each row in
-// warp order and runs the epilogue -- no CTA-wide barrier. (A warp is at most
-// `stages` items, so at most `stages` row blocks, ahead of the slowest one, and
-// stages < kRedBufs, so a buffer is reused only after its last reader is done.)
+// block each warp parks its partial sums of the block's rows in a shared buffer.
+// When the CTA's row blocks fit the kRedBufs buffers, every block has its own and the
+// rows are finished after the last block by all consumer threads at once. Otherwise
+// the buffers rotate and the last warp to arrive at a block adds its partials and runs
+// the epilogue, with no CTA-wide barrier. (A warp is at most `stages` items, so at
+// most `stages` row blocks, ahead of the slowest one, and stages < kRedBufs, so a
+// buffer is reused only after its last reader is done.) `inv` is staging's 1/rms.
 // Returns false after an abort (every consumer warp returns at the same stage).
 __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_t rb0, uint32_t rb1, RingPos& rp,
-                              int warp, int lane, volatile int* abort_flag) {
+                              int warp, int lane, volatile int* abort_flag, float inv) {
     float* red = reinterpret_cast<float*>(xs + p.off_red);
     unsigned* cnt = reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes);
     const Lane L = make_lane(lane);
     const uint32_t slab = (uint32_t)warp / kSbWarps, sbw = (uint32_t)warp % kSbWarps;
     const bool cached = rows_cached(p, rb0, rb1);
+    const bool deferred = rb1 - rb0 <= kRedBufs;
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
-        const int si = seg_of(p, rb);
-        const MatvecSeg& sg = p.a.seg[si];
-        const uint32_t local = rb - p.rb_begin[si];
+        const MatvecSeg& sg = p.a.seg[seg_of(p, rb)];
         float acc0 = 0.f, acc1 = 0.f;  // rows g8 and g8 + 8 of this warp's slab
         bool ok;
         switch (sg.m.type) {
@@ -613,6 +644,7 @@ __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_
             rd[sbw * kRB + slab * kSlabRows + L.g8] = acc0;
             rd[sbw * kRB + slab * kSlabRows + L.g8 + 8] = acc1;
         }
+        if (deferred) continue;
         __threadfence_block();
         __syncwarp();
         unsigned last = 0;
@@ -620,23 +652,14 @@ __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence_block();
-        float v = 0.f;  // lane = row slot of the block
-#pragma unroll
-        for (int w = 0; w < kSbWarps; ++w) v += rd[w * kRB + lane];
         if (lane == 0) cnt[buf] = 0u;
-        if (sg.epi == EPI_SWIGLU) {
-            const float up = __shfl_down_sync(0xffffffffu, v, kSlabRows);
-            const uint32_t row = local * kSlabRows + lane;
-            if (lane < (int)kSlabRows && row < sg.m.rows) sg.y[row] = __fmul_rn(silu(v), up);
-        } else {
-            const uint32_t row = local * kRB + lane;
-            if (row < sg.m.rows) {
-                if (sg.epi == EPI_ADD)
-                    sg.y[row] = (cached ? reinterpret_cast<const float*>(xs + p.off_rows)[(rb - rb0) * kRB + lane]
-                                        : __ldcg(sg.y + row)) + v;
-                else sg.y[row] = v;
-            }
-        }
+        finish_row(p, xs, rd, rb, rb0, (uint32_t)lane, inv, cached);  // lane = row slot of the block
+    }
+    if (deferred) {
+        named_sync(kConsumerBarrier, kCW * 32);
+        const uint32_t c = (uint32_t)(warp * 32 + lane);
+        if (c < (rb1 - rb0) * kRB)
+            finish_row(p, xs, red + (c / kRB) * (kSbWarps * kRB), rb0 + c / kRB, rb0, c % kRB, inv, cached);
     }
     return true;
 }
@@ -648,7 +671,7 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
     if (a.nseg < 1 || a.nseg > kMaxSegs || a.cols % 64 != 0 || a.cols == 0 || !a.err) return cudaErrorInvalidValue;
     // the staging reads x, norm_w and writes x_out as float4
     auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-    if (!a.x || misaligned(a.x) || misaligned(a.norm_w) || misaligned(a.x_out)) return cudaErrorMisalignedAddress;
+    if (!a.x || misaligned(a.x) || misaligned(a.norm_w)) return cudaErrorMisalignedAddress;
     p = Plan{};
     p.a = a;
     p.err = a.err;

@@ -411,7 +411,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     if (ph > 0 && !bwait(&st_empty[s], (ph - 1) & 1, &abort_flag)) break;
                     uint8_t* dst = smem + s * stage_bytes;
                     mbar_arrive_expect_tx(&st_full[s], stage_bytes);
-                    tma_load_1d(dst, A.w.q + ((uint64_t)mt * A.w.nchunks + c) * wbytes, wbytes, &st_full[s]);
+                    tma_load_1d_hint(dst, A.w.q + ((uint64_t)mt * A.w.nchunks + c) * wbytes, wbytes, &st_full[s],
+                                     l2_evict_first());
                     tma_load_1d(dst + wbytes, A.bx + (uint64_t)c * P.xchunk, P.xchunk, &st_full[s]);
                 }
                 if (abort_flag) break;

@@ -41,12 +41,14 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_kernel(const __grid_const
         return;
     }
 
+    NormRegs nr;
+    load_norm_regs(p, warp, lane, nr);
     pdl_wait();
     prefetch_rows(p, xs, rb0, rb1, (uint32_t)tid);
-    stage_input(p, xs, warp, lane, red);
+    const float inv = stage_input(p, xs, warp, lane, red, nr);
     pdl_launch_dependents();
     RingPos rp;
-    if (!consume_items(p, r, xs, rb0, rb1, rp, warp, lane, &abort_flag) && lane == 0)
+    if (!consume_items(p, r, xs, rb0, rb1, rp, warp, lane, &abort_flag, inv) && lane == 0)
         atomicExch(p.err, DEV_ERR_WAIT_TIMEOUT);
 }
 

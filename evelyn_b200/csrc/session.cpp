@@ -103,11 +103,17 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
     {  // attention with QK-norm/RoPE/append and the split merge in one cluster launch
-        // (one sequence only: a batch's many (sequence, kv head) pairs run faster on the
-        // split kernels, which keep more CTAs per SM)
+        // A batch takes the tensor-core path (f16 KV): the scalar loop of a batch's many
+        // (sequence, kv head) pairs runs slower than the split kernels. One sequence takes
+        // the scalar loop (a split holds too few positions for the tensor-core tiles to
+        // pay); EVELYN_ATTN_MMA=1 forces the tensor cores, =0 keeps them off.
         const char* fe = std::getenv("EVELYN_FUSED_ATTN");
-        if (batch == 1 && !(fe && fe[0] == '0')) {
-            const uint32_t C = 8;  // splits per kv head
+        const char* me = std::getenv("EVELYN_ATTN_MMA");
+        const bool mma_ok = elem == 2 && (me ? me[0] == '1' : batch > 1);
+        if ((batch == 1 || mma_ok) && !(fe && fe[0] == '0')) {
+            // one sequence: 8 splits per kv head; a batch: as few as keep ~2 CTAs per SM busy
+            uint32_t C = 8;
+            while (C > 1 && m->lkv_heads * batch * C > 2u * (uint32_t)sms) C /= 2;
             // EVELYN_ATTN_RING caps the ring (even, >= 2), so tests reach the streamed
             // multi-chunk case at small contexts
             const char* re = std::getenv("EVELYN_ATTN_RING");
@@ -118,6 +124,8 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             if (ring) {
                 b.cluster_splits = C;
                 b.cluster_ring = ring;
+                if (mma_ok) b.kv_tmap_ok = make_kv_tmap(b.kv.p, b.kv.bytes, (uint32_t)hd, &b.kv_tmap);
+                if (batch > 1 && !b.kv_tmap_ok) b.cluster_ring = 0;  // no tensor map: split kernels
             }
         }
     }
@@ -223,7 +231,7 @@ void Decoder::enqueue_batched(bool pdl) {
         gemm_reduce(L.v, p1, k1, b.v.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
         if (b.cluster_ring) {
             cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream,
-                                                pdl),
+                                                pdl, b.kv_tmap_ok ? &b.kv_tmap : nullptr),
                        "attention");
             kernels += 1;
         } else {
@@ -336,7 +344,8 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         kernels += B;
     }
     if (b.cluster_ring) {
-        cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream, pdl),
+        cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream, pdl,
+                                            b.kv_tmap_ok ? &b.kv_tmap : nullptr),
                    "attention");
         kernels += 1;
     } else {

@@ -457,17 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     RingPos rp;
     bool ok = true;
     for (uint32_t ph = 0; ph < A.nphases && ok; ++ph) {
+        const StepPhase& P = A.phases[ph];
+        NormRegs nr;
+        if (P.kind == PH_MATVEC) load_norm_regs(P.mv, warp, lane, nr);  // static: before the barrier
         if (ph > 0 && !grid_sync(A, bar_base + (unsigned long long)ph * gridDim.x, tc, &abort_flag, &ok_sh)) {
             ok = false;
             break;
         }
-        const StepPhase& P = A.phases[ph];
         if (P.kind == PH_MATVEC) {
             uint32_t rb0, rb1;
             cta_rows(P.mv, blockIdx.x, gridDim.x, rb0, rb1);
             prefetch_rows(P.mv, xs, rb0, rb1, (uint32_t)tc);
-            stage_input(P.mv, xs, warp, lane, red);
-            if (!consume_items(P.mv, ring, xs, rb0, rb1, rp, warp, lane, &abort_flag)) ok = false;
+            const float inv = stage_input(P.mv, xs, warp, lane, red, nr);
+            if (!consume_items(P.mv, ring, xs, rb0, rb1, rp, warp, lane, &abort_flag, inv)) ok = false;
         } else {
             const int32_t pos = __ldcg(P.att.rope.pos);
             if (pos < 0 || (uint32_t)pos / P.att.at.kv.page_size >= P.att.at.max_pages) {

@@ -62,6 +62,31 @@ def test_host_argmax_log_prob_match_oracle():
     assert evl.argmax(np.array([np.nan, 1.0], dtype=np.float32)) == 1
 
 
+def test_host_argmax_edges():
+    """The blocked scan keeps runtime.rs:897-905's semantics: the first maximum, NaN
+    never wins, nothing above f32::MIN gives 0, ties across and inside 256-value blocks,
+    ragged tails."""
+    rng = np.random.default_rng(1)
+    fmin = np.float32(np.finfo(np.float32).min)
+    for trial in range(300):
+        n = int(rng.integers(0, 1300))
+        v = rng.integers(-3, 3, n).astype(np.float32)
+        if trial % 5 == 0 and n:
+            v[rng.integers(0, n, 3)] = np.nan
+        if trial % 7 == 0:
+            v[:] = -np.inf
+        if trial % 11 == 0:
+            v[:] = fmin
+        if trial % 13 == 0 and n:
+            v[rng.integers(0, n, 2)] = 7.0
+        assert evl.argmax(v) == orc.argmax(v), (trial, n)
+    v = np.zeros(151936, dtype=np.float32)
+    v[[70000, 151935]] = 1.0
+    assert evl.argmax(v) == 70000
+    v[151935] = 2.0
+    assert evl.argmax(v) == 151935
+
+
 def test_validate_token_ids():
     evl.validate_token_ids([0, 17, 99], 100)
     with pytest.raises(evl.EvelynError) as e:

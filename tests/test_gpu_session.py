@@ -133,11 +133,16 @@ def test_failing_hook_falls_back_to_dense():
     assert s.fallbacks == 4
 
 
-@pytest.mark.parametrize("B,gemm", [(3, "1"), (32, "1"), (3, "0")])
-def test_batch_matches_independent_sessions(B, gemm, monkeypatch):
+@pytest.mark.parametrize("B,gemm,attn", [(3, "1", {}), (32, "1", {}), (3, "0", {}), (32, "1", {"EVELYN_ATTN_MMA": "0"}),
+                                         (5, "1", {"EVELYN_ATTN_RING": "2"})])
+def test_batch_matches_independent_sessions(B, gemm, attn, monkeypatch):
     """A Batch step (tensor-core products for 2..32 sequences, or one matvec per
-    sequence with EVELYN_BATCH_GEMM=0) against independent sessions and the oracle."""
+    sequence with EVELYN_BATCH_GEMM=0; tensor-core cluster attention, its pages streamed
+    through a 2-page ring, or the split attention kernels with EVELYN_ATTN_MMA=0)
+    against independent sessions and the oracle."""
     monkeypatch.setenv("EVELYN_BATCH_GEMM", gemm)
+    for k, v in attn.items():
+        monkeypatch.setenv(k, v)
     spec = synth.tiny(seed=13)
     img = synth.build(spec)
     m = evl.Model.load_memory(img, device=0)
@@ -147,7 +152,7 @@ def test_batch_matches_independent_sessions(B, gemm, monkeypatch):
     oracles = [orc.Session(r) for _ in range(min(B, 2))]
     rng = np.random.default_rng(0)
     worst = 0.0
-    for _ in range(10):
+    for _ in range(40 if attn else 10):
         toks = rng.integers(0, spec.vocab, B)
         got = batch.step(toks)
         for i, s in enumerate(sessions):
@@ -212,17 +217,20 @@ def test_load_errors():
     assert e.value.kind == "InvalidData"
 
 
-@pytest.mark.parametrize("ring", [2, 4])
-def test_cluster_attention_streamed_pages(monkeypatch, ring):
+@pytest.mark.parametrize("ring,mma", [(2, "0"), (4, "0"), (2, "1"), (16, "1")])
+def test_cluster_attention_streamed_pages(monkeypatch, ring, mma):
     """Single-sequence attention with its KV pages streamed through a small shared ring
-    (many chunks per split) against the unfused three-kernel path and the oracle."""
+    (many chunks per split), on the scalar loop or the tensor cores, against the
+    unfused three-kernel path and the oracle."""
     spec = synth.tiny(seed=23, layers=2)
     img, m, r = _models(spec)
     toks = _tokens(150, spec.vocab, seed=9)
     monkeypatch.setenv("EVELYN_ATTN_RING", str(ring))
+    monkeypatch.setenv("EVELYN_ATTN_MMA", mma)
     s1 = evl.Session(m, max_ctx=256)
     out1 = [s1.step(t) for t in toks]
     monkeypatch.delenv("EVELYN_ATTN_RING")
+    monkeypatch.delenv("EVELYN_ATTN_MMA")
     monkeypatch.setenv("EVELYN_FUSED_ATTN", "0")
     s2 = evl.Session(m, max_ctx=256)
     out2 = [s2.step(t) for t in toks]
