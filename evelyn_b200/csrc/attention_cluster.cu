@@ -38,7 +38,9 @@ namespace {
 namespace cg = cooperative_groups;
 
 constexpr int kAW = 16;  // warps per CTA
+constexpr uint32_t kMaxSplits = 8;  // CTAs per cluster (portable cluster size)
 constexpr uint32_t kMaxRingPages = 16;
+static_assert(kMaxRingPages / 2 <= 32, "warp 0 copies a chunk's pages one per lane");
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
 
 struct ClusterAttn {
@@ -125,11 +127,36 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
     lo = pack_h2(a - __half2float(ha), b - __half2float(hb));
 }
 
+// Merge weights of n partials [n][G][stride] (o..., m, l): per head g the maximum M of
+// the partials' m, fac[k][g] = exp(m_k - M) (-1 for an empty partial, m = -inf) and
+// L = sum_k l_k fac[k][g] in k order. Threads tid < G, one head each.
+template <int G>
+__device__ __forceinline__ void merge_weights(const float* part, uint32_t stride, int n, float* fac, float* mm, float* ml,
+                                              int tid) {
+    if (tid >= G) return;
+    float M = -INFINITY;
+    for (int k = 0; k < n; ++k) M = fmaxf(M, part[(k * G + tid) * stride + stride - 2]);
+    float L = 0.f;
+    for (int k = 0; k < n; ++k) {
+        const float* pp = part + (k * G + tid) * stride + stride - 2;
+        if (pp[0] == -INFINITY) {
+            fac[k * G + tid] = -1.f;
+            continue;
+        }
+        const float f = expf(pp[0] - M);
+        fac[k * G + tid] = f;
+        L += pp[1] * f;
+    }
+    mm[tid] = M;
+    ml[tid] = L;
+}
+
 // Shared-memory bytes of one CTA (ring, q, per-warp vectors, warp partials, CTA partial).
 __host__ __device__ __forceinline__ size_t cluster_smem(uint32_t ring_pages, uint32_t ps, uint32_t hd, uint32_t eb,
                                                        uint32_t G) {
     return 1024 + (size_t)ring_pages * 2 * ps * hd * eb + 4ull * G * hd + 4ull * (G + 2) * hd +
-           4ull * kAW * G * (hd + 2) + 4ull * G * (hd + 2) + 2ull * 32 * hd;  // + q fragments (hd/16 x 32 x 16 B)
+           4ull * kAW * G * (hd + 2) + 4ull * kMaxSplits * G * (hd + 2) +
+           2ull * 32 * hd;  // + q fragments (hd/16 x 32 x 16 B)
 }
 
 template <typename KV, int G, int HD, bool MM>
@@ -153,8 +180,9 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     float* qs = reinterpret_cast<float*>(smem + (size_t)F.ring_pages * 2 * tile * sizeof(KV));  // [G][HD]
     float* vec = qs + G * HD;                                                 // [G+2][HD] per-warp vectors
     float* wpart = vec + (G + 2) * HD;                                        // [warps][G][HD+2]
-    float* cpart = wpart + kAW * G * (HD + 2);                                // [G][HD+2]: o, m, l
-    uint4* qfrag = reinterpret_cast<uint4*>(cpart + G * (HD + 2));            // [HD/16][lanes]: q hi/lo fragments
+    float* cpart = wpart + kAW * G * (HD + 2);  // rank 0: [split][G][HD+2] (o, m, l) of every CTA
+    uint4* qfrag = reinterpret_cast<uint4*>(cpart + kMaxSplits * G * (HD + 2));  // [HD/16][lanes]: q hi/lo fragments
+    __shared__ float fac[kAW * G], mrg_m[G], mrg_l[G];  // merge weights, maxima and sums
 
     if (tid == 0) {
         mbar_init(&full[0], 1);
@@ -178,10 +206,14 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // c & 1 (double buffering): chunks 0 and 1 are issued now, chunk c + 2 once every
     // warp is done with chunk c.
     const uint32_t H = F.ring_pages / 2, nch = (npg + H - 1) / H;
-    auto issue = [&](uint32_t c) {  // consumer thread 0
+    // Warp 0 issues a chunk: lane 0 sets the byte count, lane i reads the page id of
+    // page p0 + i and copies it (the page ids arrive in one round trip, not one each).
+    auto issue = [&](uint32_t c) {
         const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c & 1;
-        mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
-        for (uint32_t i = p0; i < p1; ++i) {
+        if (lane == 0) mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
+        __syncwarp();
+        const uint32_t i = p0 + (uint32_t)lane;
+        if (i < p1) {
             const int32_t page = __ldcg(ptab + t0 / ps + i);
             KV* slot = ring + (half * H + (i - p0)) * 2 * tile;
             if constexpr (MM) {  // row coordinates of the K and V tiles in the pool's [rows][HD] view
@@ -199,9 +231,9 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             }
         }
     };
-    if (tid == 0) {
+    if (warp == 0) {
         if (!valid) {
-            atomicExch(a.err, DEV_ERR_POSITION);
+            if (lane == 0) atomicExch(a.err, DEV_ERR_POSITION);
         } else {
             if (nch > 0) issue(0);
             if (nch > 1) issue(1);
@@ -418,7 +450,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             }
         }
         __syncthreads();  // every warp is done with this half of the ring
-        if (tid == 0 && c + 2 < nch) issue(c + 2);
+        if (warp == 0 && c + 2 < nch) issue(c + 2);
     }
     if constexpr (MM) {
         lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
@@ -448,46 +480,39 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
     __syncthreads();
-    // ---- this CTA's partial: the warps merged in order (attention_combine_kernel's arithmetic)
+    // ---- this CTA's partial: the warps merged in order (attention_combine_kernel's
+    // arithmetic). The weight exp(m_w - M) of a (warp, head) is the same for every
+    // dimension, so G threads compute them once; the partial goes straight into rank
+    // 0's shared memory (slot `rank`), which then merges the splits from its own copy.
+    merge_weights<G>(wpart, HD + 2, kAW, fac, mrg_m, mrg_l, tid);
+    __syncthreads();
+    float* dst = cl.map_shared_rank(cpart, 0) + rank * G * (HD + 2);
     for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
         const uint32_t g = i / HD, d = i % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < kAW; ++w) M = fmaxf(M, wpart[(w * G + g) * (HD + 2) + HD]);
-        float L = 0.f, O = 0.f;
+        float O = 0.f;
         for (int w = 0; w < kAW; ++w) {
-            const float* wp = wpart + (w * G + g) * (HD + 2);
-            if (wp[HD] == -INFINITY) continue;
-            const float f = expf(wp[HD] - M);
-            L += wp[HD + 1] * f;
-            O += wp[d] * f;
+            const float f = fac[w * G + g];
+            if (f >= 0.f) O += wpart[(w * G + g) * (HD + 2) + d] * f;  // f < 0: an empty warp
         }
-        cpart[g * (HD + 2) + d] = O;
+        dst[g * (HD + 2) + d] = O;
         if (d == 0) {
-            cpart[g * (HD + 2) + HD] = M;
-            cpart[g * (HD + 2) + HD + 1] = L;
+            dst[g * (HD + 2) + HD] = mrg_m[g];
+            dst[g * (HD + 2) + HD + 1] = mrg_l[g];
         }
     }
-    cl.sync();  // every CTA's partial is in its shared memory
-    if (rank == 0) {
-        for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
-            const uint32_t g = i / HD, d = i % HD;
-            float M = -INFINITY;
-            for (uint32_t c = 0; c < C; ++c) {
-                const float* cp = cl.map_shared_rank(cpart, c);
-                M = fmaxf(M, cp[g * (HD + 2) + HD]);
-            }
-            float L = 0.f, O = 0.f;
-            for (uint32_t c = 0; c < C; ++c) {
-                const float* cp = cl.map_shared_rank(cpart, c) + g * (HD + 2);
-                if (cp[HD] == -INFINITY) continue;
-                const float f = expf(cp[HD] - M);
-                L += cp[HD + 1] * f;
-                O += cp[d] * f;
-            }
-            if (valid && !bad_sh) a.out[((uint64_t)sq * a.heads + kvh * G + g) * HD + d] = O / L;
+    cl.sync();  // every CTA's partial is in rank 0's shared memory
+    if (rank != 0) return;
+    merge_weights<G>(cpart, HD + 2, (int)C, fac, mrg_m, mrg_l, tid);
+    __syncthreads();
+    for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
+        const uint32_t g = i / HD, d = i % HD;
+        float O = 0.f;
+        for (uint32_t c = 0; c < C; ++c) {
+            const float f = fac[c * G + g];
+            if (f >= 0.f) O += cpart[(c * G + g) * (HD + 2) + d] * f;
         }
+        if (valid && !bad_sh) a.out[((uint64_t)sq * a.heads + kvh * G + g) * HD + d] = O / mrg_l[g];
     }
-    cl.sync();  // the partials stay in place until rank 0 has read them
 }
 
 template <typename KV, int G, int HD, bool MM>
@@ -571,7 +596,8 @@ bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* o
 
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
                                      bool pdl, const KvTmap* tmap) {
-    if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1))
+    if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1) ||
+        a.nsplit < 1 || a.nsplit > kMaxSplits)
         return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
     if (!a.kv_heads || a.heads % a.kv_heads ||

@@ -47,6 +47,7 @@ constexpr uint32_t kRedBufs = kMaxStages + 1;            // row-block partial bu
 constexpr uint32_t kRedBufBytes = kSbWarps * kRB * 4;
 constexpr uint32_t kRedBytes = kRedBufs * kRedBufBytes + 16 * kRedBufs;  // + arrival counters
 constexpr uint32_t kRowBuf = 256;  // residual rows a CTA keeps in shared memory
+constexpr uint32_t kMaxCtas = 1024;  // grid bound of the row-block partition's 32-bit arithmetic
 static_assert(kSbWarps * 4 == kPanelUnits, "each consumer warp of a slab takes one super-block of a panel");
 
 // need bits
@@ -56,6 +57,8 @@ constexpr uint32_t NEED_XSUM = 1, NEED_MSUM = 2;
 struct Plan {
     MatvecArgs a;
     uint32_t rb_begin[kMaxSegs + 1];  // first row-block of each segment (+ total)
+    uint32_t rb_w[kMaxSegs];          // weight of one row block of each segment (bytes >> a shift)
+    uint32_t total_w;                 // of all row blocks, < 2^31 / (2 * kMaxCtas)
     uint32_t nunits, ngroups, last_units;  // units per row, panels per row, units of the last panel
     uint32_t item_bytes;  // largest stage (two slabs x one 32-unit panel) of any segment
     uint32_t need;
@@ -457,11 +460,31 @@ __device__ __forceinline__ void prefetch_rows(const Plan& p, uint8_t* xs, uint32
     reinterpret_cast<float*>(xs + p.off_rows)[c] = row < sg.m.rows ? __ldcg(sg.y + row) : 0.f;
 }
 
-// This CTA's row blocks [rb0, rb1) of a plan. Every CTA takes a contiguous range.
+// The first row block whose byte midpoint lies at or past c / n of the plan's weight
+// bytes: row block k goes to the CTA whose equal share of the bytes holds its
+// midpoint, so segments of heavier types (a Q6_K block is 1.46 Q4_K blocks) spread
+// over more CTAs instead of doubling up on some.
+__host__ __device__ __forceinline__ uint32_t rb_boundary(const Plan& p, uint32_t c, uint32_t n) {
+    if (c >= n) return p.rb_begin[kMaxSegs];
+    // 32-bit: total_w * 2 * n < 2^31 (the host picks the weight unit)
+    const uint32_t t2 = 2u * c * p.total_w;  // (2 W_before + (2k + 1) w) n >= t2
+    uint32_t wb = 0;
+    for (int s = 0; s < kMaxSegs; ++s) {
+        const uint32_t nrb = p.rb_begin[s + 1] - p.rb_begin[s], w = p.rb_w[s];
+        if (nrb && (2 * wb + (2 * nrb - 1) * w) * n >= t2) {
+            const uint32_t base = (2 * wb + w) * n;
+            const uint32_t k = base >= t2 ? 0 : (t2 - base + 2 * w * n - 1) / (2 * w * n);
+            return p.rb_begin[s] + k;
+        }
+        wb += nrb * w;
+    }
+    return p.rb_begin[kMaxSegs];
+}
+// This CTA's row blocks [rb0, rb1) of a plan: a contiguous range of about 1/ncta of
+// the weight bytes.
 __device__ __forceinline__ void cta_rows(const Plan& p, uint32_t cta, uint32_t ncta, uint32_t& rb0, uint32_t& rb1) {
-    const uint32_t total = p.rb_begin[kMaxSegs];
-    rb0 = (uint32_t)(((uint64_t)total * cta) / ncta);
-    rb1 = (uint32_t)(((uint64_t)total * (cta + 1)) / ncta);
+    rb0 = rb_boundary(p, cta, ncta);
+    rb1 = rb_boundary(p, cta + 1, ncta);
 }
 
 // Global addresses of item (rb, g): panel g of the one or two 16-row slabs one stage
@@ -686,7 +709,7 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
             const MatvecSeg& sg = a.seg[i];
             const uint32_t t = sg.m.type;
             if (t != GGML_Q4_K && t != GGML_Q6_K && t != GGML_Q8_0) return cudaErrorInvalidValue;
-            if (sg.m.cols != a.cols || sg.m.rows == 0 || !sg.y) return cudaErrorInvalidValue;
+            if (sg.m.cols != a.cols || sg.m.rows == 0 || sg.m.row_bytes == 0 || !sg.y) return cudaErrorInvalidValue;
             if (sg.epi == EPI_SWIGLU && (sg.m2.type != t || sg.m2.rows != sg.m.rows || sg.m2.cols != a.cols))
                 return cudaErrorInvalidValue;
             if (t == GGML_Q6_K) p.need |= NEED_MSUM;
@@ -696,6 +719,19 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
             rbs = (sg.m.rows + per - 1) / per;
         }
         p.rb_begin[i + 1] = p.rb_begin[i] + rbs;
+    }
+    // row-block weights in units of 2^sh bytes, small enough for 32-bit boundaries
+    for (uint32_t sh = 0; sh < 40; ++sh) {
+        uint64_t tot = 0;
+        for (int i = 0; i < a.nseg; ++i) {
+            p.rb_w[i] = (uint32_t)std::max<uint64_t>(1, ((uint64_t)kRB * a.seg[i].m.row_bytes) >> sh);
+            tot += (uint64_t)(p.rb_begin[i + 1] - p.rb_begin[i]) * p.rb_w[i];
+        }
+        if (tot * 2 * kMaxCtas < (1ull << 31)) {
+            p.total_w = (uint32_t)tot;
+            break;
+        }
+        if (sh == 39) return cudaErrorInvalidValue;
     }
     const uint32_t K = a.cols, nb = K / 32;
     uint32_t off = p.nunits * kXUnit;  // B fragments

@@ -103,13 +103,12 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     b.nsplit = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>({want, by_len, 1u}), b.pages_per_seq));
     b.part.alloc((uint64_t)batch * m->lheads * b.nsplit * (hd + 2) * 4);
     {  // attention with QK-norm/RoPE/append and the split merge in one cluster launch
-        // A batch takes the tensor-core path (f16 KV): the scalar loop of a batch's many
-        // (sequence, kv head) pairs runs slower than the split kernels. One sequence takes
-        // the scalar loop (a split holds too few positions for the tensor-core tiles to
-        // pay); EVELYN_ATTN_MMA=1 forces the tensor cores, =0 keeps them off.
+        // f16 pages take the tensor-core loop (EVELYN_ATTN_MMA=0: the scalar one). A batch
+        // without it uses the split kernels, which run its many (sequence, kv head) pairs
+        // faster than the scalar loop.
         const char* fe = std::getenv("EVELYN_FUSED_ATTN");
         const char* me = std::getenv("EVELYN_ATTN_MMA");
-        const bool mma_ok = elem == 2 && (me ? me[0] == '1' : batch > 1);
+        const bool mma_ok = elem == 2 && !(me && me[0] == '0');
         if ((batch == 1 || mma_ok) && !(fe && fe[0] == '0')) {
             // one sequence: 8 splits per kv head; a batch: as few as keep ~2 CTAs per SM busy
             uint32_t C = 8;
