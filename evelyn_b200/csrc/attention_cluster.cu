@@ -127,28 +127,29 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
     lo = pack_h2(a - __half2float(ha), b - __half2float(hb));
 }
 
-// Merge weights of n partials [n][G][stride] (o..., m, l): per head g the maximum M of
-// the partials' m, fac[k][g] = exp(m_k - M) (-1 for an empty partial, m = -inf) and
-// L = sum_k l_k fac[k][g] in k order. Threads tid < G, one head each.
+// Merge weights of n <= 32 partials [n][G][stride] (o..., m, l): per head g the
+// maximum M of the partials' m, fac[k][g] = exp(m_k - M) (-1 for an empty partial,
+// m = -inf) and L = sum_k l_k fac[k][g]. Warp g (< G) takes head g, lane k partial k;
+// the maximum and the sum meet by butterfly shuffles.
 template <int G>
 __device__ __forceinline__ void merge_weights(const float* part, uint32_t stride, int n, float* fac, float* mm, float* ml,
-                                              int tid) {
-    if (tid >= G) return;
-    float M = -INFINITY;
-    for (int k = 0; k < n; ++k) M = fmaxf(M, part[(k * G + tid) * stride + stride - 2]);
-    float L = 0.f;
-    for (int k = 0; k < n; ++k) {
-        const float* pp = part + (k * G + tid) * stride + stride - 2;
-        if (pp[0] == -INFINITY) {
-            fac[k * G + tid] = -1.f;
-            continue;
-        }
-        const float f = expf(pp[0] - M);
-        fac[k * G + tid] = f;
-        L += pp[1] * f;
+                                              int warp, int lane) {
+    if (warp >= G) return;
+    const float* pp = part + (lane * G + warp) * stride + stride - 2;
+    const float m = lane < n ? pp[0] : -INFINITY;
+    float M = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const bool empty = m == -INFINITY;  // also every lane >= n
+    const float f = empty ? 0.f : expf(m - M);
+    float L = empty ? 0.f : pp[1] * f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane < n) fac[lane * G + warp] = empty ? -1.f : f;
+    if (lane == 0) {
+        mm[warp] = M;
+        ml[warp] = L;
     }
-    mm[tid] = M;
-    ml[tid] = L;
 }
 
 // Shared-memory bytes of one CTA (ring, q, per-warp vectors, warp partials, CTA partial).
@@ -162,6 +163,7 @@ __host__ __device__ __forceinline__ size_t cluster_smem(uint32_t ring_pages, uin
 template <typename KV, int G, int HD, bool MM>
 __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_constant__ ClusterAttn F) {
     constexpr int DPL = HD / 32;
+    static_assert(G <= kAW && kAW <= 32 && kMaxSplits <= 32, "one warp per head merges up to 32 partials");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the ring starts on a 1024-byte boundary (the swizzle atom of the tensor copies)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // arithmetic). The weight exp(m_w - M) of a (warp, head) is the same for every
     // dimension, so G threads compute them once; the partial goes straight into rank
     // 0's shared memory (slot `rank`), which then merges the splits from its own copy.
-    merge_weights<G>(wpart, HD + 2, kAW, fac, mrg_m, mrg_l, tid);
+    merge_weights<G>(wpart, HD + 2, kAW, fac, mrg_m, mrg_l, warp, lane);
     __syncthreads();
     float* dst = cl.map_shared_rank(cpart, 0) + rank * G * (HD + 2);
     for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
@@ -502,7 +504,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     }
     cl.sync();  // every CTA's partial is in rank 0's shared memory
     if (rank != 0) return;
-    merge_weights<G>(cpart, HD + 2, (int)C, fac, mrg_m, mrg_l, tid);
+    merge_weights<G>(cpart, HD + 2, (int)C, fac, mrg_m, mrg_l, warp, lane);
     __syncthreads();
     for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
         const uint32_t g = i / HD, d = i % HD;

@@ -9,7 +9,9 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -198,9 +200,20 @@ void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s);
 // returns false (nothing built) when some matrix has no GEMM layout.
 bool build_gemm_weights(Model& m);
 
+// Per-CTA budget of a matvec's L2 prefetch of the next launches' weights, in KB:
+// `dflt` scaled by the percentage in EVELYN_PREFETCH (0 turns the prefetch off).
+inline uint32_t prefetch_kb(uint32_t dflt) {
+    static const int pct = [] {
+        const char* e = std::getenv("EVELYN_PREFETCH");
+        return e ? std::max(0, std::atoi(e)) : 100;
+    }();
+    return (uint32_t)((uint64_t)dflt * (uint32_t)pct / 100);
+}
+
 // Device launch sequence of one dense FFN on `x` (already normalised when norm_w is
 // null) writing y; add=true accumulates into y (residual). TP: partial + all-reduce.
-// `next` (may be null) is the matrix the launch after the FFN reads (warmed into L2).
+// `next` (may be null) holds the three matrices the launch after the FFN reads
+// (unused entries have q == null), warmed into L2.
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
                    float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl);
 

@@ -34,8 +34,10 @@ struct MatvecArgs {
     uint32_t cols = 0;
     const float* norm_w = nullptr; // fused RMSNorm weight (null: x used as is)
     float eps = 1e-6f;
-    QMatDev prefetch;              // matrix the next launch reads (q == null: none); its
-                                   // first rows are warmed into L2 at the end
+    QMatDev prefetch[3];           // matrices the next launches read, in order (q == null:
+                                   // none); this CTA's share of each is warmed into L2 at
+                                   // the end, up to prefetch_bytes per CTA
+    uint32_t prefetch_bytes = 96u << 10;
     int* err = nullptr;            // device error flag (DeviceError), required
 };
 

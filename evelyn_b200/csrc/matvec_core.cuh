@@ -65,8 +65,8 @@ struct Plan {
     uint32_t off_fscale, off_xsum, off_msum, off_red;  // offsets in the staged-input area (B fragments at 0)
     uint32_t off_rows;                                 // residual rows of this CTA (kRowBuf floats)
     uint32_t xbytes;                                   // size of the staged-input area
-    const uint8_t* pf_base;  // next matrix to prefetch into L2 (optional)
-    uint32_t pf_row_bytes, pf_rows;
+    const uint8_t* pf_base[3];  // next matrices to prefetch into L2 (optional)
+    uint32_t pf_row_bytes[3], pf_rows[3], pf_cap;
     int* err;
 };
 
@@ -546,18 +546,23 @@ __device__ bool produce_items(const Plan& p, const Ring& r, uint32_t rb0, uint32
     return true;
 }
 
-// Producer, after its last copy of a plan: warm L2 with the first slabs of the next
-// matrix this CTA index will read (at most 96 KB).
+// Producer, after its last copy of a plan: warm L2 with this CTA index's share of the
+// next matrices, in order, at most pf_cap bytes in all. The next kernels' CTAs start
+// only as this one's leave; meanwhile HBM keeps streaming their first tiles.
 __device__ void prefetch_next(const Plan& p, uint32_t cta, uint32_t ncta) {
-    if (!p.pf_base || !p.pf_rows) return;
-    const uint32_t slabs = (p.pf_rows + kSlabRows - 1) / kSlabRows;
-    const uint32_t pr0 = (uint32_t)(((uint64_t)slabs * cta) / ncta);
-    const uint32_t pr1 = (uint32_t)(((uint64_t)slabs * (cta + 1)) / ncta);
-    uint64_t bytes = (uint64_t)(pr1 - pr0) * kSlabRows * p.pf_row_bytes;
-    if (bytes > (96u << 10)) bytes = 96u << 10;
-    const uint8_t* base = p.pf_base + (uint64_t)pr0 * kSlabRows * p.pf_row_bytes;
-    for (uint64_t o = 0; o < bytes; o += 16384)
-        prefetch_l2_bulk(base + o, (uint32_t)((bytes - o) < 16384 ? (bytes - o) & ~15ull : 16384));
+    uint64_t left = p.pf_cap;
+    for (int i = 0; i < 3 && left; ++i) {
+        if (!p.pf_base[i] || !p.pf_rows[i]) continue;
+        const uint32_t slabs = (p.pf_rows[i] + kSlabRows - 1) / kSlabRows;
+        const uint32_t pr0 = (uint32_t)(((uint64_t)slabs * cta) / ncta);
+        const uint32_t pr1 = (uint32_t)(((uint64_t)slabs * (cta + 1)) / ncta);
+        uint64_t bytes = (uint64_t)(pr1 - pr0) * kSlabRows * p.pf_row_bytes[i];
+        if (bytes > left) bytes = left;
+        left -= bytes;
+        const uint8_t* base = p.pf_base[i] + (uint64_t)pr0 * kSlabRows * p.pf_row_bytes[i];
+        for (uint64_t o = 0; o < bytes; o += 16384)
+            prefetch_l2_bulk(base + o, (uint32_t)((bytes - o) < 16384 ? (bytes - o) & ~15ull : 16384));
+    }
 }
 
 // Producer: after an abort, give the copies in flight a bounded chance to land.
@@ -748,9 +753,12 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
     p.xbytes = (off + 127) & ~127u;
     p.item_bytes = slot;
     if (p.xbytes + 2 * slot > kSmemBudget) return cudaErrorInvalidValue;
-    p.pf_base = a.prefetch.q;
-    p.pf_row_bytes = a.prefetch.row_bytes;
-    p.pf_rows = a.prefetch.q ? a.prefetch.rows : 0;
+    for (int i = 0; i < 3; ++i) {
+        p.pf_base[i] = a.prefetch[i].q;
+        p.pf_row_bytes[i] = a.prefetch[i].row_bytes;
+        p.pf_rows[i] = a.prefetch[i].q ? a.prefetch[i].rows : 0;
+    }
+    p.pf_cap = a.prefetch_bytes;
     return cudaSuccess;
 }
 

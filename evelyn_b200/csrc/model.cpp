@@ -373,7 +373,10 @@ void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, 
         a.norm_w = norm_w;
         a.eps = m.cfg.eps;
         a.err = err;
-        if (b + 1 == batch) a.prefetch = L.down.dev;
+        if (b + 1 == batch) {
+            a.prefetch[0] = L.down.dev;
+            a.prefetch_bytes = prefetch_kb(96) << 10;
+        }
         cuda_check(launch_qmatvec(a, s, pdl), "ffn gate/up");
     }
     const bool tp = m.tp_size > 1;
@@ -386,7 +389,10 @@ void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, 
         a.x = h_buf + (size_t)b * m.lffn;
         a.cols = m.lffn;
         a.err = err;
-        if (next && b + 1 == batch) a.prefetch = *next;
+        if (next && b + 1 == batch) {
+            for (int i = 0; i < 3; ++i) a.prefetch[i] = next[i];
+            a.prefetch_bytes = prefetch_kb(96) << 10;
+        }
         cuda_check(launch_qmatvec(a, s, pdl), "ffn down");
     }
     if (tp) {

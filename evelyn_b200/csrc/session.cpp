@@ -276,7 +276,11 @@ MatvecArgs Decoder::qkv_args(uint32_t li) const {
     a.norm_w = L.attn_norm;
     a.eps = c.eps;
     a.err = b.err.as<int>();
-    a.prefetch = L.o.dev;  // read after the attention kernels
+    // read after the attention kernels, which leave HBM idle
+    a.prefetch[0] = L.o.dev;
+    a.prefetch[1] = L.gate.dev;
+    a.prefetch[2] = L.up.dev;
+    a.prefetch_bytes = prefetch_kb(96) << 10;
     return a;
 }
 
@@ -363,7 +367,9 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         a.x = b.att.as<float>();
         a.cols = (uint32_t)qw;
         a.err = b.err.as<int>();
-        a.prefetch = L.gate.dev;
+        a.prefetch[0] = L.gate.dev;
+        a.prefetch[1] = L.up.dev;
+        a.prefetch_bytes = prefetch_kb(96) << 10;
         const uint64_t ys[1] = {c.dim};
         matvec_each(a, B, qw, ys, stream, pdl, "o-proj matvec");
         kernels += B;
@@ -397,7 +403,7 @@ void Decoder::build_step_kernel() {
         const LayerWeights& L = m.layers[li];
         StepLayer& s = layers[li];
         s.qkv = qkv_args(li);
-        s.qkv.prefetch = QMatDev{};
+        s.qkv.prefetch_bytes = 0;
         s.rope = rope_args(li);
         s.attn = attn_args(li, nsplit);
         s.o.nseg = 1;
@@ -491,7 +497,12 @@ void Decoder::enqueue_dense(bool pdl) {
     } else {
         for (uint32_t li = 0; li < c.layers; ++li) {
             enqueue_layer_attention(li, pdl);
-            const QMatDev* next = li + 1 < c.layers ? &m.layers[li + 1].q.dev : &m.lm_head.dev;
+            QMatDev next[3] = {m.lm_head.dev, QMatDev{}, QMatDev{}};
+            if (li + 1 < c.layers) {
+                next[0] = m.layers[li + 1].q.dev;
+                next[1] = m.layers[li + 1].k.dev;
+                next[2] = m.layers[li + 1].v.dev;
+            }
             run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch,
                           b.h.as<float>(), b.y.as<float>(), b.err.as<int>(), next, stream, pdl);
             kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);

@@ -532,8 +532,7 @@ cudaError_t step_kernel_create(const StepLayer* layers, uint32_t nlayers, int* e
             p.kind = PH_MATVEC;
             cudaError_t e = plan_matvec(*mvs[k], p.mv);
             if (e != cudaSuccess) return e;
-            p.mv.pf_base = nullptr;  // the producer runs ahead across phases instead
-            p.mv.pf_rows = 0;
+            p.mv.pf_cap = 0;  // the producer runs ahead across phases instead
             slot = std::max(slot, p.mv.item_bytes);
             xbytes = std::max(xbytes, p.mv.xbytes);
             ph.push_back(p);
