@@ -40,6 +40,7 @@ namespace cg = cooperative_groups;
 constexpr int kAW = 16;  // warps per CTA
 constexpr uint32_t kMaxSplits = 8;  // CTAs per cluster (portable cluster size)
 constexpr uint32_t kMaxRingPages = 16;
+constexpr uint32_t kMaxStages = 4;  // ring stages
 static_assert(kMaxRingPages / 2 <= 32, "warp 0 copies a chunk's pages one per lane");
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
 
@@ -48,6 +49,7 @@ struct ClusterAttn {
     RopeArgs r;
     AttnArgs a;
     uint32_t ring_pages;  // page tiles (K and V) the shared ring holds
+    uint32_t stages;      // ring stages (chunks of ring_pages / stages pages)
 };
 
 __device__ __forceinline__ const uint8_t* kv_tile(const KvCacheDev& kv, int32_t page, uint32_t layer, uint32_t which,
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the ring starts on a 1024-byte boundary (the swizzle atom of the tensor copies)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[2];  // the two halves of the page ring
+    __shared__ __align__(8) uint64_t full[kMaxStages];  // the stages of the page ring
     __shared__ int bad_sh;
     cg::cluster_group cl = cg::this_cluster();
     const RopeArgs& r = F.r;
@@ -187,8 +189,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     __shared__ float fac[kAW * G], mrg_m[G], mrg_l[G];  // merge weights, maxima and sums
 
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (uint32_t i = 0; i < F.stages; ++i) mbar_init(&full[i], 1);
         fence_barrier_init();
         bad_sh = 0;
     }
@@ -204,14 +205,15 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     const uint32_t npg = t0 < t1 ? (t1 - t0 + ps - 1) / ps : 0;
     const bool valid = pos_ok;  // the same in every thread
     const bool last = valid && npg > 0 && t1 == t_all;  // this split holds the new position
-    // The split's pages stream through the ring in chunks of H pages, chunk c into half
-    // c & 1 (double buffering): chunks 0 and 1 are issued now, chunk c + 2 once every
-    // warp is done with chunk c.
-    const uint32_t H = F.ring_pages / 2, nch = (npg + H - 1) / H;
+    // The split's pages stream through the ring in chunks of H pages, chunk c into stage
+    // c % NS: chunks 0 .. NS-1 are issued now, chunk c + NS once every warp is done with
+    // chunk c (NS = 2 for one sequence's few pages per split; a batch's long splits keep
+    // NS - 1 chunks in flight behind the one being read).
+    const uint32_t NS = F.stages, H = F.ring_pages / NS, nch = (npg + H - 1) / H;
     // Warp 0 issues a chunk: lane 0 sets the byte count, lane i reads the page id of
     // page p0 + i and copies it (the page ids arrive in one round trip, not one each).
     auto issue = [&](uint32_t c) {
-        const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c & 1;
+        const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c % NS;
         if (lane == 0) mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
         __syncwarp();
         const uint32_t i = p0 + (uint32_t)lane;
@@ -237,8 +239,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         if (!valid) {
             if (lane == 0) atomicExch(a.err, DEV_ERR_POSITION);
         } else {
-            if (nch > 0) issue(0);
-            if (nch > 1) issue(1);
+            for (uint32_t c = 0; c < NS && c < nch; ++c) issue(c);
         }
     }
     // warp w < G: q head kvh*G + w; w == G: k; w == G+1: v. Lane dims d = DPL*lane + e.
@@ -358,9 +359,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
     const uint32_t pnew = last ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
+    uint32_t cw = 0;  // chunks waited for
     for (uint32_t c = 0; valid && c < nch; ++c) {
-        const uint32_t half = c & 1, p0 = c * H, p1 = min(npg, p0 + H);
-        if (!mbar_wait(&full[half], (c >> 1) & 1)) {
+        const uint32_t half = c % NS, p0 = c * H, p1 = min(npg, p0 + H);
+        cw = c + 1;
+        if (!mbar_wait(&full[half], (c / NS) & 1)) {
             atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
             bad_sh = 1;
         }
@@ -451,9 +454,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 }
             }
         }
-        __syncthreads();  // every warp is done with this half of the ring
-        if (warp == 0 && c + 2 < nch) issue(c + 2);
+        __syncthreads();  // every warp is done with this stage of the ring
+        if (warp == 0 && c + NS < nch) issue(c + NS);
     }
+    if (bad_sh)  // a wait gave up: let the copies issued after it land before leaving
+        for (uint32_t c = cw - 1; c < nch && c < cw - 1 + NS; ++c) mbar_wait(&full[c % NS], (c / NS) & 1);
     if constexpr (MM) {
         lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
         lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
@@ -596,10 +601,10 @@ bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* o
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
-                                     bool pdl, const KvTmap* tmap) {
+cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
+                                     cudaStream_t s, bool pdl, const KvTmap* tmap) {
     if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1) ||
-        a.nsplit < 1 || a.nsplit > kMaxSplits)
+        a.nsplit < 1 || a.nsplit > kMaxSplits || stages < 2 || stages > kMaxStages || ring_pages % stages)
         return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
     if (!a.kv_heads || a.heads % a.kv_heads ||
@@ -611,6 +616,7 @@ cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint3
     F.r = r;
     F.a = a;
     F.ring_pages = ring_pages;
+    F.stages = stages;
     const bool f16 = a.kv.elem_bytes == 2;
     // tensor cores for f16 pages of 16 rows whose tiles the tensor map addresses (row
     // strides and offsets multiples of one head_dim row)

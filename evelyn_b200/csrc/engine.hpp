@@ -225,7 +225,8 @@ struct StepBuffers {
     DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
     DeviceBuffer gbx, gxinv, gpart, gpart2;  // batched products: staged x, 2^-e, partial sums
     uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
-    KvTmap kv_tmap{};                               // the KV pool for the attention's tensor-core path
+    KvTmap kv_tmap{};             // the KV pool for the attention's tensor-core path
+    uint32_t cluster_stages = 2;  // ring stages of the cluster attention
     bool kv_tmap_ok = false;
     uint32_t nsplit = 1, amax_parts = 1;
     PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;

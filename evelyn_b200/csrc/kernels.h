@@ -110,10 +110,10 @@ struct alignas(64) KvTmap {
     unsigned long long w[16];
 };
 bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* out);
-// tmap (optional): f16 pages of 16 rows run on the tensor cores (mma.sync), else the
-// scalar loop
-cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, cudaStream_t s,
-                                     bool pdl, const KvTmap* tmap = nullptr);
+// The ring streams in `stages` chunks (2 .. 4, dividing ring_pages). tmap (optional):
+// f16 pages of 16 rows run on the tensor cores (mma.sync), else the scalar loop.
+cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
+                                     cudaStream_t s, bool pdl, const KvTmap* tmap = nullptr);
 
 // ---------------------------------------------------------------- step_kernel.cu
 // One decoder layer of a single-sequence step, as the separate launches would run it:

@@ -113,6 +113,8 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             // one sequence: 8 splits per kv head; a batch: as few as keep ~2 CTAs per SM busy
             uint32_t C = 8;
             while (C > 1 && m->lkv_heads * batch * C > 2u * (uint32_t)sms) C /= 2;
+            if (const char* ce = std::getenv("EVELYN_ATTN_SPLITS"))  // 1, 2, 4 or 8 (tests)
+                for (C = 8; C > 1 && C > (uint32_t)std::strtoul(ce, nullptr, 10);) C /= 2;
             // EVELYN_ATTN_RING caps the ring (even, >= 2), so tests reach the streamed
             // multi-chunk case at small contexts
             const char* re = std::getenv("EVELYN_ATTN_RING");
@@ -123,6 +125,13 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             if (ring) {
                 b.cluster_splits = C;
                 b.cluster_ring = ring;
+                // two stages (double buffering): more, smaller chunks measured slower, the
+                // chunk's compute rather than its copy bounds a split; EVELYN_ATTN_STAGES
+                // (2 .. 4) overrides
+                const char* se = std::getenv("EVELYN_ATTN_STAGES");
+                uint32_t st = se ? (uint32_t)std::strtoul(se, nullptr, 10) : 2u;
+                while (st > 2 && (ring % st || ring / st < 2)) --st;
+                b.cluster_stages = std::max<uint32_t>(2, std::min<uint32_t>(st, 4));
                 if (mma_ok) b.kv_tmap_ok = make_kv_tmap(b.kv.p, b.kv.bytes, (uint32_t)hd, &b.kv_tmap);
                 if (batch > 1 && !b.kv_tmap_ok) b.cluster_ring = 0;  // no tensor map: split kernels
             }
@@ -229,7 +238,7 @@ void Decoder::enqueue_batched(bool pdl) {
         gemm_product(L.v, p1, k1, pdl);
         gemm_reduce(L.v, p1, k1, b.v.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
         if (b.cluster_ring) {
-            cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream,
+            cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, b.cluster_stages, stream,
                                                 pdl, b.kv_tmap_ok ? &b.kv_tmap : nullptr),
                        "attention");
             kernels += 1;
@@ -347,7 +356,7 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         kernels += B;
     }
     if (b.cluster_ring) {
-        cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, stream, pdl,
+        cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, b.cluster_stages, stream, pdl,
                                             b.kv_tmap_ok ? &b.kv_tmap : nullptr),
                    "attention");
         kernels += 1;

@@ -162,6 +162,30 @@ def test_batch_matches_independent_sessions(B, gemm, attn, monkeypatch):
     assert worst <= LOGIT_TOL, worst
 
 
+@pytest.mark.parametrize("stages", ["2", "4"])
+def test_batch_attention_ring_stages(stages, monkeypatch):
+    """Long splits streamed through a multi-stage ring (one split per sequence, 8-page
+    ring: stages of 4 or 2 pages, so the stages wrap many times) against independent
+    sessions and the oracle."""
+    monkeypatch.setenv("EVELYN_ATTN_SPLITS", "1")
+    monkeypatch.setenv("EVELYN_ATTN_RING", "8")
+    monkeypatch.setenv("EVELYN_ATTN_STAGES", stages)
+    spec = synth.tiny(seed=17, layers=2)
+    img, m, r = _models(spec)
+    batch = evl.Batch(m, 2, max_ctx=320)
+    for k in ("EVELYN_ATTN_SPLITS", "EVELYN_ATTN_RING", "EVELYN_ATTN_STAGES"):
+        monkeypatch.delenv(k)
+    s, o = evl.Session(m, max_ctx=320), orc.Session(r)
+    rng = np.random.default_rng(5)
+    worst = 0.0
+    for _ in range(300):
+        toks = rng.integers(0, spec.vocab, 2)
+        got = batch.step(toks)
+        assert np.abs(got[0] - s.step(int(toks[0]))).max() <= LOGIT_TOL
+        worst = max(worst, float(np.abs(got[1] - o.step(int(toks[1]))).max()))
+    assert worst <= LOGIT_TOL, worst
+
+
 def test_model_level_apis_match_oracle():
     spec = synth.tiny(seed=21)
     img, m, r = _models(spec)
