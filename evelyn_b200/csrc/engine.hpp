@@ -227,6 +227,7 @@ struct StepBuffers {
     uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
     KvTmap kv_tmap{};             // the KV pool for the attention's tensor-core path
     uint32_t cluster_stages = 2;  // ring stages of the cluster attention
+    uint32_t qkv_ctas = 0;        // grid cap of the QKV matvec (0: all SMs)
     bool kv_tmap_ok = false;
     uint32_t nsplit = 1, amax_parts = 1;
     PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;

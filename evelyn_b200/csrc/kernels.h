@@ -38,6 +38,7 @@ struct MatvecArgs {
                                    // none); this CTA's share of each is warmed into L2 at
                                    // the end, up to prefetch_bytes per CTA
     uint32_t prefetch_bytes = 96u << 10;
+    uint32_t max_ctas = 0;         // grid cap (0: one CTA per SM), leaving SMs to the next launch
     int* err = nullptr;            // device error flag (DeviceError), required
 };
 

@@ -76,7 +76,9 @@ cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
         g_sms[dev] = sms;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min<uint32_t>(p.rb_begin[kMaxSegs], (uint32_t)g_sms[dev]));
+    uint32_t grid = std::min<uint32_t>(p.rb_begin[kMaxSegs], (uint32_t)g_sms[dev]);
+    if (a.max_ctas) grid = std::min(grid, a.max_ctas);
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = stages * p.item_bytes + p.xbytes;
     cfg.stream = s;

@@ -132,6 +132,9 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
                 uint32_t st = se ? (uint32_t)std::strtoul(se, nullptr, 10) : 2u;
                 while (st > 2 && (ring % st || ring / st < 2)) --st;
                 b.cluster_stages = std::max<uint32_t>(2, std::min<uint32_t>(st, 4));
+                // EVELYN_QKV_CTAS caps the QKV matvec's grid so the attention's CTAs can
+                // start on the SMs it leaves free (measured slower than the full grid: off)
+                if (const char* qe = std::getenv("EVELYN_QKV_CTAS")) b.qkv_ctas = (uint32_t)std::strtoul(qe, nullptr, 10);
                 if (mma_ok) b.kv_tmap_ok = make_kv_tmap(b.kv.p, b.kv.bytes, (uint32_t)hd, &b.kv_tmap);
                 if (batch > 1 && !b.kv_tmap_ok) b.cluster_ring = 0;  // no tensor map: split kernels
             }
@@ -290,6 +293,7 @@ MatvecArgs Decoder::qkv_args(uint32_t li) const {
     a.prefetch[1] = L.gate.dev;
     a.prefetch[2] = L.up.dev;
     a.prefetch_bytes = prefetch_kb(96) << 10;
+    a.max_ctas = b.qkv_ctas;
     return a;
 }
 
