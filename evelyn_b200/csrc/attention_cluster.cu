@@ -102,21 +102,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
     return (c >> 3) * 2048u + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
 }
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-// D (rows g, g+8; cols 2t, 2t+1) = A (16 x 16 f16, rows 8-15 zero) * B (16 x 8 f16) + C;
-// only rows g (the heads) are kept: c0, c1 accumulate, the rows-g+8 outputs are dropped
-__device__ __forceinline__ void mma_rows(float& c0, float& c1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    asm("{\n .reg .f32 z2, z3;\n"
-        " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,z2,z3}, {%2,%3,%4,%5}, {%6,%7}, {%8,%9,%10,%11};\n}"
-        : "=f"(c0), "=f"(c1)
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f), "f"(0.f));
+// D (16 x 8) += A (16 x 16 f16, row) * B (16 x 8 f16, col), f32 accumulators
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
 }
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
@@ -323,16 +324,20 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
 
     // ---- online softmax over this split's positions, chunk by chunk, entirely out of
     // shared memory. Scalar path: one position per warp at a time, lanes over the head
-    // dimensions. Tensor-core path: one 8-position half page per warp at a time, the G
-    // heads as the rows of mma.sync m16n8k16 (q and the softmax weights split into f16
-    // hi + lo, so the products carry ~22 bits like the f32 reference), the scores of a
-    // head meet in its lane quad.
+    // dimensions. Tensor-core path: one 16-position page per warp at a time on
+    // mma.sync m16n8k16 with the positions as the M dimension and the G <= 8 heads as
+    // N: S^T = K Q^T (A = the K page from ldmatrix, B = q), then O^T += V^T P^T (A = the
+    // V page from ldmatrix.trans, B = the softmax weights, moved into B-fragment order
+    // by shuffles). q and the weights are split into f16 hi + lo, so the products carry
+    // ~22 bits like the f32 reference. Lane (g, t) holds positions g, g+8 (and head
+    // dims 16i + g, +8 of O^T) of heads 2t, 2t+1.
     float qr[G][DPL], m[G], l[G], o[G][DPL];
-    const uint32_t g8 = (uint32_t)lane >> 2, t4 = (uint32_t)lane & 3;  // MMA row (head) and column pair
-    float mrow = -INFINITY, lrow = 0.f, oacc[MM ? HD / 8 : 1][2];
+    const uint32_t g8 = (uint32_t)lane >> 2, t4 = (uint32_t)lane & 3;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f}, oacc[MM ? HD / 16 : 1][4];
+    const bool hv0 = 2 * t4 < (uint32_t)G, hv1 = 2 * t4 + 1 < (uint32_t)G;  // real heads of this lane
     if constexpr (MM) {
-        // the q fragments of every k step, the same for all warps: built once (lane =
-        // (head g, column pair t) of the MMA; heads >= G are zero rows)
+        // the B fragments of q for every k step, the same for all warps: built once
+        // (lane (g, t): head g, dims 16 ks + 2t, +1, +8, +9; heads >= G are zero)
         if (tid < (HD / 16) * 32) {
             const uint32_t ks = tid >> 5, fg = (tid & 31) >> 2, ft = tid & 3;
             uint4 f = make_uint4(0u, 0u, 0u, 0u);
@@ -341,11 +346,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 split_h2(qg[0], qg[1], f.x, f.z);
                 split_h2(qg[8], qg[9], f.y, f.w);
             }
-            qfrag[tid] = f;  // x, y: hi (a0, a2); z, w: lo
+            qfrag[tid] = f;  // x, y: hi (b0, b1); z, w: lo
         }
         __syncthreads();
 #pragma unroll
-        for (int nd = 0; nd < HD / 8; ++nd) oacc[nd][0] = oacc[nd][1] = 0.f;
+        for (int i = 0; i < HD / 16; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
     } else {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -385,50 +390,64 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         if (bad_sh) break;  // uniform after the barrier
         const uint32_t tc0 = t0 + p0 * ps, tc1 = min(t1, t0 + p1 * ps);
         if constexpr (MM) {
-            const uint32_t nunits = 2 * (p1 - p0);
-            for (uint32_t u = warp; u < nunits; u += kAW) {
-                const uint32_t pg = u >> 1, hf = u & 1, tu = tc0 + pg * 16 + hf * 8;
-                if (tu >= tc1) continue;  // uniform over the warp
+            for (uint32_t pg = warp; pg < p1 - p0; pg += kAW) {
+                const uint32_t tu = tc0 + pg * 16;  // first position of the page (live: tu < tc1)
                 const uint32_t kb = smem_addr(ring + (half * H + pg) * 2 * tile), vb = kb + tile * 2;
-                // scores of head g8 at positions tu + 2 t4, + 1: four independent accumulator
-                // pairs (q hi / q lo x even / odd k step) keep the MMA chains short
-                float sa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+                // S^T: four independent accumulators (q hi / lo x even / odd k step)
+                float sa[4][4] = {};
 #pragma unroll 2
                 for (int ks = 0; ks < HD / 16; ++ks) {
-                    uint32_t b0, b1;
-                    ldsm_x2(kb + swz(8 * hf + (lane & 7), 2 * ks + ((lane >> 3) & 1)), b0, b1);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(kb + swz(lane & 15, 2 * ks + (lane >> 4)), a0, a1, a2, a3);
                     const uint4 f = qfrag[ks * 32 + lane];
-                    mma_rows(sa[2 * (ks & 1)][0], sa[2 * (ks & 1)][1], f.x, f.y, b0, b1);
-                    mma_rows(sa[2 * (ks & 1) + 1][0], sa[2 * (ks & 1) + 1][1], f.z, f.w, b0, b1);
+                    mma16816(sa[2 * (ks & 1)], a0, a1, a2, a3, f.x, f.y);
+                    mma16816(sa[2 * (ks & 1) + 1], a0, a1, a2, a3, f.z, f.w);
                 }
-                float s0 = (sa[0][0] + sa[2][0]) + (sa[1][0] + sa[3][0]);
-                float s1 = (sa[0][1] + sa[2][1]) + (sa[1][1] + sa[3][1]);
-                const uint32_t pa = tu + 2 * t4;
-                s0 = pa < tc1 ? s0 * a.scale : -INFINITY;
-                s1 = pa + 1 < tc1 ? s1 * a.scale : -INFINITY;
-                float mx = fmaxf(s0, s1);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float mn = fmaxf(mrow, mx);     // finite: position tu is live
-                const float alpha = expf(mrow - mn);  // exp(-inf) = 0 on the first unit
-                const float e0 = expf(s0 - mn), e1 = expf(s1 - mn);
-                lrow = lrow * alpha + e0 + e1;        // this lane's columns; the quad adds them at the end
-                mrow = mn;
-                uint32_t ph, pl;
-                split_h2(e0, e1, ph, pl);
+                float sc[4];  // positions g8, g8, g8+8, g8+8 x heads 2t, 2t+1, 2t, 2t+1
 #pragma unroll
-                for (int j = 0; j < HD / 32; ++j) {  // four 8-value dimension tiles per ldmatrix
-                    uint32_t vv[4];
-                    ldsm_x4_t(vb + swz(8 * hf + (lane & 7), 4 * j + (lane >> 3)), vv[0], vv[1], vv[2], vv[3]);
+                for (int r = 0; r < 4; ++r) {
+                    const float v = (sa[0][r] + sa[2][r]) + (sa[1][r] + sa[3][r]);
+                    const bool live = (r & 1 ? hv1 : hv0) && tu + g8 + 8 * (r >> 1) < tc1;
+                    sc[r] = live ? v * a.scale : -INFINITY;
+                }
+                float mx[2] = {fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3])};
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float& o0 = oacc[4 * j + q][0];
-                        float& o1 = oacc[4 * j + q][1];
-                        o0 *= alpha;
-                        o1 *= alpha;
-                        mma_rows(o0, o1, ph, 0u, vv[q], 0u);  // k = the unit's 8 positions (rest zero)
-                        mma_rows(o0, o1, pl, 0u, vv[q], 0u);
-                    }
+                for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                    mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o2));
+                    mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o2));
+                }
+                float alpha[2], pw[4];
+#pragma unroll
+                for (int jh = 0; jh < 2; ++jh) {
+                    const bool hv = jh ? hv1 : hv0;
+                    const float mn = fmaxf(mrow[jh], mx[jh]);  // finite for a real head: position tu is live
+                    alpha[jh] = hv ? expf(mrow[jh] - mn) : 1.f;  // exp(-inf) = 0 on the first page
+                    pw[jh] = hv ? expf(sc[jh] - mn) : 0.f;
+                    pw[jh + 2] = hv ? expf(sc[jh + 2] - mn) : 0.f;
+                    lrow[jh] = lrow[jh] * alpha[jh] + pw[jh] + pw[jh + 2];  // this lane's two positions
+                    if (hv) mrow[jh] = mn;
+                }
+                // P^T as the B fragment: lane (g, t) takes positions 2t, 2t+1 (b0) and
+                // 2t+8, 2t+9 (b1) of head g from lanes 8t + g/2 and 8t + 4 + g/2
+                const int s1 = 8 * t4 + (g8 >> 1), s2 = s1 + 4;
+                const bool odd = g8 & 1;
+                const float x0 = __shfl_sync(0xffffffffu, pw[0], s1), x1 = __shfl_sync(0xffffffffu, pw[1], s1);
+                const float x2 = __shfl_sync(0xffffffffu, pw[2], s1), x3 = __shfl_sync(0xffffffffu, pw[3], s1);
+                const float y0 = __shfl_sync(0xffffffffu, pw[0], s2), y1 = __shfl_sync(0xffffffffu, pw[1], s2);
+                const float y2 = __shfl_sync(0xffffffffu, pw[2], s2), y3 = __shfl_sync(0xffffffffu, pw[3], s2);
+                uint32_t bh0, bl0, bh1, bl1;
+                split_h2(odd ? x1 : x0, odd ? y1 : y0, bh0, bl0);  // positions 2t, 2t+1
+                split_h2(odd ? x3 : x2, odd ? y3 : y2, bh1, bl1);  // positions 2t+8, 2t+9
+#pragma unroll
+                for (int i = 0; i < HD / 16; ++i) {  // O^T rows 16i .. 16i+15 (head dims)
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(vb + swz((lane & 7) + 8 * (lane >> 4), 2 * i + ((lane >> 3) & 1)), a0, a1, a2, a3);
+                    oacc[i][0] *= alpha[0];
+                    oacc[i][1] *= alpha[1];
+                    oacc[i][2] *= alpha[0];
+                    oacc[i][3] *= alpha[1];
+                    mma16816(oacc[i], a0, a1, a2, a3, bh0, bh1);
+                    mma16816(oacc[i], a0, a1, a2, a3, bl0, bl1);
                 }
             }
         } else {
@@ -460,18 +479,23 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     if (bad_sh)  // a wait gave up: let the copies issued after it land before leaving
         for (uint32_t c = cw - 1; c < nch && c < cw - 1 + NS; ++c) mbar_wait(&full[c % NS], (c / NS) & 1);
     if constexpr (MM) {
-        lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
-        lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
-        if (g8 < (uint32_t)G) {
-            float* wp = wpart + (warp * G + g8) * (HD + 2);
 #pragma unroll
-            for (int nd = 0; nd < HD / 8; ++nd) {
-                wp[8 * nd + 2 * t4] = oacc[nd][0];
-                wp[8 * nd + 2 * t4 + 1] = oacc[nd][1];
+        for (int o2 = 4; o2 < 32; o2 <<= 1) {  // the lane partial sums of a head over its 8 row lanes
+            lrow[0] += __shfl_xor_sync(0xffffffffu, lrow[0], o2);
+            lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], o2);
+        }
+#pragma unroll
+        for (int jh = 0; jh < 2; ++jh) {
+            if (!(jh ? hv1 : hv0)) continue;
+            float* wp = wpart + (warp * G + 2 * t4 + jh) * (HD + 2);
+#pragma unroll
+            for (int i = 0; i < HD / 16; ++i) {
+                wp[16 * i + g8] = oacc[i][jh];
+                wp[16 * i + g8 + 8] = oacc[i][2 + jh];
             }
-            if (t4 == 0) {
-                wp[HD] = mrow;
-                wp[HD + 1] = lrow;
+            if (g8 == 0) {
+                wp[HD] = mrow[jh];
+                wp[HD + 1] = lrow[jh];
             }
         }
     } else {
