@@ -40,7 +40,7 @@ namespace cg = cooperative_groups;
 constexpr int kAW = 16;  // warps per CTA
 constexpr uint32_t kMaxSplits = 8;  // CTAs per cluster (portable cluster size)
 constexpr uint32_t kMaxRingPages = 16;
-constexpr uint32_t kMaxStages = 4;  // ring stages
+constexpr uint32_t kMaxStages = 4;  // ring stages (2 or 4: a warp group per stage)
 static_assert(kMaxRingPages / 2 <= 32, "warp 0 copies a chunk's pages one per lane");
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
 
@@ -101,6 +101,9 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int32_t
 // byte offset of 16-byte column c (values 8c..8c+7) of row r in a swizzled page tile
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
     return (c >> 3) * 2048u + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
+}
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // the ring starts on a 1024-byte boundary (the swizzle atom of the tensor copies)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[kMaxStages];  // the stages of the page ring
-    __shared__ int bad_sh;
+    __shared__ int bad_sh, grp_bad[kMaxStages];
     cg::cluster_group cl = cg::this_cluster();
     const RopeArgs& r = F.r;
     const AttnArgs& a = F.a;
@@ -193,6 +196,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         for (uint32_t i = 0; i < F.stages; ++i) mbar_init(&full[i], 1);
         fence_barrier_init();
         bad_sh = 0;
+        for (uint32_t i = 0; i < kMaxStages; ++i) grp_bad[i] = 0;
     }
     __syncthreads();
     pdl_launch_dependents();  // the next kernel's weight streaming may start on idle SMs
@@ -364,33 +368,39 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
     const uint32_t pnew = last ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
-    uint32_t cw = 0;  // chunks waited for
-    for (uint32_t c = 0; valid && c < nch; ++c) {
-        const uint32_t half = c % NS, p0 = c * H, p1 = min(npg, p0 + H);
-        cw = c + 1;
+    // Warp group grp (kAW / NS warps) reads the chunks of stage grp (c = grp, grp + NS,
+    // ...), so the stages are read concurrently; a group syncs on its own named barrier
+    // and refills its own stage, so groups never wait on one another.
+    const uint32_t GW = kAW / NS, grp = (uint32_t)warp / GW, gw = (uint32_t)warp % GW;
+    uint32_t cw = grp;  // the next chunk of this group not yet waited for
+    for (uint32_t c = grp; valid && c < nch; c += NS) {
+        const uint32_t half = grp, p0 = c * H, p1 = min(npg, p0 + H);
+        cw = c;
         if (!mbar_wait(&full[half], (c / NS) & 1)) {
             atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
             bad_sh = 1;
+            grp_bad[grp] = 1;
         }
-        // the new position's k and v (registers of warps G, G+1) into the split's copy
-        if (pnew >= p0 && pnew < p1 && (warp == G || warp == G + 1)) {
-            KV* tl = ring + ((half * H + pnew - p0) * 2 + (warp == G ? 0 : 1)) * tile;
+        // the new position's k (group warp 0) and v (group warp 1) into the split's copy
+        if (pnew >= p0 && pnew < p1 && gw < 2) {
+            const float* src = vec + (G + gw) * HD + DPL * lane;
+            KV* tl = ring + ((half * H + pnew - p0) * 2 + gw) * tile;
             const uint32_t rr = (uint32_t)pos % ps;
             if constexpr (MM) {  // swizzled tile: this lane's DPL values are contiguous in one 16-byte column
                 const uint32_t d0 = DPL * lane;
                 __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(tl) + swz(rr, d0 / 8) + (d0 % 8) * 2);
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) dst[e] = __float2half_rn(vec[warp * HD + DPL * lane + e]);
+                for (int e = 0; e < DPL; ++e) dst[e] = __float2half_rn(src[e]);
             } else {
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) tl[rr * HD + DPL * lane + e] = to_kv<KV>(vec[warp * HD + DPL * lane + e]);
+                for (int e = 0; e < DPL; ++e) tl[rr * HD + DPL * lane + e] = to_kv<KV>(src[e]);
             }
         }
-        __syncthreads();
-        if (bad_sh) break;  // uniform after the barrier
+        named_sync(1 + grp, GW * 32);
+        if (grp_bad[grp]) break;  // uniform over the group after its barrier
         const uint32_t tc0 = t0 + p0 * ps, tc1 = min(t1, t0 + p1 * ps);
         if constexpr (MM) {
-            for (uint32_t pg = warp; pg < p1 - p0; pg += kAW) {
+            for (uint32_t pg = gw; pg < p1 - p0; pg += GW) {
                 const uint32_t tu = tc0 + pg * 16;  // first position of the page (live: tu < tc1)
                 const uint32_t kb = smem_addr(ring + (half * H + pg) * 2 * tile), vb = kb + tile * 2;
                 // S^T: four independent accumulators (q hi / lo x even / odd k step)
@@ -451,7 +461,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 }
             }
         } else {
-            for (uint32_t t = tc0 + warp; t < tc1; t += kAW) {
+            for (uint32_t t = tc0 + gw; t < tc1; t += GW) {
                 const uint32_t li = t - tc0;
                 const KV* kp = ring + (half * H + li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
                 float kf[DPL], vf[DPL];
@@ -473,11 +483,14 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 }
             }
         }
-        __syncthreads();  // every warp is done with this stage of the ring
-        if (warp == 0 && c + NS < nch) issue(c + NS);
+        named_sync(1 + grp, GW * 32);  // the group is done with its stage of the ring
+        cw = c + NS;
+        if (gw == 0 && c + NS < nch) issue(c + NS);
     }
-    if (bad_sh)  // a wait gave up: let the copies issued after it land before leaving
-        for (uint32_t c = cw - 1; c < nch && c < cw - 1 + NS; ++c) mbar_wait(&full[c % NS], (c / NS) & 1);
+    // a wait of this group gave up: its stage's copy may still land (later chunks of
+    // the stage were never issued); let it before leaving
+    if (cw < nch && grp_bad[grp]) mbar_wait(&full[grp], (cw / NS) & 1);
+    __syncthreads();
     if constexpr (MM) {
 #pragma unroll
         for (int o2 = 4; o2 < 32; o2 <<= 1) {  // the lane partial sums of a head over its 8 row lanes
@@ -628,7 +641,8 @@ bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* o
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
                                      cudaStream_t s, bool pdl, const KvTmap* tmap) {
     if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1) ||
-        a.nsplit < 1 || a.nsplit > kMaxSplits || stages < 2 || stages > kMaxStages || ring_pages % stages)
+        a.nsplit < 1 || a.nsplit > kMaxSplits || stages < 2 || stages > kMaxStages || kAW % stages ||
+        ring_pages % stages)
         return cudaErrorInvalidValue;
     const uint32_t G = a.kv_heads ? a.heads / a.kv_heads : 0;
     if (!a.kv_heads || a.heads % a.kv_heads ||

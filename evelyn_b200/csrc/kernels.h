@@ -111,7 +111,8 @@ struct alignas(64) KvTmap {
     unsigned long long w[16];
 };
 bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* out);
-// The ring streams in `stages` chunks (2 .. 4, dividing ring_pages). tmap (optional):
+// The ring streams in `stages` chunks (2 or 4, dividing ring_pages), each read by its
+// own warp group. tmap (optional):
 // f16 pages of 16 rows run on the tensor cores (mma.sync), else the scalar loop.
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
                                      cudaStream_t s, bool pdl, const KvTmap* tmap = nullptr);

@@ -347,6 +347,73 @@ __device__ __forceinline__ void stage_quarter(const Plan& p, uint8_t* xs, uint32
     }
 }
 
+// The same for one 8-value eighth he of the input (rows of up to 4096 values take one
+// eighth per consumer thread: twice the threads of quarters, half the chain each). The
+// four eighths of a block sit in lanes 4k..4k+3 and meet by shuffles; eighth e8 = he & 1
+// of quarter he >> 1 holds the B words of lanes t = 2 e8, 2 e8 + 1.
+__device__ __forceinline__ void stage_eighth(const Plan& p, uint8_t* xs, uint32_t he, bool on, const float (&v)[8]) {
+    uint32_t abits = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) abits = max(abits, __float_as_uint(v[e]) & 0x7fffffffu);
+    abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
+    abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 2));
+    const int s = abits ? min(max(148 - (int)(abits >> 23), -100), 120) : 0;  // as stage_quarter
+    const float up = __uint_as_float((uint32_t)(s + 127) << 23);
+    int m[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m[e] = __float_as_int(__fmaf_rn(v[e], up, 12582912.0f)) - 0x4B400000;
+    uint32_t L0[2], L1[2], L2[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) pack_limbs(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3], L0[q], L1[q], L2[q]);
+    const uint32_t hb = he >> 1, e8 = he & 1, j = hb >> 1, h = hb & 1, u = hb >> 2, part = (hb >> 1) & 1;
+    const float fs = __uint_as_float((uint32_t)(127 - s) << 23);
+    if (p.need & NEED_XSUM) {  // sum of the staged (quantised) block: exact in int32
+        int sm = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sm += m[e];
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if (on && (he & 3) == 0) reinterpret_cast<float*>(xs + p.off_xsum)[j] = __fmul_rn((float)sm, fs);
+    }
+    int s0 = 0, s1 = 0, s2 = 0;  // the quarter's limb sums (both eighths) for the Q6_K -32 offset
+    if (p.need & NEED_MSUM) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            s0 = dp4a((int)L0[q], 0x01010101, s0);
+            s1 = dp4a((int)L1[q], 0x01010101, s1);
+            s2 = dp4a((int)L2[q], 0x01010101, s2);
+        }
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+    }
+    if (!on) return;
+    if ((he & 3) == 0) reinterpret_cast<float*>(xs + p.off_fscale)[j] = fs;
+    uint8_t* b = xs + u * kXUnit + part * 96 + h * 4 + e8 * 16;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        *reinterpret_cast<uint32_t*>(b + q * 8) = L0[q];
+        *reinterpret_cast<uint32_t*>(b + 32 + q * 8) = L1[q];
+        *reinterpret_cast<uint32_t*>(b + 64 + q * 8) = L2[q];
+    }
+    if ((p.need & NEED_MSUM) && e8 == 0) {
+        int* ms = reinterpret_cast<int*>(xs + p.off_msum) + u * 8 + part * 4 + h;  // [u][t = 2 part + (limb 2)][h]
+        ms[0] = s0 + 256 * s1;
+        ms[2] = s2;
+    }
+}
+
+__device__ __forceinline__ void load_eighth(const float* x, uint32_t he, bool on, float (&v)[8]) {
+    if (on) {
+        const float4* xp = reinterpret_cast<const float4*>(x + 8 * he);
+        const float4 t0 = __ldcg(xp), t1 = __ldcg(xp + 1);
+        v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    }
+}
+
 __device__ __forceinline__ void load_quarter(const float* x, uint32_t hb, bool on, float (&v)[16]) {
     if (on) {
         const float4* xp = reinterpret_cast<const float4*>(x + 16 * hb);
@@ -391,6 +458,15 @@ __device__ __forceinline__ void load_norm_regs(const Plan& p, int warp, int lane
     const MatvecArgs& a = p.a;
     const uint32_t nq = a.cols / 16, per = kCW * 32, c = (uint32_t)(warp * 32 + lane);
     if (!a.norm_w || nq > 2 * per) return;
+    if (a.cols / 8 <= per) {  // one eighth per thread: g0[0..7]
+        if (c < a.cols / 8) {
+            const float4* gp = reinterpret_cast<const float4*>(a.norm_w + 8 * c);
+            const float4 t0 = gp[0], t1 = gp[1];
+            n.g0[0] = t0.x; n.g0[1] = t0.y; n.g0[2] = t0.z; n.g0[3] = t0.w;
+            n.g0[4] = t1.x; n.g0[5] = t1.y; n.g0[6] = t1.z; n.g0[7] = t1.w;
+        }
+        return;
+    }
     load_weights(a.norm_w, c, c < nq, n.g0);
     if (nq > per) load_weights(a.norm_w, c + per, c + per < nq, n.g1);
 }
@@ -404,7 +480,20 @@ __device__ float stage_input(const Plan& p, uint8_t* xs, int warp, int lane, flo
     const uint32_t K = a.cols, nq = K / 16, per = kCW * 32;
     const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
     float ss = 0.f;
-    if (nq <= 2 * per) {
+    if (K / 8 <= per) {  // one 8-value eighth per thread
+        const bool on = c < K / 8;  // uniform per block of four lanes
+        float v[8];
+        load_eighth(a.x, c, on, v);
+        if (a.norm_w) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+            if (on) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], nr.g0[e]);
+            }
+        }
+        stage_eighth(p, xs, c, on, v);
+    } else if (nq <= 2 * per) {
         // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
         const uint32_t q0 = c, q1 = c + per;
         const bool on0 = q0 < nq, on1 = q1 < nq, two = nq > per;

@@ -130,8 +130,8 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
                 // (2 .. 4) overrides
                 const char* se = std::getenv("EVELYN_ATTN_STAGES");
                 uint32_t st = se ? (uint32_t)std::strtoul(se, nullptr, 10) : 2u;
-                while (st > 2 && (ring % st || ring / st < 2)) --st;
-                b.cluster_stages = std::max<uint32_t>(2, std::min<uint32_t>(st, 4));
+                st = st >= 4 && ring % 4 == 0 && ring >= 8 ? 4u : 2u;
+                b.cluster_stages = st;
                 // EVELYN_QKV_CTAS caps the QKV matvec's grid so the attention's CTAs can
                 // start on the SMs it leaves free (measured slower than the full grid: off)
                 if (const char* qe = std::getenv("EVELYN_QKV_CTAS")) b.qkv_ctas = (uint32_t)std::strtoul(qe, nullptr, 10);
