@@ -47,7 +47,8 @@ constexpr uint32_t kRedBufs = kMaxStages + 1;            // row-block partial bu
 constexpr uint32_t kRedBufBytes = kSbWarps * kRB * 4;
 constexpr uint32_t kRedBytes = kRedBufs * kRedBufBytes + 16 * kRedBufs;  // + arrival counters
 constexpr uint32_t kRowBuf = 256;  // residual rows a CTA keeps in shared memory
-constexpr uint32_t kMaxCtas = 1024;  // grid bound of the row-block partition's 32-bit arithmetic
+constexpr uint32_t kMaxCtas = 1024;     // grid bound of the row-block partition's 32-bit arithmetic
+constexpr uint32_t kMaxEighths = 3;     // staging: up to three 8-value eighths per consumer thread
 static_assert(kSbWarps * 4 == kPanelUnits, "each consumer warp of a slab takes one super-block of a panel");
 
 // need bits
@@ -458,12 +459,14 @@ __device__ __forceinline__ void load_norm_regs(const Plan& p, int warp, int lane
     const MatvecArgs& a = p.a;
     const uint32_t nq = a.cols / 16, per = kCW * 32, c = (uint32_t)(warp * 32 + lane);
     if (!a.norm_w || nq > 2 * per) return;
-    if (a.cols / 8 <= per) {  // one eighth per thread: g0[0..7]
-        if (c < a.cols / 8) {
-            const float4* gp = reinterpret_cast<const float4*>(a.norm_w + 8 * c);
+    if (a.cols / 8 <= kMaxEighths * per) {  // eighths c, c + per, c + 2 per: g0[0..7], g0[8..15], g1[0..7]
+#pragma unroll
+        for (uint32_t k = 0; k < kMaxEighths; ++k) {
+            if (c + k * per >= a.cols / 8) continue;
+            const float4* gp = reinterpret_cast<const float4*>(a.norm_w + 8 * (c + k * per));
             const float4 t0 = gp[0], t1 = gp[1];
-            n.g0[0] = t0.x; n.g0[1] = t0.y; n.g0[2] = t0.z; n.g0[3] = t0.w;
-            n.g0[4] = t1.x; n.g0[5] = t1.y; n.g0[6] = t1.z; n.g0[7] = t1.w;
+            float* g = k == 2 ? n.g1 : n.g0 + 8 * k;
+            g[0] = t0.x; g[1] = t0.y; g[2] = t0.z; g[3] = t0.w; g[4] = t1.x; g[5] = t1.y; g[6] = t1.z; g[7] = t1.w;
         }
         return;
     }
@@ -480,19 +483,26 @@ __device__ float stage_input(const Plan& p, uint8_t* xs, int warp, int lane, flo
     const uint32_t K = a.cols, nq = K / 16, per = kCW * 32;
     const uint32_t c = (uint32_t)(warp * 32 + lane);  // consumer thread 0 .. kCW*32-1
     float ss = 0.f;
-    if (K / 8 <= per) {  // one 8-value eighth per thread
-        const bool on = c < K / 8;  // uniform per block of four lanes
-        float v[8];
-        load_eighth(a.x, c, on, v);
-        if (a.norm_w) {
+    if (K / 8 <= kMaxEighths * per) {  // 8-value eighths c, c + per, c + 2 per (independent chains)
+        float v[kMaxEighths][8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
-            if (on) {
+        for (uint32_t k = 0; k < kMaxEighths; ++k)
+            if (k * per < K / 8) load_eighth(a.x, c + k * per, c + k * per < K / 8, v[k]);  // uniform test first
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], nr.g0[e]);
+        for (uint32_t k = 0; k < kMaxEighths; ++k) {
+            if (k * per >= K / 8) continue;
+            const bool on = c + k * per < K / 8;  // uniform per block of four lanes
+            if (a.norm_w) {
+                const float* g = k == 2 ? nr.g1 : nr.g0 + 8 * k;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+                if (on) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[k][e] = __fmul_rn(v[k][e], g[e]);
+                }
             }
+            stage_eighth(p, xs, c + k * per, on, v[k]);
         }
-        stage_eighth(p, xs, c, on, v);
     } else if (nq <= 2 * per) {
         // nq is a multiple of 4, so a warp's 32 lanes cover whole blocks or none
         const uint32_t q0 = c, q1 = c + per;
@@ -622,14 +632,19 @@ struct RingPos {
 // Producer (one thread): stream row blocks [rb0, rb1) of `p`, one 32-unit panel of the
 // row block's slabs per stage, continuing the ring sequence at `rp`. Returns false
 // after an abort.
+// Items are numbered n = (rb - rb0) * ngroups + g; a call issues items [rp.n, stop).
 __device__ bool produce_items(const Plan& p, const Ring& r, uint32_t rb0, uint32_t rb1, RingPos& rp,
-                              volatile int* abort_flag) {
-    for (uint32_t rb = rb0; rb < rb1; ++rb) {
-        for (uint32_t g = 0; g < p.ngroups; ++g, rp.advance(r.stages)) {
-            // a slot's lap L >= 1 waits for the consumers' release of lap L - 1
-            if (rp.n >= r.stages && !wait_or_abort(&r.empty[rp.s], rp.par ^ 1, abort_flag)) return false;
-            if (*abort_flag) return false;
-            issue_item(p, r, rb, g, rp.s);
+                              volatile int* abort_flag, uint32_t stop = 0xffffffffu) {
+    const uint32_t end = min((rb1 - rb0) * p.ngroups, stop);
+    uint32_t rb = rb0 + rp.n / p.ngroups, g = rp.n % p.ngroups;
+    for (; rp.n < end; rp.advance(r.stages)) {
+        // a slot's lap L >= 1 waits for the consumers' release of lap L - 1
+        if (rp.n >= r.stages && !wait_or_abort(&r.empty[rp.s], rp.par ^ 1, abort_flag)) return false;
+        if (*abort_flag) return false;
+        issue_item(p, r, rb, g, rp.s);
+        if (++g == p.ngroups) {
+            g = 0;
+            ++rb;
         }
     }
     return true;
