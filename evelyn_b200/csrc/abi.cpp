@@ -8,6 +8,10 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
+
 #include <algorithm>
 #include <cerrno>
 #include <cfloat>
@@ -76,21 +80,21 @@ evl_status evl_validate_token_ids(const uint32_t* ids, size_t n, size_t vocab) {
     });
 }
 
-uint32_t evl_argmax(const float* v, size_t n) {
-    // The first index of the maximum under a strict '>' scan from -FLT_MAX (NaN never
-    // wins; nothing above -FLT_MAX gives 0). Blocks of 256 values reduce to their maximum
-    // in 16 interleaved lanes (vectorisable); the strict '>' across blocks keeps the first
-    // block that holds the maximum, which is then searched for its first occurrence.
-    constexpr size_t B = 256, L = 16;
+}  // extern "C"
+
+namespace {
+// The first index of the maximum under a strict '>' scan from -FLT_MAX (NaN never
+// wins; nothing above -FLT_MAX gives 0). Blocks of 256 values reduce to their maximum;
+// the strict '>' across blocks keeps the first block that holds the maximum, which is
+// then searched for its first occurrence. `blockmax` is the block's maximum under the
+// same '>' (a NaN never replaces a number).
+template <class BlockMax>
+uint32_t argmax_blocks(const float* v, size_t n, BlockMax blockmax) {
+    constexpr size_t B = 256;
     float mx = -FLT_MAX;
     size_t best = SIZE_MAX, i = 0;
     for (; i + B <= n; i += B) {
-        float lm[L];
-        for (size_t j = 0; j < L; ++j) lm[j] = -FLT_MAX;
-        for (size_t k = 0; k < B; k += L)
-            for (size_t j = 0; j < L; ++j) lm[j] = v[i + k + j] > lm[j] ? v[i + k + j] : lm[j];
-        float bm = -FLT_MAX;
-        for (size_t j = 0; j < L; ++j) bm = lm[j] > bm ? lm[j] : bm;
+        const float bm = blockmax(v + i);
         if (bm > mx) {
             mx = bm;
             best = i;
@@ -106,6 +110,51 @@ uint32_t evl_argmax(const float* v, size_t n) {
     for (size_t k = best; k < best + B; ++k)
         if (v[k] == mx) return (uint32_t)k;
     return (uint32_t)best;
+}
+
+uint32_t argmax_base(const float* v, size_t n) {
+    return argmax_blocks(v, n, [](const float* b) {
+        float lm[16];
+        for (int j = 0; j < 16; ++j) lm[j] = -FLT_MAX;
+        for (int k = 0; k < 256; k += 16)
+            for (int j = 0; j < 16; ++j) lm[j] = b[k + j] > lm[j] ? b[k + j] : lm[j];
+        float m = -FLT_MAX;
+        for (int j = 0; j < 16; ++j) m = lm[j] > m ? lm[j] : m;
+        return m;
+    });
+}
+
+#if defined(__x86_64__)
+// vmaxps(a, b) is (a > b) ? a : b per lane, the scan's own comparison
+__attribute__((target("avx2"))) float blockmax_avx2(const float* b) {
+    __m256 a0 = _mm256_set1_ps(-FLT_MAX), a1 = a0, a2 = a0, a3 = a0;
+    for (int k = 0; k < 256; k += 32) {
+        a0 = _mm256_max_ps(_mm256_loadu_ps(b + k), a0);
+        a1 = _mm256_max_ps(_mm256_loadu_ps(b + k + 8), a1);
+        a2 = _mm256_max_ps(_mm256_loadu_ps(b + k + 16), a2);
+        a3 = _mm256_max_ps(_mm256_loadu_ps(b + k + 24), a3);
+    }
+    a0 = _mm256_max_ps(_mm256_max_ps(a0, a1), _mm256_max_ps(a2, a3));
+    alignas(32) float t[8];
+    _mm256_store_ps(t, a0);
+    float m = -FLT_MAX;
+    for (int j = 0; j < 8; ++j) m = t[j] > m ? t[j] : m;
+    return m;
+}
+__attribute__((target("avx2"))) uint32_t argmax_avx2(const float* v, size_t n) {
+    return argmax_blocks(v, n, blockmax_avx2);
+}
+#endif
+}  // namespace
+
+extern "C" {
+
+uint32_t evl_argmax(const float* v, size_t n) {
+#if defined(__x86_64__)
+    static const bool avx2 = __builtin_cpu_supports("avx2");
+    if (avx2) return argmax_avx2(v, n);
+#endif
+    return argmax_base(v, n);
 }
 
 float evl_log_prob(const float* logits, size_t n, uint32_t target) {
