@@ -223,7 +223,7 @@ struct StepBuffers {
     uint32_t max_ctx = 0, pages_per_seq = 0;
     DeviceBuffer kv, page_table, pos, tokens, argmax, hist, err;
     DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
-    DeviceBuffer gbx, gxinv, gpart, gpart2;  // batched products: staged x, 2^-e, partial sums
+    DeviceBuffer gbx, gxinv, gpart, gpart2, gpart3;  // batched products: staged x, 2^-e, partial sums
     uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
     KvTmap kv_tmap{};             // the KV pool for the attention's tensor-core path
     uint32_t cluster_stages = 2;  // ring stages of the cluster attention
@@ -256,6 +256,8 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     void enqueue_batched(bool pdl);
     void gemm_stage(const float* x, uint32_t cols, uint32_t stride, const float* norm_w, bool pdl);
     void gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool pdl);
+    GemmReduce reduce_args(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride, int epi,
+                           const float* part2, uint32_t ksplit2) const;
     void gemm_reduce(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride, int epi,
                      const float* part2, uint32_t ksplit2, bool pdl);
     // Enqueue one dense step (every kernel) on `stream`.

@@ -160,6 +160,8 @@ struct GemmX {
 };
 uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols);
 cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl);
+// rows up to this many values are staged in one launch (else two)
+uint32_t gemm_stage_one_launch_cols();
 
 // part[kr][seq][rows_pad] = sum over K range kr of W x (ksplit ranges per M tile)
 struct GemmArgs {
@@ -184,6 +186,8 @@ struct GemmReduce {
     int epi = EPI_STORE;
 };
 cudaError_t launch_gemm_reduce(const GemmReduce& a, cudaStream_t s, bool pdl);
+// up to three independent reductions in one launch (e.g. the Q, K and V products)
+cudaError_t launch_gemm_reduce_n(const GemmReduce* a, uint32_t n, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------- misc.cu
 cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t batch, float* x, int32_t* err,

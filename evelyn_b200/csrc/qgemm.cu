@@ -247,8 +247,9 @@ __global__ void __launch_bounds__(kStatsThreads) gemm_stage_stats_kernel(const G
         for (uint32_t i = 0; i < kStatsPer; ++i) g[i] = tid + i * nt < K ? a.norm_w[tid + i * nt] : 0.f;
     }
     pdl_wait();
-    if (s >= a.nseq) return;  // the whole CTA
-    const float* x = a.x + (uint64_t)s * a.x_stride;
+    const bool live = s < a.nseq;
+    if (!live && !inreg) return;  // the whole CTA (padding rows are staged by gemm_stage_x_kernel)
+    const float* x = a.x + (uint64_t)(live ? s : 0) * a.x_stride;
     auto block_sum = [&](float t) {
         t = warp_sum(t);
         __syncthreads();
@@ -270,7 +271,7 @@ __global__ void __launch_bounds__(kStatsThreads) gemm_stage_stats_kernel(const G
     float inv = 1.f, mx = 0.f;
     if (inreg) {
 #pragma unroll
-        for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = tid + i * nt < K ? x[tid + i * nt] : 0.f;
+        for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = live && tid + i * nt < K ? x[tid + i * nt] : 0.f;
         if (a.norm_w) {
             float ss = 0.f;
 #pragma unroll
@@ -292,14 +293,39 @@ __global__ void __launch_bounds__(kStatsThreads) gemm_stage_stats_kernel(const G
         for (uint32_t i = tid; i < K; i += nt) mx = fmaxf(mx, fabsf(staged_val(a, x, i, inv)));
     }
     const float t = block_max(mx);
-    if (tid == 0) {
-        int e = 0;
-        if (t > 0.f) frexpf(t, &e);  // t in [2^(e-1), 2^e)
-        const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
+    int e = 0;
+    if (t > 0.f) frexpf(t, &e);  // t in [2^(e-1), 2^e)
+    const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
+    if (tid == 0 && live) {
         a.stats[2 * s] = inv;
         a.stats[2 * s + 1] = ldexpf(1.0f, sc);
         a.xinv[s] = ldexpf(1.0f, -sc);
     }
+    if (!inreg) return;
+    // rows held in registers are staged here as well (gemm_stage_x_kernel's layout:
+    // value k of chunk c as f16 hi/lo B rows s and nsp + s, the Q4_K min-term sums);
+    // padding sequences s >= nseq stage zeros
+    const float up = ldexpf(1.0f, sc);
+    const uint32_t nsp = a.nsp, N = 2 * nsp;
+#pragma unroll
+    for (uint32_t i = 0; i < kStatsPer; ++i) {
+        const uint32_t k = tid + i * nt;
+        if (i * nt >= K) break;  // uniform
+        const float val = k < K ? __fmul_rn(v[i], up) : 0.f;
+        const __half hi = __float2half_rn(val);
+        const __half lo = __float2half_rn(val - __half2float(hi));
+        uint8_t* chunk = a.bx + (uint64_t)(k / kChunk) * gemm_xchunk_bytes(nsp);
+        const uint32_t kc = k % kChunk;
+        uint8_t* tile = chunk + (kc / 16) * (N * 32u);
+        const uint32_t sl = kslot(kc % 16);
+        if (k < K) {
+            *reinterpret_cast<__half*>(tile + bt_off(s, sl)) = hi;
+            *reinterpret_cast<__half*>(tile + bt_off(nsp + s, sl)) = lo;
+        }
+        const float sm = warp_sum(val);  // the warp's 32 values are one sub-block
+        if (k < K && (k & 31) == 0) reinterpret_cast<float*>(chunk + 16 * (N * 32u))[(kc / 32) * nsp + s] = sm;
+    }
+    pdl_launch_dependents();
 }
 
 // grid (nsp, K / 256), 256 threads: thread k stages value k of the chunk
@@ -675,6 +701,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ reduce + epilogue
+struct GemmReduceN {
+    GemmReduce r[3];
+    uint64_t end[3];  // cumulative element counts
+    uint32_t n;
+};
+
+__device__ __forceinline__ void reduce_one(const GemmReduce& a, uint64_t i) {
+    const uint32_t s = (uint32_t)(i / a.rows), r = (uint32_t)(i % a.rows);
+    float sum = 0.f, sum2 = 0.f;
+    for (uint32_t k = 0; k < a.ksplit; ++k) sum += a.part[((uint64_t)k * a.nseq + s) * a.rows_pad + r];
+    if (a.part2)
+        for (uint32_t k = 0; k < a.ksplit2; ++k) sum2 += a.part2[((uint64_t)k * a.nseq + s) * a.rows_pad2 + r];
+    float* y = a.y + (uint64_t)s * a.y_stride + r;
+    if (a.epi == EPI_SWIGLU) *y = __fmul_rn(__fdiv_rn(sum, __fadd_rn(1.0f, expf(-sum))), sum2);
+    else if (a.epi == EPI_ADD) *y += sum;
+    else *y = sum;
+}
+
+__global__ void gemm_reduce_n_kernel(const GemmReduceN a) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();
+    if (i < a.end[0]) reduce_one(a.r[0], i);
+    else if (a.n > 1 && i < a.end[1]) reduce_one(a.r[1], i - a.end[0]);
+    else if (a.n > 2 && i < a.end[2]) reduce_one(a.r[2], i - a.end[1]);
+    pdl_launch_dependents();
+}
+
 __global__ void gemm_reduce_kernel(const GemmReduce a) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)a.nseq * a.rows) return;
@@ -739,13 +792,18 @@ uint64_t gemm_x_bytes(uint32_t nseq, uint32_t cols) {
     return (uint64_t)(cols / kChunk) * gemm_xchunk_bytes(nsp);
 }
 
+uint32_t gemm_stage_one_launch_cols() { return kStatsThreads * kStatsPer; }
+
 cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl) {
     if (!a.nseq || a.nseq > 32 || a.cols % kChunk || !a.x || !a.bx || !a.xinv || !a.stats) return cudaErrorInvalidValue;
     a.nsp = (a.nseq + 15) / 16 * 16;  // the MMA's N (M = 128 needs a multiple of 16)
     cudaLaunchAttribute at[1];
-    auto cfg = cfg_of(dim3(a.nseq), dim3(kStatsThreads), 0, s, pdl, at);
+    // rows of up to kStatsThreads * kStatsPer values: one launch, a CTA per sequence
+    // (padding ones included) computes the statistics and stages its row
+    const bool one = a.cols <= kStatsThreads * kStatsPer;
+    auto cfg = cfg_of(dim3(one ? a.nsp : a.nseq), dim3(kStatsThreads), 0, s, pdl, at);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_stage_stats_kernel, a);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || one) return e;
     auto cfg2 = cfg_of(dim3(a.nsp, a.cols / kChunk), dim3(kChunk), 0, s, pdl, at);
     return cudaLaunchKernelEx(&cfg2, gemm_stage_x_kernel, a);
 }
@@ -797,6 +855,22 @@ cudaError_t launch_gemm_reduce(const GemmReduce& a, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute at[1];
     auto cfg = cfg_of(dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, pdl, at);
     return cudaLaunchKernelEx(&cfg, gemm_reduce_kernel, a);
+}
+
+cudaError_t launch_gemm_reduce_n(const GemmReduce* a, uint32_t n, cudaStream_t s, bool pdl) {
+    if (!a || n < 1 || n > 3) return cudaErrorInvalidValue;
+    GemmReduceN r{};
+    r.n = n;
+    uint64_t tot = 0;
+    for (uint32_t k = 0; k < n; ++k) {
+        if (!a[k].part || !a[k].y || !a[k].nseq || !a[k].rows || !a[k].ksplit) return cudaErrorInvalidValue;
+        r.r[k] = a[k];
+        tot += (uint64_t)a[k].nseq * a[k].rows;
+        r.end[k] = tot;
+    }
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, gemm_reduce_n_kernel, r);
 }
 
 }  // namespace evl

@@ -167,6 +167,7 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             pmax = std::max<uint64_t>(pmax, (uint64_t)gemm_ksplit(q->gemm, sms) * batch * q->gemm.mtiles * 128 * 4);
         b.gpart.alloc(pmax);
         b.gpart2.alloc(pmax);
+        b.gpart3.alloc(pmax);
     }
 }
 
@@ -182,7 +183,7 @@ void Decoder::gemm_stage(const float* x, uint32_t cols, uint32_t stride, const f
     g.xinv = b.gxinv.as<float>();
     g.stats = b.gxinv.as<float>() + 32;
     cuda_check(launch_gemm_stage_x(g, stream, pdl), "stage x");
-    kernels += 2;
+    kernels += cols <= gemm_stage_one_launch_cols() ? 1 : 2;
 }
 
 void Decoder::gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool pdl) {
@@ -199,6 +200,23 @@ void Decoder::gemm_product(const QMatrix& w, float* part, uint32_t& ksplit, bool
     a.err = b.err.as<int>();
     cuda_check(launch_qgemm(a, stream, pdl), "gemm");
     kernels += 1;
+}
+
+GemmReduce Decoder::reduce_args(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride,
+                                int epi, const float* part2, uint32_t ksplit2) const {
+    GemmReduce r;
+    r.part = part;
+    r.ksplit = ksplit;
+    r.rows_pad = w.gemm.mtiles * 128;
+    r.part2 = part2;
+    r.ksplit2 = ksplit2;
+    r.rows_pad2 = r.rows_pad;
+    r.nseq = b.batch;
+    r.rows = w.rows;
+    r.y = y;
+    r.y_stride = y_stride;
+    r.epi = epi;
+    return r;
 }
 
 void Decoder::gemm_reduce(const QMatrix& w, const float* part, uint32_t ksplit, float* y, uint32_t y_stride, int epi,
@@ -234,12 +252,18 @@ void Decoder::enqueue_batched(bool pdl) {
     for (uint32_t li = 0; li < c.layers; ++li) {
         const LayerWeights& L = m.layers[li];
         gemm_stage(x, dim, dim, L.attn_norm, pdl);
-        gemm_product(L.q, p1, k1, pdl);
-        gemm_reduce(L.q, p1, k1, b.q.as<float>(), qw, EPI_STORE, nullptr, 0, pdl);
-        gemm_product(L.k, p1, k1, pdl);
-        gemm_reduce(L.k, p1, k1, b.k.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
-        gemm_product(L.v, p1, k1, pdl);
-        gemm_reduce(L.v, p1, k1, b.v.as<float>(), kw, EPI_STORE, nullptr, 0, pdl);
+        {  // Q, K, V products into three partial buffers, then one reduction launch
+            uint32_t kq = 1, kk = 1, kv = 1;
+            float* p3 = b.gpart3.as<float>();
+            gemm_product(L.q, p1, kq, pdl);
+            gemm_product(L.k, p2, kk, pdl);
+            gemm_product(L.v, p3, kv, pdl);
+            const GemmReduce r[3] = {reduce_args(L.q, p1, kq, b.q.as<float>(), qw, EPI_STORE, nullptr, 0),
+                                     reduce_args(L.k, p2, kk, b.k.as<float>(), kw, EPI_STORE, nullptr, 0),
+                                     reduce_args(L.v, p3, kv, b.v.as<float>(), kw, EPI_STORE, nullptr, 0)};
+            cuda_check(launch_gemm_reduce_n(r, 3, stream, pdl), "gemm reduce");
+            kernels += 1;
+        }
         if (b.cluster_ring) {
             cuda_check(launch_attention_cluster(rope_args(li), attn_args(li, b.cluster_splits), b.cluster_ring, b.cluster_stages, stream,
                                                 pdl, b.kv_tmap_ok ? &b.kv_tmap : nullptr),
