@@ -39,7 +39,7 @@ namespace cg = cooperative_groups;
 
 constexpr int kAW = 16;  // warps per CTA
 constexpr uint32_t kMaxSplits = 8;  // CTAs per cluster (portable cluster size)
-constexpr uint32_t kMaxRingPages = 16;
+constexpr uint32_t kMaxRingPages = 24;
 constexpr uint32_t kMaxStages = 4;  // ring stages (2 or 4: a warp group per stage)
 static_assert(kMaxRingPages / 2 <= 32, "warp 0 copies a chunk's pages one per lane");
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
@@ -158,12 +158,18 @@ __device__ __forceinline__ void merge_weights(const float* part, uint32_t stride
     }
 }
 
+// The warp partials (written after every warp is done with the ring) reuse the ring's
+// bytes when it is large enough, so a larger ring fits.
+__host__ __device__ __forceinline__ bool wpart_in_ring(uint32_t ring_pages, uint32_t ps, uint32_t hd, uint32_t eb,
+                                                       uint32_t G) {
+    return (size_t)ring_pages * 2 * ps * hd * eb >= 4ull * kAW * G * (hd + 2);
+}
 // Shared-memory bytes of one CTA (ring, q, per-warp vectors, warp partials, CTA partial).
 __host__ __device__ __forceinline__ size_t cluster_smem(uint32_t ring_pages, uint32_t ps, uint32_t hd, uint32_t eb,
                                                        uint32_t G) {
     return 1024 + (size_t)ring_pages * 2 * ps * hd * eb + 4ull * G * hd + 4ull * (G + 2) * hd +
-           4ull * kAW * G * (hd + 2) + 4ull * kMaxSplits * G * (hd + 2) +
-           2ull * 32 * hd;  // + q fragments (hd/16 x 32 x 16 B)
+           (wpart_in_ring(ring_pages, ps, hd, eb, G) ? 0 : 4ull * kAW * G * (hd + 2)) +
+           4ull * kMaxSplits * G * (hd + 2) + 2ull * 32 * hd;  // + q fragments (hd/16 x 32 x 16 B)
 }
 
 template <typename KV, int G, int HD, bool MM>
@@ -187,8 +193,9 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     KV* ring = reinterpret_cast<KV*>(smem);                                   // [ring][K|V][ps][HD]
     float* qs = reinterpret_cast<float*>(smem + (size_t)F.ring_pages * 2 * tile * sizeof(KV));  // [G][HD]
     float* vec = qs + G * HD;                                                 // [G+2][HD] per-warp vectors
-    float* wpart = vec + (G + 2) * HD;                                        // [warps][G][HD+2]
-    float* cpart = wpart + kAW * G * (HD + 2);  // rank 0: [split][G][HD+2] (o, m, l) of every CTA
+    const bool wr = wpart_in_ring(F.ring_pages, ps, HD, sizeof(KV), G);
+    float* wpart = wr ? reinterpret_cast<float*>(smem) : vec + (G + 2) * HD;  // [warps][G][HD+2]
+    float* cpart = vec + (G + 2) * HD + (wr ? 0 : kAW * G * (HD + 2));  // rank 0: [split][G][HD+2] (o, m, l)
     uint4* qfrag = reinterpret_cast<uint4*>(cpart + kMaxSplits * G * (HD + 2));  // [HD/16][lanes]: q hi/lo fragments
     __shared__ float fac[kAW * G], mrg_m[G], mrg_l[G];  // merge weights, maxima and sums
 

@@ -118,7 +118,8 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
             // EVELYN_ATTN_RING caps the ring (even, >= 2), so tests reach the streamed
             // multi-chunk case at small contexts
             const char* re = std::getenv("EVELYN_ATTN_RING");
-            const uint32_t cap = re ? (uint32_t)std::strtoul(re, nullptr, 10) & ~1u : 16;
+            // (a batch's long splits take the largest ring: the copies in flight bound them)
+            const uint32_t cap = re ? (uint32_t)std::strtoul(re, nullptr, 10) & ~1u : (batch > 1 ? 24u : 16u);
             const uint32_t ring = attention_cluster_pages(b.pages_per_seq, C, kPageSize, (uint32_t)hd, (uint32_t)elem,
                                                           m->lheads / std::max<uint32_t>(1, m->lkv_heads),
                                                           std::max<uint32_t>(cap, 2));
