@@ -41,7 +41,7 @@ constexpr int kAW = 16;  // warps per CTA
 constexpr uint32_t kMaxSplits = 8;  // CTAs per cluster (portable cluster size)
 constexpr uint32_t kMaxRingPages = 24;
 constexpr uint32_t kMaxStages = 4;  // ring stages (2 or 4: a warp group per stage)
-static_assert(kMaxRingPages / 2 <= 32, "warp 0 copies a chunk's pages one per lane");
+static_assert(kMaxRingPages <= 32, "one warp copies up to a ring of pages, one per lane");
 constexpr uint32_t kSmemCap = 225 * 1024;  // dynamic shared memory (static use stays under 2 KB)
 
 struct ClusterAttn {
@@ -176,6 +176,7 @@ template <typename KV, int G, int HD, bool MM>
 __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_constant__ ClusterAttn F) {
     constexpr int DPL = HD / 32;
     static_assert(G <= kAW && kAW <= 32 && kMaxSplits <= 32, "one warp per head merges up to 32 partials");
+    static_assert(G + 2 < kAW, "the last warp is free to issue the first page copies");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the ring starts on a 1024-byte boundary (the swizzle atom of the tensor copies)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -222,16 +223,20 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // chunk c (NS = 2 for one sequence's few pages per split; a batch's long splits keep
     // NS - 1 chunks in flight behind the one being read).
     const uint32_t NS = F.stages, H = F.ring_pages / NS, nch = (npg + H - 1) / H;
-    // Warp 0 issues a chunk: lane 0 sets the byte count, lane i reads the page id of
-    // page p0 + i and copies it (the page ids arrive in one round trip, not one each).
-    auto issue = [&](uint32_t c) {
-        const uint32_t p0 = c * H, p1 = min(npg, p0 + H), half = c % NS;
-        if (lane == 0) mbar_arrive_expect_tx(&full[half], (p1 - p0) * 2 * tile * (uint32_t)sizeof(KV));
+    // One warp issues chunks [c0, c1) (at most the ring's pages, <= 32): lane 0 sets
+    // each chunk's byte count, lane i reads the page id of the range's page i and
+    // copies it (the page ids arrive in one round trip, not one each).
+    auto issue = [&](uint32_t c0, uint32_t c1) {
+        const uint32_t p0 = c0 * H, p1 = min(npg, c1 * H);
+        if (lane == 0)
+            for (uint32_t c = c0; c < c1; ++c)
+                mbar_arrive_expect_tx(&full[c % NS], (min(npg, (c + 1) * H) - c * H) * 2 * tile * (uint32_t)sizeof(KV));
         __syncwarp();
         const uint32_t i = p0 + (uint32_t)lane;
         if (i < p1) {
+            const uint32_t half = (i / H) % NS;
             const int32_t page = __ldcg(ptab + t0 / ps + i);
-            KV* slot = ring + (half * H + (i - p0)) * 2 * tile;
+            KV* slot = ring + (half * H + i % H) * 2 * tile;
             if constexpr (MM) {  // row coordinates of the K and V tiles in the pool's [rows][HD] view
                 const uint8_t* pool = (const uint8_t*)a.kv.pool;
                 const int32_t yk = (int32_t)((kv_tile(a.kv, page, r.layer, 0, kvh) - pool) / (HD * 2));
@@ -247,11 +252,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             }
         }
     };
-    if (warp == 0) {
+    if (warp == kAW - 1) {  // a warp with no q, k or v vector to prepare
         if (!valid) {
             if (lane == 0) atomicExch(a.err, DEV_ERR_POSITION);
-        } else {
-            for (uint32_t c = 0; c < NS && c < nch; ++c) issue(c);
+        } else if (nch > 0) {
+            issue(0, min(NS, nch));  // the first NS chunks in one round trip
         }
     }
     // warp w < G: q head kvh*G + w; w == G: k; w == G+1: v. Lane dims d = DPL*lane + e.
@@ -492,7 +497,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
         named_sync(1 + grp, GW * 32);  // the group is done with its stage of the ring
         cw = c + NS;
-        if (gw == 0 && c + NS < nch) issue(c + NS);
+        if (gw == 0 && c + NS < nch) issue(c + NS, c + NS + 1);
     }
     // a wait of this group gave up: its stage's copy may still land (later chunks of
     // the stage were never issued); let it before leaving
