@@ -552,17 +552,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     const uint32_t dm = *reinterpret_cast<const uint32_t*>(wb + t * 4);
                     d = f16_exact(dm & 0xffff);
                     dmin = f16_exact(dm >> 16);
-                    const uint8_t* sc = wb + 512 + t * 12;
-                    for (int j = 0; j < 8; ++j) scale_min_bytes(j, sc, &q4_s[j], &q4_m[j]);
+                    // the 12 scale bytes as three words (gguf.rs's get_scale_min_k4 on four
+                    // sub-blocks at once): s_0..3, s_4..7, m_0..3, m_4..7 one per byte
+                    const uint32_t* sw = reinterpret_cast<const uint32_t*>(wb + 512 + t * 12);
+                    const uint32_t w0 = sw[0], w1 = sw[1], w2 = sw[2];
+                    const uint32_t sb[2] = {w0 & 0x3F3F3F3Fu, (w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u)};
+                    const uint32_t mb[2] = {w1 & 0x3F3F3F3Fu, ((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        q4_s[j] = (float)((sb[j >> 2] >> (8 * (j & 3))) & 0xffu);
+                        q4_m[j] = (float)((mb[j >> 2] >> (8 * (j & 3))) & 0xffu);
+                    }
                     // -dmin * sum_j m_j * sum(x of sub-block j), this group's sequences
+                    // (4 or 8 consecutive floats per sub-block: 16-byte loads; same FMA order)
                     const float* xs = reinterpret_cast<const float*>(wb + wbytes + 16u * (P.N * 32u)) + grp * half;
+                    float mt[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 a0 = *reinterpret_cast<const float4*>(xs + j * P.nsp);
+                        mt[0] = fmaf(q4_m[j], a0.x, mt[0]);
+                        mt[1] = fmaf(q4_m[j], a0.y, mt[1]);
+                        mt[2] = fmaf(q4_m[j], a0.z, mt[2]);
+                        mt[3] = fmaf(q4_m[j], a0.w, mt[3]);
+                        if (half == 8) {
+                            const float4 a1 = *reinterpret_cast<const float4*>(xs + j * P.nsp + 4);
+                            mt[4] = fmaf(q4_m[j], a1.x, mt[4]);
+                            mt[5] = fmaf(q4_m[j], a1.y, mt[5]);
+                            mt[6] = fmaf(q4_m[j], a1.z, mt[6]);
+                            mt[7] = fmaf(q4_m[j], a1.w, mt[7]);
+                        }
+                    }
 #pragma unroll
                     for (uint32_t i = 0; i < 8; ++i) {
                         if (i >= half) break;
-                        float mt = 0.f;
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) mt = fmaf(q4_m[j], xs[j * P.nsp + i], mt);
-                        acc[i] = fmaf(-dmin, mt, acc[i]);
+                        acc[i] = fmaf(-dmin, mt[i], acc[i]);
                     }
                 } else if (T == GGML_Q6_K) {
                     const uint4 sc4 = *reinterpret_cast<const uint4*>(wb + 24576 + t * 16);
