@@ -12,7 +12,7 @@ tensor-parallel over N GPUs (Megatron split, NCCL all-reduce after o-proj and do
 Printed JSON (rank 0): value = tok/s timed on the device with CUDA events on the
 session stream, weights and KV resident in HBM, inputs larger than L2 (5 GB of
 weights per step); e2e = the same through evl_session_step with host buffers
-(token H2D, logits + argmax D2H every step); roofline = the dominant kernel
+(token H2D, logits D2H and the host argmax every step, same context range); roofline = the dominant kernel
 (Q4_K dequant-matvec of the ffn_gate shape 12288x4096) timed live; cpu_baseline =
 the CPU oracle (a restatement of the reference's runtime) on a bounded sample.
 """
@@ -264,8 +264,18 @@ def run_ours(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     ms_max = dist_max(ms, world)
-    # end to end through evl_session_step: token H2D, logits + argmax D2H, every step
-    tok = toks[-1]
+    launches = sess.kernels_per_step * K
+    # end to end through evl_session_step: token H2D, logits D2H and the host argmax
+    # every step, on a fresh session over the same context range as the timed loop
+    del sess
+    sess = evl.Session(model, max_ctx=max_ctx)
+    for t in prompt[:-1]:
+        sess.step(int(t), logits=False)
+    tok = last
+    for _ in range(W):
+        tok = evl.argmax(sess.step(tok))
+    stream = sess.stream
+    ext = torch.cuda.ExternalStream(stream)
     barrier(world)
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -283,7 +293,6 @@ def run_ours(args):
     step_bytes = spec.weight_bytes_per_token() + kv_pos * mean_ctx + kv_pos / 1
     tok_s = K / (ms_max / 1e3)
     base = cpu_baseline(img) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
-    launches = sess.kernels_per_step * K
     del sess
     bs32 = run_batch(model, spec, args, hbm, peak_kind) if (world == 1 and args.batch > 1) else None
     if rank == 0:

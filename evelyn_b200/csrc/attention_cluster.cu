@@ -139,7 +139,7 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
 // the maximum and the sum meet by butterfly shuffles.
 template <int G>
 __device__ __forceinline__ void merge_weights(const float* part, uint32_t stride, int n, float* fac, float* mm, float* ml,
-                                              int warp, int lane) {
+                                              unsigned* live, int warp, int lane) {
     if (warp >= G) return;
     const float* pp = part + (lane * G + warp) * stride + stride - 2;
     const float m = lane < n ? pp[0] : -INFINITY;
@@ -152,9 +152,11 @@ __device__ __forceinline__ void merge_weights(const float* part, uint32_t stride
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     if (lane < n) fac[lane * G + warp] = empty ? -1.f : f;
+    const unsigned msk = __ballot_sync(0xffffffffu, !empty);  // the partials that hold positions
     if (lane == 0) {
         mm[warp] = M;
         ml[warp] = L;
+        live[warp] = msk;
     }
 }
 
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     float* cpart = vec + (G + 2) * HD + (wr ? 0 : kAW * G * (HD + 2));  // rank 0: [split][G][HD+2] (o, m, l)
     uint4* qfrag = reinterpret_cast<uint4*>(cpart + kMaxSplits * G * (HD + 2));  // [HD/16][lanes]: q hi/lo fragments
     __shared__ float fac[kAW * G], mrg_m[G], mrg_l[G];  // merge weights, maxima and sums
+    __shared__ unsigned live[G];                         // per head: the partials holding positions
 
     if (tid == 0) {
         for (uint32_t i = 0; i < F.stages; ++i) mbar_init(&full[i], 1);
@@ -540,15 +543,15 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // arithmetic). The weight exp(m_w - M) of a (warp, head) is the same for every
     // dimension, so G threads compute them once; the partial goes straight into rank
     // 0's shared memory (slot `rank`), which then merges the splits from its own copy.
-    merge_weights<G>(wpart, HD + 2, kAW, fac, mrg_m, mrg_l, warp, lane);
+    merge_weights<G>(wpart, HD + 2, kAW, fac, mrg_m, mrg_l, live, warp, lane);
     __syncthreads();
     float* dst = cl.map_shared_rank(cpart, 0) + rank * G * (HD + 2);
     for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
         const uint32_t g = i / HD, d = i % HD;
         float O = 0.f;
-        for (int w = 0; w < kAW; ++w) {
-            const float f = fac[w * G + g];
-            if (f >= 0.f) O += wpart[(w * G + g) * (HD + 2) + d] * f;  // f < 0: an empty warp
+        for (unsigned msk = live[g]; msk; msk &= msk - 1) {  // the warps that read positions, in order
+            const int w = __ffs(msk) - 1;
+            O += wpart[(w * G + g) * (HD + 2) + d] * fac[w * G + g];
         }
         dst[g * (HD + 2) + d] = O;
         if (d == 0) {
@@ -558,14 +561,14 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     }
     cl.sync();  // every CTA's partial is in rank 0's shared memory
     if (rank != 0) return;
-    merge_weights<G>(cpart, HD + 2, (int)C, fac, mrg_m, mrg_l, warp, lane);
+    merge_weights<G>(cpart, HD + 2, (int)C, fac, mrg_m, mrg_l, live, warp, lane);
     __syncthreads();
     for (uint32_t i = tid; i < (uint32_t)(G * HD); i += kAW * 32) {
         const uint32_t g = i / HD, d = i % HD;
         float O = 0.f;
-        for (uint32_t c = 0; c < C; ++c) {
-            const float f = fac[c * G + g];
-            if (f >= 0.f) O += cpart[(c * G + g) * (HD + 2) + d] * f;
+        for (unsigned msk = live[g]; msk; msk &= msk - 1) {
+            const int c = __ffs(msk) - 1;
+            O += cpart[(c * G + g) * (HD + 2) + d] * fac[c * G + g];
         }
         if (valid && !bad_sh) a.out[((uint64_t)sq * a.heads + kvh * G + g) * HD + d] = O / mrg_l[g];
     }
