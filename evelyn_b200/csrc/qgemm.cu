@@ -141,13 +141,24 @@ __host__ __device__ inline uint32_t mma_idesc(uint32_t n) {
     return (1u << 4) | ((n >> 3) << 17) | ((kMT >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t h2bits(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
 // two 10-bit unsigned integers in the low 10 bits of each half -> exact f16 pair,
 // times (s, s) minus (bias, bias): (1024 + v) * s - 1024 * s = v * s, one rounding of
 // an exact value (all terms < 65504)
+// Exact conversions on the FMA and ALU pipes instead of the conversion unit: an
+// integer 0 <= k < 1024 sits in the mantissa of half 1024 + k (0x6400 | k), and
+// 0 <= k < 2^23 in that of float 2^23 + k.
+__device__ __forceinline__ uint32_t small_int_h2(uint32_t k) {  // half2(k, k)
+    const uint32_t h = 0x64006400u | (k * 0x00010001u);
+    const uint32_t c = 0x64006400u;  // half2(1024, 1024)
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), *reinterpret_cast<const __half2*>(&c));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ float small_int_f(uint32_t k) { return __uint_as_float(0x4B000000u | k) - 8388608.f; }
+
 __device__ __forceinline__ uint32_t magic_fma(uint32_t v2, uint32_t s2, uint32_t b2) {
     const uint32_t h = v2 | 0x64006400u;
     __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), *reinterpret_cast<const __half2*>(&s2),
@@ -545,7 +556,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                 if (!bwait(&st_full[s], (n / kStages) & 1, &abort_flag)) { ok = false; break; }
                 const uint8_t* wb = smem + s * stage_bytes;
                 // this row's scales for the chunk
-                float q4_s[8], q4_m[8], d = 0.f, dmin = 0.f;
+                float q4_m[8], d = 0.f, dmin = 0.f;
+                uint32_t q4_sb[8];
                 float q8_d[8];
                 uint32_t q6_sc[4];
                 if (T == GGML_Q4_K) {
@@ -560,8 +572,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                     const uint32_t mb[2] = {w1 & 0x3F3F3F3Fu, ((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)};
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        q4_s[j] = (float)((sb[j >> 2] >> (8 * (j & 3))) & 0xffu);
-                        q4_m[j] = (float)((mb[j >> 2] >> (8 * (j & 3))) & 0xffu);
+                        q4_sb[j] = (sb[j >> 2] >> (8 * (j & 3))) & 0xffu;
+                        q4_m[j] = small_int_f((mb[j >> 2] >> (8 * (j & 3))) & 0xffu);
                     }
                     // -dmin * sum_j m_j * sum(x of sub-block j), this group's sequences
                     // (4 or 8 consecutive floats per sub-block: 16-byte loads; same FMA order)
@@ -610,9 +622,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                         tc_after();
                         uint32_t v[32];
                         if (T == GGML_Q4_K) {  // unit q: qs bytes 32q..32q+31, sub-blocks 2q (low), 2q+1 (high)
-                            const uint32_t sl = (uint32_t)q4_s[2 * q], sh = (uint32_t)q4_s[2 * q + 1];
-                            const uint32_t s2l = h2bits((float)sl, (float)sl), b2l = h2bits(-1024.f * sl, -1024.f * sl);
-                            const uint32_t s2h = h2bits((float)sh, (float)sh), b2h = h2bits(-1024.f * sh, -1024.f * sh);
+                            // half2 (s, s) and (-1024 s, -1024 s), exact (s <= 63)
+                            const uint32_t s2l = small_int_h2(q4_sb[2 * q]), b2l = hmul2_bits(s2l, 0xE400E400u);
+                            const uint32_t s2h = small_int_h2(q4_sb[2 * q + 1]), b2h = hmul2_bits(s2h, 0xE400E400u);
                             for (uint32_t hc = 0; hc < 2; ++hc) {
                                 const uint32_t ci = 2 * q + hc;
                                 const uint4 w = *reinterpret_cast<const uint4*>(wb + 2048 + t * 128 + ((ci ^ (t & 7)) * 16));
@@ -642,13 +654,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                             const uint32_t sidx0 = 8 * hh + 2 * kq, sidx1 = sidx0 + 1;
                             const int sc0 = (int8_t)(q6_sc[sidx0 >> 2] >> (8 * (sidx0 & 3)));
                             const int sc1 = (int8_t)(q6_sc[sidx1 >> 2] >> (8 * (sidx1 & 3)));
-                            const __half2 bias = __floats2half2_rn(1056.f, 1056.f);
+                            const uint32_t bias_b = 0x64206420u;  // half2(1056, 1056)
+                            const __half2 bias = *reinterpret_cast<const __half2*>(&bias_b);
+                            // per run: half2 of sc & 15 and of 16 (sc >> 4), exact, for the two planes
+                            uint32_t p1b[2], p2b[2];
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int sc = h ? sc1 : sc0;
+                                const int shi = sc >> 4, slo = sc - 16 * shi;     // shi in [-8, 7], slo in [0, 15]
+                                p1b[h] = small_int_h2((uint32_t)slo);
+                                const uint32_t sh8 = small_int_h2((uint32_t)(shi + 8));  // shi + 8, then - 8 and x 16
+                                const uint32_t m8 = 0xC800C800u;                       // half2(-8, -8)
+                                __half2 t = __hadd2(*reinterpret_cast<const __half2*>(&sh8), *reinterpret_cast<const __half2*>(&m8));
+                                const uint32_t c16 = 0x4C004C00u;                      // half2(16, 16)
+                                t = __hmul2(t, *reinterpret_cast<const __half2*>(&c16));
+                                p2b[h] = *reinterpret_cast<uint32_t*>(&t);
+                            }
 #pragma unroll
                             for (int a = 0; a < 8; ++a) {  // bytes 4a..4a+3 of the 32-value run pair
-                                const int sc = a < 4 ? sc0 : sc1;
-                                const int shi = sc >> 4, slo = sc - 16 * shi;
-                                const __half2 p1 = __floats2half2_rn((float)slo, (float)slo);
-                                const __half2 p2 = __floats2half2_rn((float)(16 * shi), (float)(16 * shi));
+                                const __half2 p1 = *reinterpret_cast<const __half2*>(&p1b[a < 4 ? 0 : 1]);
+                                const __half2 p2 = *reinterpret_cast<const __half2*>(&p2b[a < 4 ? 0 : 1]);
                                 const uint32_t nib = (kq < 2) ? (lw[a] & 0x0F0F0F0Fu) : ((lw[a] >> 4) & 0x0F0F0F0Fu);
                                 const uint32_t qv = nib | (((hw[a] >> (2 * kq)) & 0x03030303u) << 4);  // 0..63 per byte
                                 const uint32_t e0 = (qv & 0x00FF00FFu) | 0x64006400u, e1 = ((qv >> 8) & 0x00FF00FFu) | 0x64006400u;
@@ -663,7 +688,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
                             tmem_st16(tm + lane_addr + kColA + as * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                             tmem_st16(tm + lane_addr + kColA + as * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                         } else {  // Q8_0 block q: qs bytes 32q..32q+31
-                            const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+                            const uint32_t bias_b = 0x64806480u;  // half2(1152, 1152)
+                            const __half2 bias = *reinterpret_cast<const __half2*>(&bias_b);
                             for (uint32_t hc = 0; hc < 2; ++hc) {
                                 const uint32_t ci = 2 * q + hc;
                                 const uint4 w = *reinterpret_cast<const uint4*>(
