@@ -7,19 +7,21 @@
 // max-subtracted softmax of q.k / sqrt(hd) and the weighted sum of v (:723-766).
 //
 // Layout of the launch: one thread-block cluster of C CTAs per (sequence, kv head);
-// CTA `rank` of the cluster owns positions [rank*S, (rank+1)*S) (S whole pages). A
-// batch of many sequences uses C = 1 (one CTA per sequence and kv head, no merge). Everything
-// that does not come from the QKV matvec is done before griddepcontrol.wait: the
-// position and page table are read, the split's K and V page tiles are copied into
-// shared memory with TMA bulk copies, and the norm weights and RoPE sin/cos for the
-// position are loaded. (The position, the page table and the cached K/V rows were
-// written by earlier steps or by the host before this step's first kernel; the
-// launch before this one has passed its own griddepcontrol.wait, so every kernel
-// before it has completed.) After the wait, one warp per q head, k and v loads its
-// vector, normalises and rotates it in registers, the split that holds the new
-// position appends k and v (to HBM and to its shared copy), and the 16 warps run an
-// online softmax over the split's positions, one position per warp at a time,
-// entirely out of shared memory. The C partials (m, l, o) of a kv head meet through
+// CTA `rank` of the cluster owns positions [rank*S, (rank+1)*S) (S whole pages). One
+// sequence uses C = 8; a batch the largest C (down to 1, no merge) that keeps about
+// two CTAs per SM. Everything that does not come from the QKV matvec is done before
+// griddepcontrol.wait: the position and page table are read, the first chunks of the
+// split's K and V page tiles are copied into a shared-memory ring with TMA, and the
+// norm weights and RoPE sin/cos for the position are loaded. (The position, the page
+// table and the cached K/V rows were written by earlier steps or by the host before
+// this step's first kernel; the launch before this one has passed its own
+// griddepcontrol.wait, so every kernel before it has completed.) After the wait, one
+// warp per q head, k and v loads its vector, normalises and rotates it in registers,
+// the split that holds the new position appends k and v (to HBM and to its shared
+// copy), and the warps run an online softmax over the split's positions entirely out
+// of shared memory: on the tensor cores one 16-position page per warp (f16 pages), or
+// one position per warp (the scalar loop). The ring streams any number of chunks; a
+// warp group per ring stage. The C partials (m, l, o) of a kv head meet through
 // distributed shared memory: cluster rank 0 merges them in rank order.
 #include <cooperative_groups.h>
 #include <cuda.h>
