@@ -50,7 +50,7 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms around the timed regions."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -64,7 +64,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -214,6 +214,8 @@ def kernel_roofline(evl_rt, stream, hbm_peak, peak_kind, reps=8):
     gbs = alg / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(gbs / hbm_peak, 4), "traffic": profiled_traffic("qmatvec_q4k_12288x4096"),
+            "traffic_source": "copied from profiles/qmatvec_q4k_12288x4096.md (one ncu capture of this kernel "
+                              "and shape), not measured in this run",
             "peak_source": peak_kind,
             "kernel": "qmatvec_kernel (Q4_K, 12288x4096, ffn_gate shape)", "launch_us": round(ms * 1e3, 2),
             "bytes_per_launch": alg}
@@ -247,6 +249,9 @@ def run_ours(args):
         sess.step(int(t), logits=False)
     last = int(prompt[-1])
     # warm-up, then K timed device-resident steps (greedy loop stays on the GPU)
+    # clocks are sampled from the warm-up on (the timed region alone can be shorter than
+    # one sampling period) through the end-to-end loop below
+    clk = ClockSampler(local).__enter__()
     toks = sess.generate(last, W)
     stream = sess.stream
     ext = torch.cuda.ExternalStream(stream)
@@ -254,13 +259,12 @@ def run_ours(args):
     barrier(world)
     torch.cuda.synchronize()
     ctx0 = sess.pos
-    with ClockSampler(local) as clk:
-        e0.record(ext)
-        torch.cuda.nvtx.range_push("decode_steps")
-        toks = sess.generate(toks[-1], K)
-        torch.cuda.nvtx.range_pop()
-        e1.record(ext)
-        e1.synchronize()
+    e0.record(ext)
+    torch.cuda.nvtx.range_push("decode_steps")
+    toks = sess.generate(toks[-1], K)
+    torch.cuda.nvtx.range_pop()
+    e1.record(ext)
+    e1.synchronize()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     ms_max = dist_max(ms, world)
@@ -285,6 +289,7 @@ def run_ours(args):
         tok = evl.argmax(lg)
     f1.record(ext)
     f1.synchronize()
+    clk.__exit__(None, None, None)
     e2e_ms = dist_max(f0.elapsed_time(f1), world)
     hbm, peak_kind = peaks()
     roof = kernel_roofline(runtime, stream, hbm, peak_kind) if rank == 0 else None

@@ -535,7 +535,9 @@ evl_status evl_qmatrix_dequantize(const evl_qmatrix* q, float* d_out, void* stre
     });
 }
 
-namespace {
+}  // extern "C"
+
+namespace evl {
 
 void check_attention_args(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table,
                           uint32_t t, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size,
@@ -590,9 +592,13 @@ void attention_standalone(const float* d_q, const void* d_k_pages, const void* d
     cuda_check(launch_attention(a, s, false), "attention");
 }
 
-constexpr size_t kWsHeader = 256;  // error flag, padded so the partials stay aligned
+}  // namespace evl
 
+namespace {
+constexpr size_t kWsHeader = 256;  // error flag, padded so the partials stay aligned
 }  // namespace
+
+extern "C" {
 
 evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
                                 const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,

@@ -23,9 +23,10 @@
 //     time (from two host threads) race on it and can corrupt each other's output.
 //     Callers serialise them.
 //   * The first call on a device does the set-up (it resolves the array's device
-//     address with cudaGetSymbolAddress, which may load this library's device code);
-//     make that first call before any stream capture begins.
-#include <cmath>
+//     address with cudaGetSymbolAddress, which may load this library's device code).
+//   * Every call reads the error flag back into host memory and synchronises
+//     `stream`, so the entry point cannot be used inside a CUDA stream capture;
+//     evl_attention_decode_ws is the asynchronous variant on caller memory.
 #include <cstdio>
 #include <mutex>
 
@@ -63,29 +64,13 @@ uint8_t* scratch_for_current_device() {
     return static_cast<uint8_t*>(g_scratch_ptr[dev]);
 }
 
-// The split count of evl_attention_decode: enough (kv_head, split) CTAs to cover the
-// SMs twice, never more splits than pages.
-uint32_t noalloc_splits(uint32_t t, uint32_t kv_heads, uint32_t page_size) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint32_t pages = (t + page_size - 1) / page_size;
-    const uint32_t by_sms = (2u * (uint32_t)sms) / kv_heads;
-    return by_sms < 1 ? 1 : (pages < by_sms ? pages : by_sms);
-}
-
 void run(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table, uint32_t t,
          uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size, float* d_out, cudaStream_t s) {
-    if (!d_q || !d_k_pages || !d_v_pages || !d_page_table || !d_out) raise(EVL_ERR_INVALID_INPUT, "null argument");
-    if (t == 0) raise(EVL_ERR_INVALID_INPUT, "no positions to attend");
-    if (head_dim != 64 && head_dim != 128) raise(EVL_ERR_INVALID_INPUT, "head_dim must be 64 or 128");
-    if (page_size != 16) raise(EVL_ERR_INVALID_INPUT, "page_size must be 16");
-    if (!kv_heads || heads % kv_heads) raise(EVL_ERR_INVALID_INPUT, "heads must be a multiple of kv_heads");
-    const uint32_t g = heads / kv_heads;
-    if (g != 1 && g != 2 && g != 4 && g != 8) raise(EVL_ERR_INVALID_INPUT, "heads / kv_heads must be 1, 2, 4 or 8");
-
-    const uint32_t nsplit = noalloc_splits(t, kv_heads, page_size);
-    const size_t need = kNoAllocHeader + (size_t)heads * nsplit * (head_dim + 2) * sizeof(float);
+    // the same checks, split count and launch as evl_attention_decode (abi.cpp); only
+    // where the partials and the error flag live differs
+    check_attention_args(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out);
+    const uint32_t nsplit = attention_splits(t, kv_heads, page_size);
+    const size_t need = kNoAllocHeader + attention_part_bytes(heads, nsplit, head_dim);
     if (need > kNoAllocScratchBytes) {
         char msg[192];
         std::snprintf(msg, sizeof msg,
@@ -97,29 +82,8 @@ void run(const float* d_q, const void* d_k_pages, const void* d_v_pages, const i
     uint8_t* scratch = scratch_for_current_device();
     int32_t* d_err = reinterpret_cast<int32_t*>(scratch);
     cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int32_t), s), "memset");
-
-    AttnArgs a;
-    a.q = d_q;
-    a.out = d_out;
-    a.kv.pool = const_cast<void*>(d_k_pages);
-    a.kv.head_stride = (uint64_t)page_size * head_dim * 2;
-    a.kv.page_stride = a.kv.head_stride * kv_heads;
-    a.kv.layer_stride = 0;
-    a.kv.v_offset = static_cast<const uint8_t*>(d_v_pages) - static_cast<const uint8_t*>(d_k_pages);
-    a.kv.page_size = page_size;
-    a.kv.elem_bytes = 2;
-    a.page_table = d_page_table;
-    a.max_pages = (t + page_size - 1) / page_size;
-    a.pos = nullptr;
-    a.pos_value = (int32_t)(t - 1);
-    a.heads = heads;
-    a.kv_heads = kv_heads;
-    a.head_dim = head_dim;
-    a.nsplit = nsplit;
-    a.part = reinterpret_cast<float*>(scratch + kNoAllocHeader);
-    a.scale = 1.0f / sqrtf((float)head_dim);
-    a.err = d_err;
-    cuda_check(launch_attention(a, s, false), "attention");
+    attention_standalone(d_q, d_k_pages, d_v_pages, d_page_table, t, heads, kv_heads, head_dim, page_size, d_out,
+                         reinterpret_cast<float*>(scratch + kNoAllocHeader), nsplit, d_err, s);
 
     int32_t err = 0;
     cuda_check(cudaMemcpyAsync(&err, d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s), "D2H");

@@ -217,6 +217,20 @@ inline uint32_t prefetch_kb(uint32_t dflt) {
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
                    float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl);
 
+// ------------------------------------------------------------------ decode attention on caller buffers
+// Shared by the evl_attention_decode* entry points (abi.cpp, attention_noalloc.cu):
+// argument checks (InvalidInput), the split count over the sequence, the size of the
+// split partials, and one split-K attention launch with caller-provided partials and
+// device error flag.
+void check_attention_args(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table,
+                          uint32_t t, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size,
+                          const float* d_out);
+uint32_t attention_splits(uint32_t t, uint32_t kv_heads, uint32_t page_size);
+size_t attention_part_bytes(uint32_t heads, uint32_t nsplit, uint32_t head_dim);
+void attention_standalone(const float* d_q, const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table,
+                          uint32_t t, uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t page_size,
+                          float* d_out, float* part, uint32_t nsplit, int32_t* d_err, cudaStream_t s);
+
 // ------------------------------------------------------------------ sessions
 struct StepBuffers {
     uint32_t batch = 1;

@@ -130,6 +130,13 @@ private:
         fcntl(fd, F_SETFL, fl & ~O_NONBLOCK);
         int one = 1;
         setsockopt(fd, IPPROTO_TCP, TCP_NODELAY, &one, sizeof(one));
+        // set_read_timeout(Some(Duration::ZERO)) is an error in the reference (a zero
+        // SO_RCVTIMEO would mean "no timeout" here): the connection fails, so the layer
+        // falls back to the dense FFN like remote.rs:62-64 does
+        if (timeout_ms_ == 0) {
+            ::close(fd);
+            throw IoError{"cannot set a 0 duration timeout"};
+        }
         timeval rt{(time_t)(timeout_ms_ / 1000), (suseconds_t)((timeout_ms_ % 1000) * 1000)};
         setsockopt(fd, SOL_SOCKET, SO_RCVTIMEO, &rt, sizeof(rt));
         timeval wt{30, 0};
@@ -141,6 +148,7 @@ private:
         const uint8_t* b = static_cast<const uint8_t*>(p);
         while (n) {
             ssize_t w = ::send(fd_, b, n, MSG_NOSIGNAL);
+            if (w < 0 && errno == EINTR) continue;  // write_all retries Interrupted
             if (w <= 0) throw IoError{w == 0 ? "write zero" : strerror(errno)};
             b += w;
             n -= (size_t)w;
@@ -150,6 +158,7 @@ private:
         uint8_t* b = static_cast<uint8_t*>(p);
         while (n) {
             ssize_t r = ::recv(fd_, b, n, 0);
+            if (r < 0 && errno == EINTR) continue;  // read_exact retries Interrupted
             if (r == 0) throw IoError{"failed to fill whole buffer"};
             if (r < 0) throw IoError{strerror(errno)};
             b += r;

@@ -3,7 +3,7 @@
  *
  * Every entry point is a drop-in for one item of the reference's Rust runtime
  * API (paths below are inside the neuralmimicry/evelyn tree). A Rust FFI crate
- * binds these one-to-one; INTEGRATION.md shows the binding.
+ * binds these one-to-one.
  *
  * Conventions
  *   - Plain pointers and sizes only. "host" buffers are ordinary CPU memory;
@@ -198,10 +198,11 @@ evl_status evl_attention_decode_ws(const float* d_q, const void* d_k_pages, cons
  * 1.5 MiB array per device inside this library; a shape needing more is rejected
  * with EVL_ERR_INVALID_INPUT (on a 148-SM B200 every accepted shape fits). The call
  * clears the scratch's error flag itself and synchronises `stream` before returning.
- * The first call on a device resolves the array's address (set-up): make it before
- * any stream capture. Calls on one device that overlap in time race on the shared
- * scratch; the caller serialises them. Same arguments and results as
- * evl_attention_decode. */
+ * The first call on a device resolves the array's address (set-up). Every call reads
+ * the error flag back to the host and synchronises `stream`, so it cannot be used
+ * inside a stream capture (evl_attention_decode_ws is the asynchronous variant).
+ * Calls on one device that overlap in time race on the shared scratch; the caller
+ * serialises them. Same arguments and results as evl_attention_decode. */
 evl_status evl_attention_decode_noalloc(const float* d_q, const void* d_k_pages, const void* d_v_pages,
                                         const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,
                                         uint32_t head_dim, uint32_t page_size, float* d_out, void* stream);

@@ -1,0 +1,142 @@
+"""Parity at the benchmarked shapes (src/runtime.rs:773-808 through the C ABI against
+the CPU oracle):
+
+* the Qwen3-0.6B-shape (28 layers, all Q8_0) and Qwen3-8B-shape (36 layers, Q4_K_M
+  mix) synthetic models: a 16-token random prompt fed to both, teacher-forced
+  perplexity over it, then 64 greedy steps from each side's own argmax -- logits
+  within max-abs 2e-3 at every step, identical greedy tokens, PPL within 0.5 %
+  (the protocol of src/bin/evelyn-generate.rs:69-86);
+* head_dim 128 sessions with GQA groups 2, 4 and 8 run past 1200 positions, so the
+  single-sequence cluster attention streams its 8 splits through the page ring at the
+  benchmark's head size (with the default ring and with a 2-page ring);
+* the matvec paths only the big shapes reach: the LM-head shape 151936x4096 Q8_0
+  (more row blocks per CTA than partial buffers: rotating buffers, last-warp
+  reduction) and 5120x25600 Q6_K (rows longer than 12288 values: quarter staging).
+"""
+import ctypes as C
+import math
+
+import numpy as np
+import pytest
+
+import evelyn_b200 as evl
+from evelyn_b200 import runtime, synth
+from oracle import oracle as orc
+from tests import gpu_util as gu
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-3
+
+
+def _tokens(n, vocab, seed):
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+def _top2_margin(logits):
+    top = np.partition(logits, -2)[-2:]
+    return float(top[1] - top[0])
+
+
+def _generate_protocol(spec, prompt_len=16, steps=64, seed=0):
+    """Prompt (teacher-forced PPL) then greedy decode on both sides; returns the worst
+    logit difference, both PPLs and both token streams."""
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=0)
+    r = orc.Model(img)
+    s = evl.Session(m, max_ctx=prompt_len + steps + 8)
+    rs = orc.Session(r)
+    prompt = _tokens(prompt_len, spec.vocab, seed)
+    worst, nll_g, nll_o = 0.0, 0.0, 0.0
+    for i, tok in enumerate(prompt):
+        lg, lo = s.step(tok), rs.step(tok)
+        worst = max(worst, float(np.abs(lg - lo).max()))
+        if i + 1 < len(prompt):
+            nll_g -= evl.log_prob(lg, prompt[i + 1])
+            nll_o -= orc.log_prob(lo, prompt[i + 1])
+    n = len(prompt) - 1
+    ppl_g, ppl_o = math.exp(nll_g / n), math.exp(nll_o / n)
+    tg, to = evl.argmax(lg), orc.argmax(lo)
+    out_g, out_o, margins = [], [], []
+    for _ in range(steps):
+        out_g.append(tg)
+        out_o.append(to)
+        lg, lo = s.step(tg), rs.step(to)
+        worst = max(worst, float(np.abs(lg - lo).max()))
+        margins.append(_top2_margin(lo))
+        tg, to = evl.argmax(lg), orc.argmax(lo)
+    return worst, ppl_g, ppl_o, out_g, out_o, min(margins)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("shape", ["qwen3_0_6b", "qwen3_8b"])
+def test_benchmark_shape_generate_matches_oracle(shape):
+    spec = getattr(synth, shape)(seed=0)
+    worst, ppl_g, ppl_o, out_g, out_o, margin = _generate_protocol(spec)
+    assert worst <= LOGIT_TOL, worst
+    assert abs(ppl_g / ppl_o - 1) < 0.005, (ppl_g, ppl_o)
+    assert out_g == out_o, (out_g, out_o, margin)
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(4, 2), (8, 2), (8, 1)])
+@pytest.mark.parametrize("ring", [None, "2"])
+def test_hd128_cluster_attention_long_context(heads, kv_heads, ring, monkeypatch):
+    """GQA group 2 / 4 / 8 at head_dim 128 (the 0.6B, 8B and 32B groups) past 1200
+    positions: every 25th step's logits against the oracle, and greedy agreement."""
+    if ring:
+        monkeypatch.setenv("EVELYN_ATTN_RING", ring)
+    spec = synth.tiny(seed=31 + heads + kv_heads, head_dim=128, heads=heads, kv_heads=kv_heads, layers=2)
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=0)
+    r = orc.Model(img)
+    s, rs = evl.Session(m, max_ctx=1280), orc.Session(r)
+    toks = _tokens(1240, spec.vocab, seed=heads * 10 + kv_heads)
+    worst = 0.0
+    for i, tok in enumerate(toks):
+        want = rs.step(tok)
+        if i % 25 == 0 or i >= len(toks) - 4:
+            got = s.step(tok)
+            worst = max(worst, float(np.abs(got - want).max()))
+            assert evl.argmax(got) == orc.argmax(want) or _top2_margin(want) < 2 * LOGIT_TOL
+        else:
+            s.step(tok, logits=False)
+    assert s.pos == rs.pos == len(toks)
+    assert worst <= LOGIT_TOL, worst
+
+
+def _big_matvec_case(t, rows, cols, seed):
+    rng = np.random.default_rng(seed)
+    block = 32 if t == synth.GGML_Q8_0 else 256
+    raw = gu.random_blocks(t, rows * cols // block, rng)
+    x = rng.standard_normal(cols).astype(np.float32)
+    # reference in row chunks: exact dequantisation by the oracle, product in float64
+    rb = synth.type_bytes(t, cols)
+    want = np.empty(rows)
+    scale = np.empty(rows)
+    xd = x.astype(np.float64)
+    step = 4096
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        w = orc.dequantize(t, raw[r0 * rb:r1 * rb], (r1 - r0) * cols).reshape(r1 - r0, cols).astype(np.float64)
+        want[r0:r1] = w @ xd
+        scale[r0:r1] = np.abs(w) @ np.abs(xd)
+    return raw, x, want, scale
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("t,rows,cols", [(synth.GGML_Q8_0, 151936, 4096), (synth.GGML_Q6_K, 5120, 25600),
+                                         (synth.GGML_Q4_K, 25600, 5120)])
+def test_big_shape_matvec(t, rows, cols):
+    raw, x, want, scale = _big_matvec_case(t, rows, cols, seed=rows ^ cols)
+    h = C.c_void_p()
+    buf = np.frombuffer(raw, dtype=np.uint8)
+    runtime.check(runtime.lib().evl_qmatrix_create(t, rows, cols, C.c_void_p(buf.ctypes.data), 0, C.byref(h)))
+    try:
+        dx, dy = gu.to_dev(x), gu.empty_f32(rows)
+        for _ in range(2):  # the second launch reuses the first one's buffers
+            runtime.check(runtime.lib().evl_qmatrix_matvec(h, gu.ptr(dx), gu.ptr(dy), None))
+            gu.sync()
+            got = dy.cpu().numpy().astype(np.float64)
+            assert np.all(np.abs(got - want) <= 5e-5 * scale + 1e-7), float(np.abs(got - want).max())
+    finally:
+        runtime.lib().evl_qmatrix_free(h)

@@ -180,3 +180,19 @@ def test_stats_for_unrouted_layer_is_not_found():
         assert rc == 3  # NotFound
     finally:
         runtime.lib().evl_remote_ffn_free(h)
+
+
+def test_zero_read_timeout_falls_back():
+    """set_read_timeout(Some(Duration::ZERO)) fails in the reference's connect
+    (remote.rs:62-64), so the layer falls back to the dense FFN instead of blocking."""
+    srv = FakeRegion(["ok"] * 4)
+    h, b = make_remote({0: f"127.0.0.1:{srv.port}"}, timeout_ms=0)
+    try:
+        rc, _ = call(b, 0, np.ones(4, dtype=np.float32))
+        assert rc == EVL_FFN_DENSE
+        assert runtime.lib().evl_remote_ffn_fallbacks(h) == 1
+        st = stats(h, 0)
+        assert st.failures == 1 and st.retries == 1 and srv.requests == 0
+    finally:
+        runtime.lib().evl_remote_ffn_free(h)
+        srv.close()
