@@ -245,6 +245,12 @@ struct StepBuffers {
     bool kv_tmap_ok = false;
     uint32_t nsplit = 1, amax_parts = 1;
     PinnedBuffer h_tokens, h_argmax, h_logits, h_xn, h_y, h_err;
+    // persistent step kernel (decode_step.cu): its tagged vectors (x, q, k, v, attention
+    // partials, attention output, h) and the step counter their tags derive from
+    DeviceBuffer tagpool, epoch;
+    uint64_t *xt = nullptr, *qt = nullptr, *kt = nullptr, *vt = nullptr, *partt = nullptr, *attt = nullptr,
+             *ht = nullptr;
+    uint32_t tag_period = 0;
 };
 
 struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
@@ -256,7 +262,7 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     bool graph_pdl = true;
     std::vector<uint64_t> host_pos;
     uint32_t kernels = 0, kernels_per_step = 0;
-    StepKernel* step_k = nullptr;  // persistent layer-stack kernel (single sequence, one GPU)
+    StepKernel* step_k = nullptr;  // persistent whole-step kernel (single sequence)
     bool step_tried = false;
     std::string step_note;        // why the step kernel is not used, if it is not
 

@@ -117,24 +117,65 @@ bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* o
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
                                      cudaStream_t s, bool pdl, const KvTmap* tmap = nullptr);
 
-// ---------------------------------------------------------------- step_kernel.cu
-// One decoder layer of a single-sequence step, as the separate launches would run it:
-// fused QKV matvec (attn norm), QK-norm/RoPE/append, attention (its nsplit and part
-// sized for this kernel), o matvec + residual, SwiGLU gate/up (ffn norm), down + residual.
-struct StepLayer {
-    MatvecArgs qkv;
-    RopeArgs rope;
-    AttnArgs attn;
-    MatvecArgs o, gateup, down;
+// ---------------------------------------------------------------- decode_step.cu
+// A whole single-sequence decode step as one persistent kernel (decode_step.cu). Its
+// phases hand vectors to one another as tagged pairs: each element is one 8-byte word,
+// (tag << 32) | f32 bits, stored in a single access; a reader waits until the words it
+// needs carry the tag it expects. Tags are `epoch * period + 1 + slot`, where epoch is
+// the number of completed steps (a device counter the step's argmax advances) and
+// slot names the (layer, vector) the word belongs to.
+constexpr int kMaxPeers = 8;  // tensor-parallel ranks a phase writes its rows to
+
+// Where the rows of a matvec segment (or the attention output) go: the same rows
+// [row0, row0 + rows) of ndst full-length vectors -- this rank's copy first, then the
+// peers' copies (tensor parallelism) -- as tagged words (dst) or plain floats (plain).
+struct TaggedOut {
+    uint64_t* dst[kMaxPeers] = {};
+    float* plain[kMaxPeers] = {};
+    uint32_t ndst = 0, row0 = 0, tag = 0;
+    const uint64_t* resid = nullptr;  // EPI_ADD: the residual (this rank's full vector, tagged)
+    uint32_t resid_tag = 0;
+};
+
+// QK-norm, RoPE, KV append, split-K GQA attention and the split merge of one layer.
+struct StepAttn {
+    const uint64_t *q = nullptr, *k = nullptr, *v = nullptr;  // tagged [lheads*hd], [lkv*hd], [lkv*hd]
+    uint32_t qkv_tag = 0;
+    uint64_t* part = nullptr;  // tagged partials [lkv][nsplit][G][hd + 2] (o..., m, l)
+    uint32_t part_tag = 0;
+    TaggedOut out;             // attention output rows [lheads * hd] at row0 of [heads * hd]
+    RopeArgs rope;             // norms, RoPE table, KV cache, layer, page table, position, shape
+    uint32_t nsplit = 1;       // splits per kv head (one CTA each)
+    uint32_t ring_pages = 2;   // K/V page pairs a split stages at a time (even)
+    float scale = 0.f;
+};
+
+enum StepPhaseKind : uint32_t { STEP_MATVEC = 0, STEP_ATTN = 1 };
+struct StepPhaseDesc {
+    uint32_t kind = STEP_MATVEC;
+    MatvecArgs mv;                 // segments, cols, norm_w, eps (x and seg[].y unused)
+    const uint64_t* xt = nullptr;  // tagged input [cols]
+    uint32_t x_tag = 0;
+    TaggedOut out[kMaxSegs];
+    StepAttn at;
 };
 struct StepKernel;
-// Builds the persistent layer-stack kernel (one cooperative CTA per SM) for these
-// layers; cudaErrorNotSupported / cudaErrorInvalidValue when it does not apply.
-cudaError_t step_kernel_create(const StepLayer* layers, uint32_t nlayers, int* err, StepKernel** out);
+// Builds the persistent step kernel over `n` phases (one cooperative CTA per SM);
+// `epoch` is read at the start of every launch, `period` the tag slots per step.
+// cudaErrorInvalidValue / cudaErrorNotSupported when the phases do not fit it.
+cudaError_t step_kernel_create(const StepPhaseDesc* phases, uint32_t n, const uint32_t* epoch, uint32_t period,
+                               int* err, StepKernel** out);
 cudaError_t step_kernel_launch(const StepKernel* k, cudaStream_t s);
-// Clears the grid-barrier and abort state (after a step that reported an error).
+// Clears the grid abort flag (after a step that reported an error).
 cudaError_t step_kernel_reset(const StepKernel* k, cudaStream_t s);
 void step_kernel_destroy(StepKernel* k);
+// Splits and page-ring size the step kernel's attention phase uses for a cache of
+// max_pages pages per sequence on a GPU with `sms` SMs.
+uint32_t step_attn_splits(uint32_t kv_heads, uint32_t max_pages, int sms);
+// The embedding row of tokens[0] (QMatrix::row, src/runtime.rs:54-69) as tagged words
+// with slot 0 of the current epoch.
+cudaError_t launch_embed_tagged(const QMatDev& embed, const int32_t* tokens, uint64_t* xt, const uint32_t* epoch,
+                                uint32_t period, int32_t* err, cudaStream_t s);
 
 // ---------------------------------------------------------------- qgemm.cu
 // A matrix in the GEMM layout (per 128-row M tile and 256-value K chunk, one block of
@@ -198,8 +239,9 @@ cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, boo
 // Greedy pick over [batch][n] logits: first maximum wins (strict '>' like src/runtime.rs:897-905).
 // Optionally writes the pick to next_tokens, logs it at hist[b*hist_stride + pos[b]] and
 // advances pos[b] (null pointers skip each part).
+// epoch (optional) is advanced once the pick is made: the step's last kernel.
 cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t batch, float* part_v, int32_t* part_i,
                           uint32_t parts, int32_t* out, int32_t* next_tokens, int32_t* pos, int32_t* hist,
-                          uint32_t hist_stride, cudaStream_t s, bool pdl);
+                          uint32_t hist_stride, cudaStream_t s, bool pdl, uint32_t* epoch = nullptr);
 
 }  // namespace evl

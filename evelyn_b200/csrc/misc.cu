@@ -116,7 +116,8 @@ __global__ void argmax_part_kernel(const float* __restrict__ logits, uint32_t n,
 // input (greedy loop on the device), is logged at hist[b][pos], and pos advances
 // (Session::step's `self.pos += 1`, src/runtime.rs:806).
 __global__ void argmax_final_kernel(const float* part_v, const int32_t* part_i, uint32_t parts, int32_t* out,
-                                    int32_t* next_tokens, int32_t* pos, int32_t* hist, uint32_t hist_stride) {
+                                    int32_t* next_tokens, int32_t* pos, int32_t* hist, uint32_t hist_stride,
+                                    uint32_t* epoch) {
     pdl_wait();
     const uint32_t b = blockIdx.x;
     float bv = -FLT_MAX;
@@ -136,6 +137,7 @@ __global__ void argmax_final_kernel(const float* part_v, const int32_t* part_i, 
             if (hist && (uint32_t)p < hist_stride) hist[(uint64_t)b * hist_stride + p] = r;
             pos[b] = p + 1;
         }
+        if (epoch && b == 0) *epoch += 1;  // the step is complete: the next one's tags
     }
     pdl_launch_dependents();
 }
@@ -164,14 +166,14 @@ cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, boo
 
 cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t batch, float* part_v, int32_t* part_i,
                           uint32_t parts, int32_t* out, int32_t* next_tokens, int32_t* pos, int32_t* hist,
-                          uint32_t hist_stride, cudaStream_t s, bool pdl) {
+                          uint32_t hist_stride, cudaStream_t s, bool pdl, uint32_t* epoch) {
     cudaLaunchAttribute at[1];
     auto cfg = cfg_of(dim3(parts, batch), dim3(256), s, pdl, at);
     cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_part_kernel, logits, n, part_v, part_i);
     if (e != cudaSuccess) return e;
     auto cfg2 = cfg_of(dim3(batch), dim3(32), s, pdl, at);
     return cudaLaunchKernelEx(&cfg2, argmax_final_kernel, (const float*)part_v, (const int32_t*)part_i, parts, out,
-                              next_tokens, pos, hist, hist_stride);
+                              next_tokens, pos, hist, hist_stride, epoch);
 }
 
 }  // namespace evl

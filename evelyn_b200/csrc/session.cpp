@@ -419,58 +419,144 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
     }
 }
 
-// The persistent layer-stack kernel for a single sequence on one GPU (step_kernel.cu),
-// used when EVELYN_STEP_KERNEL=1. It is correct (same matvec code, tested against the
-// launch sequence and the oracle) but not yet faster than the launch sequence with
-// programmatic dependent launches, which stays the default.
+// The persistent whole-step kernel for a single sequence (decode_step.cu): every layer
+// and the LM head in one cooperative launch, phases handing vectors on as tagged words.
+// Used unless EVELYN_STEP_KERNEL=0; when it cannot be built (or captured) the step
+// runs as the launch sequence below, and step_note says why.
 void Decoder::build_step_kernel() {
     Model& m = *model;
     const Config& c = m.cfg;
     step_tried = true;
     const char* env = std::getenv("EVELYN_STEP_KERNEL");
-    if (!env || env[0] != '1') return;
-    if (b.batch != 1 || m.tp_size != 1) return;
+    if (env && env[0] == '0') return;
+    if (b.batch != 1) return;
+    if (m.tp_size != 1) {
+        step_note = "step kernel not used: tensor parallelism";
+        return;
+    }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m.device);
-    const uint32_t nsplit =
-        std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sms / std::max<uint32_t>(1, m.lkv_heads), b.pages_per_seq));
-    if (nsplit > b.nsplit) return;  // the partials buffer is sized for b.nsplit
-    const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd;
-    std::vector<StepLayer> layers(c.layers);
-    for (uint32_t li = 0; li < c.layers; ++li) {
-        const LayerWeights& L = m.layers[li];
-        StepLayer& s = layers[li];
-        s.qkv = qkv_args(li);
-        s.qkv.prefetch_bytes = 0;
-        s.rope = rope_args(li);
-        s.attn = attn_args(li, nsplit);
-        s.o.nseg = 1;
-        s.o.seg[0].m = L.o.dev;
-        s.o.seg[0].y = b.x.as<float>();
-        s.o.seg[0].epi = EPI_ADD;
-        s.o.x = b.att.as<float>();
-        s.o.cols = (uint32_t)qw;
-        s.o.err = b.err.as<int>();
-        s.gateup.nseg = 1;
-        s.gateup.seg[0].m = L.gate.dev;
-        s.gateup.seg[0].m2 = L.up.dev;
-        s.gateup.seg[0].y = b.h.as<float>();
-        s.gateup.seg[0].epi = EPI_SWIGLU;
-        s.gateup.x = b.x.as<float>();
-        s.gateup.cols = (uint32_t)c.dim;
-        s.gateup.norm_w = L.ffn_norm;
-        s.gateup.eps = c.eps;
-        s.gateup.err = b.err.as<int>();
-        s.down.nseg = 1;
-        s.down.seg[0].m = L.down.dev;
-        s.down.seg[0].y = b.x.as<float>();
-        s.down.seg[0].epi = EPI_ADD;
-        s.down.x = b.h.as<float>();
-        s.down.cols = m.lffn;
-        s.down.err = b.err.as<int>();
+    const uint32_t hd = (uint32_t)c.head_dim, G = m.lheads / std::max<uint32_t>(1, m.lkv_heads);
+    const uint32_t L = (uint32_t)c.layers, T = (uint32_t)m.tp_size, R = (uint32_t)m.tp_rank;
+    const uint32_t nsplit = step_attn_splits(m.lkv_heads, b.pages_per_seq, sms);
+    const uint32_t eb = m.kv_f32 ? 4 : 2;
+    // page pairs staged per split at a time: as many as the per-warp partials' bytes hold
+    uint32_t ring = (uint32_t)((16ull * G * (hd + 2) * 4) / (2ull * 16 * hd * eb)) & ~1u;
+    ring = std::max<uint32_t>(2, std::min<uint32_t>(16, ring));
+    // tagged vectors, each on a 256-byte boundary (words)
+    auto up = [](uint64_t n) { return (n + 31) & ~31ull; };
+    const uint64_t nx = up(c.dim), nq = up((uint64_t)m.lheads * hd), nk = up((uint64_t)m.lkv_heads * hd);
+    const uint64_t np = up((uint64_t)m.lkv_heads * nsplit * G * (hd + 2)), na = up(c.heads * hd), nh = up(c.ffn);
+    b.tagpool.alloc((nx + nq + 2 * nk + np + na + nh) * 8);
+    cuda_check(cudaMemset(b.tagpool.p, 0xff, b.tagpool.bytes), "memset");  // tag 0xffffffff: never expected
+    uint64_t* w = b.tagpool.as<uint64_t>();
+    b.xt = w, w += nx;
+    b.qt = w, w += nq;
+    b.kt = w, w += nk;
+    b.vt = w, w += nk;
+    b.partt = w, w += np;
+    b.attt = w, w += na;
+    b.ht = w;
+    b.epoch.alloc(4);
+    cuda_check(cudaMemset(b.epoch.p, 0, 4), "memset");
+    b.tag_period = 8 * (L + 1);
+    // slots per layer l: x entering it 8l, q/k/v 8l+1, partials 8l+2, attention 8l+3,
+    // x after o 8l+4, h 8l+5; x entering the LM head 8L
+    auto out1 = [](uint64_t* dst, uint32_t row0, uint32_t slot) {
+        TaggedOut o;
+        o.dst[0] = dst;
+        o.ndst = 1;
+        o.row0 = row0;
+        o.tag = slot;
+        return o;
+    };
+    const uint32_t o_row0 = R * (uint32_t)(c.dim / T);
+    uint64_t f0 = 0;
+    {  // this rank's first FFN row (the gate/up shard)
+        const uint64_t nb = c.ffn / 256, base = nb / T, rem = nb % T;
+        f0 = T > 1 ? (R * base + std::min<uint64_t>(R, rem)) * 256 : 0;
+    }
+    std::vector<StepPhaseDesc> ph;
+    for (uint32_t li = 0; li < L; ++li) {
+        const LayerWeights& LW = m.layers[li];
+        StepPhaseDesc d;
+        d.mv = qkv_args(li);
+        d.xt = b.xt;
+        d.x_tag = 8 * li;
+        d.out[0] = out1(b.qt, 0, 8 * li + 1);
+        d.out[1] = out1(b.kt, 0, 8 * li + 1);
+        d.out[2] = out1(b.vt, 0, 8 * li + 1);
+        ph.push_back(d);
+        StepPhaseDesc at;
+        at.kind = STEP_ATTN;
+        at.at.q = b.qt;
+        at.at.k = b.kt;
+        at.at.v = b.vt;
+        at.at.qkv_tag = 8 * li + 1;
+        at.at.part = b.partt;
+        at.at.part_tag = 8 * li + 2;
+        at.at.out = out1(b.attt, R * m.lheads * hd, 8 * li + 3);
+        at.at.rope = rope_args(li);
+        at.at.nsplit = nsplit;
+        at.at.ring_pages = ring;
+        at.at.scale = 1.0f / sqrtf((float)hd);
+        ph.push_back(at);
+        StepPhaseDesc o;
+        o.mv.nseg = 1;
+        o.mv.seg[0].m = LW.o.dev;
+        o.mv.seg[0].epi = EPI_ADD;
+        o.mv.cols = LW.o.cols;
+        o.mv.err = b.err.as<int>();
+        o.xt = b.attt;
+        o.x_tag = 8 * li + 3;
+        o.out[0] = out1(b.xt, o_row0, 8 * li + 4);
+        o.out[0].resid = b.xt;
+        o.out[0].resid_tag = 8 * li;
+        ph.push_back(o);
+        StepPhaseDesc gu;
+        gu.mv.nseg = 1;
+        gu.mv.seg[0].m = LW.gate.dev;
+        gu.mv.seg[0].m2 = LW.up.dev;
+        gu.mv.seg[0].epi = EPI_SWIGLU;
+        gu.mv.cols = (uint32_t)c.dim;
+        gu.mv.norm_w = LW.ffn_norm;
+        gu.mv.eps = c.eps;
+        gu.mv.err = b.err.as<int>();
+        gu.xt = b.xt;
+        gu.x_tag = 8 * li + 4;
+        gu.out[0] = out1(b.ht, (uint32_t)f0, 8 * li + 5);
+        ph.push_back(gu);
+        StepPhaseDesc dn;
+        dn.mv.nseg = 1;
+        dn.mv.seg[0].m = LW.down.dev;
+        dn.mv.seg[0].epi = EPI_ADD;
+        dn.mv.cols = LW.down.cols;
+        dn.mv.err = b.err.as<int>();
+        dn.xt = b.ht;
+        dn.x_tag = 8 * li + 5;
+        dn.out[0] = out1(b.xt, o_row0, 8 * (li + 1));
+        dn.out[0].resid = b.xt;
+        dn.out[0].resid_tag = 8 * li + 4;
+        ph.push_back(dn);
+    }
+    {  // final RMSNorm + LM head into the logits (plain floats)
+        StepPhaseDesc hd_;
+        hd_.mv.nseg = 1;
+        hd_.mv.seg[0].m = m.lm_head.dev;
+        hd_.mv.cols = (uint32_t)c.dim;
+        hd_.mv.norm_w = m.out_norm;
+        hd_.mv.eps = c.eps;
+        hd_.mv.err = b.err.as<int>();
+        hd_.xt = b.xt;
+        hd_.x_tag = 8 * L;
+        hd_.out[0].plain[0] = b.logits.as<float>();
+        hd_.out[0].ndst = 1;
+        hd_.out[0].row0 = m.vocab0;
+        ph.push_back(hd_);
     }
     StepKernel* k = nullptr;
-    const cudaError_t e = step_kernel_create(layers.data(), (uint32_t)layers.size(), b.err.as<int>(), &k);
+    const cudaError_t e =
+        step_kernel_create(ph.data(), (uint32_t)ph.size(), b.epoch.as<uint32_t>(), b.tag_period, b.err.as<int>(), &k);
     if (e != cudaSuccess) {
         cudaGetLastError();
         step_note = std::string("step kernel not used: ") + cudaGetErrorString(e);
@@ -520,6 +606,19 @@ void Decoder::enqueue_dense(bool pdl) {
     Model& m = *model;
     const Config& c = m.cfg;
     kernels = 0;
+    if (step_k) {  // every layer and the LM head in one launch, then the argmax
+        cuda_check(launch_embed_tagged(m.embed.dev, b.tokens.as<int32_t>(), b.xt, b.epoch.as<uint32_t>(), b.tag_period,
+                                       b.err.as<int32_t>(), stream),
+                   "embed");
+        cuda_check(step_kernel_launch(step_k, stream), "step kernel");
+        cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, 1, b.amax_v.as<float>(),
+                                 b.amax_i.as<int32_t>(), b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(),
+                                 b.pos.as<int32_t>(), b.hist.as<int32_t>(), b.max_ctx, stream, false,
+                                 b.epoch.as<uint32_t>()),
+                   "argmax");
+        kernels_per_step = kernels = 4;
+        return;
+    }
     cuda_check(launch_embed(m.embed.dev, b.tokens.as<int32_t>(), b.batch, b.x.as<float>(), b.err.as<int32_t>(), stream,
                             pdl),
                "embed");
@@ -529,10 +628,7 @@ void Decoder::enqueue_dense(bool pdl) {
         kernels_per_step = kernels;
         return;
     }
-    if (step_k) {
-        cuda_check(step_kernel_launch(step_k, stream), "step kernel");
-        kernels += 1;
-    } else {
+    {
         for (uint32_t li = 0; li < c.layers; ++li) {
             enqueue_layer_attention(li, pdl);
             QMatDev next[3] = {m.lm_head.dev, QMatDev{}, QMatDev{}};

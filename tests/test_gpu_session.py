@@ -266,23 +266,44 @@ def test_cluster_attention_streamed_pages(monkeypatch, ring, mma):
 
 
 def test_step_kernel_matches_launch_sequence(monkeypatch):
-    """The persistent layer-stack kernel (one launch per step) against the per-kernel
-    launch sequence on the same model and tokens: same logits within the attention's
-    summation-order tolerance, same greedy tokens, and far fewer launches."""
+    """The persistent whole-step kernel (every layer and the LM head in one launch,
+    phases handing vectors on as tagged words) against the per-kernel launch sequence
+    on the same model and tokens: same logits within the attention's summation-order
+    tolerance, same greedy tokens, and far fewer launches; then against the oracle."""
     spec = synth.tiny(seed=21, layers=3)
     img, m, r = _models(spec)
-    toks = _tokens(40, spec.vocab, seed=4)
-    monkeypatch.setenv("EVELYN_STEP_KERNEL", "1")
+    toks = _tokens(150, spec.vocab, seed=4)
+    monkeypatch.delenv("EVELYN_STEP_KERNEL", raising=False)
     s1 = evl.Session(m, max_ctx=256)
     out1 = [s1.step(t) for t in toks]
     monkeypatch.setenv("EVELYN_STEP_KERNEL", "0")
     s2 = evl.Session(m, max_ctx=256)
     out2 = [s2.step(t) for t in toks]
-    assert s1.kernels_per_step < 8 < s2.kernels_per_step
+    assert s1.kernels_per_step == 4 < s2.kernels_per_step
     assert max(float(np.abs(a - b).max()) for a, b in zip(out1, out2)) <= 1e-4
     g1 = s1.generate(evl.argmax(out1[-1]), 24)
     g2 = s2.generate(evl.argmax(out2[-1]), 24)
     assert list(g1) == list(g2)
     rs = orc.Session(r)  # and the oracle
     worst = max(float(np.abs(a - rs.step(t)).max()) for a, t in zip(out1, toks))
+    assert worst <= LOGIT_TOL, worst
+
+
+@pytest.mark.parametrize("heads,kv_heads,kv_f32", [(4, 2, False), (8, 1, False), (4, 4, True), (8, 2, True)])
+def test_step_kernel_groups_and_kv_types(heads, kv_heads, kv_f32, monkeypatch):
+    """The persistent step kernel at GQA groups 2, 8, 1, 4 (head_dim 128) with f16 and
+    f32 KV pages, past several attention chunks per split, against the oracle."""
+    monkeypatch.delenv("EVELYN_STEP_KERNEL", raising=False)
+    spec = synth.tiny(seed=40 + heads + kv_heads, head_dim=128, heads=heads, kv_heads=kv_heads, layers=2)
+    img, m, r = _models(spec, kv_f32=kv_f32)
+    s, rs = evl.Session(m, max_ctx=700), orc.Session(r)
+    worst = 0.0
+    for i, tok in enumerate(_tokens(650, spec.vocab, seed=heads)):
+        want = rs.step(tok)
+        if i % 13 == 0 or i > 640:
+            got = s.step(tok)
+            assert s.kernels_per_step == 4
+            worst = max(worst, float(np.abs(got - want).max()))
+        else:
+            s.step(tok, logits=False)
     assert worst <= LOGIT_TOL, worst
