@@ -314,35 +314,72 @@ __device__ __forceinline__ bool finish_tagged(const DPhase& P, const float* rd, 
     return ok;
 }
 
+// The fields of a matvec phase the consumers' inner loop needs, held in registers: the
+// descriptor lives in shared memory, and every barrier or mbarrier operation (a
+// "memory" clobber) would otherwise make the compiler load them again per item.
+struct MvCtx {
+    uint32_t ngroups, last_units, cap, rb1_, rb2_;
+    uint32_t type[kMaxSegs], rb0[kMaxSegs], dual[kMaxSegs], rows2[kMaxSegs];
+    const float* fscale;
+    const float* xsum;
+    const int* msum;
+};
+__device__ __forceinline__ MvCtx mv_ctx(const Plan& p, const uint8_t* xs, uint32_t cap) {
+    MvCtx c;
+    c.ngroups = p.ngroups;
+    c.last_units = p.last_units;
+    c.cap = cap;
+    c.rb1_ = p.rb_begin[1];
+    c.rb2_ = p.rb_begin[2];
+#pragma unroll
+    for (int s = 0; s < kMaxSegs; ++s) {
+        const MatvecSeg& sg = p.a.seg[s];
+        c.type[s] = sg.m.type;
+        c.rb0[s] = p.rb_begin[s];
+        c.dual[s] = sg.epi == EPI_SWIGLU;
+        c.rows2[s] = c.dual[s] ? sg.m2.rows : sg.m.rows;
+    }
+    c.fscale = reinterpret_cast<const float*>(xs + p.off_fscale);
+    c.xsum = reinterpret_cast<const float*>(xs + p.off_xsum);
+    c.msum = reinterpret_cast<const int*>(xs + p.off_msum);
+    return c;
+}
+__device__ __forceinline__ uint32_t ctx_seg(const MvCtx& c, uint32_t rb) { return rb >= c.rb2_ ? 2 : rb >= c.rb1_ ? 1 : 0; }
+// bytes of item (rb, g): the panel of one or two 16-row slabs (item_slabs of matvec_core.cuh)
+__device__ __forceinline__ uint32_t ctx_item_bytes(const MvCtx& c, uint32_t si, uint32_t rb, uint32_t g) {
+    const uint32_t local = rb - c.rb0[si], U = g + 1 == c.ngroups ? c.last_units : kPanelUnits;
+    const uint32_t sbk = c.dual[si] ? local : 2 * local + 1;
+    return (sbk * kSlabRows < c.rows2[si] ? 2u : 1u) * U * unit16_bytes(c.type[si]);
+}
+
 // One consumer warp's part of a row block of type T out of the byte ring (consume_rows
 // of matvec_core.cuh): for every panel, super-block `sbw` of slab `slab`. After an
 // abort the warp keeps walking (and releasing) the items without computing, so every
 // consumer warp reaches the same barriers.
 template <uint32_t T>
-__device__ __forceinline__ void rows_from_ring(const Plan& p, uint8_t* base, uint64_t* full, uint64_t* empty,
-                                               uint32_t cap, const uint8_t* xs, uint32_t& n, uint32_t& off,
+__device__ __forceinline__ void rows_from_ring(const MvCtx& c, uint32_t si, uint8_t* base, uint64_t* full,
+                                               uint64_t* empty, const uint8_t* xs, uint32_t& n, uint32_t& off,
                                                uint32_t rb, uint32_t slab, uint32_t sbw, const Lane& L, int lane,
                                                volatile int* abort_flag, float& acc0, float& acc1, bool& bad) {
     constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q6_K ? 840u : 1088u;
-    const float* fscale = reinterpret_cast<const float*>(xs + p.off_fscale);
     const float wt = ((L.t & 1) ? 65536.f : 1.f) * ((T == GGML_Q4_K && L.part) ? 0.0625f : 1.f);
-    for (uint32_t g = 0; g < p.ngroups; ++g, ++n) {
-        const uint32_t o = ring_place(off, item_bytes(p, rb, g), cap);
+    for (uint32_t g = 0; g < c.ngroups; ++g, ++n) {
+        const uint32_t o = ring_place(off, ctx_item_bytes(c, si, rb, g), c.cap);
         const uint32_t s = n % kSlots;
         if (!bad && !wait_or_abort(&full[s], (n / kSlots) & 1, abort_flag)) bad = true;
         if (!bad) {
-            const uint32_t U = g + 1 == p.ngroups ? p.last_units : kPanelUnits, ub = 4 * sbw;
+            const uint32_t U = g + 1 == c.ngroups ? c.last_units : kPanelUnits, ub = 4 * sbw;
             const uint8_t* q = base + o + slab * U * u16 + ub * u16;
             const uint32_t u0 = g * kPanelUnits + ub;
             if (ub < U) {
                 if constexpr (T == GGML_Q4_K) {
-                    sb_q4k(q, u0, xs, fscale, reinterpret_cast<const float*>(xs + p.off_xsum), L, lane, wt, acc0, acc1);
+                    sb_q4k(q, u0, xs, c.fscale, c.xsum, L, lane, wt, acc0, acc1);
                 } else if constexpr (T == GGML_Q6_K) {
-                    sb_q6k(q, u0, xs, fscale, reinterpret_cast<const int*>(xs + p.off_msum), L, lane, wt, acc0, acc1);
+                    sb_q6k(q, u0, xs, c.fscale, c.msum, L, lane, wt, acc0, acc1);
                 } else {
 #pragma unroll
                     for (uint32_t i = 0; i < 4; ++i)
-                        if (ub + i < U) unit_q8_0(q + i * 1088, u0 + i, xs, fscale, L, lane, wt, acc0, acc1);
+                        if (ub + i < U) unit_q8_0(q + i * 1088, u0 + i, xs, c.fscale, L, lane, wt, acc0, acc1);
                 }
             }
         }
@@ -358,6 +395,7 @@ __device__ bool consume_phase(const DPhase& P, uint8_t* base, uint64_t* full, ui
                               uint8_t* xs, uint32_t rb0, uint32_t rb1, uint32_t& n, uint32_t& off, int warp, int lane,
                               volatile int* abort_flag, float inv, uint32_t tb, const Waiter& wt) {
     const Plan& p = P.p;
+    const MvCtx c = mv_ctx(p, xs, cap);
     float* red = reinterpret_cast<float*>(xs + p.off_red);
     unsigned* cnt = reinterpret_cast<unsigned*>(xs + p.off_red + kRedBufs * kRedBufBytes);
     const Lane L = make_lane(lane);
@@ -365,20 +403,20 @@ __device__ bool consume_phase(const DPhase& P, uint8_t* base, uint64_t* full, ui
     const bool deferred = rb1 - rb0 <= kRedBufs;
     bool bad = false;
     for (uint32_t rb = rb0; rb < rb1; ++rb) {
-        const MatvecSeg& sg = p.a.seg[seg_of(p, rb)];
+        const uint32_t si = ctx_seg(c, rb);
         float acc0 = 0.f, acc1 = 0.f;
-        switch (sg.m.type) {
+        switch (c.type[si]) {
             case GGML_Q4_K:
-                rows_from_ring<GGML_Q4_K>(p, base, full, empty, cap, xs, n, off, rb, slab, sbw, L, lane, abort_flag,
-                                          acc0, acc1, bad);
+                rows_from_ring<GGML_Q4_K>(c, si, base, full, empty, xs, n, off, rb, slab, sbw, L, lane, abort_flag, acc0,
+                                          acc1, bad);
                 break;
             case GGML_Q6_K:
-                rows_from_ring<GGML_Q6_K>(p, base, full, empty, cap, xs, n, off, rb, slab, sbw, L, lane, abort_flag,
-                                          acc0, acc1, bad);
+                rows_from_ring<GGML_Q6_K>(c, si, base, full, empty, xs, n, off, rb, slab, sbw, L, lane, abort_flag, acc0,
+                                          acc1, bad);
                 break;
             default:
-                rows_from_ring<GGML_Q8_0>(p, base, full, empty, cap, xs, n, off, rb, slab, sbw, L, lane, abort_flag,
-                                          acc0, acc1, bad);
+                rows_from_ring<GGML_Q8_0>(c, si, base, full, empty, xs, n, off, rb, slab, sbw, L, lane, abort_flag, acc0,
+                                          acc1, bad);
         }
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -403,9 +441,10 @@ __device__ bool consume_phase(const DPhase& P, uint8_t* base, uint64_t* full, ui
     }
     if (deferred) {
         bad = consumers_sync_any(bad);
-        const uint32_t c = (uint32_t)(warp * 32 + lane);
-        if (!bad && c < (rb1 - rb0) * kRB)
-            if (!finish_tagged(P, red + (c / kRB) * (kSbWarps * kRB), rb0 + c / kRB, c % kRB, inv, tb, wt)) bad = true;
+        const uint32_t cth = (uint32_t)(warp * 32 + lane);
+        if (!bad && cth < (rb1 - rb0) * kRB)
+            if (!finish_tagged(P, red + (cth / kRB) * (kSbWarps * kRB), rb0 + cth / kRB, cth % kRB, inv, tb, wt))
+                bad = true;
     }
     return consumers_sync_any(bad);
 }
@@ -706,17 +745,48 @@ __device__ __noinline__ bool attn_item(const StepAttn& A, uint32_t kvh, uint32_t
     }
     if (consumers_sync_any(!ok)) return false;
     const uint32_t per = (G * HD + ns - 1) / ns, i0 = split * per, i1 = min((uint32_t)(G * HD), i0 + per);
-    for (uint32_t i = i0 + tid; i < i1; i += kCW * 32) {
-        const uint32_t g = i / HD, d = i % HD;
-        float O = 0.f;
-        for (uint32_t k = 0; k < ns && ok; ++k) {
-            float ok_v;
-            ok = ld_wait1(kpart + ((uint64_t)k * G + g) * (HD + 2) + d, tb + A.part_tag, ok_v, wt);
-            O += ok_v * S.fac2[k * G + g];
+    // warp w takes outputs i0 + 4w .. +3, then 64 further on, ...; lane k loads split k's
+    // partial of each (one round trip for all of them), and the warp adds them in a
+    // fixed butterfly order
+    for (uint32_t ib = i0 + 4 * (uint32_t)warp; ib < i1; ib += 4 * kCW) {
+        uint64_t w4[4];
+        uint32_t live = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = ib + j;
+            w4[j] = 0;
+            if (i < i1 && (uint32_t)lane < ns) {
+                w4[j] = ld_word(kpart + ((uint64_t)lane * G + i / HD) * (HD + 2) + i % HD);
+                live |= 1u << j;
+            }
         }
-        const float res = O / S.ml2[g];
-        for (uint32_t dd = 0; dd < A.out.ndst; ++dd)
-            st_word(A.out.dst[dd] + A.out.row0 + kvh * G * HD + i, res, tb + A.out.tag);
+        uint64_t t0w = 0;
+        for (;;) {
+            bool all = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) all &= !((live >> j) & 1) || tag_of(w4[j]) == tb + A.part_tag;
+            if (all) break;
+            if (give_up(wt, t0w)) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (((live >> j) & 1) && tag_of(w4[j]) != tb + A.part_tag)
+                    w4[j] = ld_word(kpart + ((uint64_t)lane * G + (ib + j) / HD) * (HD + 2) + (ib + j) % HD);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = ib + j;
+            if (i >= i1) break;  // uniform over the warp
+            const uint32_t g = i / HD;
+            const float O = warp_sum((live >> j) & 1 ? val_of(w4[j]) * S.fac2[lane * G + g] : 0.f);
+            if (lane == 0) {
+                const float res = O / S.ml2[g];
+                for (uint32_t dd = 0; dd < A.out.ndst; ++dd)
+                    st_word(A.out.dst[dd] + A.out.row0 + kvh * G * HD + i, res, tb + A.out.tag);
+            }
+        }
     }
     return !consumers_sync_any(!ok);
 }

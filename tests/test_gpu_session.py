@@ -249,6 +249,7 @@ def test_cluster_attention_streamed_pages(monkeypatch, ring, mma):
     spec = synth.tiny(seed=23, layers=2)
     img, m, r = _models(spec)
     toks = _tokens(150, spec.vocab, seed=9)
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "0")  # the launch sequence's attention kernels
     monkeypatch.setenv("EVELYN_ATTN_RING", str(ring))
     monkeypatch.setenv("EVELYN_ATTN_MMA", mma)
     s1 = evl.Session(m, max_ctx=256)

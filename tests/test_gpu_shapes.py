@@ -4,11 +4,13 @@ the CPU oracle):
 * the Qwen3-0.6B-shape (28 layers, all Q8_0) and Qwen3-8B-shape (36 layers, Q4_K_M
   mix) synthetic models: a 16-token random prompt fed to both, teacher-forced
   perplexity over it, then 64 greedy steps from each side's own argmax -- logits
-  within max-abs 2e-3 at every step, identical greedy tokens, PPL within 0.5 %
-  (the protocol of src/bin/evelyn-generate.rs:69-86);
+  within max-abs 2e-3 at every step (f32 KV, the reference's precision; f16 KV pages
+  within 2e-2), identical greedy tokens, PPL within 0.5 % (the protocol of
+  src/bin/evelyn-generate.rs:69-86);
 * head_dim 128 sessions with GQA groups 2, 4 and 8 run past 1200 positions, so the
   single-sequence cluster attention streams its 8 splits through the page ring at the
-  benchmark's head size (with the default ring and with a 2-page ring);
+  benchmark's head size (with the default ring and with a 2-page ring), and the
+  persistent step kernel's attention phase runs its splits over many chunks;
 * the matvec paths only the big shapes reach: the LM-head shape 151936x4096 Q8_0
   (more row blocks per CTA than partial buffers: rotating buffers, last-warp
   reduction) and 5120x25600 Q6_K (rows longer than 12288 values: quarter staging).
@@ -38,11 +40,11 @@ def _top2_margin(logits):
     return float(top[1] - top[0])
 
 
-def _generate_protocol(spec, prompt_len=16, steps=64, seed=0):
+def _generate_protocol(spec, prompt_len=16, steps=64, seed=0, kv_f32=True):
     """Prompt (teacher-forced PPL) then greedy decode on both sides; returns the worst
     logit difference, both PPLs and both token streams."""
     img = synth.build(spec)
-    m = evl.Model.load_memory(img, device=0)
+    m = evl.Model.load_memory(img, device=0, kv_f32=kv_f32)
     r = orc.Model(img)
     s = evl.Session(m, max_ctx=prompt_len + steps + 8)
     rs = orc.Session(r)
@@ -68,21 +70,32 @@ def _generate_protocol(spec, prompt_len=16, steps=64, seed=0):
     return worst, ppl_g, ppl_o, out_g, out_o, min(margins)
 
 
+# f16 KV pages round every cached K and V element to 11 bits, which the f32 reference
+# (src/runtime.rs:721-722 keeps f32 rows) does not: at the 8B shape that moves logits by
+# about 1e-2 (measured 0.011 worst over 28 steps) while the greedy tokens stay the same.
+# The strict bar applies to the reference's own KV precision.
+F16_KV_LOGIT_TOL = 2e-2
+
+
 @pytest.mark.slow
+@pytest.mark.parametrize("kv_f32", [True, False], ids=["kv_f32", "kv_f16"])
 @pytest.mark.parametrize("shape", ["qwen3_0_6b", "qwen3_8b"])
-def test_benchmark_shape_generate_matches_oracle(shape):
+def test_benchmark_shape_generate_matches_oracle(shape, kv_f32):
     spec = getattr(synth, shape)(seed=0)
-    worst, ppl_g, ppl_o, out_g, out_o, margin = _generate_protocol(spec)
-    assert worst <= LOGIT_TOL, worst
+    worst, ppl_g, ppl_o, out_g, out_o, margin = _generate_protocol(spec, kv_f32=kv_f32)
+    assert worst <= (LOGIT_TOL if kv_f32 else F16_KV_LOGIT_TOL), worst
     assert abs(ppl_g / ppl_o - 1) < 0.005, (ppl_g, ppl_o)
     assert out_g == out_o, (out_g, out_o, margin)
 
 
 @pytest.mark.parametrize("heads,kv_heads", [(4, 2), (8, 2), (8, 1)])
-@pytest.mark.parametrize("ring", [None, "2"])
-def test_hd128_cluster_attention_long_context(heads, kv_heads, ring, monkeypatch):
+@pytest.mark.parametrize("path,ring", [("cluster", None), ("cluster", "2"), ("step", None)])
+def test_hd128_attention_long_context(heads, kv_heads, path, ring, monkeypatch):
     """GQA group 2 / 4 / 8 at head_dim 128 (the 0.6B, 8B and 32B groups) past 1200
-    positions: every 25th step's logits against the oracle, and greedy agreement."""
+    positions, through the launch sequence's cluster attention (default ring and a
+    2-page ring) and through the persistent step kernel: every 25th step's logits
+    against the oracle, and greedy agreement."""
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "1" if path == "step" else "0")
     if ring:
         monkeypatch.setenv("EVELYN_ATTN_RING", ring)
     spec = synth.tiny(seed=31 + heads + kv_heads, head_dim=128, heads=heads, kv_heads=kv_heads, layers=2)
