@@ -249,7 +249,6 @@ def test_cluster_attention_streamed_pages(monkeypatch, ring, mma):
     spec = synth.tiny(seed=23, layers=2)
     img, m, r = _models(spec)
     toks = _tokens(150, spec.vocab, seed=9)
-    monkeypatch.setenv("EVELYN_STEP_KERNEL", "0")  # the launch sequence's attention kernels
     monkeypatch.setenv("EVELYN_ATTN_RING", str(ring))
     monkeypatch.setenv("EVELYN_ATTN_MMA", mma)
     s1 = evl.Session(m, max_ctx=256)
@@ -274,7 +273,7 @@ def test_step_kernel_matches_launch_sequence(monkeypatch):
     spec = synth.tiny(seed=21, layers=3)
     img, m, r = _models(spec)
     toks = _tokens(150, spec.vocab, seed=4)
-    monkeypatch.delenv("EVELYN_STEP_KERNEL", raising=False)
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "1")
     s1 = evl.Session(m, max_ctx=256)
     out1 = [s1.step(t) for t in toks]
     monkeypatch.setenv("EVELYN_STEP_KERNEL", "0")
@@ -294,7 +293,7 @@ def test_step_kernel_matches_launch_sequence(monkeypatch):
 def test_step_kernel_groups_and_kv_types(heads, kv_heads, kv_f32, monkeypatch):
     """The persistent step kernel at GQA groups 2, 8, 1, 4 (head_dim 128) with f16 and
     f32 KV pages, past several attention chunks per split, against the oracle."""
-    monkeypatch.delenv("EVELYN_STEP_KERNEL", raising=False)
+    monkeypatch.setenv("EVELYN_STEP_KERNEL", "1")
     spec = synth.tiny(seed=40 + heads + kv_heads, head_dim=128, heads=heads, kv_heads=kv_heads, layers=2)
     img, m, r = _models(spec, kv_f32=kv_f32)
     s, rs = evl.Session(m, max_ctx=700), orc.Session(r)
