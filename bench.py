@@ -7,14 +7,18 @@ random prompt then greedy decode (ctx up to 512 + warmup + steps).
 One step = one decode token through every layer (embedding, 36 x {RMSNorm+QKV,
 QK-norm+RoPE+KV append, paged GQA attention, o-proj+residual, RMSNorm+gate/up+SwiGLU,
 down+residual}, final norm, LM head, argmax). With N > 1 (torchrun) the model is
-tensor-parallel over N GPUs (Megatron split, NCCL all-reduce after o-proj and down).
+tensor-parallel over N GPUs (Megatron split; the o-proj and down partial sums and the
+greedy pick over the vocabulary shards go through peer-memory inboxes over NVLink).
 
 Printed JSON (rank 0): value = tok/s timed on the device with CUDA events on the
-session stream, weights and KV resident in HBM, inputs larger than L2 (5 GB of
-weights per step); e2e = the same through evl_session_step with host buffers
-(token H2D, logits D2H and the host argmax every step, same context range); roofline = the dominant kernel
-(Q4_K dequant-matvec of the ffn_gate shape 12288x4096) timed live; cpu_baseline =
-the CPU oracle (a restatement of the reference's runtime) on a bounded sample.
+session stream, weights and KV (f32 pages, the reference's precision) resident in HBM,
+inputs larger than L2 (5 GB of weights per step); e2e = the same through
+evl_session_step with host buffers (token H2D, logits D2H and the host argmax every
+step, same context range); roofline = the dominant kernel (Q4_K dequant-matvec of the
+ffn_gate shape 12288x4096) timed live; cpu_baseline = the CPU oracle (a restatement of
+the reference's runtime) on a bounded sample. Extra keys: bs32 (32 sequences, 2048-token
+prefix each, f16 KV pages, at every N), c1 (Qwen3-0.6B shape, all Q8_0, bs1, N = 1),
+c4 (the isolated kernel sweep, N = 1).
 """
 from __future__ import annotations
 
@@ -221,6 +225,64 @@ def kernel_roofline(evl_rt, stream, hbm_peak, peak_kind, reps=8):
             "bytes_per_launch": alg}
 
 
+def measure_bs1(evl, model, spec, prompt_len, K, W, world):
+    """One sequence: `prompt_len` prompt tokens fed step by step, W warm-up steps, then
+    K timed device-resident greedy steps (device time on the session stream, max over
+    ranks); then the same context range end to end through evl_session_step (token H2D,
+    logits D2H and the host argmax every step)."""
+    import torch
+    max_ctx = prompt_len + 2 * (W + K) + 16
+    prompt = np.random.default_rng(0).integers(0, spec.vocab, prompt_len)
+    sess = evl.Session(model, max_ctx=max_ctx)
+    for t in prompt[:-1]:
+        sess.step(int(t), logits=False)
+    toks = sess.generate(int(prompt[-1]), W)
+    ext = torch.cuda.ExternalStream(sess.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    ctx0 = sess.pos
+    e0.record(ext)
+    torch.cuda.nvtx.range_push("decode_steps")
+    sess.generate(toks[-1], K)
+    torch.cuda.nvtx.range_pop()
+    e1.record(ext)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    ms = dist_max(e0.elapsed_time(e1), world)
+    kernels = sess.kernels_per_step
+    del sess
+    sess = evl.Session(model, max_ctx=max_ctx)
+    for t in prompt[:-1]:
+        sess.step(int(t), logits=False)
+    tok = int(prompt[-1])
+    for _ in range(W):
+        tok = evl.argmax(sess.step(tok))
+    ext = torch.cuda.ExternalStream(sess.stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(ext)
+    for _ in range(K):
+        tok = evl.argmax(sess.step(tok))
+    f1.record(ext)
+    f1.synchronize()
+    e2e_ms = dist_max(f0.elapsed_time(f1), world)
+    del sess
+    return {"ms": ms, "e2e_ms": e2e_ms, "ctx0": ctx0, "kernels": kernels}
+
+
+def step_hbm(spec, kv_elem, ctx0, K, hbm, peak_kind, ms, batch=1, world=1):
+    """Weight bytes (every matrix once) + KV bytes read over the timed context range,
+    per step, against the measured copy bandwidth; with tensor parallelism the bytes
+    are spread over `world` GPUs (reported per GPU)."""
+    kv_pos = spec.kv_bytes_per_position(kv_elem)
+    step_bytes = spec.weight_bytes_per_token() + batch * kv_pos * (ctx0 + (K + 1) / 2)
+    gbs = step_bytes * K / (ms / 1e3) / 1e9 / world
+    return {"bytes_per_step": int(step_bytes), "achieved_gbs_per_gpu": round(gbs, 1), "frac": round(gbs / hbm, 4),
+            "peak": hbm, "peak_source": peak_kind}
+
+
 def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     import torch
@@ -232,107 +294,89 @@ def run_ours(args):
     t0 = time.perf_counter()
     img = synth.build(spec)
     log(f"[rank {rank}] synthetic GGUF {img.nbytes / 1e9:.2f} GB in {time.perf_counter() - t0:.1f}s")
-    nccl_id = None
-    if world > 1:
-        import torch.distributed as dist
-        obj = [evl.tp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    t0 = time.perf_counter()
-    model = evl.Model.load_memory(img, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
-    log(f"[rank {rank}] loaded in {time.perf_counter() - t0:.1f}s; {model.weight_bytes / 1e9:.3f} GB/step on this rank")
+
+    def load(image, kv_f32):
+        nccl_id = None
+        if world > 1:
+            import torch.distributed as dist
+            obj = [evl.tp_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            nccl_id = obj[0]
+        t = time.perf_counter()
+        m = evl.Model.load_memory(image, device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, kv_f32=kv_f32)
+        log(f"[rank {rank}] loaded in {time.perf_counter() - t:.1f}s; {m.weight_bytes / 1e9:.3f} GB/step on this rank")
+        return m
+
     K, W = args.steps, args.warmup
-    max_ctx = PROMPT + 2 * (W + K) + 16
-    sess = evl.Session(model, max_ctx=max_ctx)
-    prompt = np.random.default_rng(0).integers(0, spec.vocab, PROMPT)
-    for t in prompt[:-1]:
-        sess.step(int(t), logits=False)
-    last = int(prompt[-1])
-    # warm-up, then K timed device-resident steps (greedy loop stays on the GPU)
-    # clocks are sampled from the warm-up on (the timed region alone can be shorter than
-    # one sampling period) through the end-to-end loop below
-    clk = ClockSampler(local).__enter__()
-    toks = sess.generate(last, W)
-    stream = sess.stream
-    ext = torch.cuda.ExternalStream(stream)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    ctx0 = sess.pos
-    e0.record(ext)
-    torch.cuda.nvtx.range_push("decode_steps")
-    toks = sess.generate(toks[-1], K)
-    torch.cuda.nvtx.range_pop()
-    e1.record(ext)
-    e1.synchronize()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    ms_max = dist_max(ms, world)
-    launches = sess.kernels_per_step * K
-    # end to end through evl_session_step: token H2D, logits D2H and the host argmax
-    # every step, on a fresh session over the same context range as the timed loop
-    del sess
-    sess = evl.Session(model, max_ctx=max_ctx)
-    for t in prompt[:-1]:
-        sess.step(int(t), logits=False)
-    tok = last
-    for _ in range(W):
-        tok = evl.argmax(sess.step(tok))
-    stream = sess.stream
-    ext = torch.cuda.ExternalStream(stream)
-    barrier(world)
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(ext)
-    for _ in range(K):
-        lg = sess.step(tok)
-        tok = evl.argmax(lg)
-    f1.record(ext)
-    f1.synchronize()
-    clk.__exit__(None, None, None)
-    e2e_ms = dist_max(f0.elapsed_time(f1), world)
     hbm, peak_kind = peaks()
-    roof = kernel_roofline(runtime, stream, hbm, peak_kind) if rank == 0 else None
-    kv_pos = spec.kv_bytes_per_position(2)
-    mean_ctx = ctx0 + (K + 1) / 2
-    step_bytes = spec.weight_bytes_per_token() + kv_pos * mean_ctx + kv_pos / 1
-    tok_s = K / (ms_max / 1e3)
+    # clocks are sampled from the first warm-up on (one timed region alone can be
+    # shorter than a sampling period) through every timed loop below
+    clk = ClockSampler(local).__enter__()
+    # bs1 keeps the KV cache in f32 pages, the reference's precision (src/runtime.rs:
+    # 721-722), at which the logits are parity-tested against the oracle
+    model = load(img, kv_f32=True)
+    r1 = measure_bs1(evl, model, spec, PROMPT, K, W, world)
+    roof = None
+    if rank == 0:  # on a stream of its own (a session would be a collective under TP)
+        roof = kernel_roofline(runtime, torch.cuda.Stream().cuda_stream, hbm, peak_kind)
+    del model
     base = cpu_baseline(img) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
-    del sess
-    bs32 = run_batch(model, spec, args, hbm, peak_kind) if (world == 1 and args.batch > 1) else None
+    bs32 = None
+    if args.batch > 1:  # the batched config: f16 KV pages, as the config names them
+        model = load(img, kv_f32=False)
+        bs32 = run_batch(model, spec, args, hbm, peak_kind, world)
+        del model
+    c1 = None
+    if world == 1 and not args.no_c1:  # Qwen3-0.6B shape, all Q8_0, bs1, 128 + 128
+        spec1 = synth.qwen3_0_6b(seed=0)
+        img1 = synth.build(spec1)
+        m1 = evl.Model.load_memory(img1, device=local, kv_f32=True)
+        r = measure_bs1(evl, m1, spec1, 128, 128, W, world)
+        c1 = {"value": round(128 / (r["ms"] / 1e3), 2), "unit": "tok/s", "ms_per_step": round(r["ms"] / 128, 4),
+              "e2e": {"value": round(128 / (r["e2e_ms"] / 1e3), 2), "unit": "tok/s"},
+              "workload": f"Qwen3-0.6B-shape all-Q8_0 decode bs1, 128-token prompt then 128 greedy steps "
+                          f"(ctx {r['ctx0']}..{r['ctx0'] + 128}), f32 KV pages",
+              "step_hbm": step_hbm(spec1, 4, r["ctx0"], 128, hbm, peak_kind, r["ms"])}
+        del m1
+    c4 = run_c4_summary(args, hbm, peak_kind) if (rank == 0 and world == 1 and not args.no_c4) else None
+    clk.__exit__(None, None, None)
+    tok_s = K / (r1["ms"] / 1e3)
     if rank == 0:
-        clocks = clk.summary()
         line = {
             "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(ms_max / K, 4), "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q4_k/q6_k/q8_0 weights, f32 math",
+            "ms_per_step": round(r1["ms"] / K, 4), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "q4_k/q6_k/q8_0 weights, f32 math",
             "data": "synthetic: seeded N(0,0.02) weights quantised to a Q4_K_M-style mix, uniform-random prompt ids",
             "config": {"workload": f"Qwen3-8B-shape decode bs1, {PROMPT}-token prompt then greedy decode "
-                                   f"(ctx {ctx0}..{ctx0 + K})", "model": "qwen3-8b-shape (36L, d4096, 32Q/8KV x128,"
-                       " ffn 12288, vocab 151936)", "global_batch": 1, "seq_len": ctx0 + K,
+                                   f"(ctx {r1['ctx0']}..{r1['ctx0'] + K})", "model": "qwen3-8b-shape (36L, d4096, "
+                       "32Q/8KV x128, ffn 12288, vocab 151936)", "global_batch": 1, "seq_len": r1["ctx0"] + K,
                        "parallelism": f"tp{world}" if world > 1 else "single GPU",
-                       "kv_cache": "paged f16, 16-token pages", "l2": "inputs larger than L2 (5.08 GB weights/step)"},
-            "step_hbm": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes * K / (ms_max / 1e3) / 1e9, 1),
-                         "frac": round(step_bytes * K / (ms_max / 1e3) / 1e9 / hbm, 4), "peak": hbm,
-                         "peak_source": peak_kind},
-            "e2e": {"value": round(K / (e2e_ms / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                       "kv_cache": "paged f32 (the reference's precision), 16-token pages",
+                       "l2": "inputs larger than L2 (5.08 GB weights/step)"},
+            "step_hbm": step_hbm(spec, 4, r1["ctx0"], K, hbm, peak_kind, r1["ms"], world=world),
+            "e2e": {"value": round(K / (r1["e2e_ms"] / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": spec.vocab * 4 + 4 + 4},
             "roofline": roof,
-            "gpu_launches": launches,
-            "clocks": clocks,
+            "gpu_launches": r1["kernels"] * K,
+            "kernels_per_step": r1["kernels"],
+            "clocks": clk.summary(),
         }
         if base:
             line["cpu_baseline"] = base
         if bs32:
             line["bs32"] = bs32
+        if c1:
+            line["c1"] = c1
+        if c4:
+            line["c4"] = c4
         print(json.dumps(line), flush=True)
-    del model
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def run_batch(model, spec, args, hbm, peak_kind):
+def run_batch(model, spec, args, hbm, peak_kind, world=1):
     """The batched half of the metric: `args.batch` sequences decoded together after a
     `args.batch_prefix`-token prefix each (prefilled by batch steps); K timed steps through
     evl_batch_step (tokens H2D, argmax D2H, synchronised each step)."""
@@ -341,12 +385,14 @@ def run_batch(model, spec, args, hbm, peak_kind):
     B, P, K = args.batch, args.batch_prefix, args.batch_steps
     batch = evl_rt.Batch(model, B, max_ctx=P + K + 8)
     rng = np.random.default_rng(1)
+    barrier(world)
     for _ in range(P):
         batch.step(rng.integers(0, spec.vocab, B), logits=False)
     toks = rng.integers(0, spec.vocab, B)
     for _ in range(3):  # warm-up
         toks = batch.step(toks, logits=False)
     ext = torch.cuda.ExternalStream(batch.stream)
+    barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(ext)
@@ -356,18 +402,15 @@ def run_batch(model, spec, args, hbm, peak_kind):
     torch.cuda.nvtx.range_pop()
     e1.record(ext)
     e1.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = dist_max(e0.elapsed_time(e1), world)
     ctx0 = P + 3
-    kv_pos = spec.kv_bytes_per_position(2)
-    step_bytes = spec.weight_bytes_per_token() + B * kv_pos * (ctx0 + (K + 1) / 2)
-    gbs = step_bytes * K / (ms / 1e3) / 1e9
     del batch
     return {"value": round(B * K / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / K, 4),
             "global_batch": B, "workload": f"{B} sequences, {P}-token prefix each, then {K} greedy steps "
                                            f"(ctx {ctx0}..{ctx0 + K}); products on tcgen05 tensor cores",
             "e2e_note": "each step through evl_batch_step: token ids H2D, argmax D2H, synchronised",
-            "step_hbm": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
-                         "frac": round(gbs / hbm, 4), "peak": hbm, "peak_source": peak_kind}}
+            "parallelism": f"tp{world}" if world > 1 else "single GPU", "kv_cache": "paged f16, 16-token pages",
+            "step_hbm": step_hbm(spec, 2, ctx0, K, hbm, peak_kind, ms, batch=B, world=world)}
 
 
 def _random_raw(ggml_type: int, rows: int, cols: int, rng) -> np.ndarray:
@@ -387,10 +430,13 @@ def _random_raw(ggml_type: int, rows: int, cols: int, rng) -> np.ndarray:
     return raw.reshape(-1)
 
 
-def run_sweep(args):
+def run_sweep(args, emit=None):
     """Isolated kernel sweep: dequant-matvec for 4096x4096, 4096x12288, 12288x4096, 151936x4096
     in Q4_K/Q6_K/Q8_0, and GQA decode attention 32Q/8KV hd128 at KV length 512..32768.
-    Each case cycles enough distinct copies to exceed L2 twice; CUDA events on one stream."""
+    Each case cycles enough distinct copies to exceed L2 twice; CUDA events on one stream.
+    Every case's result goes to `emit` (default: one JSON line on stdout)."""
+    if emit is None:
+        emit = lambda d: print(json.dumps(d), flush=True)  # noqa: E731
     import torch
     from evelyn_b200 import runtime, synth
     lib = runtime.lib()
@@ -434,9 +480,9 @@ def run_sweep(args):
             us = e0.elapsed_time(e1) * 1e3 / (reps * len(mats))
             alg = nbytes + 4 * (rows + cols)
             gbs = alg / (us * 1e-6) / 1e9
-            print(json.dumps({"kernel": "qmatvec", "case": name, "bytes": alg, "us": round(us, 2),
+            emit({"kernel": "qmatvec", "case": name, "bytes": alg, "us": round(us, 2),
                               "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
-                              "peak_source": peak_kind}), flush=True)
+                              "peak_source": peak_kind})
             for h in mats:
                 lib.evl_qmatrix_free(h)
             del mats
@@ -473,10 +519,10 @@ def run_sweep(args):
             e1.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (reps * len(mats))
             flops = 2.0 * rows * cols * nvec
-            print(json.dumps({"kernel": "qgemm (stage + gemm + reduce, synchronised call)", "case": name,
+            emit({"kernel": "qgemm (stage + gemm + reduce, synchronised call)", "case": name,
                               "bytes": raw.size + 4 * nvec * (rows + cols), "us": round(us, 2),
                               "tflops": round(flops / (us * 1e-6) / 1e12, 2),
-                              "gbs": round(raw.size / (us * 1e-6) / 1e9, 1)}), flush=True)
+                              "gbs": round(raw.size / (us * 1e-6) / 1e9, 1)})
             for h in mats:
                 lib.evl_qmatrix_free(h)
             del mats
@@ -518,11 +564,27 @@ def run_sweep(args):
             us = e0.elapsed_time(e1) * 1e3 / (reps * len(kvs))
             alg = kv_bytes + 2 * heads * hd * 4
             gbs = alg / (us * 1e-6) / 1e9
-            print(json.dumps({"kernel": "attention", "case": name, "bytes": alg, "us": round(us, 2),
+            emit({"kernel": "attention", "case": name, "bytes": alg, "us": round(us, 2),
                               "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
-                              "peak_source": peak_kind}), flush=True)
+                              "peak_source": peak_kind})
             del kvs
         L *= 2
+
+
+def run_c4_summary(args, hbm, peak_kind):
+    """The kernel sweep (every matvec shape x type and the decode attention at KV 512 ..
+    32768, 3 timed passes each) as one summary for the bench line."""
+    import argparse as _ap
+    a = _ap.Namespace(sweep_only="", reps=3)
+    res = []
+    run_sweep(a, emit=res.append)
+    out = {"workload": "isolated kernels: dequant-matvec 4096x4096, 4096x12288, 12288x4096, 151936x4096 in "
+                       "Q4_K/Q6_K/Q8_0 (x f32), GQA decode attention 32Q/8KV hd128 over f16 pages at KV "
+                       "512..32768; each case cycles distinct copies larger than L2",
+           "peak": hbm, "peak_source": peak_kind}
+    for d in res:
+        out[f"{d['kernel']}:{d['case']}"] = {"us": d["us"], "gbs": d["gbs"], "frac": d.get("frac")}
+    return out
 
 
 def run_reference(args):
@@ -578,6 +640,8 @@ def main():
     ap.add_argument("--batch-prefix", type=int, default=2048, help="prefix tokens per sequence before timing")
     ap.add_argument("--batch-steps", type=int, default=64, help="timed batched steps")
     ap.add_argument("--reps", type=int, default=10, help="timed passes per sweep case")
+    ap.add_argument("--no-c1", action="store_true", help="skip the Qwen3-0.6B-shape bs1 line")
+    ap.add_argument("--no-c4", action="store_true", help="skip the kernel-sweep summary")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -165,6 +165,25 @@ float evl_log_prob(const float* logits, size_t n, uint32_t target) {
     return logits[target] - (mx + std::log(sum));
 }
 
+evl_status evl_tp_shard_plan(const evl_config* cfg, int32_t tp_size, int32_t rank, evl_tp_shard* out) {
+    return guarded([&] {
+        require(cfg && out, "null argument");
+        Config c;
+        c.heads = cfg->heads;
+        c.kv_heads = cfg->kv_heads;
+        c.head_dim = cfg->head_dim;
+        c.ffn = cfg->ffn;
+        c.vocab = cfg->vocab;
+        const TpShard s = tp_shard_plan(c, tp_size, rank);
+        for (int i = 0; i < 2; ++i) {
+            out->q_rows[i] = s.q[i];
+            out->kv_rows[i] = s.kv[i];
+            out->ffn_rows[i] = s.ffn[i];
+            out->vocab_rows[i] = s.vocab[i];
+        }
+    });
+}
+
 evl_status evl_tp_unique_id(uint8_t out[128]) {
     return guarded([&] {
         require(out, "null output");

@@ -170,11 +170,6 @@ __device__ __forceinline__ uint32_t ring_place(uint32_t& off, uint32_t bytes, ui
     off += sz;
     return o;
 }
-__device__ __forceinline__ uint32_t item_bytes(const Plan& p, uint32_t rb, uint32_t g) {
-    const uint8_t *a, *b;
-    uint32_t sb;
-    return item_slabs(p, rb, g, a, b, sb) * sb;
-}
 
 // ---------------------------------------------------------------- matvec phases
 // NE 8-value eighths of a tagged input, c, c + 512, ... (those below cols / 8), staged by

@@ -72,6 +72,7 @@ struct Nccl {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -194,6 +195,15 @@ struct Model {
 
 std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_model_options& opts);
 
+// The tensor-parallel shard of rank R of T: [first, last) rows of attn_q (and columns
+// of attn_output), attn_k / attn_v, ffn_gate / ffn_up (columns of ffn_down, on
+// 256-value super-block boundaries, uneven when the block count does not divide) and
+// the LM head. Raises InvalidInput / Unsupported like load_model.
+struct TpShard {
+    uint64_t q[2], kv[2], ffn[2], vocab[2];
+};
+TpShard tp_shard_plan(const Config& c, int T, int R);
+
 void allreduce_sum(Model& m, float* buf, size_t n, cudaStream_t s);
 
 // Makes the GEMM-layout copies (QMatrix::gemm) of the layer matrices and the LM head;
@@ -214,8 +224,11 @@ inline uint32_t prefetch_kb(uint32_t dflt) {
 // null) writing y; add=true accumulates into y (residual). TP: partial + all-reduce.
 // `next` (may be null) holds the three matrices the launch after the FFN reads
 // (unused entries have q == null), warmed into L2.
+// peers (tensor parallelism inside a step) sums the down-proj partials through the
+// ranks' peer-memory inboxes at tag slot `slot`; null uses an NCCL all-reduce.
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
-                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl);
+                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl,
+                   const TpPeers* peers = nullptr, uint32_t slot = 0);
 
 // ------------------------------------------------------------------ decode attention on caller buffers
 // Shared by the evl_attention_decode* entry points (abi.cpp, attention_noalloc.cu):
@@ -248,6 +261,12 @@ struct StepBuffers {
     // persistent step kernel (decode_step.cu): its tagged vectors (x, q, k, v, attention
     // partials, attention output, h) and the step counter their tags derive from
     DeviceBuffer tagpool, epoch;
+    // tensor parallelism: this rank's inbox for the step's exchanges (tp_comm.cu), the
+    // peers' inboxes and logits buffers mapped into this process
+    DeviceBuffer tpinbox;
+    TpPeers tp;
+    const float* peer_logits[kMaxPeers] = {};
+    std::vector<void*> ipc_open;
     uint64_t *xt = nullptr, *qt = nullptr, *kt = nullptr, *vt = nullptr, *partt = nullptr, *attt = nullptr,
              *ht = nullptr;
     uint32_t tag_period = 0;
@@ -268,6 +287,7 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
 
     ~Decoder();
     void init(Model* m, uint32_t batch, uint32_t max_ctx);
+    void init_tp();  // collective over the model's ranks: inboxes, peer mappings
     MatvecArgs qkv_args(uint32_t layer) const;
     RopeArgs rope_args(uint32_t layer) const;
     AttnArgs attn_args(uint32_t layer, uint32_t nsplit) const;
@@ -284,6 +304,7 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     void enqueue_dense(bool pdl);
     void enqueue_layer_attention(uint32_t layer, bool pdl);
     void enqueue_head(bool pdl);
+    void gather_peer_logits();
     // A step with a routed-FFN hook (eager, synchronising at routed layers).
     void run_routed(const evl_ffn_backend& ffn);
     void launch_graph();

@@ -177,6 +177,29 @@ uint32_t step_attn_splits(uint32_t kv_heads, uint32_t max_pages, int sms);
 cudaError_t launch_embed_tagged(const QMatDev& embed, const int32_t* tokens, uint64_t* xt, const uint32_t* epoch,
                                 uint32_t period, int32_t* err, cudaStream_t s);
 
+// ---------------------------------------------------------------- tp_comm.cu
+// Tensor-parallel exchanges of a step through inboxes in peer memory (tp_comm.cu).
+// inbox[r] is rank r's inbox as mapped into this process: [purpose][sender][cap] tagged
+// words. Tags are epoch * period + 1 + slot, as in decode_step.cu.
+enum TpPurpose : uint32_t { TP_O = 0, TP_DOWN = 1, TP_PICK = 2, TP_PURPOSES = 3 };
+struct TpPeers {
+    uint64_t* inbox[kMaxPeers] = {};
+    uint32_t rank = 0, size = 1;
+    uint32_t cap = 0;  // words per (purpose, sender)
+    const uint32_t* epoch = nullptr;
+    uint32_t period = 0;  // tag slots per step
+};
+// x[i] += (sum over ranks in rank order of each rank's part[i]) for i < n.
+cudaError_t launch_tp_allreduce_add(const TpPeers& P, uint32_t purpose, uint32_t slot, float* x, const float* part,
+                                    uint32_t n, int* err, cudaStream_t s, bool pdl);
+// Greedy pick (src/runtime.rs:897-905) over the ranks' vocabulary shards: this rank's
+// shard is logits[b * stride + v0 + i], i < n; ends the step like launch_argmax and
+// advances epoch.
+cudaError_t launch_tp_argmax(const TpPeers& P, uint32_t slot, const float* logits, uint32_t stride, uint32_t v0,
+                             uint32_t n, uint32_t batch, float* part_v, int32_t* part_i, uint32_t parts, int32_t* out,
+                             int32_t* next_tokens, int32_t* pos, int32_t* hist, uint32_t hist_stride, uint32_t* epoch,
+                             int* err, cudaStream_t s, bool pdl);
+
 // ---------------------------------------------------------------- qgemm.cu
 // A matrix in the GEMM layout (per 128-row M tile and 256-value K chunk, one block of
 // the original quant bytes split by field), made on the device from the matvec layout.

@@ -50,6 +50,31 @@ void split_range(uint64_t n, int p, int i, uint64_t* lo, uint64_t* hi) {
 
 }  // namespace
 
+TpShard tp_shard_plan(const Config& c, int T, int R) {
+    if (T < 1 || R < 0 || R >= T) raise(EVL_ERR_INVALID_INPUT, "tp_rank outside [0, tp_size)");
+    if (c.kv_heads == 0 || c.kv_heads % T) raise(EVL_ERR_INVALID_INPUT, "tp_size must divide head_count_kv");
+    TpShard s;
+    const uint64_t hd = c.head_dim, lh = c.heads / T, lkv = c.kv_heads / T;
+    s.q[0] = (uint64_t)R * lh * hd;
+    s.q[1] = s.q[0] + lh * hd;
+    s.kv[0] = (uint64_t)R * lkv * hd;
+    s.kv[1] = s.kv[0] + lkv * hd;
+    // the FFN is split on 256-value boundaries so ffn_down shards stay block aligned
+    s.ffn[0] = 0;
+    s.ffn[1] = c.ffn;
+    if (T > 1) {
+        if (c.ffn % 256) raise(EVL_ERR_UNSUPPORTED, "tensor parallelism needs feed_forward_length % 256 == 0");
+        uint64_t b0, b1;
+        split_range(c.ffn / 256, T, R, &b0, &b1);
+        s.ffn[0] = b0 * 256;
+        s.ffn[1] = b1 * 256;
+    }
+    s.vocab[0] = 0;
+    s.vocab[1] = c.vocab;
+    if (T > 1) split_range(c.vocab, T, R, &s.vocab[0], &s.vocab[1]);
+    return s;
+}
+
 Model::~Model() {
     if (comm) nccl().CommDestroy(comm);
     if (stream) cudaStreamDestroy(stream);
@@ -133,7 +158,7 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         raise(EVL_ERR_UNSUPPORTED,
               "GQA group size " + std::to_string(group) + " (device attention handles 1, 2, 4, 8)");
     const int T = m.tp_size, R = m.tp_rank;
-    if (c.kv_heads % T) raise(EVL_ERR_INVALID_INPUT, "tp_size must divide head_count_kv");
+    const TpShard sh = tp_shard_plan(c, T, R);
     m.lkv_heads = (uint32_t)(c.kv_heads / T);
     m.lheads = (uint32_t)(c.heads / T);
     const uint64_t hd = c.head_dim, qw = c.heads * hd, kw = c.kv_heads * hd;
@@ -180,25 +205,14 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         m.matrices[name] = &q;
     };
 
-    // the FFN is split on 256-value boundaries so ffn_down shards stay block aligned
-    uint64_t f0 = 0, f1 = c.ffn;
-    if (T > 1) {
-        if (c.ffn % 256) raise(EVL_ERR_UNSUPPORTED, "tensor parallelism needs feed_forward_length % 256 == 0");
-        uint64_t b0, b1;
-        split_range(c.ffn / 256, T, R, &b0, &b1);
-        f0 = b0 * 256;
-        f1 = b1 * 256;
-    }
+    const uint64_t f0 = sh.ffn[0], f1 = sh.ffn[1], v0 = sh.vocab[0], v1 = sh.vocab[1];
     m.lffn = (uint32_t)(f1 - f0);
-    uint64_t v0 = 0, v1 = c.vocab;
-    if (T > 1) split_range(c.vocab, T, R, &v0, &v1);
     m.vocab0 = (uint32_t)v0;
     m.lvocab = (uint32_t)(v1 - v0);
 
     add_matrix(m.embed, "token_embd.weight", 0, c.dim, 0, 0, 0, 0);
     m.layers.resize(c.layers);
-    const uint64_t hq0 = (uint64_t)R * m.lheads * hd, hq1 = hq0 + (uint64_t)m.lheads * hd;
-    const uint64_t hk0 = (uint64_t)R * m.lkv_heads * hd, hk1 = hk0 + (uint64_t)m.lkv_heads * hd;
+    const uint64_t hq0 = sh.q[0], hq1 = sh.q[1], hk0 = sh.kv[0], hk1 = sh.kv[1];
     for (uint64_t i = 0; i < c.layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
         if (g.has(p + "attn_qkv.weight"))
@@ -358,7 +372,8 @@ bool build_gemm_weights(Model& m) {
 }
 
 void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, float* y, bool add, uint32_t batch,
-                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl) {
+                   float* h_buf, float* y_buf, int* err, const QMatDev* next, cudaStream_t s, bool pdl,
+                   const TpPeers* peers, uint32_t slot) {
     const LayerWeights& L = m.layers[layer];
     const uint32_t dim = (uint32_t)m.cfg.dim;
     for (uint32_t b = 0; b < batch; ++b) {
@@ -395,7 +410,9 @@ void run_dense_ffn(Model& m, size_t layer, const float* x, const float* norm_w, 
         }
         cuda_check(launch_qmatvec(a, s, pdl), "ffn down");
     }
-    if (tp) {
+    if (tp && peers && add) {  // partial sums through the peer inboxes, residual add fused
+        cuda_check(launch_tp_allreduce_add(*peers, TP_DOWN, slot, y, y_buf, batch * dim, err, s, pdl), "ffn sum");
+    } else if (tp) {
         allreduce_sum(m, y_buf, (size_t)batch * dim, s);
         if (add) {
             cuda_check(launch_add(y, y_buf, (size_t)batch * dim, s, false), "residual add");

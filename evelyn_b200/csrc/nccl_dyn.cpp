@@ -7,7 +7,7 @@
 //   2. a libnccl.so.2 already loaded in the process,
 //   3. the system libnccl.so.2.
 // The calls used (unique id, communicator init/destroy/abort, all-reduce, broadcast,
-// group start/end) are stable across NCCL 2.x.
+// all-gather, group start/end) are stable across NCCL 2.x.
 #include <dlfcn.h>
 
 #include <cstdlib>
@@ -41,6 +41,7 @@ void load() {
     bool ok = sym(h, "ncclGetUniqueId", &n.GetUniqueId) && sym(h, "ncclCommInitRank", &n.CommInitRank) &&
               sym(h, "ncclCommDestroy", &n.CommDestroy) && sym(h, "ncclCommAbort", &n.CommAbort) &&
               sym(h, "ncclAllReduce", &n.AllReduce) && sym(h, "ncclBroadcast", &n.Broadcast) &&
+              sym(h, "ncclAllGather", &n.AllGather) &&
               sym(h, "ncclGroupStart", &n.GroupStart) && sym(h, "ncclGroupEnd", &n.GroupEnd) &&
               sym(h, "ncclGetErrorString", &n.GetErrorString);
     if (!ok) {

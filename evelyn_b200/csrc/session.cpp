@@ -43,6 +43,7 @@ Decoder::~Decoder() {
         if (graph) cudaGraphExecDestroy(graph);
         if (step_k) step_kernel_destroy(step_k);
         if (stream) cudaStreamDestroy(stream);
+        for (void* p : b.ipc_open) cudaIpcCloseMemHandle(p);
     }
 }
 
@@ -155,7 +156,7 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     host_pos.assign(batch, 0);
     // a batch of sequences on one GPU runs its products on the tensor cores
     const char* env = std::getenv("EVELYN_BATCH_GEMM");
-    if (batch > 1 && batch <= 32 && m->tp_size == 1 && !(env && env[0] == '0') && build_gemm_weights(*m)) {
+    if (batch > 1 && batch <= 32 && !(env && env[0] == '0') && build_gemm_weights(*m)) {
         use_gemm = true;
         const uint64_t kmax = std::max<uint64_t>({c.dim, (uint64_t)m->lffn, qw});
         b.gbx.alloc(gemm_x_bytes(32, (uint32_t)kmax));
@@ -170,6 +171,55 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
         b.gpart2.alloc(pmax);
         b.gpart3.alloc(pmax);
     }
+    if (m->tp_size > 1) init_tp();
+}
+
+// Tensor parallelism: this rank's inbox for the step's exchanges and the mappings of
+// every peer's inbox and logits buffer (CUDA IPC handles swapped with one NCCL
+// all-gather). Every rank creates its session or batch together with the others.
+void Decoder::init_tp() {
+    Model& m = *model;
+    const uint32_t T = (uint32_t)m.tp_size, R = (uint32_t)m.tp_rank, L = (uint32_t)m.cfg.layers;
+    if (T > (uint32_t)kMaxPeers) raise(EVL_ERR_UNSUPPORTED, "tensor parallelism over more than 8 ranks");
+    const uint64_t cap = ((std::max<uint64_t>((uint64_t)b.batch * m.cfg.dim, 2ull * b.batch)) + 31) & ~31ull;
+    b.tpinbox.alloc((uint64_t)TP_PURPOSES * T * cap * 8);
+    cuda_check(cudaMemset(b.tpinbox.p, 0xff, b.tpinbox.bytes), "memset");  // tag 0xffffffff: never expected
+    if (!b.epoch.p) {
+        b.epoch.alloc(4);
+        cuda_check(cudaMemset(b.epoch.p, 0, 4), "memset");
+    }
+    cudaIpcMemHandle_t mine[2];
+    cuda_check(cudaIpcGetMemHandle(&mine[0], b.tpinbox.p), "cudaIpcGetMemHandle");
+    cuda_check(cudaIpcGetMemHandle(&mine[1], b.logits.p), "cudaIpcGetMemHandle");
+    DeviceBuffer send, all;
+    send.alloc(sizeof(mine));
+    all.alloc(sizeof(mine) * T);
+    cuda_check(cudaMemcpy(send.p, mine, sizeof(mine), cudaMemcpyHostToDevice), "H2D handles");
+    nccl_check(nccl().AllGather(send.p, all.p, sizeof(mine), ncclUint8, m.comm, stream), "ncclAllGather");
+    std::vector<cudaIpcMemHandle_t> hs(2 * T);
+    cuda_check(cudaMemcpyAsync(hs.data(), all.p, sizeof(mine) * T, cudaMemcpyDeviceToHost, stream), "D2H handles");
+    cuda_check(cudaStreamSynchronize(stream), "handle exchange");
+    b.tp = TpPeers{};
+    for (uint32_t r = 0; r < T; ++r) {
+        if (r == R) {
+            b.tp.inbox[r] = b.tpinbox.as<uint64_t>();
+            b.peer_logits[r] = b.logits.as<float>();
+            continue;
+        }
+        void* pi = nullptr;
+        void* pl = nullptr;
+        cuda_check(cudaIpcOpenMemHandle(&pi, hs[2 * r], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        b.ipc_open.push_back(pi);
+        cuda_check(cudaIpcOpenMemHandle(&pl, hs[2 * r + 1], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        b.ipc_open.push_back(pl);
+        b.tp.inbox[r] = static_cast<uint64_t*>(pi);
+        b.peer_logits[r] = static_cast<const float*>(pl);
+    }
+    b.tp.rank = R;
+    b.tp.size = T;
+    b.tp.cap = (uint32_t)cap;
+    b.tp.epoch = b.epoch.as<uint32_t>();
+    b.tp.period = 2 * L + 1;  // slots: o of layer l 2l, down 2l + 1, the pick 2L
 }
 
 void Decoder::gemm_stage(const float* x, uint32_t cols, uint32_t stride, const float* norm_w, bool pdl) {
@@ -244,6 +294,7 @@ void Decoder::gemm_reduce(const QMatrix& w, const float* part, uint32_t ksplit, 
 void Decoder::enqueue_batched(bool pdl) {
     Model& m = *model;
     const Config& c = m.cfg;
+    const bool tp = m.tp_size > 1;
     const uint32_t dim = (uint32_t)c.dim, hd = (uint32_t)c.head_dim;
     const uint32_t qw = m.lheads * hd, kw = m.lkv_heads * hd, F = m.lffn;
     float* x = b.x.as<float>();
@@ -277,22 +328,48 @@ void Decoder::enqueue_batched(bool pdl) {
         }
         gemm_stage(b.att.as<float>(), qw, qw, nullptr, pdl);
         gemm_product(L.o, p1, k1, pdl);
-        gemm_reduce(L.o, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+        if (tp) {  // partial sums through the peer inboxes, residual add fused
+            gemm_reduce(L.o, p1, k1, b.y.as<float>(), dim, EPI_STORE, nullptr, 0, pdl);
+            cuda_check(launch_tp_allreduce_add(b.tp, TP_O, 2 * li, x, b.y.as<float>(), b.batch * dim,
+                                               b.err.as<int>(), stream, pdl),
+                       "o sum");
+            kernels += 1;
+        } else {
+            gemm_reduce(L.o, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+        }
         gemm_stage(x, dim, dim, L.ffn_norm, pdl);
         gemm_product(L.gate, p1, k1, pdl);
         gemm_product(L.up, p2, k2, pdl);
         gemm_reduce(L.gate, p1, k1, b.h.as<float>(), F, EPI_SWIGLU, p2, k2, pdl);
         gemm_stage(b.h.as<float>(), F, F, nullptr, pdl);
         gemm_product(L.down, p1, k1, pdl);
-        gemm_reduce(L.down, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+        if (tp) {
+            gemm_reduce(L.down, p1, k1, b.y.as<float>(), dim, EPI_STORE, nullptr, 0, pdl);
+            cuda_check(launch_tp_allreduce_add(b.tp, TP_DOWN, 2 * li + 1, x, b.y.as<float>(), b.batch * dim,
+                                               b.err.as<int>(), stream, pdl),
+                       "ffn sum");
+            kernels += 1;
+        } else {
+            gemm_reduce(L.down, p1, k1, x, dim, EPI_ADD, nullptr, 0, pdl);
+        }
     }
     gemm_stage(x, dim, dim, m.out_norm, pdl);
     gemm_product(m.lm_head, p1, k1, pdl);
-    gemm_reduce(m.lm_head, p1, k1, b.logits.as<float>(), (uint32_t)c.vocab, EPI_STORE, nullptr, 0, pdl);
-    cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, b.batch, b.amax_v.as<float>(),
-                             b.amax_i.as<int32_t>(), b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(),
-                             b.pos.as<int32_t>(), b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
-               "argmax");
+    // this rank's vocabulary shard into its columns of the [batch][vocab] logits
+    gemm_reduce(m.lm_head, p1, k1, b.logits.as<float>() + m.vocab0, (uint32_t)c.vocab, EPI_STORE, nullptr, 0, pdl);
+    if (tp) {
+        cuda_check(launch_tp_argmax(b.tp, 2 * (uint32_t)c.layers, b.logits.as<float>(), (uint32_t)c.vocab, m.vocab0,
+                                    m.lvocab, b.batch, b.amax_v.as<float>(), b.amax_i.as<int32_t>(), b.amax_parts,
+                                    b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),
+                                    b.hist.as<int32_t>(), b.max_ctx, b.epoch.as<uint32_t>(), b.err.as<int>(), stream,
+                                    pdl),
+                   "argmax");
+    } else {
+        cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, b.batch, b.amax_v.as<float>(),
+                                 b.amax_i.as<int32_t>(), b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(),
+                                 b.pos.as<int32_t>(), b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
+                   "argmax");
+    }
     kernels += 2;
 }
 
@@ -411,9 +488,10 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         const uint64_t ys[1] = {c.dim};
         matvec_each(a, B, qw, ys, stream, pdl, "o-proj matvec");
         kernels += B;
-        if (tp) {
-            allreduce_sum(m, b.y.as<float>(), (size_t)B * c.dim, stream);
-            cuda_check(launch_add(x, b.y.as<float>(), (size_t)B * c.dim, stream, false), "residual add");
+        if (tp) {  // partial sums through the peer inboxes, residual add fused
+            cuda_check(launch_tp_allreduce_add(b.tp, TP_O, 2 * li, x, b.y.as<float>(), B * (uint32_t)c.dim,
+                                               b.err.as<int>(), stream, pdl),
+                       "o sum");
             kernels += 1;
         }
     }
@@ -572,36 +650,51 @@ void Decoder::enqueue_head(bool pdl) {
     const Config& c = m.cfg;
     const uint32_t B = b.batch;
     const bool tp = m.tp_size > 1;
+    const uint64_t V = c.vocab;
+    // the LM head (this rank's vocabulary shard under tensor parallelism) into its
+    // columns of the [batch][vocab] logits
     MatvecArgs a;
     a.nseg = 1;
     a.seg[0].m = m.lm_head.dev;
-    a.seg[0].y = tp ? b.y.as<float>() : b.logits.as<float>();
+    a.seg[0].y = b.logits.as<float>() + m.vocab0;
     a.x = b.x.as<float>();
     a.cols = (uint32_t)c.dim;
     a.norm_w = m.out_norm;
     a.eps = c.eps;
     a.err = b.err.as<int>();
-    const uint64_t ys[1] = {tp ? (uint64_t)m.lvocab : c.vocab};
+    const uint64_t ys[1] = {V};
     matvec_each(a, B, c.dim, ys, stream, pdl, "lm-head matvec");
     kernels += B;
-    if (tp) {  // vocabulary shards -> full logits on every rank
-        const uint64_t V = c.vocab;
-        const Nccl& nc = nccl();
-        nccl_check(nc.GroupStart(), "ncclGroupStart");
-        for (int r = 0; r < m.tp_size; ++r) {
-            const uint64_t base = V / m.tp_size, rem = V % m.tp_size;
-            const uint64_t lo = r * base + std::min<uint64_t>(r, rem), n = base + (r < (int)rem ? 1 : 0);
-            for (uint32_t bi = 0; bi < B; ++bi)
-                nc.Broadcast(b.y.as<float>() + (uint64_t)bi * m.lvocab, b.logits.as<float>() + bi * V + lo, n,
-                             ncclFloat32, r, m.comm, stream);
-        }
-        nccl_check(nc.GroupEnd(), "logits gather");
+    if (tp) {  // each rank's best of its shard, picked the same way on every rank
+        cuda_check(launch_tp_argmax(b.tp, 2 * (uint32_t)c.layers, b.logits.as<float>(), (uint32_t)V, m.vocab0, m.lvocab,
+                                    B, b.amax_v.as<float>(), b.amax_i.as<int32_t>(), b.amax_parts,
+                                    b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),
+                                    b.hist.as<int32_t>(), b.max_ctx, b.epoch.as<uint32_t>(), b.err.as<int>(), stream,
+                                    pdl),
+                   "argmax");
+    } else {
+        cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)V, B, b.amax_v.as<float>(), b.amax_i.as<int32_t>(),
+                                 b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),
+                                 b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
+                   "argmax");
     }
-    cuda_check(launch_argmax(b.logits.as<float>(), (uint32_t)c.vocab, B, b.amax_v.as<float>(), b.amax_i.as<int32_t>(),
-                             b.amax_parts, b.argmax.as<int32_t>(), b.tokens.as<int32_t>(), b.pos.as<int32_t>(),
-                             b.hist.as<int32_t>(), b.max_ctx, stream, pdl),
-               "argmax");
     kernels += 2;
+}
+
+// Tensor parallelism: the other ranks' vocabulary shards of the last step's logits,
+// read from their buffers over NVLink (each rank wrote its shard before the step's
+// pick, which every rank waited for).
+void Decoder::gather_peer_logits() {
+    Model& m = *model;
+    const uint64_t V = m.cfg.vocab, T = (uint64_t)m.tp_size;
+    for (uint64_t r = 0; r < T; ++r) {
+        if ((int)r == m.tp_rank) continue;
+        const uint64_t base = V / T, rem = V % T;
+        const uint64_t lo = r * base + std::min<uint64_t>(r, rem), n = base + (r < rem ? 1 : 0);
+        cuda_check(cudaMemcpy2DAsync(b.logits.as<float>() + lo, V * 4, b.peer_logits[r] + lo, V * 4, n * 4, b.batch,
+                                     cudaMemcpyDeviceToDevice, stream),
+                   "peer logits");
+    }
 }
 
 void Decoder::enqueue_dense(bool pdl) {
@@ -640,7 +733,8 @@ void Decoder::enqueue_dense(bool pdl) {
                 next[2] = m.layers[li + 1].v.dev;
             }
             run_dense_ffn(m, li, b.x.as<float>(), m.layers[li].ffn_norm, b.x.as<float>(), true, b.batch,
-                          b.h.as<float>(), b.y.as<float>(), b.err.as<int>(), next, stream, pdl);
+                          b.h.as<float>(), b.y.as<float>(), b.err.as<int>(), next, stream, pdl,
+                          m.tp_size > 1 ? &b.tp : nullptr, 2 * li + 1);
             kernels += 2 * b.batch + (m.tp_size > 1 ? 1 : 0);
         }
     }
@@ -760,6 +854,7 @@ void Decoder::step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* lo
     } else {
         launch_graph();
     }
+    if (logits_out && m.tp_size > 1 && !(ffn && ffn->ffn)) gather_peer_logits();
     if (logits_out)
         cuda_check(cudaMemcpyAsync(b.h_logits.p, b.logits.p, (size_t)b.batch * c.vocab * 4, cudaMemcpyDeviceToHost,
                                    stream),

@@ -70,6 +70,11 @@ class _EndpointStats(C.Structure):
                 ("max_ns", C.c_uint64)]
 
 
+class _TpShard(C.Structure):
+    _fields_ = [("q_rows", C.c_uint64 * 2), ("kv_rows", C.c_uint64 * 2), ("ffn_rows", C.c_uint64 * 2),
+                ("vocab_rows", C.c_uint64 * 2)]
+
+
 @dataclasses.dataclass(frozen=True)
 class Config:
     """runtime.rs:93-110 (dense-attention fields)."""
@@ -103,6 +108,7 @@ SIGNATURES = {
     "evl_argmax": (C.c_uint32, [_F, C.c_size_t]),
     "evl_log_prob": (C.c_float, [_F, C.c_size_t, C.c_uint32]),
     "evl_tp_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
+    "evl_tp_shard_plan": (C.c_int, [C.POINTER(_Config), C.c_int32, C.c_int32, C.POINTER(_TpShard)]),
     "evl_model_load": (C.c_int, [C.c_char_p, C.POINTER(_Options), C.POINTER(_P)]),
     "evl_model_load_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_Options), C.POINTER(_P)]),
     "evl_model_free": (None, [_P]),

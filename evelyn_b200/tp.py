@@ -1,23 +1,20 @@
-"""Tensor-parallel shard plan (the same split csrc/model.cpp applies when it loads a
-model with tp_size > 1), for callers that want to reason about the shards.
+"""Tensor-parallel shard plan of the engine (evl_tp_shard_plan: the split
+csrc/model.cpp applies when it loads a model with tp_size > 1), for callers that want
+to reason about the shards. Host only: no device needed.
 
 Column split (by output rows): attn_q by query heads, attn_k / attn_v by kv heads,
 ffn_gate / ffn_up by FFN rows on 256-value super-block boundaries, the LM head by
 vocabulary rows. Row split (by inputs): attn_output over this rank's query-head
 dimensions, ffn_down over this rank's FFN rows. The partial outputs of attn_output
-and ffn_down are summed across ranks (all-reduce); the vocabulary shards of the
-logits are gathered.
+and ffn_down are summed across ranks; each rank picks the greedy token of its
+vocabulary shard and the ranks agree on the best.
 """
 from __future__ import annotations
 
+import ctypes as C
 import dataclasses
 
-
-def split_range(n: int, parts: int, i: int) -> tuple[int, int]:
-    """Even split of n items over `parts`: the first n % parts parts get one more."""
-    base, rem = divmod(n, parts)
-    lo = i * base + min(i, rem)
-    return lo, lo + base + (1 if i < rem else 0)
+from . import runtime
 
 
 @dataclasses.dataclass(frozen=True)
@@ -29,13 +26,11 @@ class Shard:
 
 
 def shard(heads: int, kv_heads: int, head_dim: int, ffn: int, vocab: int, tp_size: int, rank: int) -> Shard:
-    if kv_heads % tp_size:
-        raise ValueError("tp_size must divide head_count_kv")
-    if tp_size > 1 and ffn % 256:
-        raise ValueError("tensor parallelism needs feed_forward_length % 256 == 0")
-    lh, lkv = heads // tp_size, kv_heads // tp_size
-    b0, b1 = split_range(ffn // 256, tp_size, rank) if tp_size > 1 else (0, ffn // 256)
-    f = (b0 * 256, b1 * 256) if tp_size > 1 else (0, ffn)
-    return Shard(q_rows=(rank * lh * head_dim, (rank + 1) * lh * head_dim),
-                 kv_rows=(rank * lkv * head_dim, (rank + 1) * lkv * head_dim),
-                 ffn_rows=f, vocab_rows=split_range(vocab, tp_size, rank))
+    """The engine's shard of rank `rank`; raises EvelynError (InvalidInput / Unsupported)."""
+    cfg = runtime._Config()
+    cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab = heads, kv_heads, head_dim, ffn, vocab
+    out = runtime._TpShard()
+    lib = runtime.lib()
+    runtime.check(lib.evl_tp_shard_plan(C.byref(cfg), int(tp_size), int(rank), C.byref(out)))
+    pair = lambda a: (int(a[0]), int(a[1]))  # noqa: E731
+    return Shard(pair(out.q_rows), pair(out.kv_rows), pair(out.ffn_rows), pair(out.vocab_rows))

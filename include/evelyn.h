@@ -96,6 +96,16 @@ uint32_t evl_argmax(const float* logits, size_t n);
 float evl_log_prob(const float* logits, size_t n, uint32_t target);
 /* ncclGetUniqueId for tensor parallelism: rank 0 calls it and shares the bytes. */
 evl_status evl_tp_unique_id(uint8_t out[128]);
+/* The tensor-parallel shard that rank `rank` of `tp_size` loads (the Megatron split that
+ * stands in for one process running src/runtime.rs:773-808): [first, last) rows of
+ * attn_q (and input columns of attn_output), of attn_k / attn_v, of ffn_gate / ffn_up
+ * (and input columns of ffn_down, on 256-value super-block boundaries, uneven when the
+ * block count does not divide) and of the LM head. Host only; uses heads, kv_heads,
+ * head_dim, ffn and vocab of cfg. InvalidInput / Unsupported as evl_model_load. */
+typedef struct evl_tp_shard {
+    uint64_t q_rows[2], kv_rows[2], ffn_rows[2], vocab_rows[2];
+} evl_tp_shard;
+evl_status evl_tp_shard_plan(const evl_config* cfg, int32_t tp_size, int32_t rank, evl_tp_shard* out);
 
 /* ------------------------------------------------------------------ model */
 /* Model::load (src/runtime.rs:199-406). Weights stay quantised, repacked in HBM. */

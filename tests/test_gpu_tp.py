@@ -1,6 +1,8 @@
-"""Tensor parallelism on real GPUs: 2 (and 4 when present) ranks, one process per GPU
-over NCCL, logits within the session tolerance of the CPU oracle and greedy tokens
-identical. Skipped on a box with fewer GPUs than ranks."""
+"""Tensor parallelism on real GPUs: 2 (and 4 when present) ranks, one process per GPU,
+the step's exchanges through peer-memory inboxes: a session's logits within the
+session tolerance of the CPU oracle and greedy tokens identical, and a three-sequence
+batch (tensor-core products) within the same tolerance. Skipped on a box with fewer
+GPUs than ranks."""
 import json
 import os
 import socket
@@ -39,4 +41,5 @@ def test_tp_logits_and_greedy_match_oracle(world, tmp_path):
     res = json.loads(out.read_text())
     assert res["world"] == world
     assert res["max_abs"] <= LOGIT_TOL, res
+    assert res["batch_max_abs"] <= LOGIT_TOL, res
     assert res["greedy"] == res["greedy_oracle"], res

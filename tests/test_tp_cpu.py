@@ -1,6 +1,8 @@
-"""Tensor-parallel partition math on the CPU: simulated ranks, each holding its shard
-of the oracle's dequantised weights, reproduce the unsharded layer (the reference has
-one process; its Megatron split is new here). The 2-rank case also runs as two gloo
+"""Tensor-parallel partition math on the CPU: the engine's own shard plan
+(evl_tp_shard_plan, the function model.cpp loads shards with) covers every tensor,
+and simulated ranks, each holding its shard of the oracle's dequantised weights,
+reproduce the unsharded layer (the reference has one process; its Megatron split is
+new here). The 2-rank case also runs as two gloo
 processes that all-reduce their FFN partials, the host-side path `bench.py --gpus N`
 takes for its plumbing."""
 import os
@@ -43,6 +45,18 @@ def test_shards_cover_everything(T):
     for k, ranges in cover.items():
         assert ranges[0][0] == 0 and ranges[-1][1] == totals[k]
         assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+
+
+def test_shard_plan_errors():
+    import evelyn_b200 as evl
+    with pytest.raises(evl.EvelynError) as e:
+        tp.shard(SPEC.heads, SPEC.kv_heads, SPEC.head_dim, SPEC.ffn, SPEC.vocab, 3, 0)  # 3 does not divide 8
+    assert e.value.kind == "InvalidInput"
+    with pytest.raises(evl.EvelynError) as e:
+        tp.shard(SPEC.heads, SPEC.kv_heads, SPEC.head_dim, 1000, SPEC.vocab, 2, 0)  # 1000 % 256 != 0
+    assert e.value.kind == "Unsupported"
+    with pytest.raises(evl.EvelynError):
+        tp.shard(SPEC.heads, SPEC.kv_heads, SPEC.head_dim, SPEC.ffn, SPEC.vocab, 2, 2)  # rank outside
 
 
 def test_uneven_ffn_blocks_for_32b_shape():

@@ -29,6 +29,10 @@ def main(out_path):
     toks = [int(t) for t in np.random.default_rng(9).integers(0, spec.vocab, 24)]
     logits = [s.step(t) for t in toks]
     greedy = s.generate(evl.argmax(logits[-1]), 16)
+    # a batch of three sequences (tensor-core products, the same exchanges)
+    btoks = np.random.default_rng(11).integers(0, spec.vocab, (8, 3))
+    bat = evl.Batch(m, 3, max_ctx=64)
+    blogits = [bat.step(row) for row in btoks]
     dist.barrier()
     if rank == 0:
         from oracle import oracle as orc
@@ -41,10 +45,20 @@ def main(out_path):
         for _ in range(16):
             tok = orc.argmax(rs.step(tok))
             want.append(tok)
+        bworst = 0.0
+        ors = [orc.Session(r) for _ in range(3)]
+        for row, got in zip(btoks, blogits):
+            for i in range(3):
+                bworst = max(bworst, float(np.abs(got[i] - ors[i].step(int(row[i]))).max()))
+        res = {"world": world, "max_abs": worst, "batch_max_abs": bworst, "greedy": list(map(int, greedy)),
+               "greedy_oracle": want}
         with open(out_path, "w") as f:
-            f.write(json.dumps({"world": world, "max_abs": worst, "greedy": list(map(int, greedy)),
-                                "greedy_oracle": want}) + "\n")
-    del s, m
+            f.write(json.dumps(res) + "\n")
+        rdir = os.environ.get("EVELYN_TP_RESULT_DIR")
+        if rdir:
+            with open(os.path.join(rdir, f"tp_world{world}.json"), "w") as f:
+                f.write(json.dumps(res) + "\n")
+    del bat, s, m
     dist.destroy_process_group()
 
 
