@@ -395,6 +395,28 @@ evl_status evl_session_generate(evl_session* s, uint32_t token, uint32_t n, uint
     });
 }
 
+evl_status evl_session_prefill(evl_session* s, const uint32_t* tokens, size_t n, float* logits_out,
+                               uint32_t* argmax_out) {
+    return guarded([&] {
+        require(s && (tokens || n == 0), "null argument");
+        s->d.prefill(tokens, n, logits_out, argmax_out);
+    });
+}
+
+evl_status evl_session_sample(evl_session* s, float temperature, uint64_t* rng_state, uint32_t* token_out) {
+    return guarded([&] {
+        require(s && rng_state && token_out, "null argument");
+        s->d.sample(temperature, rng_state, token_out);
+    });
+}
+
+evl_status evl_batch_sample(evl_batch* b, float temperature, uint64_t* rng_states, uint32_t* tokens_out) {
+    return guarded([&] {
+        require(b && rng_states && tokens_out, "null argument");
+        b->d.sample(temperature, rng_states, tokens_out);
+    });
+}
+
 void* evl_session_stream(evl_session* s) { return s ? (void*)s->d.stream : nullptr; }
 uint32_t evl_session_kernels_per_step(const evl_session* s) { return s ? s->d.kernels_per_step : 0; }
 

@@ -24,10 +24,13 @@
 //         at h*512 + 16L holding the q words at bytes 16h + 4t of A row g8, A row g8+8,
 //         B row g8, B row g8+8; then the f16 scales (A, B) of each row.
 //   F16, BF16, F32: plain values, each row of the panel contiguous.
-// No byte is added or dropped: a slab of Q4_K / Q6_K / Q8_0 is exactly 16 rows of GGUF
-// blocks, and block_byte_address maps every GGUF byte to its place (4-byte payload
-// words stay contiguous). Q5_K has no device-matrix layout (it is read only through
-// the raw dequantiser).
+//   Q5_K  per super-block (2816 B): the qs groups as Q4_K (2048 B), then the qh words
+//         of each lane (bytes 4t..4t+3 and 16+4t.. of rows g8 and g8 + 8, the fifth bits
+//         of the values its qs words hold) at 2048 + 16L in the same order, then the
+//         16-byte header (d, dmin, scales[12]) of each row.
+// No byte is added or dropped: a slab of Q4_K / Q5_K / Q6_K / Q8_0 is exactly 16 rows
+// of GGUF blocks, and block_byte_address maps every GGUF byte to its place (4-byte
+// payload words stay contiguous).
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -54,6 +57,7 @@ constexpr uint32_t kPanelUnits = 32;
 __host__ __device__ inline uint32_t unit16_bytes(uint32_t type) {
     switch (type) {
         case GGML_Q4_K: return 576;   // 16 x 144 / 4
+        case GGML_Q5_K: return 704;   // 16 x 176 / 4
         case GGML_Q6_K: return 840;   // 16 x 210 / 4
         case GGML_Q8_0: return 1088;  // 16 x 2 x 34
         case GGML_F16:
@@ -96,6 +100,15 @@ __host__ __device__ inline uint64_t block_byte_address(const QMatDev& m, uint32_
     if (T == GGML_Q4_K) {
         if (o < 16) return base + 2048u + r16 * 16u + o;
         const uint32_t q = o - 16, j = q >> 5, w = (q >> 2) & 7, t = w & 3;
+        return base + j * 512u + (g8 * 4u + t) * 16u + ((w >> 2) * 2u + hi) * 4u + (q & 3u);
+    }
+    if (T == GGML_Q5_K) {
+        if (o < 16) return base + 2560u + r16 * 16u + o;
+        if (o < 48) {  // qh: byte l holds the fifth bits of value l of the eight sub-blocks
+            const uint32_t q = o - 16, w = q >> 2, t = w & 3;
+            return base + 2048u + (g8 * 4u + t) * 16u + ((w >> 2) * 2u + hi) * 4u + (q & 3u);
+        }
+        const uint32_t q = o - 48, j = q >> 5, w = (q >> 2) & 7, t = w & 3;
         return base + j * 512u + (g8 * 4u + t) * 16u + ((w >> 2) * 2u + hi) * 4u + (q & 3u);
     }
     // Q6_K

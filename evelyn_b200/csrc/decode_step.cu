@@ -356,7 +356,7 @@ __device__ __forceinline__ void rows_from_ring(const MvCtx& c, uint32_t si, uint
                                                uint64_t* empty, const uint8_t* xs, uint32_t& n, uint32_t& off,
                                                uint32_t rb, uint32_t slab, uint32_t sbw, const Lane& L, int lane,
                                                volatile int* abort_flag, float& acc0, float& acc1, bool& bad) {
-    constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q6_K ? 840u : 1088u;
+    constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q5_K ? 704u : T == GGML_Q6_K ? 840u : 1088u;
     const float wt = ((L.t & 1) ? 65536.f : 1.f) * ((T == GGML_Q4_K && L.part) ? 0.0625f : 1.f);
     for (uint32_t g = 0; g < c.ngroups; ++g, ++n) {
         const uint32_t o = ring_place(off, ctx_item_bytes(c, si, rb, g), c.cap);
@@ -369,6 +369,8 @@ __device__ __forceinline__ void rows_from_ring(const MvCtx& c, uint32_t si, uint
             if (ub < U) {
                 if constexpr (T == GGML_Q4_K) {
                     sb_q4k(q, u0, xs, c.fscale, c.xsum, L, lane, wt, acc0, acc1);
+                } else if constexpr (T == GGML_Q5_K) {
+                    sb_q5k(q, u0, xs, c.fscale, c.xsum, L, lane, wt, acc0, acc1);
                 } else if constexpr (T == GGML_Q6_K) {
                     sb_q6k(q, u0, xs, c.fscale, c.msum, L, lane, wt, acc0, acc1);
                 } else {
@@ -403,6 +405,10 @@ __device__ bool consume_phase(const DPhase& P, uint8_t* base, uint64_t* full, ui
         switch (c.type[si]) {
             case GGML_Q4_K:
                 rows_from_ring<GGML_Q4_K>(c, si, base, full, empty, xs, n, off, rb, slab, sbw, L, lane, abort_flag, acc0,
+                                          acc1, bad);
+                break;
+            case GGML_Q5_K:
+                rows_from_ring<GGML_Q5_K>(c, si, base, full, empty, xs, n, off, rb, slab, sbw, L, lane, abort_flag, acc0,
                                           acc1, bad);
                 break;
             case GGML_Q6_K:

@@ -102,6 +102,19 @@ __device__ __forceinline__ float dq_repacked_value(const QMatDev& m, uint32_t r,
             float q = (float)(hi ? (v >> 4) : (v & 0xf));
             return __fsub_rn(__fmul_rn(__fmul_rn(d, s), q), __fmul_rn(dmin, mm));
         }
+        case GGML_Q5_K: {
+            const uint32_t b = c >> 8, e = c & 255;
+            uint8_t blk[16];
+            for (uint32_t i = 0; i < 16; ++i) blk[i] = byte(b, i);
+            float d = f16_exact(ld_u16(blk)), dmin = f16_exact(ld_u16(blk + 2));
+            const uint32_t j = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+            float s, mm;
+            scale_min_bytes(2 * j + hi, blk + 4, &s, &mm);
+            const uint8_t v = byte(b, 48 + j * 32 + l);
+            const uint8_t qh = byte(b, 16 + l);
+            const int q = (hi ? (v >> 4) : (v & 0xf)) + (((qh >> (2 * j + hi)) & 1) ? 16 : 0);
+            return __fsub_rn(__fmul_rn(__fmul_rn(d, s), (float)q), __fmul_rn(dmin, mm));
+        }
         case GGML_Q6_K: {
             const uint32_t b = c >> 8, e = c & 255, half = e >> 7, rr = e & 127, k = rr >> 5, l = rr & 31;
             const uint8_t lo = byte(b, 64 * half + ((k & 1) ? 32 : 0) + l);

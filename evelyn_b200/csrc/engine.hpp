@@ -263,6 +263,8 @@ struct StepBuffers {
     DeviceBuffer tagpool, epoch;
     // tensor parallelism: this rank's inbox for the step's exchanges (tp_comm.cu), the
     // peers' inboxes and logits buffers mapped into this process
+    DeviceBuffer smp_rng, smp_out, smp_m, smp_s;  // sampling: states, picks, per-part max and sums
+    PinnedBuffer h_rng;
     DeviceBuffer tpinbox;
     TpPeers tp;
     const float* peer_logits[kMaxPeers] = {};
@@ -286,7 +288,8 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     std::string step_note;        // why the step kernel is not used, if it is not
 
     ~Decoder();
-    void init(Model* m, uint32_t batch, uint32_t max_ctx);
+    // share_kv: a prefill child whose rows are positions of that (single) sequence
+    void init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* share_kv = nullptr);
     void init_tp();  // collective over the model's ranks: inboxes, peer mappings
     MatvecArgs qkv_args(uint32_t layer) const;
     RopeArgs rope_args(uint32_t layer) const;
@@ -313,6 +316,14 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     void step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* logits_out, uint32_t* argmax_out);
     // On-device greedy loop of n steps (single sequence).
     void generate(uint32_t token, uint32_t n, uint32_t* tokens_out);
+    // Temperature sampling of every sequence from the last step's logits (host states
+    // in/out, host tokens out).
+    void sample(float temperature, uint64_t* states, uint32_t* tokens_out);
+    // Batched prompt processing (single sequence): n tokens, optional logits [n][vocab]
+    // and argmax [n] (host).
+    void prefill(const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out);
+    std::unique_ptr<Decoder> pf;  // prefill child (made on first use)
+    bool prefill_child = false;
 };
 
 }  // namespace evl

@@ -262,6 +262,13 @@ cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, boo
 // Greedy pick over [batch][n] logits: first maximum wins (strict '>' like src/runtime.rs:897-905).
 // Optionally writes the pick to next_tokens, logs it at hist[b*hist_stride + pos[b]] and
 // advances pos[b] (null pointers skip each part).
+// Temperature sampling of each of `batch` logits rows (src/server.rs:326-352): rng[b] is
+// the xorshift64* state (device), advanced as the reference advances it; argmax[b] is
+// the greedy pick of the same row (the fallback). part_m [batch][parts] and part_s
+// (doubles) are scratch. temperature > FLT_EPSILON (the caller takes argmax otherwise).
+cudaError_t launch_sample(const float* logits, uint32_t n, uint32_t batch, float temperature, uint64_t* rng,
+                          const int32_t* argmax, float* part_m, double* part_s, uint32_t parts, int32_t* out,
+                          cudaStream_t s);
 // epoch (optional) is advanced once the pick is made: the step's last kernel.
 cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t batch, float* part_v, int32_t* part_i,
                           uint32_t parts, int32_t* out, int32_t* next_tokens, int32_t* pos, int32_t* hist,

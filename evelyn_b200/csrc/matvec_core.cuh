@@ -198,6 +198,39 @@ __device__ __forceinline__ void sb_q4k(const uint8_t* sb, uint32_t u0, const uin
     }
 }
 
+// Q5_K: one super-block (4 units from u0) of 16 rows, as Q4_K with the fifth bit of every
+// value from the lane's qh words (bit 2j of qh byte l for value l of sub-block 2j, bit
+// 2j + 1 for sub-block 2j + 1, gguf.rs:373-396); the high nibbles are shifted down
+// to 0..31 as well, so the lane weight has no 1/16.
+__device__ __forceinline__ uint32_t q5_lo(uint32_t a, uint32_t h, uint32_t bit) {
+    return (a & 0x0F0F0F0Fu) | (((h >> bit) & 0x01010101u) << 4);
+}
+__device__ __forceinline__ uint32_t q5_hi(uint32_t a, uint32_t h, uint32_t bit) {
+    return ((a >> 4) & 0x0F0F0F0Fu) | (((h >> bit) & 0x01010101u) << 4);
+}
+__device__ __forceinline__ void sb_q5k(const uint8_t* sb, uint32_t u0, const uint8_t* xb, const float* fs,
+                                       const float* xsum, const Lane& L, int lane, float wt, float& acc0,
+                                       float& acc1) {
+    float c0[4], c1[4];
+    q4k_row_scales(*reinterpret_cast<const uint4*>(sb + 2560 + L.g8 * 16), L, wt, xsum + 2 * u0, c0, acc0);
+    q4k_row_scales(*reinterpret_cast<const uint4*>(sb + 2560 + (L.g8 + 8) * 16), L, wt, xsum + 2 * u0, c1, acc1);
+    const uint4 H = *reinterpret_cast<const uint4*>(sb + 2048 + lane * 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t u = u0 + j;
+        const uint4 A = *reinterpret_cast<const uint4*>(sb + j * 512 + lane * 16);
+        const uint2 B = load_b(xb, u, L);
+        int d[4] = {0, 0, 0, 0};
+        mma_u8s8(d, q5_lo(A.x, H.x, 2 * j), q5_lo(A.y, H.y, 2 * j), q5_hi(A.x, H.x, 2 * j + 1),
+                 q5_hi(A.y, H.y, 2 * j + 1), B.x & L.mlo, B.x & L.mhi);
+        mma_u8s8(d, q5_lo(A.z, H.z, 2 * j), q5_lo(A.w, H.w, 2 * j), q5_hi(A.z, H.z, 2 * j + 1),
+                 q5_hi(A.w, H.w, 2 * j + 1), B.y & L.mlo, B.y & L.mhi);
+        const float f = fs[2 * u + L.part];
+        acc0 = fmaf(c0[j] * f, (float)(d[0] + 256 * d[1]), acc0);
+        acc1 = fmaf(c1[j] * f, (float)(d[2] + 256 * d[3]), acc1);
+    }
+}
+
 // Q6_K: one super-block of 16 rows. Step (unit j = 2H + jj, half h) holds the values
 // 128H + 32kq + 16h + l', kq = 2jj (part 0) and 2jj + 1 (part 1), i.e. sub-blocks
 // 4j + h and 4j + 2 + h; q = 6-bit value (u8), the -32 offset is taken off the integer
@@ -680,7 +713,7 @@ template <uint32_t T>
 __device__ __forceinline__ bool consume_rows(const Plan& p, const Ring& r, const uint8_t* xs, RingPos& rp,
                                              uint32_t slab, uint32_t sbw, const Lane& L, int lane,
                                              volatile int* abort_flag, float& acc0, float& acc1) {
-    constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q6_K ? 840u : 1088u;
+    constexpr uint32_t u16 = T == GGML_Q4_K ? 576u : T == GGML_Q5_K ? 704u : T == GGML_Q6_K ? 840u : 1088u;
     const uint8_t* xb = xs;
     const float* fscale = reinterpret_cast<const float*>(xs + p.off_fscale);
     // limb weight of this lane's D columns (and the 16x of Q4_K high nibbles)
@@ -695,6 +728,8 @@ __device__ __forceinline__ bool consume_rows(const Plan& p, const Ring& r, const
         if (ub < U) {
             if constexpr (T == GGML_Q4_K) {
                 sb_q4k(q, u0, xb, fscale, reinterpret_cast<const float*>(xs + p.off_xsum), L, lane, wt, acc0, acc1);
+            } else if constexpr (T == GGML_Q5_K) {
+                sb_q5k(q, u0, xb, fscale, reinterpret_cast<const float*>(xs + p.off_xsum), L, lane, wt, acc0, acc1);
             } else if constexpr (T == GGML_Q6_K) {
                 sb_q6k(q, u0, xb, fscale, reinterpret_cast<const int*>(xs + p.off_msum), L, lane, wt, acc0, acc1);
             } else {
@@ -762,6 +797,7 @@ __device__ bool consume_items(const Plan& p, const Ring& r, uint8_t* xs, uint32_
         bool ok;
         switch (sg.m.type) {
             case GGML_Q4_K: ok = consume_rows<GGML_Q4_K>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1); break;
+            case GGML_Q5_K: ok = consume_rows<GGML_Q5_K>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1); break;
             case GGML_Q6_K: ok = consume_rows<GGML_Q6_K>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1); break;
             default: ok = consume_rows<GGML_Q8_0>(p, r, xs, rp, slab, sbw, L, lane, abort_flag, acc0, acc1);
         }
@@ -817,12 +853,12 @@ __host__ cudaError_t plan_matvec(const MatvecArgs& a, Plan& p) {
         if (i < a.nseg) {
             const MatvecSeg& sg = a.seg[i];
             const uint32_t t = sg.m.type;
-            if (t != GGML_Q4_K && t != GGML_Q6_K && t != GGML_Q8_0) return cudaErrorInvalidValue;
+            if (t != GGML_Q4_K && t != GGML_Q5_K && t != GGML_Q6_K && t != GGML_Q8_0) return cudaErrorInvalidValue;
             if (sg.m.cols != a.cols || sg.m.rows == 0 || sg.m.row_bytes == 0 || !sg.y) return cudaErrorInvalidValue;
             if (sg.epi == EPI_SWIGLU && (sg.m2.type != t || sg.m2.rows != sg.m.rows || sg.m2.cols != a.cols))
                 return cudaErrorInvalidValue;
             if (t == GGML_Q6_K) p.need |= NEED_MSUM;
-            if (t == GGML_Q4_K) p.need |= NEED_XSUM;
+            if (t == GGML_Q4_K || t == GGML_Q5_K) p.need |= NEED_XSUM;
             slot = std::max(slot, 2 * panel_bytes(t, kPanelUnits));
             const uint32_t per = sg.epi == EPI_SWIGLU ? kRB / 2 : kRB;
             rbs = (sg.m.rows + per - 1) / per;

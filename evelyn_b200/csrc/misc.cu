@@ -142,7 +142,119 @@ __global__ void argmax_final_kernel(const float* part_v, const int32_t* part_i, 
     pdl_launch_dependents();
 }
 
+// ---- sampling (src/server.rs:326-352, sample_token): max, f32 weights exp((v - max) / T)
+// summed in f64, one xorshift64* draw, the first index whose running sum reaches
+// draw * total. The sum runs in parts (a fixed order, so a result never changes from
+// run to run); its rounding can differ from the reference's left-to-right f64 sum only
+// in the last bits, which moves the pick only when the draw lands within that of a
+// boundary between two tokens.
+
+// grid (parts, batch), block 256: per part the maximum (f32::max: NaN ignored)
+__global__ void sample_max_kernel(const float* __restrict__ logits, uint32_t n, float* part_m) {
+    const uint32_t b = blockIdx.y, parts = gridDim.x, per = (n + parts - 1) / parts;
+    const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
+    const float* lb = logits + (uint64_t)b * n;
+    float m = -INFINITY;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, lb[i]);
+    m = warp_max(m);
+    __shared__ float sm[8];
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float r = sm[0];
+        for (uint32_t w = 1; w < blockDim.x / 32; ++w) r = fmaxf(r, sm[w]);
+        part_m[b * parts + blockIdx.x] = r;
+    }
+}
+
+__device__ __forceinline__ float seq_max(const float* part_m, uint32_t b, uint32_t parts) {
+    float m = -INFINITY;
+    for (uint32_t p = 0; p < parts; ++p) m = fmaxf(m, part_m[b * parts + p]);
+    return m;
+}
+__device__ __forceinline__ double sample_weight(float v, float maximum, float temperature) {
+    return (double)expf(__fdiv_rn(__fsub_rn(v, maximum), temperature));
+}
+
+// grid (parts, batch), block 256: per part the f64 sum of the weights (fixed tree order)
+__global__ void sample_sum_kernel(const float* __restrict__ logits, uint32_t n, const float* part_m, float temperature,
+                                  double* part_s) {
+    const uint32_t b = blockIdx.y, parts = gridDim.x, per = (n + parts - 1) / parts;
+    const uint32_t lo = blockIdx.x * per, hi = min(n, lo + per);
+    const float* lb = logits + (uint64_t)b * n;
+    const float maximum = seq_max(part_m, b, parts);
+    double s = 0.0;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) s += sample_weight(lb[i], maximum, temperature);
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __shared__ double sd[8];
+    if ((threadIdx.x & 31) == 0) sd[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double r = 0.0;
+        for (uint32_t w = 0; w < blockDim.x / 32; ++w) r += sd[w];
+        part_s[b * parts + blockIdx.x] = r;
+    }
+}
+
+// grid (batch), block 32: the draw, the part holding the threshold, then the index
+// inside it (32 weights at a time, an f64 scan across the lanes); the greedy pick
+// `argmax[b]` when the total is not finite and positive or nothing reaches the draw.
+__global__ void sample_pick_kernel(const float* __restrict__ logits, uint32_t n, const float* part_m,
+                                   const double* part_s, uint32_t parts, float temperature, uint64_t* rng,
+                                   const int32_t* argmax, int32_t* out) {
+    const uint32_t b = blockIdx.x, lane = threadIdx.x;
+    const float* lb = logits + (uint64_t)b * n;
+    const float maximum = seq_max(part_m, b, parts);
+    double total = 0.0;
+    for (uint32_t p = 0; p < parts; ++p) total += part_s[b * parts + p];
+    int32_t pick = argmax[b];
+    if (isfinite(total) && total > 0.0) {
+        uint64_t x = rng[b];
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        __syncwarp();
+        if (lane == 0) rng[b] = x;
+        const double unit = (double)((x * 0x2545F4914F6CDD1Dull) >> 11) / 9007199254740992.0;  // / 2^53
+        const double threshold = unit * total;
+        double cum = 0.0;
+        uint32_t p = 0;
+        for (; p < parts; ++p) {
+            if (cum + part_s[b * parts + p] >= threshold) break;
+            cum += part_s[b * parts + p];
+        }
+        if (p < parts) {
+            const uint32_t per = (n + parts - 1) / parts, lo = p * per, hi = min(n, lo + per);
+            for (uint32_t i0 = lo; i0 < hi; i0 += 32) {
+                const uint32_t i = i0 + lane;
+                double w = i < hi ? sample_weight(lb[i], maximum, temperature) : 0.0;
+                for (int o = 1; o < 32; o <<= 1) {  // inclusive scan
+                    const double t = __shfl_up_sync(0xffffffffu, w, o);
+                    if (lane >= (uint32_t)o) w += t;
+                }
+                const unsigned hit = __ballot_sync(0xffffffffu, i < hi && cum + w >= threshold);
+                if (hit) {
+                    pick = (int32_t)(i0 + __ffs(hit) - 1);
+                    break;
+                }
+                cum += __shfl_sync(0xffffffffu, w, 31);
+            }
+        }
+    }
+    if (lane == 0) out[b] = pick;
+}
+
 }  // namespace
+
+cudaError_t launch_sample(const float* logits, uint32_t n, uint32_t batch, float temperature, uint64_t* rng,
+                          const int32_t* argmax, float* part_m, double* part_s, uint32_t parts, int32_t* out,
+                          cudaStream_t s) {
+    if (!parts || !batch) return cudaErrorInvalidValue;
+    sample_max_kernel<<<dim3(parts, batch), 256, 0, s>>>(logits, n, part_m);
+    sample_sum_kernel<<<dim3(parts, batch), 256, 0, s>>>(logits, n, part_m, temperature, part_s);
+    sample_pick_kernel<<<batch, 32, 0, s>>>(logits, n, part_m, part_s, parts, temperature, rng, argmax, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t batch, float* x, int32_t* err,
                          cudaStream_t s, bool pdl) {

@@ -18,6 +18,7 @@ void repack_sizes(QMatrix& m) {
     const uint64_t cols = m.cols;
     switch (m.type) {
         case GGML_Q4_K:
+        case GGML_Q5_K:
         case GGML_Q6_K:
             if (cols % 256) raise(EVL_ERR_INVALID_DATA, m.name + ": row length is not a multiple of 256");
             break;
@@ -59,6 +60,13 @@ void repack_rows(const QMatrix& m, const uint8_t* raw, size_t stride, uint8_t* d
                     const uint8_t* blk = src + (size_t)b * 144;
                     put(b, 0, blk, 16);
                     for (uint32_t o = 16; o < 144; o += 4) put(b, o, blk + o, 4);
+                }
+                break;
+            case GGML_Q5_K:
+                for (uint32_t b = 0; b < m.cols / 256; ++b) {
+                    const uint8_t* blk = src + (size_t)b * 176;
+                    put(b, 0, blk, 16);
+                    for (uint32_t o = 16; o < 176; o += 4) put(b, o, blk + o, 4);
                 }
                 break;
             case GGML_Q6_K:

@@ -12,6 +12,7 @@
 // (runtime.rs:801-804) break the graph: the step then runs eagerly and crosses to
 // the host only at those layers.
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -47,11 +48,12 @@ Decoder::~Decoder() {
     }
 }
 
-void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
+void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* share_kv) {
     model = m;
     const Config& c = m->cfg;
     if (batch == 0) raise(EVL_ERR_INVALID_INPUT, "batch must be at least 1");
     if (max_ctx == 0) raise(EVL_ERR_INVALID_INPUT, "max_ctx must be at least 1");
+    prefill_child = share_kv != nullptr;
     b.batch = batch;
     b.max_ctx = max_ctx;
     b.pages_per_seq = (max_ctx + kPageSize - 1) / kPageSize;
@@ -61,15 +63,27 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
     const uint64_t layer_stride = 2ull * m->lkv_heads * head_stride;
     const uint64_t page_stride = L * layer_stride;
     const uint64_t pages = (uint64_t)batch * b.pages_per_seq;
-    b.kv.alloc(pages * page_stride);
-    kv.pool = b.kv.p;
-    kv.page_stride = page_stride;
-    kv.layer_stride = layer_stride;
-    kv.head_stride = head_stride;
-    kv.v_offset = (int64_t)(m->lkv_heads * head_stride);
-    kv.page_size = kPageSize;
-    kv.elem_bytes = (uint32_t)elem;
-    {  // every sequence owns a contiguous run of pages
+    if (share_kv) {
+        // the prompt rows of a prefill write and read their session's cache; every row's
+        // page table starts as the session's (identity) one
+        kv = share_kv->kv;
+        b.pages_per_seq = share_kv->b.pages_per_seq;
+        std::vector<int32_t> pt((uint64_t)batch * b.pages_per_seq);
+        for (uint64_t i = 0; i < pt.size(); ++i) pt[i] = (int32_t)(i % b.pages_per_seq);
+        b.page_table.alloc(pt.size() * 4);
+        cuda_check(cudaMemcpy(b.page_table.p, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice), "page table");
+    } else {
+        // a single sequence keeps one spare page past its own: a prefill's padding rows
+        // write there
+        b.kv.alloc((pages + (batch == 1 ? 1 : 0)) * page_stride);
+        kv.pool = b.kv.p;
+        kv.page_stride = page_stride;
+        kv.layer_stride = layer_stride;
+        kv.head_stride = head_stride;
+        kv.v_offset = (int64_t)(m->lkv_heads * head_stride);
+        kv.page_size = kPageSize;
+        kv.elem_bytes = (uint32_t)elem;
+        // every sequence owns a contiguous run of pages
         std::vector<int32_t> pt(pages);
         for (uint64_t i = 0; i < pages; ++i) pt[i] = (int32_t)i;
         b.page_table.alloc(pages * 4);
@@ -110,7 +124,9 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx) {
         const char* fe = std::getenv("EVELYN_FUSED_ATTN");
         const char* me = std::getenv("EVELYN_ATTN_MMA");
         const bool mma_ok = elem == 2 && !(me && me[0] == '0');
-        if ((batch == 1 || mma_ok) && !(fe && fe[0] == '0')) {
+        // (a prefill's rows append before any of them reads: the split kernels, whose
+        // append is a launch of its own)
+        if ((batch == 1 || mma_ok) && !(fe && fe[0] == '0') && !prefill_child) {
             // one sequence: 8 splits per kv head; a batch: as few as keep ~2 CTAs per SM busy
             uint32_t C = 8;
             while (C > 1 && m->lkv_heads * batch * C > 2u * (uint32_t)sms) C /= 2;
@@ -867,6 +883,107 @@ void Decoder::step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* lo
     for (auto& p : host_pos) ++p;
     if (logits_out) std::memcpy(logits_out, b.h_logits.p, (size_t)b.batch * c.vocab * 4);
     if (argmax_out) std::memcpy(argmax_out, b.h_argmax.p, b.batch * 4);
+}
+
+// Prompt processing in chunks of kPrefillRows tokens: each chunk is one batched step of
+// a child decoder whose rows are the chunk's positions of this (single) sequence -- the
+// same kernels as a batch, the products on the tensor cores with the prompt tokens as
+// the N dimension, every row's K/V appended before any row attends, and row i attending
+// positions [0, p0 + i] of this session's cache. Equal to n Session::step calls
+// (src/runtime.rs:773-808, fed one token at a time by src/bin/evelyn-generate.rs:69-80)
+// up to the products' summation order.
+void Decoder::prefill(const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out) {
+    constexpr uint32_t kPrefillRows = 32;
+    Model& m = *model;
+    const Config& c = m.cfg;
+    DeviceGuard g(m.device);
+    if (b.batch != 1) raise(EVL_ERR_INVALID_INPUT, "prefill feeds a single sequence");
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= c.vocab)
+            raise(EVL_ERR_INVALID_INPUT, "token ID " + std::to_string(tokens[i]) + " is outside model vocabulary (" +
+                                             std::to_string(c.vocab) + "); check that tokenizer and GGUF match");
+    if (host_pos[0] + n > b.max_ctx)
+        raise(EVL_ERR_INVALID_INPUT, "session context is full (" + std::to_string(b.max_ctx) + " positions)");
+    if (n == 0) return;
+    if (!pf) {
+        auto child = std::make_unique<Decoder>();
+        child->init(&m, kPrefillRows, b.max_ctx, this);
+        if (!child->use_gemm) raise(EVL_ERR_UNSUPPORTED, "prefill needs the tensor-core products for this model");
+        pf = std::move(child);
+    }
+    Decoder& P = *pf;
+    const uint32_t C = P.b.batch, pps = b.pages_per_seq;
+    const int32_t spare = (int32_t)pps;  // the page past this sequence's own
+    std::vector<int32_t> pt((uint64_t)C * pps);
+    uint32_t rows_set = C;  // rows whose page table is the session's
+    for (size_t off = 0; off < n; off += C) {
+        const uint32_t nr = (uint32_t)std::min<size_t>(C, n - off);
+        int32_t* tok = P.b.h_tokens.as<int32_t>();
+        std::vector<int32_t> pos(C);
+        for (uint32_t i = 0; i < C; ++i) {
+            tok[i] = i < nr ? (int32_t)tokens[off + i] : 0;
+            pos[i] = i < nr ? (int32_t)(host_pos[0] + off + i) : 0;
+        }
+        if (nr != rows_set) {  // padding rows append into the spare page and read only it
+            for (uint32_t i = 0; i < C; ++i)
+                for (uint32_t j = 0; j < pps; ++j) pt[(uint64_t)i * pps + j] = i < nr ? (int32_t)j : spare;
+            cuda_check(cudaMemcpyAsync(P.b.page_table.p, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, P.stream),
+                       "page table");
+            rows_set = nr;
+        }
+        cuda_check(cudaMemcpyAsync(P.b.tokens.p, tok, C * 4, cudaMemcpyHostToDevice, P.stream), "H2D tokens");
+        cuda_check(cudaMemcpyAsync(P.b.pos.p, pos.data(), C * 4, cudaMemcpyHostToDevice, P.stream), "H2D positions");
+        P.launch_graph();
+        if (m.tp_size > 1 && logits_out) P.gather_peer_logits();
+        if (logits_out)
+            cuda_check(cudaMemcpyAsync(logits_out + off * c.vocab, P.b.logits.p, (size_t)nr * c.vocab * 4,
+                                       cudaMemcpyDeviceToHost, P.stream),
+                       "D2H logits");
+        if (argmax_out)
+            cuda_check(cudaMemcpyAsync(argmax_out + off, P.b.argmax.p, nr * 4, cudaMemcpyDeviceToHost, P.stream),
+                       "D2H argmax");
+        // pos/tokens must not be rewritten before this chunk's graph has read them
+        cuda_check(cudaStreamSynchronize(P.stream), "prefill chunk");
+    }
+    cuda_check(cudaMemcpyAsync(P.b.h_err.p, P.b.err.p, 4, cudaMemcpyDeviceToHost, P.stream), "D2H error flag");
+    cuda_check(cudaStreamSynchronize(P.stream), "prefill");
+    P.check_device_error();
+    host_pos[0] += n;
+    const int32_t p = (int32_t)host_pos[0];
+    cuda_check(cudaMemcpy(b.pos.p, &p, 4, cudaMemcpyHostToDevice), "position");
+}
+
+// sample_token (src/server.rs:326-352) on the last step's logits, on the device: only
+// the xorshift states and the picked tokens cross to and from the host.
+void Decoder::sample(float temperature, uint64_t* states, uint32_t* tokens_out) {
+    Model& m = *model;
+    DeviceGuard g(m.device);
+    const uint32_t B = b.batch;
+    if (temperature <= FLT_EPSILON) {  // the greedy pick; the state is not touched
+        cuda_check(cudaMemcpyAsync(b.h_argmax.p, b.argmax.p, B * 4, cudaMemcpyDeviceToHost, stream), "D2H argmax");
+        cuda_check(cudaStreamSynchronize(stream), "sample");
+        std::memcpy(tokens_out, b.h_argmax.p, B * 4);
+        return;
+    }
+    if (!b.smp_rng.p) {
+        b.smp_rng.alloc(B * 8);
+        b.smp_out.alloc(B * 4);
+        b.smp_m.alloc((uint64_t)B * b.amax_parts * 4);
+        b.smp_s.alloc((uint64_t)B * b.amax_parts * 8);
+        b.h_rng.alloc(B * 8);
+    }
+    if (m.tp_size > 1) gather_peer_logits();
+    std::memcpy(b.h_rng.p, states, B * 8);
+    cuda_check(cudaMemcpyAsync(b.smp_rng.p, b.h_rng.p, B * 8, cudaMemcpyHostToDevice, stream), "H2D rng");
+    cuda_check(launch_sample(b.logits.as<float>(), (uint32_t)m.cfg.vocab, B, temperature, b.smp_rng.as<uint64_t>(),
+                             b.argmax.as<int32_t>(), b.smp_m.as<float>(), b.smp_s.as<double>(), b.amax_parts,
+                             b.smp_out.as<int32_t>(), stream),
+               "sample");
+    cuda_check(cudaMemcpyAsync(b.h_argmax.p, b.smp_out.p, B * 4, cudaMemcpyDeviceToHost, stream), "D2H token");
+    cuda_check(cudaMemcpyAsync(b.h_rng.p, b.smp_rng.p, B * 8, cudaMemcpyDeviceToHost, stream), "D2H rng");
+    cuda_check(cudaStreamSynchronize(stream), "sample");
+    std::memcpy(tokens_out, b.h_argmax.p, B * 4);
+    std::memcpy(states, b.h_rng.p, B * 8);
 }
 
 void Decoder::generate(uint32_t token, uint32_t n, uint32_t* tokens_out) {

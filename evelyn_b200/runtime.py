@@ -123,6 +123,9 @@ SIGNATURES = {
     "evl_session_pos": (C.c_uint64, [_P]),
     "evl_session_step": (C.c_int, [_P, C.c_uint32, C.POINTER(_Backend), _F, _U32P]),
     "evl_session_generate": (C.c_int, [_P, C.c_uint32, C.c_uint32, _U32P]),
+    "evl_session_prefill": (C.c_int, [_P, _U32P, C.c_size_t, _F, _U32P]),
+    "evl_session_sample": (C.c_int, [_P, C.c_float, C.POINTER(C.c_uint64), _U32P]),
+    "evl_batch_sample": (C.c_int, [_P, C.c_float, C.POINTER(C.c_uint64), _U32P]),
     "evl_session_stream": (_P, [_P]),
     "evl_session_kernels_per_step": (C.c_uint32, [_P]),
     "evl_batch_new": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(_P)]),
@@ -473,6 +476,24 @@ class Session:
             self.fallbacks += int(keep[2].value)
         return out if logits else int(am.value)
 
+    def sample(self, temperature: float, state: int) -> tuple[int, int]:
+        """server.rs:326-352 on the device from the last step's logits: returns (token,
+        new xorshift64* state); temperature <= FLT_EPSILON is the greedy pick."""
+        st = C.c_uint64(state)
+        tok = C.c_uint32()
+        _check(lib().evl_session_sample(self._h, float(temperature), C.byref(st), C.byref(tok)))
+        return int(tok.value), int(st.value)
+
+    def prefill(self, tokens, logits: bool = False):
+        """Feed a prompt in batched steps (as len(tokens) step calls would); returns the
+        per-position logits [n][vocab] when logits=True, else the per-position argmax."""
+        t = np.ascontiguousarray(np.asarray(list(tokens), dtype=np.uint32))
+        am = np.empty(max(1, t.size), dtype=np.uint32)
+        out = np.empty((t.size, self.model.cfg.vocab), dtype=np.float32) if logits else None
+        _check(lib().evl_session_prefill(self._h, t.ctypes.data_as(_U32P), t.size,
+                                         _fp(out) if logits else None, am.ctypes.data_as(_U32P)))
+        return out if logits else [int(v) for v in am[:t.size]]
+
     def generate(self, token: int, n: int) -> list[int]:
         """Greedy decode on the device: feeds `token`, then each step's argmax (n steps)."""
         out = np.empty(max(1, n), dtype=np.uint32)
@@ -513,3 +534,13 @@ class Batch:
         _check(lib().evl_batch_step(self._h, t.ctypes.data_as(_U32P), _fp(out) if logits else None,
                                     am.ctypes.data_as(_U32P)))
         return out if logits else am
+
+    def sample(self, temperature: float, states):
+        """Session.sample for every sequence: returns (tokens, new states)."""
+        st = np.ascontiguousarray(np.asarray(states, dtype=np.uint64))
+        if st.size != self.n:
+            raise EvelynError(1, f"expected {self.n} states, got {st.size}")
+        tok = np.empty(self.n, dtype=np.uint32)
+        _check(lib().evl_batch_sample(self._h, float(temperature), st.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                      tok.ctypes.data_as(_U32P)))
+        return [int(v) for v in tok], [int(v) for v in st]

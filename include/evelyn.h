@@ -143,6 +143,23 @@ evl_status evl_session_step(evl_session* s, uint32_t token, const evl_ffn_backen
  * feeds `token`, then n-1 times the argmax of the previous step; tokens_out[i] is the
  * argmax after step i (n entries, host). Dense FFN on every layer. */
 evl_status evl_session_generate(evl_session* s, uint32_t token, uint32_t n, uint32_t* tokens_out);
+/* Prompt processing: feeds tokens[0 .. n) as n evl_session_step calls would (the loop
+ * of src/bin/evelyn-generate.rs:69-80, one Session::step per prompt token), but in
+ * batched steps of up to 32 prompt positions whose products run on the tensor cores.
+ * logits_out ([n][vocab], host) and argmax_out ([n], host) are each optional: row i is
+ * what step i would have returned. Dense FFN on every layer. Under tensor parallelism
+ * every rank makes the same call. */
+evl_status evl_session_prefill(evl_session* s, const uint32_t* tokens, size_t n, float* logits_out,
+                               uint32_t* argmax_out);
+/* sample_token (src/server.rs:326-352) on the device, from the logits of the session's
+ * last step, so the logits never cross to the host: temperature <= FLT_EPSILON gives
+ * the step's greedy pick and leaves *rng_state alone; otherwise *rng_state (the
+ * xorshift64* state the caller keeps per request, host in/out) advances once and
+ * *token_out (host) is the first index whose running sum of exp((v - max) / T)
+ * reaches the draw times the total (the greedy pick if the total is not finite and
+ * positive). Feeding the token and stopping at the model's eos_token_id
+ * (server.rs:514-519) stay with the caller. */
+evl_status evl_session_sample(evl_session* s, float temperature, uint64_t* rng_state, uint32_t* token_out);
 /* Device CUDA stream the session launches on (cudaStream_t), for event timing. */
 void* evl_session_stream(evl_session* s);
 /* Number of engine kernels one dense step launches (known after the first step). */
@@ -157,6 +174,9 @@ uint64_t evl_batch_pos(const evl_batch* b, uint32_t seq);
 /* tokens[n_seqs] (host) in; logits_out [n_seqs][vocab] and argmax_out [n_seqs], both optional (host). */
 evl_status evl_batch_step(evl_batch* b, const uint32_t* tokens, float* logits_out, uint32_t* argmax_out);
 void* evl_batch_stream(evl_batch* b);
+/* evl_session_sample for every sequence of a batch: rng_states[n_seqs] (host in/out),
+ * tokens_out[n_seqs] (host). */
+evl_status evl_batch_sample(evl_batch* b, float temperature, uint64_t* rng_states, uint32_t* tokens_out);
 
 /* ------------------------------------------------------------------ kernels on caller buffers */
 /* dequantize (src/gguf.rs:338-430) of raw GGUF blocks: d_raw holds type_bytes(type, n)

@@ -1034,6 +1034,34 @@ uint32_t orc_argmax(const float* v, size_t n) {  // runtime.rs:897-905: strict '
     return (uint32_t)bi;
 }
 
+// server.rs:326-352 (sample_token): temperature <= f32::EPSILON -> argmax; else the f32
+// weights exp((v - max) / T) summed in f64 in index order, one xorshift64* draw of 53
+// bits, and the first index whose running f64 sum reaches draw * total (argmax when the
+// total is not finite and positive, or no index reaches it).
+uint32_t orc_sample_token(const float* logits, size_t n, float temperature, uint64_t* state) {
+    if (temperature <= 1.1920929e-7f) return orc_argmax(logits, n);
+    float maximum = -INFINITY;
+    for (size_t i = 0; i < n; ++i) maximum = std::fmax(maximum, logits[i]);  // f32::max ignores NaN
+    std::vector<double> w(n);
+    for (size_t i = 0; i < n; ++i) w[i] = (double)std::exp((logits[i] - maximum) / temperature);
+    double total = 0.0;
+    for (size_t i = 0; i < n; ++i) total += w[i];
+    if (!std::isfinite(total) || total <= 0.0) return orc_argmax(logits, n);
+    uint64_t x = *state;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *state = x;
+    const double unit = (double)((x * 0x2545F4914F6CDD1Dull) >> 11) / (double)(1ull << 53);
+    const double threshold = unit * total;
+    double cumulative = 0.0;
+    for (size_t i = 0; i < n; ++i) {
+        cumulative += w[i];
+        if (cumulative >= threshold) return (uint32_t)i;
+    }
+    return orc_argmax(logits, n);
+}
+
 float orc_log_prob(const float* logits, size_t n, uint32_t target) {  // runtime.rs:908-912
     float mx = -3.40282347e38f;
     for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, logits[i]);

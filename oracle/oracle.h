@@ -74,6 +74,7 @@ int orc_session_fill_kv(orc_session* s, uint64_t n, uint64_t seed);
 /* runtime.rs:125, :897, :908 */
 int orc_validate_token_ids(const uint32_t* ids, size_t n, size_t vocab);
 uint32_t orc_argmax(const float* v, size_t n);
+uint32_t orc_sample_token(const float* logits, size_t n, float temperature, uint64_t* state);
 float orc_log_prob(const float* logits, size_t n, uint32_t target);
 
 #ifdef __cplusplus

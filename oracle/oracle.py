@@ -85,6 +85,8 @@ def lib():
         L.orc_validate_token_ids.argtypes = [C.POINTER(C.c_uint32), C.c_size_t, C.c_size_t]
         L.orc_argmax.restype = C.c_uint32
         L.orc_argmax.argtypes = [f, C.c_size_t]
+        L.orc_sample_token.restype = C.c_uint32
+        L.orc_sample_token.argtypes = [f, C.c_size_t, C.c_float, C.POINTER(C.c_uint64)]
         L.orc_log_prob.restype = C.c_float
         L.orc_log_prob.argtypes = [f, C.c_size_t, C.c_uint32]
         _lib = L
@@ -135,6 +137,14 @@ def validate_token_ids(ids, vocab: int):
 def argmax(v: np.ndarray) -> int:
     v = np.ascontiguousarray(v, dtype=np.float32)
     return int(lib().orc_argmax(_fp(v), v.size))
+
+
+def sample_token(logits: np.ndarray, temperature: float, state: int) -> tuple[int, int]:
+    """server.rs:326-352; returns (token, new xorshift state)."""
+    v = np.ascontiguousarray(logits, dtype=np.float32)
+    st = C.c_uint64(state)
+    tok = lib().orc_sample_token(_fp(v), v.size, temperature, C.byref(st))
+    return int(tok), int(st.value)
 
 
 def log_prob(logits: np.ndarray, target: int) -> float:

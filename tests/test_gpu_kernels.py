@@ -59,7 +59,7 @@ def _qmatrix(t, rows, cols, raw):
 SHAPES = [(1, 256), (37, 768), (64, 4096), (33, 2304), (130, 12288 // 4)]
 
 
-@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q6_K, synth.GGML_F16,
+@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K, synth.GGML_F16,
                                synth.GGML_BF16, synth.GGML_F32])
 @pytest.mark.parametrize("rows,cols", SHAPES)
 def test_repack_round_trip_bit_exact(t, rows, cols):
@@ -79,7 +79,7 @@ def test_repack_round_trip_bit_exact(t, rows, cols):
         runtime.lib().evl_qmatrix_free(h)
 
 
-@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q6_K])
+@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K])
 @pytest.mark.parametrize("rows,cols", SHAPES + [(4096, 4096), (1000, 12288)])
 def test_qmatrix_matvec(t, rows, cols):
     """y = W x against the oracle's sequential f32 dot; tolerance: 5e-5 of sum|w*x| (f32 reordering)."""

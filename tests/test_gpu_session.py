@@ -25,13 +25,13 @@ def _tokens(n, vocab, seed=0):
 
 
 @pytest.mark.parametrize("kv_f32", [False, True])
-@pytest.mark.parametrize("mix", ["q4k_mix", "q8_0", "q6k"])
+@pytest.mark.parametrize("mix", ["q4k_mix", "q8_0", "q6k", "q5k"])
 def test_step_logits_match_oracle(mix, kv_f32):
     spec = synth.tiny(seed=11)
     if mix == "q8_0":
         spec = spec.with_types(synth.GGML_Q8_0)
-    elif mix == "q6k":
-        spec = spec.with_types(synth.GGML_Q6_K)
+    elif mix in ("q6k", "q5k"):
+        spec = spec.with_types(synth.GGML_Q6_K if mix == "q6k" else synth.GGML_Q5_K)
         spec.embed = spec.output = synth.GGML_Q8_0
     img, m, r = _models(spec, kv_f32)
     s, rs = evl.Session(m, max_ctx=256), orc.Session(r)

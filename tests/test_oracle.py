@@ -154,3 +154,41 @@ def test_oracle_ffn_hook_and_dense_ffn():
     for tok in [3, 9, 27]:
         assert np.array_equal(a.step(tok, hook), b.step(tok))
     assert calls == [0, 1] * 3
+
+
+def _sample_py(logits, temperature, state):
+    """src/server.rs:326-352 in plain Python (float32 weights summed in float64)."""
+    if temperature <= np.finfo(np.float32).eps:
+        return orc.argmax(logits), state
+    lf = np.asarray(logits, dtype=np.float32)
+    mx = np.float32(np.max(lf))
+    w = np.exp((lf - mx) / np.float32(temperature)).astype(np.float64)
+    total = 0.0
+    for v in w:
+        total += float(v)
+    mask = (1 << 64) - 1
+    x = state
+    x ^= x >> 12
+    x ^= (x << 25) & mask
+    x ^= x >> 27
+    unit = (((x * 0x2545F4914F6CDD1D) & mask) >> 11) / float(1 << 53)
+    threshold = unit * total
+    cum = 0.0
+    for i, v in enumerate(w):
+        cum += float(v)
+        if cum >= threshold:
+            return i, x
+    return orc.argmax(logits), x
+
+
+def test_sample_token_restatement():
+    """The oracle's sample_token against a plain-Python restatement: same tokens, same
+    xorshift64* states (exact integers), temperature 0 leaves the state alone."""
+    rng = np.random.default_rng(0)
+    for temperature in (0.0, 0.3, 1.0, 2.5):
+        state = 12345
+        for _ in range(20):
+            logits = (rng.standard_normal(500) * 3).astype(np.float32)
+            got = orc.sample_token(logits, temperature, state)
+            assert got == _sample_py(logits, temperature, state)
+            state = got[1]
