@@ -71,6 +71,7 @@ public:
 
     void resize(int n) {
         if (n < 1) n = 1;
+        std::lock_guard<std::mutex> job_lock(job_mu_);
         stop();
         quit_ = false;
         nthreads_ = n;
@@ -78,50 +79,58 @@ public:
     }
     int size() const { return nthreads_; }
 
+    // Each call owns its task counters; a worker joins a job only while holding mu_
+    // and while the job is published, and run() returns only after every worker that
+    // joined has left it, so no worker can carry an index or the task function of one
+    // job into the next.
     void run(size_t ntasks, const std::function<void(size_t)>& fn) {
         if (ntasks == 0) return;
         if (nthreads_ == 1 || ntasks == 1) {
             for (size_t t = 0; t < ntasks; ++t) fn(t);
             return;
         }
-        std::unique_lock<std::mutex> job_lock(job_mu_);  // one parallel job at a time
+        std::lock_guard<std::mutex> job_lock(job_mu_);  // one parallel job at a time
+        Job job{&fn, ntasks};
         {
             std::lock_guard<std::mutex> g(mu_);
-            fn_ = &fn;
-            ntasks_ = ntasks;
-            next_.store(0);
-            done_.store(0);
+            job_ = &job;
             ++gen_;
         }
         cv_.notify_all();
-        work();
+        job.work();
         std::unique_lock<std::mutex> g(mu_);
-        done_cv_.wait(g, [&] { return done_.load() == ntasks_; });
-        fn_ = nullptr;
+        job_ = nullptr;  // no worker joins from here on
+        done_cv_.wait(g, [&] { return job.active == 0; });
     }
 
 private:
-    void work() {
-        for (;;) {
-            size_t t = next_.fetch_add(1);
-            if (t >= ntasks_) break;
-            (*fn_)(t);
-            if (done_.fetch_add(1) + 1 == ntasks_) {
-                std::lock_guard<std::mutex> g(mu_);
-                done_cv_.notify_all();
-            }
+    struct Job {
+        const std::function<void(size_t)>* fn;
+        size_t ntasks;
+        std::atomic<size_t> next{0};
+        int active = 0;  // workers inside work(), guarded by the pool's mu_
+        Job(const std::function<void(size_t)>* f, size_t n) : fn(f), ntasks(n) {}
+        void work() {
+            for (size_t t = next.fetch_add(1); t < ntasks; t = next.fetch_add(1)) (*fn)(t);
         }
-    }
+    };
+
     void loop() {
         uint64_t seen = 0;
         for (;;) {
+            Job* job;
             {
                 std::unique_lock<std::mutex> g(mu_);
                 cv_.wait(g, [&] { return quit_ || gen_ != seen; });
                 if (quit_) return;
                 seen = gen_;
+                job = job_;
+                if (!job) continue;  // woke after that job was already finished
+                ++job->active;
             }
-            work();
+            job->work();
+            std::lock_guard<std::mutex> g(mu_);
+            if (--job->active == 0) done_cv_.notify_all();
         }
     }
     void stop() {
@@ -137,9 +146,7 @@ private:
     std::vector<std::thread> workers_;
     std::mutex mu_, job_mu_;
     std::condition_variable cv_, done_cv_;
-    const std::function<void(size_t)>* fn_ = nullptr;
-    size_t ntasks_ = 0;
-    std::atomic<size_t> next_{0}, done_{0};
+    Job* job_ = nullptr;
     uint64_t gen_ = 0;
     bool quit_ = false;
     int nthreads_ = 1;

@@ -16,6 +16,7 @@ the CPU oracle):
   reduction) and 5120x25600 Q6_K (rows longer than 12288 values: quarter staging).
 """
 import ctypes as C
+import gc
 import math
 
 import numpy as np
@@ -40,34 +41,42 @@ def _top2_margin(logits):
     return float(top[1] - top[0])
 
 
-def _generate_protocol(spec, prompt_len=16, steps=64, seed=0, kv_f32=True):
-    """Prompt (teacher-forced PPL) then greedy decode on both sides; returns the worst
-    logit difference, both PPLs and both token streams."""
-    img = synth.build(spec)
-    m = evl.Model.load_memory(img, device=0, kv_f32=kv_f32)
+def _oracle_protocol(img, spec, prompt, steps):
+    """The oracle's side of the protocol: logits at every prompt position and greedy
+    step, its teacher-forced NLL and greedy tokens."""
     r = orc.Model(img)
-    s = evl.Session(m, max_ctx=prompt_len + steps + 8)
     rs = orc.Session(r)
-    prompt = _tokens(prompt_len, spec.vocab, seed)
-    worst, nll_g, nll_o = 0.0, 0.0, 0.0
+    logits, nll = [], 0.0
     for i, tok in enumerate(prompt):
-        lg, lo = s.step(tok), rs.step(tok)
-        worst = max(worst, float(np.abs(lg - lo).max()))
+        logits.append(rs.step(tok))
         if i + 1 < len(prompt):
-            nll_g -= evl.log_prob(lg, prompt[i + 1])
-            nll_o -= orc.log_prob(lo, prompt[i + 1])
-    n = len(prompt) - 1
-    ppl_g, ppl_o = math.exp(nll_g / n), math.exp(nll_o / n)
-    tg, to = evl.argmax(lg), orc.argmax(lo)
-    out_g, out_o, margins = [], [], []
+            nll -= orc.log_prob(logits[-1], prompt[i + 1])
+    greedy = []
     for _ in range(steps):
-        out_g.append(tg)
-        out_o.append(to)
-        lg, lo = s.step(tg), rs.step(to)
-        worst = max(worst, float(np.abs(lg - lo).max()))
-        margins.append(_top2_margin(lo))
-        tg, to = evl.argmax(lg), orc.argmax(lo)
-    return worst, ppl_g, ppl_o, out_g, out_o, min(margins)
+        greedy.append(orc.argmax(logits[-1]))
+        logits.append(rs.step(greedy[-1]))
+    return logits, math.exp(nll / (len(prompt) - 1)), greedy
+
+
+def _engine_protocol(img, spec, prompt, steps, want, kv_f32):
+    """The same protocol on the device (greedy from its own argmax); returns the worst
+    logit difference from the oracle's `want`, its PPL and greedy tokens."""
+    m = evl.Model.load_memory(img, device=0, kv_f32=kv_f32)
+    s = evl.Session(m, max_ctx=len(prompt) + steps + 8)
+    worst, nll = 0.0, 0.0
+    for i, tok in enumerate(prompt):
+        lg = s.step(tok)
+        worst = max(worst, float(np.abs(lg - want[i]).max()))
+        if i + 1 < len(prompt):
+            nll -= evl.log_prob(lg, prompt[i + 1])
+    greedy = []
+    for j in range(steps):
+        greedy.append(evl.argmax(lg))
+        lg = s.step(greedy[-1])
+        worst = max(worst, float(np.abs(lg - want[len(prompt) + j]).max()))
+    del s, m
+    gc.collect()
+    return worst, math.exp(nll / (len(prompt) - 1)), greedy
 
 
 # f16 KV pages round every cached K and V element to 11 bits, which the f32 reference
@@ -78,14 +87,20 @@ F16_KV_LOGIT_TOL = 2e-2
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("kv_f32", [True, False], ids=["kv_f32", "kv_f16"])
 @pytest.mark.parametrize("shape", ["qwen3_0_6b", "qwen3_8b"])
-def test_benchmark_shape_generate_matches_oracle(shape, kv_f32):
+def test_benchmark_shape_generate_matches_oracle(shape):
+    """16 prompt tokens (teacher-forced PPL) then 64 greedy steps, the oracle once and
+    the engine with f32 KV pages and with f16 KV pages."""
     spec = getattr(synth, shape)(seed=0)
-    worst, ppl_g, ppl_o, out_g, out_o, margin = _generate_protocol(spec, kv_f32=kv_f32)
-    assert worst <= (LOGIT_TOL if kv_f32 else F16_KV_LOGIT_TOL), worst
-    assert abs(ppl_g / ppl_o - 1) < 0.005, (ppl_g, ppl_o)
-    assert out_g == out_o, (out_g, out_o, margin)
+    img = synth.build(spec)
+    prompt, steps = _tokens(16, spec.vocab, 0), 64
+    want, ppl_o, greedy_o = _oracle_protocol(img, spec, prompt, steps)
+    margin = min(_top2_margin(w) for w in want[len(prompt) - 1:])
+    for kv_f32, tol in ((True, LOGIT_TOL), (False, F16_KV_LOGIT_TOL)):
+        worst, ppl_g, greedy_g = _engine_protocol(img, spec, prompt, steps, want, kv_f32)
+        assert worst <= tol, (kv_f32, worst)
+        assert abs(ppl_g / ppl_o - 1) < 0.005, (kv_f32, ppl_g, ppl_o)
+        assert greedy_g == greedy_o, (kv_f32, greedy_g, greedy_o, margin)
 
 
 @pytest.mark.parametrize("heads,kv_heads", [(4, 2), (8, 2), (8, 1)])
