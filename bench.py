@@ -370,7 +370,7 @@ def run_ours(args):
             line["c1"] = c1
         if c4:
             line["c4"] = c4
-        print(json.dumps(line), flush=True)
+        emit_line(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -436,7 +436,7 @@ def run_sweep(args, emit=None):
     Each case cycles enough distinct copies to exceed L2 twice; CUDA events on one stream.
     Every case's result goes to `emit` (default: one JSON line on stdout)."""
     if emit is None:
-        emit = lambda d: print(json.dumps(d), flush=True)  # noqa: E731
+        emit = emit_line
     import torch
     from evelyn_b200 import runtime, synth
     lib = runtime.lib()
@@ -616,17 +616,31 @@ def run_reference(args):
     v = n / dt
     sample = (f"{n} of {args.steps} requested decode steps (capped at {budget:.0f}s) at ctx {PROMPT + 1}.., "
               f"synthetic KV prefix, {threads} threads")
-    print(json.dumps({
+    emit_line({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": round(dt / n * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"Qwen3-8B-shape decode bs1, ctx {PROMPT}+ (CPU, sampled)"},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+_RESULT_FD = None
+
+
+def emit_line(d):
+    """Writes one JSON result line to the process's original stdout. Everything else the
+    process prints (NCCL's version banner, library messages) goes to stderr, so stdout
+    carries the result lines only."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(d) + "\n").encode())
 
 
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1024)
