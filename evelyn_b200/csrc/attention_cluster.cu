@@ -20,7 +20,7 @@
 // the split that holds the new position appends k and v (to HBM and to its shared
 // copy), and the warps run an online softmax over the split's positions entirely out
 // of shared memory: on the tensor cores one 16-position page per warp (f16 pages), or
-// one position per warp (the scalar loop). The ring streams any number of chunks; a
+// a batch of 32 / G positions per warp (the scalar loop). The ring streams any number of chunks; a
 // warp group per ring stage. The C partials (m, l, o) of a kv head meet through
 // distributed shared memory: cluster rank 0 merges them in rank order.
 #include <cooperative_groups.h>
@@ -80,9 +80,17 @@ __device__ __forceinline__ void load_kv(const __half* p, float (&o)[N]) {
     }
 }
 template <int N>
-__device__ __forceinline__ void load_kv(const float* p, float (&o)[N]) {
+__device__ __forceinline__ void load_kv(const float* p, float (&o)[N]) {  // p: 4 N-byte aligned
+    if constexpr (N == 4) {
+        const float4 r = *reinterpret_cast<const float4*>(p);
+        o[0] = r.x; o[1] = r.y; o[2] = r.z; o[3] = r.w;
+    } else if constexpr (N == 2) {
+        const float2 r = *reinterpret_cast<const float2*>(p);
+        o[0] = r.x; o[1] = r.y;
+    } else {
 #pragma unroll
-    for (int e = 0; e < N; ++e) o[e] = p[e];
+        for (int e = 0; e < N; ++e) o[e] = p[e];
+    }
 }
 template <typename KV>
 __device__ __forceinline__ KV to_kv(float v) {
@@ -195,6 +203,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     const int32_t* ptab = a.page_table + (uint64_t)sq * a.max_pages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t ps = a.kv.page_size, tile = ps * HD;  // elements of one K (or V) page tile
+    const uint32_t lps = 31u - __clz(ps);                // ps is a power of two
     KV* ring = reinterpret_cast<KV*>(smem);                                   // [ring][K|V][ps][HD]
     float* qs = reinterpret_cast<float*>(smem + (size_t)F.ring_pages * 2 * tile * sizeof(KV));  // [G][HD]
     float* vec = qs + G * HD;                                                 // [G+2][HD] per-warp vectors
@@ -296,6 +305,10 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
 
+    // the page the new position's k and v go to (the page table is not written by the
+    // previous kernel), so the append does no dependent load after the wait
+    const int32_t apage = vw && warp >= G && last ? __ldcg(ptab + (uint32_t)pos / ps) : 0;
+
     pdl_wait();
 
     // ---- q, k, v of this kv head: norm + rope in registers
@@ -332,8 +345,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
 #pragma unroll
             for (int e = 0; e < DPL; ++e) qs[warp * HD + DPL * lane + e] = val[e];
         } else if (last) {  // KV append at pos (src/runtime.rs:721-722)
-            const int32_t page = __ldcg(ptab + (uint32_t)pos / ps);
-            KV* dst = (KV*)kv_tile(a.kv, page, r.layer, warp == G ? 0 : 1, kvh) + ((uint32_t)pos % ps) * HD;
+            KV* dst = (KV*)kv_tile(a.kv, apage, r.layer, warp == G ? 0 : 1, kvh) + ((uint32_t)pos % ps) * HD;
 #pragma unroll
             for (int e = 0; e < DPL; ++e) {
                 dst[DPL * lane + e] = to_kv<KV>(val[e]);
@@ -352,7 +364,9 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     // by shuffles). q and the weights are split into f16 hi + lo, so the products carry
     // ~22 bits like the f32 reference. Lane (g, t) holds positions g, g+8 (and head
     // dims 16i + g, +8 of O^T) of heads 2t, 2t+1.
-    float qr[G][DPL], m[G], l[G], o[G][DPL];
+    // scalar path: q and o over this lane's dimensions; the running maximum and sum of
+    // head lane / (32 / G), the same in every lane of that head
+    float qr[G][DPL], o[G][DPL], mrun = -INFINITY, lrun = 0.f;
     const uint32_t g8 = (uint32_t)lane >> 2, t4 = (uint32_t)lane & 3;
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f}, oacc[MM ? HD / 16 : 1][4];
     const bool hv0 = 2 * t4 < (uint32_t)G, hv1 = 2 * t4 + 1 < (uint32_t)G;  // real heads of this lane
@@ -375,8 +389,6 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     } else {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            m[g] = -INFINITY;
-            l[g] = 0.f;
 #pragma unroll
             for (int e = 0; e < DPL; ++e) {
                 qr[g][e] = qs[g * HD + DPL * lane + e];
@@ -478,25 +490,79 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
                 }
             }
         } else {
-            for (uint32_t t = tc0 + gw; t < tc1; t += GW) {
-                const uint32_t li = t - tc0;
-                const KV* kp = ring + (half * H + li / ps) * 2 * tile + (li % ps) * HD + DPL * lane;
-                float kf[DPL], vf[DPL];
-                load_kv<DPL>(kp, kf);
-                load_kv<DPL>(kp + tile, vf);
+            // a batch of P = 32 / G consecutive positions per warp: the G x P dot
+            // products are summed over the lanes' head dimensions by one reduce-scatter,
+            // after which lane j = g * P + p holds the score of head g at position p, so
+            // the softmax bookkeeping (maximum, two exps, sum) runs once per lane and
+            // batch; the weights return to the dimension lanes by shuffles for the V sum
+            constexpr int P = 32 / G;
+            // row li of the chunk: K at li * HD + (li / ps) * tile past the chunk's first
+            // K tile (page tiles K, V alternate), V one tile further
+            const KV* kc = ring + half * H * 2 * tile + DPL * lane;
+            const uint32_t nb = (tc1 - tc0 + P - 1) / P;
+            for (uint32_t bt = gw; bt < nb; bt += GW) {
+                const uint32_t tb = tc0 + bt * P;  // live: tb < tc1
+                float dot[32];
+#pragma unroll
+                for (int p = 0; p < P; ++p) {
+                    float kf[DPL];
+                    const uint32_t li = bt * P + p;
+                    if (tb + p < tc1) {
+                        load_kv<DPL>(kc + li * HD + (li >> lps) * tile, kf);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < DPL; ++e) kf[e] = 0.f;
+                    }
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float sc = qr[g][0] * kf[0];
+#pragma unroll
+                        for (int e = 1; e < DPL; ++e) sc = fmaf(qr[g][e], kf[e], sc);
+                        dot[g * P + p] = sc;
+                    }
+                }
+                // reduce-scatter: at offset o2 a lane keeps the half of its sums whose index
+                // bit o2 matches its own lane bit and adds its partner's copy of that half
+#pragma unroll
+                for (int o2 = 16; o2 >= 1; o2 >>= 1) {
+                    const bool up = (lane & o2) != 0;
+#pragma unroll
+                    for (int i = 0; i < o2; ++i) {
+                        const float send = up ? dot[i] : dot[i + o2];
+                        const float keep = up ? dot[i + o2] : dot[i];
+                        dot[i] = keep + __shfl_xor_sync(0xffffffffu, send, o2);
+                    }
+                }
+                const float sc = tb + (uint32_t)lane % P < tc1 ? dot[0] * a.scale : -INFINITY;
+                float bm = sc;
+#pragma unroll
+                for (int o2 = 1; o2 < P; o2 <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o2));
+                const float mn = fmaxf(mrun, bm);     // finite: position tb is live
+                const float alpha = expf(mrun - mn);  // exp(-inf) = 0 on the first batch
+                const float w = expf(sc - mn);
+                float ws = w;
+#pragma unroll
+                for (int o2 = 1; o2 < P; o2 <<= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o2);
+                lrun = lrun * alpha + ws;
+                mrun = mn;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    float sc = qr[g][0] * kf[0];
+                    const float ag = __shfl_sync(0xffffffffu, alpha, g * P);
 #pragma unroll
-                    for (int e = 1; e < DPL; ++e) sc = fmaf(qr[g][e], kf[e], sc);
-                    sc = warp_sum(sc) * a.scale;
-                    const float mn = fmaxf(m[g], sc);
-                    const float alpha = expf(m[g] - mn);  // exp(-inf) = 0 on the first position
-                    const float w = expf(sc - mn);
-                    l[g] = l[g] * alpha + w;
+                    for (int e = 0; e < DPL; ++e) o[g][e] *= ag;
+                }
 #pragma unroll
-                    for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(w, vf[e], o[g][e] * alpha);
-                    m[g] = mn;
+                for (int p = 0; p < P; ++p) {
+                    if (tb + p >= tc1) break;  // uniform over the warp
+                    const uint32_t li = bt * P + p;
+                    float vf[DPL];
+                    load_kv<DPL>(kc + tile + li * HD + (li >> lps) * tile, vf);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float wg = __shfl_sync(0xffffffffu, w, g * P + p);
+#pragma unroll
+                        for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(wg, vf[e], o[g][e]);
+                    }
                 }
             }
         }
@@ -534,9 +600,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             float* wp = wpart + (warp * G + g) * (HD + 2);
 #pragma unroll
             for (int e = 0; e < DPL; ++e) wp[DPL * lane + e] = o[g][e];
+            const float mg = __shfl_sync(0xffffffffu, mrun, g * (32 / G));
+            const float lg = __shfl_sync(0xffffffffu, lrun, g * (32 / G));
             if (lane == 0) {
-                wp[HD] = m[g];
-                wp[HD + 1] = l[g];
+                wp[HD] = mg;
+                wp[HD + 1] = lg;
             }
         }
     }
@@ -624,6 +692,7 @@ uint32_t attention_cluster_pages(uint32_t max_pages, uint32_t nsplit, uint32_t p
     if (head_dim != 64 && head_dim != 128) return 0;
     if (group != 1 && group != 2 && group != 4 && group != 8) return 0;
     if (elem_bytes != 2 && elem_bytes != 4) return 0;
+    if (page_size & (page_size - 1)) return 0;  // the loops address rows by shifts
     // a split holds at most ceil(ceil(t / nsplit) / page) pages; longer splits stream
     // through the ring, which holds an even number of pages (two halves)
     uint32_t ring = std::min<uint32_t>(std::min<uint32_t>(kMaxRingPages, std::max<uint32_t>(cap, 2) & ~1u),
