@@ -326,6 +326,9 @@ def run_ours(args):
         model = load(img, kv_f32=False)
         bs32 = run_batch(model, spec, args, hbm, peak_kind, world)
         del model
+    c5 = None
+    if world > 1 and not args.no_c5:  # Qwen3-32B shape, bs8, tensor-parallel
+        c5 = run_c5(evl, synth, args, hbm, peak_kind, rank, world, local)
     c1 = None
     if world == 1 and not args.no_c1:  # Qwen3-0.6B shape, all Q8_0, bs1, 128 + 128
         spec1 = synth.qwen3_0_6b(seed=0)
@@ -370,24 +373,110 @@ def run_ours(args):
             line["c1"] = c1
         if c4:
             line["c4"] = c4
+        if c5:
+            line["c5"] = c5
         emit_line(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
+def prefill_batch(batch, B, P, vocab, rng, world):
+    """Every sequence's P-token random prefix through evl_batch_prefill (32-position
+    chunks on the tensor cores), host-synchronised: the prefill line."""
+    prompts = [rng.integers(0, vocab, P) for _ in range(B)]
+    barrier(world)
+    t = time.perf_counter()
+    for i in range(B):
+        batch.prefill(i, prompts[i])
+    barrier(world)
+    sec = dist_max(time.perf_counter() - t, world)
+    return {"value": round(B * P / sec, 1), "unit": "tok/s", "tokens": B * P, "seconds": round(sec, 3),
+            "note": "evl_batch_prefill per sequence, 32-position chunks, wall clock with a barrier on both sides"}
+
+
+def run_c5(evl, synth, args, hbm, peak_kind, rank, world, local):
+    """Qwen3-32B shape (Q4_K_M-style mix) tensor-parallel over the ranks: 8 sequences,
+    each prefilled with an args.c5_prompt-token random prompt, then args.c5_steps timed
+    batched greedy steps. Rank 0 builds the synthetic GGUF once and writes it to a
+    temporary file that every rank maps; any failure (disk, memory) on any rank gives
+    an "unavailable" entry on all of them."""
+    import shutil
+    import tempfile
+    import torch
+    import torch.distributed as dist
+    spec = synth.qwen3_32b(seed=0)
+    obj = [None, None]
+    if rank == 0:
+        d = None
+        try:
+            t = time.perf_counter()
+            img = synth.build(spec)
+            d = tempfile.mkdtemp(prefix="evl_c5_")
+            path = os.path.join(d, "qwen3_32b_shape.gguf")
+            img.write(path)
+            log(f"[rank 0] 32B synthetic GGUF {img.nbytes / 1e9:.2f} GB in {time.perf_counter() - t:.1f}s")
+            img.close()
+            obj = [path, None]
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            if d:
+                shutil.rmtree(d, ignore_errors=True)
+            obj = [None, f"building the 32B image: {type(e).__name__}: {e}"]
+    dist.broadcast_object_list(obj, src=0)
+    path, err = obj
+    if err:
+        return {"unavailable": err}
+    ids = [evl.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    model, err = None, None
+    try:
+        model = evl.Model.load(path, device=local, tp_rank=rank, tp_size=world, nccl_id=ids[0], kv_f32=False)
+    except Exception as e:  # noqa: BLE001
+        err = f"rank {rank} loading the 32B image: {type(e).__name__}: {e}"
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    if rank == 0:
+        shutil.rmtree(os.path.dirname(path), ignore_errors=True)
+    errs = [e for e in errs if e]
+    if errs:
+        del model
+        return {"unavailable": errs[0]}
+    B, P, K = 8, args.c5_prompt, args.c5_steps
+    bat = evl.Batch(model, B, max_ctx=P + K + 8)
+    rng = np.random.default_rng(5)
+    pf = prefill_batch(bat, B, P, spec.vocab, rng, world)
+    toks = rng.integers(0, spec.vocab, B)
+    for _ in range(3):  # warm-up
+        toks = bat.step(toks, logits=False)
+    ext = torch.cuda.ExternalStream(bat.stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(K):
+        toks = bat.step(toks, logits=False)
+    e1.record(ext)
+    e1.synchronize()
+    ms = dist_max(e0.elapsed_time(e1), world)
+    ctx0 = P + 3
+    del bat, model
+    return {"value": round(B * K / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / K, 4),
+            "global_batch": B, "parallelism": f"tp{world}",
+            "workload": f"Qwen3-32B-shape (64L, d5120, 64Q/8KV x128, ffn 25600) Q4_K_M-style mix, {B} sequences, "
+                        f"{P}-token random prompt each, then {K} greedy steps (ctx {ctx0}..{ctx0 + K}); f16 KV pages",
+            "prefill": pf, "step_hbm": step_hbm(spec, 2, ctx0, K, hbm, peak_kind, ms, batch=B, world=world)}
+
+
 def run_batch(model, spec, args, hbm, peak_kind, world=1):
     """The batched half of the metric: `args.batch` sequences decoded together after a
-    `args.batch_prefix`-token prefix each (prefilled by batch steps); K timed steps through
+    `args.batch_prefix`-token prefix each (evl_batch_prefill); K timed steps through
     evl_batch_step (tokens H2D, argmax D2H, synchronised each step)."""
     import torch
     from evelyn_b200 import runtime as evl_rt
     B, P, K = args.batch, args.batch_prefix, args.batch_steps
     batch = evl_rt.Batch(model, B, max_ctx=P + K + 8)
     rng = np.random.default_rng(1)
-    barrier(world)
-    for _ in range(P):
-        batch.step(rng.integers(0, spec.vocab, B), logits=False)
+    pf = prefill_batch(batch, B, P, spec.vocab, rng, world)
     toks = rng.integers(0, spec.vocab, B)
     for _ in range(3):  # warm-up
         toks = batch.step(toks, logits=False)
@@ -408,6 +497,7 @@ def run_batch(model, spec, args, hbm, peak_kind, world=1):
     return {"value": round(B * K / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / K, 4),
             "global_batch": B, "workload": f"{B} sequences, {P}-token prefix each, then {K} greedy steps "
                                            f"(ctx {ctx0}..{ctx0 + K}); products on tcgen05 tensor cores",
+            "prefill": pf,
             "e2e_note": "each step through evl_batch_step: token ids H2D, argmax D2H, synchronised",
             "parallelism": f"tp{world}" if world > 1 else "single GPU", "kv_cache": "paged f16, 16-token pages",
             "step_hbm": step_hbm(spec, 2, ctx0, K, hbm, peak_kind, ms, batch=B, world=world)}
@@ -656,6 +746,9 @@ def main():
     ap.add_argument("--reps", type=int, default=10, help="timed passes per sweep case")
     ap.add_argument("--no-c1", action="store_true", help="skip the Qwen3-0.6B-shape bs1 line")
     ap.add_argument("--no-c4", action="store_true", help="skip the kernel-sweep summary")
+    ap.add_argument("--no-c5", action="store_true", help="skip the Qwen3-32B-shape bs8 line (N > 1 only)")
+    ap.add_argument("--c5-prompt", type=int, default=4096, help="prompt tokens per sequence of the 32B line")
+    ap.add_argument("--c5-steps", type=int, default=64, help="timed batched steps of the 32B line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

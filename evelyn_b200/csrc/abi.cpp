@@ -399,7 +399,7 @@ evl_status evl_session_prefill(evl_session* s, const uint32_t* tokens, size_t n,
                                uint32_t* argmax_out) {
     return guarded([&] {
         require(s && (tokens || n == 0), "null argument");
-        s->d.prefill(tokens, n, logits_out, argmax_out);
+        s->d.prefill(0, tokens, n, logits_out, argmax_out);
     });
 }
 
@@ -407,6 +407,14 @@ evl_status evl_session_sample(evl_session* s, float temperature, uint64_t* rng_s
     return guarded([&] {
         require(s && rng_state && token_out, "null argument");
         s->d.sample(temperature, rng_state, token_out);
+    });
+}
+
+evl_status evl_batch_prefill(evl_batch* b, uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out,
+                             uint32_t* argmax_out) {
+    return guarded([&] {
+        require(b && (tokens || n == 0), "null argument");
+        b->d.prefill(seq, tokens, n, logits_out, argmax_out);
     });
 }
 

@@ -288,7 +288,7 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     std::string step_note;        // why the step kernel is not used, if it is not
 
     ~Decoder();
-    // share_kv: a prefill child whose rows are positions of that (single) sequence
+    // share_kv: a prefill child whose rows are positions of one sequence of that decoder
     void init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* share_kv = nullptr);
     void init_tp();  // collective over the model's ranks: inboxes, peer mappings
     MatvecArgs qkv_args(uint32_t layer) const;
@@ -319,11 +319,14 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     // Temperature sampling of every sequence from the last step's logits (host states
     // in/out, host tokens out).
     void sample(float temperature, uint64_t* states, uint32_t* tokens_out);
-    // Batched prompt processing (single sequence): n tokens, optional logits [n][vocab]
+    // Batched prompt processing of sequence `seq`: n tokens, optional logits [n][vocab]
     // and argmax [n] (host).
-    void prefill(const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out);
+    void prefill(uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out);
     std::unique_ptr<Decoder> pf;  // prefill child (made on first use)
     bool prefill_child = false;
+    // what the child's device page table holds: its rows [0, pf_rows) map sequence
+    // pf_seq's pages, the rest the spare page (pf_rows = 0: not written yet)
+    uint32_t pf_rows = 0, pf_seq = 0;
 };
 
 }  // namespace evl

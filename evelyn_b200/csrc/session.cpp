@@ -64,18 +64,14 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* sh
     const uint64_t page_stride = L * layer_stride;
     const uint64_t pages = (uint64_t)batch * b.pages_per_seq;
     if (share_kv) {
-        // the prompt rows of a prefill write and read their session's cache; every row's
-        // page table starts as the session's (identity) one
+        // the prompt rows of a prefill write and read their parent's cache; the page
+        // table is written per prefill call (Decoder::prefill)
         kv = share_kv->kv;
         b.pages_per_seq = share_kv->b.pages_per_seq;
-        std::vector<int32_t> pt((uint64_t)batch * b.pages_per_seq);
-        for (uint64_t i = 0; i < pt.size(); ++i) pt[i] = (int32_t)(i % b.pages_per_seq);
-        b.page_table.alloc(pt.size() * 4);
-        cuda_check(cudaMemcpy(b.page_table.p, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice), "page table");
+        b.page_table.alloc((uint64_t)batch * b.pages_per_seq * 4);
     } else {
-        // a single sequence keeps one spare page past its own: a prefill's padding rows
-        // write there
-        b.kv.alloc((pages + (batch == 1 ? 1 : 0)) * page_stride);
+        // one spare page past the sequences' own: a prefill's padding rows write there
+        b.kv.alloc((pages + 1) * page_stride);
         kv.pool = b.kv.p;
         kv.page_stride = page_stride;
         kv.layer_stride = layer_stride;
@@ -892,17 +888,19 @@ void Decoder::step(const uint32_t* tokens, const evl_ffn_backend* ffn, float* lo
 // positions [0, p0 + i] of this session's cache. Equal to n Session::step calls
 // (src/runtime.rs:773-808, fed one token at a time by src/bin/evelyn-generate.rs:69-80)
 // up to the products' summation order.
-void Decoder::prefill(const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out) {
+void Decoder::prefill(uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out) {
     constexpr uint32_t kPrefillRows = 32;
     Model& m = *model;
     const Config& c = m.cfg;
     DeviceGuard g(m.device);
-    if (b.batch != 1) raise(EVL_ERR_INVALID_INPUT, "prefill feeds a single sequence");
+    if (seq >= b.batch)
+        raise(EVL_ERR_INVALID_INPUT, "sequence " + std::to_string(seq) + " is outside the batch of " +
+                                         std::to_string(b.batch));
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] >= c.vocab)
             raise(EVL_ERR_INVALID_INPUT, "token ID " + std::to_string(tokens[i]) + " is outside model vocabulary (" +
                                              std::to_string(c.vocab) + "); check that tokenizer and GGUF match");
-    if (host_pos[0] + n > b.max_ctx)
+    if (host_pos[seq] + n > b.max_ctx)
         raise(EVL_ERR_INVALID_INPUT, "session context is full (" + std::to_string(b.max_ctx) + " positions)");
     if (n == 0) return;
     if (!pf) {
@@ -913,23 +911,23 @@ void Decoder::prefill(const uint32_t* tokens, size_t n, float* logits_out, uint3
     }
     Decoder& P = *pf;
     const uint32_t C = P.b.batch, pps = b.pages_per_seq;
-    const int32_t spare = (int32_t)pps;  // the page past this sequence's own
+    const int32_t spare = (int32_t)(b.batch * pps);  // the page past every sequence's own
     std::vector<int32_t> pt((uint64_t)C * pps);
-    uint32_t rows_set = C;  // rows whose page table is the session's
     for (size_t off = 0; off < n; off += C) {
         const uint32_t nr = (uint32_t)std::min<size_t>(C, n - off);
         int32_t* tok = P.b.h_tokens.as<int32_t>();
         std::vector<int32_t> pos(C);
         for (uint32_t i = 0; i < C; ++i) {
             tok[i] = i < nr ? (int32_t)tokens[off + i] : 0;
-            pos[i] = i < nr ? (int32_t)(host_pos[0] + off + i) : 0;
+            pos[i] = i < nr ? (int32_t)(host_pos[seq] + off + i) : 0;
         }
-        if (nr != rows_set) {  // padding rows append into the spare page and read only it
+        if (nr != pf_rows || seq != pf_seq) {  // padding rows append into the spare page and read only it
             for (uint32_t i = 0; i < C; ++i)
-                for (uint32_t j = 0; j < pps; ++j) pt[(uint64_t)i * pps + j] = i < nr ? (int32_t)j : spare;
+                for (uint32_t j = 0; j < pps; ++j) pt[(uint64_t)i * pps + j] = i < nr ? (int32_t)(seq * pps + j) : spare;
             cuda_check(cudaMemcpyAsync(P.b.page_table.p, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, P.stream),
                        "page table");
-            rows_set = nr;
+            pf_rows = nr;
+            pf_seq = seq;
         }
         cuda_check(cudaMemcpyAsync(P.b.tokens.p, tok, C * 4, cudaMemcpyHostToDevice, P.stream), "H2D tokens");
         cuda_check(cudaMemcpyAsync(P.b.pos.p, pos.data(), C * 4, cudaMemcpyHostToDevice, P.stream), "H2D positions");
@@ -948,9 +946,9 @@ void Decoder::prefill(const uint32_t* tokens, size_t n, float* logits_out, uint3
     cuda_check(cudaMemcpyAsync(P.b.h_err.p, P.b.err.p, 4, cudaMemcpyDeviceToHost, P.stream), "D2H error flag");
     cuda_check(cudaStreamSynchronize(P.stream), "prefill");
     P.check_device_error();
-    host_pos[0] += n;
-    const int32_t p = (int32_t)host_pos[0];
-    cuda_check(cudaMemcpy(b.pos.p, &p, 4, cudaMemcpyHostToDevice), "position");
+    host_pos[seq] += n;
+    const int32_t p = (int32_t)host_pos[seq];
+    cuda_check(cudaMemcpy(b.pos.as<int32_t>() + seq, &p, 4, cudaMemcpyHostToDevice), "position");
 }
 
 // sample_token (src/server.rs:326-352) on the last step's logits, on the device: only

@@ -126,6 +126,7 @@ SIGNATURES = {
     "evl_session_prefill": (C.c_int, [_P, _U32P, C.c_size_t, _F, _U32P]),
     "evl_session_sample": (C.c_int, [_P, C.c_float, C.POINTER(C.c_uint64), _U32P]),
     "evl_batch_sample": (C.c_int, [_P, C.c_float, C.POINTER(C.c_uint64), _U32P]),
+    "evl_batch_prefill": (C.c_int, [_P, C.c_uint32, _U32P, C.c_size_t, _F, _U32P]),
     "evl_session_stream": (_P, [_P]),
     "evl_session_kernels_per_step": (C.c_uint32, [_P]),
     "evl_batch_new": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(_P)]),
@@ -534,6 +535,16 @@ class Batch:
         _check(lib().evl_batch_step(self._h, t.ctypes.data_as(_U32P), _fp(out) if logits else None,
                                     am.ctypes.data_as(_U32P)))
         return out if logits else am
+
+    def prefill(self, seq: int, tokens, logits: bool = False):
+        """Session.prefill for sequence `seq` of the batch: its prompt in batched steps;
+        per-position logits [n][vocab] when logits=True, else the per-position argmax."""
+        t = np.ascontiguousarray(np.asarray(list(tokens), dtype=np.uint32))
+        am = np.empty(max(1, t.size), dtype=np.uint32)
+        out = np.empty((t.size, self.model.cfg.vocab), dtype=np.float32) if logits else None
+        _check(lib().evl_batch_prefill(self._h, int(seq), t.ctypes.data_as(_U32P), t.size,
+                                       _fp(out) if logits else None, am.ctypes.data_as(_U32P)))
+        return out if logits else [int(v) for v in am[:t.size]]
 
     def sample(self, temperature: float, states):
         """Session.sample for every sequence: returns (tokens, new states)."""

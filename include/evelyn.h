@@ -174,6 +174,11 @@ uint64_t evl_batch_pos(const evl_batch* b, uint32_t seq);
 /* tokens[n_seqs] (host) in; logits_out [n_seqs][vocab] and argmax_out [n_seqs], both optional (host). */
 evl_status evl_batch_step(evl_batch* b, const uint32_t* tokens, float* logits_out, uint32_t* argmax_out);
 void* evl_batch_stream(evl_batch* b);
+/* evl_session_prefill for sequence `seq` of a batch: its prompt tokens[0 .. n) in batched
+ * steps of up to 32 positions on the tensor cores; the other sequences are untouched.
+ * logits_out ([n][vocab]) and argmax_out ([n]) are optional (host). */
+evl_status evl_batch_prefill(evl_batch* b, uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out,
+                             uint32_t* argmax_out);
 /* evl_session_sample for every sequence of a batch: rng_states[n_seqs] (host in/out),
  * tokens_out[n_seqs] (host). */
 evl_status evl_batch_sample(evl_batch* b, float temperature, uint64_t* rng_states, uint32_t* tokens_out);

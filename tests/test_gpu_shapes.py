@@ -7,17 +7,20 @@ the CPU oracle):
   within max-abs 2e-3 at every step (f32 KV, the reference's precision; f16 KV pages
   within 2e-2), identical greedy tokens, PPL within 0.5 % (the protocol of
   src/bin/evelyn-generate.rs:69-86);
-* head_dim 128 sessions with GQA groups 2, 4 and 8 run past 1200 positions, so the
+* head_dim 128 sessions with GQA groups 1, 2, 4 and 8 run past 1200 positions, so the
   single-sequence cluster attention streams its 8 splits through the page ring at the
-  benchmark's head size (with the default ring and with a 2-page ring), and the
-  persistent step kernel's attention phase runs its splits over many chunks;
+  benchmark's head size (tensor-core loop over f16 pages, scalar loop over f16 and f32
+  pages; the default ring and a 2-page ring), and the persistent step kernel's
+  attention phase runs its splits over many chunks;
 * the matvec paths only the big shapes reach: the LM-head shape 151936x4096 Q8_0
   (more row blocks per CTA than partial buffers: rotating buffers, last-warp
   reduction) and 5120x25600 Q6_K (rows longer than 12288 values: quarter staging).
 """
 import ctypes as C
 import gc
+import json
 import math
+import os
 
 import numpy as np
 import pytest
@@ -96,11 +99,19 @@ def test_benchmark_shape_generate_matches_oracle(shape):
     prompt, steps = _tokens(16, spec.vocab, 0), 64
     want, ppl_o, greedy_o = _oracle_protocol(img, spec, prompt, steps)
     margin = min(_top2_margin(w) for w in want[len(prompt) - 1:])
+    rows = []
     for kv_f32, tol in ((True, LOGIT_TOL), (False, F16_KV_LOGIT_TOL)):
         worst, ppl_g, greedy_g = _engine_protocol(img, spec, prompt, steps, want, kv_f32)
+        rows.append({"shape": shape, "kv": "f32" if kv_f32 else "f16", "max_abs": worst, "tol": tol, "ppl": ppl_g,
+                     "ppl_oracle": ppl_o, "greedy_equal": greedy_g == greedy_o, "greedy_steps": steps,
+                     "min_top2_margin": margin})
         assert worst <= tol, (kv_f32, worst)
         assert abs(ppl_g / ppl_o - 1) < 0.005, (kv_f32, ppl_g, ppl_o)
         assert greedy_g == greedy_o, (kv_f32, greedy_g, greedy_o, margin)
+    rdir = os.environ.get("EVELYN_PARITY_RESULT_DIR")
+    if rdir:  # the measured figures, for a summary beside the test run
+        with open(os.path.join(rdir, f"parity_{shape}.json"), "w") as f:
+            f.write(json.dumps(rows) + "\n")
 
 
 @pytest.mark.parametrize("heads,kv_heads", [(4, 4), (4, 2), (8, 2), (8, 1)])
