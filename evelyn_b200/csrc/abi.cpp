@@ -427,6 +427,11 @@ evl_status evl_batch_sample(evl_batch* b, float temperature, uint64_t* rng_state
 
 void* evl_session_stream(evl_session* s) { return s ? (void*)s->d.stream : nullptr; }
 uint32_t evl_session_kernels_per_step(const evl_session* s) { return s ? s->d.kernels_per_step : 0; }
+const char* evl_session_notes(const evl_session* s) {
+    if (!s) return "";
+    s->notes = s->d.step_note;
+    return s->notes.c_str();
+}
 
 evl_status evl_batch_new(evl_model* model, uint32_t n_seqs, uint32_t max_ctx, evl_batch** out) {
     return guarded([&] {

@@ -336,6 +336,7 @@ struct evl_model {
 };
 struct evl_session {
     evl::Decoder d;
+    mutable std::string notes;  // evl_session_notes' text
 };
 struct evl_batch {
     evl::Decoder d;

@@ -129,6 +129,7 @@ SIGNATURES = {
     "evl_batch_prefill": (C.c_int, [_P, C.c_uint32, _U32P, C.c_size_t, _F, _U32P]),
     "evl_session_stream": (_P, [_P]),
     "evl_session_kernels_per_step": (C.c_uint32, [_P]),
+    "evl_session_notes": (C.c_char_p, [_P]),
     "evl_batch_new": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(_P)]),
     "evl_batch_free": (None, [_P]),
     "evl_batch_pos": (C.c_uint64, [_P, C.c_uint32]),
@@ -465,6 +466,11 @@ class Session:
     @property
     def kernels_per_step(self) -> int:
         return int(lib().evl_session_kernels_per_step(self._h))
+
+    @property
+    def notes(self) -> str:
+        """Why the opt-in persistent step kernel is not used, if it was asked for."""
+        return (lib().evl_session_notes(self._h) or b"").decode()
 
     def step(self, token: int, ffn: Optional[FfnBackend] = None, logits: bool = True):
         """Feed one token; returns next-token logits (a new array), or the argmax when logits=False."""

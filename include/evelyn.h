@@ -164,6 +164,10 @@ evl_status evl_session_sample(evl_session* s, float temperature, uint64_t* rng_s
 void* evl_session_stream(evl_session* s);
 /* Number of engine kernels one dense step launches (known after the first step). */
 uint32_t evl_session_kernels_per_step(const evl_session* s);
+/* Human-readable notes on the launches the session's step uses (the opt-in persistent
+ * step kernel) and, where one is not used, why; empty when there is nothing to say.
+ * Valid until the next call on the session or its release. */
+const char* evl_session_notes(const evl_session* s);
 
 /* ------------------------------------------------------------------ batched decode */
 /* n_seqs independent Sessions stepped together (one token each per step), sharing
