@@ -486,10 +486,12 @@ evl_status evl_qmatrix_create(uint32_t type, uint32_t rows, uint32_t cols, const
             q->err.alloc(4);
             cuda_check(cudaMemset(q->err.p, 0, 4), "memset");
             place(q->m, q->buf.as<uint8_t>());
-            std::vector<uint8_t> staging(q->m.bytes());
-            repack_host(q->m, static_cast<const uint8_t*>(host_raw), type_bytes(type, cols), staging.data(),
-                        (int)std::max(1u, std::thread::hardware_concurrency()));
-            cuda_check(cudaMemcpy(q->buf.p, staging.data(), staging.size(), cudaMemcpyHostToDevice), "upload");
+            const uint64_t stride = type_bytes(type, cols);
+            DeviceBuffer raw;
+            raw.alloc(stride * rows);
+            cuda_check(cudaMemcpy(raw.p, host_raw, stride * rows, cudaMemcpyHostToDevice), "upload");
+            cuda_check(launch_repack(q->m.dev, q->buf.as<uint8_t>(), q->m.bytes(), raw.p, stride, 0), "repack");
+            cuda_check(cudaDeviceSynchronize(), "repack");
         } catch (...) {
             delete q;
             throw;

@@ -137,9 +137,6 @@ struct QMatrix {
 
 // Sizes of the repacked form of a [rows][cols] tensor of `type`; raises Unsupported.
 void repack_sizes(QMatrix& m);
-// Repacks raw GGUF rows [rows][type_bytes(type, cols)] (already sliced to the shard)
-// into host memory at dst (the tile layout of common.cuh), using `threads` threads.
-void repack_host(const QMatrix& m, const uint8_t* raw, size_t raw_row_stride, uint8_t* dst, int threads);
 // Points m.dev at base + m.offset.
 void place(QMatrix& m, uint8_t* base);
 

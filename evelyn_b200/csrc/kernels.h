@@ -10,6 +10,10 @@ namespace evl {
 // ---------------------------------------------------------------- dequant.cu
 cudaError_t launch_dequant_raw(uint32_t type, const void* raw, uint64_t n, float* out, cudaStream_t s);
 cudaError_t launch_dequant_repacked(const QMatDev& m, uint32_t row0, uint32_t nrows, float* out, cudaStream_t s);
+// Repack raw GGUF rows (device memory, `stride` bytes apart) into the matvec layout of
+// `d` at dst (dst_bytes, zeroed first: the padding rows of the last slab).
+cudaError_t launch_repack(const QMatDev& d, uint8_t* dst, uint64_t dst_bytes, const void* raw, uint64_t stride,
+                          cudaStream_t s);
 
 // ---------------------------------------------------------------- qmatvec.cu
 enum MatvecEpilogue : int {

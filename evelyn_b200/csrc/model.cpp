@@ -268,28 +268,33 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     }
     m.weights.alloc(total);
     m.vectors.alloc(vfloats * 4);
-    size_t max_bytes = 0, max_raw = 0;
+    // the raw tensor bytes go to the device as they are and are repacked there
+    // (launch_repack); a column shard of a tensor-parallel rank is gathered on the host
+    // first, so only its own bytes cross
+    size_t max_raw = 0, max_gather = 0;
     for (auto& p : plan) {
         place(*p.m, m.weights.as<uint8_t>());
-        max_bytes = std::max(max_bytes, p.m->bytes());
-        if (p.col_bytes) max_raw = std::max(max_raw, (size_t)p.col_bytes * p.m->rows);
+        const size_t row = p.col_bytes ? p.col_bytes : p.stride;
+        max_raw = std::max(max_raw, row * p.m->rows);
+        if (p.col_bytes) max_gather = std::max(max_gather, (size_t)p.col_bytes * p.m->rows);
     }
-    std::vector<uint8_t> staging(max_bytes), rawbuf(max_raw);
-    const int threads = (int)std::max(1u, std::thread::hardware_concurrency());
+    std::vector<uint8_t> gather(max_gather);
+    DeviceBuffer draw;
+    draw.alloc(max_raw);
     for (auto& p : plan) {
         const uint8_t* src = p.raw;
         size_t stride = p.stride;
-        if (p.col_bytes) {  // gather the column shard into a contiguous buffer
+        if (p.col_bytes) {
             for (uint32_t r = 0; r < p.m->rows; ++r)
-                std::memcpy(rawbuf.data() + (size_t)r * p.col_bytes, p.raw + (size_t)r * p.stride + p.col_byte0,
+                std::memcpy(gather.data() + (size_t)r * p.col_bytes, p.raw + (size_t)r * p.stride + p.col_byte0,
                             p.col_bytes);
-            src = rawbuf.data();
+            src = gather.data();
             stride = p.col_bytes;
         }
-        repack_host(*p.m, src, stride, staging.data(), threads);
-        cuda_check(cudaMemcpy(m.weights.as<uint8_t>() + p.m->offset, staging.data(), p.m->bytes(),
-                              cudaMemcpyHostToDevice),
-                   "upload weights");
+        // (the legacy stream orders each copy after the previous repack that read the buffer)
+        cuda_check(cudaMemcpy(draw.p, src, stride * p.m->rows, cudaMemcpyHostToDevice), "upload weights");
+        cuda_check(launch_repack(p.m->dev, m.weights.as<uint8_t>() + p.m->offset, p.m->bytes(), draw.p, stride, 0),
+                   "repack weights");
     }
     float* vbase = m.vectors.as<float>();
     m.rope_inv_freq = vbase;

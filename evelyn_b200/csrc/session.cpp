@@ -72,6 +72,10 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* sh
     } else {
         // one spare page past the sequences' own: a prefill's padding rows write there
         b.kv.alloc((pages + 1) * page_stride);
+        // zeroed: the tensor-core attention multiplies whole 16-position page tiles by
+        // the softmax weights, 0 for the positions not written yet, so those must hold
+        // finite values (0 * NaN would poison the sum)
+        cuda_check(cudaMemset(b.kv.p, 0, b.kv.bytes), "memset KV cache");
         kv.pool = b.kv.p;
         kv.page_stride = page_stride;
         kv.layer_stride = layer_stride;
