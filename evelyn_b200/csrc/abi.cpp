@@ -645,6 +645,39 @@ void attention_standalone(const float* d_q, const void* d_k_pages, const void* d
     a.part = part;
     a.scale = 1.0f / sqrtf((float)head_dim);
     a.err = d_err;
+    // 16-row f16 pages of head_dim 64 / 128 and a GQA group of 1, 2, 4 or 8: the cluster
+    // kernel (split-K over 8 CTAs per kv head, tensor-core loop, on-chip merge, one
+    // launch) in its standalone mode (q ready, k and v already in the pages). K and V
+    // share one tensor map based at the lower of the two buffers; the map's extent is a
+    // bound, the loads only touch the pages the table names.
+    const uint32_t G = heads / kv_heads;
+    const uint32_t ring = attention_cluster_pages(a.max_pages, 8, page_size, head_dim, 2, G, 16);
+    if (page_size == 16 && ring) {
+        const uint8_t* k8 = static_cast<const uint8_t*>(d_k_pages);
+        const uint8_t* v8 = static_cast<const uint8_t*>(d_v_pages);
+        const uint8_t* base = std::min(k8, v8);
+        const uint64_t row = 2ull * head_dim;
+        KvTmap tmap;
+        if ((uint64_t)(k8 - base) % row == 0 && (uint64_t)(v8 - base) % row == 0 &&
+            make_kv_tmap(base, (1ull << 30) * row, head_dim, &tmap)) {
+            AttnArgs c = a;
+            c.kv.pool = const_cast<uint8_t*>(base);
+            c.kv.k_offset = k8 - base;
+            c.nsplit = 8;
+            RopeArgs r;
+            r.q = const_cast<float*>(d_q);
+            r.kv = c.kv;
+            r.page_table = d_page_table;
+            r.max_pages = a.max_pages;
+            r.batch = 1;
+            r.heads = heads;
+            r.kv_heads = kv_heads;
+            r.head_dim = head_dim;
+            r.err = d_err;
+            cuda_check(launch_attention_cluster(r, c, ring, 2, s, false, &tmap), "attention");
+            return;
+        }
+    }
     cuda_check(launch_attention(a, s, false), "attention");
 }
 

@@ -23,7 +23,7 @@ namespace {
 
 __device__ __forceinline__ uint8_t* kv_tile(const KvCacheDev& kv, int32_t page, uint32_t layer, uint32_t which,
                                             uint32_t head) {
-    return (uint8_t*)kv.pool + (uint64_t)page * kv.page_stride + (uint64_t)layer * kv.layer_stride +
+    return (uint8_t*)kv.pool + kv.k_offset + (uint64_t)page * kv.page_stride + (uint64_t)layer * kv.layer_stride +
            (uint64_t)head * kv.head_stride + (which ? kv.v_offset : 0);
 }
 

@@ -56,7 +56,7 @@ struct ClusterAttn {
 
 __device__ __forceinline__ const uint8_t* kv_tile(const KvCacheDev& kv, int32_t page, uint32_t layer, uint32_t which,
                                                   uint32_t head) {
-    return (const uint8_t*)kv.pool + (uint64_t)page * kv.page_stride + (uint64_t)layer * kv.layer_stride +
+    return (const uint8_t*)kv.pool + kv.k_offset + (uint64_t)page * kv.page_stride + (uint64_t)layer * kv.layer_stride +
            (uint64_t)head * kv.head_stride + (which ? kv.v_offset : 0);
 }
 
@@ -224,7 +224,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
     pdl_launch_dependents();  // the next kernel's weight streaming may start on idle SMs
 
     // ---- before the wait: position, pages, static vectors
-    const int32_t pos = __ldcg(a.pos + sq);
+    // (a.pos null: one caller-given position; r.k null: q is ready and k, v are already in
+    // the pages -- the standalone decode attention -- so nothing is normed, rotated or
+    // appended)
+    const int32_t pos = a.pos ? __ldcg(a.pos + sq) : a.pos_value;
+    const bool app = r.k != nullptr;
     const bool pos_ok = pos >= 0 && (uint32_t)pos / ps < a.max_pages;
     const uint32_t t_all = pos_ok ? (uint32_t)pos + 1 : 0;
     const uint32_t S = pos_ok ? split_len(t_all, C, ps) : 0;
@@ -274,7 +278,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
     // warp w < G: q head kvh*G + w; w == G: k; w == G+1: v. Lane dims d = DPL*lane + e.
-    const bool vw = warp < G + 2, normed = warp <= G;
+    const bool vw = warp < (app ? G + 2 : G), normed = warp <= G;
     float nw[DPL], sn[DPL], cs[DPL];
     uint32_t i0[DPL], i1[DPL];
     bool rot[DPL], second[DPL];
@@ -396,7 +400,7 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             }
         }
     }
-    const uint32_t pnew = last ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
+    const uint32_t pnew = last && app ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
     // Warp group grp (kAW / NS warps) reads the chunks of stage grp (c = grp, grp + NS,
     // ...), so the stages are read concurrently; a group syncs on its own named barrier
     // and refills its own stage, so groups never wait on one another.
@@ -726,7 +730,9 @@ bool make_kv_tmap(const void* pool, uint64_t bytes, uint32_t head_dim, KvTmap* o
 
 cudaError_t launch_attention_cluster(const RopeArgs& r, const AttnArgs& a, uint32_t ring_pages, uint32_t stages,
                                      cudaStream_t s, bool pdl, const KvTmap* tmap) {
-    if (!a.batch || r.batch != a.batch || !a.out || !a.pos || r.pos != a.pos || ring_pages < 2 || (ring_pages & 1) ||
+    const bool standalone = !a.pos && !r.pos && !r.k && !r.v && a.batch == 1;  // q ready, k and v in the pages
+    if (!a.batch || r.batch != a.batch || !a.out || (!standalone && (!a.pos || r.pos != a.pos)) || ring_pages < 2 ||
+        (ring_pages & 1) ||
         a.nsplit < 1 || a.nsplit > kMaxSplits || stages < 2 || stages > kMaxStages || kAW % stages ||
         ring_pages % stages)
         return cudaErrorInvalidValue;

@@ -61,6 +61,7 @@ struct KvCacheDev {
     uint64_t layer_stride = 0;     // bytes per layer inside a page
     uint64_t head_stride = 0;      // bytes per (k|v, head) tile
     int64_t v_offset = 0;          // bytes from a K tile to its V tile
+    int64_t k_offset = 0;          // bytes from pool to the K tiles (0 for the engine's pool)
     uint32_t page_size = 16;
     uint32_t elem_bytes = 2;       // 2 = f16, 4 = f32
 };
