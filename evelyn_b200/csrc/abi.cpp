@@ -674,6 +674,8 @@ void attention_standalone(const float* d_q, const void* d_k_pages, const void* d
             r.kv_heads = kv_heads;
             r.head_dim = head_dim;
             r.err = d_err;
+            // two stages: 8-page chunks keep every warp of a group on a page (the
+            // double-buffered 4-stage ring measured slower here: 83 vs 66 us at 32K)
             cuda_check(launch_attention_cluster(r, c, ring, 2, s, false, &tmap), "attention");
             return;
         }

@@ -401,13 +401,16 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
         }
     }
     const uint32_t pnew = last && app ? ((uint32_t)pos - t0) / ps : 0xffffffffu;  // page of the new position
-    // Warp group grp (kAW / NS warps) reads the chunks of stage grp (c = grp, grp + NS,
-    // ...), so the stages are read concurrently; a group syncs on its own named barrier
-    // and refills its own stage, so groups never wait on one another.
-    const uint32_t GW = kAW / NS, grp = (uint32_t)warp / GW, gw = (uint32_t)warp % GW;
+    // Chunk c sits in stage c % NS. With 2 stages, warp group grp (half the warps) reads
+    // the chunks of stage grp; with 4 stages, two groups of 8 warps read chunks grp,
+    // grp + 2, ..., alternating between their two stages, so a group's next chunk is
+    // already in flight while it reads the current one (double buffering: the copy
+    // latency hides behind the reading of long splits). A group syncs on its own named
+    // barrier and refills the stage it has just read, so groups never wait on one another.
+    const uint32_t NG = NS >= 4 ? NS / 2 : NS, GW = kAW / NG, grp = (uint32_t)warp / GW, gw = (uint32_t)warp % GW;
     uint32_t cw = grp;  // the next chunk of this group not yet waited for
-    for (uint32_t c = grp; valid && c < nch; c += NS) {
-        const uint32_t half = grp, p0 = c * H, p1 = min(npg, p0 + H);
+    for (uint32_t c = grp; valid && c < nch; c += NG) {
+        const uint32_t half = c % NS, p0 = c * H, p1 = min(npg, p0 + H);
         cw = c;
         if (!mbar_wait(&full[half], (c / NS) & 1)) {
             atomicExch(a.err, DEV_ERR_WAIT_TIMEOUT);
@@ -571,12 +574,15 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             }
         }
         named_sync(1 + grp, GW * 32);  // the group is done with its stage of the ring
-        cw = c + NS;
+        cw = c + NG;
         if (gw == 0 && c + NS < nch) issue(c + NS, c + NS + 1);
     }
-    // a wait of this group gave up: its stage's copy may still land (later chunks of
-    // the stage were never issued); let it before leaving
-    if (cw < nch && grp_bad[grp]) mbar_wait(&full[grp], (cw / NS) & 1);
+    // a wait of this group gave up: the copies of its chunk cw and (double buffering) of
+    // its next chunk may still land; let them before leaving
+    if (grp_bad[grp]) {
+        if (cw < nch) mbar_wait(&full[cw % NS], (cw / NS) & 1);
+        if (NS > NG && cw + NG < nch) mbar_wait(&full[(cw + NG) % NS], ((cw + NG) / NS) & 1);
+    }
     __syncthreads();
     if constexpr (MM) {
 #pragma unroll

@@ -115,18 +115,21 @@ def test_benchmark_shape_generate_matches_oracle(shape):
 
 
 @pytest.mark.parametrize("heads,kv_heads", [(4, 4), (4, 2), (8, 2), (8, 1)])
-@pytest.mark.parametrize("path,ring", [("cluster", None), ("cluster", "2"), ("scalar", None), ("f32", None),
-                                       ("f32", "2"), ("step", None)])
+@pytest.mark.parametrize("path,ring", [("cluster", None), ("cluster", "2"), ("stages4", "8"), ("scalar", None),
+                                       ("f32", None), ("f32", "2"), ("step", None)])
 def test_hd128_attention_long_context(heads, kv_heads, path, ring, monkeypatch):
     """GQA group 1 / 2 / 4 / 8 at head_dim 128 (the 0.6B, 8B and 32B groups are 2, 4
     and 8) past 1200 positions, through the launch sequence's cluster attention -- the
     tensor-core loop over f16 pages, the scalar loop over f16 pages (EVELYN_ATTN_MMA=0)
-    and over f32 pages, each with the default ring and some with a 2-page ring -- and
+    and over f32 pages, each with the default ring and some with a 2-page ring, and the
+    double-buffered 4-stage ring (8 pages) -- and
     through the persistent step kernel: every 25th step's logits against the oracle,
     and greedy agreement."""
     monkeypatch.setenv("EVELYN_STEP_KERNEL", "1" if path == "step" else "0")
     if path == "scalar":
         monkeypatch.setenv("EVELYN_ATTN_MMA", "0")
+    if path == "stages4":  # double-buffered: two warp groups, each alternating between two stages
+        monkeypatch.setenv("EVELYN_ATTN_STAGES", "4")
     if ring:
         monkeypatch.setenv("EVELYN_ATTN_RING", ring)
     spec = synth.tiny(seed=31 + heads + kv_heads, head_dim=128, heads=heads, kv_heads=kv_heads, layers=2)
