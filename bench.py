@@ -442,24 +442,35 @@ def run_c5(evl, synth, args, hbm, peak_kind, rank, world, local):
         del model
         return {"unavailable": errs[0]}
     B, P, K = 8, args.c5_prompt, args.c5_steps
-    bat = evl.Batch(model, B, max_ctx=P + K + 8)
-    rng = np.random.default_rng(5)
-    pf = prefill_batch(bat, B, P, spec.vocab, rng, world)
-    toks = rng.integers(0, spec.vocab, B)
-    for _ in range(3):  # warm-up
-        toks = bat.step(toks, logits=False)
-    ext = torch.cuda.ExternalStream(bat.stream)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ext)
-    for _ in range(K):
-        toks = bat.step(toks, logits=False)
-    e1.record(ext)
-    e1.synchronize()
-    ms = dist_max(e0.elapsed_time(e1), world)
+    err, ms = None, 0.0
+    try:
+        bat = evl.Batch(model, B, max_ctx=P + K + 8)
+        rng = np.random.default_rng(5)
+        pf = prefill_batch(bat, B, P, spec.vocab, rng, world)
+        toks = rng.integers(0, spec.vocab, B)
+        for _ in range(3):  # warm-up
+            toks = bat.step(toks, logits=False)
+        ext = torch.cuda.ExternalStream(bat.stream)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        for _ in range(K):
+            toks = bat.step(toks, logits=False)
+        e1.record(ext)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        del bat
+    except Exception as e:  # noqa: BLE001 - reported in the line; every rank learns of it below
+        err = f"rank {rank}: {type(e).__name__}: {e}"
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    del model
+    errs = [e for e in errs if e]
+    if errs:
+        return {"unavailable": errs[0]}
+    ms = dist_max(ms, world)
     ctx0 = P + 3
-    del bat, model
     return {"value": round(B * K / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / K, 4),
             "global_batch": B, "parallelism": f"tp{world}",
             "workload": f"Qwen3-32B-shape (64L, d5120, 64Q/8KV x128, ffn 25600) Q4_K_M-style mix, {B} sequences, "
