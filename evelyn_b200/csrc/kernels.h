@@ -47,8 +47,14 @@ struct MatvecArgs {
 };
 
 // One fused launch over up to three matrices that share the input vector (all of
-// the same width). Types Q4_K, Q6_K, Q8_0.
+// the same width). Types Q4_K, Q5_K, Q6_K, Q8_0; a launch with any F16, BF16 or F32
+// matrix, or a gate and up of two types, runs as launch_plain_matvec.
 cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
+
+// plain_matvec.cu: the same launch, warp per row, for unquantised matrices (a
+// quantised matrix in it is read through the exact dequantiser).
+bool matvec_has_plain(const MatvecArgs& a);
+cudaError_t launch_plain_matvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------- attention.cu
 // Paged KV cache. The K tile of (page, layer, head) starts at

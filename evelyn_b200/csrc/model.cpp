@@ -225,7 +225,6 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         add_matrix(L.gate, p + "ffn_gate.weight", c.ffn, c.dim, f0, f1, 0, 0);
         add_matrix(L.up, p + "ffn_up.weight", c.ffn, c.dim, f0, f1, 0, 0);
         add_matrix(L.down, p + "ffn_down.weight", c.dim, c.ffn, 0, 0, T > 1 ? f0 : 0, T > 1 ? f1 : 0);
-        if (L.gate.type != L.up.type) raise(EVL_ERR_UNSUPPORTED, p + "ffn_gate and ffn_up differ in type");
     }
     // LM head: output.weight, else the tied embedding (runtime.rs:392-396). Tied, it is
     // planned as its own (vocabulary-sharded) copy and the embedding keeps the name.

@@ -58,6 +58,7 @@ std::atomic<int> g_sms[kMaxDevices];  // SM count per device, 0 until set up (ze
 }  // namespace
 
 cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl) {
+    if (matvec_has_plain(a)) return launch_plain_matvec(a, s, pdl);
     Plan p;
     cudaError_t e = plan_matvec(a, p);
     if (e != cudaSuccess) return e;

@@ -79,10 +79,13 @@ def test_repack_round_trip_bit_exact(t, rows, cols):
         runtime.lib().evl_qmatrix_free(h)
 
 
-@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K])
-@pytest.mark.parametrize("rows,cols", SHAPES + [(4096, 4096), (1000, 12288)])
+@pytest.mark.parametrize("t", [synth.GGML_Q8_0, synth.GGML_Q4_K, synth.GGML_Q5_K, synth.GGML_Q6_K, synth.GGML_F16,
+                               synth.GGML_BF16, synth.GGML_F32])
+@pytest.mark.parametrize("rows,cols", SHAPES + [(4096, 4096), (1000, 12288), (40, 16384)])
 def test_qmatrix_matvec(t, rows, cols):
-    """y = W x against the oracle's sequential f32 dot; tolerance: 5e-5 of sum|w*x| (f32 reordering)."""
+    """y = W x against the oracle's sequential f32 dot; tolerance: 5e-5 of sum|w*x| (f32 reordering).
+    F16 / BF16 / F32 matrices run the warp-per-row kernel (rows of 16384 values need its
+    shared-memory opt-in)."""
     rng = np.random.default_rng(rows + cols + t)
     w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
     raw = synth.encode(t, w)

@@ -25,14 +25,25 @@ def _tokens(n, vocab, seed=0):
 
 
 @pytest.mark.parametrize("kv_f32", [False, True])
-@pytest.mark.parametrize("mix", ["q4k_mix", "q8_0", "q6k", "q5k"])
+@pytest.mark.parametrize("mix", ["q4k_mix", "q8_0", "q6k", "q5k", "f16", "bf16", "f32", "float_mix", "gate_up_mix"])
 def test_step_logits_match_oracle(mix, kv_f32):
+    """Unquantised (F16 / BF16 / F32) projections run the warp-per-row matvec; in
+    "float_mix" the fused Q/K/V and gate/up launches hold an F16 matrix beside quantised
+    ones, read through the exact dequantiser; "gate_up_mix" has a Q4_K gate beside a Q6_K up."""
     spec = synth.tiny(seed=11)
     if mix == "q8_0":
         spec = spec.with_types(synth.GGML_Q8_0)
     elif mix in ("q6k", "q5k"):
         spec = spec.with_types(synth.GGML_Q6_K if mix == "q6k" else synth.GGML_Q5_K)
         spec.embed = spec.output = synth.GGML_Q8_0
+    elif mix in ("f16", "bf16", "f32"):
+        spec = spec.with_types({"f16": synth.GGML_F16, "bf16": synth.GGML_BF16, "f32": synth.GGML_F32}[mix])
+    elif mix == "float_mix":
+        spec.attn_k = spec.ffn_up = synth.GGML_F16
+        spec.attn_output = synth.GGML_BF16
+        spec.output = synth.GGML_F32
+    elif mix == "gate_up_mix":
+        spec.ffn_up = synth.GGML_Q6_K
     img, m, r = _models(spec, kv_f32)
     s, rs = evl.Session(m, max_ctx=256), orc.Session(r)
     worst = 0.0
