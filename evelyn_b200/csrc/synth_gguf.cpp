@@ -311,6 +311,7 @@ struct Tensor {
     std::vector<uint64_t> dims;
     uint32_t type;
     bool ones;  // norm weight (all 1.0) instead of N(0, sd)
+    float sd = 0.f;  // > 0: N(0, sd) instead of the spec's stddev; < 0: the decay rates below
     uint64_t offset = 0, nbytes = 0;
 };
 
@@ -328,6 +329,7 @@ struct Buf {
     void kv_u32(const std::string& k, uint32_t v) { str(k); put<uint32_t>(4); put<uint32_t>(v); }
     void kv_f32(const std::string& k, float v) { str(k); put<uint32_t>(6); put<float>(v); }
     void kv_str(const std::string& k, const std::string& v) { str(k); put<uint32_t>(8); str(v); }
+    void kv_bool(const std::string& k, bool v) { str(k); put<uint32_t>(7); put<uint8_t>(v ? 1 : 0); }
 };
 
 uint64_t tensor_bytes(uint32_t t, uint64_t n) {
@@ -387,30 +389,52 @@ int evs_build(const evs_model_spec* s, uint8_t** out, size_t* out_len) {
     *out = nullptr;
     *out_len = 0;
     const uint64_t hd = s->head_dim, qw = (uint64_t)s->heads * hd, kw = (uint64_t)s->kv_heads * hd;
-    uint32_t types[] = {s->type_attn_q, s->type_attn_k, s->type_attn_v, s->type_attn_output,
-                        s->type_ffn_gate, s->type_ffn_up, s->type_ffn_down, s->type_embed, s->type_output};
+    const std::string a = s->arch[0] ? s->arch : "qwen3";
+    const bool q35 = a == "qwen35";
+    uint32_t types[] = {s->type_attn_q, s->type_attn_k,    s->type_attn_v, s->type_attn_output,
+                        s->type_ffn_gate, s->type_ffn_up,  s->type_ffn_down, s->type_embed,
+                        s->type_output,   q35 ? s->type_ssm : F32};
     for (uint32_t t : types)
         if (!valid_type(t)) {
             g_err = "unsupported ggml type " + std::to_string(t);
             return 4;
         }
+    if (q35 && (!s->ssm_value_heads || s->ssm_inner % s->ssm_value_heads || !s->ssm_conv_kernel)) {
+        g_err = "qwen35 needs ssm_value_heads dividing ssm_inner and a conv kernel";
+        return 2;
+    }
     std::vector<Tensor> ts;
-    auto add = [&](const std::string& n, std::vector<uint64_t> dims, uint32_t type, bool ones) {
-        ts.push_back(Tensor{n, dims, type, ones});
+    auto add = [&](const std::string& n, std::vector<uint64_t> dims, uint32_t type, bool ones, float sd = 0.f) {
+        ts.push_back(Tensor{n, dims, type, ones, sd});
     };
+    const uint64_t kwd = (uint64_t)s->ssm_state * s->ssm_groups, vwd = s->ssm_inner;
+    const uint64_t channels = 2 * kwd + vwd, vh = s->ssm_value_heads;
     add("token_embd.weight", {s->dim, s->vocab}, s->type_embed, false);
     for (uint32_t i = 0; i < s->layers; ++i) {
         std::string p = "blk." + std::to_string(i) + ".";
         add(p + "attn_norm.weight", {s->dim}, F32, true);
-        add(p + "attn_q.weight", {s->dim, qw}, s->type_attn_q, false);
-        add(p + "attn_k.weight", {s->dim, kw}, s->type_attn_k, false);
-        add(p + "attn_v.weight", {s->dim, kw}, s->type_attn_v, false);
-        add(p + "attn_output.weight", {qw, s->dim}, s->type_attn_output, false);
-        if (s->qk_norm) {
-            add(p + "attn_q_norm.weight", {hd}, F32, true);
-            add(p + "attn_k_norm.weight", {hd}, F32, true);
+        const bool delta = q35 && s->full_attention_interval && (i + 1) % s->full_attention_interval != 0;
+        if (delta) {  // runtime.rs:315-324 names and shapes
+            add(p + "attn_qkv.weight", {s->dim, channels}, s->type_ssm, false);
+            add(p + "attn_gate.weight", {s->dim, vwd}, s->type_ssm, false);
+            add(p + "ssm_conv1d.weight", {s->ssm_conv_kernel, channels}, F32, false, 0.5f);
+            add(p + "ssm_alpha.weight", {s->dim, vh}, s->type_ssm, false);
+            add(p + "ssm_beta.weight", {s->dim, vh}, s->type_ssm, false);
+            add(p + "ssm_a", {vh}, F32, false, -1.f);
+            add(p + "ssm_dt", {vh}, F32, false, 0.5f);
+            add(p + "ssm_norm.weight", {vwd / vh}, F32, true);
+            add(p + "ssm_out.weight", {vwd, s->dim}, s->type_ssm, false);
+        } else {
+            add(p + "attn_q.weight", {s->dim, q35 ? 2 * qw : qw}, s->type_attn_q, false);
+            add(p + "attn_k.weight", {s->dim, kw}, s->type_attn_k, false);
+            add(p + "attn_v.weight", {s->dim, kw}, s->type_attn_v, false);
+            add(p + "attn_output.weight", {qw, s->dim}, s->type_attn_output, false);
+            if (s->qk_norm) {
+                add(p + "attn_q_norm.weight", {hd}, F32, true);
+                add(p + "attn_k_norm.weight", {hd}, F32, true);
+            }
         }
-        add(p + "ffn_norm.weight", {s->dim}, F32, true);
+        add(p + (q35 ? "post_attention_norm.weight" : "ffn_norm.weight"), {s->dim}, F32, true);
         add(p + "ffn_gate.weight", {s->dim, s->ffn}, s->type_ffn_gate, false);
         add(p + "ffn_up.weight", {s->dim, s->ffn}, s->type_ffn_up, false);
         add(p + "ffn_down.weight", {s->ffn, s->dim}, s->type_ffn_down, false);
@@ -438,8 +462,7 @@ int evs_build(const evs_model_spec* s, uint8_t** out, size_t* out_len) {
     h.b.insert(h.b.end(), {'G', 'G', 'U', 'F'});
     h.put<uint32_t>(3);
     h.put<uint64_t>(ts.size());
-    const std::string a = s->arch[0] ? s->arch : "qwen3";
-    const uint32_t n_kv = 13;
+    const uint32_t n_kv = 13 + (q35 ? 6 : 0) + (s->rope_dim ? 1 : 0) + (s->mrope_interleaved ? 1 : 0);
     h.put<uint64_t>(n_kv);
     h.kv_str("general.architecture", a);
     h.kv_str("general.name", "evelyn-synthetic");
@@ -454,6 +477,16 @@ int evs_build(const evs_model_spec* s, uint8_t** out, size_t* out_len) {
     h.kv_f32(a + ".rope.freq_base", s->rope_base);
     h.kv_f32(a + ".attention.layer_norm_rms_epsilon", s->eps);
     h.kv_u32("tokenizer.ggml.eos_token_id", s->eos_token_id);
+    if (q35) {  // runtime.rs:225-235, 258
+        h.kv_u32(a + ".ssm.conv_kernel", s->ssm_conv_kernel);
+        h.kv_u32(a + ".ssm.inner_size", s->ssm_inner);
+        h.kv_u32(a + ".ssm.state_size", s->ssm_state);
+        h.kv_u32(a + ".ssm.group_count", s->ssm_groups);
+        h.kv_u32(a + ".ssm.time_step_rank", s->ssm_value_heads);
+        h.kv_u32(a + ".full_attention_interval", s->full_attention_interval);
+    }
+    if (s->rope_dim) h.kv_u32(a + ".rope.dimension_count", s->rope_dim);
+    if (s->mrope_interleaved) h.kv_bool(a + ".rope.mrope_interleaved", true);
     for (auto& t : ts) {
         h.str(t.name);
         h.put<uint32_t>((uint32_t)t.dims.size());
@@ -488,6 +521,15 @@ int evs_build(const evs_model_spec* s, uint8_t** out, size_t* out_len) {
             continue;
         }
         const uint64_t key = mix(s->seed * 0x100000001B3ULL + ti + 1);
+        if (t.sd != 0.f) {  // small F32 vectors: N(0, sd), or (sd < 0) decay rates -(0.25 + |N(0, 1)|)
+            std::vector<float> x(n + (n & 1));
+            gen_normal(key, 0, x.size(), t.sd > 0 ? t.sd : 1.0f, x.data());
+            for (uint64_t i = 0; i < n; ++i) {
+                const float v = t.sd > 0 ? x[i] : -(0.25f + std::fabs(x[i]));
+                std::memcpy(dst + 4 * i, &v, 4);
+            }
+            continue;
+        }
         const size_t be = block_elems(t.type), bb = block_bytes(t.type);
         const size_t chunk_blocks = std::max<size_t>(1, 65536 / be);
         const size_t nblocks = n / be;

@@ -1,5 +1,5 @@
 /*
- * synth_gguf.h -- seeded synthetic GGUF images for Qwen3-family decoders, and
+ * synth_gguf.h -- seeded synthetic GGUF images for Qwen3 / Qwen3.5-family decoders, and
  * the GGUF block encoders behind them (the reference ships dequantisers only).
  * Tooling for tests and benchmarks; not part of the decode path.
  */
@@ -22,6 +22,14 @@ typedef struct {
     uint32_t eos_token_id;
     uint64_t seed;
     int32_t threads;          /* <= 0: all hardware threads */
+    /* arch "qwen35" (runtime.rs:225-235, 276-371): layer i is a gated-delta layer unless
+       (i + 1) % full_attention_interval == 0; full-attention layers carry the gated query
+       (attn_q rows = 2 * heads * head_dim); every layer's FFN norm is post_attention_norm. */
+    uint32_t full_attention_interval;
+    uint32_t ssm_conv_kernel, ssm_state, ssm_groups, ssm_value_heads, ssm_inner;
+    uint32_t type_ssm;        /* attn_qkv, attn_gate, ssm_alpha, ssm_beta, ssm_out */
+    uint32_t rope_dim;        /* rope.dimension_count (0: not written, = head_dim) */
+    uint32_t mrope_interleaved; /* rope.mrope_interleaved = true */
 } evs_model_spec;
 
 const char* evs_last_error(void);

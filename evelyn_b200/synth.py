@@ -35,6 +35,9 @@ class _Spec(C.Structure):
         ("type_ffn_down", C.c_uint32), ("type_embed", C.c_uint32), ("type_output", C.c_uint32),
         ("qk_norm", C.c_uint32), ("tied_output", C.c_uint32), ("eos_token_id", C.c_uint32),
         ("seed", C.c_uint64), ("threads", C.c_int32),
+        ("full_attention_interval", C.c_uint32), ("ssm_conv_kernel", C.c_uint32), ("ssm_state", C.c_uint32),
+        ("ssm_groups", C.c_uint32), ("ssm_value_heads", C.c_uint32), ("ssm_inner", C.c_uint32),
+        ("type_ssm", C.c_uint32), ("rope_dim", C.c_uint32), ("mrope_interleaved", C.c_uint32),
     ]
 
 
@@ -64,6 +67,16 @@ class ModelSpec:
     eos_token_id: int = 151645
     seed: int = 0
     arch: str = "qwen3"
+    # arch "qwen35": gated-delta layers except every full_attention_interval-th
+    full_attention_interval: int = 4
+    ssm_conv_kernel: int = 4
+    ssm_state: int = 64        # key_dim
+    ssm_groups: int = 2        # key heads
+    ssm_value_heads: int = 4
+    ssm_inner: int = 256       # value_heads * value_dim
+    ssm_type: int = GGML_Q8_0  # attn_qkv, attn_gate, ssm_alpha, ssm_beta, ssm_out
+    rope_dim: int = 0          # 0: head_dim (key not written)
+    mrope_interleaved: bool = False
 
     def with_types(self, t: int) -> "ModelSpec":
         return dataclasses.replace(self, attn_q=t, attn_k=t, attn_v=t, attn_output=t, ffn_gate=t, ffn_up=t,
@@ -85,6 +98,15 @@ class ModelSpec:
 
 
 # The decoder shapes of the benchmark configurations.
+def qwen35_tiny(**kw) -> ModelSpec:
+    """A small Qwen3.5-style hybrid decoder (runtime.rs:455-630): gated-delta layers with
+    one gated full-attention layer in every four, interleaved rotary positions."""
+    base = dict(layers=4, dim=256, ffn=512, heads=4, kv_heads=2, head_dim=64, vocab=1024, arch="qwen35",
+                mrope_interleaved=True)
+    base.update(kw)
+    return ModelSpec(**base)
+
+
 def qwen3_0_6b(**kw) -> ModelSpec:
     """Qwen3-0.6B shape, every linear weight Q8_0."""
     return ModelSpec(layers=28, dim=1024, ffn=3072, heads=16, kv_heads=8, **kw).with_types(GGML_Q8_0)
@@ -163,6 +185,11 @@ def build(spec: ModelSpec, threads: int = 0) -> GGUFImage:
     s.qk_norm = int(spec.qk_norm)
     s.tied_output = int(spec.tied_output)
     s.threads = threads
+    for f in ("full_attention_interval", "ssm_conv_kernel", "ssm_state", "ssm_groups", "ssm_value_heads",
+              "ssm_inner", "rope_dim"):
+        setattr(s, f, getattr(spec, f))
+    s.type_ssm = spec.ssm_type
+    s.mrope_interleaved = int(spec.mrope_interleaved)
     p = C.c_void_p()
     n = C.c_size_t()
     _check(_lib().evs_build(C.byref(s), C.byref(p), C.byref(n)))

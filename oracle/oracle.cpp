@@ -12,15 +12,17 @@
 //   * Model::load            src/runtime.rs:199-406 (metadata keys, defaults, tied LM head)
 //   * dense_ffn / SiLU       src/runtime.rs:409-418, src/activation.rs:50
 //   * rope_neox / interleave src/runtime.rs:437-474
-//   * full_attention         src/runtime.rs:663-768 (f32 KV, softmax order, w/sum*v)
+//   * full_attention         src/runtime.rs:663-768 (f32 KV, softmax order, w/sum*v; the
+//                            gated query of qwen35, :684-695, :753-761)
+//   * gated-delta layers     src/runtime.rs:476-630 (sigmoid, softplus, SiLU x*sigmoid(x),
+//                            causal depthwise conv, gated delta rule, per-head norm and gate)
 //   * Session::step          src/runtime.rs:773-808
 //   * argmax / log_prob      src/runtime.rs:897-912, validate_token_ids :125-135
 //
 // Built with -ffp-contract=off so that a*b-c*d is two roundings and a subtraction,
 // exactly like the Rust source (rustc never contracts to FMA). Transcendentals call
 // glibc's powf/sinf/cosf/expf/sqrtf, which are what Rust's f32 methods lower to on
-// Linux. Out of scope (returns Unsupported): the Qwen3.5 gated-delta layers and the
-// gated query of `qwen35` (runtime.rs:112-120, 494-630, 686-695).
+// Linux (log1pf for `ln_1p`).
 
 #include "oracle.h"
 
@@ -572,18 +574,34 @@ struct QMatrix {  // runtime.rs:23-51
     }
 };
 
+struct SsmConfig {  // runtime.rs:112-120
+    size_t conv_kernel = 0, inner = 0, state = 0, groups = 0, value_heads = 0;
+};
+
 struct Config {  // runtime.rs:93-110
     std::string arch;
     size_t layers = 0, dim = 0, ffn = 0, heads = 0, kv_heads = 0, head_dim = 0, rope_dim = 0, vocab = 0;
     float rope_base = 10000.0f, eps = 1e-6f;
     bool rope_interleaved = false;
+    size_t full_attention_interval = 4;
+    bool has_ssm = false;
+    SsmConfig ssm;
     int64_t eos = -1;
 };
 
-struct Layer {  // runtime.rs:142-181 (full attention only)
+struct GatedDelta {  // runtime.rs:155-170
+    QMatrix qkv, z, alpha, beta, out;
+    std::vector<float> conv, a, dt, norm;
+    size_t conv_kernel = 0, key_dim = 0, key_heads = 0, value_dim = 0, value_heads = 0;
+};
+
+struct Layer {  // runtime.rs:142-181
     std::vector<float> attn_norm, ffn_norm, q_norm, k_norm;
     bool has_q_norm = false, has_k_norm = false;
+    bool delta = false;  // Attention::GatedDelta (else Attention::Full)
+    bool gated = false;  // Full: the q projection interleaves a sigmoid gate per head (qwen35)
     QMatrix q, k, v, o, gate, up, down;
+    GatedDelta gd;
 };
 
 // runtime.rs:193-196
@@ -627,6 +645,42 @@ void rope_interleaved(float* v, size_t heads, size_t hd, size_t rotary_dim, size
             s[i] = a * cs - b * sn;
             s[i + 1] = a * sn + b * cs;
         }
+    }
+}
+
+// runtime.rs:476-483
+inline float sigmoid(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+
+// runtime.rs:485-487
+inline float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// runtime.rs:489-491: the SiLU of the gated-delta layers, x * sigmoid(x) (the FFN's is
+// activation.rs's z / (1 + e^-z))
+inline float silu_sigmoid(float x) { return x * sigmoid(x); }
+
+// runtime.rs:493-528: state [width][nv] row-major (key, value); decay, then the delta
+// rule's correction, then the read-out by q over sqrt(width).
+void gated_delta_step(float* state, const float* q, const float* k, const float* v, size_t width, size_t nv,
+                      float decay, float beta, float* out) {
+    for (size_t value = 0; value < nv; ++value)
+        for (size_t key = 0; key < width; ++key) state[key * nv + value] *= decay;
+    std::vector<float> delta(nv);
+    for (size_t value = 0; value < nv; ++value) {
+        float predicted = 0.0f;
+        for (size_t key = 0; key < width; ++key) predicted += state[key * nv + value] * k[key];
+        delta[value] = (v[value] - predicted) * beta;
+    }
+    for (size_t key = 0; key < width; ++key)
+        for (size_t value = 0; value < nv; ++value) state[key * nv + value] += k[key] * delta[value];
+    const float root = sqrtf((float)width);
+    for (size_t value = 0; value < nv; ++value) {
+        float acc = 0.0f;
+        for (size_t key = 0; key < width; ++key) acc += state[key * nv + value] * q[key];
+        out[value] = acc / root;
     }
 }
 
@@ -677,8 +731,14 @@ struct orc_model {
         uint64_t hd;
         const Value* kl = g.meta(arch + ".attention.key_length");
         cfg.head_dim = (kl && kl->as_u64(&hd)) ? hd : cfg.dim / cfg.heads;
-        if (arch == "qwen35")
-            raise(UNSUPPORTED, "qwen35 gated-delta layers are outside this oracle's scope");
+        if (arch == "qwen35") {  // runtime.rs:225-235
+            cfg.has_ssm = true;
+            cfg.ssm.conv_kernel = need("ssm.conv_kernel");
+            cfg.ssm.inner = need("ssm.inner_size");
+            cfg.ssm.state = need("ssm.state_size");
+            cfg.ssm.groups = need("ssm.group_count");
+            cfg.ssm.value_heads = need("ssm.time_step_rank");
+        }
         cfg.layers = need("block_count");
         cfg.ffn = need("feed_forward_length");
         double f;
@@ -689,6 +749,9 @@ struct orc_model {
         cfg.rope_dim = (rdv && rdv->as_u64(&rd)) ? rd : cfg.head_dim;
         const Value* ri = g.meta(arch + ".rope.mrope_interleaved");
         cfg.rope_interleaved = ri && ri->kind == Value::BOOL && ri->b;
+        uint64_t fai;
+        const Value* fav = g.meta(arch + ".full_attention_interval");
+        cfg.full_attention_interval = (fav && fav->as_u64(&fai)) ? fai : 4;  // runtime.rs:258
         const Value* ep = g.meta(arch + ".attention.layer_norm_rms_epsilon");
         cfg.eps = (ep && ep->as_f64(&f)) ? (float)f : 1e-6f;
         auto te = g.tensors.find("token_embd.weight");
@@ -708,19 +771,54 @@ struct orc_model {
         for (size_t i = 0; i < cfg.layers; ++i) {
             std::string p = "blk." + std::to_string(i) + ".";
             Layer& L = layers[i];
-            if (g.tensors.count(p + "attn_qkv.weight"))
-                raise(UNSUPPORTED, p + "gated-delta layers are outside this oracle's scope");
-            L.q = mat(p + "attn_q.weight");
-            L.k = mat(p + "attn_k.weight");
-            L.v = mat(p + "attn_v.weight");
-            L.o = mat(p + "attn_output.weight");
-            if (g.tensors.count(p + "attn_q_norm.weight")) {
-                L.q_norm = g.tensor_f32(p + "attn_q_norm.weight");
-                L.has_q_norm = true;
+            const bool has_gated_delta = g.tensors.count(p + "attn_qkv.weight") != 0;
+            if (arch == "qwen35" && cfg.full_attention_interval > 0) {  // runtime.rs:278-290
+                const bool expected = (i + 1) % cfg.full_attention_interval != 0;
+                if (has_gated_delta != expected)
+                    raise(INVALID_DATA, p + "attention type does not match qwen35.full_attention_interval=" +
+                                            std::to_string(cfg.full_attention_interval));
             }
-            if (g.tensors.count(p + "attn_k_norm.weight")) {
-                L.k_norm = g.tensor_f32(p + "attn_k_norm.weight");
-                L.has_k_norm = true;
+            if (has_gated_delta) {  // runtime.rs:298-356
+                if (!cfg.has_ssm) raise(INVALID_DATA, "gated-delta tensors found without SSM architecture metadata");
+                GatedDelta& d = L.gd;
+                L.delta = true;
+                d.key_dim = cfg.ssm.state;
+                d.key_heads = cfg.ssm.groups;
+                d.value_heads = cfg.ssm.value_heads;
+                if (d.value_heads == 0 || cfg.ssm.inner % d.value_heads != 0)
+                    raise(INVALID_DATA, "Qwen3.5 SSM inner size must divide evenly across value heads");
+                d.value_dim = cfg.ssm.inner / d.value_heads;
+                d.conv_kernel = cfg.ssm.conv_kernel;
+                d.qkv = mat(p + "attn_qkv.weight");
+                d.z = mat(p + "attn_gate.weight");
+                d.conv = g.tensor_f32(p + "ssm_conv1d.weight");
+                d.alpha = mat(p + "ssm_alpha.weight");
+                d.beta = mat(p + "ssm_beta.weight");
+                d.a = g.tensor_f32(p + "ssm_a");
+                d.dt = g.tensor_f32(p + "ssm_dt");
+                d.norm = g.tensor_f32(p + "ssm_norm.weight");
+                d.out = mat(p + "ssm_out.weight");
+                const size_t channels = 2 * d.key_dim * d.key_heads + d.value_dim * d.value_heads;
+                if (d.qkv.rows != channels || d.z.rows != d.value_dim * d.value_heads ||
+                    d.conv.size() != d.conv_kernel * channels || d.alpha.rows != d.value_heads ||
+                    d.beta.rows != d.value_heads || d.a.size() != d.value_heads || d.dt.size() != d.value_heads ||
+                    d.norm.size() != d.value_dim || d.out.cols != d.value_dim * d.value_heads ||
+                    d.out.rows != cfg.dim)
+                    raise(INVALID_DATA, p + "gated-delta tensor shapes do not match Qwen3.5 metadata");
+            } else {
+                L.q = mat(p + "attn_q.weight");
+                L.k = mat(p + "attn_k.weight");
+                L.v = mat(p + "attn_v.weight");
+                L.o = mat(p + "attn_output.weight");
+                if (g.tensors.count(p + "attn_q_norm.weight")) {
+                    L.q_norm = g.tensor_f32(p + "attn_q_norm.weight");
+                    L.has_q_norm = true;
+                }
+                if (g.tensors.count(p + "attn_k_norm.weight")) {
+                    L.k_norm = g.tensor_f32(p + "attn_k_norm.weight");
+                    L.has_k_norm = true;
+                }
+                L.gated = arch == "qwen35";  // runtime.rs:371
             }
             std::string ffn_norm_name = g.tensors.count(p + "post_attention_norm.weight")
                                             ? p + "post_attention_norm.weight"
@@ -749,22 +847,93 @@ struct orc_model {
     }
 };
 
+struct GatedDeltaState {  // runtime.rs:532-549
+    std::vector<float> conv_history;  // the last kernel - 1 un-convolved projection rows
+    std::vector<float> recurrent;     // [value_heads][key_dim][value_dim]
+};
+
 struct orc_session {  // runtime.rs:634-661
     const orc_model* model;
     std::vector<std::vector<float>> k_cache, v_cache;
+    std::vector<GatedDeltaState> delta;  // per layer (empty for full-attention layers)
     size_t pos = 0;
 };
 
 namespace {
 
-// runtime.rs:663-768 (non-gated Full attention)
+// runtime.rs:551-630
+std::vector<float> gated_delta_attention(const GatedDelta& d, GatedDeltaState& st, const float* x, float eps) {
+    const size_t key_width = d.key_dim * d.key_heads, value_width = d.value_dim * d.value_heads;
+    const size_t channels = 2 * key_width + value_width;
+    std::vector<float> projection(channels), z(value_width);
+    d.qkv.matvec(x, projection.data());
+    d.z.matvec(x, z.data());
+    // the previous kernel - 1 projections, then this token; one depthwise causal
+    // convolution per channel
+    const size_t history_len = st.conv_history.size();
+    std::vector<float> conv_input(st.conv_history);
+    conv_input.insert(conv_input.end(), projection.begin(), projection.end());
+    std::vector<float> conv_output(channels);
+    for (size_t ch = 0; ch < channels; ++ch) {
+        float sum = 0.0f;
+        for (size_t tap = 0; tap < d.conv_kernel; ++tap)
+            sum += conv_input[tap * channels + ch] * d.conv[ch * d.conv_kernel + tap];
+        conv_output[ch] = silu_sigmoid(sum);
+    }
+    if (history_len > 0)
+        std::copy(conv_input.end() - (std::ptrdiff_t)history_len, conv_input.end(), st.conv_history.begin());
+    std::vector<float> alpha(d.value_heads), beta(d.value_heads);
+    d.alpha.matvec(x, alpha.data());
+    d.beta.matvec(x, beta.data());
+    std::vector<float> output(value_width, 0.0f);
+    for (size_t head = 0; head < d.value_heads; ++head) {
+        const size_t key_head = head % d.key_heads;
+        std::vector<float> q(conv_output.begin() + key_head * d.key_dim,
+                             conv_output.begin() + (key_head + 1) * d.key_dim);
+        std::vector<float> k(conv_output.begin() + key_width + key_head * d.key_dim,
+                             conv_output.begin() + key_width + (key_head + 1) * d.key_dim);
+        const float* v = conv_output.data() + 2 * key_width + head * d.value_dim;
+        float qs = 0.0f, ks = 0.0f;
+        for (float e : q) qs += e * e;
+        for (float e : k) ks += e * e;
+        const float q_norm = sqrtf(qs + eps), k_norm = sqrtf(ks + eps);
+        for (auto& e : q) e /= q_norm;
+        for (auto& e : k) e /= k_norm;
+        const float decay = expf(softplus(alpha[head] + d.dt[head]) * d.a[head]);
+        const float b = sigmoid(beta[head]);
+        float* state = st.recurrent.data() + head * d.key_dim * d.value_dim;
+        gated_delta_step(state, q.data(), k.data(), v, d.key_dim, d.value_dim, decay, b,
+                         output.data() + head * d.value_dim);
+    }
+    // per-head RMSNorm and the projected SiLU gate after the recurrent update
+    for (size_t head = 0; head < d.value_heads; ++head) {
+        float* o = output.data() + head * d.value_dim;
+        std::vector<float> normalized = rms_norm(o, d.value_dim, d.norm.data(), eps);
+        for (size_t i = 0; i < d.value_dim; ++i) o[i] = normalized[i] * silu_sigmoid(z[head * d.value_dim + i]);
+    }
+    std::vector<float> y(d.out.rows);
+    d.out.matvec(output.data(), y.data());
+    return y;
+}
+
+// runtime.rs:663-768
 std::vector<float> full_attention(const Layer& layer, const float* xn, const Config& c, size_t pos,
                                   std::vector<float>& k_cache, std::vector<float>& v_cache) {
-    std::vector<float> qv(layer.q.rows), kv(layer.k.rows), vv(layer.v.rows);
-    layer.q.matvec(xn, qv.data());
+    std::vector<float> projected(layer.q.rows), kv(layer.k.rows), vv(layer.v.rows);
+    layer.q.matvec(xn, projected.data());
     layer.k.matvec(xn, kv.data());
     layer.v.matvec(xn, vv.data());
     size_t query_width = c.heads * c.head_dim;
+    std::vector<float> qv, query_gate;
+    if (layer.gated) {  // runtime.rs:687-693: per head [query | gate]
+        for (size_t h = 0; h < c.heads; ++h) {
+            const float* st = projected.data() + h * c.head_dim * 2;
+            qv.insert(qv.end(), st, st + c.head_dim);
+            query_gate.insert(query_gate.end(), st + c.head_dim, st + 2 * c.head_dim);
+        }
+    } else {
+        qv = std::move(projected);
+    }
     size_t kv_heads = layer.k.rows / c.head_dim;
     size_t group = c.heads / kv_heads;
     if (layer.has_q_norm) {
@@ -818,6 +987,8 @@ std::vector<float> full_attention(const Layer& layer, const float* xn, const Con
             float w = scores[p];
             for (size_t d = 0; d < hd; ++d) out[d] += w / sum * vp[d];
         }
+        if (layer.gated)  // runtime.rs:753-761
+            for (size_t d = 0; d < hd; ++d) out[d] *= sigmoid(query_gate[head * hd + d]);
     });
     std::vector<float> y(layer.o.rows);
     layer.o.matvec(att.data(), y.data());
@@ -911,6 +1082,12 @@ int orc_model_config(const orc_model* m, orc_config* o) {
     o->rope_base = m->cfg.rope_base;
     o->eps = m->cfg.eps;
     o->rope_interleaved = m->cfg.rope_interleaved;
+    o->full_attention_interval = m->cfg.full_attention_interval;
+    o->ssm_conv_kernel = m->cfg.ssm.conv_kernel;
+    o->ssm_inner = m->cfg.ssm.inner;
+    o->ssm_state = m->cfg.ssm.state;
+    o->ssm_groups = m->cfg.ssm.groups;
+    o->ssm_value_heads = m->cfg.ssm.value_heads;
     o->eos_token_id = m->cfg.eos;
     return OK;
 }
@@ -963,6 +1140,15 @@ int orc_session_new(const orc_model* m, orc_session** out) {
     s->model = m;
     s->k_cache.resize(m->cfg.layers);
     s->v_cache.resize(m->cfg.layers);
+    s->delta.resize(m->cfg.layers);
+    for (size_t i = 0; i < m->layers.size(); ++i) {  // runtime.rs:539-548
+        const Layer& L = m->layers[i];
+        if (!L.delta) continue;
+        const GatedDelta& d = L.gd;
+        const size_t channels = 2 * d.key_dim * d.key_heads + d.value_dim * d.value_heads;
+        s->delta[i].conv_history.assign((d.conv_kernel - 1) * channels, 0.0f);
+        s->delta[i].recurrent.assign(d.value_heads * d.key_dim * d.value_dim, 0.0f);
+    }
     *out = s;
     return OK;
 }
@@ -990,7 +1176,9 @@ int orc_session_step(orc_session* s, uint32_t token, orc_ffn_fn ffn, void* ctx, 
         for (size_t li = 0; li < m->layers.size(); ++li) {
             const Layer& layer = m->layers[li];
             std::vector<float> normalized = rms_norm(x.data(), c.dim, layer.attn_norm.data(), c.eps);
-            std::vector<float> a = full_attention(layer, normalized.data(), c, s->pos, s->k_cache[li], s->v_cache[li]);
+            std::vector<float> a =
+                layer.delta ? gated_delta_attention(layer.gd, s->delta[li], normalized.data(), c.eps)
+                            : full_attention(layer, normalized.data(), c, s->pos, s->k_cache[li], s->v_cache[li]);
             for (size_t i = 0; i < x.size(); ++i) x[i] += a[i];
             std::vector<float> fin = rms_norm(x.data(), c.dim, layer.ffn_norm.data(), c.eps);
             const float* fo;
@@ -1028,6 +1216,15 @@ int orc_session_fill_kv(orc_session* s, uint64_t n, uint64_t seed) {
     }
     s->pos += n;
     return OK;
+}
+
+void orc_gated_delta_step(float* state, const float* q, const float* k, const float* v, size_t width, size_t nv,
+                          float decay, float beta, float* out) {
+    gated_delta_step(state, q, k, v, width, nv, decay, beta, out);
+}
+
+void orc_rope_interleaved(float* v, size_t heads, size_t hd, size_t rotary_dim, size_t pos, float base) {
+    rope_interleaved(v, heads, hd, rotary_dim, pos, base);
 }
 
 uint32_t orc_argmax(const float* v, size_t n) {  // runtime.rs:897-905: strict '>' keeps the first max

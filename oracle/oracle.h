@@ -33,6 +33,8 @@ typedef struct {
     float rope_base, eps;
     int32_t rope_interleaved;
     int64_t eos_token_id; /* -1 when absent */
+    uint64_t full_attention_interval;
+    uint64_t ssm_conv_kernel, ssm_inner, ssm_state, ssm_groups, ssm_value_heads; /* 0 without SSM metadata */
 } orc_config;
 
 const char* orc_last_error(void);
@@ -73,6 +75,10 @@ int orc_session_fill_kv(orc_session* s, uint64_t n, uint64_t seed);
 
 /* runtime.rs:125, :897, :908 */
 int orc_validate_token_ids(const uint32_t* ids, size_t n, size_t vocab);
+/* runtime.rs:493-528 and 455-474, for their known-answer tests */
+void orc_gated_delta_step(float* state, const float* q, const float* k, const float* v, size_t width, size_t nv,
+                          float decay, float beta, float* out);
+void orc_rope_interleaved(float* v, size_t heads, size_t hd, size_t rotary_dim, size_t pos, float base);
 uint32_t orc_argmax(const float* v, size_t n);
 uint32_t orc_sample_token(const float* logits, size_t n, float temperature, uint64_t* state);
 float orc_log_prob(const float* logits, size_t n, uint32_t target);

@@ -36,6 +36,9 @@ class Config(C.Structure):
         ("rope_base", C.c_float), ("eps", C.c_float),
         ("rope_interleaved", C.c_int32),
         ("eos_token_id", C.c_int64),
+        ("full_attention_interval", C.c_uint64),
+        ("ssm_conv_kernel", C.c_uint64), ("ssm_inner", C.c_uint64), ("ssm_state", C.c_uint64),
+        ("ssm_groups", C.c_uint64), ("ssm_value_heads", C.c_uint64),
     ]
 
 
@@ -83,6 +86,10 @@ def lib():
         L.orc_session_step.argtypes = [C.c_void_p, C.c_uint32, FFN_FN, C.c_void_p, f]
         L.orc_session_fill_kv.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64]
         L.orc_validate_token_ids.argtypes = [C.POINTER(C.c_uint32), C.c_size_t, C.c_size_t]
+        L.orc_gated_delta_step.restype = None
+        L.orc_gated_delta_step.argtypes = [f, f, f, f, C.c_size_t, C.c_size_t, C.c_float, C.c_float, f]
+        L.orc_rope_interleaved.restype = None
+        L.orc_rope_interleaved.argtypes = [f, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_float]
         L.orc_argmax.restype = C.c_uint32
         L.orc_argmax.argtypes = [f, C.c_size_t]
         L.orc_sample_token.restype = C.c_uint32
@@ -132,6 +139,22 @@ def dequantize(t: int, raw: bytes | np.ndarray, n: int) -> np.ndarray:
 def validate_token_ids(ids, vocab: int):
     a = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
     _check(lib().orc_validate_token_ids(a.ctypes.data_as(C.POINTER(C.c_uint32)), a.size, vocab))
+
+
+def gated_delta_step(state: np.ndarray, q, k, v, decay: float, beta: float) -> np.ndarray:
+    """runtime.rs:493-528 on a [len(q), len(v)] f32 state, updated in place; returns the read-out."""
+    q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+    assert state.dtype == np.float32 and state.flags.c_contiguous and state.size == q.size * v.size
+    out = np.empty(v.size, dtype=np.float32)
+    lib().orc_gated_delta_step(_fp(state), _fp(q), _fp(k), _fp(v), q.size, v.size, decay, beta, _fp(out))
+    return out
+
+
+def rope_interleaved(v: np.ndarray, heads: int, hd: int, rotary_dim: int, pos: int, base: float) -> np.ndarray:
+    """runtime.rs:455-474 on a copy of v."""
+    out = np.array(v, dtype=np.float32)
+    lib().orc_rope_interleaved(_fp(out), heads, hd, rotary_dim, pos, base)
+    return out
 
 
 def argmax(v: np.ndarray) -> int:
