@@ -265,6 +265,23 @@ evl_status evl_model_config(const evl_model* model, evl_config* o) {
     });
 }
 
+evl_status evl_model_ssm_config(const evl_model* model, evl_ssm_config* o) {
+    return guarded([&] {
+        require(model && o, "null argument");
+        const Model& m = *model->m;
+        const Config& c = m.cfg;
+        std::memset(o, 0, sizeof(*o));
+        o->has_ssm = c.has_ssm;
+        o->delta_layers = m.delta_layers;
+        o->full_attention_interval = c.full_attention_interval;
+        o->conv_kernel = c.ssm_conv_kernel;
+        o->inner = c.ssm_inner;
+        o->state = c.ssm_state;
+        o->groups = c.ssm_groups;
+        o->value_heads = c.ssm_value_heads;
+    });
+}
+
 uint64_t evl_model_weight_bytes(const evl_model* model) { return model ? model->m->weight_bytes_per_step : 0; }
 
 evl_status evl_model_dense_ffn(evl_model* model, size_t layer, const float* x, float* y) {

@@ -147,6 +147,21 @@ struct Config {
     float rope_base = 10000.f, eps = 1e-6f;
     bool rope_interleaved = false;
     int64_t eos = -1;
+    // Qwen3.5 (runtime.rs:106-120, 225-235, 258)
+    uint64_t full_attention_interval = 4;
+    bool has_ssm = false;
+    uint64_t ssm_conv_kernel = 0, ssm_inner = 0, ssm_state = 0, ssm_groups = 0, ssm_value_heads = 0;
+};
+
+// A Qwen3.5 gated-delta layer (runtime.rs:155-170): key_dim = ssm_state, key_heads =
+// ssm_groups, value_dim = ssm_inner / value_heads.
+struct DeltaWeights {
+    QMatrix qkv, z, alpha, beta, out;
+    float* conv = nullptr;  // [channels][kernel]
+    float* a = nullptr;     // [value_heads]
+    float* dt = nullptr;    // [value_heads]
+    float* norm = nullptr;  // [value_dim]
+    uint32_t index = 0;     // among the model's gated-delta layers (its state slot)
 };
 
 struct LayerWeights {
@@ -155,6 +170,10 @@ struct LayerWeights {
     float* ffn_norm = nullptr;
     float* q_norm = nullptr;  // null when the GGUF has no attn_q_norm
     float* k_norm = nullptr;
+    bool delta = false;       // Attention::GatedDelta: `d` holds it and q/k/v/o are empty
+    bool gated = false;       // qwen35 full attention: `qg` is the query gate
+    QMatrix qg;               // the gate rows of the interleaved attn_q (runtime.rs:687-693)
+    DeltaWeights d;
 };
 
 struct Model {
@@ -175,6 +194,8 @@ struct Model {
     std::map<std::string, QMatrix*> matrices;
     std::map<std::string, std::pair<float*, size_t>> vecs;
     uint64_t weight_bytes_per_step = 0;
+    // Qwen3.5: gated-delta layer count and sizes (0 for other models)
+    uint32_t delta_layers = 0, delta_channels = 0, delta_value_width = 0;
 
     // GEMM-layout copies of every layer matrix and the LM head, built on the device the
     // first time a batch of more than one sequence is created (build_gemm_weights)
@@ -247,6 +268,9 @@ struct StepBuffers {
     uint32_t max_ctx = 0, pages_per_seq = 0;
     DeviceBuffer kv, page_table, pos, tokens, argmax, hist, err;
     DeviceBuffer x, q, k, v, att, h, y, logits, xn, part, amax_v, amax_i;
+    // Qwen3.5: query gate; gated-delta projections (qkv channels, z, alpha | beta), the
+    // recurrent output, and per sequence the conv history (two copies) and states
+    DeviceBuffer qgate, dproj, dz, dab, dout, dhist, dstate;
     DeviceBuffer gbx, gxinv, gpart, gpart2, gpart3;  // batched products: staged x, 2^-e, partial sums
     uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
     KvTmap kv_tmap{};             // the KV pool for the attention's tensor-core path
@@ -303,6 +327,7 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     // Enqueue one dense step (every kernel) on `stream`.
     void enqueue_dense(bool pdl);
     void enqueue_layer_attention(uint32_t layer, bool pdl);
+    void enqueue_delta(uint32_t layer, bool pdl);  // a Qwen3.5 gated-delta layer's attention half
     void enqueue_head(bool pdl);
     void gather_peer_logits();
     // A step with a routed-FFN hook (eager, synchronising at routed layers).

@@ -1,0 +1,186 @@
+// gated_delta.cu -- the recurrent half of a Qwen3.5 gated-delta layer
+// (gated_delta_attention, src/runtime.rs:551-630, and gated_delta_step, :493-528), and
+// the sigmoid query gate of its full-attention layers (:753-761).
+//
+// The projections around it are ordinary matvec launches: attn_qkv and attn_gate (z)
+// in one, ssm_alpha and ssm_beta in a second, ssm_out with the residual add after it.
+// One CTA per (value head, sequence) then does everything between:
+//   * the depthwise causal convolution of the channels it reads (its key head's q and
+//     k channels, its own v channels) over the kernel - 1 previous projections and this
+//     token's, then x * sigmoid(x);
+//   * the L2 normalisation of q and k (sqrt(sum + eps));
+//   * decay = exp(softplus(alpha + dt) * a), beta = sigmoid(beta);
+//   * the delta rule on its [key_dim][value_dim] state, one thread per value column:
+//     the decayed column's prediction k.S, the correction (v - k.S) * beta added as
+//     k (x) delta, the read-out q.S / sqrt(key_dim); the state is read twice (the second
+//     read from L2) and written once;
+//   * the per-head RMSNorm with ssm_norm and the SiLU(z) gate.
+// Products and sums keep the reference's f32 operation order where it is sequential
+// (one rounding per multiply and per add, no fused multiply-add), except the q, k and
+// output sums of squares, which are block reductions.
+//
+// Convolution history. A key head's q and k channels are read by every value head that
+// maps to it (head % key_heads) but written by one; so that no CTA reads history that
+// another has already moved on, each sequence keeps two copies of its kernel - 1 rows
+// and the token at position p reads copy p % 2 and writes copy (p + 1) % 2. The CTA of
+// value head h writes its v channels and, when h < key_heads, key head h's q and k
+// channels (a key head that no value head maps to is never read).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace evl {
+
+namespace {
+
+constexpr int kThreads = 128;
+
+// runtime.rs:476-483
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    const float e = expf(x);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
+// runtime.rs:485-487
+__device__ __forceinline__ float softplus_ref(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// sum over the block (kThreads threads); every thread gets the total
+__device__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // red may still be read by a previous call
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+    return t;
+}
+
+__global__ void __launch_bounds__(kThreads) gated_delta_kernel(const __grid_constant__ GatedDeltaArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float red[kThreads / 32];
+    const uint32_t KD = a.key_dim, VD = a.value_dim, CH = a.channels, KW = a.key_dim * a.key_heads;
+    float* qs = sm;         // [KD] q, then q / |q|
+    float* ks = qs + KD;    // [KD]
+    float* vs = ks + KD;    // [VD]
+    float* os = vs + VD;    // [VD] the read-out
+    const uint32_t head = blockIdx.x, seq = blockIdx.y, kh = head % a.key_heads;
+    const int tid = threadIdx.x;
+    pdl_wait();
+    const int32_t p = a.pos[seq];
+    const uint32_t K1 = a.kernel - 1;
+    const float* proj = a.proj + (uint64_t)seq * CH;
+    const float* hr = a.hist + (uint64_t)seq * a.hist_stride + (uint64_t)(p & 1) * K1 * CH;
+    float* hw = a.hist + (uint64_t)seq * a.hist_stride + (uint64_t)((p + 1) & 1) * K1 * CH;
+    // ---- convolution (runtime.rs:562-579) of this CTA's 2 KD + VD channels
+    for (uint32_t i = tid; i < 2 * KD + VD; i += kThreads) {
+        const uint32_t ch = i < KD ? kh * KD + i : i < 2 * KD ? KW + kh * KD + (i - KD) : 2 * KW + head * VD + (i - 2 * KD);
+        float sum = 0.0f;
+        for (uint32_t tap = 0; tap < a.kernel; ++tap) {
+            const float in = tap < K1 ? hr[(uint64_t)tap * CH + ch] : proj[ch];
+            sum = __fadd_rn(sum, __fmul_rn(in, a.conv[(uint64_t)ch * a.kernel + tap]));
+        }
+        const float c = __fmul_rn(sum, sigmoid_ref(sum));
+        if (i < KD) qs[i] = c; else if (i < 2 * KD) ks[i - KD] = c; else vs[i - 2 * KD] = c;
+        if (i >= 2 * KD || head == kh)  // this CTA owns the channel's history
+            for (uint32_t tap = 0; tap < K1; ++tap)
+                hw[(uint64_t)tap * CH + ch] = tap + 1 < K1 ? hr[(uint64_t)(tap + 1) * CH + ch] : proj[ch];
+    }
+    __syncthreads();
+    // ---- q and k over their L2 norms (runtime.rs:596-600)
+    float sq = 0.f, sk = 0.f;
+    for (uint32_t i = tid; i < KD; i += kThreads) {
+        sq += qs[i] * qs[i];
+        sk += ks[i] * ks[i];
+    }
+    const float qn = __fsqrt_rn(__fadd_rn(block_sum(sq, red), a.eps));
+    const float kn = __fsqrt_rn(__fadd_rn(block_sum(sk, red), a.eps));
+    for (uint32_t i = tid; i < KD; i += kThreads) {
+        qs[i] = __fdiv_rn(qs[i], qn);
+        ks[i] = __fdiv_rn(ks[i], kn);
+    }
+    const float* ab = a.ab + (uint64_t)seq * 2 * a.value_heads;
+    const float decay = expf(__fmul_rn(softplus_ref(__fadd_rn(ab[head], a.dt[head])), a.a[head]));
+    const float beta = sigmoid_ref(ab[a.value_heads + head]);
+    __syncthreads();
+    // ---- the delta rule (runtime.rs:493-528), one thread per value column
+    float* S = a.state + (uint64_t)seq * a.state_stride + (uint64_t)head * KD * VD;
+    const float root = __fsqrt_rn((float)KD);
+    for (uint32_t v = tid; v < VD; v += kThreads) {
+        float pred = 0.0f;
+        for (uint32_t key = 0; key < KD; ++key)
+            pred = __fadd_rn(pred, __fmul_rn(__fmul_rn(S[(uint64_t)key * VD + v], decay), ks[key]));
+        const float delta = __fmul_rn(__fsub_rn(vs[v], pred), beta);
+        float acc = 0.0f;
+        for (uint32_t key = 0; key < KD; ++key) {
+            const uint64_t o = (uint64_t)key * VD + v;
+            const float s = __fadd_rn(__fmul_rn(S[o], decay), __fmul_rn(ks[key], delta));
+            S[o] = s;
+            acc = __fadd_rn(acc, __fmul_rn(s, qs[key]));
+        }
+        os[v] = __fdiv_rn(acc, root);
+    }
+    __syncthreads();
+    // ---- per-head RMSNorm and the SiLU(z) gate (runtime.rs:617-628, 193-196)
+    float ss = 0.f;
+    for (uint32_t v = tid; v < VD; v += kThreads) ss += os[v] * os[v];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(block_sum(ss, red), (float)VD), a.eps)));
+    const uint64_t o0 = (uint64_t)seq * a.value_heads * VD + (uint64_t)head * VD;
+    for (uint32_t v = tid; v < VD; v += kThreads) {
+        const float zz = a.z[o0 + v];
+        a.out[o0 + v] = __fmul_rn(__fmul_rn(__fmul_rn(os[v], inv), a.norm[v]), __fmul_rn(zz, sigmoid_ref(zz)));
+    }
+}
+
+__global__ void sigmoid_gate_kernel(float* __restrict__ x, const float* __restrict__ gate, uint64_t n) {
+    pdl_wait();
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        x[i] = __fmul_rn(x[i], sigmoid_ref(gate[i]));
+}
+
+cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+}  // namespace
+
+size_t gated_delta_smem(uint32_t key_dim, uint32_t value_dim) { return 4ull * (2 * key_dim + 2 * value_dim); }
+
+cudaError_t launch_gated_delta(const GatedDeltaArgs& a, cudaStream_t s, bool pdl) {
+    if (!a.proj || !a.z || !a.ab || !a.conv || !a.a || !a.dt || !a.norm || !a.hist || !a.state || !a.out || !a.pos)
+        return cudaErrorInvalidValue;
+    if (!a.batch || !a.kernel || !a.key_dim || !a.key_heads || !a.value_dim || !a.value_heads ||
+        a.channels != 2 * a.key_dim * a.key_heads + a.value_dim * a.value_heads)
+        return cudaErrorInvalidValue;
+    if (a.hist_stride < 2ull * (a.kernel - 1) * a.channels ||
+        a.state_stride < (uint64_t)a.value_heads * a.key_dim * a.value_dim)
+        return cudaErrorInvalidValue;
+    const size_t smem = gated_delta_smem(a.key_dim, a.value_dim);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;  // key_dim + value_dim up to 6144
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3(a.value_heads, a.batch), dim3(kThreads), smem, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, gated_delta_kernel, a);
+}
+
+cudaError_t launch_sigmoid_gate(float* x, const float* gate, uint64_t n, cudaStream_t s, bool pdl) {
+    if (!x || !gate || !n) return cudaErrorInvalidValue;
+    cudaLaunchAttribute at[1];
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 1184);
+    auto cfg = cfg_of(dim3(blocks), dim3(256), 0, s, pdl, at);
+    return cudaLaunchKernelEx(&cfg, sigmoid_gate_kernel, x, gate, n);
+}
+
+}  // namespace evl

@@ -51,6 +51,31 @@ struct MatvecArgs {
 // matrix, or a gate and up of two types, runs as launch_plain_matvec.
 cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
 
+// ---------------------------------------------------------------- gated_delta.cu
+// The recurrent half of a Qwen3.5 gated-delta layer (runtime.rs:551-630) between its
+// projections and ssm_out: conv, q/k normalisation, the delta rule on the state, the
+// per-head norm and SiLU(z) gate. One CTA per (value head, sequence).
+struct GatedDeltaArgs {
+    const float* proj = nullptr;   // [batch][channels] attn_qkv output (q | k | v channels)
+    const float* z = nullptr;      // [batch][value_heads * value_dim] attn_gate output
+    const float* ab = nullptr;     // [batch][2 * value_heads] ssm_alpha | ssm_beta outputs
+    const float* conv = nullptr;   // [channels][kernel]
+    const float* a = nullptr;      // [value_heads]
+    const float* dt = nullptr;     // [value_heads]
+    const float* norm = nullptr;   // [value_dim]
+    float* hist = nullptr;         // per sequence [2][kernel - 1][channels] (copy pos % 2 read)
+    float* state = nullptr;        // per sequence [value_heads][key_dim][value_dim]
+    float* out = nullptr;          // [batch][value_heads * value_dim]
+    const int32_t* pos = nullptr;  // [batch] this token's position
+    uint32_t batch = 1, channels = 0, kernel = 0, key_dim = 0, key_heads = 0, value_dim = 0, value_heads = 0;
+    uint64_t hist_stride = 0, state_stride = 0;  // floats per sequence
+    float eps = 1e-6f;
+};
+size_t gated_delta_smem(uint32_t key_dim, uint32_t value_dim);
+cudaError_t launch_gated_delta(const GatedDeltaArgs& a, cudaStream_t s, bool pdl);
+// x[i] *= sigmoid(gate[i]) (the gated query, runtime.rs:753-761)
+cudaError_t launch_sigmoid_gate(float* x, const float* gate, uint64_t n, cudaStream_t s, bool pdl);
+
 // plain_matvec.cu: the same launch, warp per row, for unquantised matrices (a
 // quantised matrix in it is read through the exact dequantiser).
 bool matvec_has_plain(const MatvecArgs& a);

@@ -29,6 +29,9 @@ struct Planned {
     size_t stride;           // bytes between rows in `raw`
     uint32_t col_byte0 = 0;  // byte offset of the shard's first column within a row
     uint32_t col_bytes = 0;  // bytes per row in the shard (0: whole row)
+    // row selection (0: rows in order): row r of the matrix is source row
+    // (r / run) * period + offset + r % run -- one half of each head's interleaved rows
+    uint32_t run = 0, period = 0, offset = 0;
 };
 
 uint32_t block_elems(uint32_t t) {
@@ -128,8 +131,14 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     const GgufValue* kl = g.meta(arch + ".attention.key_length");
     if (c.heads == 0) raise(EVL_ERR_INVALID_DATA, arch + ".attention.head_count is zero");
     c.head_dim = (kl && kl->as_u64(&u64)) ? u64 : c.dim / c.heads;
-    if (arch == "qwen35")
-        raise(EVL_ERR_UNSUPPORTED, "qwen35 gated-delta layers are not part of the device decode path");
+    if (arch == "qwen35") {  // runtime.rs:225-235
+        c.has_ssm = true;
+        c.ssm_conv_kernel = need("ssm.conv_kernel");
+        c.ssm_inner = need("ssm.inner_size");
+        c.ssm_state = need("ssm.state_size");
+        c.ssm_groups = need("ssm.group_count");
+        c.ssm_value_heads = need("ssm.time_step_rank");
+    }
     c.layers = need("block_count");
     c.ffn = need("feed_forward_length");
     double f64;
@@ -141,6 +150,8 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     c.rope_interleaved = ri && ri->kind == GgufValue::BOOL && ri->b;
     const GgufValue* ep = g.meta(arch + ".attention.layer_norm_rms_epsilon");
     c.eps = (ep && ep->as_f64(&f64)) ? (float)f64 : 1e-6f;
+    const GgufValue* fa = g.meta(arch + ".full_attention_interval");
+    c.full_attention_interval = (fa && fa->as_u64(&u64)) ? u64 : 4;  // runtime.rs:258
     c.vocab = g.has("token_embd.weight") && g.tensor("token_embd.weight").dims.size() > 1
                   ? g.tensor("token_embd.weight").dims[1]
                   : 0;
@@ -158,6 +169,8 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         raise(EVL_ERR_UNSUPPORTED,
               "GQA group size " + std::to_string(group) + " (device attention handles 1, 2, 4, 8)");
     const int T = m.tp_size, R = m.tp_rank;
+    if (c.has_ssm && T > 1)
+        raise(EVL_ERR_UNSUPPORTED, "tensor parallelism over Qwen3.5 gated-delta layers is not supported");
     const TpShard sh = tp_shard_plan(c, T, R);
     m.lkv_heads = (uint32_t)(c.kv_heads / T);
     m.lheads = (uint32_t)(c.heads / T);
@@ -204,6 +217,24 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         plan.push_back(p);
         m.matrices[name] = &q;
     };
+    // the query or the gate half of a gated attn_q (runtime.rs:687-693: per head
+    // [query | gate], head_dim rows each), as a matrix of its own
+    auto add_query_half = [&](QMatrix& q, const std::string& name, bool gate_half) {
+        add_matrix(q, name, 2 * qw, c.dim, 0, 0, 0, 0);
+        m.matrices.erase(name);
+        q.name = name + (gate_half ? ":gate" : ":query");
+        q.rows = (uint32_t)qw;
+        repack_sizes(q);
+        Planned& pl = plan.back();
+        pl.run = (uint32_t)hd;
+        pl.period = (uint32_t)(2 * hd);
+        pl.offset = gate_half ? (uint32_t)hd : 0;
+        m.matrices[q.name] = &q;
+    };
+    auto dims_of = [&](const std::string& name) {
+        const GgufTensor& t = g.tensor(name);
+        return std::make_pair(t.dims.size() > 0 ? t.dims[0] : 0, t.dims.size() > 1 ? t.dims[1] : 1);
+    };
 
     const uint64_t f0 = sh.ffn[0], f1 = sh.ffn[1], v0 = sh.vocab[0], v1 = sh.vocab[1];
     m.lffn = (uint32_t)(f1 - f0);
@@ -213,12 +244,66 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     add_matrix(m.embed, "token_embd.weight", 0, c.dim, 0, 0, 0, 0);
     m.layers.resize(c.layers);
     const uint64_t hq0 = sh.q[0], hq1 = sh.q[1], hk0 = sh.kv[0], hk1 = sh.kv[1];
+    uint64_t key_dim = 0, key_heads = 0, value_heads = 0, value_dim = 0, channels = 0;
+    if (c.has_ssm) {
+        key_dim = c.ssm_state;
+        key_heads = c.ssm_groups;
+        value_heads = c.ssm_value_heads;
+    }
     for (uint64_t i = 0; i < c.layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
-        if (g.has(p + "attn_qkv.weight"))
-            raise(EVL_ERR_UNSUPPORTED, p + "gated-delta layers are not part of the device decode path");
         LayerWeights& L = m.layers[i];
-        add_matrix(L.q, p + "attn_q.weight", qw, c.dim, hq0, hq1, 0, 0);
+        const bool has_delta = g.has(p + "attn_qkv.weight");
+        if (arch == "qwen35" && c.full_attention_interval > 0 &&  // runtime.rs:278-290
+            has_delta != ((i + 1) % c.full_attention_interval != 0))
+            raise(EVL_ERR_INVALID_DATA, p + "attention type does not match qwen35.full_attention_interval=" +
+                                            std::to_string(c.full_attention_interval));
+        if (has_delta) {  // runtime.rs:298-356
+            if (!c.has_ssm)
+                raise(EVL_ERR_INVALID_DATA, "gated-delta tensors found without SSM architecture metadata");
+            if (value_heads == 0 || c.ssm_inner % value_heads)
+                raise(EVL_ERR_INVALID_DATA, "Qwen3.5 SSM inner size must divide evenly across value heads");
+            value_dim = c.ssm_inner / value_heads;
+            channels = 2 * key_dim * key_heads + value_dim * value_heads;
+            const uint64_t vw = value_dim * value_heads;
+            const std::string names[] = {"attn_qkv.weight", "attn_gate.weight", "ssm_conv1d.weight",
+                                         "ssm_alpha.weight", "ssm_beta.weight", "ssm_a",
+                                         "ssm_dt", "ssm_norm.weight", "ssm_out.weight"};
+            for (const auto& n : names) g.tensor(p + n);  // NotFound in the reference's order
+            auto elems = [&](const std::string& n) { return g.tensor(p + n).elements(); };
+            const auto qkv = dims_of(p + "attn_qkv.weight"), z = dims_of(p + "attn_gate.weight"),
+                       al = dims_of(p + "ssm_alpha.weight"), be = dims_of(p + "ssm_beta.weight"),
+                       out = dims_of(p + "ssm_out.weight");
+            if (qkv.second != channels || z.second != vw || elems("ssm_conv1d.weight") != c.ssm_conv_kernel * channels ||
+                al.second != value_heads || be.second != value_heads || elems("ssm_a") != value_heads ||
+                elems("ssm_dt") != value_heads || elems("ssm_norm.weight") != value_dim || out.first != vw ||
+                out.second != c.dim || qkv.first != c.dim || z.first != c.dim || al.first != c.dim || be.first != c.dim)
+                raise(EVL_ERR_INVALID_DATA, p + "gated-delta tensor shapes do not match Qwen3.5 metadata");
+            if (c.ssm_conv_kernel == 0 || key_dim == 0 || key_heads == 0)
+                raise(EVL_ERR_INVALID_DATA, p + "ssm.conv_kernel, ssm.state_size and ssm.group_count must be non-zero");
+            if (gated_delta_smem((uint32_t)key_dim, (uint32_t)value_dim) > 48 * 1024)
+                raise(EVL_ERR_UNSUPPORTED, p + "gated-delta key and value widths above 6144 values");
+            L.delta = true;
+            L.d.index = m.delta_layers++;
+            m.delta_channels = (uint32_t)channels;
+            m.delta_value_width = (uint32_t)vw;
+            add_matrix(L.d.qkv, p + "attn_qkv.weight", channels, c.dim, 0, 0, 0, 0);
+            add_matrix(L.d.z, p + "attn_gate.weight", vw, c.dim, 0, 0, 0, 0);
+            add_matrix(L.d.alpha, p + "ssm_alpha.weight", value_heads, c.dim, 0, 0, 0, 0);
+            add_matrix(L.d.beta, p + "ssm_beta.weight", value_heads, c.dim, 0, 0, 0, 0);
+            add_matrix(L.d.out, p + "ssm_out.weight", c.dim, vw, 0, 0, 0, 0);
+            add_matrix(L.gate, p + "ffn_gate.weight", c.ffn, c.dim, f0, f1, 0, 0);
+            add_matrix(L.up, p + "ffn_up.weight", c.ffn, c.dim, f0, f1, 0, 0);
+            add_matrix(L.down, p + "ffn_down.weight", c.dim, c.ffn, 0, 0, T > 1 ? f0 : 0, T > 1 ? f1 : 0);
+            continue;
+        }
+        if (arch == "qwen35") {  // the gated query (runtime.rs:371)
+            L.gated = true;
+            add_query_half(L.q, p + "attn_q.weight", false);
+            add_query_half(L.qg, p + "attn_q.weight", true);
+        } else {
+            add_matrix(L.q, p + "attn_q.weight", qw, c.dim, hq0, hq1, 0, 0);
+        }
         add_matrix(L.k, p + "attn_k.weight", kw, c.dim, hk0, hk1, 0, 0);
         add_matrix(L.v, p + "attn_v.weight", kw, c.dim, hk0, hk1, 0, 0);
         add_matrix(L.o, p + "attn_output.weight", c.dim, qw, 0, 0, T > 1 ? hq0 : 0, T > 1 ? hq1 : 0);
@@ -246,6 +331,13 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         const std::string fn = g.has(p + "post_attention_norm.weight") ? p + "post_attention_norm.weight"
                                                                          : p + "ffn_norm.weight";
         vplan.push_back({fn, &L.ffn_norm, c.dim});
+        if (L.delta) {
+            vplan.push_back({p + "ssm_conv1d.weight", &L.d.conv, channels * c.ssm_conv_kernel});
+            vplan.push_back({p + "ssm_a", &L.d.a, value_heads});
+            vplan.push_back({p + "ssm_dt", &L.d.dt, value_heads});
+            vplan.push_back({p + "ssm_norm.weight", &L.d.norm, value_dim});
+            continue;
+        }
         if (g.has(p + "attn_q_norm.weight")) vplan.push_back({p + "attn_q_norm.weight", &L.q_norm, hd});
         if (g.has(p + "attn_k_norm.weight")) vplan.push_back({p + "attn_k_norm.weight", &L.k_norm, hd});
     }
@@ -275,7 +367,7 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         place(*p.m, m.weights.as<uint8_t>());
         const size_t row = p.col_bytes ? p.col_bytes : p.stride;
         max_raw = std::max(max_raw, row * p.m->rows);
-        if (p.col_bytes) max_gather = std::max(max_gather, (size_t)p.col_bytes * p.m->rows);
+        if (p.col_bytes || p.run) max_gather = std::max(max_gather, row * p.m->rows);
     }
     std::vector<uint8_t> gather(max_gather);
     DeviceBuffer draw;
@@ -283,12 +375,14 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     for (auto& p : plan) {
         const uint8_t* src = p.raw;
         size_t stride = p.stride;
-        if (p.col_bytes) {
-            for (uint32_t r = 0; r < p.m->rows; ++r)
-                std::memcpy(gather.data() + (size_t)r * p.col_bytes, p.raw + (size_t)r * p.stride + p.col_byte0,
-                            p.col_bytes);
+        if (p.col_bytes || p.run) {
+            const size_t rb = p.col_bytes ? p.col_bytes : p.stride;
+            for (uint32_t r = 0; r < p.m->rows; ++r) {
+                const size_t sr = p.run ? (size_t)(r / p.run) * p.period + p.offset + r % p.run : r;
+                std::memcpy(gather.data() + (size_t)r * rb, p.raw + sr * p.stride + p.col_byte0, rb);
+            }
             src = gather.data();
-            stride = p.col_bytes;
+            stride = rb;
         }
         // (the legacy stream orders each copy after the previous repack that read the buffer)
         cuda_check(cudaMemcpy(draw.p, src, stride * p.m->rows, cudaMemcpyHostToDevice), "upload weights");
@@ -326,7 +420,8 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     // weight bytes one decode step streams on this rank
     uint64_t wb = 0;
     for (auto& L : m.layers)
-        wb += L.q.bytes() + L.k.bytes() + L.v.bytes() + L.o.bytes() + L.gate.bytes() + L.up.bytes() + L.down.bytes();
+        wb += L.q.bytes() + L.k.bytes() + L.v.bytes() + L.o.bytes() + L.gate.bytes() + L.up.bytes() + L.down.bytes() +
+              L.qg.bytes() + L.d.qkv.bytes() + L.d.z.bytes() + L.d.alpha.bytes() + L.d.beta.bytes() + L.d.out.bytes();
     wb += m.lm_head.bytes();
     m.weight_bytes_per_step = wb;
 

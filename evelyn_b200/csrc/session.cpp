@@ -107,6 +107,21 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* sh
     b.y.alloc(batch * std::max<uint64_t>(c.dim, m->lvocab) * 4);
     b.logits.alloc(batch * c.vocab * 4);
     b.xn.alloc(batch * c.dim * 4);
+    if (c.has_ssm) {  // Qwen3.5: query gates; gated-delta projections and per-sequence state
+        b.qgate.alloc(batch * qw * 4);
+        if (m->delta_layers) {
+            const uint64_t CH = m->delta_channels, VW = m->delta_value_width, VH = c.ssm_value_heads;
+            b.dproj.alloc(batch * CH * 4);
+            b.dz.alloc(batch * VW * 4);
+            b.dab.alloc(batch * 2 * VH * 4);
+            b.dout.alloc(batch * VW * 4);
+            // zero at the start of every sequence (runtime.rs:539-548)
+            b.dhist.alloc(std::max<uint64_t>(4, batch * m->delta_layers * 2 * (c.ssm_conv_kernel - 1) * CH * 4));
+            b.dstate.alloc((uint64_t)batch * m->delta_layers * VH * c.ssm_state * (c.ssm_inner / VH) * 4);
+            cuda_check(cudaMemset(b.dhist.p, 0, b.dhist.bytes), "memset");
+            cuda_check(cudaMemset(b.dstate.p, 0, b.dstate.bytes), "memset");
+        }
+    }
     // enough (kv_head, split) CTAs to cover the SMs twice
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
@@ -172,7 +187,8 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* sh
     host_pos.assign(batch, 0);
     // a batch of sequences on one GPU runs its products on the tensor cores
     const char* env = std::getenv("EVELYN_BATCH_GEMM");
-    if (batch > 1 && batch <= 32 && !(env && env[0] == '0') && build_gemm_weights(*m)) {
+    // (not for the Qwen3.5 hybrid layers, which run as matvecs per sequence)
+    if (batch > 1 && batch <= 32 && !(env && env[0] == '0') && !c.has_ssm && build_gemm_weights(*m)) {
         use_gemm = true;
         const uint64_t kmax = std::max<uint64_t>({c.dim, (uint64_t)m->lffn, qw});
         b.gbx.alloc(gemm_x_bytes(32, (uint32_t)kmax));
@@ -472,9 +488,27 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
     const uint32_t B = b.batch;
     const uint64_t hd = c.head_dim, qw = (uint64_t)m.lheads * hd, kw = (uint64_t)m.lkv_heads * hd;
     float* x = b.x.as<float>();
+    if (L.delta) {
+        enqueue_delta(li, pdl);
+        return;
+    }
     {
         const uint64_t ys[3] = {qw, kw, kw};
         matvec_each(qkv_args(li), B, c.dim, ys, stream, pdl, "qkv matvec");
+        kernels += B;
+    }
+    if (L.gated) {  // the query gate rows of attn_q (runtime.rs:687-693)
+        MatvecArgs a;
+        a.nseg = 1;
+        a.seg[0].m = L.qg.dev;
+        a.seg[0].y = b.qgate.as<float>();
+        a.x = x;
+        a.cols = (uint32_t)c.dim;
+        a.norm_w = L.attn_norm;
+        a.eps = c.eps;
+        a.err = b.err.as<int>();
+        const uint64_t ys[1] = {qw};
+        matvec_each(a, B, c.dim, ys, stream, pdl, "query gate matvec");
         kernels += B;
     }
     if (b.cluster_ring) {
@@ -487,6 +521,10 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         kernels += 1;
         cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
         kernels += 2;
+    }
+    if (L.gated) {  // attention output times sigmoid(gate) (runtime.rs:753-761)
+        cuda_check(launch_sigmoid_gate(b.att.as<float>(), b.qgate.as<float>(), B * qw, stream, pdl), "query gate");
+        kernels += 1;
     }
     {  // o-proj, residual add fused (TP: partial sums, all-reduce, then add)
         const bool tp = m.tp_size > 1;
@@ -513,6 +551,93 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
     }
 }
 
+// A Qwen3.5 gated-delta layer (runtime.rs:551-630): attn RMSNorm fused into the
+// attn_qkv + attn_gate launch and the ssm_alpha + ssm_beta launch, the recurrent kernel
+// (gated_delta.cu), then ssm_out with the residual add.
+void Decoder::enqueue_delta(uint32_t li, bool pdl) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const LayerWeights& L = m.layers[li];
+    const DeltaWeights& D = L.d;
+    const uint32_t B = b.batch, CH = m.delta_channels, VW = m.delta_value_width;
+    const uint32_t VH = (uint32_t)c.ssm_value_heads, KD = (uint32_t)c.ssm_state, VD = VW / VH;
+    float* x = b.x.as<float>();
+    MatvecArgs a;
+    a.x = x;
+    a.cols = (uint32_t)c.dim;
+    a.norm_w = L.attn_norm;
+    a.eps = c.eps;
+    a.err = b.err.as<int>();
+    {
+        MatvecArgs p = a;
+        p.nseg = 2;
+        p.seg[0].m = D.qkv.dev;
+        p.seg[0].y = b.dproj.as<float>();
+        p.seg[1].m = D.z.dev;
+        p.seg[1].y = b.dz.as<float>();
+        p.prefetch[0] = D.alpha.dev;
+        p.prefetch[1] = D.beta.dev;
+        p.prefetch[2] = D.out.dev;
+        p.prefetch_bytes = prefetch_kb(96) << 10;
+        const uint64_t ys[2] = {CH, VW};
+        matvec_each(p, B, c.dim, ys, stream, pdl, "gated-delta qkv/z matvec");
+        kernels += B;
+    }
+    {
+        MatvecArgs p = a;
+        p.nseg = 2;
+        p.seg[0].m = D.alpha.dev;
+        p.seg[0].y = b.dab.as<float>();
+        p.seg[1].m = D.beta.dev;
+        p.seg[1].y = b.dab.as<float>() + VH;
+        const uint64_t ys[2] = {2ull * VH, 2ull * VH};
+        matvec_each(p, B, c.dim, ys, stream, pdl, "gated-delta alpha/beta matvec");
+        kernels += B;
+    }
+    {
+        GatedDeltaArgs g;
+        g.proj = b.dproj.as<float>();
+        g.z = b.dz.as<float>();
+        g.ab = b.dab.as<float>();
+        g.conv = D.conv;
+        g.a = D.a;
+        g.dt = D.dt;
+        g.norm = D.norm;
+        g.batch = B;
+        g.channels = CH;
+        g.kernel = (uint32_t)c.ssm_conv_kernel;
+        g.key_dim = KD;
+        g.key_heads = (uint32_t)c.ssm_groups;
+        g.value_dim = VD;
+        g.value_heads = VH;
+        g.hist_stride = (uint64_t)m.delta_layers * 2 * (g.kernel - 1) * CH;
+        g.state_stride = (uint64_t)m.delta_layers * VH * KD * VD;
+        g.hist = b.dhist.as<float>() + (uint64_t)D.index * 2 * (g.kernel - 1) * CH;
+        g.state = b.dstate.as<float>() + (uint64_t)D.index * VH * KD * VD;
+        g.out = b.dout.as<float>();
+        g.pos = b.pos.as<int32_t>();
+        g.eps = c.eps;
+        cuda_check(launch_gated_delta(g, stream, pdl), "gated delta");
+        kernels += 1;
+    }
+    {  // ssm_out, residual add fused
+        MatvecArgs p;
+        p.nseg = 1;
+        p.seg[0].m = D.out.dev;
+        p.seg[0].y = x;
+        p.seg[0].epi = EPI_ADD;
+        p.x = b.dout.as<float>();
+        p.cols = VW;
+        p.err = b.err.as<int>();
+        p.prefetch[0] = L.gate.dev;
+        p.prefetch[1] = L.up.dev;
+        p.prefetch_bytes = prefetch_kb(96) << 10;
+        const uint64_t ys[1] = {c.dim};
+        matvec_each(p, B, VW, ys, stream, pdl, "ssm_out matvec");
+        kernels += B;
+    }
+}
+
 // The persistent whole-step kernel for a single sequence (decode_step.cu): every layer
 // and the LM head in one cooperative launch, phases handing vectors on as tagged words.
 // Opt-in with EVELYN_STEP_KERNEL=1: it is correct (tested against the launch sequence
@@ -528,6 +653,10 @@ void Decoder::build_step_kernel() {
     if (b.batch != 1) return;
     if (m.tp_size != 1) {
         step_note = "step kernel not used: tensor parallelism";
+        return;
+    }
+    if (c.has_ssm) {
+        step_note = "step kernel not used: Qwen3.5 gated-delta and gated-query layers";
         return;
     }
     int sms = 148;

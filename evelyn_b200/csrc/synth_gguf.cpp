@@ -447,7 +447,8 @@ int evs_build(const evs_model_spec* s, uint8_t** out, size_t* out_len) {
     for (auto& t : ts) {
         uint64_t n = 1;
         for (auto d : t.dims) n *= d;
-        if (n % block_elems(t.type) != 0 ||
+        // (norm weights and the small F32 vectors are written element by element)
+        if ((!t.ones && t.sd == 0.f && n % block_elems(t.type) != 0) ||
             (t.type != F32 && t.type != F16 && t.type != BF16 && t.dims[0] % block_elems(t.type) != 0)) {
             g_err = t.name + ": row length is not a whole number of quant blocks";
             return 2;

@@ -50,6 +50,14 @@ class _Config(C.Structure):
     ]
 
 
+class _SsmConfig(C.Structure):
+    _fields_ = [
+        ("has_ssm", C.c_int32), ("delta_layers", C.c_uint32), ("full_attention_interval", C.c_uint64),
+        ("conv_kernel", C.c_uint64), ("inner", C.c_uint64), ("state", C.c_uint64), ("groups", C.c_uint64),
+        ("value_heads", C.c_uint64),
+    ]
+
+
 class _Options(C.Structure):
     _fields_ = [
         ("struct_size", C.c_uint32), ("device", C.c_int32), ("tp_rank", C.c_int32), ("tp_size", C.c_int32),
@@ -118,6 +126,7 @@ SIGNATURES = {
     "evl_model_dequantize": (C.c_int, [_P, C.c_char_p, _F, C.c_size_t]),
     "evl_model_matvec": (C.c_int, [_P, C.c_char_p, _F, C.c_size_t, _F, C.c_size_t]),
     "evl_model_weight_bytes": (C.c_uint64, [_P]),
+    "evl_model_ssm_config": (C.c_int, [_P, C.POINTER(_SsmConfig)]),
     "evl_session_new": (C.c_int, [_P, C.c_uint32, C.POINTER(_P)]),
     "evl_session_free": (None, [_P]),
     "evl_session_pos": (C.c_uint64, [_P]),
@@ -290,6 +299,16 @@ class Model:
     @property
     def weight_bytes(self) -> int:
         return int(lib().evl_model_weight_bytes(self._h))
+
+    @property
+    def ssm_config(self) -> dict:
+        """Config::full_attention_interval and SsmConfig (runtime.rs:106-120), with the
+        number of gated-delta layers; has_ssm False for models other than qwen35."""
+        c = _SsmConfig()
+        _check(lib().evl_model_ssm_config(self._h, C.byref(c)))
+        return {"has_ssm": bool(c.has_ssm), "delta_layers": c.delta_layers,
+                "full_attention_interval": c.full_attention_interval, "conv_kernel": c.conv_kernel,
+                "inner": c.inner, "state": c.state, "groups": c.groups, "value_heads": c.value_heads}
 
     def dense_ffn(self, layer: int, x: np.ndarray) -> np.ndarray:
         """runtime.rs:409-418, on the device."""

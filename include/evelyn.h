@@ -115,6 +115,16 @@ evl_status evl_model_load_memory(const void* data, size_t len, const evl_model_o
 void evl_model_free(evl_model* model);
 /* Model.cfg (src/runtime.rs:185) */
 evl_status evl_model_config(const evl_model* model, evl_config* out);
+/* Config::full_attention_interval and SsmConfig (src/runtime.rs:106-120) of a Qwen3.5
+ * ("qwen35") model, whose layers are gated-delta layers except every interval-th one
+ * (gated full attention). All zero but full_attention_interval for other models. */
+typedef struct evl_ssm_config {
+    int32_t has_ssm;
+    uint32_t delta_layers; /* layers with Attention::GatedDelta */
+    uint64_t full_attention_interval;
+    uint64_t conv_kernel, inner, state, groups, value_heads;
+} evl_ssm_config;
+evl_status evl_model_ssm_config(const evl_model* model, evl_ssm_config* out);
 /* Model::dense_ffn (src/runtime.rs:409-418): host x[dim] -> host y[dim], on the device.
  * With tp_size > 1 every rank must make the same call (it runs a collective). */
 evl_status evl_model_dense_ffn(evl_model* model, size_t layer, const float* x, float* y);

@@ -141,11 +141,15 @@ class _Ref:
         return self.W("output.weight", s.vocab) @ _rms(x, self.t("output_norm.weight"), s.eps)
 
 
-@pytest.mark.parametrize("interleaved,rope_dim", [(True, 0), (False, 32)])
-def test_hybrid_step_matches_float64_restatement(interleaved, rope_dim):
-    spec = synth.qwen35_tiny(seed=21, mrope_interleaved=interleaved, rope_dim=rope_dim)
+ODD = dict(ssm_conv_kernel=2, ssm_groups=1, ssm_value_heads=3, ssm_inner=192, full_attention_interval=2)
+
+
+@pytest.mark.parametrize("interleaved,rope_dim,kw", [(True, 0, {}), (False, 32, {}), (True, 0, ODD)])
+def test_hybrid_step_matches_float64_restatement(interleaved, rope_dim, kw):
+    spec = synth.qwen35_tiny(seed=21, mrope_interleaved=interleaved, rope_dim=rope_dim, **kw)
     m = orc.Model(synth.build(spec))
-    assert m.cfg.full_attention_interval == 4 and m.cfg.ssm_value_heads == spec.ssm_value_heads
+    assert m.cfg.full_attention_interval == spec.full_attention_interval
+    assert m.cfg.ssm_value_heads == spec.ssm_value_heads
     ref, sess = _Ref(m, spec), orc.Session(m)
     if not interleaved:  # the NeoX split-half rotation
         def rope(v, heads):
