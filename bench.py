@@ -18,7 +18,8 @@ step, same context range); roofline = the dominant kernel (Q4_K dequant-matvec o
 ffn_gate shape 12288x4096) timed live; cpu_baseline = the CPU oracle (a restatement of
 the reference's runtime) on a bounded sample. Extra keys: bs32 (32 sequences, 2048-token
 prefix each, f16 KV pages, at every N), c1 (Qwen3-0.6B shape, all Q8_0, bs1, N = 1),
-c4 (the isolated kernel sweep, N = 1).
+c4 (the isolated kernel sweep, N = 1), c5 (Qwen3-32B shape, 8 sequences, N > 1), hybrid
+(a Qwen3.5-style gated-delta / gated-query hybrid, bs1, N = 1).
 """
 from __future__ import annotations
 
@@ -341,6 +342,9 @@ def run_ours(args):
                           f"(ctx {r['ctx0']}..{r['ctx0'] + 128}), f32 KV pages",
               "step_hbm": step_hbm(spec1, 4, r["ctx0"], 128, hbm, peak_kind, r["ms"])}
         del m1
+    hybrid = None
+    if world == 1 and not args.no_hybrid:  # Qwen3.5-style gated-delta / gated-query hybrid, bs1
+        hybrid = run_hybrid(evl, synth, args, hbm, peak_kind, local, W)
     c4 = run_c4_summary(args, hbm, peak_kind) if (rank == 0 and world == 1 and not args.no_c4) else None
     clk.__exit__(None, None, None)
     tok_s = K / (r1["ms"] / 1e3)
@@ -375,10 +379,57 @@ def run_ours(args):
             line["c4"] = c4
         if c5:
             line["c5"] = c5
+        if hybrid:
+            line["hybrid"] = hybrid
         emit_line(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_hybrid(evl, synth, args, hbm, peak_kind, local, W, prompt_len=128, K=128, cpu_steps=3):
+    """Qwen3.5-style hybrid decoder (synth.qwen35_hybrid_2b), bs1: 128 prompt tokens then
+    128 timed greedy steps, device time and end to end, like the headline line. Step
+    bytes: the engine's weight bytes, the full-attention layers' f32 KV over the timed
+    range, and the gated-delta layers' f32 recurrent state read and written; then the
+    oracle on the host cores for a few steps (the same prompt start)."""
+    spec = synth.qwen35_hybrid_2b(seed=0)
+    img = synth.build(spec)
+    m = evl.Model.load_memory(img, device=local, kv_f32=True)
+    sc = m.ssm_config
+    r = measure_bs1(evl, m, spec, prompt_len, K, W, 1)
+    full_layers = spec.layers - sc["delta_layers"]
+    kv_pos = 2 * full_layers * spec.kv_heads * spec.head_dim * 4
+    vd = spec.ssm_inner // spec.ssm_value_heads
+    state = sc["delta_layers"] * spec.ssm_value_heads * spec.ssm_state * vd * 4 * 2
+    step_bytes = m.weight_bytes + kv_pos * (r["ctx0"] + (K + 1) / 2) + state
+    gbs = step_bytes * K / (r["ms"] / 1e3) / 1e9
+    out = {"value": round(K / (r["ms"] / 1e3), 2), "unit": "tok/s", "ms_per_step": round(r["ms"] / K, 4),
+           "e2e": {"value": round(K / (r["e2e_ms"] / 1e3), 2), "unit": "tok/s"},
+           "workload": f"Qwen3.5-style hybrid decode bs1 ({spec.layers}L: {sc['delta_layers']} gated-delta + "
+                       f"{full_layers} gated full-attention, d{spec.dim}, {spec.ssm_value_heads} value heads x "
+                       f"{spec.ssm_state}x{vd} state, head_dim {spec.head_dim}), {prompt_len}-token prompt then "
+                       f"{K} greedy steps (ctx {r['ctx0']}..{r['ctx0'] + K}), f32 KV pages",
+           "kernels_per_step": r["kernels"],
+           "step_hbm": {"bytes_per_step": int(step_bytes), "recurrent_state_bytes": state,
+                        "achieved_gbs_per_gpu": round(gbs, 1), "frac": round(gbs / hbm, 4), "peak": hbm,
+                        "peak_source": peak_kind}}
+    del m
+    if not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        orc.set_threads(os.cpu_count() or 1)
+        om = orc.Model(img)
+        sess = orc.Session(om)
+        toks = np.random.default_rng(0).integers(0, spec.vocab, cpu_steps + 1)
+        sess.step(int(toks[0]))
+        t = time.perf_counter()
+        for tk in toks[1:]:
+            sess.step(int(tk))
+        sec = time.perf_counter() - t
+        out["cpu_baseline"] = {"value": round(cpu_steps / sec, 3), "unit": "tok/s", "cores": orc.threads(),
+                               "kind": "port", "sample": f"{cpu_steps} oracle steps at ctx 1..{cpu_steps + 1}"}
+        del sess, om
+    return out
 
 
 def prefill_batch(batch, B, P, vocab, rng, world):
@@ -757,6 +808,7 @@ def main():
     ap.add_argument("--reps", type=int, default=10, help="timed passes per sweep case")
     ap.add_argument("--no-c1", action="store_true", help="skip the Qwen3-0.6B-shape bs1 line")
     ap.add_argument("--no-c4", action="store_true", help="skip the kernel-sweep summary")
+    ap.add_argument("--no-hybrid", action="store_true", help="skip the Qwen3.5-style hybrid line")
     ap.add_argument("--no-c5", action="store_true", help="skip the Qwen3-32B-shape bs8 line (N > 1 only)")
     ap.add_argument("--c5-prompt", type=int, default=4096, help="prompt tokens per sequence of the 32B line")
     ap.add_argument("--c5-steps", type=int, default=64, help="timed batched steps of the 32B line")
