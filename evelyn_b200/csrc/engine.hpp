@@ -157,6 +157,7 @@ struct Config {
 // ssm_groups, value_dim = ssm_inner / value_heads.
 struct DeltaWeights {
     QMatrix qkv, z, alpha, beta, out;
+    QMatrix ab;             // alpha rows then beta rows, when the two share a type (else empty)
     float* conv = nullptr;  // [channels][kernel]
     float* a = nullptr;     // [value_heads]
     float* dt = nullptr;    // [value_heads]

@@ -2,8 +2,9 @@
 // (gated_delta_attention, src/runtime.rs:551-630, and gated_delta_step, :493-528), and
 // the sigmoid query gate of its full-attention layers (:753-761).
 //
-// The projections around it are ordinary matvec launches: attn_qkv and attn_gate (z)
-// in one, ssm_alpha and ssm_beta in a second, ssm_out with the residual add after it.
+// The projections around it are ordinary matvec launches: attn_qkv, attn_gate (z) and
+// ssm_alpha | ssm_beta (stacked at load into one matrix) in one, ssm_out with the
+// residual add after it.
 // One CTA per (value head, sequence) then does everything between:
 //   * the depthwise causal convolution of the channels it reads (its key head's q and
 //     k channels, its own v channels) over the kernel - 1 previous projections and this

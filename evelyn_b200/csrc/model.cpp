@@ -14,6 +14,7 @@
 // does not divide), LM head split by vocabulary rows, norms replicated.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -32,6 +33,9 @@ struct Planned {
     // row selection (0: rows in order): row r of the matrix is source row
     // (r / run) * period + offset + r % run -- one half of each head's interleaved rows
     uint32_t run = 0, period = 0, offset = 0;
+    // two tensors stacked as one matrix: rows from `split` on come from raw2
+    const uint8_t* raw2 = nullptr;
+    uint32_t split = 0;
 };
 
 uint32_t block_elems(uint32_t t) {
@@ -289,8 +293,24 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
             m.delta_value_width = (uint32_t)vw;
             add_matrix(L.d.qkv, p + "attn_qkv.weight", channels, c.dim, 0, 0, 0, 0);
             add_matrix(L.d.z, p + "attn_gate.weight", vw, c.dim, 0, 0, 0, 0);
-            add_matrix(L.d.alpha, p + "ssm_alpha.weight", value_heads, c.dim, 0, 0, 0, 0);
-            add_matrix(L.d.beta, p + "ssm_beta.weight", value_heads, c.dim, 0, 0, 0, 0);
+            // alpha and beta stacked, so they join the attn_qkv / attn_gate launch
+            // (EVELYN_DELTA_STACK=0: two matrices and a launch of their own)
+            const char* se = std::getenv("EVELYN_DELTA_STACK");
+            if (g.tensor(p + "ssm_alpha.weight").type == g.tensor(p + "ssm_beta.weight").type &&
+                !(se && se[0] == '0')) {
+                add_matrix(L.d.ab, p + "ssm_alpha.weight", value_heads, c.dim, 0, 0, 0, 0);
+                m.matrices.erase(p + "ssm_alpha.weight");
+                L.d.ab.name = p + "ssm_alpha.weight+ssm_beta.weight";
+                L.d.ab.rows = (uint32_t)(2 * value_heads);
+                repack_sizes(L.d.ab);
+                size_t nb2;
+                plan.back().raw2 = g.raw(g.tensor(p + "ssm_beta.weight"), &nb2);
+                plan.back().split = (uint32_t)value_heads;
+                m.matrices[L.d.ab.name] = &L.d.ab;
+            } else {
+                add_matrix(L.d.alpha, p + "ssm_alpha.weight", value_heads, c.dim, 0, 0, 0, 0);
+                add_matrix(L.d.beta, p + "ssm_beta.weight", value_heads, c.dim, 0, 0, 0, 0);
+            }
             add_matrix(L.d.out, p + "ssm_out.weight", c.dim, vw, 0, 0, 0, 0);
             add_matrix(L.gate, p + "ffn_gate.weight", c.ffn, c.dim, f0, f1, 0, 0);
             add_matrix(L.up, p + "ffn_up.weight", c.ffn, c.dim, f0, f1, 0, 0);
@@ -367,7 +387,7 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
         place(*p.m, m.weights.as<uint8_t>());
         const size_t row = p.col_bytes ? p.col_bytes : p.stride;
         max_raw = std::max(max_raw, row * p.m->rows);
-        if (p.col_bytes || p.run) max_gather = std::max(max_gather, row * p.m->rows);
+        if (p.col_bytes || p.run || p.raw2) max_gather = std::max(max_gather, row * p.m->rows);
     }
     std::vector<uint8_t> gather(max_gather);
     DeviceBuffer draw;
@@ -375,11 +395,12 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     for (auto& p : plan) {
         const uint8_t* src = p.raw;
         size_t stride = p.stride;
-        if (p.col_bytes || p.run) {
+        if (p.col_bytes || p.run || p.raw2) {
             const size_t rb = p.col_bytes ? p.col_bytes : p.stride;
             for (uint32_t r = 0; r < p.m->rows; ++r) {
                 const size_t sr = p.run ? (size_t)(r / p.run) * p.period + p.offset + r % p.run : r;
-                std::memcpy(gather.data() + (size_t)r * rb, p.raw + sr * p.stride + p.col_byte0, rb);
+                const uint8_t* row = p.raw2 && r >= p.split ? p.raw2 + (sr - p.split) * p.stride : p.raw + sr * p.stride;
+                std::memcpy(gather.data() + (size_t)r * rb, row + p.col_byte0, rb);
             }
             src = gather.data();
             stride = rb;
@@ -421,7 +442,8 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     uint64_t wb = 0;
     for (auto& L : m.layers)
         wb += L.q.bytes() + L.k.bytes() + L.v.bytes() + L.o.bytes() + L.gate.bytes() + L.up.bytes() + L.down.bytes() +
-              L.qg.bytes() + L.d.qkv.bytes() + L.d.z.bytes() + L.d.alpha.bytes() + L.d.beta.bytes() + L.d.out.bytes();
+              L.qg.bytes() + L.d.qkv.bytes() + L.d.z.bytes() + L.d.alpha.bytes() + L.d.beta.bytes() + L.d.ab.bytes() +
+              L.d.out.bytes();
     wb += m.lm_head.bytes();
     m.weight_bytes_per_step = wb;
 
