@@ -387,12 +387,13 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_hybrid(evl, synth, args, hbm, peak_kind, local, W, prompt_len=128, K=128, cpu_steps=3):
+def run_hybrid(evl, synth, args, hbm, peak_kind, local, W, prompt_len=128, K=None, cpu_steps=3):
     """Qwen3.5-style hybrid decoder (synth.qwen35_hybrid_2b), bs1: 128 prompt tokens then
     128 timed greedy steps, device time and end to end, like the headline line. Step
     bytes: the engine's weight bytes, the full-attention layers' f32 KV over the timed
     range, and the gated-delta layers' f32 recurrent state read and written; then the
     oracle on the host cores for a few steps (the same prompt start)."""
+    K = K or args.hybrid_steps
     spec = synth.qwen35_hybrid_2b(seed=0)
     img = synth.build(spec)
     m = evl.Model.load_memory(img, device=local, kv_f32=True)
@@ -809,6 +810,9 @@ def main():
     ap.add_argument("--no-c1", action="store_true", help="skip the Qwen3-0.6B-shape bs1 line")
     ap.add_argument("--no-c4", action="store_true", help="skip the kernel-sweep summary")
     ap.add_argument("--no-hybrid", action="store_true", help="skip the Qwen3.5-style hybrid line")
+    ap.add_argument("--hybrid-steps", type=int, default=128, help="timed steps of the hybrid line")
+    ap.add_argument("--hybrid-only", action="store_true",
+                    help="only the hybrid line, printed as its own JSON object (N = 1)")
     ap.add_argument("--no-c5", action="store_true", help="skip the Qwen3-32B-shape bs8 line (N > 1 only)")
     ap.add_argument("--c5-prompt", type=int, default=4096, help="prompt tokens per sequence of the 32B line")
     ap.add_argument("--c5-steps", type=int, default=64, help="timed batched steps of the 32B line")
@@ -819,6 +823,13 @@ def main():
     PROMPT = max(1, args.prompt)
     if args.sweep:
         run_sweep(args)
+    elif args.hybrid_only:
+        import torch
+        import evelyn_b200 as evl
+        from evelyn_b200 import synth
+        torch.cuda.set_device(0)
+        hbm, peak_kind = peaks()
+        emit_line({"hybrid": run_hybrid(evl, synth, args, hbm, peak_kind, 0, args.warmup)})
     elif args.impl == "reference":
         run_reference(args)
     else:
