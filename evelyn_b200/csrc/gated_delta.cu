@@ -62,6 +62,16 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
 // runtime.rs:485-487
 __device__ __forceinline__ float softplus_ref(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
+// 16-byte asynchronous copy global -> shared (completes at cp_async_wait)
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // sum over the block (kThreads threads); every thread gets the total
 __device__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -198,19 +208,33 @@ __global__ void __launch_bounds__(kThreads) gated_delta_slice_kernel(const __gri
     const float* hr = a.hist + (uint64_t)seq * a.hist_stride + (uint64_t)(p & 1) * K1 * CH;
     float* hw = a.hist + (uint64_t)seq * a.hist_stride + (uint64_t)((p + 1) & 1) * K1 * CH;
     float* St = a.state + (uint64_t)seq * a.state_stride + (uint64_t)head * KD * VD;
-    // ---- the state slice into shared memory (rows of C floats at column c0)
+    // ---- the state slice into shared memory (rows of C floats at column c0), in flight
+    // during the convolution and the q / k norms
     const uint32_t q4 = C / 4;
     for (uint32_t i = tid; i < KD * q4; i += kThreads)
-        reinterpret_cast<float4*>(Ss)[i] =
-            *reinterpret_cast<const float4*>(St + (uint64_t)(i / q4) * VD + c0 + 4 * (i % q4));
+        cp_async16(Ss + 4 * i, St + (uint64_t)(i / q4) * VD + c0 + 4 * (i % q4));
     // ---- convolution of the key head's q and k channels and this slice's v channels
+    // (up to 8 taps with their loads issued together, longer kernels tap by tap)
     for (uint32_t i = tid; i < 2 * KD + C; i += kThreads) {
         const uint32_t ch =
             i < KD ? kh * KD + i : i < 2 * KD ? KW + kh * KD + (i - KD) : 2 * KW + head * VD + c0 + (i - 2 * KD);
         float sum = 0.0f;
-        for (uint32_t tap = 0; tap < a.kernel; ++tap) {
-            const float in = tap < K1 ? hr[(uint64_t)tap * CH + ch] : proj[ch];
-            sum = __fadd_rn(sum, __fmul_rn(in, a.conv[(uint64_t)ch * a.kernel + tap]));
+        if (a.kernel <= 8) {
+            float in[8], w[8];
+#pragma unroll
+            for (uint32_t tap = 0; tap < 8; ++tap)
+                if (tap < a.kernel) {
+                    in[tap] = tap < K1 ? hr[(uint64_t)tap * CH + ch] : proj[ch];
+                    w[tap] = a.conv[(uint64_t)ch * a.kernel + tap];
+                }
+#pragma unroll
+            for (uint32_t tap = 0; tap < 8; ++tap)
+                if (tap < a.kernel) sum = __fadd_rn(sum, __fmul_rn(in[tap], w[tap]));
+        } else {
+            for (uint32_t tap = 0; tap < a.kernel; ++tap) {
+                const float in = tap < K1 ? hr[(uint64_t)tap * CH + ch] : proj[ch];
+                sum = __fadd_rn(sum, __fmul_rn(in, a.conv[(uint64_t)ch * a.kernel + tap]));
+            }
         }
         const float c = __fmul_rn(sum, sigmoid_ref(sum));
         if (i < KD) qs[i] = c; else if (i < 2 * KD) ks[i - KD] = c; else vs[i - 2 * KD] = c;
@@ -233,7 +257,8 @@ __global__ void __launch_bounds__(kThreads) gated_delta_slice_kernel(const __gri
     const float* ab = a.ab + (uint64_t)seq * 2 * a.value_heads;
     const float decay = expf(__fmul_rn(softplus_ref(__fadd_rn(ab[head], a.dt[head])), a.a[head]));
     const float beta = sigmoid_ref(ab[a.value_heads + head]);
-    __syncthreads();
+    cp_async_wait();  // this thread's slice copies
+    __syncthreads();  // everyone's, and the normalised q / k
     // ---- the delta rule: thread (key group kg, column c) takes keys kg, kg + G, ...
     const uint32_t kg = G > 1 ? tid / C : 0;
     const uint32_t cfirst = G > 1 ? tid % C : (uint32_t)tid, cstride = G > 1 ? C : (uint32_t)kThreads;

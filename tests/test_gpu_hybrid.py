@@ -101,7 +101,7 @@ def test_hybrid_batch_matches_oracle_per_sequence():
 def test_hybrid_routed_ffn_and_unsupported_paths():
     """The FFN hook sees the hybrid layers like any other (a host FFN from the oracle
     gives the oracle's logits); prefill, which needs the batched tensor-core products,
-    answers Unsupported for the hybrid model."""
+    and tensor parallelism answer Unsupported for the hybrid model."""
     spec = synth.qwen35_tiny(seed=3)
     img = synth.build(spec)
     m, r = evl.Model.load_memory(img, device=0), orc.Model(img)
@@ -122,4 +122,8 @@ def test_hybrid_routed_ffn_and_unsupported_paths():
     p = evl.Session(m, max_ctx=64)
     with pytest.raises(evl.EvelynError) as e:
         p.prefill(_tokens(8, spec.vocab, seed=1))
+    assert e.value.kind == "Unsupported"
+    # tensor parallelism is refused at load, before any communicator is made
+    with pytest.raises(evl.EvelynError) as e:
+        evl.Model.load_memory(img, device=0, tp_rank=0, tp_size=2, nccl_id=evl.tp_unique_id())
     assert e.value.kind == "Unsupported"
