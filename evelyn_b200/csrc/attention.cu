@@ -288,7 +288,8 @@ __global__ void attention_combine_kernel(const __grid_constant__ AttnArgs a) {
         L += p[HD + 1] * f;
         O += p[d] * f;
     }
-    a.out[(uint64_t)b * a.heads * HD + head * HD + d] = O / L;
+    const uint64_t o = (uint64_t)b * a.heads * HD + head * HD + d;
+    a.out[o] = a.gate ? __fmul_rn(O / L, sigmoid_ref(a.gate[o])) : O / L;
     pdl_launch_dependents();
 }
 

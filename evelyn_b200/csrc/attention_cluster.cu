@@ -650,7 +650,11 @@ __global__ void __launch_bounds__(kAW * 32, 1) attn_cluster_kernel(const __grid_
             const int c = __ffs(msk) - 1;
             O += cpart[(c * G + g) * (HD + 2) + d] * fac[c * G + g];
         }
-        if (valid && !bad_sh) a.out[((uint64_t)sq * a.heads + kvh * G + g) * HD + d] = O / mrg_l[g];
+        if (valid && !bad_sh) {
+            const uint64_t o = ((uint64_t)sq * a.heads + kvh * G + g) * HD + d;
+            const float r = O / mrg_l[g];
+            a.out[o] = a.gate ? __fmul_rn(r, sigmoid_ref(a.gate[o])) : r;
+        }
     }
 }
 

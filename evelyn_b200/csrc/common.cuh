@@ -133,6 +133,14 @@ __host__ __device__ inline uint64_t plain_value_address(const QMatDev& m, uint32
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// The reference's sigmoid (src/runtime.rs:476-483): 1 / (1 + e^-x) for x >= 0, else
+// e^x / (1 + e^x).
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    const float e = expf(x);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
 __device__ __forceinline__ uint4 ldg_nc(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -1,6 +1,7 @@
 // gated_delta.cu -- the recurrent half of a Qwen3.5 gated-delta layer
-// (gated_delta_attention, src/runtime.rs:551-630, and gated_delta_step, :493-528), and
-// the sigmoid query gate of its full-attention layers (:753-761).
+// (gated_delta_attention, src/runtime.rs:551-630, and gated_delta_step, :493-528). (The
+// sigmoid query gate of its full-attention layers, :753-761, is applied by the
+// attention kernels as they write their output.)
 //
 // The projections around it are ordinary matvec launches: attn_qkv, attn_gate (z) and
 // ssm_alpha | ssm_beta (stacked at load into one matrix) in one, ssm_out with the
@@ -51,13 +52,6 @@ namespace cg = cooperative_groups;
 namespace {
 
 constexpr int kThreads = 128;
-
-// runtime.rs:476-483
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
-    const float e = expf(x);
-    return __fdiv_rn(e, __fadd_rn(1.0f, e));
-}
 
 // runtime.rs:485-487
 __device__ __forceinline__ float softplus_ref(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
@@ -312,12 +306,6 @@ __global__ void __launch_bounds__(kThreads) gated_delta_slice_kernel(const __gri
     }
 }
 
-__global__ void sigmoid_gate_kernel(float* __restrict__ x, const float* __restrict__ gate, uint64_t n) {
-    pdl_wait();
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
-        x[i] = __fmul_rn(x[i], sigmoid_ref(gate[i]));
-}
-
 cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -375,14 +363,6 @@ cudaError_t launch_gated_delta(const GatedDeltaArgs& a, cudaStream_t s, bool pdl
     cudaLaunchAttribute at[1];
     auto cfg = cfg_of(dim3(a.value_heads, a.batch), dim3(kThreads), smem, s, pdl, at);
     return cudaLaunchKernelEx(&cfg, gated_delta_kernel, a);
-}
-
-cudaError_t launch_sigmoid_gate(float* x, const float* gate, uint64_t n, cudaStream_t s, bool pdl) {
-    if (!x || !gate || !n) return cudaErrorInvalidValue;
-    cudaLaunchAttribute at[1];
-    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 1184);
-    auto cfg = cfg_of(dim3(blocks), dim3(256), 0, s, pdl, at);
-    return cudaLaunchKernelEx(&cfg, sigmoid_gate_kernel, x, gate, n);
 }
 
 }  // namespace evl

@@ -73,8 +73,6 @@ struct GatedDeltaArgs {
 };
 size_t gated_delta_smem(uint32_t key_dim, uint32_t value_dim);
 cudaError_t launch_gated_delta(const GatedDeltaArgs& a, cudaStream_t s, bool pdl);
-// x[i] *= sigmoid(gate[i]) (the gated query, runtime.rs:753-761)
-cudaError_t launch_sigmoid_gate(float* x, const float* gate, uint64_t n, cudaStream_t s, bool pdl);
 
 // plain_matvec.cu: the same launch, warp per row, for unquantised matrices (a
 // quantised matrix in it is read through the exact dequantiser).
@@ -131,6 +129,8 @@ struct AttnArgs {
     float* part = nullptr;         // scratch [batch][heads][nsplit][head_dim + 2]
     float scale = 0.f;
     int* err = nullptr;            // device error flag (DeviceError)
+    const float* gate = nullptr;   // [batch][heads*hd] or null: out *= sigmoid(gate), the
+                                   // gated query of Qwen3.5 (runtime.rs:753-761)
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // QK-norm + RoPE + append, split-K attention and the split merge in one launch of one

@@ -478,6 +478,7 @@ AttnArgs Decoder::attn_args(uint32_t li, uint32_t nsplit) const {
     at.part = b.part.as<float>();
     at.scale = 1.0f / sqrtf((float)hd);
     at.err = b.err.as<int>();
+    if (m.layers[li].gated) at.gate = b.qgate.as<float>();  // the sigmoid query gate on the output
     return at;
 }
 
@@ -521,10 +522,6 @@ void Decoder::enqueue_layer_attention(uint32_t li, bool pdl) {
         kernels += 1;
         cuda_check(launch_attention(attn_args(li, b.nsplit), stream, pdl), "attention");
         kernels += 2;
-    }
-    if (L.gated) {  // attention output times sigmoid(gate) (runtime.rs:753-761)
-        cuda_check(launch_sigmoid_gate(b.att.as<float>(), b.qgate.as<float>(), B * qw, stream, pdl), "query gate");
-        kernels += 1;
     }
     {  // o-proj, residual add fused (TP: partial sums, all-reduce, then add)
         const bool tp = m.tp_size > 1;

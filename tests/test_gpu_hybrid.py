@@ -80,12 +80,15 @@ def test_hybrid_greedy_64_and_ppl():
     assert out_g == out_o
 
 
-def test_hybrid_batch_matches_oracle_per_sequence():
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_hybrid_batch_matches_oracle_per_sequence(kv_f32):
     """Three sequences with their own recurrent states and positions (the batch runs the
-    matvecs per sequence; the gated-delta kernel takes the batch as its grid's y)."""
+    matvecs per sequence; the gated-delta kernel takes the batch as its grid's y). f16
+    pages take the cluster attention, f32 pages the split kernels: both apply the query
+    gate as they write their output."""
     spec = synth.qwen35_tiny(seed=12)
     img = synth.build(spec)
-    m, r = evl.Model.load_memory(img, device=0), orc.Model(img)
+    m, r = evl.Model.load_memory(img, device=0, kv_f32=kv_f32), orc.Model(img)
     n = 3
     bt = evl.Batch(m, n, max_ctx=64)
     sessions = [orc.Session(r) for _ in range(n)]
