@@ -101,11 +101,25 @@ __global__ void qk_norm_rope_append_kernel(const __grid_constant__ RopeArgs a) {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kChunkPages = 4;  // pages staged per pipeline stage
+// pages per stage for an element type and head size: 4, or 2 for rows of 1 KB (head_dim
+// 256 in f32), which keeps the two double-buffered K and V stages within 128 KB
+template <typename KV, int HD>
+constexpr int chunk_pages() { return HD * (int)sizeof(KV) >= 1024 ? 2 : kChunkPages; }
 
-// N consecutive cache values (N = 2 or 4) as floats
+// N consecutive cache values (N = 2, 4 or 8) as floats
 template <int N>
 __device__ __forceinline__ void load_vals(const __half* p, float (&o)[N]) {
-    if constexpr (N == 4) {
+    static_assert(N == 2 || N == 4 || N == 8, "2, 4 or 8 values per lane");
+    if constexpr (N == 8) {
+        const uint4 r = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            o[2 * i] = x.x;
+            o[2 * i + 1] = x.y;
+        }
+    } else if constexpr (N == 4) {
         const uint2 r = *reinterpret_cast<const uint2*>(p);
         const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
         const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
@@ -117,7 +131,12 @@ __device__ __forceinline__ void load_vals(const __half* p, float (&o)[N]) {
 }
 template <int N>
 __device__ __forceinline__ void load_vals(const float* p, float (&o)[N]) {
-    if constexpr (N == 4) {
+    static_assert(N == 2 || N == 4 || N == 8, "2, 4 or 8 values per lane");
+    if constexpr (N == 8) {
+        const float4 r0 = *reinterpret_cast<const float4*>(p), r1 = *reinterpret_cast<const float4*>(p + 4);
+        o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+        o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+    } else if constexpr (N == 4) {
         const float4 r = *reinterpret_cast<const float4*>(p);
         o[0] = r.x; o[1] = r.y; o[2] = r.z; o[3] = r.w;
     } else {
@@ -143,9 +162,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_split_kernel(const __g
 
     const uint32_t kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int CP = chunk_pages<KV, HD>();
     const uint32_t ps = a.kv.page_size;
     const uint32_t tile_bytes = ps * HD * sizeof(KV);  // one (k|v, head) page tile
-    const uint32_t stage_bytes = 2 * kChunkPages * tile_bytes;
+    const uint32_t stage_bytes = 2 * CP * tile_bytes;
     KV* stage[2] = {reinterpret_cast<KV*>(smem_raw), reinterpret_cast<KV*>(smem_raw + stage_bytes)};
 
     if (tid == 0) {
@@ -161,7 +181,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_split_kernel(const __g
     if (t0 >= t_all) return;  // empty split
     const uint32_t t1 = min(t_all, t0 + S);
     const int32_t* pt = a.page_table + (uint64_t)b * a.max_pages;
-    const uint32_t chunk_tokens = kChunkPages * ps;
+    const uint32_t chunk_tokens = CP * ps;
     const uint32_t nchunks = (t1 - t0 + chunk_tokens - 1) / chunk_tokens;
 
     auto issue = [&](uint32_t c, int s) {  // thread 0 only
@@ -171,7 +191,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_split_kernel(const __g
         for (uint32_t p = p0; p < p1; ++p) {
             const int32_t page = pt[p];
             uint8_t* kd = reinterpret_cast<uint8_t*>(stage[s]) + (p - p0) * tile_bytes;
-            uint8_t* vd = kd + kChunkPages * tile_bytes;
+            uint8_t* vd = kd + CP * tile_bytes;
             tma_load_1d(kd, kv_tile(a.kv, page, a.layer, 0, kvh), tile_bytes, &bar[s]);
             tma_load_1d(vd, kv_tile(a.kv, page, a.layer, 1, kvh), tile_bytes, &bar[s]);
         }
@@ -204,7 +224,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_split_kernel(const __g
         const uint32_t c0 = t0 + c * chunk_tokens, c1 = min(t1, c0 + chunk_tokens);
         const uint32_t base = (c0 / ps) * ps;  // first position held by the stage
         const KV* ks = stage[s];
-        const KV* vs = stage[s] + kChunkPages * ps * HD;
+        const KV* vs = stage[s] + CP * ps * HD;
         for (uint32_t t = c0 + warp; t < c1; t += kAttnWarps) {
             const uint32_t r = t - base;
             float kf[DPL], vf[DPL];
@@ -309,7 +329,7 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, 
 template <typename KV, int G, int HD>
 cudaError_t launch_split(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const uint32_t tile = a.kv.page_size * HD * sizeof(KV);
-    const size_t smem = 2 * 2 * kChunkPages * (size_t)tile;
+    const size_t smem = 2 * 2 * chunk_pages<KV, HD>() * (size_t)tile;
     cudaError_t e = cudaFuncSetAttribute(attention_split_kernel<KV, G, HD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -346,6 +366,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (!a.err || a.nsplit == 0 || a.kv_heads == 0 || a.heads % a.kv_heads) return cudaErrorInvalidValue;
     if (a.head_dim == 128) return launch_hd<128>(a, s, pdl);
     if (a.head_dim == 64) return launch_hd<64>(a, s, pdl);
+    if (a.head_dim == 256) return launch_hd<256>(a, s, pdl);  // Qwen3.5's full-attention heads
     return cudaErrorInvalidValue;
 }
 

@@ -163,9 +163,10 @@ std::unique_ptr<Model> load_model(const uint8_t* data, size_t len, const evl_mod
     c.eos = (eos && eos->as_u64(&u64) && u64 <= 0xffffffffu) ? (int64_t)u64 : -1;
 
     // ---- device-path constraints
-    if (c.head_dim != 64 && c.head_dim != 128)
+    // (64 and 128 take the cluster attention, 256 the split kernels)
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
         raise(EVL_ERR_UNSUPPORTED,
-              "head_dim " + std::to_string(c.head_dim) + " (device attention handles 64 and 128)");
+              "head_dim " + std::to_string(c.head_dim) + " (device attention handles 64, 128 and 256)");
     if (c.kv_heads == 0 || c.heads % c.kv_heads)
         raise(EVL_ERR_INVALID_DATA, "head_count is not a multiple of head_count_kv");
     const uint64_t group = c.heads / c.kv_heads;

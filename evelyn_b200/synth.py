@@ -109,11 +109,10 @@ def qwen35_tiny(**kw) -> ModelSpec:
 
 def qwen35_hybrid_2b(**kw) -> ModelSpec:
     """A Qwen3.5-style hybrid decoder of about 2B parameters: 24 layers, every fourth full
-    attention (16 Q / 2 KV heads x 128, gated query, interleaved rotary positions), the
-    rest gated-delta layers (16 key heads x 128, 32 value heads x 128, conv kernel 4),
-    Q4_K_M-style weights. (Qwen3.5's own full-attention heads are 256 wide, which the
-    device attention does not take; 128 keeps the layer mix and the state sizes.)"""
-    base = dict(layers=24, dim=2048, ffn=6144, heads=16, kv_heads=2, head_dim=128, arch="qwen35",
+    attention (8 Q / 2 KV heads x 256 with 64 rotary dimensions, gated query, interleaved
+    rotary positions), the rest gated-delta layers (16 key heads x 128, 32 value heads x
+    128, conv kernel 4), Q4_K_M-style weights."""
+    base = dict(layers=24, dim=2048, ffn=6144, heads=8, kv_heads=2, head_dim=256, rope_dim=64, arch="qwen35",
                 mrope_interleaved=True, full_attention_interval=4, ssm_conv_kernel=4, ssm_state=128,
                 ssm_groups=16, ssm_value_heads=32, ssm_inner=4096, ssm_type=GGML_Q4_K)
     base.update(kw)

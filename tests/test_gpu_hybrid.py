@@ -23,7 +23,7 @@ def _tokens(n, vocab, seed):
 
 @pytest.mark.parametrize("kv_f32", [False, True])
 @pytest.mark.parametrize("variant", ["q8_0", "q4_k", "neox_partial_rope", "kernel2", "alpha_beta_apart",
-                                     "one_cta_per_head"])
+                                     "one_cta_per_head", "head_dim_256"])
 def test_hybrid_step_logits_match_oracle(variant, kv_f32, monkeypatch):
     """alpha_beta_apart: ssm_alpha and ssm_beta as two matrices with a launch of their
     own (EVELYN_DELTA_STACK=0) instead of stacked into the projections' launch;
@@ -34,6 +34,8 @@ def test_hybrid_step_logits_match_oracle(variant, kv_f32, monkeypatch):
         monkeypatch.setenv("EVELYN_DELTA_STACK", "0")
     if variant == "one_cta_per_head":
         monkeypatch.setenv("EVELYN_DELTA_SLICES", "0")
+    if variant == "head_dim_256":  # Qwen3.5's own full-attention heads: 256 wide, 64 rotary dims
+        kw = dict(head_dim=256, rope_dim=64)
     if variant == "q4_k":
         kw = dict(ssm_type=synth.GGML_Q4_K)
     elif variant == "neox_partial_rope":

@@ -318,3 +318,26 @@ def test_step_kernel_groups_and_kv_types(heads, kv_heads, kv_f32, monkeypatch):
         else:
             s.step(tok, logits=False)
     assert worst <= LOGIT_TOL, worst
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_head_dim_256_session_and_batch(kv_f32):
+    """256-wide heads (GQA group 8) take the split attention kernels, one sequence and a
+    batch of three (tensor-core products, paged attention per sequence)."""
+    spec = synth.tiny(seed=41, head_dim=256, heads=8, kv_heads=1, layers=2)
+    img, m, r = _models(spec, kv_f32)
+    s, rs = evl.Session(m, max_ctx=128), orc.Session(r)
+    worst = 0.0
+    for tok in _tokens(40, spec.vocab, seed=3):
+        worst = max(worst, float(np.abs(s.step(tok) - rs.step(tok)).max()))
+    assert worst <= LOGIT_TOL, worst
+    n = 3
+    bt = evl.Batch(m, n, max_ctx=64)
+    sessions = [orc.Session(r) for _ in range(n)]
+    toks = [_tokens(20, spec.vocab, seed=50 + i) for i in range(n)]
+    worst = 0.0
+    for t in range(20):
+        got = bt.step([toks[i][t] for i in range(n)])
+        for i in range(n):
+            worst = max(worst, float(np.abs(got[i] - sessions[i].step(toks[i][t])).max()))
+    assert worst <= LOGIT_TOL, worst
