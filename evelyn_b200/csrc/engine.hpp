@@ -272,6 +272,7 @@ struct StepBuffers {
     // Qwen3.5: query gate; gated-delta projections (qkv channels, z, alpha | beta), the
     // recurrent output, and per sequence the conv history (two copies) and states
     DeviceBuffer qgate, dproj, dz, dab, dout, dhist, dstate;
+    cudaEvent_t routed_ev = nullptr;  // routed FFN: the D2H of its input, waited on alone
     DeviceBuffer gbx, gxinv, gpart, gpart2, gpart3;  // batched products: staged x, 2^-e, partial sums
     uint32_t cluster_splits = 0, cluster_ring = 0;  // single-sequence cluster attention (ring 0: off)
     KvTmap kv_tmap{};             // the KV pool for the attention's tensor-core path

@@ -295,6 +295,13 @@ cudaError_t launch_embed(const QMatDev& embed, const int32_t* tokens, uint32_t b
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t batch, float eps,
                            cudaStream_t s, bool pdl);
 cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, bool pdl);
+// Warm up to four device ranges into L2 (bulk prefetches of 16 KB, 16-byte aligned
+// starts; a null base is skipped): the device's work while the host waits on something.
+struct L2Ranges {
+    const uint8_t* base[4] = {};
+    uint64_t bytes[4] = {};
+};
+cudaError_t launch_l2_prefetch(const L2Ranges& r, cudaStream_t s);
 // Greedy pick over [batch][n] logits: first maximum wins (strict '>' like src/runtime.rs:897-905).
 // Optionally writes the pick to next_tokens, logs it at hist[b*hist_stride + pos[b]] and
 // advances pos[b] (null pointers skip each part).

@@ -270,6 +270,26 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float* y, uint32_t n,
     return cudaLaunchKernelEx(&cfg, rmsnorm_kernel, x, w, y, n, eps);
 }
 
+__global__ void l2_prefetch_kernel(const __grid_constant__ L2Ranges r) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x, first = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+    for (int i = 0; i < 4; ++i) {
+        if (!r.base[i]) continue;
+        const uint64_t chunks = (r.bytes[i] + 16383) / 16384;
+        for (uint64_t c = first; c < chunks; c += stride) {
+            const uint64_t off = c * 16384, n = (r.bytes[i] - off < 16384 ? r.bytes[i] - off : 16384) & ~15ull;
+            if (n) prefetch_l2_bulk(r.base[i] + off, (uint32_t)n);
+        }
+    }
+}
+
+cudaError_t launch_l2_prefetch(const L2Ranges& r, cudaStream_t s) {
+    for (int i = 0; i < 4; ++i)
+        if (r.base[i] && (reinterpret_cast<uintptr_t>(r.base[i]) & 15)) return cudaErrorMisalignedAddress;
+    cudaLaunchAttribute at[1];
+    auto cfg = cfg_of(dim3(148), dim3(32), s, false, at);
+    return cudaLaunchKernelEx(&cfg, l2_prefetch_kernel, r);
+}
+
 cudaError_t launch_add(float* x, const float* y, uint64_t n, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute at[1];
     auto cfg = cfg_of(dim3((unsigned)((n + 255) / 256)), dim3(256), s, pdl, at);

@@ -43,6 +43,7 @@ Decoder::~Decoder() {
         DeviceGuard g(model->device);
         if (graph) cudaGraphExecDestroy(graph);
         if (step_k) step_kernel_destroy(step_k);
+        if (b.routed_ev) cudaEventDestroy(b.routed_ev);
         if (stream) cudaStreamDestroy(stream);
         for (void* p : b.ipc_open) cudaIpcCloseMemHandle(p);
     }
@@ -908,7 +909,27 @@ void Decoder::run_routed(const evl_ffn_backend& ffn) {
         float* xn = b.xn.as<float>();
         cuda_check(launch_rmsnorm(x, m.layers[li].ffn_norm, xn, (uint32_t)c.dim, 1, c.eps, stream, pdl), "ffn norm");
         cuda_check(cudaMemcpyAsync(b.h_xn.p, xn, c.dim * 4, cudaMemcpyDeviceToHost, stream), "D2H ffn input");
-        cuda_check(cudaStreamSynchronize(stream), "sync");
+        if (!b.routed_ev) cuda_check(cudaEventCreateWithFlags(&b.routed_ev, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventRecord(b.routed_ev, stream), "event");
+        {  // while the host runs the backend, the device warms the next launches' weights
+            L2Ranges r;
+            auto put = [&](int i, const QMatrix& q) {
+                r.base[i] = q.dev.q;
+                r.bytes[i] = q.dev.q ? q.bytes() : 0;
+            };
+            if (li + 1 < c.layers) {
+                const LayerWeights& N = m.layers[li + 1];
+                if (N.delta) {
+                    put(0, N.d.qkv), put(1, N.d.z), put(2, N.d.out);
+                } else {
+                    put(0, N.q), put(1, N.k), put(2, N.v), put(3, N.o);
+                }
+            } else {
+                put(0, m.lm_head);
+            }
+            cuda_check(launch_l2_prefetch(r, stream), "L2 prefetch");
+        }
+        cuda_check(cudaEventSynchronize(b.routed_ev), "sync");  // the input only, not the prefetch
         const int rc = ffn.ffn(ffn.ctx, li, b.h_xn.as<float>(), c.dim, b.h_y.as<float>());
         if (rc == 0) {
             cuda_check(cudaMemcpyAsync(b.y.p, b.h_y.p, c.dim * 4, cudaMemcpyHostToDevice, stream), "H2D ffn output");
