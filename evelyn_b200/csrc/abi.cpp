@@ -617,7 +617,7 @@ void check_attention_args(const float* d_q, const void* d_k_pages, const void* d
                           const float* d_out) {
     require(d_q && d_k_pages && d_v_pages && d_page_table && d_out, "null argument");
     require(t > 0, "no positions to attend");
-    require(head_dim == 128 || head_dim == 64, "head_dim must be 64 or 128");
+    require(head_dim == 128 || head_dim == 64 || head_dim == 256, "head_dim must be 64, 128 or 256");
     require(page_size == 16, "page_size must be 16");
     require(kv_heads && heads % kv_heads == 0, "heads must be a multiple of kv_heads");
     const uint32_t g = heads / kv_heads;

@@ -225,7 +225,7 @@ evl_status evl_qmatrix_dequantize(const evl_qmatrix* m, float* d_out, void* stre
  *   d_k_pages  [n_pages][kv_heads][page_size][head_dim] f16, likewise d_v_pages
  *   d_page_table [ceil(t / page_size)] int32 page ids, t = positions to attend
  *   d_out      [heads][head_dim] f32
- * head_dim must be 64 or 128 and page_size 16. Allocates its split scratch per call
+ * head_dim must be 64, 128 or 256 and page_size 16. Allocates its split scratch per call
  * and synchronises `stream` before returning. */
 evl_status evl_attention_decode(const float* d_q, const void* d_k_pages, const void* d_v_pages,
                                 const int32_t* d_page_table, uint32_t t, uint32_t heads, uint32_t kv_heads,

@@ -115,7 +115,7 @@ def _attention_ref(q, K, V, heads, kv_heads):
     return out
 
 
-@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("hd", [64, 128, 256])
 @pytest.mark.parametrize("t", [1, 15, 16, 17, 100, 1000, 3000])
 def test_attention_decode_paged(t, hd):
     heads, kv_heads, ps = 32, 8, 16
