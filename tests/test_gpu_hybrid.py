@@ -23,7 +23,7 @@ def _tokens(n, vocab, seed):
 
 @pytest.mark.parametrize("kv_f32", [False, True])
 @pytest.mark.parametrize("variant", ["q8_0", "q4_k", "neox_partial_rope", "kernel2", "alpha_beta_apart",
-                                     "one_cta_per_head", "head_dim_256"])
+                                     "one_cta_per_head", "head_dim_256", "f16_ssm", "q5_k_ssm", "all_full_attention"])
 def test_hybrid_step_logits_match_oracle(variant, kv_f32, monkeypatch):
     """alpha_beta_apart: ssm_alpha and ssm_beta as two matrices with a launch of their
     own (EVELYN_DELTA_STACK=0) instead of stacked into the projections' launch;
@@ -36,6 +36,12 @@ def test_hybrid_step_logits_match_oracle(variant, kv_f32, monkeypatch):
         monkeypatch.setenv("EVELYN_DELTA_SLICES", "0")
     if variant == "head_dim_256":  # Qwen3.5's own full-attention heads: 256 wide, 64 rotary dims
         kw = dict(head_dim=256, rope_dim=64)
+    if variant == "f16_ssm":  # unquantised projections: the warp-per-row matvec, three segments
+        kw = dict(ssm_type=synth.GGML_F16)
+    if variant == "q5_k_ssm":
+        kw = dict(ssm_type=synth.GGML_Q5_K)
+    if variant == "all_full_attention":  # interval 1: every layer gated full attention
+        kw = dict(full_attention_interval=1)
     if variant == "q4_k":
         kw = dict(ssm_type=synth.GGML_Q4_K)
     elif variant == "neox_partial_rope":

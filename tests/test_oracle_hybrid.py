@@ -144,7 +144,9 @@ class _Ref:
 ODD = dict(ssm_conv_kernel=2, ssm_groups=1, ssm_value_heads=3, ssm_inner=192, full_attention_interval=2)
 
 
-@pytest.mark.parametrize("interleaved,rope_dim,kw", [(True, 0, {}), (False, 32, {}), (True, 0, ODD)])
+@pytest.mark.parametrize("interleaved,rope_dim,kw", [(True, 0, {}), (False, 32, {}), (True, 0, ODD),
+                                                     (True, 0, dict(full_attention_interval=1)),
+                                                     (True, 64, dict(head_dim=256))])
 def test_hybrid_step_matches_float64_restatement(interleaved, rope_dim, kw):
     spec = synth.qwen35_tiny(seed=21, mrope_interleaved=interleaved, rope_dim=rope_dim, **kw)
     m = orc.Model(synth.build(spec))
