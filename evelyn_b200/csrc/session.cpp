@@ -159,11 +159,12 @@ void Decoder::init(Model* m, uint32_t batch, uint32_t max_ctx, const Decoder* sh
             if (ring) {
                 b.cluster_splits = C;
                 b.cluster_ring = ring;
-                // two stages (double buffering): more, smaller chunks measured slower, the
-                // chunk's compute rather than its copy bounds a split; EVELYN_ATTN_STAGES
-                // (2 .. 4) overrides
+                // one sequence: two stages (double buffering; more, smaller chunks measured
+                // slower, the chunk's compute rather than its copy bounds a split); a batch:
+                // four (two warp groups double-buffered, measured 2914 against 2874 tok/s at
+                // 32 sequences); EVELYN_ATTN_STAGES (2 .. 4) overrides
                 const char* se = std::getenv("EVELYN_ATTN_STAGES");
-                uint32_t st = se ? (uint32_t)std::strtoul(se, nullptr, 10) : 2u;
+                uint32_t st = se ? (uint32_t)std::strtoul(se, nullptr, 10) : (batch > 1 ? 4u : 2u);
                 st = st >= 4 && ring % 4 == 0 && ring >= 8 ? 4u : 2u;
                 b.cluster_stages = st;
                 // EVELYN_QKV_CTAS caps the QKV matvec's grid so the attention's CTAs can
