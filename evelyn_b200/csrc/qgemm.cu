@@ -34,6 +34,8 @@
 // and MMAs land, frees its tensor memory and leaves.
 #include <algorithm>
 #include <atomic>
+#include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "dequant.cuh"
@@ -335,6 +337,93 @@ __global__ void __launch_bounds__(kStatsThreads) gemm_stage_stats_kernel(const G
         }
         const float sm = warp_sum(val);  // the warp's 32 values are one sub-block
         if (k < K && (k & 31) == 0) reinterpret_cast<float*>(chunk + 16 * (N * 32u))[(kc / 32) * nsp + s] = sm;
+    }
+    pdl_launch_dependents();
+}
+
+// The same statistics and staging with a row split over a cluster of kStageSplit CTAs
+// (rows of K % (kStageSplit * 256) == 0 values, at most kStatsThreads * kStatsPer per
+// CTA): CTA rank r reads and stages values [r K / S, (r + 1) K / S) of its sequence. The
+// row's sum of squares and maximum meet over distributed shared memory, every CTA
+// storing its block total into slot `rank` of every CTA of the cluster and adding the
+// slots in rank order.
+constexpr uint32_t kStageSplit = 4;
+__global__ void __launch_bounds__(kStatsThreads) gemm_stage_cluster_kernel(const GemmX a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    const uint32_t rank = blockIdx.x % kStageSplit, s = blockIdx.x / kStageSplit;
+    const uint32_t K = a.cols, Kp = K / kStageSplit, k0 = rank * Kp, tid = threadIdx.x, nt = blockDim.x;
+    __shared__ float red[32];
+    __shared__ float xch[2][kStageSplit];  // per rank: sum of squares, maximum
+    auto block_reduce = [&](float t, bool is_max) {
+        t = is_max ? warp_max(t) : warp_sum(t);
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = t;
+        __syncthreads();
+        float r = 0.f;
+        for (uint32_t w = 0; w < nt / 32; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+        return r;
+    };
+    float v[kStatsPer], g[kStatsPer];
+    if (a.norm_w) {
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) g[i] = tid + i * nt < Kp ? a.norm_w[k0 + tid + i * nt] : 0.f;
+    }
+    pdl_wait();
+    const bool live = s < a.nseq;  // padding sequences stage zeros
+    const float* x = a.x + (uint64_t)(live ? s : 0) * a.x_stride;
+#pragma unroll
+    for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = live && tid + i * nt < Kp ? x[k0 + tid + i * nt] : 0.f;
+    float inv = 1.f;
+    if (a.norm_w) {
+        float ss = 0.f;
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) ss += v[i] * v[i];
+        const float t = block_reduce(ss, false);
+        if (tid < kStageSplit) *cl.map_shared_rank(&xch[0][rank], tid) = t;
+        cl.sync();
+        float tot = 0.f;
+        for (uint32_t r = 0; r < kStageSplit; ++r) tot += xch[0][r];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+#pragma unroll
+        for (uint32_t i = 0; i < kStatsPer; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), g[i]);  // staged_val
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < kStatsPer; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    const float tm = block_reduce(mx, true);
+    if (tid < kStageSplit) *cl.map_shared_rank(&xch[1][rank], tid) = tm;
+    cl.sync();
+    float T = 0.f;
+    for (uint32_t r = 0; r < kStageSplit; ++r) T = fmaxf(T, xch[1][r]);
+    int e = 0;
+    if (T > 0.f) frexpf(T, &e);  // T in [2^(e-1), 2^e)
+    const int sc = max(-100, min(100, 14 - e));  // |x| * 2^sc < 2^14
+    if (rank == 0 && tid == 0 && live) {
+        a.stats[2 * s] = inv;
+        a.stats[2 * s + 1] = ldexpf(1.0f, sc);
+        a.xinv[s] = ldexpf(1.0f, -sc);
+    }
+    const float up = ldexpf(1.0f, sc);
+    const uint32_t nsp = a.nsp, N = 2 * nsp;
+#pragma unroll
+    for (uint32_t i = 0; i < kStatsPer; ++i) {
+        if (i * nt >= Kp) break;  // uniform
+        const bool in = tid + i * nt < Kp;
+        const uint32_t k = k0 + tid + i * nt;
+        const float val = in ? __fmul_rn(v[i], up) : 0.f;
+        const __half hi = __float2half_rn(val);
+        const __half lo = __float2half_rn(val - __half2float(hi));
+        uint8_t* chunk = a.bx + (uint64_t)(k / kChunk) * gemm_xchunk_bytes(nsp);
+        const uint32_t kc = k % kChunk;
+        uint8_t* tile = chunk + (kc / 16) * (N * 32u);
+        const uint32_t sl = kslot(kc % 16);
+        if (in) {
+            *reinterpret_cast<__half*>(tile + bt_off(s, sl)) = hi;
+            *reinterpret_cast<__half*>(tile + bt_off(nsp + s, sl)) = lo;
+        }
+        const float sm = warp_sum(val);  // the warp's 32 values are one sub-block
+        if (in && (k & 31) == 0) reinterpret_cast<float*>(chunk + 16 * (N * 32u))[(kc / 32) * nsp + s] = sm;
     }
     pdl_launch_dependents();
 }
@@ -850,6 +939,22 @@ cudaError_t launch_gemm_stage_x(GemmX a, cudaStream_t s, bool pdl) {
     // rows of up to kStatsThreads * kStatsPer values: one launch, a CTA per sequence
     // (padding ones included) computes the statistics and stages its row
     const bool one = a.cols <= kStatsThreads * kStatsPer;
+    // a row split over a cluster of kStageSplit CTAs when it divides into whole 256-value
+    // chunks (EVELYN_STAGE_SPLIT=0: one CTA per sequence)
+    static const bool split_off = [] {
+        const char* e = std::getenv("EVELYN_STAGE_SPLIT");
+        return e && e[0] == '0';
+    }();
+    if (one && a.cols % (kStageSplit * kChunk) == 0 && !split_off) {
+        cudaLaunchAttribute at2[2];
+        auto cfg = cfg_of(dim3(a.nsp * kStageSplit), dim3(kStatsThreads), 0, s, pdl, at2);
+        at2[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        at2[cfg.numAttrs].val.clusterDim.x = kStageSplit;
+        at2[cfg.numAttrs].val.clusterDim.y = 1;
+        at2[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs += 1;
+        return cudaLaunchKernelEx(&cfg, gemm_stage_cluster_kernel, a);
+    }
     auto cfg = cfg_of(dim3(one ? a.nsp : a.nseq), dim3(kStatsThreads), 0, s, pdl, at);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_stage_stats_kernel, a);
     if (e != cudaSuccess || one) return e;
