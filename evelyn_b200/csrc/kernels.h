@@ -54,7 +54,9 @@ cudaError_t launch_qmatvec(const MatvecArgs& a, cudaStream_t s, bool pdl);
 // ---------------------------------------------------------------- gated_delta.cu
 // The recurrent half of a Qwen3.5 gated-delta layer (runtime.rs:551-630) between its
 // projections and ssm_out: conv, q/k normalisation, the delta rule on the state, the
-// per-head norm and SiLU(z) gate. One CTA per (value head, sequence).
+// per-head norm and SiLU(z) gate. A cluster of up to 4 CTAs per (value head, sequence),
+// each on a slice of the head's value columns (one CTA per head where the slice does
+// not fit in shared memory).
 struct GatedDeltaArgs {
     const float* proj = nullptr;   // [batch][channels] attn_qkv output (q | k | v channels)
     const float* z = nullptr;      // [batch][value_heads * value_dim] attn_gate output
