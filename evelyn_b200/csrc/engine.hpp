@@ -347,6 +347,8 @@ struct Decoder {  // shared by Session (batch 1) and Batch (batch n)
     // and argmax [n] (host).
     void prefill(uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out, uint32_t* argmax_out);
     std::unique_ptr<Decoder> pf;  // prefill child (made on first use)
+    bool pf_stepwise = false;     // no tensor-core products for this model: a single
+                                  // session's prefill runs one step per prompt token
     bool prefill_child = false;
     // what the child's device page table holds: its rows [0, pf_rows) map sequence
     // pf_seq's pages, the rest the spare page (pf_rows = 0: not written yet)

@@ -1059,11 +1059,21 @@ void Decoder::prefill(uint32_t seq, const uint32_t* tokens, size_t n, float* log
     if (host_pos[seq] + n > b.max_ctx)
         raise(EVL_ERR_INVALID_INPUT, "session context is full (" + std::to_string(b.max_ctx) + " positions)");
     if (n == 0) return;
-    if (!pf) {
+    if (!pf && !pf_stepwise) {
         auto child = std::make_unique<Decoder>();
         child->init(&m, kPrefillRows, b.max_ctx, this);
-        if (!child->use_gemm) raise(EVL_ERR_UNSUPPORTED, "prefill needs the tensor-core products for this model");
-        pf = std::move(child);
+        if (child->use_gemm) {
+            pf = std::move(child);
+        } else if (b.batch == 1) {
+            pf_stepwise = true;  // (Qwen3.5 hybrid layers, unquantised matrices)
+        } else {
+            raise(EVL_ERR_UNSUPPORTED, "batch prefill needs the tensor-core products for this model");
+        }
+    }
+    if (pf_stepwise) {  // the reference's own prompt loop: one step per token
+        for (size_t i = 0; i < n; ++i)
+            step(tokens + i, nullptr, logits_out ? logits_out + i * c.vocab : nullptr, argmax_out ? argmax_out + i : nullptr);
+        return;
     }
     Decoder& P = *pf;
     const uint32_t C = P.b.batch, pps = b.pages_per_seq;

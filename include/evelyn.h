@@ -158,7 +158,8 @@ evl_status evl_session_generate(evl_session* s, uint32_t token, uint32_t n, uint
  * batched steps of up to 32 prompt positions whose products run on the tensor cores.
  * logits_out ([n][vocab], host) and argmax_out ([n], host) are each optional: row i is
  * what step i would have returned. Dense FFN on every layer. Under tensor parallelism
- * every rank makes the same call. */
+ * every rank makes the same call. Models without the tensor-core products (Qwen3.5
+ * hybrid layers, unquantised matrices) take the prompt one step per token. */
 evl_status evl_session_prefill(evl_session* s, const uint32_t* tokens, size_t n, float* logits_out,
                                uint32_t* argmax_out);
 /* sample_token (src/server.rs:326-352) on the device, from the logits of the session's
@@ -190,7 +191,8 @@ evl_status evl_batch_step(evl_batch* b, const uint32_t* tokens, float* logits_ou
 void* evl_batch_stream(evl_batch* b);
 /* evl_session_prefill for sequence `seq` of a batch: its prompt tokens[0 .. n) in batched
  * steps of up to 32 positions on the tensor cores; the other sequences are untouched.
- * logits_out ([n][vocab]) and argmax_out ([n]) are optional (host). */
+ * logits_out ([n][vocab]) and argmax_out ([n]) are optional (host). EVL_ERR_UNSUPPORTED
+ * for a batch of several sequences of a model without the tensor-core products. */
 evl_status evl_batch_prefill(evl_batch* b, uint32_t seq, const uint32_t* tokens, size_t n, float* logits_out,
                              uint32_t* argmax_out);
 /* evl_session_sample for every sequence of a batch: rng_states[n_seqs] (host in/out),

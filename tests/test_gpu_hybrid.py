@@ -111,8 +111,8 @@ def test_hybrid_batch_matches_oracle_per_sequence(kv_f32):
 
 def test_hybrid_routed_ffn_and_unsupported_paths():
     """The FFN hook sees the hybrid layers like any other (a host FFN from the oracle
-    gives the oracle's logits); prefill, which needs the batched tensor-core products,
-    and tensor parallelism answer Unsupported for the hybrid model."""
+    gives the oracle's logits); a single session's prefill runs one step per prompt
+    token; batch prefill and tensor parallelism answer Unsupported for the hybrid model."""
     spec = synth.qwen35_tiny(seed=3)
     img = synth.build(spec)
     m, r = evl.Model.load_memory(img, device=0), orc.Model(img)
@@ -130,9 +130,17 @@ def test_hybrid_routed_ffn_and_unsupported_paths():
         worst = max(worst, float(np.abs(s.step(tok, ffn=ffn) - rs.step(tok)).max()))
     assert worst <= LOGIT_TOL, worst
     assert seen == list(range(spec.layers)) * 6
-    p = evl.Session(m, max_ctx=64)
+    # prefill: one step per prompt token for a single session (the reference's own loop),
+    # refused for a batch of several sequences
+    p, po = evl.Session(m, max_ctx=64), orc.Session(r)
+    prompt = _tokens(8, spec.vocab, seed=1)
+    rows = p.prefill(prompt, logits=True)
+    worst = max(float(np.abs(rows[i] - po.step(t)).max()) for i, t in enumerate(prompt))
+    worst = max(worst, float(np.abs(p.step(5) - po.step(5)).max()))
+    assert p.pos == po.pos == 9 and worst <= LOGIT_TOL, worst
+    bt = evl.Batch(m, 2, max_ctx=64)
     with pytest.raises(evl.EvelynError) as e:
-        p.prefill(_tokens(8, spec.vocab, seed=1))
+        bt.prefill(0, prompt)
     assert e.value.kind == "Unsupported"
     # tensor parallelism is refused at load, before any communicator is made
     with pytest.raises(evl.EvelynError) as e:
