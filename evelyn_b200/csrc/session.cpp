@@ -620,6 +620,7 @@ void Decoder::enqueue_delta(uint32_t li, bool pdl) {
         g.eps = c.eps;
         // launched after the projections complete, not early under programmatic
         // dependent launch: measured 941 against 722 tok/s on the 2B-class hybrid shape
+        // (the one-CTA-per-head kernel), 1099 against 997 (the cluster kernel)
         cuda_check(launch_gated_delta(g, stream, false), "gated delta");
         kernels += 1;
     }
